@@ -1,0 +1,273 @@
+"""ctypes view of the CPU restatement in ``mslim_oracle.c``.
+
+TEST INFRASTRUCTURE ONLY.  Imported by ``tests/``, ``__graft_entry__.smoke()``
+and the CPU legs of ``bench.py`` (``cpu_baseline`` and ``--impl reference``)
+as the checker / timed CPU reference.  The product library never imports it.
+
+Every function documents the reference source it restates; the C file holds
+the operation-by-operation restatement and its citations.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+import threading
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "build", "libmslim_oracle.so")
+_lock = threading.Lock()
+_lib = None
+
+_u16p = np.ctypeslib.ndpointer(dtype=np.uint16, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
+_f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
+_u64p = np.ctypeslib.ndpointer(dtype=np.uint64, flags="C_CONTIGUOUS")
+_sz = ctypes.c_size_t
+
+OK, ERR_GEOMETRY, ERR_SHAPE, ERR_NONFINITE = 0, 1, 2, 3
+
+
+def build() -> str:
+    """Compile the restatement with its Makefile (gcc, -ffp-contract=off)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        src = os.path.join(_HERE, "mslim_oracle.c")
+        if not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(src):
+            build()
+        L = ctypes.CDLL(_LIB_PATH)
+        L.mo_bf16_from_f32.argtypes = [ctypes.c_float]
+        L.mo_bf16_from_f32.restype = ctypes.c_uint16
+        L.mo_bf16_to_f32.argtypes = [ctypes.c_uint16]
+        L.mo_bf16_to_f32.restype = ctypes.c_float
+        L.mo_f16_to_f32.argtypes = [ctypes.c_uint16]
+        L.mo_f16_to_f32.restype = ctypes.c_float
+        L.mo_round_bf16.argtypes = [ctypes.c_float]
+        L.mo_round_bf16.restype = ctypes.c_float
+        L.mo_bf16_encode.argtypes = [_f32p, _u16p, _sz]
+        L.mo_bf16_decode.argtypes = [_u16p, _f32p, _sz]
+        L.mo_rms_norm.argtypes = [_f32p, _f32p, _sz, ctypes.c_float, _f32p]
+        L.mo_rms_norm_rows_bf16.argtypes = [_u16p, _u16p, _u16p, _sz, _sz, ctypes.c_float]
+        L.mo_apply_rope.argtypes = [_f32p, _sz, _sz, _sz, ctypes.c_float]
+        L.mo_apply_rope_rows_bf16.argtypes = [_u16p, _u16p, _sz, _sz, _sz, _sz, ctypes.c_float]
+        L.mo_softmax.argtypes = [_f32p, _sz]
+        L.mo_attention_scale.argtypes = [_sz]
+        L.mo_attention_scale.restype = ctypes.c_float
+        L.mo_dense_attention_bf16.argtypes = [_sz, _sz, _sz, _f32p, _u16p, _u16p, _sz, _f32p, ctypes.c_int]
+        L.mo_dense_attention_bf16.restype = ctypes.c_int
+        L.mo_causal_prefill_bf16.argtypes = [_sz, _sz, _sz, _u16p, _u16p, _u16p, _sz, _sz, _u16p, ctypes.c_int]
+        L.mo_causal_prefill_bf16.restype = ctypes.c_int
+        L.mo_paged_attention_bf16.argtypes = [_sz, _sz, _sz, _f32p, _u16p, _u16p, _i32p, _sz, _sz, _f32p, ctypes.c_int]
+        L.mo_paged_attention_bf16.restype = ctypes.c_int
+        L.mo_cpu_reference_decode_f64.argtypes = [_sz, _sz, _sz, _f32p, ctypes.c_void_p, ctypes.c_void_p,
+                                                  ctypes.c_int, ctypes.c_int, _sz, _f32p]
+        L.mo_cpu_reference_decode_f64.restype = ctypes.c_int
+        L.mo_rope_inverse_frequency.argtypes = [ctypes.c_float, ctypes.c_uint32, ctypes.c_float, ctypes.c_float,
+                                                ctypes.c_float, ctypes.c_float, _sz, _sz]
+        L.mo_rope_inverse_frequency.restype = ctypes.c_float
+        L.mo_gpu_rope_rows_bf16.argtypes = [_u16p, _u16p, _sz, _sz, _sz, _sz, ctypes.c_float, ctypes.c_uint32,
+                                            ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float]
+        L.mo_fnv1a64.argtypes = [_u8p, _sz]
+        L.mo_fnv1a64.restype = ctypes.c_uint64
+        L.mo_token_hashes.argtypes = [_u8p, _sz, _sz, _sz, _u64p]
+        L.mo_page_from_token_major.argtypes = [_u16p, _u16p, _sz, _sz, _sz]
+        L.mo_openmp_max_threads.restype = ctypes.c_int
+        _lib = L
+        return L
+
+
+def max_threads() -> int:
+    return int(lib().mo_openmp_max_threads())
+
+
+# ------------------------------------------------------------------ bf16 --
+
+def bf16_from_f32(x: np.ndarray) -> np.ndarray:
+    """half 2.7.1 ``bf16::from_f32`` on every element (native_cpu_adapter.rs:179)."""
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    out = np.empty(x.shape, np.uint16)
+    lib().mo_bf16_encode(x, out, x.size)
+    return out
+
+
+def bf16_to_f32(b: np.ndarray) -> np.ndarray:
+    b = np.ascontiguousarray(b, dtype=np.uint16).reshape(-1)
+    out = np.empty(b.shape, np.float32)
+    lib().mo_bf16_decode(b, out, b.size)
+    return out
+
+
+# ------------------------------------------------------------- helpers --
+
+def rms_norm(x: np.ndarray, weight: np.ndarray, eps: float) -> np.ndarray:
+    """native_cpu_adapter.rs:194-204 on one f32 vector."""
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(weight, np.float32)
+    out = np.empty_like(x)
+    lib().mo_rms_norm(x, w, x.size, eps, out)
+    return out
+
+
+def rms_norm_rows_bf16(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    """rms_norm per token row of a bf16 [tokens][hidden] matrix."""
+    x = np.ascontiguousarray(x, np.uint16)
+    tokens, hidden = x.shape
+    y = np.empty_like(x)
+    lib().mo_rms_norm_rows_bf16(x, np.ascontiguousarray(w, np.uint16), y, tokens, hidden, eps)
+    return y
+
+
+def apply_rope(values: np.ndarray, heads: int, dim: int, position: int, theta: float) -> np.ndarray:
+    """native_cpu_adapter.rs:206-221 (in place on a copy)."""
+    v = np.array(values, dtype=np.float32, copy=True).reshape(-1)
+    lib().mo_apply_rope(v, heads, dim, position, theta)
+    return v
+
+
+def rope_rows_bf16(x: np.ndarray, start_position: int, theta: float) -> np.ndarray:
+    """CPU RoPE on bf16 rows [tokens][heads][dim]; row t at start_position+t."""
+    x = np.ascontiguousarray(x, np.uint16)
+    tokens, heads, dim = x.shape
+    out = np.empty_like(x)
+    lib().mo_apply_rope_rows_bf16(x, out, tokens, heads, dim, start_position, theta)
+    return out
+
+
+def gpu_rope_rows_bf16(x: np.ndarray, start_position: int, theta: float, llama3: bool = False,
+                       factor: float = 1.0, low: float = 1.0, high: float = 2.0,
+                       original_max_position: float = 1.0) -> np.ndarray:
+    """assets/gpu_llm.cl:412-456 formula on bf16 rows [tokens][heads][dim]."""
+    x = np.ascontiguousarray(x, np.uint16)
+    tokens, heads, dim = x.shape
+    out = np.empty_like(x)
+    lib().mo_gpu_rope_rows_bf16(x, out, tokens, heads, dim, start_position, theta, int(llama3), factor,
+                                low, high, original_max_position)
+    return out
+
+
+def rope_inverse_frequency(theta: float, frequency_dim: int, head_dim: int, llama3: bool = False,
+                           factor: float = 1.0, low: float = 1.0, high: float = 2.0,
+                           original_max_position: float = 1.0) -> float:
+    """src/gpu_llm/kernels.rs:50-67."""
+    return float(lib().mo_rope_inverse_frequency(theta, int(llama3), factor, low, high,
+                                                  original_max_position, frequency_dim, head_dim))
+
+
+def softmax(values: np.ndarray) -> np.ndarray:
+    v = np.array(values, dtype=np.float32, copy=True).reshape(-1)
+    lib().mo_softmax(v, v.size)
+    return v
+
+
+# ----------------------------------------------------------- attention --
+
+def dense_attention_bf16(query_heads: int, kv_heads: int, head_dim: int, query_f32: np.ndarray,
+                         keys: np.ndarray, values: np.ndarray, threads: int = 0) -> np.ndarray:
+    """native_cpu_adapter.rs:253-307.  keys/values bf16 [T][KVH][D]."""
+    q = np.ascontiguousarray(query_f32, np.float32).reshape(-1)
+    k = np.ascontiguousarray(keys, np.uint16).reshape(-1)
+    v = np.ascontiguousarray(values, np.uint16).reshape(-1)
+    row = kv_heads * head_dim
+    tokens = k.size // row
+    if q.size != query_heads * head_dim or k.size != tokens * row or v.size != k.size:
+        raise ValueError("geometría KV caliente incompatible")
+    out = np.empty(query_heads * head_dim, np.float32)
+    rc = lib().mo_dense_attention_bf16(query_heads, kv_heads, head_dim, q, k, v, tokens, out,
+                                       threads or max_threads())
+    if rc:
+        raise ValueError(f"oracle dense attention error {rc}")
+    return out
+
+
+def paged_attention_bf16(query_heads: int, kv_heads: int, head_dim: int, query_f32: np.ndarray,
+                         k_pool: np.ndarray, v_pool: np.ndarray, page_table: np.ndarray,
+                         page_tokens: int, tokens: int, threads: int = 0) -> np.ndarray:
+    """ColdStore-exact branch (native_cpu_adapter.rs:386-455, epsilon 0)."""
+    q = np.ascontiguousarray(query_f32, np.float32).reshape(-1)
+    out = np.empty(query_heads * head_dim, np.float32)
+    rc = lib().mo_paged_attention_bf16(query_heads, kv_heads, head_dim, q,
+                                       np.ascontiguousarray(k_pool, np.uint16).reshape(-1),
+                                       np.ascontiguousarray(v_pool, np.uint16).reshape(-1),
+                                       np.ascontiguousarray(page_table, np.int32).reshape(-1),
+                                       page_tokens, tokens, out, threads or max_threads())
+    if rc:
+        raise ValueError(f"oracle paged attention error {rc}")
+    return out
+
+
+def causal_prefill_bf16(query_heads: int, kv_heads: int, head_dim: int, q: np.ndarray,
+                        keys: np.ndarray, values: np.ndarray, queries: int, prior: int,
+                        threads: int = 0) -> np.ndarray:
+    """Per-row dense attention = CPU prefill (native_cpu_adapter.rs:717-784).
+    q bf16 [queries][QH][D]; keys/values bf16 [prior+queries][KVH][D]."""
+    qa = np.ascontiguousarray(q, np.uint16).reshape(-1)
+    out = np.empty(queries * query_heads * head_dim, np.uint16)
+    rc = lib().mo_causal_prefill_bf16(query_heads, kv_heads, head_dim, qa,
+                                      np.ascontiguousarray(keys, np.uint16).reshape(-1),
+                                      np.ascontiguousarray(values, np.uint16).reshape(-1),
+                                      queries, prior, out, threads or max_threads())
+    if rc:
+        raise ValueError(f"oracle prefill error {rc}")
+    return out.reshape(queries, query_heads, head_dim)
+
+
+DTYPE_CODES = {"bf16": 1, "f16": 2, "f32": 3}
+
+
+def cpu_reference_decode_f64(query_heads: int, kv_heads: int, head_dim: int, query: np.ndarray,
+                             keys: np.ndarray, values: np.ndarray, key_dtype: str = "bf16",
+                             value_dtype: str = "bf16") -> np.ndarray:
+    """src/portable.rs:575-646 (f64 online softmax).  Raises ArithmeticError
+    for the PortableError::NonFinite conditions."""
+    q = np.ascontiguousarray(query, np.float32).reshape(-1)
+    k = np.ascontiguousarray(keys)
+    v = np.ascontiguousarray(values)
+    ebytes = {"bf16": 2, "f16": 2, "f32": 4}
+    tokens = k.nbytes // (kv_heads * head_dim * ebytes[key_dtype])
+    out = np.zeros(query_heads * head_dim, np.float32)
+    rc = lib().mo_cpu_reference_decode_f64(query_heads, kv_heads, head_dim, q,
+                                           k.ctypes.data_as(ctypes.c_void_p),
+                                           v.ctypes.data_as(ctypes.c_void_p),
+                                           DTYPE_CODES[key_dtype], DTYPE_CODES[value_dtype], tokens, out)
+    if rc == ERR_NONFINITE:
+        raise ArithmeticError("non-finite computation")
+    if rc:
+        raise ValueError(f"invalid geometry ({rc})")
+    return out
+
+
+# ----------------------------------------------------------- ColdStore --
+
+def fnv1a64(data: bytes | np.ndarray) -> int:
+    """src/cold_store.rs:909-922."""
+    a = np.frombuffer(bytes(data), np.uint8) if not isinstance(data, np.ndarray) else \
+        np.ascontiguousarray(data).view(np.uint8).reshape(-1)
+    return int(lib().mo_fnv1a64(np.ascontiguousarray(a), a.size))
+
+
+def token_hashes(page_payload: np.ndarray, heads: int, tokens: int) -> np.ndarray:
+    """src/cold_store.rs:763-781 over a head-major page payload."""
+    p = np.ascontiguousarray(page_payload).view(np.uint8).reshape(-1)
+    per = p.size // (heads * tokens)
+    out = np.empty(tokens, np.uint64)
+    lib().mo_token_hashes(p, heads, tokens, per, out)
+    return out
+
+
+def page_from_token_major(token_major: np.ndarray, kv_heads: int, head_dim: int) -> np.ndarray:
+    """src/gpu_region_store.rs:470-483 for one page."""
+    t = np.ascontiguousarray(token_major, np.uint16).reshape(-1)
+    n = t.size // (kv_heads * head_dim)
+    page = np.empty(kv_heads * n * head_dim, np.uint16)
+    lib().mo_page_from_token_major(t, page, n, kv_heads, head_dim)
+    return page.reshape(kv_heads, n, head_dim)
