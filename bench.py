@@ -1,0 +1,419 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 attention hot path (one JSON line on stdout).
+
+Headline (BASELINE.json metric "GQA decode attn HBM GB/s & tokens/s; prefill
+attn TFLOPS"): configuration C4, batched long-context decode -- 64 sessions
+per GPU with lengths uniform in [4096, 32768] (seed 3), K/V in 256-token
+ColdStore-exact pages under a random physical page permutation, 32 query /
+8 KV heads of dim 128.  One step = one split-KV decode of every session
+(mslim_decode_split + mslim_decode_merge).  `value` is algorithmic bytes
+(K+V of every session, Q and O rows, page-table entries) per second, summed
+over all ranks; inputs (4.8 GB per GPU) are larger than L2, so no flush is
+needed between steps.
+
+Multi-GPU: one process per GPU (torchrun); each rank owns its own sessions
+(independent objects, no data-path collective); NCCL is used only for the
+barrier and the max-over-ranks step time.  --scaling weak (default) gives
+every rank the 64 C4 sessions; --scaling strong shards the 64 sessions of one
+C4 draw across ranks by longest-processing-time.
+
+--impl reference times the reference's CPU hot-dense path (its C
+restatement in oracle/, OpenMP across query heads like the reference's rayon
+loop) on a bounded sample of the same sessions, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "vk-shei_b200"))
+
+METRIC = "GQA decode attn HBM GB/s (C4 batched split-KV decode; tokens/s and prefill TFLOPS alongside)"
+QH, KVH, D, PAGE = 32, 8, 128, 256
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
+    ap.add_argument("--sessions", type=int, default=64, help="sessions per GPU (small profiling cases)")
+    ap.add_argument("--split-tokens", type=int, default=0)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------ clocks --
+
+_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+            0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+            0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+
+class ClockSampler:
+    """Polls NVML (read-only) every few ms during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._nvml = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nvml = None
+
+    def _run(self):
+        p = self._nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(p.nvmlDeviceGetClockInfo(self._h, p.NVML_CLOCK_SM))
+                self.reasons |= int(p.nvmlDeviceGetCurrentClocksEventReasons(self._h))
+            except Exception:
+                pass
+            time.sleep(0.005)
+
+    def start(self):
+        if self._nvml:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+
+    def stop(self) -> dict:
+        self._stop.set()
+        if self._thread:
+            self._thread.join()
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        reasons = [name for bit, name in _REASONS.items() if self.reasons & bit and bit != 0x1]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+# -------------------------------------------------------------- utilities --
+
+def measured_peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d.get("hbm_gbs"), "bf16_tflops": d.get("bf16_tflops"),
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def profile_traffic(name: str):
+    """dram bytes per launch from a committed ncu summary (profiles/*.json)."""
+    p = os.path.join(ROOT, "profiles", name)
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return None
+
+
+def lpt_shard(lengths, world: int, rank: int) -> list[int]:
+    """Longest-processing-time assignment of sessions to ranks."""
+    order = sorted(range(len(lengths)), key=lambda i: (-int(lengths[i]), i))
+    loads = [0] * world
+    owner = {}
+    for i in order:
+        r = min(range(world), key=lambda j: (loads[j], j))
+        loads[r] += int(lengths[i])
+        owner[i] = r
+    return sorted(i for i in order if owner[i] == rank)
+
+
+# --------------------------------------------------------------- CPU legs --
+
+def cpu_sample_gbs(lengths, seconds: float, seed: int = 3) -> dict:
+    """Times the CPU restatement of the reference hot-dense / ColdStore-exact
+    decode (native_cpu_adapter.rs:253-307, :386-455) on sessions of the C4
+    draw, repeating passes until `seconds` of CPU work have elapsed."""
+    import numpy as np
+    from oracle import oracle
+    from mslim_b200 import workloads
+    rng = np.random.default_rng(seed)
+    threads = oracle.max_threads()
+    sample = []
+    for L in lengths:
+        L = int(L)
+        npg = (L + PAGE - 1) // PAGE
+        k = workloads.normal_bf16(rng, (npg, KVH, PAGE, D))
+        v = workloads.normal_bf16(rng, (npg, KVH, PAGE, D))
+        q = workloads.bf16_to_f32(workloads.normal_bf16(rng, (QH * D,)))
+        sample.append((L, q, k, v, np.arange(npg, dtype=np.int32)))
+    done_bytes = 0
+    t0 = time.perf_counter()
+    passes = 0
+    while True:
+        for L, q, k, v, table in sample:
+            oracle.paged_attention_bf16(QH, KVH, D, q, k, v, table, PAGE, L, threads)
+            done_bytes += L * KVH * D * 2 * 2 + 2 * QH * D * 2
+        passes += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or passes >= 1000:
+            break
+    return {"value": done_bytes / el / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{len(sample)} C4 sessions (L={','.join(str(int(x)) for x in lengths)}) x {passes} passes, "
+                      f"{el:.1f} s, oracle/mslim_oracle.c paged_attention_bf16 with {threads} OpenMP threads"}
+
+
+def run_reference(args, rank: int) -> None:
+    if rank != 0:
+        return
+    from mslim_b200 import workloads
+    layout = workloads.c4_layout(seed=3)
+    import numpy as np
+    from oracle import oracle
+    lengths = layout.lengths[:4]
+    rng = np.random.default_rng(3)
+    threads = oracle.max_threads()
+    data = []
+    for L in lengths:
+        npg = (int(L) + PAGE - 1) // PAGE
+        data.append((int(L), workloads.bf16_to_f32(workloads.normal_bf16(rng, (QH * D,))),
+                     workloads.normal_bf16(rng, (npg, KVH, PAGE, D)), workloads.normal_bf16(rng, (npg, KVH, PAGE, D)),
+                     np.arange(npg, dtype=np.int32)))
+    step_bytes = sum(L * KVH * D * 4 + 2 * QH * D * 2 for L, *_ in data)
+
+    def step():
+        for L, q, k, v, t in data:
+            oracle.paged_attention_bf16(QH, KVH, D, q, k, v, t, PAGE, L, threads)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    value = step_bytes * args.steps / el / 1e9
+    sample = (f"{len(data)} C4 sessions per step (L={','.join(str(L) for L, *_ in data)}), "
+              f"oracle/mslim_oracle.c paged_attention_bf16, {threads} OpenMP threads")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": el * 1e3 / args.steps,
+            "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) bf16)",
+            "config": {"workload": "C4 batched long-context decode (bounded CPU sample)", "page_tokens": PAGE,
+                       "query_heads": QH, "kv_heads": KVH, "head_dim": D},
+            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------- GPU leg --
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    import numpy as np
+    import torch
+    import mslim_b200 as m
+    from mslim_b200 import workloads
+
+    torch.cuda.set_device(local)
+    device = f"cuda:{local}"
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device(device))
+    m.load()
+
+    layout = workloads.c4_layout(seed=3)
+    if args.scaling == "strong" and world > 1:
+        mine = lpt_shard(layout.lengths, world, rank)
+    else:
+        mine = list(range(min(args.sessions, len(layout.lengths))))
+    lengths = layout.lengths[mine].astype(np.int32)
+    n_seq = len(mine)
+    # pages for L + 1 tokens: the e2e leg appends the step's new token at L
+    pages = (lengths + 1 + PAGE - 1) // PAGE
+    n_pages = int(pages.sum())
+    rng = np.random.default_rng(3 + rank)
+    perm = rng.permutation(n_pages).astype(np.int32)
+    max_pages = int(pages.max())
+    table = np.zeros((n_seq, max_pages), np.int32)
+    cur = 0
+    for s in range(n_seq):
+        table[s, :pages[s]] = perm[cur:cur + pages[s]]
+        cur += pages[s]
+
+    gen = torch.Generator(device=device)
+    gen.manual_seed(3 + rank)
+    k_pool = torch.randn((n_pages, KVH, PAGE, D), generator=gen, device=device, dtype=torch.bfloat16)
+    v_pool = torch.randn((n_pages, KVH, PAGE, D), generator=gen, device=device, dtype=torch.bfloat16)
+    q = torch.randn((n_seq, QH, D), generator=gen, device=device, dtype=torch.bfloat16)
+    out = torch.empty((n_seq, QH, D), device=device, dtype=torch.bfloat16)
+    table_d = torch.from_numpy(table).to(device)
+    seq_d = torch.from_numpy(lengths).to(device)
+    g = m.AttentionGeometry.new(QH, KVH, D)
+    max_tokens = max_pages * PAGE
+    ws = torch.empty(m.decode_workspace_bytes(g, n_seq, max_tokens, args.split_tokens), dtype=torch.uint8,
+                     device=device)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        m.decode_paged(g, q, k_pool, v_pool, n_pages, PAGE, table_d, max_pages, seq_d, n_seq, ws, out,
+                       args.split_tokens, stream)
+
+    step_bytes = int(lengths.astype(np.int64).sum()) * KVH * D * 4 + n_seq * QH * D * 4 + int(
+        ((lengths + PAGE - 1) // PAGE).sum()) * 4
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if m.device_status(local) != 0:
+        raise SystemExit("device status reported a bounded wait timeout during warm-up")
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    # ---- device-timed region (CUDA events on the launching stream) ----
+    sampler = ClockSampler(local)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(args.steps):
+        evs[i][0].record(stream)
+        step()
+        evs[i][1].record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    elapsed_ms = t_start.elapsed_time(t_end)
+    launch_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    if dist is not None:
+        t = torch.tensor([elapsed_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+        tb = torch.tensor([step_bytes, n_seq], device=device, dtype=torch.float64)
+        dist.all_reduce(tb, op=dist.ReduceOp.SUM)
+        total_bytes, total_seq = float(tb[0].item()), int(tb[1].item())
+    else:
+        total_bytes, total_seq = float(step_bytes), n_seq
+    ms_per_step = elapsed_ms / args.steps
+    value = total_bytes / (ms_per_step * 1e-3) / 1e9
+    status = m.device_status(local)
+
+    # ---- end-to-end leg: the C-ABI calls a decode step makes, host buffers ----
+    e2e = None
+    if not args.no_e2e:
+        rope_cfg = m.RopeKernelConfig(theta=500000.0)
+        q_host = torch.randn((n_seq, QH, D), generator=torch.Generator().manual_seed(5)).to(torch.bfloat16).pin_memory()
+        kv_host = torch.randn((2, n_seq, KVH, D), generator=torch.Generator().manual_seed(6)).to(torch.bfloat16).pin_memory()
+        out_host = torch.empty((n_seq, QH, D), dtype=torch.bfloat16).pin_memory()
+        q_in = torch.empty_like(q)
+        q_rot = torch.empty_like(q)
+        kv_in = torch.empty((2, n_seq, KVH, D), device=device, dtype=torch.bfloat16)
+        pos_d = torch.from_numpy(lengths).to(device)          # new token at position L
+        seq1_d = torch.from_numpy(lengths + 1).to(device)     # then attend over L + 1
+
+        def e2e_step():
+            q_in.copy_(q_host, non_blocking=True)
+            kv_in.copy_(kv_host, non_blocking=True)
+            m.rope_append_decode_paged(g, q_in, q_rot, kv_in[0], kv_in[1], pos_d, n_seq, rope_cfg, k_pool,
+                                       v_pool, n_pages, PAGE, table_d, max_pages, stream)
+            m.decode_paged(g, q_rot, k_pool, v_pool, n_pages, PAGE, table_d, max_pages, seq1_d, n_seq, ws,
+                           out, args.split_tokens, stream)
+            out_host.copy_(out, non_blocking=True)
+            stream.synchronize()
+
+        for _ in range(3):
+            e2e_step()
+        e_bytes = int((lengths + 1).astype(np.int64).sum()) * KVH * D * 4 + n_seq * QH * D * 4 + int(
+            ((lengths + 1 + PAGE - 1) // PAGE).sum()) * 4
+        barrier()
+        torch.cuda.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        b.record(stream)
+        torch.cuda.synchronize()
+        e_ms = a.elapsed_time(b)
+        if dist is not None:
+            t = torch.tensor([e_ms], device=device, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e_ms = float(t.item())
+            tb = torch.tensor([e_bytes], device=device, dtype=torch.float64)
+            dist.all_reduce(tb, op=dist.ReduceOp.SUM)
+            e_bytes = float(tb[0].item())
+        e2e = {"value": e_bytes / (e_ms / args.steps * 1e-3) / 1e9, "unit": "GB/s",
+               "h2d_bytes_per_step": int((q_host.numel() + kv_host.numel()) * 2) * world,
+               "d2h_bytes_per_step": int(out_host.numel() * 2) * world,
+               "ms_per_step": e_ms / args.steps,
+               "path": "pinned host q/k/v -> mslim_cuda_rope_append_decode_paged -> mslim_cuda_decode_paged "
+                       "-> host output, stream synchronised every step"}
+        if m.device_status(local) != 0:
+            raise SystemExit("device status reported an error during the e2e leg")
+
+    if rank != 0:
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+
+    peaks = measured_peaks()
+    achieved = step_bytes / (launch_ms * 1e-3) / 1e9
+    traffic = profile_traffic("decode_c4_traffic.json")
+    roofline = {"bound": "hbm", "kernel": "mslim_decode_split + mslim_decode_merge",
+                "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"] if peaks["hbm_gbs"] else None,
+                "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)" if peaks["source"] == "measured"
+                else "fallback 6650 GB/s",
+                "traffic": (traffic["dram_bytes_per_launch_scaled"] if traffic and n_seq == 64 else None),
+                "algorithmic_bytes_per_launch": step_bytes}
+    cpu = None
+    if not args.no_cpu and world == 1:
+        cpu = cpu_sample_gbs(lengths[:4], args.cpu_seconds)
+    line = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": args.scaling, "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) bf16 K/V/Q; no dataset)",
+            "config": {"workload": "C4 batched long-context decode: sessions with L ~ U[4096,32768] (seed 3), "
+                                   "256-token ColdStore-exact pages in a random physical permutation, "
+                                   "QH 32 / KVH 8 / D 128, one query per session",
+                       "sessions_per_gpu": n_seq, "global_sessions": total_seq, "page_tokens": PAGE,
+                       "split_tokens": args.split_tokens or "policy",
+                       "l2": "no flush: inputs larger than L2 (%.2f GB per GPU per step)" % (step_bytes / 1e9),
+                       "parallelism": f"session-sharded x{world} ({args.scaling})"},
+            "tokens_per_s": total_seq / (ms_per_step * 1e-3),
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": 2 * args.steps, "clocks": clocks, "device_status": status}
+    print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,267 @@
+/*
+ * mslim_cuda.h -- C ABI of the B200 (sm_100a) attention hot path for M-SLIM.
+ *
+ * The Rust host side of M-SLIM keeps its attention-kernel / backend API and
+ * calls these functions through `extern "C"`; every entry point names the
+ * reference interface it replaces (paths inside sheilyneural-afk/VK-SHEI).
+ *
+ * Conventions (modelled on native/hipblaslt_bridge.cpp:25-38,155-160):
+ *   - every function returns an int status, MSLIM_OK (0) on success;
+ *   - the message of the last failure on the calling thread is returned by
+ *     mslim_cuda_last_error() (thread-local, valid until the next call);
+ *   - device pointers are owned by the caller; no function allocates device
+ *     memory per call.  Scratch is passed in (workspace) or owned by a plan
+ *     created once, like TiledAttention::build owns its split partials
+ *     (src/gpu_llm/tiled_attention.rs:127-129);
+ *   - work is enqueued on the caller's stream (`stream` is a cudaStream_t,
+ *     NULL = legacy default stream); no host synchronisation inside decode;
+ *   - inputs are read-only and must not alias the output
+ *     (src/gpu_llm/tiled_attention.rs:204-207).
+ *
+ * Data formats: "bf16" is raw little-endian uint16 bits.  K/V are either
+ * token-major [tokens][kv_heads][head_dim] (the reference's dense GPU caches,
+ * src/gpu_llm/mod.rs:2099-2116) or ColdStore-exact pages, head-major
+ * [kv_heads][page_tokens][head_dim] per page (src/cold_store.rs:725-742,
+ * src/gpu_region_store.rs:470-483), addressed through a device page table.
+ */
+#ifndef MSLIM_CUDA_H
+#define MSLIM_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  1..5 map one-to-one onto PortableError (src/portable.rs:39-59);
+ * 6 is the anyhow error of AttentionKernelConfig::validate
+ * (src/attention_kernel.rs:43-79); 7 is a device-side wait that hit its
+ * bound (the kernel recorded it and returned; see mslim_cuda_device_status). */
+#define MSLIM_OK 0
+#define MSLIM_ERR_INVALID_GEOMETRY 1
+#define MSLIM_ERR_SHAPE_MISMATCH 2
+#define MSLIM_ERR_NON_FINITE 3
+#define MSLIM_ERR_UNSUPPORTED_DEVICE 4
+#define MSLIM_ERR_BACKEND_FAILURE 5
+#define MSLIM_ERR_INVALID_CONFIG 6
+#define MSLIM_ERR_DEVICE_TIMEOUT 7
+
+/* AttentionGeometry, src/portable.rs:413-457. */
+typedef struct {
+    uint32_t query_heads;
+    uint32_t kv_heads;
+    uint32_t head_dim;
+} mslim_geometry_t;
+
+/* AttentionKernelMode, src/attention_kernel.rs:8-14 (serde snake_case names:
+ * "reference", "strict_tiled", "online_experimental", "split_kv_experimental"). */
+#define MSLIM_MODE_REFERENCE 0
+#define MSLIM_MODE_STRICT_TILED 1
+#define MSLIM_MODE_ONLINE_EXPERIMENTAL 2
+#define MSLIM_MODE_SPLIT_KV_EXPERIMENTAL 3
+
+/* AttentionKernelConfig, src/attention_kernel.rs:18-34 (same fields, same
+ * defaults: mode reference, block_queries 1, block_keys 64, work_group 64,
+ * splits 1). */
+typedef struct {
+    int32_t mode;
+    uint32_t block_queries;
+    uint32_t block_keys;
+    uint32_t work_group;
+    uint32_t splits;
+} mslim_kernel_config_t;
+
+/* RopeKernelConfig, src/gpu_llm/kernels.rs:16-47. */
+typedef struct {
+    float theta;
+    uint32_t llama3_scaling;
+    float factor;
+    float low_freq_factor;
+    float high_freq_factor;
+    float original_max_position;
+} mslim_rope_config_t;
+
+/* ------------------------------------------------------------ errors -- */
+
+/* Thread-local message of the last failure (hipblaslt_bridge.cpp:157-159). */
+const char *mslim_cuda_last_error(void);
+
+/* Reads (and with reset != 0 clears) the device status word that kernels set
+ * when a bounded device-side wait gives up (*status = MSLIM_ERR_DEVICE_TIMEOUT,
+ * same return code) or a page-table entry lies outside the page pool
+ * (*status = MSLIM_ERR_SHAPE_MISMATCH, same return code, nothing written);
+ * synchronises `device`.  No reference counterpart: the
+ * reference relies on the OpenCL queue timeout (docs/validation/
+ * tiled-attention.json:790-796). */
+int mslim_cuda_device_status(int device, int reset, int *status);
+
+/* ------------------------------------------- configuration contract -- */
+
+/* AttentionGeometry::new (src/portable.rs:421-443). */
+int mslim_cuda_geometry_validate(const mslim_geometry_t *geometry);
+
+/* AttentionKernelConfig::default (src/attention_kernel.rs:25-35). */
+mslim_kernel_config_t mslim_cuda_config_default(void);
+
+/* AttentionKernelConfig::validate / validate_activation
+ * (src/attention_kernel.rs:43-79,93-100).  allow_experimental < 0 runs
+ * validate() only. */
+int mslim_cuda_config_validate(const mslim_kernel_config_t *config, int allow_experimental);
+
+/* AttentionKernelConfig::id (src/attention_kernel.rs:101-110); writes a NUL
+ * terminated string of at most len bytes. */
+int mslim_cuda_config_id(const mslim_kernel_config_t *config, char *out, size_t len);
+
+/* AttentionKernelConfig::local_bytes / decode_scratch_bytes
+ * (src/attention_kernel.rs:113-138). */
+int mslim_cuda_config_local_bytes(const mslim_kernel_config_t *config, uint32_t head_dim,
+                                  size_t *bytes);
+int mslim_cuda_config_decode_scratch_bytes(const mslim_kernel_config_t *config, uint32_t heads,
+                                           uint32_t head_dim, size_t *bytes);
+
+/* ---------------------------------------------- attention plan (L3) -- */
+
+typedef struct mslim_plan mslim_plan_t;
+
+/* TiledAttention::build (src/gpu_llm/tiled_attention.rs:39-145): validates
+ * config and geometry, checks the device is sm_100, and allocates the plan's
+ * split scratch once on `device`.  Every mode runs the same B200 numeric
+ * contract (split-KV online softmax with a fixed-order combine). */
+int mslim_cuda_plan_build(const mslim_kernel_config_t *config, const mslim_geometry_t *geometry,
+                          int device, mslim_plan_t **plan);
+void mslim_cuda_plan_destroy(mslim_plan_t *plan);
+
+/* TiledAttention::run (src/gpu_llm/tiled_attention.rs:161-293): `queries`
+ * new query rows at positions prior..prior+queries attend causally to keys
+ * 0..=prior+row.  q/out: bf16 [queries][QH][D]; k/v: bf16 token-major
+ * [prior+queries][KVH][D].  The *_bytes arguments are the allocation sizes
+ * (checked like Buffer::size() at tiled_attention.rs:198-203). */
+int mslim_cuda_plan_run(mslim_plan_t *plan, const void *q, size_t q_bytes, const void *k,
+                        size_t k_bytes, const void *v, size_t v_bytes, void *out,
+                        size_t out_bytes, uint32_t queries, uint32_t prior, void *stream);
+
+/* TiledAttention::diagnostics (src/gpu_llm/tiled_attention.rs:147-158):
+ * JSON with the same keys. */
+int mslim_cuda_plan_diagnostics(const mslim_plan_t *plan, char *out, size_t len);
+
+/* ------------------------------------------------- decode attention -- */
+
+/* Bytes of split scratch that mslim_cuda_decode_* need for n_seq sequences
+ * of at most max_tokens tokens split every split_tokens tokens
+ * (split_tokens 0 = library policy).  Counterpart of
+ * AttentionKernelConfig::decode_scratch_bytes (src/attention_kernel.rs:124-138). */
+int mslim_cuda_decode_workspace_bytes(const mslim_geometry_t *geometry, uint32_t n_seq,
+                                      uint32_t max_tokens, uint32_t split_tokens, size_t *bytes);
+
+/* Dense decode: GpuEngine::attention / exact_hot_fused_attention
+ * (src/gpu_llm/gpu_resources.rs:583-643,783-828) for a batch of sequences.
+ * q: bf16 [n_seq][QH][D] (post-RoPE); k_cache/v_cache: bf16 token-major
+ * [n_seq][max_tokens][KVH][D]; seq_tokens: device int32 [n_seq], each in
+ * 0..=max_tokens; out: bf16 [n_seq][QH][D].  A sequence with 0 tokens gives
+ * zeros.  workspace: >= mslim_cuda_decode_workspace_bytes, 16-byte aligned. */
+int mslim_cuda_decode_dense(const mslim_geometry_t *geometry, const void *q, const void *k_cache,
+                            const void *v_cache, const int32_t *seq_tokens, uint32_t n_seq,
+                            uint32_t max_tokens, uint32_t split_tokens, void *workspace,
+                            size_t workspace_bytes, void *out, void *stream);
+
+/* Paged decode over ColdStore-exact pages: the device-resident replacement of
+ * GpuEngine::attention_gpu_region (src/gpu_llm/gpu_resources.rs:883-1063),
+ * which staged V from the ColdStore through the host.  k_pool/v_pool: bf16
+ * [n_pages][KVH][page_tokens][D]; page_table: device int32
+ * [n_seq][max_pages_per_seq] of physical page ids; seq_tokens: device int32
+ * [n_seq].  page_tokens must be a multiple of 64.  Results are bit-identical
+ * to mslim_cuda_decode_dense on the same K/V bytes. */
+int mslim_cuda_decode_paged(const mslim_geometry_t *geometry, const void *q, const void *k_pool,
+                            const void *v_pool, uint32_t n_pages, uint32_t page_tokens,
+                            const int32_t *page_table, uint32_t max_pages_per_seq,
+                            const int32_t *seq_tokens, uint32_t n_seq, uint32_t split_tokens,
+                            void *workspace, size_t workspace_bytes, void *out, void *stream);
+
+/* ------------------------------------------------ prefill attention -- */
+
+/* BatchKernels::attention (src/gpu_llm/prefill.rs:363-435): chunked causal
+ * prefill, tcgen05/TMEM tensor cores.  q/out: bf16 [queries][QH][D];
+ * k/v: bf16 token-major [prior+queries][KVH][D]. */
+int mslim_cuda_prefill_causal(const mslim_geometry_t *geometry, const void *q, const void *k,
+                              const void *v, void *out, uint32_t queries, uint32_t prior,
+                              void *stream);
+
+/* ------------------------------------------------------ prologue -- */
+
+/* GpuEngine::norm / BatchKernels::norm (src/gpu_llm/gpu_resources.rs:485-507,
+ * src/gpu_llm/prefill.rs:292-320): per token y = bf16(bf16(x*s)*w),
+ * s = 1/sqrt(mean(x^2)+eps).  x/y: bf16 [tokens][hidden]; w: bf16 [hidden]. */
+int mslim_cuda_rmsnorm(const void *x, const void *w, void *y, uint32_t tokens, uint32_t hidden,
+                       float eps, void *stream);
+
+/* GpuEngine::rope / BatchKernels::rope (src/gpu_llm/gpu_resources.rs:509-537,
+ * src/gpu_llm/prefill.rs:322-361): rotate_half RoPE of bf16
+ * [tokens][heads][head_dim], row t at position start_position+t. */
+int mslim_cuda_rope(const void *in, void *out, uint32_t tokens, uint32_t heads, uint32_t head_dim,
+                    uint32_t start_position, const mslim_rope_config_t *rope, void *stream);
+
+/* RoPE of new q/k rows fused with the K/V append into ColdStore-exact pages:
+ * replaces rope(q), rope(k) + the K/V copies of run_layer
+ * (src/gpu_llm/mod.rs:2099-2116) and the host transpose of
+ * GpuRegionStore::append_batch (src/gpu_region_store.rs:470-483).
+ * q_in/q_out: bf16 [tokens][QH][D]; k_in/v_in: bf16 [tokens][KVH][D]; row t is
+ * token position start_position+t of one sequence whose page ids are
+ * page_table[0..]. */
+int mslim_cuda_rope_append_paged(const mslim_geometry_t *geometry, const void *q_in, void *q_out,
+                                 const void *k_in, const void *v_in, uint32_t tokens,
+                                 uint32_t start_position, const mslim_rope_config_t *rope,
+                                 void *k_pool, void *v_pool, uint32_t n_pages, uint32_t page_tokens,
+                                 const int32_t *page_table, uint32_t max_pages, void *stream);
+
+/* Decode-step form of the fused append for a batch of sessions, one new token
+ * each: session s appends its token at position positions[s] (device int32,
+ * usually its current length) into the pages page_table[s][..].  Replaces, per
+ * session, rope(q) + rope(k) + the K/V copies of run_layer
+ * (src/gpu_llm/mod.rs:2099-2116).  q_in/q_out: bf16 [n_seq][QH][D];
+ * k_in/v_in: bf16 [n_seq][KVH][D].  A position beyond the page table or a page
+ * id outside the pool writes nothing and is reported by
+ * mslim_cuda_device_status. */
+int mslim_cuda_rope_append_decode_paged(const mslim_geometry_t *geometry, const void *q_in,
+                                        void *q_out, const void *k_in, const void *v_in,
+                                        const int32_t *positions, uint32_t n_seq,
+                                        const mslim_rope_config_t *rope, void *k_pool,
+                                        void *v_pool, uint32_t n_pages, uint32_t page_tokens,
+                                        const int32_t *page_table, uint32_t max_pages,
+                                        void *stream);
+
+/* ------------------------------------------- isolated backend (L3) -- */
+
+typedef struct mslim_backend mslim_backend_t;
+
+/* GpuBackend::new (src/gpu_backend.rs:56-140): selects `device` (it must be
+ * an sm_100 GPU, else MSLIM_ERR_UNSUPPORTED_DEVICE) and creates the backend's
+ * stream.  Device buffers are grown on demand and reused across calls. */
+int mslim_cuda_backend_create(int device, mslim_backend_t **backend);
+void mslim_cuda_backend_destroy(mslim_backend_t *backend);
+
+/* AttentionBackend::decode as GpuBackend implements it
+ * (src/gpu_backend.rs:149-377): host query f32 [QH*D] (any finite f32; it is
+ * carried as a bf16 hi + lo pair), host K/V frames concatenated token-major
+ * [tokens][KVH][D] of dtype 1 = bf16 (2 = f16 and 3 = f32 return
+ * MSLIM_ERR_UNSUPPORTED_DEVICE: the B200 path is a bf16 path), host output
+ * f32 [QH*D].  Uploads, runs the dense decode, reads back and synchronises,
+ * like the reference's blocking dispatch.  tokens == 0 gives zeros; a
+ * non-finite query or output gives MSLIM_ERR_NON_FINITE. */
+int mslim_cuda_backend_decode(mslim_backend_t *backend, const mslim_geometry_t *geometry,
+                              const float *query_host, const void *keys_host,
+                              const void *values_host, int dtype, uint32_t tokens,
+                              float *out_host);
+
+/* GpuBackend::last_timings (src/gpu_backend.rs:142-147, GpuTimings :34-44)
+ * as JSON: dispatch_ms, kernel_ms, input_kv_bytes, scratch_bytes,
+ * output_bytes. */
+int mslim_cuda_backend_last_timings(const mslim_backend_t *backend, char *out, size_t len);
+
+/* Library version string (for diagnostics). */
+const char *mslim_cuda_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MSLIM_CUDA_H */

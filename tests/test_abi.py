@@ -1,0 +1,126 @@
+"""CPU tests of the C ABI: the library loads, exports every symbol the header
+declares, and its host-side contract checks match the reference's rules
+(src/attention_kernel.rs:141-206, src/portable.rs:806-825)."""
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "mslim_cuda.h")
+
+
+def header_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(mslim_cuda_\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def m():
+    import mslim_b200
+    mslim_b200.load()
+    return mslim_b200
+
+
+def test_library_exports_every_declared_symbol(m):
+    from mslim_b200 import _lib
+    L = _lib.lib()
+    declared = header_functions()
+    assert len(declared) >= 20
+    for name in declared:
+        assert hasattr(L, name), f"{name} declared in the header but not exported"
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+    assert sorted(_lib.SIGNATURES) == declared
+
+
+def test_static_archive_and_shared_library_built():
+    base = os.path.join(ROOT, "vk-shei_b200", "mslim_b200")
+    assert os.path.exists(os.path.join(base, "libmslim_cuda.so"))
+    assert os.path.exists(os.path.join(base, "libmslim_cuda.a"))
+
+
+def test_default_is_reference_and_experimental_opt_in_is_mandatory(m):
+    # src/attention_kernel.rs:145-158
+    assert m.AttentionKernelConfig.from_json("{}") == m.AttentionKernelConfig()
+    c = m.AttentionKernelConfig(mode=m.AttentionKernelMode.ONLINE_EXPERIMENTAL)
+    with pytest.raises(m.InvalidConfig):
+        c.validate_activation(False)
+    c.validate_activation(True)
+
+
+@pytest.mark.parametrize("kw", [
+    dict(work_group=0),
+    dict(block_keys=33),
+    dict(splits=2),
+    dict(mode="strict_tiled", splits=2),
+    dict(mode="split_kv_experimental", splits=65),
+    dict(mode="split_kv_experimental", splits=1),
+    dict(mode="split_kv_experimental", splits=8, block_queries=2),
+    dict(block_queries=3),
+    dict(block_queries=2),  # reference mode cannot carry tuning values
+])
+def test_reject_ignored_or_unbounded_configuration(m, kw):
+    # src/attention_kernel.rs:159-187
+    if "mode" in kw:
+        kw = dict(kw, mode=m.AttentionKernelMode(kw["mode"]))
+    with pytest.raises(m.InvalidConfig):
+        m.AttentionKernelConfig(**kw).validate()
+
+
+def test_unknown_fields_rejected(m):
+    with pytest.raises(m.InvalidConfig):
+        m.AttentionKernelConfig.from_json('{"epsilon":0.1}')
+    with pytest.raises(m.InvalidConfig):
+        m.AttentionKernelConfig.from_json('{"mode":"fast"}')
+
+
+def test_scratch_is_bounded_and_strict_has_no_global_scores(m):
+    # src/attention_kernel.rs:188-205
+    strict = m.AttentionKernelConfig(mode=m.AttentionKernelMode.STRICT_TILED)
+    assert strict.decode_scratch_bytes(32, 128) == 0
+    assert strict.local_bytes(128) < 64 * 1024
+    split = m.AttentionKernelConfig(mode=m.AttentionKernelMode.SPLIT_KV_EXPERIMENTAL, splits=8)
+    assert split.decode_scratch_bytes(32, 128) == 32 * 8 * 130 * 4
+    with pytest.raises(m.InvalidConfig):
+        split.decode_scratch_bytes(2 ** 40, 128)
+    with pytest.raises(m.InvalidConfig):
+        strict.local_bytes(257)
+
+
+def test_ids_follow_the_reference_format(m):
+    # src/attention_kernel.rs:101-110: Debug name of the mode, lower-cased.
+    assert m.AttentionKernelConfig().id() == "reference"
+    c = m.AttentionKernelConfig(mode=m.AttentionKernelMode.SPLIT_KV_EXPERIMENTAL, splits=8)
+    assert c.id() == "splitkvexperimental-q1-k64-wg64-s8"
+    c = m.AttentionKernelConfig(mode=m.AttentionKernelMode.ONLINE_EXPERIMENTAL, block_queries=2)
+    assert c.id() == "onlineexperimental-q2-k64-wg64-s1"
+
+
+def test_snapshot_contract(m):
+    # src/attention_kernel.rs:80-91
+    m.AttentionKernelConfig().check_snapshot(None)
+    strict = m.AttentionKernelConfig(mode=m.AttentionKernelMode.STRICT_TILED)
+    with pytest.raises(m.InvalidConfig):
+        strict.check_snapshot(None)
+    strict.check_snapshot({"mode": "strict_tiled"})
+
+
+def test_geometry_rules(m):
+    # src/portable.rs:421-443, :808
+    with pytest.raises(m.InvalidGeometry):
+        m.AttentionGeometry.new(3, 2, 32)
+    with pytest.raises(m.InvalidGeometry):
+        m.AttentionGeometry.new(0, 1, 8)
+    g = m.AttentionGeometry.new(32, 8, 128)
+    assert [g.kv_head_for_query(h) for h in (0, 3, 4, 31)] == [0, 0, 1, 7]
+    with pytest.raises(m.ShapeMismatch):
+        g.kv_head_for_query(32)
+
+
+def test_decode_workspace_bytes(m):
+    g = m.AttentionGeometry.new(32, 8, 128)
+    assert m.decode_workspace_bytes(g, 64, 32768, 2048) == 64 * 32 * 16 * 130 * 4
+    with pytest.raises(m.ShapeMismatch):
+        m.decode_workspace_bytes(g, 1, 100, 100)

@@ -1,0 +1,1075 @@
+// capi.cu -- the extern "C" boundary (include/mslim_cuda.h).
+//
+// Host-side validation mirrors the reference's checks before every dispatch
+// (src/portable.rs:421-443, src/attention_kernel.rs:43-138,
+// src/gpu_llm/tiled_attention.rs:161-235, src/gpu_backend.rs:149-207); the
+// error convention is an int status plus a thread-local message
+// (native/hipblaslt_bridge.cpp:25-38,155-160).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/mslim_cuda.h"
+#include "decode.cuh"
+#include "prefill.cuh"
+#include "prologue.cuh"
+
+// One status word per device; kernels record bounded-wait timeouts here.
+__device__ int g_mslim_status_word;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t err, const char *what) {
+    return fail(MSLIM_ERR_BACKEND_FAILURE, "%s: %s", what, cudaGetErrorString(err));
+}
+
+bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+constexpr int kMaxDevices = 64;
+std::mutex g_dev_mutex;
+int *g_status_ptr[kMaxDevices] = {};
+int g_dev_checked[kMaxDevices] = {};  // 0 unknown, 1 sm_100, -1 other
+
+// Current device, checked to be sm_100 (B200) once.
+int current_device(int *dev) {
+    cudaError_t err = cudaGetDevice(dev);
+    if (err != cudaSuccess) return cuda_fail(err, "no CUDA device");
+    if (*dev < 0 || *dev >= kMaxDevices) return fail(MSLIM_ERR_UNSUPPORTED_DEVICE, "device index %d", *dev);
+    std::lock_guard<std::mutex> lock(g_dev_mutex);
+    if (g_dev_checked[*dev] == 0) {
+        int major = 0, minor = 0;
+        cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, *dev);
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, *dev);
+        g_dev_checked[*dev] = (major == 10 && minor == 0) ? 1 : -1;
+        if (g_dev_checked[*dev] < 0) {
+            return fail(MSLIM_ERR_UNSUPPORTED_DEVICE,
+                        "no native kernel registered for compute capability %d.%d (needs sm_100)",
+                        major, minor);
+        }
+    }
+    if (g_dev_checked[*dev] < 0)
+        return fail(MSLIM_ERR_UNSUPPORTED_DEVICE, "no native kernel registered for this device");
+    return MSLIM_OK;
+}
+
+int *status_ptr(int dev) {
+    std::lock_guard<std::mutex> lock(g_dev_mutex);
+    if (!g_status_ptr[dev]) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_mslim_status_word) == cudaSuccess)
+            g_status_ptr[dev] = static_cast<int *>(p);
+    }
+    return g_status_ptr[dev];
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// bf16 tensor map with 128-byte swizzle; dims[0] innermost.
+int make_tmap(CUtensorMap *map, const void *base, int rank, const uint64_t *dims,
+              const uint64_t *strides_bytes, const uint32_t *box) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(MSLIM_ERR_BACKEND_FAILURE, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t gdim[5], gstr[4];
+    cuuint32_t bx[5], es[5];
+    for (int i = 0; i < rank; ++i) {
+        gdim[i] = dims[i];
+        bx[i] = box[i];
+        es[i] = 1;
+        if (i + 1 < rank) gstr[i] = strides_bytes[i];
+    }
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void *>(base), gdim,
+                    gstr, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(MSLIM_ERR_BACKEND_FAILURE, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return MSLIM_OK;
+}
+
+int check_geometry(const mslim_geometry_t *g) {
+    if (!g) return fail(MSLIM_ERR_INVALID_GEOMETRY, "geometry is null");
+    const uint64_t qh = g->query_heads, kvh = g->kv_heads, d = g->head_dim;
+    if (qh == 0 || kvh == 0 || d == 0 || qh % kvh != 0 || qh * d > 0xffffffffull ||
+        kvh * d > 0xffffffffull)
+        return fail(MSLIM_ERR_INVALID_GEOMETRY,
+                    "heads and dimension must be positive, q_heads divisible by kv_heads, "
+                    "products finite");
+    return MSLIM_OK;
+}
+
+bool kernel_head_dim(uint32_t d) { return d >= 8 && d <= 256 && d % 8 == 0; }
+
+// ------------------------------------------------------ decode plumbing --
+
+struct DecodeShapeInfo {
+    int group, head_chunks, heads_per_cta, q_per_cta, q_blocks;
+};
+
+int decode_shape(const mslim_geometry_t *g, uint32_t nq, DecodeShapeInfo *s) {
+    s->group = (int)(g->query_heads / g->kv_heads);
+    if (s->group <= 16) {
+        s->heads_per_cta = s->group;
+        s->head_chunks = 1;
+    } else if (s->group % 16 == 0) {
+        s->heads_per_cta = 16;
+        s->head_chunks = s->group / 16;
+    } else {
+        return fail(MSLIM_ERR_INVALID_GEOMETRY,
+                    "query heads per KV head above 16 must be a multiple of 16 (got %d)", s->group);
+    }
+    s->q_per_cta = std::max(1, std::min<int>((int)nq, 16 / s->heads_per_cta));
+    s->q_blocks = (int)((nq + s->q_per_cta - 1) / s->q_per_cta);
+    return MSLIM_OK;
+}
+
+// Split policy: aim for about eight waves of two CTAs per SM, with splits of
+// 64..2048 tokens (multiples of the 64-token TMA stage).
+uint32_t policy_split_tokens(uint64_t work_items, uint64_t max_tokens) {
+    const uint64_t target = 148ull * 2 * 8;
+    uint64_t st = (work_items * max_tokens + target - 1) / target;
+    st = (st + 63) / 64 * 64;
+    return (uint32_t)std::min<uint64_t>(std::max<uint64_t>(st, 64), 2048);
+}
+
+// The kernel runs at the next head_dim in {64, 128, 256}; the caller's
+// head_dim must be a multiple of 8 (16-byte TMA row strides) and at most 256.
+uint32_t kernel_dim_for(uint32_t d) { return d <= 64 ? 64 : d <= 128 ? 128 : 256; }
+
+uint64_t partial_bytes(const mslim_geometry_t *g, uint64_t n_seq, uint64_t nq, uint64_t splits) {
+    return n_seq * nq * g->query_heads * splits * (kernel_dim_for(g->head_dim) + 2) * sizeof(float);
+}
+
+struct DecodeCall {
+    const mslim_geometry_t *g;
+    const void *q;
+    const float *q_f32;
+    const void *k;
+    const void *v;
+    bool paged;
+    uint32_t n_pages, page_tokens;
+    const int32_t *page_table;
+    uint32_t max_pages;
+    const int32_t *seq_tokens;
+    int fixed_tokens;
+    uint32_t n_seq, nq, max_tokens;
+    uint32_t split_tokens;
+    void *workspace;
+    size_t workspace_bytes;
+    void *out;
+    float *out_f32;
+    float scale_log2;
+    uint32_t kernel_dim;  // head_dim the kernel runs at (>= g->head_dim)
+    cudaStream_t stream;
+};
+
+int run_decode(const DecodeCall &c) {
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    const mslim_geometry_t *g = c.g;
+    const uint32_t D = c.kernel_dim;
+    DecodeShapeInfo sh;
+    if (int rc = decode_shape(g, c.nq, &sh)) return rc;
+    if (c.split_tokens == 0 || c.split_tokens % 64 != 0)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "split_tokens must be a positive multiple of 64");
+    const uint64_t max_splits = (c.max_tokens + c.split_tokens - 1) / c.split_tokens;
+    if (max_splits == 0 || max_splits > 0x7fffffff)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "split count out of range");
+    const uint64_t need = partial_bytes(g, c.n_seq, c.nq, max_splits);
+    if (c.workspace_bytes < need || !c.workspace)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "workspace holds %zu bytes, needs %llu",
+                    c.workspace_bytes, (unsigned long long)need);
+    if ((uint64_t)g->kv_heads * sh.head_chunks > 65535 || (uint64_t)c.n_seq * sh.q_blocks > 65535)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "launch grid exceeds 65535 along y or z");
+    if (!aligned(c.k, 16) || !aligned(c.v, 16) || !aligned(c.workspace, 16) ||
+        (c.q && !aligned(c.q, 4)) || (c.q_f32 && !aligned(c.q_f32, 8)) || !aligned(c.out, 4))
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "K/V/workspace must be 16-byte aligned, Q/out 4-byte");
+    if (c.out == c.q || c.out == c.k || c.out == c.v)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "output must not alias read-only Q/K/V");
+
+    CUtensorMap kmap, vmap;
+    // Tensor maps describe the caller's head_dim (GD); the kernel runs at D >= GD
+    // and the TMA fills the columns past GD with zeros.
+    const uint64_t GD = g->head_dim;
+    if (c.paged) {
+        const uint64_t dims[3] = {GD, c.page_tokens, (uint64_t)c.n_pages * g->kv_heads};
+        const uint64_t str[2] = {GD * 2ull, (uint64_t)c.page_tokens * GD * 2};
+        const uint32_t box[3] = {64, 64, 1};
+        if (int rc = make_tmap(&kmap, c.k, 3, dims, str, box)) return rc;
+        if (int rc = make_tmap(&vmap, c.v, 3, dims, str, box)) return rc;
+    } else {
+        const uint64_t dims[4] = {GD, g->kv_heads, c.max_tokens, c.n_seq};
+        const uint64_t str[3] = {GD * 2ull, (uint64_t)g->kv_heads * GD * 2,
+                                 (uint64_t)c.max_tokens * g->kv_heads * GD * 2};
+        const uint32_t box[4] = {64, 1, 64, 1};
+        if (int rc = make_tmap(&kmap, c.k, 4, dims, str, box)) return rc;
+        if (int rc = make_tmap(&vmap, c.v, 4, dims, str, box)) return rc;
+    }
+    mslim::DecodeParams p{};
+    p.q = static_cast<const uint16_t *>(c.q);
+    p.q_f32 = c.q_f32;
+    p.seq_tokens = c.seq_tokens;
+    p.page_table = c.page_table;
+    p.partials = static_cast<float *>(c.workspace);
+    p.status = status_ptr(dev);
+    p.qheads = (int)g->query_heads;
+    p.kvheads = (int)g->kv_heads;
+    p.group = sh.group;
+    p.head_chunks = sh.head_chunks;
+    p.heads_per_cta = sh.heads_per_cta;
+    p.nq = (int)c.nq;
+    p.q_per_cta = sh.q_per_cta;
+    p.q_blocks = sh.q_blocks;
+    p.split_tokens = (int)c.split_tokens;
+    p.max_splits = (int)max_splits;
+    p.page_tokens = (int)c.page_tokens;
+    p.max_pages = (int)c.max_pages;
+    p.n_seq = (int)c.n_seq;
+    p.head_dim = (int)g->head_dim;
+    p.token_cap = c.paged ? (int)std::min<uint64_t>((uint64_t)c.max_pages * c.page_tokens, 0x7fffffff)
+                          : (int)c.max_tokens;
+    p.fixed_tokens = c.fixed_tokens;
+    p.scale_log2 = c.scale_log2;
+    p.out_f32 = c.out_f32;
+    cudaError_t err = mslim::launch_decode((int)D, c.paged, kmap, vmap, p,
+                                           static_cast<uint16_t *>(c.out), c.stream);
+    if (err != cudaSuccess) return cuda_fail(err, "decode launch");
+    return MSLIM_OK;
+}
+
+float scale_log2_for(uint32_t head_dim) {
+    return (float)(1.4426950408889634 / std::sqrt((double)head_dim));
+}
+
+// ------------------------------------------------------------- RoPE ----
+
+int build_rope_table(const mslim_rope_config_t *rope, uint32_t dim, mslim::RopeTable *t) {
+    if (!rope) return fail(MSLIM_ERR_INVALID_CONFIG, "rope config is null");
+    if (!(std::isfinite(rope->theta) && rope->theta > 0.0f))
+        return fail(MSLIM_ERR_INVALID_CONFIG, "invalid RoPE theta");
+    if (dim == 0 || dim % 2 != 0 || dim > 256)
+        return fail(MSLIM_ERR_INVALID_GEOMETRY, "RoPE head_dim must be even and at most 256");
+    std::memset(t, 0, sizeof(*t));
+    const uint32_t half = dim / 2;
+    if (!rope->llama3_scaling) {
+        // CPU decoder formula (native_cpu_adapter.rs:211): theta^(2i/dim) in f32.
+        t->multiply = 0;
+        for (uint32_t i = 0; i < half; ++i)
+            t->freq[i] = powf(rope->theta, (float)(2 * i) / (float)dim);
+    } else {
+        // RopeKernelConfig::inverse_frequency (src/gpu_llm/kernels.rs:50-67).
+        t->multiply = 1;
+        for (uint32_t i = 0; i < half; ++i) {
+            float inv = expf(-(float)(2 * i) * logf(rope->theta) / (float)dim);
+            const float tau = 6.28318530717958647692f;
+            const float wavelength = tau / inv;
+            const float low_wavelength = rope->original_max_position / rope->low_freq_factor;
+            const float high_wavelength = rope->original_max_position / rope->high_freq_factor;
+            if (wavelength > low_wavelength) {
+                inv /= rope->factor;
+            } else if (wavelength >= high_wavelength) {
+                const float smooth = (rope->original_max_position / wavelength - rope->low_freq_factor) /
+                                     (rope->high_freq_factor - rope->low_freq_factor);
+                inv = (1.0f - smooth) * (inv / rope->factor) + smooth * inv;
+            }
+            t->freq[i] = inv;
+        }
+    }
+    return MSLIM_OK;
+}
+
+// IEEE binary16 -> binary32 (exact).
+float half_bits_to_float(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    uint32_t exp = (h >> 10) & 0x1fu, man = h & 0x3ffu, bits;
+    if (exp == 0x1f) {
+        bits = sign | 0x7f800000u | (man << 13);
+    } else if (exp == 0) {
+        if (man == 0) {
+            bits = sign;
+        } else {
+            int e = -1;
+            do { ++e; man <<= 1; } while ((man & 0x400u) == 0);
+            bits = sign | ((uint32_t)(127 - 15 - e) << 23) | ((man & 0x3ffu) << 13);
+        }
+    } else {
+        bits = sign | ((exp + 112u) << 23) | (man << 13);
+    }
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+const char *mode_debug_name(int32_t mode) {
+    switch (mode) {
+        case MSLIM_MODE_REFERENCE: return "Reference";
+        case MSLIM_MODE_STRICT_TILED: return "StrictTiled";
+        case MSLIM_MODE_ONLINE_EXPERIMENTAL: return "OnlineExperimental";
+        case MSLIM_MODE_SPLIT_KV_EXPERIMENTAL: return "SplitKvExperimental";
+        default: return nullptr;
+    }
+}
+
+const char *mode_serde_name(int32_t mode) {
+    switch (mode) {
+        case MSLIM_MODE_REFERENCE: return "reference";
+        case MSLIM_MODE_STRICT_TILED: return "strict_tiled";
+        case MSLIM_MODE_ONLINE_EXPERIMENTAL: return "online_experimental";
+        case MSLIM_MODE_SPLIT_KV_EXPERIMENTAL: return "split_kv_experimental";
+        default: return "invalid";
+    }
+}
+
+bool is_experimental(const mslim_kernel_config_t &c) {
+    return c.mode == MSLIM_MODE_ONLINE_EXPERIMENTAL || c.mode == MSLIM_MODE_SPLIT_KV_EXPERIMENTAL;
+}
+
+// Split scratch owned by a plan: the reference's split scratch bound.
+constexpr size_t kPlanScratchBytes = 16u << 20;
+
+}  // namespace
+
+struct mslim_plan {
+    mslim_kernel_config_t config;
+    mslim_geometry_t geometry;
+    int device;
+    void *scratch;
+    size_t scratch_bytes;
+    std::atomic<uint64_t> calls{0};
+    std::atomic<uint64_t> split_calls{0};
+    std::atomic<uint64_t> prefill_calls{0};
+};
+
+struct mslim_backend {
+    int device;
+    cudaStream_t stream;
+    void *buf;
+    size_t buf_bytes;
+    cudaEvent_t ev0, ev1;
+    double dispatch_ms, kernel_ms;
+    size_t input_kv_bytes, scratch_bytes, output_bytes;
+    bool have_timings;
+};
+
+extern "C" {
+
+const char *mslim_cuda_last_error(void) { return g_last_error.c_str(); }
+
+const char *mslim_cuda_version(void) { return "mslim-cuda 0.1.0 (sm_100a)"; }
+
+int mslim_cuda_device_status(int device, int reset, int *status) {
+    if (!status) return fail(MSLIM_ERR_SHAPE_MISMATCH, "status pointer is null");
+    int prev;
+    if (cudaGetDevice(&prev) != cudaSuccess) return fail(MSLIM_ERR_BACKEND_FAILURE, "no CUDA device");
+    if (cudaSetDevice(device) != cudaSuccess) return fail(MSLIM_ERR_UNSUPPORTED_DEVICE, "bad device %d", device);
+    int value = 0;
+    cudaError_t err = cudaDeviceSynchronize();
+    if (err == cudaSuccess) err = cudaMemcpyFromSymbol(&value, g_mslim_status_word, sizeof(int));
+    if (err == cudaSuccess && reset) {
+        const int zero = 0;
+        err = cudaMemcpyToSymbol(g_mslim_status_word, &zero, sizeof(int));
+    }
+    cudaSetDevice(prev);
+    if (err != cudaSuccess) return cuda_fail(err, "device status");
+    *status = value & 0xff;
+    if (*status == MSLIM_DEVICE_BAD_PAGE_CODE)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "a page table entry was outside the page pool");
+    if (value) {
+        return fail(MSLIM_ERR_DEVICE_TIMEOUT, "a device-side wait hit its bound (site %d)",
+                    value >> 8);
+    }
+    return MSLIM_OK;
+}
+
+int mslim_cuda_geometry_validate(const mslim_geometry_t *geometry) { return check_geometry(geometry); }
+
+mslim_kernel_config_t mslim_cuda_config_default(void) {
+    mslim_kernel_config_t c;
+    c.mode = MSLIM_MODE_REFERENCE;
+    c.block_queries = 1;
+    c.block_keys = 64;
+    c.work_group = 64;
+    c.splits = 1;
+    return c;
+}
+
+int mslim_cuda_config_validate(const mslim_kernel_config_t *config, int allow_experimental) {
+    if (!config) return fail(MSLIM_ERR_INVALID_CONFIG, "config is null");
+    const mslim_kernel_config_t c = *config;
+    if (!mode_debug_name(c.mode)) return fail(MSLIM_ERR_INVALID_CONFIG, "unknown attention mode %d", c.mode);
+    if (!(c.block_queries == 1 || c.block_queries == 2 || c.block_queries == 4))
+        return fail(MSLIM_ERR_INVALID_CONFIG, "attention block_queries must be 1,2,4");
+    if (!(c.block_keys == 32 || c.block_keys == 64 || c.block_keys == 128))
+        return fail(MSLIM_ERR_INVALID_CONFIG, "attention block_keys must be 32,64,128");
+    if (!(c.work_group == 32 || c.work_group == 64 || c.work_group == 128))
+        return fail(MSLIM_ERR_INVALID_CONFIG, "attention work_group must be 32,64,128");
+    if (c.splits < 1 || c.splits > 64)
+        return fail(MSLIM_ERR_INVALID_CONFIG, "attention splits must be 1..=64");
+    if (c.mode == MSLIM_MODE_SPLIT_KV_EXPERIMENTAL) {
+        if (!(c.block_queries == 1 && c.splits >= 2))
+            return fail(MSLIM_ERR_INVALID_CONFIG,
+                        "split-KV requires one query per group and at least two splits");
+    } else if (c.splits != 1) {
+        return fail(MSLIM_ERR_INVALID_CONFIG, "only explicit split-KV may request multiple splits");
+    }
+    if (c.mode == MSLIM_MODE_REFERENCE) {
+        const mslim_kernel_config_t d = mslim_cuda_config_default();
+        if (c.block_queries != d.block_queries || c.block_keys != d.block_keys ||
+            c.work_group != d.work_group || c.splits != d.splits)
+            return fail(MSLIM_ERR_INVALID_CONFIG, "reference attention cannot carry ignored tuning values");
+    }
+    if (allow_experimental >= 0 && is_experimental(c) && !allow_experimental)
+        return fail(MSLIM_ERR_INVALID_CONFIG,
+                    "experimental attention requires explicit numeric-contract opt-in");
+    return MSLIM_OK;
+}
+
+int mslim_cuda_config_id(const mslim_kernel_config_t *config, char *out, size_t len) {
+    if (int rc = mslim_cuda_config_validate(config, -1)) return rc;
+    if (!out || len == 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "output buffer is empty");
+    std::string id;
+    if (config->mode == MSLIM_MODE_REFERENCE) {
+        id = "reference";
+    } else {
+        char buf[128];
+        snprintf(buf, sizeof(buf), "%s-q%u-k%u-wg%u-s%u", mode_debug_name(config->mode),
+                 config->block_queries, config->block_keys, config->work_group, config->splits);
+        id = buf;
+        for (auto &ch : id) ch = (char)tolower((unsigned char)ch);
+    }
+    if (id.size() + 1 > len) return fail(MSLIM_ERR_SHAPE_MISMATCH, "output buffer too small");
+    memcpy(out, id.c_str(), id.size() + 1);
+    return MSLIM_OK;
+}
+
+int mslim_cuda_config_local_bytes(const mslim_kernel_config_t *config, uint32_t head_dim,
+                                  size_t *bytes) {
+    if (int rc = mslim_cuda_config_validate(config, -1)) return rc;
+    if (head_dim < 1 || head_dim > 256)
+        return fail(MSLIM_ERR_INVALID_CONFIG, "tiled attention head dimension must be 1..=256");
+    const size_t bk = config->block_keys, bq = config->block_queries;
+    *bytes = 2 * bk * head_dim + 2 * bq * head_dim + 4 * bq * bk + 4 * bq * 4;
+    return MSLIM_OK;
+}
+
+int mslim_cuda_config_decode_scratch_bytes(const mslim_kernel_config_t *config, uint32_t heads,
+                                           uint32_t head_dim, size_t *bytes) {
+    if (int rc = mslim_cuda_config_validate(config, -1)) return rc;
+    if (config->mode != MSLIM_MODE_SPLIT_KV_EXPERIMENTAL) {
+        *bytes = 0;
+        return MSLIM_OK;
+    }
+    const unsigned __int128 n =
+        (unsigned __int128)heads * config->splits * ((unsigned __int128)head_dim + 2) * 4;
+    if (n == 0 || n > (16u << 20))
+        return fail(MSLIM_ERR_INVALID_CONFIG, "split-KV scratch exceeds its 16 MiB bound or overflows");
+    *bytes = (size_t)n;
+    return MSLIM_OK;
+}
+
+// ------------------------------------------------------------ decode --
+
+int mslim_cuda_decode_workspace_bytes(const mslim_geometry_t *geometry, uint32_t n_seq,
+                                      uint32_t max_tokens, uint32_t split_tokens, size_t *bytes) {
+    if (int rc = check_geometry(geometry)) return rc;
+    if (!bytes) return fail(MSLIM_ERR_SHAPE_MISMATCH, "bytes pointer is null");
+    if (n_seq == 0 || max_tokens == 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty batch");
+    DecodeShapeInfo sh;
+    if (int rc = decode_shape(geometry, 1, &sh)) return rc;
+    if (split_tokens == 0)
+        split_tokens = policy_split_tokens((uint64_t)n_seq * geometry->kv_heads * sh.head_chunks,
+                                           max_tokens);
+    if (split_tokens % 64 != 0)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "split_tokens must be a multiple of 64");
+    const uint64_t splits = (max_tokens + split_tokens - 1) / split_tokens;
+    *bytes = partial_bytes(geometry, n_seq, 1, splits);
+    return MSLIM_OK;
+}
+
+static int decode_common_checks(const mslim_geometry_t *geometry, uint32_t n_seq,
+                                uint32_t *split_tokens, uint32_t max_tokens) {
+    if (int rc = check_geometry(geometry)) return rc;
+    if (!kernel_head_dim(geometry->head_dim))
+        return fail(MSLIM_ERR_INVALID_GEOMETRY,
+                    "head_dim %u has no sm_100a decode kernel (multiples of 8 up to 256)",
+                    geometry->head_dim);
+    if (n_seq == 0 || max_tokens == 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty batch");
+    DecodeShapeInfo sh;
+    if (int rc = decode_shape(geometry, 1, &sh)) return rc;
+    if (*split_tokens == 0)
+        *split_tokens = policy_split_tokens((uint64_t)n_seq * geometry->kv_heads * sh.head_chunks,
+                                            max_tokens);
+    return MSLIM_OK;
+}
+
+int mslim_cuda_decode_dense(const mslim_geometry_t *geometry, const void *q, const void *k_cache,
+                            const void *v_cache, const int32_t *seq_tokens, uint32_t n_seq,
+                            uint32_t max_tokens, uint32_t split_tokens, void *workspace,
+                            size_t workspace_bytes, void *out, void *stream) {
+    if (int rc = decode_common_checks(geometry, n_seq, &split_tokens, max_tokens)) return rc;
+    if (!q || !k_cache || !v_cache || !seq_tokens || !out)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
+    DecodeCall c{};
+    c.g = geometry;
+    c.q = q;
+    c.k = k_cache;
+    c.v = v_cache;
+    c.seq_tokens = seq_tokens;
+    c.fixed_tokens = -1;
+    c.n_seq = n_seq;
+    c.nq = 1;
+    c.max_tokens = max_tokens;
+    c.split_tokens = split_tokens;
+    c.workspace = workspace;
+    c.workspace_bytes = workspace_bytes;
+    c.out = out;
+    c.scale_log2 = scale_log2_for(geometry->head_dim);
+    c.kernel_dim = kernel_dim_for(geometry->head_dim);
+    c.stream = static_cast<cudaStream_t>(stream);
+    return run_decode(c);
+}
+
+int mslim_cuda_decode_paged(const mslim_geometry_t *geometry, const void *q, const void *k_pool,
+                            const void *v_pool, uint32_t n_pages, uint32_t page_tokens,
+                            const int32_t *page_table, uint32_t max_pages_per_seq,
+                            const int32_t *seq_tokens, uint32_t n_seq, uint32_t split_tokens,
+                            void *workspace, size_t workspace_bytes, void *out, void *stream) {
+    if (page_tokens == 0 || page_tokens % 64 != 0)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "page_tokens must be a positive multiple of 64");
+    if (n_pages == 0 || max_pages_per_seq == 0)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty page pool or page table");
+    const uint64_t max_tokens64 = (uint64_t)max_pages_per_seq * page_tokens;
+    if (max_tokens64 > 0x7fffffffull) return fail(MSLIM_ERR_SHAPE_MISMATCH, "page table spans too many tokens");
+    const uint32_t max_tokens = (uint32_t)max_tokens64;
+    if (int rc = decode_common_checks(geometry, n_seq, &split_tokens, max_tokens)) return rc;
+    if (!q || !k_pool || !v_pool || !page_table || !seq_tokens || !out)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
+    if ((uint64_t)n_pages * geometry->kv_heads > 0xffffffffull)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "page pool too large for a tensor map");
+    DecodeCall c{};
+    c.g = geometry;
+    c.q = q;
+    c.k = k_pool;
+    c.v = v_pool;
+    c.paged = true;
+    c.n_pages = n_pages;
+    c.page_tokens = page_tokens;
+    c.page_table = page_table;
+    c.max_pages = max_pages_per_seq;
+    c.seq_tokens = seq_tokens;
+    c.fixed_tokens = -1;
+    c.n_seq = n_seq;
+    c.nq = 1;
+    c.max_tokens = max_tokens;
+    c.split_tokens = split_tokens;
+    c.workspace = workspace;
+    c.workspace_bytes = workspace_bytes;
+    c.out = out;
+    c.scale_log2 = scale_log2_for(geometry->head_dim);
+    c.kernel_dim = kernel_dim_for(geometry->head_dim);
+    c.stream = static_cast<cudaStream_t>(stream);
+    return run_decode(c);
+}
+
+// ----------------------------------------------------------- prefill --
+
+int mslim_cuda_prefill_causal(const mslim_geometry_t *geometry, const void *q, const void *k,
+                              const void *v, void *out, uint32_t queries, uint32_t prior,
+                              void *stream) {
+    if (int rc = check_geometry(geometry)) return rc;
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    if (!q || !k || !v || !out) return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
+    if (queries == 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "prefill needs at least one query");
+    const uint64_t history = (uint64_t)prior + queries;
+    if (history > 0x7fffffffull) return fail(MSLIM_ERR_SHAPE_MISMATCH, "history exceeds indexing bound");
+    if (out == q || out == k || out == v)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "output must not alias read-only Q/K/V");
+    if (!mslim::prefill_supported(geometry->head_dim, geometry->query_heads / geometry->kv_heads))
+        return fail(MSLIM_ERR_INVALID_GEOMETRY, "head_dim %u has no sm_100a prefill kernel (128)",
+                    geometry->head_dim);
+    if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(out, 16))
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "prefill buffers must be 16-byte aligned");
+    int rc = mslim::launch_prefill(geometry->query_heads, geometry->kv_heads, geometry->head_dim,
+                                   static_cast<const uint16_t *>(q), static_cast<const uint16_t *>(k),
+                                   static_cast<const uint16_t *>(v), static_cast<uint16_t *>(out),
+                                   queries, prior, scale_log2_for(geometry->head_dim),
+                                   status_ptr(dev), static_cast<cudaStream_t>(stream),
+                                   &g_last_error);
+    return rc;
+}
+
+// ---------------------------------------------------------- prologue --
+
+int mslim_cuda_rmsnorm(const void *x, const void *w, void *y, uint32_t tokens, uint32_t hidden,
+                       float eps, void *stream) {
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    if (!x || !w || !y) return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
+    if (tokens == 0 || hidden == 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty RMSNorm");
+    if (!std::isfinite(eps) || eps < 0.f) return fail(MSLIM_ERR_INVALID_CONFIG, "invalid epsilon");
+    if (hidden % 8 == 0 && (!aligned(x, 16) || !aligned(w, 16) || !aligned(y, 16)))
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "RMSNorm buffers must be 16-byte aligned");
+    if (tokens > 0x7fffffffu) return fail(MSLIM_ERR_SHAPE_MISMATCH, "too many tokens");
+    cudaError_t err = mslim::launch_rmsnorm(static_cast<const uint16_t *>(x),
+                                            static_cast<const uint16_t *>(w),
+                                            static_cast<uint16_t *>(y), tokens, hidden, eps,
+                                            static_cast<cudaStream_t>(stream));
+    return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "RMSNorm launch");
+}
+
+int mslim_cuda_rope(const void *in, void *out, uint32_t tokens, uint32_t heads, uint32_t head_dim,
+                    uint32_t start_position, const mslim_rope_config_t *rope, void *stream) {
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    if (!in || !out) return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
+    if (tokens == 0 || heads == 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty RoPE");
+    if ((uint64_t)start_position + tokens > 0xffffffffull)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "RoPE position overflow");
+    mslim::RopeTable table;
+    if (int rc = build_rope_table(rope, head_dim, &table)) return rc;
+    cudaError_t err = mslim::launch_rope(static_cast<const uint16_t *>(in),
+                                         static_cast<uint16_t *>(out), tokens, heads, head_dim,
+                                         start_position, table, static_cast<cudaStream_t>(stream));
+    return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "RoPE launch");
+}
+
+int mslim_cuda_rope_append_paged(const mslim_geometry_t *geometry, const void *q_in, void *q_out,
+                                 const void *k_in, const void *v_in, uint32_t tokens,
+                                 uint32_t start_position, const mslim_rope_config_t *rope,
+                                 void *k_pool, void *v_pool, uint32_t n_pages, uint32_t page_tokens,
+                                 const int32_t *page_table, uint32_t max_pages, void *stream) {
+    if (int rc = check_geometry(geometry)) return rc;
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    if (!q_in || !q_out || !k_in || !v_in || !k_pool || !v_pool || !page_table)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
+    if (tokens == 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty append");
+    if (page_tokens == 0 || n_pages == 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty page pool");
+    if ((uint64_t)start_position + tokens > (uint64_t)max_pages * page_tokens)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "append past the end of the page table");
+    mslim::RopeTable table;
+    if (int rc = build_rope_table(rope, geometry->head_dim, &table)) return rc;
+    cudaError_t err = mslim::launch_rope_append_paged(
+        static_cast<const uint16_t *>(q_in), static_cast<uint16_t *>(q_out),
+        static_cast<const uint16_t *>(k_in), static_cast<const uint16_t *>(v_in), tokens,
+        geometry->query_heads, geometry->kv_heads, geometry->head_dim, start_position, nullptr,
+        static_cast<uint16_t *>(k_pool), static_cast<uint16_t *>(v_pool), n_pages, page_tokens,
+        page_table, max_pages, table, status_ptr(dev), static_cast<cudaStream_t>(stream));
+    return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "RoPE append launch");
+}
+
+int mslim_cuda_rope_append_decode_paged(const mslim_geometry_t *geometry, const void *q_in,
+                                        void *q_out, const void *k_in, const void *v_in,
+                                        const int32_t *positions, uint32_t n_seq,
+                                        const mslim_rope_config_t *rope, void *k_pool,
+                                        void *v_pool, uint32_t n_pages, uint32_t page_tokens,
+                                        const int32_t *page_table, uint32_t max_pages,
+                                        void *stream) {
+    if (int rc = check_geometry(geometry)) return rc;
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    if (!q_in || !q_out || !k_in || !v_in || !positions || !k_pool || !v_pool || !page_table)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
+    if (n_seq == 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty batch");
+    if (page_tokens == 0 || n_pages == 0 || max_pages == 0)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty page pool");
+    if (n_seq > 0x7fffffffu) return fail(MSLIM_ERR_SHAPE_MISMATCH, "too many sessions");
+    mslim::RopeTable table;
+    if (int rc = build_rope_table(rope, geometry->head_dim, &table)) return rc;
+    cudaError_t err = mslim::launch_rope_append_paged(
+        static_cast<const uint16_t *>(q_in), static_cast<uint16_t *>(q_out),
+        static_cast<const uint16_t *>(k_in), static_cast<const uint16_t *>(v_in), n_seq,
+        geometry->query_heads, geometry->kv_heads, geometry->head_dim, 0, positions,
+        static_cast<uint16_t *>(k_pool), static_cast<uint16_t *>(v_pool), n_pages, page_tokens,
+        page_table, max_pages, table, status_ptr(dev), static_cast<cudaStream_t>(stream));
+    return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "RoPE decode append launch");
+}
+
+// -------------------------------------------------------------- plan --
+
+int mslim_cuda_plan_build(const mslim_kernel_config_t *config, const mslim_geometry_t *geometry,
+                          int device, mslim_plan_t **plan) {
+    if (!plan) return fail(MSLIM_ERR_SHAPE_MISMATCH, "plan pointer is null");
+    *plan = nullptr;
+    if (int rc = mslim_cuda_config_validate(config, -1)) return rc;
+    if (int rc = check_geometry(geometry)) return rc;
+    if (config->mode == MSLIM_MODE_REFERENCE)
+        return fail(MSLIM_ERR_INVALID_CONFIG, "reference does not compile tiled kernels");
+    size_t local = 0;
+    if (int rc = mslim_cuda_config_local_bytes(config, geometry->head_dim, &local)) return rc;
+    if (!kernel_head_dim(geometry->head_dim))
+        return fail(MSLIM_ERR_INVALID_GEOMETRY,
+                    "head_dim %u has no sm_100a kernel (multiples of 8 up to 256)",
+                    geometry->head_dim);
+    DecodeShapeInfo sh;
+    if (int rc = decode_shape(geometry, 1, &sh)) return rc;
+    int prev;
+    if (cudaGetDevice(&prev) != cudaSuccess) return fail(MSLIM_ERR_BACKEND_FAILURE, "no CUDA device");
+    if (cudaSetDevice(device) != cudaSuccess) return fail(MSLIM_ERR_UNSUPPORTED_DEVICE, "bad device %d", device);
+    int dev;
+    int rc = current_device(&dev);
+    void *scratch = nullptr;
+    if (rc == MSLIM_OK) {
+        cudaError_t err = cudaMalloc(&scratch, kPlanScratchBytes);
+        if (err != cudaSuccess) rc = cuda_fail(err, "allocate plan split scratch");
+    }
+    cudaSetDevice(prev);
+    if (rc) return rc;
+    mslim_plan *p = new mslim_plan();
+    p->config = *config;
+    p->geometry = *geometry;
+    p->device = device;
+    p->scratch = scratch;
+    p->scratch_bytes = kPlanScratchBytes;
+    *plan = p;
+    return MSLIM_OK;
+}
+
+void mslim_cuda_plan_destroy(mslim_plan_t *plan) {
+    if (!plan) return;
+    int prev;
+    if (cudaGetDevice(&prev) == cudaSuccess) {
+        cudaSetDevice(plan->device);
+        cudaFree(plan->scratch);
+        cudaSetDevice(prev);
+    }
+    delete plan;
+}
+
+int mslim_cuda_plan_run(mslim_plan_t *plan, const void *q, size_t q_bytes, const void *k,
+                        size_t k_bytes, const void *v, size_t v_bytes, void *out,
+                        size_t out_bytes, uint32_t queries, uint32_t prior, void *stream) {
+    if (!plan) return fail(MSLIM_ERR_SHAPE_MISMATCH, "plan is null");
+    const mslim_geometry_t *g = &plan->geometry;
+    if (queries == 0 || queries > 512) return fail(MSLIM_ERR_SHAPE_MISMATCH, "attention query count must be 1..=512");
+    const uint64_t history = (uint64_t)prior + queries;
+    if (history > 0xffffffffull - 64 || history > 0x7fffffffull)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "attention history exceeds indexing bound");
+    const uint64_t qbytes = (uint64_t)queries * g->query_heads * g->head_dim * 2;
+    const uint64_t kvbytes = history * g->kv_heads * g->head_dim * 2;
+    if (q_bytes < qbytes || out_bytes < qbytes || k_bytes < kvbytes || v_bytes < kvbytes)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "tiled attention buffer is smaller than its declared geometry");
+    if (out == q || out == k || out == v)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "tiled attention output must not alias read-only Q/K/V");
+    int prev;
+    if (cudaGetDevice(&prev) != cudaSuccess) return fail(MSLIM_ERR_BACKEND_FAILURE, "no CUDA device");
+    if (prev != plan->device) return fail(MSLIM_ERR_UNSUPPORTED_DEVICE, "plan belongs to device %d", plan->device);
+    int rc;
+    if (queries >= mslim::kPrefillMinQueries && mslim::prefill_supported(g->head_dim, g->query_heads / g->kv_heads)) {
+        rc = mslim_cuda_prefill_causal(g, q, k, v, out, queries, prior, stream);
+        if (rc == MSLIM_OK) plan->prefill_calls++;
+    } else {
+        DecodeShapeInfo sh;
+        if ((rc = decode_shape(g, queries, &sh))) return rc;
+        uint32_t st;
+        if (plan->config.mode == MSLIM_MODE_SPLIT_KV_EXPERIMENTAL && queries == 1) {
+            // tiled_attention.rs:208-213: splits = min(configured splits, history).
+            const uint64_t splits = std::min<uint64_t>(plan->config.splits, history);
+            st = (uint32_t)(((history + splits - 1) / splits + 63) / 64 * 64);
+        } else {
+            st = policy_split_tokens((uint64_t)sh.q_blocks * g->kv_heads * sh.head_chunks, history);
+        }
+        // Keep the partials inside the plan's scratch.
+        while (partial_bytes(g, 1, queries, (history + st - 1) / st) > plan->scratch_bytes) st *= 2;
+        DecodeCall c{};
+        c.g = g;
+        c.q = q;
+        c.k = k;
+        c.v = v;
+        c.fixed_tokens = (int)history;
+        c.n_seq = 1;
+        c.nq = queries;
+        c.max_tokens = (uint32_t)history;
+        c.split_tokens = st;
+        c.workspace = plan->scratch;
+        c.workspace_bytes = plan->scratch_bytes;
+        c.out = out;
+        c.scale_log2 = scale_log2_for(g->head_dim);
+        c.kernel_dim = kernel_dim_for(g->head_dim);
+        c.stream = static_cast<cudaStream_t>(stream);
+        rc = run_decode(c);
+        if (rc == MSLIM_OK && (history + st - 1) / st > 1) plan->split_calls++;
+    }
+    if (rc == MSLIM_OK) plan->calls++;
+    return rc;
+}
+
+int mslim_cuda_plan_diagnostics(const mslim_plan_t *plan, char *out, size_t len) {
+    if (!plan || !out) return fail(MSLIM_ERR_SHAPE_MISMATCH, "null argument");
+    const mslim_kernel_config_t &c = plan->config;
+    char id[128];
+    mslim_cuda_config_id(&c, id, sizeof(id));
+    std::string json;
+    char buf[2048];
+    snprintf(buf, sizeof(buf),
+             "{\"settings\":{\"mode\":\"%s\",\"block_queries\":%u,\"block_keys\":%u,"
+             "\"work_group\":%u,\"splits\":%u},"
+             "\"program_key\":\"sm_100a-%s-d%u-qh%u-kvh%u\","
+             "\"numeric_contract\":\"%s\","
+             "\"local_bytes_per_group\":%d,\"local_memory_type\":1,"
+             "\"preferred_work_group_multiple\":32,"
+             "\"global_score_matrix_bytes\":0,\"split_scratch_bytes\":%zu,"
+             "\"unused_memory_argument_bytes\":0,"
+             "\"dispatches_since_configuration\":%llu,"
+             "\"split_dispatches_since_configuration\":%llu,"
+             "\"prefill_dispatches_since_configuration\":%llu,"
+             "\"split_policy\":\"split-KV over 64-token stages for every query count; "
+             "fixed split-order merge\","
+             "\"fallback_policy\":\"none: ColdStore pages are read on the device through the "
+             "page table\"}",
+             mode_serde_name(c.mode), c.block_queries, c.block_keys, c.work_group, c.splits, id,
+             plan->geometry.head_dim, plan->geometry.query_heads, plan->geometry.kv_heads,
+             is_experimental(c) ? "experimental_online_not_bitwise"
+                                : "b200_split_kv_online_fixed_order",
+             (int)(3 * 2 * 64 * plan->geometry.head_dim * 2), plan->scratch_bytes,
+             (unsigned long long)plan->calls.load(), (unsigned long long)plan->split_calls.load(),
+             (unsigned long long)plan->prefill_calls.load());
+    json = buf;
+    if (json.size() + 1 > len) return fail(MSLIM_ERR_SHAPE_MISMATCH, "output buffer too small");
+    memcpy(out, json.c_str(), json.size() + 1);
+    return MSLIM_OK;
+}
+
+// ----------------------------------------------------------- backend --
+
+int mslim_cuda_backend_create(int device, mslim_backend_t **backend) {
+    if (!backend) return fail(MSLIM_ERR_SHAPE_MISMATCH, "backend pointer is null");
+    *backend = nullptr;
+    int prev;
+    if (cudaGetDevice(&prev) != cudaSuccess) return fail(MSLIM_ERR_UNSUPPORTED_DEVICE, "no GPU matches device filter");
+    if (cudaSetDevice(device) != cudaSuccess) return fail(MSLIM_ERR_UNSUPPORTED_DEVICE, "no GPU %d", device);
+    int dev;
+    int rc = current_device(&dev);
+    mslim_backend *b = nullptr;
+    if (rc == MSLIM_OK) {
+        b = new mslim_backend();
+        b->device = device;
+        cudaError_t err = cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking);
+        if (err == cudaSuccess) err = cudaEventCreate(&b->ev0);
+        if (err == cudaSuccess) err = cudaEventCreate(&b->ev1);
+        if (err != cudaSuccess) {
+            rc = cuda_fail(err, "create GPU command queue");
+            delete b;
+            b = nullptr;
+        }
+    }
+    cudaSetDevice(prev);
+    if (rc) return rc;
+    *backend = b;
+    return MSLIM_OK;
+}
+
+void mslim_cuda_backend_destroy(mslim_backend_t *b) {
+    if (!b) return;
+    int prev;
+    if (cudaGetDevice(&prev) == cudaSuccess) {
+        cudaSetDevice(b->device);
+        cudaStreamSynchronize(b->stream);
+        cudaFree(b->buf);
+        cudaEventDestroy(b->ev0);
+        cudaEventDestroy(b->ev1);
+        cudaStreamDestroy(b->stream);
+        cudaSetDevice(prev);
+    }
+    delete b;
+}
+
+int mslim_cuda_backend_decode(mslim_backend_t *b, const mslim_geometry_t *geometry,
+                              const float *query_host, const void *keys_host,
+                              const void *values_host, int dtype, uint32_t tokens,
+                              float *out_host) {
+    if (!b) return fail(MSLIM_ERR_BACKEND_FAILURE, "backend is null");
+    if (int rc = check_geometry(geometry)) return rc;
+    if (!query_host || !out_host) return fail(MSLIM_ERR_SHAPE_MISMATCH, "GPU Q shape");
+    const uint32_t QH = geometry->query_heads, KVH = geometry->kv_heads, D = geometry->head_dim;
+    const size_t qn = (size_t)QH * D;
+    for (size_t i = 0; i < qn; ++i)
+        if (!std::isfinite(query_host[i])) return fail(MSLIM_ERR_NON_FINITE, "non-finite computation: GPU Q");
+    if (tokens == 0) {
+        std::fill(out_host, out_host + qn, 0.0f);
+        return MSLIM_OK;
+    }
+    if (dtype < 1 || dtype > 3) return fail(MSLIM_ERR_UNSUPPORTED_DEVICE, "unknown frame format %d", dtype);
+    if (!keys_host || !values_host) return fail(MSLIM_ERR_SHAPE_MISMATCH, "null KV frames");
+    // The sm_100a path is a bf16 path.  FP16/FP32 frames are carried only when
+    // every value is exactly a bf16 value (bits preserved, no quantization).
+    std::vector<uint16_t> conv_k, conv_v;
+    if (dtype != 1) {
+        const size_t n = (size_t)tokens * KVH * D;
+        conv_k.resize(n);
+        conv_v.resize(n);
+        for (int which = 0; which < 2; ++which) {
+            const void *src = which ? values_host : keys_host;
+            uint16_t *dst = which ? conv_v.data() : conv_k.data();
+            for (size_t i = 0; i < n; ++i) {
+                float f;
+                if (dtype == 3) {
+                    memcpy(&f, static_cast<const uint8_t *>(src) + 4 * i, 4);
+                } else {
+                    uint16_t h;
+                    memcpy(&h, static_cast<const uint8_t *>(src) + 2 * i, 2);
+                    f = half_bits_to_float(h);
+                }
+                uint32_t bits;
+                memcpy(&bits, &f, 4);
+                if (!std::isfinite(f) || (bits & 0xffffu) != 0)
+                    return fail(MSLIM_ERR_UNSUPPORTED_DEVICE,
+                                "no native kernel registered for %s frames whose values are not "
+                                "exact bf16 values (sm_100a path is bf16)",
+                                dtype == 2 ? "FP16" : "FP32");
+                dst[i] = (uint16_t)(bits >> 16);
+            }
+        }
+        keys_host = conv_k.data();
+        values_host = conv_v.data();
+    }
+    if (D > 256) return fail(MSLIM_ERR_INVALID_GEOMETRY, "head_dim above 256");
+    if (tokens > 0x7fffffffu) return fail(MSLIM_ERR_INVALID_GEOMETRY, "GPU token count > i32");
+    // The kernel runs at the next supported head_dim; pad with zeros (zero
+    // query/key lanes add nothing to q.k and padded value lanes are dropped).
+    const uint32_t KD = D <= 64 ? 64 : D <= 128 ? 128 : 256;
+    DecodeShapeInfo sh;
+    if (int rc = decode_shape(geometry, 1, &sh)) return rc;
+    const uint32_t st = policy_split_tokens((uint64_t)KVH * sh.head_chunks, tokens);
+    const uint64_t splits = (tokens + st - 1) / st;
+    mslim_geometry_t kg = {QH, KVH, KD};
+    const size_t q_bytes = (size_t)QH * KD * 4;
+    const size_t kv_bytes = (size_t)tokens * KVH * KD * 2;
+    const size_t out_bytes = (size_t)QH * KD * 4;
+    const size_t ws_bytes = partial_bytes(&kg, 1, 1, splits);
+    auto up = [](size_t x) { return (x + 255) / 256 * 256; };
+    const size_t total = up(q_bytes) + 2 * up(kv_bytes) + up(out_bytes) + up(ws_bytes);
+    int prev;
+    if (cudaGetDevice(&prev) != cudaSuccess) return fail(MSLIM_ERR_BACKEND_FAILURE, "no CUDA device");
+    cudaSetDevice(b->device);
+    auto done = [&](int rc) {
+        cudaSetDevice(prev);
+        return rc;
+    };
+    cudaError_t err;
+    if (total > b->buf_bytes) {
+        cudaFree(b->buf);
+        b->buf = nullptr;
+        b->buf_bytes = 0;
+        err = cudaMalloc(&b->buf, total);
+        if (err != cudaSuccess) return done(cuda_fail(err, "allocate KV"));
+        b->buf_bytes = total;
+    }
+    uint8_t *base = static_cast<uint8_t *>(b->buf);
+    float *dq = reinterpret_cast<float *>(base);
+    uint16_t *dk = reinterpret_cast<uint16_t *>(base + up(q_bytes));
+    uint16_t *dv = reinterpret_cast<uint16_t *>(base + up(q_bytes) + up(kv_bytes));
+    float *dout = reinterpret_cast<float *>(base + up(q_bytes) + 2 * up(kv_bytes));
+    void *dws = base + up(q_bytes) + 2 * up(kv_bytes) + up(out_bytes);
+    const auto t0 = std::chrono::steady_clock::now();
+    // Host staging with zero padding of the head dimension.
+    std::vector<float> qpad((size_t)QH * KD, 0.0f);
+    for (uint32_t h = 0; h < QH; ++h) memcpy(&qpad[(size_t)h * KD], query_host + (size_t)h * D, D * 4);
+    err = cudaMemcpyAsync(dq, qpad.data(), q_bytes, cudaMemcpyHostToDevice, b->stream);
+    if (err == cudaSuccess && KD == D) {
+        err = cudaMemcpyAsync(dk, keys_host, kv_bytes, cudaMemcpyHostToDevice, b->stream);
+        if (err == cudaSuccess) err = cudaMemcpyAsync(dv, values_host, kv_bytes, cudaMemcpyHostToDevice, b->stream);
+    } else if (err == cudaSuccess) {
+        err = cudaMemcpy2DAsync(dk, KD * 2, keys_host, D * 2, D * 2, (size_t)tokens * KVH,
+                                cudaMemcpyHostToDevice, b->stream);
+        if (err == cudaSuccess)
+            err = cudaMemcpy2DAsync(dv, KD * 2, values_host, D * 2, D * 2, (size_t)tokens * KVH,
+                                    cudaMemcpyHostToDevice, b->stream);
+        if (err == cudaSuccess) err = cudaMemset2DAsync(dk + D, KD * 2, 0, (KD - D) * 2, (size_t)tokens * KVH, b->stream);
+        if (err == cudaSuccess) err = cudaMemset2DAsync(dv + D, KD * 2, 0, (KD - D) * 2, (size_t)tokens * KVH, b->stream);
+    }
+    if (err != cudaSuccess) return done(cuda_fail(err, "write KV"));
+    DecodeCall c{};
+    c.g = &kg;
+    c.q_f32 = dq;
+    c.k = dk;
+    c.v = dv;
+    c.fixed_tokens = (int)tokens;
+    c.n_seq = 1;
+    c.nq = 1;
+    c.max_tokens = tokens;
+    c.split_tokens = st;
+    c.workspace = dws;
+    c.workspace_bytes = ws_bytes;
+    c.out = dout;
+    c.out_f32 = dout;
+    c.scale_log2 = scale_log2_for(D);
+    c.kernel_dim = KD;
+    c.stream = b->stream;
+    cudaEventRecord(b->ev0, b->stream);
+    int rc = run_decode(c);
+    if (rc) return done(rc);
+    cudaEventRecord(b->ev1, b->stream);
+    std::vector<float> opad((size_t)QH * KD);
+    err = cudaMemcpyAsync(opad.data(), dout, out_bytes, cudaMemcpyDeviceToHost, b->stream);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(b->stream);
+    if (err != cudaSuccess) return done(cuda_fail(err, "GPU output readback"));
+    int status = 0;
+    mslim_cuda_device_status(b->device, 1, &status);
+    if (status) return done(fail(MSLIM_ERR_DEVICE_TIMEOUT, "device wait bound hit during decode"));
+    float kernel_ms = 0.f;
+    cudaEventElapsedTime(&kernel_ms, b->ev0, b->ev1);
+    for (uint32_t h = 0; h < QH; ++h) memcpy(out_host + (size_t)h * D, &opad[(size_t)h * KD], D * 4);
+    b->dispatch_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    b->kernel_ms = kernel_ms;
+    b->input_kv_bytes = 2 * (size_t)tokens * KVH * D * 2;
+    b->scratch_bytes = ws_bytes;
+    b->output_bytes = qn * 4;
+    b->have_timings = true;
+    for (size_t i = 0; i < qn; ++i)
+        if (!std::isfinite(out_host[i])) return done(fail(MSLIM_ERR_NON_FINITE, "non-finite computation: GPU output"));
+    return done(MSLIM_OK);
+}
+
+int mslim_cuda_backend_last_timings(const mslim_backend_t *b, char *out, size_t len) {
+    if (!b || !out) return fail(MSLIM_ERR_SHAPE_MISMATCH, "null argument");
+    if (!b->have_timings) return fail(MSLIM_ERR_BACKEND_FAILURE, "no dispatch yet");
+    char buf[512];
+    snprintf(buf, sizeof(buf),
+             "{\"dispatch_ms\":%.6f,\"kernel_ms\":%.6f,\"input_kv_bytes\":%zu,"
+             "\"scratch_bytes\":%zu,\"output_bytes\":%zu}",
+             b->dispatch_ms, b->kernel_ms, b->input_kv_bytes, b->scratch_bytes, b->output_bytes);
+    if (strlen(buf) + 1 > len) return fail(MSLIM_ERR_SHAPE_MISMATCH, "output buffer too small");
+    memcpy(out, buf, strlen(buf) + 1);
+    return MSLIM_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,453 @@
+// decode.cu -- split-KV flash-decoding over dense or ColdStore-paged bf16 K/V.
+//
+// Replaces the reference decode attention (QK / softmax / PV of
+// assets/gpu_llm.cl:150-212, the fused kernel of gpu_llm.cl:975-1026, the
+// tiled split-KV kernel + merge of assets/tiled_attention.cl:9-155 and the
+// ColdStore-staged PV of gpu_llm.cl:280-323) with one B200 kernel pair:
+//
+//   mslim_decode_split  one CTA per (split, KV-head chunk, sequence x query
+//                       block).  A producer warp streams 64-token K and V
+//                       tiles with TMA (128-byte swizzle, this GPU's HBM, no
+//                       multicast) through an mbarrier ring; four consumer
+//                       warps each own 16 tokens of every tile.  Rows of the
+//                       MMA are the (query, head) pairs that share the KV
+//                       head, so K/V bytes are read once per group.
+//   mslim_decode_merge  fixed split-order combine of {m, l, acc[D]} partials.
+//
+// Numeric contract (same code for dense and paged K/V, so the two layouts are
+// bit-identical by construction, and run-to-run deterministic):
+//   s = (q . k) * (log2(e)/sqrt(D))          fp32 accumulate (mma.sync bf16)
+//   p = exp2(s - m_running)                   online softmax, fp32
+//   acc += p_hi * v + p_lo * v                p split into two bf16 terms, so
+//                                             the PV product keeps ~16 bits of p
+//   out = bf16(sum_s w_s acc_s / sum_s w_s l_s)   fixed split order.
+#include "decode.cuh"
+
+namespace mslim {
+
+namespace {
+
+constexpr int kTileT = 64;       // tokens per pipeline stage
+constexpr int kWarpTokens = 16;  // tokens per consumer warp per stage
+constexpr int kConsumerWarps = kTileT / kWarpTokens;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kBoxBytes = kTileT * 128;  // one 64-column (128 B) swizzled box
+
+template <int D>
+struct Shape {
+    static constexpr int kBoxes = D / 64;
+    static constexpr int kTensorBytes = kBoxes * kBoxBytes;
+    static constexpr int kStageBytes = 2 * kTensorBytes;
+    static constexpr int kKSteps = D / 16;
+    static constexpr int kNTiles = D / 8;
+};
+
+__device__ __forceinline__ uint32_t ld_u32(const uint16_t *p) {
+    return *reinterpret_cast<const uint32_t *>(p);
+}
+
+// Byte offset of the 16-byte chunk `chunk` (along D) of tile row `row` inside a
+// stage tensor laid out as kBoxes boxes of [kTileT rows][128 B] with the TMA
+// 128-byte swizzle (chunk index XOR row % 8).
+__device__ __forceinline__ uint32_t swz(int row, int chunk) {
+    return (uint32_t)((chunk >> 3) * kBoxBytes + row * 128 + (((chunk & 7) ^ (row & 7)) << 4));
+}
+
+template <int D, int STAGES, bool PAGED, bool QSPLIT>
+__global__ void __launch_bounds__(kThreads)
+    mslim_decode_split(const __grid_constant__ CUtensorMap kmap,
+                       const __grid_constant__ CUtensorMap vmap, const DecodeParams p) {
+    using S = Shape<D>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * S::kStageBytes);
+    uint64_t *empty = full + STAGES;
+
+    const int split = blockIdx.x;
+    const int kvh = blockIdx.y / p.head_chunks;
+    const int hchunk = blockIdx.y % p.head_chunks;
+    const int seq = blockIdx.z / p.q_blocks;
+    const int qblock = blockIdx.z % p.q_blocks;
+
+    // Causal extent of this CTA: query row qg (0-based among the nq new rows)
+    // sees tokens [0, prior + qg], prior = tokens - nq.
+    const int ntok = min(p.token_cap, p.fixed_tokens >= 0 ? p.fixed_tokens : p.seq_tokens[seq]);
+    const int prior = ntok - p.nq;
+    const int qg_first = qblock * p.q_per_cta;
+    const int qg_last = min(p.nq, qg_first + p.q_per_cta) - 1;
+    const int cta_end = prior + qg_last + 1;  // exclusive token bound of the block
+    const int t_begin = split * p.split_tokens;
+    if (ntok <= 0 || cta_end <= 0 || t_begin >= cta_end) return;  // CTA-uniform
+    const int t_end = min(cta_end, t_begin + p.split_tokens);
+    const int ntiles = (t_end - t_begin + kTileT - 1) / kTileT;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        fence_mbarrier_init();
+    }
+    __syncthreads();
+
+    if (warp == kConsumerWarps) {
+        // ------------------------------------------------------ producer --
+        if (lane == 0) {
+            prefetch_tmap(&kmap);
+            prefetch_tmap(&vmap);
+            int issued = 0;
+            for (int i = 0; i < ntiles; ++i) {
+                const int s = i % STAGES;
+                if (!mbar_wait(&empty[s], ((i / STAGES) & 1) ^ 1, p.status, 1)) break;
+                const int t0 = t_begin + i * kTileT;
+                uint8_t *kdst = smem + s * S::kStageBytes;
+                uint8_t *vdst = kdst + S::kTensorBytes;
+                mbar_arrive_expect_tx(&full[s], S::kStageBytes);
+                if constexpr (PAGED) {
+                    const int lp = t0 / p.page_tokens;
+                    const int off = t0 - lp * p.page_tokens;
+                    const int phys = p.page_table[(size_t)seq * p.max_pages + lp];
+                    const int z = phys * p.kvheads + kvh;
+#pragma unroll
+                    for (int b = 0; b < S::kBoxes; ++b) {
+                        tma_load_3d(kdst + b * kBoxBytes, &kmap, &full[s], b * 64, off, z);
+                        tma_load_3d(vdst + b * kBoxBytes, &vmap, &full[s], b * 64, off, z);
+                    }
+                } else {
+#pragma unroll
+                    for (int b = 0; b < S::kBoxes; ++b) {
+                        tma_load_4d(kdst + b * kBoxBytes, &kmap, &full[s], b * 64, kvh, t0, seq);
+                        tma_load_4d(vdst + b * kBoxBytes, &vmap, &full[s], b * 64, kvh, t0, seq);
+                    }
+                }
+                issued = i + 1;
+            }
+            // Do not retire while our copies may still be landing in this CTA's
+            // shared memory: wait (bounded) for the last stages issued.
+            for (int i = max(0, issued - STAGES); i < issued; ++i)
+                mbar_wait(&full[i % STAGES], (i / STAGES) & 1, p.status, 2);
+        }
+        return;
+    }
+
+    // ----------------------------------------------------------- consumers --
+    const int g = lane >> 2;  // fragment row (and row + 8)
+    const int c = lane & 3;   // fragment column pair
+    const int hc = p.heads_per_cta;
+    // MMA row r <-> (query qg_first + r / hc, head kvh*group + hchunk*hc + r % hc)
+    int row_q[2], row_limit[2];
+    bool row_ok[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int r = g + 8 * h;
+        const int qi = r / hc;
+        row_q[h] = qg_first + qi;
+        row_ok[h] = (r < p.q_per_cta * hc) && (row_q[h] <= qg_last);
+        row_limit[h] = row_ok[h] ? prior + row_q[h] : -1;  // last visible token
+    }
+
+    // A fragments of Q (16 rows x 16 dims per k-step).  With QSPLIT the query
+    // arrives as f32 and is carried as qa (bf16 of q) + qb (bf16 of the
+    // remainder), two MMAs per k-step.
+    uint32_t qa[S::kKSteps][4];
+    uint32_t qb[QSPLIT ? S::kKSteps : 1][4];
+#pragma unroll
+    for (int ks = 0; ks < S::kKSteps; ++ks) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int r = g + 8 * h;
+            uint32_t k0 = 0, k8 = 0, k0r = 0, k8r = 0;
+            if (row_ok[h]) {
+                const int qh = kvh * p.group + hchunk * hc + r % hc;
+                const int d0 = ks * 16 + 2 * c;  // dims d0, d0+1 and d0+8, d0+9
+                const size_t off =
+                    (((size_t)seq * p.nq + row_q[h]) * p.qheads + qh) * p.head_dim + d0;
+                if constexpr (QSPLIT) {
+                    const float2 f0 = d0 < p.head_dim
+                                          ? *reinterpret_cast<const float2 *>(p.q_f32 + off)
+                                          : make_float2(0.f, 0.f);
+                    const float2 f8 = d0 + 8 < p.head_dim
+                                          ? *reinterpret_cast<const float2 *>(p.q_f32 + off + 8)
+                                          : make_float2(0.f, 0.f);
+                    k0 = pack_bf16x2(f0.x, f0.y);
+                    k8 = pack_bf16x2(f8.x, f8.y);
+                    k0r = pack_bf16x2(f0.x - bf16lo_f32(k0), f0.y - bf16hi_f32(k0));
+                    k8r = pack_bf16x2(f8.x - bf16lo_f32(k8), f8.y - bf16hi_f32(k8));
+                } else {
+                    k0 = d0 < p.head_dim ? ld_u32(p.q + off) : 0u;
+                    k8 = d0 + 8 < p.head_dim ? ld_u32(p.q + off + 8) : 0u;
+                }
+            }
+            qa[ks][h] = k0;      // a0 (row g) / a1 (row g+8): k = 2c, 2c+1
+            qa[ks][2 + h] = k8;  // a2 / a3: k = 2c+8, 2c+9
+            if constexpr (QSPLIT) {
+                qb[ks][h] = k0r;
+                qb[ks][2 + h] = k8r;
+            }
+        }
+    }
+
+    float o[S::kNTiles][4];
+#pragma unroll
+    for (int n = 0; n < S::kNTiles; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float m_run[2] = {-INFINITY, -INFINITY};
+    float l_run[2] = {0.f, 0.f};
+    const float scale = p.scale_log2;
+    const uint32_t smem_base = smem_u32(smem);
+
+    for (int i = 0; i < ntiles; ++i) {
+        const int s = i % STAGES;
+        if (!mbar_wait(&full[s], (i / STAGES) & 1, p.status, 3)) break;
+        const int row0 = warp * kWarpTokens;
+        const int t0 = t_begin + i * kTileT + row0;
+        const int valid = min(kWarpTokens, t_end - t0);
+        if (valid > 0) {
+            const uint32_t kt = smem_base + s * S::kStageBytes;
+            const uint32_t vt = kt + S::kTensorBytes;
+            if (valid < kWarpTokens) {
+                // Rows past the sequence end hold whatever the page or cache held;
+                // zero their V so p == 0 cannot meet a NaN/Inf payload.
+                uint8_t *vrow = smem + s * S::kStageBytes + S::kTensorBytes;
+                for (int x = lane; x < (kWarpTokens - valid) * S::kBoxes * 8; x += 32) {
+                    const int r = row0 + valid + x / (S::kBoxes * 8);
+                    const int ch = x % (S::kBoxes * 8);
+                    *reinterpret_cast<uint4 *>(vrow + swz(r, ch)) = make_uint4(0, 0, 0, 0);
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+            }
+            // ---- S = Q K^T for this warp's 16 tokens (two n-tiles of 8) ----
+            float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+            for (int j = 0; j < D / 32; ++j) {
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt) {
+                    const int r = row0 + nt * 8 + (lane & 7);
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4(kt + swz(r, 4 * j + (lane >> 3)), b0, b1, b2, b3);
+                    mma_bf16_16816(sc[nt], qa[2 * j], b0, b1);
+                    mma_bf16_16816(sc[nt], qa[2 * j + 1], b2, b3);
+                    if constexpr (QSPLIT) {
+                        mma_bf16_16816(sc[nt], qb[2 * j], b0, b1);
+                        mma_bf16_16816(sc[nt], qb[2 * j + 1], b2, b3);
+                    }
+                }
+            }
+            // ---- online softmax over the 16 tokens (rows g, g+8) ----
+            float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int h = e >> 1;
+                    const int tok = t0 + nt * 8 + 2 * c + (e & 1);
+                    const float v = (tok <= row_limit[h]) ? sc[nt][e] * scale : -INFINITY;
+                    sc[nt][e] = v;
+                    mx[h] = fmaxf(mx[h], v);
+                }
+            float alpha[2], base[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+                mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+                const float m_new = fmaxf(m_run[h], mx[h]);
+                base[h] = (m_new == -INFINITY) ? 0.f : m_new;
+                alpha[h] = fast_exp2(m_run[h] - base[h]);
+                m_run[h] = m_new;
+            }
+            float ps[2] = {0.f, 0.f};
+            uint32_t phi[4], plo[4];
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const float p0 = fast_exp2(sc[nt][2 * h] - base[h]);
+                    const float p1 = fast_exp2(sc[nt][2 * h + 1] - base[h]);
+                    ps[h] += p0 + p1;
+                    const uint32_t hi = pack_bf16x2(p0, p1);
+                    const uint32_t lo = pack_bf16x2(p0 - bf16lo_f32(hi), p1 - bf16hi_f32(hi));
+                    // A fragment of P (16 rows x 16 tokens): a0 = (g, 2c..), a1 = (g+8, 2c..),
+                    // a2 = (g, 2c+8..), a3 = (g+8, 2c+8..).
+                    phi[nt * 2 + h] = hi;
+                    plo[nt * 2 + h] = lo;
+                }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) l_run[h] = l_run[h] * alpha[h] + ps[h];
+#pragma unroll
+            for (int n = 0; n < S::kNTiles; ++n) {
+                o[n][0] *= alpha[0];
+                o[n][1] *= alpha[0];
+                o[n][2] *= alpha[1];
+                o[n][3] *= alpha[1];
+            }
+            // ---- O += P V (V^T fragments via transposed ldmatrix) ----
+            const uint32_t pa_hi[4] = {phi[0], phi[1], phi[2], phi[3]};
+            const uint32_t pa_lo[4] = {plo[0], plo[1], plo[2], plo[3]};
+#pragma unroll
+            for (int j = 0; j < D / 16; ++j) {
+                const int mtx = lane >> 3;
+                const int r = row0 + (mtx & 1) * 8 + (lane & 7);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4_trans(vt + swz(r, 2 * j + (mtx >> 1)), b0, b1, b2, b3);
+                mma_bf16_16816(o[2 * j], pa_hi, b0, b1);
+                mma_bf16_16816(o[2 * j], pa_lo, b0, b1);
+                mma_bf16_16816(o[2 * j + 1], pa_hi, b2, b3);
+                mma_bf16_16816(o[2 * j + 1], pa_lo, b2, b3);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+
+    // ---- combine the four warps' states (fixed warp order) ----
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 1);
+        l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 2);
+    }
+    // All consumers are done with the ring (the producer has issued nothing
+    // further), so its first stage is reused as [warp][16 rows][D + 2] floats.
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+    float *st = reinterpret_cast<float *>(smem);
+    constexpr int kRowF = D + 2;
+    float *mine = st + warp * 16 * kRowF;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int r = g + 8 * h;
+        if (c == 0) {
+            mine[r * kRowF + D] = m_run[h];
+            mine[r * kRowF + D + 1] = l_run[h];
+        }
+#pragma unroll
+        for (int n = 0; n < S::kNTiles; ++n) {
+            mine[r * kRowF + n * 8 + 2 * c] = o[n][2 * h];
+            mine[r * kRowF + n * 8 + 2 * c + 1] = o[n][2 * h + 1];
+        }
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+    const int rows = p.q_per_cta * hc;
+    for (int x = threadIdx.x; x < rows * (D / 2); x += kConsumerWarps * 32) {
+        const int r = x / (D / 2);
+        const int d = (x % (D / 2)) * 2;
+        const int qg = qg_first + r / hc;
+        if (qg > qg_last) continue;
+        float m = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) m = fmaxf(m, st[(w * 16 + r) * kRowF + D]);
+        const float mb = (m == -INFINITY) ? 0.f : m;
+        float l = 0.f, a0 = 0.f, a1 = 0.f;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) {
+            const float *src = st + (w * 16 + r) * kRowF;
+            const float wgt = fast_exp2(src[D] - mb);
+            l += wgt * src[D + 1];
+            a0 += wgt * src[d];
+            a1 += wgt * src[d + 1];
+        }
+        const int qh = kvh * p.group + hchunk * hc + r % hc;
+        float *dst = p.partials +
+                     ((((size_t)seq * p.nq + qg) * p.qheads + qh) * p.max_splits + split) * kRowF;
+        dst[d] = a0;
+        dst[d + 1] = a1;
+        if (d == 0) {
+            dst[D] = m;
+            dst[D + 1] = l;
+        }
+    }
+}
+
+// One warp per (sequence, query row, query head): fixed split-order combine.
+template <int D>
+__global__ void __launch_bounds__(128) mslim_decode_merge(const DecodeParams p, uint16_t *out) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const size_t item = (size_t)blockIdx.x * 4 + warp;
+    const size_t items = (size_t)p.n_seq * p.nq * p.qheads;
+    if (item >= items) return;
+    const size_t sq = item / p.qheads;  // seq * nq + qg
+    const int qg = (int)(sq % p.nq);
+    const int seq = (int)(sq / p.nq);
+    constexpr int kRowF = D + 2;
+    constexpr int kPer = D / 32;
+    const int ntok = min(p.token_cap, p.fixed_tokens >= 0 ? p.fixed_tokens : p.seq_tokens[seq]);
+    const int prior = ntok - p.nq;
+    const int qblock = qg / p.q_per_cta;
+    const int qg_last = min(p.nq, (qblock + 1) * p.q_per_cta) - 1;
+    const int cta_end = prior + qg_last + 1;
+    const int splits = (ntok <= 0 || cta_end <= 0)
+                           ? 0
+                           : min((int)p.max_splits, (cta_end + p.split_tokens - 1) / p.split_tokens);
+    const float *src = p.partials + item * p.max_splits * kRowF;
+    float m = -INFINITY;
+    for (int s = 0; s < splits; ++s) m = fmaxf(m, src[s * kRowF + D]);
+    const float mb = (m == -INFINITY) ? 0.f : m;
+    float l = 0.f;
+    float acc[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) acc[k] = 0.f;
+    for (int s = 0; s < splits; ++s) {
+        const float *part = src + s * kRowF;
+        const float w = fast_exp2(part[D] - mb);
+        l += w * part[D + 1];
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) acc[k] += w * part[lane + 32 * k];
+    }
+    const float inv = (l > 0.f) ? 1.0f / l : 0.f;
+    const size_t obase = item * p.head_dim;
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+        const int d = lane + 32 * k;
+        if (d >= p.head_dim) continue;
+        if (p.out_f32)
+            p.out_f32[obase + d] = acc[k] * inv;
+        else
+            out[obase + d] = bf16_bits_rn(acc[k] * inv);
+    }
+}
+
+template <int D, int STAGES, bool PAGED, bool QSPLIT>
+cudaError_t launch_impl(const CUtensorMap &kmap, const CUtensorMap &vmap, const DecodeParams &p,
+                        uint16_t *out, cudaStream_t stream) {
+    using S = Shape<D>;
+    const size_t smem = (size_t)STAGES * S::kStageBytes + 2 * STAGES * sizeof(uint64_t) + 1024;
+    auto kernel = mslim_decode_split<D, STAGES, PAGED, QSPLIT>;
+    cudaError_t err =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (err != cudaSuccess) return err;
+    dim3 grid(p.max_splits, p.kvheads * p.head_chunks, p.n_seq * p.q_blocks);
+    kernel<<<grid, kThreads, smem, stream>>>(kmap, vmap, p);
+    err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
+    const size_t items = (size_t)p.n_seq * p.nq * p.qheads;
+    mslim_decode_merge<D><<<(unsigned)((items + 3) / 4), 128, 0, stream>>>(p, out);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_decode(int head_dim, bool paged, const CUtensorMap &kmap,
+                          const CUtensorMap &vmap, const DecodeParams &p, uint16_t *out,
+                          cudaStream_t stream) {
+    const bool qsplit = p.q_f32 != nullptr;
+    if (qsplit && paged) return cudaErrorInvalidValue;
+    switch (head_dim) {
+        case 64:
+            if (qsplit) return launch_impl<64, 4, false, true>(kmap, vmap, p, out, stream);
+            return paged ? launch_impl<64, 4, true, false>(kmap, vmap, p, out, stream)
+                         : launch_impl<64, 4, false, false>(kmap, vmap, p, out, stream);
+        case 128:
+            if (qsplit) return launch_impl<128, 3, false, true>(kmap, vmap, p, out, stream);
+            return paged ? launch_impl<128, 3, true, false>(kmap, vmap, p, out, stream)
+                         : launch_impl<128, 3, false, false>(kmap, vmap, p, out, stream);
+        case 256:
+            if (qsplit) return launch_impl<256, 2, false, true>(kmap, vmap, p, out, stream);
+            return paged ? launch_impl<256, 2, true, false>(kmap, vmap, p, out, stream)
+                         : launch_impl<256, 2, false, false>(kmap, vmap, p, out, stream);
+        default:
+            return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace mslim

@@ -1,0 +1,32 @@
+// prologue.cuh -- launchers of the RMSNorm / RoPE / RoPE+append kernels.
+#pragma once
+
+#include <algorithm>
+
+#include "mslim_common.cuh"
+
+namespace mslim {
+
+// Per-dimension RoPE frequency table, built on the host once per call.
+// multiply == 0: angle = position / freq[i]  (CPU formula, freq = theta^(2i/D))
+// multiply != 0: angle = position * freq[i]  (inverse frequency, optionally
+//                Llama-3 scaled, src/gpu_llm/kernels.rs:50-67)
+struct RopeTable {
+    float freq[128];
+    int multiply;
+};
+
+cudaError_t launch_rmsnorm(const uint16_t *x, const uint16_t *w, uint16_t *y, uint32_t tokens,
+                           uint32_t hidden, float eps, cudaStream_t stream);
+cudaError_t launch_rope(const uint16_t *in, uint16_t *out, uint32_t tokens, uint32_t heads,
+                        uint32_t dim, uint32_t start_position, const RopeTable &table,
+                        cudaStream_t stream);
+cudaError_t launch_rope_append_paged(const uint16_t *q_in, uint16_t *q_out, const uint16_t *k_in,
+                                     const uint16_t *v_in, uint32_t tokens, uint32_t qheads,
+                                     uint32_t kvheads, uint32_t dim, uint32_t start_position,
+                                     const int32_t *positions, uint16_t *k_pool,
+                                     uint16_t *v_pool, uint32_t n_pages, uint32_t page_tokens,
+                                     const int32_t *page_table, uint32_t max_pages,
+                                     const RopeTable &table, int *status, cudaStream_t stream);
+
+}  // namespace mslim

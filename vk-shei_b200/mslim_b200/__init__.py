@@ -1,0 +1,20 @@
+"""B200 (sm_100a) attention hot path of M-SLIM behind its attention API.
+
+The compute lives in libmslim_cuda.so (vk-shei_b200/csrc, C ABI in
+include/mslim_cuda.h); this package is the host-side mirror of the
+reference's interfaces plus seeded workload generators.
+"""
+from . import _lib
+from .attention import (AttentionGeometry, AttentionKernelConfig, AttentionKernelMode, BackendFailure,
+                        DeviceTimeout, ExactKvFrames, GpuBackend, GpuEngine, InvalidConfig,
+                        InvalidGeometry, NonFinite, PortableError, RopeKernelConfig, ShapeMismatch,
+                        TiledAttention, UnsupportedDevice, check, decode_dense, decode_paged,
+                        decode_workspace_bytes, device_status, prefill_causal, rmsnorm, rope,
+                        rope_append_decode_paged, rope_append_paged)
+
+LIB_PATH = _lib.LIB_PATH
+
+
+def load():
+    """Loads the native library (raises if it was not built)."""
+    return _lib.lib()
