@@ -178,6 +178,31 @@ int mslim_cuda_decode_paged(const mslim_geometry_t *geometry, const void *q, con
                             const int32_t *seq_tokens, uint32_t n_seq, uint32_t split_tokens,
                             void *workspace, size_t workspace_bytes, void *out, void *stream);
 
+/* Paged decode that allocates nothing and takes no workspace.  No counterpart
+ * in the reference: it is for callers that cannot allocate device memory --
+ * code running while a stream is being captured into a CUDA graph, a serving
+ * loop that must never hit the implicit device synchronisation of
+ * cudaMalloc/cudaFree, or a host (e.g. a Rust FFI caller) that holds only the
+ * K/V, page-table and output pointers and has no device allocator bound.
+ * Same arguments and results as mslim_cuda_decode_paged minus the workspace;
+ * with the same split_tokens the output is bit-identical to it.
+ * The split partials live in a library-owned static device array of
+ * MSLIM_STATIC_SCRATCH_BYTES (16 MiB, the reference's split-scratch bound,
+ * src/attention_kernel.rs:124-138), held by every GPU that loads the library
+ * until the process exits.  A request whose partials exceed it fails with
+ * MSLIM_ERR_SHAPE_MISMATCH; split_tokens == 0 picks the library's split size
+ * and, if needed, larger splits until the partials fit.  The first call on a
+ * device looks up the array's device address (no allocation); make that first
+ * call before any stream capture.  Every call shares the one array: calls
+ * that can overlap on the GPU (different streams, no ordering) race on it. */
+#define MSLIM_STATIC_SCRATCH_BYTES (16u << 20)
+int mslim_cuda_decode_paged_static_scratch(const mslim_geometry_t *geometry, const void *q,
+                                           const void *k_pool, const void *v_pool,
+                                           uint32_t n_pages, uint32_t page_tokens,
+                                           const int32_t *page_table, uint32_t max_pages_per_seq,
+                                           const int32_t *seq_tokens, uint32_t n_seq,
+                                           uint32_t split_tokens, void *out, void *stream);
+
 /* ------------------------------------------------ prefill attention -- */
 
 /* BatchKernels::attention (src/gpu_llm/prefill.rs:363-435): chunked causal

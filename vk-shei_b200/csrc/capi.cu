@@ -27,6 +27,12 @@
 // One status word per device; kernels record bounded-wait timeouts here.
 __device__ int g_mslim_status_word;
 
+// Split partials of mslim_cuda_decode_paged_static_scratch: a fixed device
+// array, so that entry point never allocates.  Its contents persist between
+// calls; every partial the merge reads is written by the split kernel of the
+// same call first, so nothing in it has to start at zero.
+static __device__ __align__(256) float g_static_decode_scratch[MSLIM_STATIC_SCRATCH_BYTES / sizeof(float)];
+
 namespace {
 
 thread_local std::string g_last_error;
@@ -82,6 +88,25 @@ int *status_ptr(int dev) {
             g_status_ptr[dev] = static_cast<int *>(p);
     }
     return g_status_ptr[dev];
+}
+
+// Device address of g_static_decode_scratch, looked up once per device with
+// that device current (host code may not take the address of a __device__
+// array directly: that would be a host-side stand-in, not device memory).
+void *g_static_scratch_ptr[kMaxDevices] = {};
+
+int static_scratch_ptr(int dev, void **ptr) {
+    std::lock_guard<std::mutex> lock(g_dev_mutex);
+    if (!g_static_scratch_ptr[dev]) {
+        void *p = nullptr;
+        cudaError_t err = cudaGetSymbolAddress(&p, g_static_decode_scratch);
+        if (err != cudaSuccess || !p)
+            return fail(MSLIM_ERR_BACKEND_FAILURE, "static scratch address lookup failed: %s",
+                        cudaGetErrorString(err));
+        g_static_scratch_ptr[dev] = p;
+    }
+    *ptr = g_static_scratch_ptr[dev];
+    return MSLIM_OK;
 }
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
@@ -606,6 +631,43 @@ int mslim_cuda_decode_paged(const mslim_geometry_t *geometry, const void *q, con
     c.kernel_dim = kernel_dim_for(geometry->head_dim);
     c.stream = static_cast<cudaStream_t>(stream);
     return run_decode(c);
+}
+
+int mslim_cuda_decode_paged_static_scratch(const mslim_geometry_t *geometry, const void *q,
+                                           const void *k_pool, const void *v_pool,
+                                           uint32_t n_pages, uint32_t page_tokens,
+                                           const int32_t *page_table, uint32_t max_pages_per_seq,
+                                           const int32_t *seq_tokens, uint32_t n_seq,
+                                           uint32_t split_tokens, void *out, void *stream) {
+    if (int rc = check_geometry(geometry)) return rc;
+    if (page_tokens == 0 || page_tokens % 64 != 0)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "page_tokens must be a positive multiple of 64");
+    if (n_pages == 0 || max_pages_per_seq == 0 || n_seq == 0)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty page pool, page table or batch");
+    const uint64_t max_tokens = (uint64_t)max_pages_per_seq * page_tokens;
+    if (max_tokens > 0x7fffffffull) return fail(MSLIM_ERR_SHAPE_MISMATCH, "page table spans too many tokens");
+    if (split_tokens % 64 != 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "split_tokens must be a multiple of 64");
+    uint32_t st = split_tokens;
+    if (st == 0) {
+        if (int rc = decode_common_checks(geometry, n_seq, &st, (uint32_t)max_tokens)) return rc;
+        // Larger splits until the partials fit the static array.
+        while (partial_bytes(geometry, n_seq, 1, (max_tokens + st - 1) / st) > MSLIM_STATIC_SCRATCH_BYTES &&
+               st < max_tokens)
+            st *= 2;
+    }
+    const uint64_t need = partial_bytes(geometry, n_seq, 1, (max_tokens + st - 1) / st);
+    if (need > MSLIM_STATIC_SCRATCH_BYTES)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH,
+                    "split partials need %llu bytes; the static scratch holds %u bytes "
+                    "(use fewer sessions, larger split_tokens or mslim_cuda_decode_paged)",
+                    (unsigned long long)need, (unsigned)MSLIM_STATIC_SCRATCH_BYTES);
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    void *scratch = nullptr;
+    if (int rc = static_scratch_ptr(dev, &scratch)) return rc;
+    return mslim_cuda_decode_paged(geometry, q, k_pool, v_pool, n_pages, page_tokens, page_table,
+                                   max_pages_per_seq, seq_tokens, n_seq, st, scratch,
+                                   MSLIM_STATIC_SCRATCH_BYTES, out, stream);
 }
 
 // ----------------------------------------------------------- prefill --

@@ -8,7 +8,7 @@ from . import _lib
 from .attention import (AttentionGeometry, AttentionKernelConfig, AttentionKernelMode, BackendFailure,
                         DeviceTimeout, ExactKvFrames, GpuBackend, GpuEngine, InvalidConfig,
                         InvalidGeometry, NonFinite, PortableError, RopeKernelConfig, ShapeMismatch,
-                        TiledAttention, UnsupportedDevice, check, decode_dense, decode_paged,
+                        TiledAttention, UnsupportedDevice, check, decode_dense, decode_paged, decode_paged_static_scratch,
                         decode_workspace_bytes, device_status, prefill_causal, rmsnorm, rope,
                         rope_append_decode_paged, rope_append_paged)
 

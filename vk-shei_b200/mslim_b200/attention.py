@@ -273,6 +273,20 @@ def decode_paged(geometry: AttentionGeometry, q, k_pool, v_pool, n_pages: int, p
         _nbytes(workspace), _ptr(out), _stream(stream)))
 
 
+STATIC_SCRATCH_BYTES = 16 << 20
+
+
+def decode_paged_static_scratch(geometry: AttentionGeometry, q, k_pool, v_pool, n_pages: int,
+                                page_tokens: int, page_table, max_pages_per_seq: int, seq_tokens,
+                                n_seq: int, out, split_tokens: int = 0, stream=None) -> None:
+    """Paged decode without a workspace: the split partials live in the
+    library's 16 MiB static device array (shared by all calls on a device)."""
+    check(_lib.lib().mslim_cuda_decode_paged_static_scratch(
+        ctypes.byref(geometry.c()), _ptr(q), _ptr(k_pool), _ptr(v_pool), n_pages, page_tokens,
+        _ptr(page_table), max_pages_per_seq, _ptr(seq_tokens), n_seq, split_tokens, _ptr(out),
+        _stream(stream)))
+
+
 def prefill_causal(geometry: AttentionGeometry, q, k, v, out, queries: int, prior: int,
                    stream=None) -> None:
     """BatchKernels::attention (src/gpu_llm/prefill.rs:363-435)."""
