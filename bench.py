@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-prefill", action="store_true", help="skip the C2 prefill leg")
+    ap.add_argument("--prefill-only", action="store_true", help="run only the C2 prefill leg (profiling)")
     return ap.parse_args()
 
 
@@ -218,6 +220,57 @@ def run_reference(args, rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------- prefill leg --
+
+def bench_prefill(m, torch, device, args) -> dict:
+    """C2: causal prefill, S = 2048, 32/8 heads,
+    D = 128.  Its 24 MB of inputs fit in L2, so a 256 MB buffer is written
+    between timed iterations and each iteration is timed alone."""
+    S = 2048
+    g = m.AttentionGeometry.new(QH, KVH, D)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(1)
+    q = torch.randn((S, QH, D), generator=gen, device=device, dtype=torch.bfloat16)
+    k = torch.randn((S, KVH, D), generator=gen, device=device, dtype=torch.bfloat16)
+    v = torch.randn((S, KVH, D), generator=gen, device=device, dtype=torch.bfloat16)
+    out = torch.empty_like(q)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream()
+    for _ in range(max(args.warmup, 3)):
+        m.prefill_causal(g, q, k, v, out, S, 0, stream)
+    torch.cuda.synchronize()
+    steps = max(10, min(args.steps, 100))
+    times = []
+    sampler = ClockSampler(torch.cuda.current_device())
+    sampler.start()
+    for _ in range(steps):
+        flush.zero_()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        m.prefill_causal(g, q, k, v, out, S, 0, stream)
+        b.record(stream)
+        b.synchronize()
+        times.append(a.elapsed_time(b))
+    clocks = sampler.stop()
+    if m.device_status(torch.cuda.current_device()) != 0:
+        raise SystemExit("device status reported an error during the prefill leg")
+    flops = 4 * D * QH * S * (S + 1) // 2
+    ms = statistics.mean(times)
+    tflops = flops / (ms * 1e-3) / 1e12
+    peaks = measured_peaks()
+    return {"metric": "prefill attn TFLOPS (C2 causal, S 2048, 32/8 heads, D 128)", "value": tflops,
+            "unit": "TFLOP/s", "ms_per_step": ms, "ms_min": min(times), "steps": steps,
+            "algorithmic_flops": flops, "l2": "256 MB written between timed iterations",
+            "roofline": {"bound": "tensor", "kernel": "mslim_prefill_causal", "achieved": tflops,
+                         "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": tflops / peaks["bf16_tflops"] if peaks["bf16_tflops"] else None,
+                         "peak_source": ("measured (MEASURED_PEAKS.json bf16_tflops, burst: kernel timed alone)"
+                                         if peaks["source"] == "measured" else "fallback 1590 TFLOP/s"),
+                         "traffic": None},
+            "gpu_launches": steps, "clocks": clocks}
+
+
 # --------------------------------------------------------------- GPU leg --
 
 def main():
@@ -242,6 +295,9 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device(device))
     m.load()
+    if args.prefill_only:
+        print(json.dumps({"prefill": bench_prefill(m, torch, device, args)}), flush=True)
+        return
 
     layout = workloads.c4_layout(seed=3)
     if args.scaling == "strong" and world > 1:
@@ -378,6 +434,10 @@ def main():
         if m.device_status(local) != 0:
             raise SystemExit("device status reported an error during the e2e leg")
 
+    prefill = None
+    if rank == 0 and not args.no_prefill:
+        prefill = bench_prefill(m, torch, device, args)
+
     if rank != 0:
         if dist is not None:
             dist.destroy_process_group()
@@ -408,7 +468,7 @@ def main():
                        "l2": "no flush: inputs larger than L2 (%.2f GB per GPU per step)" % (step_bytes / 1e9),
                        "parallelism": f"session-sharded x{world} ({args.scaling})"},
             "tokens_per_s": total_seq / (ms_per_step * 1e-3),
-            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "prefill": prefill,
             "gpu_launches": 2 * args.steps, "clocks": clocks, "device_status": status}
     print(json.dumps(line), flush=True)
     if dist is not None:

@@ -1,0 +1,77 @@
+"""GPU parity of the tcgen05/TMEM causal prefill kernel against the CPU path
+(the reference prefills by running forward_token per prompt row,
+src/native_cpu_adapter.rs:717-784, so row i attends over keys 0..=prior+i with
+dense_attention_bf16)."""
+import numpy as np
+import pytest
+
+from gpu_util import bf16_f32, dev, empty_u16, host_u16, max_abs, torch_mod
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+
+
+@pytest.fixture(scope="module")
+def m():
+    import mslim_b200
+    mslim_b200.load()
+    return mslim_b200
+
+
+def run_prefill(m, g, q, k, v, queries, prior):
+    torch = torch_mod()
+    out = empty_u16((queries, g.query_heads, g.head_dim))
+    kd, vd = dev(k), dev(v)
+    m.prefill_causal(g, dev(q), kd, vd, out, queries, prior)
+    torch.cuda.synchronize()
+    assert m.device_status(0) == 0
+    assert np.array_equal(host_u16(kd), k) and np.array_equal(host_u16(vd), v), "K/V modified"
+    return host_u16(out)
+
+
+CASES = [(1, 0), (5, 0), (128, 0), (129, 0), (200, 37), (256, 256), (64, 1000), (300, 129)]
+
+
+@pytest.mark.parametrize("geom", [(32, 8, 128), (8, 2, 128), (4, 1, 128), (4, 4, 128)])
+def test_prefill_matches_cpu_path(m, oracle, geom):
+    from mslim_b200 import workloads as wl
+    qh, kvh, d = geom
+    g = m.AttentionGeometry.new(qh, kvh, d)
+    rng = np.random.default_rng(qh * 7 + kvh)
+    for queries, prior in CASES:
+        hist = prior + queries
+        q = wl.normal_bf16(rng, (queries, qh, d))
+        k = wl.normal_bf16(rng, (hist, kvh, d))
+        v = wl.normal_bf16(rng, (hist, kvh, d))
+        got = run_prefill(m, g, q, k, v, queries, prior)
+        ref = oracle.causal_prefill_bf16(qh, kvh, d, q, k, v, queries, prior)
+        err = max_abs(bf16_f32(got), bf16_f32(ref))
+        assert err <= TOL, (geom, queries, prior, err)
+        again = run_prefill(m, g, q, k, v, queries, prior)
+        assert again.tobytes() == got.tobytes(), "repeat run differs"
+
+
+def test_c2_full_size_matches_cpu_path(m, oracle):
+    """C2: S = 2048, 32/8 heads, D = 128, RoPE theta 5e5 on positions 0..2047."""
+    from mslim_b200 import workloads as wl
+    case = wl.c2_prefill()
+    q = oracle.rope_rows_bf16(case.q_raw, 0, case.theta)
+    k = oracle.rope_rows_bf16(case.k_raw, 0, case.theta)
+    g = m.AttentionGeometry.new(32, 8, 128)
+    got = run_prefill(m, g, q, k, case.v, 2048, 0)
+    ref = oracle.causal_prefill_bf16(32, 8, 128, q, k, case.v, 2048, 0)
+    err = max_abs(bf16_f32(got), bf16_f32(ref))
+    assert err <= TOL, err
+    # P enters the PV product as bf16 (relative 2^-9), so many outputs land one
+    # bf16 ulp from the CPU's f32-weighted sum; none further than the tolerance.
+    same = np.mean(got == ref)
+    assert same > 0.5, same
+
+
+def test_prefill_rejects_unsupported(m):
+    torch = torch_mod()
+    b = torch.zeros(64, dtype=torch.int16, device="cuda:0")
+    with pytest.raises(m.InvalidGeometry):
+        m.prefill_causal(m.AttentionGeometry.new(4, 1, 64), b, b, b, b.clone(), 1, 0)
+    with pytest.raises(m.ShapeMismatch):
+        m.prefill_causal(m.AttentionGeometry.new(4, 1, 128), b, b, b, b, 1, 0)

@@ -689,13 +689,33 @@ int mslim_cuda_prefill_causal(const mslim_geometry_t *geometry, const void *q, c
                     geometry->head_dim);
     if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(out, 16))
         return fail(MSLIM_ERR_SHAPE_MISMATCH, "prefill buffers must be 16-byte aligned");
-    int rc = mslim::launch_prefill(geometry->query_heads, geometry->kv_heads, geometry->head_dim,
-                                   static_cast<const uint16_t *>(q), static_cast<const uint16_t *>(k),
-                                   static_cast<const uint16_t *>(v), static_cast<uint16_t *>(out),
-                                   queries, prior, scale_log2_for(geometry->head_dim),
-                                   status_ptr(dev), static_cast<cudaStream_t>(stream),
-                                   &g_last_error);
-    return rc;
+    const uint64_t D = geometry->head_dim;
+    CUtensorMap qmap, kmap, vmap;
+    {
+        const uint64_t qd[3] = {D, geometry->query_heads, queries};
+        const uint64_t qs[2] = {D * 2, (uint64_t)geometry->query_heads * D * 2};
+        const uint64_t kd[3] = {D, geometry->kv_heads, history};
+        const uint64_t ks[2] = {D * 2, (uint64_t)geometry->kv_heads * D * 2};
+        const uint32_t box[3] = {64, 1, 128};
+        if (int rc = make_tmap(&qmap, q, 3, qd, qs, box)) return rc;
+        if (int rc = make_tmap(&kmap, k, 3, kd, ks, box)) return rc;
+        if (int rc = make_tmap(&vmap, v, 3, kd, ks, box)) return rc;
+    }
+    mslim::PrefillParams p{};
+    p.out = static_cast<uint16_t *>(out);
+    p.status = status_ptr(dev);
+    p.qheads = (int)geometry->query_heads;
+    p.kvheads = (int)geometry->kv_heads;
+    p.group = (int)(geometry->query_heads / geometry->kv_heads);
+    p.queries = (int)queries;
+    p.prior = (int)prior;
+    p.n_qtiles = (int)((queries + 127) / 128);
+    p.scale_log2 = scale_log2_for(geometry->head_dim);
+    if ((uint64_t)p.n_qtiles * p.qheads > 0x7fffffffull)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "prefill grid too large");
+    cudaError_t err = mslim::launch_prefill(qmap, kmap, vmap, p, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail(err, "prefill launch");
+    return MSLIM_OK;
 }
 
 // ---------------------------------------------------------- prologue --

@@ -1,16 +1,322 @@
-// prefill.cu -- causal prefill attention (tcgen05/TMEM kernel: in progress).
+// prefill.cu -- chunked causal prefill attention on the 5th-generation tensor
+// cores (tcgen05 + TMEM, TMA-fed).
+//
+// Replaces the reference prefill attention (assets/gpu_llm.cl:462-543, a
+// materialised [B][QH][history] score matrix; and the tiled online kernel of
+// assets/tiled_attention.cl:9-130 for queries > 1): query row i (absolute
+// position prior + i) attends to keys 0..=prior+i.
+//
+// One CTA per (128-row query tile, query head); heavy tiles (more keys)
+// launch first.  Warp roles:
+//   warp 0     TMA producer: the Q tile once, then 128-key K and V tiles through
+//              a two-stage ring (128-byte swizzle, this GPU's HBM, no multicast);
+//   warp 1     allocates 512 TMEM columns (S double buffer + O) and, from one
+//              lane, issues tcgen05.mma: S_j = Q K_j^T (K-major operands) and
+//              O_j = P_j V_j (P from shared memory, V as an MN-major operand);
+//   warps 2-5  one thread per query row (its TMEM lane): read S_j, causal mask,
+//              online softmax in exp2, P_j as bf16 into a swizzled shared tile,
+//              O accumulated in registers as acc = acc * alpha + O_j.
+// Every mbarrier wait is bounded; the CTA always frees its TMEM.
 #include "../../include/mslim_cuda.h"
 #include "prefill.cuh"
 
 namespace mslim {
 
-bool prefill_supported(unsigned, unsigned) { return false; }
+namespace {
 
-int launch_prefill(unsigned, unsigned, unsigned, const uint16_t *, const uint16_t *,
-                   const uint16_t *, uint16_t *, unsigned, unsigned, float, int *, cudaStream_t,
-                   std::string *err) {
-    *err = "the tcgen05 prefill kernel is not built";
-    return MSLIM_ERR_INVALID_GEOMETRY;
+constexpr int kRows = 128;                 // query rows per CTA = TMEM lanes
+constexpr int kKeys = 128;                 // keys per tile
+constexpr int kDim = 128;                  // head_dim
+constexpr int kBox = kRows * 128;          // one [128 rows][64 bf16] swizzled box: 16 KB
+constexpr int kQBytes = 2 * kBox;          // Q tile (two 64-column boxes)
+constexpr int kTileBytes = 2 * kBox;       // one K or V tile
+constexpr int kStages = 2;
+constexpr int kStageBytes = 2 * kTileBytes;  // K + V
+constexpr int kPBytes = 2 * kBox;
+constexpr int kOffKV = kQBytes;
+constexpr int kOffP = kOffKV + kStages * kStageBytes;
+constexpr int kOffBar = kOffP + kPBytes;
+constexpr int kSmemBytes = kOffBar + 256 + 1024;  // barriers + alignment slack
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256;
+
+// Instruction descriptors (kind::f16): D f32, A/B bf16, M=128, N=128;
+// S: A and B K-major; PV: B (V) MN-major.
+constexpr uint32_t kIdescS = (1u << 4) | (1u << 7) | (1u << 10) | ((kKeys >> 3) << 17) | ((kRows >> 4) << 24);
+constexpr uint32_t kIdescPV = kIdescS | (1u << 16);
+
+struct Bars {
+    uint64_t q_full;
+    uint64_t kv_full[kStages];
+    uint64_t kv_empty[kStages];
+    uint64_t s_full[2];
+    uint64_t s_empty[2];
+    uint64_t p_full;
+    uint64_t o_full;
+    uint64_t o_empty;
+    uint32_t tmem_base;
+    int abort;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    mslim_prefill_causal(const __grid_constant__ CUtensorMap qmap,
+                         const __grid_constant__ CUtensorMap kmap,
+                         const __grid_constant__ CUtensorMap vmap, const PrefillParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Bars *bars = reinterpret_cast<Bars *>(smem + kOffBar);
+    volatile int *abort_flag = &bars->abort;
+
+    const int bid = blockIdx.x;
+    const int qt = p.n_qtiles - 1 - bid / p.qheads;  // heavy (late) tiles first
+    const int qh = bid % p.qheads;
+    const int kvh = qh / p.group;
+    const int q0 = qt * kRows;
+    const int last_row = min(q0 + kRows, p.queries) - 1;
+    const int n_kv = (p.prior + last_row) / kKeys + 1;  // key tiles this CTA needs
+    const int first_pos = p.prior + q0;                 // smallest query position here
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        mbar_init(&bars->q_full, 1);
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&bars->kv_full[s], 1);
+            mbar_init(&bars->kv_empty[s], 1);
+        }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&bars->s_full[s], 1);
+            mbar_init(&bars->s_empty[s], 4);
+        }
+        mbar_init(&bars->p_full, 4);
+        mbar_init(&bars->o_full, 1);
+        mbar_init(&bars->o_empty, 4);
+        bars->abort = 0;
+        fence_mbarrier_init();
+    }
+    if (warp == 1) tmem_alloc(&bars->tmem_base, kTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+    const uint32_t sbase = smem_u32(smem);
+
+    if (warp == 0) {
+        // ---------------------------------------------------------- TMA --
+        if (lane == 0) {
+            prefetch_tmap(&qmap);
+            prefetch_tmap(&kmap);
+            prefetch_tmap(&vmap);
+            mbar_arrive_expect_tx(&bars->q_full, kQBytes);
+            tma_load_3d(smem, &qmap, &bars->q_full, 0, qh, q0);
+            tma_load_3d(smem + kBox, &qmap, &bars->q_full, 64, qh, q0);
+            int issued = 0;
+            for (int j = 0; j < n_kv && !*abort_flag; ++j) {
+                const int st = j % kStages;
+                if (!mbar_wait(&bars->kv_empty[st], ((j / kStages) & 1) ^ 1, p.status, 11)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                uint8_t *kdst = smem + kOffKV + st * kStageBytes;
+                uint8_t *vdst = kdst + kTileBytes;
+                mbar_arrive_expect_tx(&bars->kv_full[st], kStageBytes);
+                tma_load_3d(kdst, &kmap, &bars->kv_full[st], 0, kvh, j * kKeys);
+                tma_load_3d(kdst + kBox, &kmap, &bars->kv_full[st], 64, kvh, j * kKeys);
+                tma_load_3d(vdst, &vmap, &bars->kv_full[st], 0, kvh, j * kKeys);
+                tma_load_3d(vdst + kBox, &vmap, &bars->kv_full[st], 64, kvh, j * kKeys);
+                issued = j + 1;
+            }
+            // Our copies must land before the CTA can retire.
+            mbar_wait(&bars->q_full, 0, p.status, 12);
+            for (int j = max(0, issued - kStages); j < issued; ++j)
+                mbar_wait(&bars->kv_full[j % kStages], (j / kStages) & 1, p.status, 13);
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------- MMA --
+        if (lane == 0) {
+            bool ok = mbar_wait(&bars->q_full, 0, p.status, 21);
+            auto issue_s = [&](int j) -> bool {
+                const int st = j % kStages, sb = j & 1;
+                if (!mbar_wait(&bars->kv_full[st], (j / kStages) & 1, p.status, 22)) return false;
+                if (!mbar_wait(&bars->s_empty[sb], ((j >> 1) & 1) ^ 1, p.status, 23)) return false;
+                tc_fence_after();
+                const uint32_t kaddr = sbase + kOffKV + st * kStageBytes;
+#pragma unroll
+                for (int kk = 0; kk < kDim / 16; ++kk) {
+                    const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
+                    umma_bf16(tmem + (sb ? kColS1 : kColS0), umma_desc_sw128(sbase + off, 16, 1024),
+                              umma_desc_sw128(kaddr + off, 16, 1024), kIdescS, kk > 0);
+                }
+                umma_commit(&bars->s_full[sb]);
+                return true;
+            };
+            auto issue_pv = [&](int i) -> bool {
+                const int st = i % kStages;
+                if (!mbar_wait(&bars->p_full, i & 1, p.status, 24)) return false;
+                if (!mbar_wait(&bars->o_empty, (i & 1) ^ 1, p.status, 25)) return false;
+                tc_fence_after();
+                const uint32_t vaddr = sbase + kOffKV + st * kStageBytes + kTileBytes;
+                const uint32_t paddr = sbase + kOffP;
+#pragma unroll
+                for (int kk = 0; kk < kKeys / 16; ++kk) {
+                    // A = P (K-major, keys contiguous), B = V (MN-major: 64-dim
+                    // rows of 128 B, 8-key groups 1 KB apart, dim halves one box apart)
+                    const uint64_t a = umma_desc_sw128(paddr + (kk >> 2) * kBox + (kk & 3) * 32, 16, 1024);
+                    const uint64_t b = umma_desc_sw128(vaddr + kk * 16 * 128, kBox, 1024);
+                    umma_bf16(tmem + kColO, a, b, kIdescPV, kk > 0);
+                }
+                umma_commit(&bars->o_full);
+                umma_commit(&bars->kv_empty[st]);
+                return true;
+            };
+            for (int j = 0; ok && j <= n_kv && !*abort_flag; ++j) {
+                if (j < n_kv) ok = issue_s(j);
+                if (ok && j >= 1) ok = issue_pv(j - 1);
+            }
+            if (!ok) *abort_flag = 1;
+        }
+    } else {
+        // ------------------------------------------------------ softmax --
+        const int quarter = warp & 3;                  // TMEM lane quarter of this warp
+        const int row = quarter * 32 + lane;           // query row within the tile
+        const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+        const int qpos = p.prior + q0 + row;           // absolute position of this row
+        const float scale = p.scale_log2;
+        float acc[kDim];
+#pragma unroll
+        for (int d = 0; d < kDim; ++d) acc[d] = 0.f;
+        float m_run = -INFINITY, l_run = 0.f, alpha_prev = 1.f;
+        uint8_t *prow = smem + kOffP;
+        bool ok = true;
+        for (int j = 0; j < n_kv; ++j) {
+            const int sb = j & 1;
+            const uint32_t scol = lane_addr + (sb ? kColS1 : kColS0);
+            // every lane waits; the decision is made warp-uniform so the
+            // .sync.aligned TMEM loads below never run divergently
+            const bool got = mbar_wait(&bars->s_full[sb], (j >> 1) & 1, p.status, 31);
+            if (!__all_sync(0xffffffffu, got) || __any_sync(0xffffffffu, *abort_flag != 0)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const int kv0 = j * kKeys;
+            const bool masked = kv0 + kKeys - 1 > first_pos;
+            // pass 1: row maximum of the scaled, masked scores
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                float v[32];
+                tmem_ld32(scol + c * 32, v);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const float s = (masked && kv0 + c * 32 + i > qpos) ? -INFINITY : v[i] * scale;
+                    mx = fmaxf(mx, s);
+                }
+            }
+            const float m_new = fmaxf(m_run, mx);
+            const float base = (m_new == -INFINITY) ? 0.f : m_new;
+            const float alpha = fast_exp2(m_run - base);
+            // finish acc with the previous tile's O (this also frees P)
+            if (j > 0) {
+                const bool gotc = mbar_wait(&bars->o_full, (j - 1) & 1, p.status, 32);
+                if (!__all_sync(0xffffffffu, gotc)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    float o[32];
+                    tmem_ld32(lane_addr + kColO + c * 32, o);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) acc[c * 32 + i] = acc[c * 32 + i] * alpha_prev + o[i];
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->o_empty);
+            }
+            // pass 2: P = exp2(s - m) as bf16 into the swizzled P tile
+            float ps = 0.f;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                float v[32];
+                tmem_ld32(scol + c * 32, v);
+                uint32_t w[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int k0 = kv0 + c * 32 + 2 * i;
+                    const float p0 = (masked && k0 > qpos) ? 0.f : fast_exp2(v[2 * i] * scale - base);
+                    const float p1 = (masked && k0 + 1 > qpos) ? 0.f : fast_exp2(v[2 * i + 1] * scale - base);
+                    ps += p0 + p1;
+                    w[i] = pack_bf16x2(p0, p1);
+                }
+                uint8_t *box = prow + (c >> 1) * kBox + row * 128;
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const int ch = (c & 1) * 4 + t;
+                    *reinterpret_cast<uint4 *>(box + ((ch ^ (row & 7)) << 4)) =
+                        make_uint4(w[4 * t], w[4 * t + 1], w[4 * t + 2], w[4 * t + 3]);
+                }
+            }
+            tc_fence_before();
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&bars->s_empty[sb]);
+                mbar_arrive(&bars->p_full);
+            }
+            l_run = l_run * alpha + ps;
+            m_run = m_new;
+            alpha_prev = alpha;
+        }
+        const bool last = ok && mbar_wait(&bars->o_full, (n_kv - 1) & 1, p.status, 33);
+        if (__all_sync(0xffffffffu, last)) {
+            tc_fence_after();
+            const int qrow = q0 + row;
+            const float inv = 1.0f / l_run;
+            uint16_t *dst = p.out + ((size_t)qrow * p.qheads + qh) * kDim;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                float o[32];
+                tmem_ld32(lane_addr + kColO + c * 32, o);
+                uint32_t w[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    w[i] = pack_bf16x2((acc[c * 32 + 2 * i] * alpha_prev + o[2 * i]) * inv,
+                                       (acc[c * 32 + 2 * i + 1] * alpha_prev + o[2 * i + 1]) * inv);
+                if (qrow < p.queries) {
+#pragma unroll
+                    for (int t = 0; t < 4; ++t)
+                        reinterpret_cast<uint4 *>(dst + c * 32)[t] =
+                            make_uint4(w[4 * t], w[4 * t + 1], w[4 * t + 2], w[4 * t + 3]);
+                }
+            }
+        } else {
+            *abort_flag = 1;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+}  // namespace
+
+bool prefill_supported(unsigned head_dim, unsigned group) { return head_dim == 128 && group >= 1; }
+
+cudaError_t launch_prefill(const CUtensorMap &qmap, const CUtensorMap &kmap,
+                           const CUtensorMap &vmap, const PrefillParams &p, cudaStream_t stream) {
+    cudaError_t err = cudaFuncSetAttribute(mslim_prefill_causal,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (err != cudaSuccess) return err;
+    const unsigned grid = (unsigned)(p.n_qtiles * p.qheads);
+    mslim_prefill_causal<<<grid, kThreads, kSmemBytes, stream>>>(qmap, kmap, vmap, p);
+    return cudaGetLastError();
 }
 
 }  // namespace mslim

@@ -1,7 +1,5 @@
-// prefill.cuh -- launcher of the tcgen05/TMEM causal prefill kernel.
+// prefill.cuh -- parameters and launcher of the tcgen05/TMEM causal prefill.
 #pragma once
-
-#include <string>
 
 #include "mslim_common.cuh"
 
@@ -11,13 +9,19 @@ namespace mslim {
 // rather than the multi-query split-KV decode kernel.
 constexpr unsigned kPrefillMinQueries = 64;
 
+struct PrefillParams {
+    uint16_t *out;      // bf16 [queries][QH][D]
+    int *status;        // device status word
+    int qheads, kvheads, group;
+    int queries, prior; // rows prior..prior+queries-1 attend to keys 0..=row
+    int n_qtiles;       // ceil(queries / 128)
+    float scale_log2;   // log2(e) / sqrt(D)
+};
+
 bool prefill_supported(unsigned head_dim, unsigned group);
 
-// Enqueues causal attention of `queries` rows at positions prior.. over keys
-// 0..=prior+row.  Returns an MSLIM_* status; *err receives the message.
-int launch_prefill(unsigned qheads, unsigned kvheads, unsigned head_dim, const uint16_t *q,
-                   const uint16_t *k, const uint16_t *v, uint16_t *out, unsigned queries,
-                   unsigned prior, float scale_log2, int *status, cudaStream_t stream,
-                   std::string *err);
+// q/k/v maps: bf16, dims (D, heads, rows), box (64, 1, 128), 128-byte swizzle.
+cudaError_t launch_prefill(const CUtensorMap &qmap, const CUtensorMap &kmap,
+                           const CUtensorMap &vmap, const PrefillParams &p, cudaStream_t stream);
 
 }  // namespace mslim
