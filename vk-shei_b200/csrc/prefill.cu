@@ -13,9 +13,12 @@
 //   warp 1     allocates 512 TMEM columns (S double buffer + O) and, from one
 //              lane, issues tcgen05.mma: S_j = Q K_j^T (K-major operands) and
 //              O_j = P_j V_j (P from shared memory, V as an MN-major operand);
-//   warps 2-5  one thread per query row (its TMEM lane): read S_j, causal mask,
-//              online softmax in exp2, P_j as bf16 into a swizzled shared tile,
-//              O accumulated in registers as acc = acc * alpha + O_j.
+//   warps 2-9  two threads per query row (the row's TMEM lane, 64 columns
+//              each; the pair shares the row max through shared memory): read
+//              S_j once, causal mask, online softmax in exp2, P_j as bf16 into a
+//              swizzled shared tile.  O accumulates in TMEM across tiles; a row's
+//              max moves (and its O is rescaled in place) only when a tile's max
+//              exceeds it by more than 2^8.
 // Every mbarrier wait is bounded; the CTA always frees its TMEM.
 #include "../../include/mslim_cuda.h"
 #include "prefill.cuh"
@@ -35,11 +38,18 @@ constexpr int kStageBytes = 2 * kTileBytes;  // K + V
 constexpr int kPBytes = 2 * kBox;
 constexpr int kOffKV = kQBytes;
 constexpr int kOffP = kOffKV + kStages * kStageBytes;
-constexpr int kOffBar = kOffP + kPBytes;
+constexpr int kOffX = kOffP + kPBytes;       // row-max / row-sum exchange
+constexpr int kXBytes = (2 * 2 + 2) * kRows * 4;
+constexpr int kOffBar = kOffX + kXBytes;
 constexpr int kSmemBytes = kOffBar + 256 + 1024;  // barriers + alignment slack
-constexpr int kThreads = 192;
+constexpr int kSoftmaxWarps = 8;
+constexpr int kThreads = (2 + kSoftmaxWarps) * 32;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256;
+constexpr uint32_t kColS = 0, kColO = 256;     // S[2] at 0/128, O (accumulating) at 256
+// A row's running max is only moved (and O rescaled in TMEM) when a tile's
+// max exceeds it by more than 2^8; until then P uses the stale max, which is
+// exact arithmetic (numerator and denominator share it) with P <= 256.
+constexpr float kRescaleLog2 = 8.0f;
 
 // Instruction descriptors (kind::f16): D f32, A/B bf16, M=128, N=128;
 // S: A and B K-major; PV: B (V) MN-major.
@@ -53,11 +63,15 @@ struct Bars {
     uint64_t s_full[2];
     uint64_t s_empty[2];
     uint64_t p_full;
-    uint64_t o_full;
-    uint64_t o_empty;
+    uint64_t o_full;   // completes once per PV MMA group (O and P both safe after it)
     uint32_t tmem_base;
     int abort;
 };
+
+__device__ __forceinline__ void pair_sync(int quarter) {
+    // the two softmax warps that own the same 32 TMEM lanes (rows)
+    asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+}
 
 __global__ void __launch_bounds__(kThreads, 1)
     mslim_prefill_causal(const __grid_constant__ CUtensorMap qmap,
@@ -88,11 +102,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int s = 0; s < 2; ++s) {
             mbar_init(&bars->s_full[s], 1);
-            mbar_init(&bars->s_empty[s], 4);
+            mbar_init(&bars->s_empty[s], kSoftmaxWarps);
         }
-        mbar_init(&bars->p_full, 4);
+        mbar_init(&bars->p_full, kSoftmaxWarps);
         mbar_init(&bars->o_full, 1);
-        mbar_init(&bars->o_empty, 4);
         bars->abort = 0;
         fence_mbarrier_init();
     }
@@ -146,7 +159,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int kk = 0; kk < kDim / 16; ++kk) {
                     const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
-                    umma_bf16(tmem + (sb ? kColS1 : kColS0), umma_desc_sw128(sbase + off, 16, 1024),
+                    umma_bf16(tmem + kColS + sb * 128, umma_desc_sw128(sbase + off, 16, 1024),
                               umma_desc_sw128(kaddr + off, 16, 1024), kIdescS, kk > 0);
                 }
                 umma_commit(&bars->s_full[sb]);
@@ -154,8 +167,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             };
             auto issue_pv = [&](int i) -> bool {
                 const int st = i % kStages;
+                // P_i stored (and, when needed, O rescaled) by the softmax warps
                 if (!mbar_wait(&bars->p_full, i & 1, p.status, 24)) return false;
-                if (!mbar_wait(&bars->o_empty, (i & 1) ^ 1, p.status, 25)) return false;
                 tc_fence_after();
                 const uint32_t vaddr = sbase + kOffKV + st * kStageBytes + kTileBytes;
                 const uint32_t paddr = sbase + kOffP;
@@ -165,7 +178,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // rows of 128 B, 8-key groups 1 KB apart, dim halves one box apart)
                     const uint64_t a = umma_desc_sw128(paddr + (kk >> 2) * kBox + (kk & 3) * 32, 16, 1024);
                     const uint64_t b = umma_desc_sw128(vaddr + kk * 16 * 128, kBox, 1024);
-                    umma_bf16(tmem + kColO, a, b, kIdescPV, kk > 0);
+                    umma_bf16(tmem + kColO, a, b, kIdescPV, (i > 0 || kk > 0) ? 1u : 0u);
                 }
                 umma_commit(&bars->o_full);
                 umma_commit(&bars->kv_empty[st]);
@@ -179,113 +192,113 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ------------------------------------------------------ softmax --
-        const int quarter = warp & 3;                  // TMEM lane quarter of this warp
-        const int row = quarter * 32 + lane;           // query row within the tile
+        // Warps 2..9: a warp pair (w, w+4) owns the 32 rows of TMEM lane
+        // quarter w % 4; the first warp of the pair takes columns (keys, and
+        // output dims) 0..63, the second 64..127.
+        const int quarter = warp & 3;
+        const int half = (warp - 2) >> 2;
+        const int row = quarter * 32 + lane;
+        const int col0 = half * 64;
         const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+        const uint32_t ocol = lane_addr + kColO + col0;
         const int qpos = p.prior + q0 + row;           // absolute position of this row
         const float scale = p.scale_log2;
-        float acc[kDim];
-#pragma unroll
-        for (int d = 0; d < kDim; ++d) acc[d] = 0.f;
-        float m_run = -INFINITY, l_run = 0.f, alpha_prev = 1.f;
-        uint8_t *prow = smem + kOffP;
+        float *xmax = reinterpret_cast<float *>(smem + kOffX);  // [2 parity][2 half][128]
+        float *xsum = xmax + 4 * kRows;                          // [2 half][128]
+        float m_used = -INFINITY, l_part = 0.f;
+        uint8_t *pbox = smem + kOffP + half * kBox + row * 128;
         bool ok = true;
         for (int j = 0; j < n_kv; ++j) {
             const int sb = j & 1;
-            const uint32_t scol = lane_addr + (sb ? kColS1 : kColS0);
-            // every lane waits; the decision is made warp-uniform so the
-            // .sync.aligned TMEM loads below never run divergently
+            // every lane waits; decisions are warp-uniform so the
+            // .sync.aligned TMEM accesses never run divergently
             const bool got = mbar_wait(&bars->s_full[sb], (j >> 1) & 1, p.status, 31);
             if (!__all_sync(0xffffffffu, got) || __any_sync(0xffffffffu, *abort_flag != 0)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const int kv0 = j * kKeys;
-            const bool masked = kv0 + kKeys - 1 > first_pos;
-            // pass 1: row maximum of the scaled, masked scores
+            float sv[64];
+            tmem_ld32(lane_addr + kColS + sb * 128 + col0, *reinterpret_cast<float(*)[32]>(&sv[0]));
+            tmem_ld32(lane_addr + kColS + sb * 128 + col0 + 32, *reinterpret_cast<float(*)[32]>(&sv[32]));
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->s_empty[sb]);  // S buffer free for S_{j+2}
+            const int k0 = j * kKeys + col0;
+            const bool masked = j * kKeys + kKeys - 1 > first_pos;
             float mx = -INFINITY;
+            if (masked) {
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                float v[32];
-                tmem_ld32(scol + c * 32, v);
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const float s = (masked && kv0 + c * 32 + i > qpos) ? -INFINITY : v[i] * scale;
-                    mx = fmaxf(mx, s);
+                for (int i = 0; i < 64; ++i) {
+                    if (k0 + i > qpos) sv[i] = -INFINITY;
+                    mx = fmaxf(mx, sv[i]);
                 }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 64; ++i) mx = fmaxf(mx, sv[i]);
             }
-            const float m_new = fmaxf(m_run, mx);
+            xmax[((j & 1) * 2 + half) * kRows + row] = mx;
+            pair_sync(quarter);
+            mx = fmaxf(mx, xmax[((j & 1) * 2 + (half ^ 1)) * kRows + row]) * scale;
+            // move the row max only when this tile exceeds it by > 2^8
+            const bool move = mx > m_used + kRescaleLog2;
+            const float m_new = move ? mx : m_used;
             const float base = (m_new == -INFINITY) ? 0.f : m_new;
-            const float alpha = fast_exp2(m_run - base);
-            // finish acc with the previous tile's O (this also frees P)
+            const float alpha = move ? fast_exp2(m_used - base) : 1.f;
+            float ps = 0.f;
+            uint32_t w[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const float p0 = fast_exp2(fmaf(sv[2 * i], scale, -base));
+                const float p1 = fast_exp2(fmaf(sv[2 * i + 1], scale, -base));
+                ps += p0 + p1;
+                w[i] = pack_bf16x2(p0, p1);
+            }
             if (j > 0) {
+                // PV_{j-1} must be done: it reads the P tile and writes O
                 const bool gotc = mbar_wait(&bars->o_full, (j - 1) & 1, p.status, 32);
                 if (!__all_sync(0xffffffffu, gotc)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
+                if (__any_sync(0xffffffffu, move)) {
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    float o[32];
-                    tmem_ld32(lane_addr + kColO + c * 32, o);
+                    for (int c = 0; c < 2; ++c) {
+                        float o[32];
+                        tmem_ld32(ocol + c * 32, o);
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) acc[c * 32 + i] = acc[c * 32 + i] * alpha_prev + o[i];
-                }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&bars->o_empty);
-            }
-            // pass 2: P = exp2(s - m) as bf16 into the swizzled P tile
-            float ps = 0.f;
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                float v[32];
-                tmem_ld32(scol + c * 32, v);
-                uint32_t w[16];
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int k0 = kv0 + c * 32 + 2 * i;
-                    const float p0 = (masked && k0 > qpos) ? 0.f : fast_exp2(v[2 * i] * scale - base);
-                    const float p1 = (masked && k0 + 1 > qpos) ? 0.f : fast_exp2(v[2 * i + 1] * scale - base);
-                    ps += p0 + p1;
-                    w[i] = pack_bf16x2(p0, p1);
-                }
-                uint8_t *box = prow + (c >> 1) * kBox + row * 128;
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    const int ch = (c & 1) * 4 + t;
-                    *reinterpret_cast<uint4 *>(box + ((ch ^ (row & 7)) << 4)) =
-                        make_uint4(w[4 * t], w[4 * t + 1], w[4 * t + 2], w[4 * t + 3]);
+                        for (int i = 0; i < 32; ++i) o[i] *= alpha;
+                        tmem_st32(ocol + c * 32, o);
+                    }
                 }
             }
+#pragma unroll
+            for (int t = 0; t < 8; ++t)
+                *reinterpret_cast<uint4 *>(pbox + ((t ^ (row & 7)) << 4)) =
+                    make_uint4(w[4 * t], w[4 * t + 1], w[4 * t + 2], w[4 * t + 3]);
             tc_fence_before();
             fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&bars->s_empty[sb]);
-                mbar_arrive(&bars->p_full);
-            }
-            l_run = l_run * alpha + ps;
-            m_run = m_new;
-            alpha_prev = alpha;
+            if (lane == 0) mbar_arrive(&bars->p_full);
+            l_part = l_part * alpha + ps;
+            m_used = m_new;
         }
         const bool last = ok && mbar_wait(&bars->o_full, (n_kv - 1) & 1, p.status, 33);
         if (__all_sync(0xffffffffu, last)) {
             tc_fence_after();
+            xsum[half * kRows + row] = l_part;
+            pair_sync(quarter);
+            const float inv = 1.0f / (l_part + xsum[(half ^ 1) * kRows + row]);
             const int qrow = q0 + row;
-            const float inv = 1.0f / l_run;
-            uint16_t *dst = p.out + ((size_t)qrow * p.qheads + qh) * kDim;
+            uint16_t *dst = p.out + ((size_t)qrow * p.qheads + qh) * kDim + col0;
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < 2; ++c) {
                 float o[32];
-                tmem_ld32(lane_addr + kColO + c * 32, o);
+                tmem_ld32(ocol + c * 32, o);
                 uint32_t w[16];
 #pragma unroll
-                for (int i = 0; i < 16; ++i)
-                    w[i] = pack_bf16x2((acc[c * 32 + 2 * i] * alpha_prev + o[2 * i]) * inv,
-                                       (acc[c * 32 + 2 * i + 1] * alpha_prev + o[2 * i + 1]) * inv);
+                for (int i = 0; i < 16; ++i) w[i] = pack_bf16x2(o[2 * i] * inv, o[2 * i + 1] * inv);
                 if (qrow < p.queries) {
 #pragma unroll
                     for (int t = 0; t < 4; ++t)
