@@ -8,8 +8,10 @@
 //
 // One CTA per (128-row query tile, query head); heavy tiles (more keys)
 // launch first.  Warp roles:
-//   warp 0     TMA producer: the Q tile once, then 128-key K and V tiles through
-//              a two-stage ring (128-byte swizzle, this GPU's HBM, no multicast);
+//   warps 0,10 TMA producers: the Q tile once and 128-key K tiles (warp 0),
+//              V tiles (warp 10), each through its own two-slot ring (128-byte
+//              swizzle, this GPU's HBM, no multicast); a K slot is released as
+//              soon as S_j is computed, a V slot after PV_j;
 //   warp 1     allocates 512 TMEM columns (S double buffer + O) and, from one
 //              lane, issues tcgen05.mma: S_j = Q K_j^T (K-major operands) and
 //              O_j = P_j V_j (P from shared memory, V as an MN-major operand);
@@ -33,17 +35,18 @@ constexpr int kDim = 128;                  // head_dim
 constexpr int kBox = kRows * 128;          // one [128 rows][64 bf16] swizzled box: 16 KB
 constexpr int kQBytes = 2 * kBox;          // Q tile (two 64-column boxes)
 constexpr int kTileBytes = 2 * kBox;       // one K or V tile
-constexpr int kStages = 2;
-constexpr int kStageBytes = 2 * kTileBytes;  // K + V
+constexpr int kStages = 2;                   // slots in each of the K and V rings
 constexpr int kPBytes = 2 * kBox;
-constexpr int kOffKV = kQBytes;
-constexpr int kOffP = kOffKV + kStages * kStageBytes;
+constexpr int kOffK = kQBytes;               // K ring: slot s at kOffK + s * kTileBytes
+constexpr int kOffV = kOffK + kStages * kTileBytes;
+constexpr int kOffP = kOffV + kStages * kTileBytes;
 constexpr int kOffX = kOffP + kPBytes;       // row-max / row-sum exchange
 constexpr int kXBytes = (2 * 2 + 2) * kRows * 4;
 constexpr int kOffBar = kOffX + kXBytes;
 constexpr int kSmemBytes = kOffBar + 256 + 1024;  // barriers + alignment slack
 constexpr int kSoftmaxWarps = 8;
-constexpr int kThreads = (2 + kSoftmaxWarps) * 32;
+constexpr int kVWarp = 2 + kSoftmaxWarps;      // the V producer warp
+constexpr int kThreads = (3 + kSoftmaxWarps) * 32;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColO = 256;     // S[2] at 0/128, O (accumulating) at 256
 // A row's running max is only moved (and O rescaled in TMEM) when a tile's
@@ -58,8 +61,10 @@ constexpr uint32_t kIdescPV = kIdescS | (1u << 16);
 
 struct Bars {
     uint64_t q_full;
-    uint64_t kv_full[kStages];
-    uint64_t kv_empty[kStages];
+    uint64_t k_full[kStages];
+    uint64_t k_empty[kStages];   // freed when S_j (its only reader) completes
+    uint64_t v_full[kStages];
+    uint64_t v_empty[kStages];   // freed when PV_j completes
     uint64_t s_full[2];
     uint64_t s_empty[2];
     uint64_t p_full;
@@ -97,8 +102,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
         mbar_init(&bars->q_full, 1);
         for (int s = 0; s < kStages; ++s) {
-            mbar_init(&bars->kv_full[s], 1);
-            mbar_init(&bars->kv_empty[s], 1);
+            mbar_init(&bars->k_full[s], 1);
+            mbar_init(&bars->k_empty[s], 1);
+            mbar_init(&bars->v_full[s], 1);
+            mbar_init(&bars->v_empty[s], 1);
         }
         for (int s = 0; s < 2; ++s) {
             mbar_init(&bars->s_full[s], 1);
@@ -116,35 +123,39 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = bars->tmem_base;
     const uint32_t sbase = smem_u32(smem);
 
-    if (warp == 0) {
+    if (warp == 0 || warp == kVWarp) {
         // ---------------------------------------------------------- TMA --
+        // warp 0 loads Q and the K ring, warp kVWarp the V ring
         if (lane == 0) {
-            prefetch_tmap(&qmap);
-            prefetch_tmap(&kmap);
-            prefetch_tmap(&vmap);
-            mbar_arrive_expect_tx(&bars->q_full, kQBytes);
-            tma_load_3d(smem, &qmap, &bars->q_full, 0, qh, q0);
-            tma_load_3d(smem + kBox, &qmap, &bars->q_full, 64, qh, q0);
+            const bool is_k = warp == 0;
+            const CUtensorMap *map = is_k ? &kmap : &vmap;
+            uint64_t *full = is_k ? bars->k_full : bars->v_full;
+            uint64_t *empty = is_k ? bars->k_empty : bars->v_empty;
+            uint8_t *ring = smem + (is_k ? kOffK : kOffV);
+            prefetch_tmap(map);
+            if (is_k) {
+                prefetch_tmap(&qmap);
+                mbar_arrive_expect_tx(&bars->q_full, kQBytes);
+                tma_load_3d(smem, &qmap, &bars->q_full, 0, qh, q0);
+                tma_load_3d(smem + kBox, &qmap, &bars->q_full, 64, qh, q0);
+            }
             int issued = 0;
             for (int j = 0; j < n_kv && !*abort_flag; ++j) {
                 const int st = j % kStages;
-                if (!mbar_wait(&bars->kv_empty[st], ((j / kStages) & 1) ^ 1, p.status, 11)) {
+                if (!mbar_wait(&empty[st], ((j / kStages) & 1) ^ 1, p.status, is_k ? 11 : 14)) {
                     *abort_flag = 1;
                     break;
                 }
-                uint8_t *kdst = smem + kOffKV + st * kStageBytes;
-                uint8_t *vdst = kdst + kTileBytes;
-                mbar_arrive_expect_tx(&bars->kv_full[st], kStageBytes);
-                tma_load_3d(kdst, &kmap, &bars->kv_full[st], 0, kvh, j * kKeys);
-                tma_load_3d(kdst + kBox, &kmap, &bars->kv_full[st], 64, kvh, j * kKeys);
-                tma_load_3d(vdst, &vmap, &bars->kv_full[st], 0, kvh, j * kKeys);
-                tma_load_3d(vdst + kBox, &vmap, &bars->kv_full[st], 64, kvh, j * kKeys);
+                uint8_t *dst = ring + st * kTileBytes;
+                mbar_arrive_expect_tx(&full[st], kTileBytes);
+                tma_load_3d(dst, map, &full[st], 0, kvh, j * kKeys);
+                tma_load_3d(dst + kBox, map, &full[st], 64, kvh, j * kKeys);
                 issued = j + 1;
             }
             // Our copies must land before the CTA can retire.
-            mbar_wait(&bars->q_full, 0, p.status, 12);
+            if (is_k) mbar_wait(&bars->q_full, 0, p.status, 12);
             for (int j = max(0, issued - kStages); j < issued; ++j)
-                mbar_wait(&bars->kv_full[j % kStages], (j / kStages) & 1, p.status, 13);
+                mbar_wait(&full[j % kStages], (j / kStages) & 1, p.status, 13);
         }
     } else if (warp == 1) {
         // ---------------------------------------------------------- MMA --
@@ -152,10 +163,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = mbar_wait(&bars->q_full, 0, p.status, 21);
             auto issue_s = [&](int j) -> bool {
                 const int st = j % kStages, sb = j & 1;
-                if (!mbar_wait(&bars->kv_full[st], (j / kStages) & 1, p.status, 22)) return false;
+                if (!mbar_wait(&bars->k_full[st], (j / kStages) & 1, p.status, 22)) return false;
                 if (!mbar_wait(&bars->s_empty[sb], ((j >> 1) & 1) ^ 1, p.status, 23)) return false;
                 tc_fence_after();
-                const uint32_t kaddr = sbase + kOffKV + st * kStageBytes;
+                const uint32_t kaddr = sbase + kOffK + st * kTileBytes;
 #pragma unroll
                 for (int kk = 0; kk < kDim / 16; ++kk) {
                     const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
@@ -163,14 +174,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                               umma_desc_sw128(kaddr + off, 16, 1024), kIdescS, kk > 0);
                 }
                 umma_commit(&bars->s_full[sb]);
+                umma_commit(&bars->k_empty[st]);
                 return true;
             };
             auto issue_pv = [&](int i) -> bool {
                 const int st = i % kStages;
                 // P_i stored (and, when needed, O rescaled) by the softmax warps
+                if (!mbar_wait(&bars->v_full[st], (i / kStages) & 1, p.status, 26)) return false;
                 if (!mbar_wait(&bars->p_full, i & 1, p.status, 24)) return false;
                 tc_fence_after();
-                const uint32_t vaddr = sbase + kOffKV + st * kStageBytes + kTileBytes;
+                const uint32_t vaddr = sbase + kOffV + st * kTileBytes;
                 const uint32_t paddr = sbase + kOffP;
 #pragma unroll
                 for (int kk = 0; kk < kKeys / 16; ++kk) {
@@ -181,7 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     umma_bf16(tmem + kColO, a, b, kIdescPV, (i > 0 || kk > 0) ? 1u : 0u);
                 }
                 umma_commit(&bars->o_full);
-                umma_commit(&bars->kv_empty[st]);
+                umma_commit(&bars->v_empty[st]);
                 return true;
             };
             for (int j = 0; ok && j <= n_kv && !*abort_flag; ++j) {
@@ -190,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (!ok) *abort_flag = 1;
         }
-    } else {
+    } else if (warp >= 2 && warp < 2 + kSoftmaxWarps) {
         // ------------------------------------------------------ softmax --
         // Warps 2..9: a warp pair (w, w+4) owns the 32 rows of TMEM lane
         // quarter w % 4; the first warp of the pair takes columns (keys, and
@@ -219,24 +232,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tc_fence_after();
             float sv[64];
-            tmem_ld32(lane_addr + kColS + sb * 128 + col0, *reinterpret_cast<float(*)[32]>(&sv[0]));
-            tmem_ld32(lane_addr + kColS + sb * 128 + col0 + 32, *reinterpret_cast<float(*)[32]>(&sv[32]));
+            tmem_ld64(lane_addr + kColS + sb * 128 + col0, sv);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars->s_empty[sb]);  // S buffer free for S_{j+2}
             const int k0 = j * kKeys + col0;
             const bool masked = j * kKeys + kKeys - 1 > first_pos;
-            float mx = -INFINITY;
             if (masked) {
 #pragma unroll
-                for (int i = 0; i < 64; ++i) {
+                for (int i = 0; i < 64; ++i)
                     if (k0 + i > qpos) sv[i] = -INFINITY;
-                    mx = fmaxf(mx, sv[i]);
-                }
-            } else {
-#pragma unroll
-                for (int i = 0; i < 64; ++i) mx = fmaxf(mx, sv[i]);
             }
+            // eight independent partial maxima (short dependency chains)
+            float m8[8];
+#pragma unroll
+            for (int a = 0; a < 8; ++a) m8[a] = sv[a];
+#pragma unroll
+            for (int i = 8; i < 64; ++i) m8[i & 7] = fmaxf(m8[i & 7], sv[i]);
+            float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
             xmax[((j & 1) * 2 + half) * kRows + row] = mx;
             pair_sync(quarter);
             mx = fmaxf(mx, xmax[((j & 1) * 2 + (half ^ 1)) * kRows + row]) * scale;
@@ -245,15 +259,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float m_new = move ? mx : m_used;
             const float base = (m_new == -INFINITY) ? 0.f : m_new;
             const float alpha = move ? fast_exp2(m_used - base) : 1.f;
-            float ps = 0.f;
+            float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
             uint32_t w[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
                 const float p0 = fast_exp2(fmaf(sv[2 * i], scale, -base));
                 const float p1 = fast_exp2(fmaf(sv[2 * i + 1], scale, -base));
-                ps += p0 + p1;
+                s8[i & 7] += p0 + p1;
                 w[i] = pack_bf16x2(p0, p1);
             }
+            const float ps = ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
             if (j > 0) {
                 // PV_{j-1} must be done: it reads the P tile and writes O
                 const bool gotc = mbar_wait(&bars->o_full, (j - 1) & 1, p.status, 32);
