@@ -697,9 +697,10 @@ int mslim_cuda_prefill_causal(const mslim_geometry_t *geometry, const void *q, c
         const uint64_t kd[3] = {D, geometry->kv_heads, history};
         const uint64_t ks[2] = {D * 2, (uint64_t)geometry->kv_heads * D * 2};
         const uint32_t box[3] = {64, 1, 128};
+        const uint32_t kvbox[3] = {64, 1, 128};
         if (int rc = make_tmap(&qmap, q, 3, qd, qs, box)) return rc;
-        if (int rc = make_tmap(&kmap, k, 3, kd, ks, box)) return rc;
-        if (int rc = make_tmap(&vmap, v, 3, kd, ks, box)) return rc;
+        if (int rc = make_tmap(&kmap, k, 3, kd, ks, kvbox)) return rc;
+        if (int rc = make_tmap(&vmap, v, 3, kd, ks, kvbox)) return rc;
     }
     mslim::PrefillParams p{};
     p.out = static_cast<uint16_t *>(out);

@@ -159,12 +159,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 1) {
         // ---------------------------------------------------------- MMA --
-        if (lane == 0) {
-            bool ok = mbar_wait(&bars->q_full, 0, p.status, 21);
+        // the whole warp runs this loop (uniform control flow); umma_* elect
+        // the issuing lane
+        {
+            bool ok = __all_sync(0xffffffffu, mbar_wait(&bars->q_full, 0, p.status, 21));
             auto issue_s = [&](int j) -> bool {
                 const int st = j % kStages, sb = j & 1;
-                if (!mbar_wait(&bars->k_full[st], (j / kStages) & 1, p.status, 22)) return false;
-                if (!mbar_wait(&bars->s_empty[sb], ((j >> 1) & 1) ^ 1, p.status, 23)) return false;
+                if (!__all_sync(0xffffffffu, mbar_wait(&bars->k_full[st], (j / kStages) & 1, p.status, 22))) return false;
+                if (!__all_sync(0xffffffffu, mbar_wait(&bars->s_empty[sb], ((j >> 1) & 1) ^ 1, p.status, 23))) return false;
                 tc_fence_after();
                 const uint32_t kaddr = sbase + kOffK + st * kTileBytes;
 #pragma unroll
@@ -180,8 +182,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             auto issue_pv = [&](int i) -> bool {
                 const int st = i % kStages;
                 // P_i stored (and, when needed, O rescaled) by the softmax warps
-                if (!mbar_wait(&bars->v_full[st], (i / kStages) & 1, p.status, 26)) return false;
-                if (!mbar_wait(&bars->p_full, i & 1, p.status, 24)) return false;
+                if (!__all_sync(0xffffffffu, mbar_wait(&bars->v_full[st], (i / kStages) & 1, p.status, 26))) return false;
+                if (!__all_sync(0xffffffffu, mbar_wait(&bars->p_full, i & 1, p.status, 24))) return false;
                 tc_fence_after();
                 const uint32_t vaddr = sbase + kOffV + st * kTileBytes;
                 const uint32_t paddr = sbase + kOffP;
@@ -197,11 +199,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 umma_commit(&bars->v_empty[st]);
                 return true;
             };
-            for (int j = 0; ok && j <= n_kv && !*abort_flag; ++j) {
-                if (j < n_kv) ok = issue_s(j);
-                if (ok && j >= 1) ok = issue_pv(j - 1);
+            for (int j = 0; ok && j <= n_kv; ++j) {
+                if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
+                if (j < n_kv) ok = __all_sync(0xffffffffu, issue_s(j));
+                if (ok && j >= 1) ok = __all_sync(0xffffffffu, issue_pv(j - 1));
             }
-            if (!ok) *abort_flag = 1;
+            if (!ok && lane == 0) *abort_flag = 1;
         }
     } else if (warp >= 2 && warp < 2 + kSoftmaxWarps) {
         // ------------------------------------------------------ softmax --
@@ -333,12 +336,319 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Two heads per CTA (ping-pong), P kept in tensor memory.  A CTA takes one
+// 128-row query tile of two query heads that share a KV head: every K/V byte it
+// loads serves both, both heads have the same causal extent, and while one
+// head's softmax warpgroup works, the tensor core runs the other head's MMAs.
+//   smem: Q_A, Q_B (32 KB each), K ring 2 x 32 KB, V ring 2 x 32 KB (192 KB);
+//   TMEM: S_A (0), S_B (128), O_A (256), O_B (384); P_h is written as bf16
+//         pairs over the first 64 columns of S_h once S_h has been read, and
+//         O_h += P_h V is a TS-MMA (A from TMEM), so P never touches shared
+//         memory and shared-memory operand traffic stays under the tensor
+//         core's rate.
+//   Tensor-core order per key tile j: PV_A(j), S_A(j+1), PV_B(j), S_B(j+1);
+//   S_h(j+1) overwrites P_h(j) only after PV_h(j), which precedes it in the
+//   (in-order) tcgen05 pipe, and S_h(j) done implies PV_h(j-1) done.
+//   Warps: 0 TMA Q+K, 1 MMA, 2 TMA V, 3 idle (warpgroup 0, 88 registers);
+//          4-7 softmax head A, 8-11 softmax head B (200 registers each;
+//          128 x 88 + 256 x 200 <= the 384 x 168 registers of the launch).
+constexpr int kPOffQ = 0;                           // Q_h at h * kQBytes
+constexpr int kPOffK = 2 * kQBytes;                 // K slot s at kPOffK + s * kTileBytes
+constexpr int kPOffV = kPOffK + 2 * kTileBytes;
+constexpr int kPOffBar = kPOffV + 2 * kTileBytes;
+constexpr int kPSmemBytes = kPOffBar + 512 + 1024;
+constexpr int kPThreads = 12 * 32;
+
+struct PairBars {
+    uint64_t q_full;
+    uint64_t k_full[2], k_empty[2];
+    uint64_t v_full[2], v_empty[2];
+    uint64_t s_full[2];   // [head], once per key tile
+    uint64_t p_full[2];   // [head], once per key tile (4 warps)
+    uint64_t o_done[2];   // [head], after the last PV
+    uint32_t tmem_base;
+    int abort;
+};
+
+__global__ void __launch_bounds__(kPThreads, 1)
+    mslim_prefill_pair(const __grid_constant__ CUtensorMap qmap,
+                       const __grid_constant__ CUtensorMap kmap,
+                       const __grid_constant__ CUtensorMap vmap, const PrefillParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    PairBars *bars = reinterpret_cast<PairBars *>(smem + kPOffBar);
+    volatile int *abort_flag = &bars->abort;
+
+    const int pairs = p.qheads / 2;
+    const int bid = blockIdx.x;
+    const int qt = p.n_qtiles - 1 - bid / pairs;  // heavy (late) tiles first
+    const int qh0 = 2 * (bid % pairs);            // heads qh0, qh0 + 1 share a KV head
+    const int kvh = qh0 / p.group;
+    const int q0 = qt * kRows;
+    const int last_row = min(q0 + kRows, p.queries) - 1;
+    const int n_kv = (p.prior + last_row) / kKeys + 1;
+    const int first_pos = p.prior + q0;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        mbar_init(&bars->q_full, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&bars->k_full[b], 1);
+            mbar_init(&bars->k_empty[b], 1);
+            mbar_init(&bars->v_full[b], 1);
+            mbar_init(&bars->v_empty[b], 1);
+            mbar_init(&bars->s_full[b], 1);
+            mbar_init(&bars->p_full[b], 4);
+            mbar_init(&bars->o_done[b], 1);
+        }
+        bars->abort = 0;
+        fence_mbarrier_init();
+    }
+    if (warp == 1) tmem_alloc(&bars->tmem_base, kTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+    const uint32_t sbase = smem_u32(smem);
+
+    if (warp < 4) {
+        warpgroup_reg_dealloc<88>();
+        if ((warp == 0 || warp == 2) && lane == 0) {
+            // ------------------------------------------------------ TMA --
+            const bool is_k = warp == 0;
+            const CUtensorMap *map = is_k ? &kmap : &vmap;
+            uint64_t *full = is_k ? bars->k_full : bars->v_full;
+            uint64_t *empty = is_k ? bars->k_empty : bars->v_empty;
+            uint8_t *ring = smem + (is_k ? kPOffK : kPOffV);
+            prefetch_tmap(map);
+            if (is_k) {
+                prefetch_tmap(&qmap);
+                mbar_arrive_expect_tx(&bars->q_full, 2 * kQBytes);
+                for (int h = 0; h < 2; ++h) {
+                    tma_load_3d(smem + kPOffQ + h * kQBytes, &qmap, &bars->q_full, 0, qh0 + h, q0);
+                    tma_load_3d(smem + kPOffQ + h * kQBytes + kBox, &qmap, &bars->q_full, 64, qh0 + h, q0);
+                }
+            }
+            int issued = 0;
+            for (int j = 0; j < n_kv && !*abort_flag; ++j) {
+                const int st = j & 1;
+                if (!mbar_wait(&empty[st], ((j >> 1) & 1) ^ 1, p.status, is_k ? 41 : 42)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                uint8_t *dst = ring + st * kTileBytes;
+                mbar_arrive_expect_tx(&full[st], kTileBytes);
+                tma_load_3d(dst, map, &full[st], 0, kvh, j * kKeys);
+                tma_load_3d(dst + kBox, map, &full[st], 64, kvh, j * kKeys);
+                issued = j + 1;
+            }
+            if (is_k) mbar_wait(&bars->q_full, 0, p.status, 43);
+            for (int j = max(0, issued - 2); j < issued; ++j)
+                mbar_wait(&full[j & 1], (j >> 1) & 1, p.status, 44);
+        } else if (warp == 1) {
+            // ------------------------------------------------------ MMA --
+            // the whole warp runs the loop; umma_* elect the issuing lane
+            auto wait_all = [&](uint64_t *bar, uint32_t parity, int where) -> bool {
+                return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.status, where));
+            };
+            auto issue_s = [&](int h, int j) {
+                const uint32_t qaddr = sbase + kPOffQ + h * kQBytes;
+                const uint32_t kaddr = sbase + kPOffK + (j & 1) * kTileBytes;
+#pragma unroll
+                for (int kk = 0; kk < kDim / 16; ++kk) {
+                    const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
+                    umma_bf16(tmem + h * 128, umma_desc_sw128(qaddr + off, 16, 1024),
+                              umma_desc_sw128(kaddr + off, 16, 1024), kIdescS, kk > 0);
+                }
+                umma_commit(&bars->s_full[h]);
+            };
+            bool ok = wait_all(&bars->q_full, 0, 51) && wait_all(&bars->k_full[0], 0, 52);
+            if (ok) {
+                tc_fence_after();
+                issue_s(0, 0);
+                issue_s(1, 0);
+                umma_commit(&bars->k_empty[0]);
+            }
+            for (int j = 0; ok && j < n_kv; ++j) {
+                if (__any_sync(0xffffffffu, *abort_flag != 0)) {
+                    ok = false;
+                    break;
+                }
+                const bool next = j + 1 < n_kv;
+                ok = wait_all(&bars->v_full[j & 1], (j >> 1) & 1, 54);
+                if (ok && next) ok = wait_all(&bars->k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, 52);
+                const uint32_t vaddr = sbase + kPOffV + (j & 1) * kTileBytes;
+                for (int h = 0; ok && h < 2; ++h) {
+                    ok = wait_all(&bars->p_full[h], j & 1, 55);
+                    if (!ok) break;
+                    tc_fence_after();
+#pragma unroll
+                    for (int kk = 0; kk < kKeys / 16; ++kk)
+                        umma_bf16_ts(tmem + kColO + h * 128, tmem + h * 128 + kk * 8,
+                                     umma_desc_sw128(vaddr + kk * 16 * 128, kBox, 1024), kIdescPV,
+                                     (j > 0 || kk > 0) ? 1u : 0u);
+                    if (next) issue_s(h, j + 1);
+                }
+                if (ok) {
+                    umma_commit(&bars->v_empty[j & 1]);
+                    if (next) umma_commit(&bars->k_empty[(j + 1) & 1]);
+                }
+            }
+            if (ok) {
+                umma_commit(&bars->o_done[0]);
+                umma_commit(&bars->o_done[1]);
+            } else if (lane == 0) {
+                *abort_flag = 1;
+            }
+        }
+    } else {
+        warpgroup_reg_alloc<200>();
+        // ---------------------------------------------------------- softmax --
+        // warpgroup 1 (warps 4-7) owns head qh0, warpgroup 2 (8-11) head qh0 + 1;
+        // one thread per query row, all 128 keys of a tile
+        const int h = (warp >> 2) - 1;
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+        const uint32_t scol = lane_addr + h * 128;
+        const uint32_t ocol = lane_addr + kColO + h * 128;
+        const int qpos = p.prior + q0 + row;
+        const float scale = p.scale_log2;
+        float m_used = -INFINITY, l_run = 0.f;
+        bool ok = true;
+        for (int j = 0; j < n_kv; ++j) {
+            const bool got = mbar_wait(&bars->s_full[h], j & 1, p.status, 61);
+            if (!__all_sync(0xffffffffu, got) || __any_sync(0xffffffffu, *abort_flag != 0)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const int k0 = j * kKeys;
+            const bool diag = k0 + kKeys - 1 > first_pos;
+            // pass 1: row max over the two 64-column halves of S (raw scores;
+            // the scale is positive, so it is applied to the max only)
+            float m8[8];
+#pragma unroll
+            for (int a = 0; a < 8; ++a) m8[a] = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                float v[64];
+                tmem_ld64(scol + c * 64, v);
+                if (diag) {
+#pragma unroll
+                    for (int i = 0; i < 64; ++i)
+                        if (k0 + c * 64 + i > qpos) v[i] = -INFINITY;
+                }
+#pragma unroll
+                for (int i = 0; i < 64; ++i) m8[i & 7] = fmaxf(m8[i & 7], v[i]);
+            }
+            const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                                   fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * scale;
+            const bool move = mx > m_used + kRescaleLog2;
+            const float m_new = move ? mx : m_used;
+            const float base = (m_new == -INFINITY) ? 0.f : m_new;
+            const float alpha = move ? fast_exp2(m_used - base) : 1.f;
+            if (j > 0 && __any_sync(0xffffffffu, move)) {
+                // S_h(j) done implies PV_h(j-1) done: O_h is final for j-1
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    float o[32];
+                    tmem_ld32(ocol + c * 32, o);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[i] *= alpha;
+                    tmem_st32(ocol + c * 32, o);
+                }
+            }
+            // pass 2: P = 2^(s*scale - base), half by half (S is re-read from
+            // TMEM rather than held, keeping registers low); keys 64c..64c+63
+            // go to columns 32c..32c+31, which hold S values already consumed
+            const uint64_t scale2 = f2_pack(scale, scale);
+            const uint64_t nbase2 = f2_pack(-base, -base);
+            uint64_t sum2[4] = {0, 0, 0, 0};
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                float v[64];
+                tmem_ld64(scol + c * 64, v);
+                if (diag) {
+#pragma unroll
+                    for (int i = 0; i < 64; ++i)
+                        if (k0 + c * 64 + i > qpos) v[i] = -INFINITY;
+                }
+                uint32_t w[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    float x0, x1;
+                    f2_unpack(f2_fma(f2_pack(v[2 * i], v[2 * i + 1]), scale2, nbase2), x0, x1);
+                    // one pair in four on the FMA pipe, the rest on MUFU
+                    const float p0 = (i & 3) == 3 ? exp2_fma(x0) : fast_exp2(x0);
+                    const float p1 = (i & 3) == 3 ? exp2_fma(x1) : fast_exp2(x1);
+                    sum2[i & 3] = f2_add(sum2[i & 3], f2_pack(p0, p1));
+                    w[i] = pack_bf16x2(p0, p1);
+                }
+                tmem_st32u_nowait(scol + c * 32, w);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->p_full[h]);
+            float s8[8];
+#pragma unroll
+            for (int a = 0; a < 4; ++a) f2_unpack(sum2[a], s8[2 * a], s8[2 * a + 1]);
+            const float ps = ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
+            l_run = l_run * alpha + ps;
+            m_used = m_new;
+        }
+        const bool last = ok && mbar_wait(&bars->o_done[h], 0, p.status, 64);
+        if (__all_sync(0xffffffffu, last)) {
+            tc_fence_after();
+            const float inv = 1.0f / l_run;
+            const int qrow = q0 + row;
+            uint16_t *dst = p.out + ((size_t)qrow * p.qheads + qh0 + h) * kDim;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                float o[32];
+                tmem_ld32(ocol + c * 32, o);
+                uint32_t w[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) w[i] = pack_bf16x2(o[2 * i] * inv, o[2 * i + 1] * inv);
+                if (qrow < p.queries) {
+#pragma unroll
+                    for (int t = 0; t < 4; ++t)
+                        reinterpret_cast<uint4 *>(dst + c * 32)[t] =
+                            make_uint4(w[4 * t], w[4 * t + 1], w[4 * t + 2], w[4 * t + 3]);
+                }
+            }
+        } else {
+            *abort_flag = 1;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
 }  // namespace
 
 bool prefill_supported(unsigned head_dim, unsigned group) { return head_dim == 128 && group >= 1; }
 
+bool prefill_pairs_heads(unsigned group) { return group % 2 == 0; }
+
 cudaError_t launch_prefill(const CUtensorMap &qmap, const CUtensorMap &kmap,
                            const CUtensorMap &vmap, const PrefillParams &p, cudaStream_t stream) {
+    if (prefill_pairs_heads((unsigned)p.group)) {
+        cudaError_t err = cudaFuncSetAttribute(mslim_prefill_pair,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytes);
+        if (err != cudaSuccess) return err;
+        const unsigned grid = (unsigned)(p.n_qtiles * (p.qheads / 2));
+        mslim_prefill_pair<<<grid, kPThreads, kPSmemBytes, stream>>>(qmap, kmap, vmap, p);
+        return cudaGetLastError();
+    }
     cudaError_t err = cudaFuncSetAttribute(mslim_prefill_causal,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (err != cudaSuccess) return err;
