@@ -35,18 +35,6 @@ constexpr int kDim = 128;                  // head_dim
 constexpr int kBox = kRows * 128;          // one [128 rows][64 bf16] swizzled box: 16 KB
 constexpr int kQBytes = 2 * kBox;          // Q tile (two 64-column boxes)
 constexpr int kTileBytes = 2 * kBox;       // one K or V tile
-constexpr int kStages = 2;                   // slots in each of the K and V rings
-constexpr int kPBytes = 2 * kBox;
-constexpr int kOffK = kQBytes;               // K ring: slot s at kOffK + s * kTileBytes
-constexpr int kOffV = kOffK + kStages * kTileBytes;
-constexpr int kOffP = kOffV + kStages * kTileBytes;
-constexpr int kOffX = kOffP + kPBytes;       // row-max / row-sum exchange
-constexpr int kXBytes = (2 * 2 + 2) * kRows * 4;
-constexpr int kOffBar = kOffX + kXBytes;
-constexpr int kSmemBytes = kOffBar + 256 + 1024;  // barriers + alignment slack
-constexpr int kSoftmaxWarps = 8;
-constexpr int kVWarp = 2 + kSoftmaxWarps;      // the V producer warp
-constexpr int kThreads = (3 + kSoftmaxWarps) * 32;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColO = 256;     // S[2] at 0/128, O (accumulating) at 256
 // A row's running max is only moved (and O rescaled in TMEM) when a tile's
@@ -59,16 +47,36 @@ constexpr float kRescaleLog2 = 8.0f;
 constexpr uint32_t kIdescS = (1u << 4) | (1u << 7) | (1u << 10) | ((kKeys >> 3) << 17) | ((kRows >> 4) << 24);
 constexpr uint32_t kIdescPV = kIdescS | (1u << 16);
 
-struct Bars {
+// One head per CTA, S double-buffered in TMEM.
+//   TMEM: S[0] (0), S[1] (128), O (256, accumulating).  P(j) is written as bf16
+//         pairs over the first 64 columns of S[j & 1] once S(j) sits in
+//         registers, and O += P V is a TS-MMA (A from TMEM).
+//   Tensor-core order: S(0), then per tile j: S(j+1), PV(j).  S(j+1) goes to
+//         the other buffer, so the softmax of tile j+1 overlaps PV(j) and
+//         S(j+2); S(j+2) reuses buffer j & 1 only after PV(j) (in-order pipe).
+//   smem: Q (32 KB), K ring 2 x 32 KB, V ring 2 x 32 KB (160 KB).
+//   Warps: 0 TMA Q+K, 1 MMA, 2 TMA V, 3 idle; 4-11 softmax, a warp pair
+//         (w, w+4) per 32 TMEM lanes (rows): warps 4-7 keys 0..63 of a tile
+//         (and output dims 0..63), warps 8-11 keys 64..127 (dims 64..127); the
+//         pair exchanges row maxima through shared memory.
+constexpr int kSOffK = kQBytes;
+constexpr int kSOffV = kSOffK + 2 * kTileBytes;
+constexpr int kSOffX = kSOffV + 2 * kTileBytes;     // row-max / row-sum exchange
+constexpr int kSOffBar = kSOffX + 6 * kRows * 4;
+constexpr int kSSmemBytes = kSOffBar + 512 + 1024;
+constexpr int kSThreads = 12 * 32;
+// Columns in one pair in eight go through the FMA-pipe exp2 (measured best split).
+#define MSLIM_EXP_ON_FMA(i) (((i) & 7) == 7)
+
+struct SingleBars {
     uint64_t q_full;
-    uint64_t k_full[kStages];
-    uint64_t k_empty[kStages];   // freed when S_j (its only reader) completes
-    uint64_t v_full[kStages];
-    uint64_t v_empty[kStages];   // freed when PV_j completes
-    uint64_t s_full[2];
-    uint64_t s_empty[2];
-    uint64_t p_full;
-    uint64_t o_full;   // completes once per PV MMA group (O and P both safe after it)
+    uint64_t k_full[2], k_empty[2];
+    uint64_t v_full[2], v_empty[2];
+    uint64_t s_full[2];   // [buffer]
+    uint64_t p_full[2];   // [buffer], 8 warps per tile: a phase per two tiles, so the
+                          // MMA warp can never fall two phases behind
+    uint64_t o_full;      // once per PV (waited only for PV(j-1) while S(j) is held)
+    uint64_t o_done;      // once, after the last PV
     uint32_t tmem_base;
     int abort;
 };
@@ -78,14 +86,14 @@ __device__ __forceinline__ void pair_sync(int quarter) {
     asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kSThreads, 1)
     mslim_prefill_causal(const __grid_constant__ CUtensorMap qmap,
                          const __grid_constant__ CUtensorMap kmap,
                          const __grid_constant__ CUtensorMap vmap, const PrefillParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    Bars *bars = reinterpret_cast<Bars *>(smem + kOffBar);
+    SingleBars *bars = reinterpret_cast<SingleBars *>(smem + kSOffBar);
     volatile int *abort_flag = &bars->abort;
 
     const int bid = blockIdx.x;
@@ -101,18 +109,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         mbar_init(&bars->q_full, 1);
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(&bars->k_full[s], 1);
-            mbar_init(&bars->k_empty[s], 1);
-            mbar_init(&bars->v_full[s], 1);
-            mbar_init(&bars->v_empty[s], 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&bars->k_full[b], 1);
+            mbar_init(&bars->k_empty[b], 1);
+            mbar_init(&bars->v_full[b], 1);
+            mbar_init(&bars->v_empty[b], 1);
+            mbar_init(&bars->s_full[b], 1);
+            mbar_init(&bars->p_full[b], 8);
         }
-        for (int s = 0; s < 2; ++s) {
-            mbar_init(&bars->s_full[s], 1);
-            mbar_init(&bars->s_empty[s], kSoftmaxWarps);
-        }
-        mbar_init(&bars->p_full, kSoftmaxWarps);
         mbar_init(&bars->o_full, 1);
+        mbar_init(&bars->o_done, 1);
         bars->abort = 0;
         fence_mbarrier_init();
     }
@@ -123,15 +129,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = bars->tmem_base;
     const uint32_t sbase = smem_u32(smem);
 
-    if (warp == 0 || warp == kVWarp) {
-        // ---------------------------------------------------------- TMA --
-        // warp 0 loads Q and the K ring, warp kVWarp the V ring
-        if (lane == 0) {
+    if (warp < 4) {
+        if ((warp == 0 || warp == 2) && lane == 0) {
+            // ------------------------------------------------------ TMA --
             const bool is_k = warp == 0;
             const CUtensorMap *map = is_k ? &kmap : &vmap;
             uint64_t *full = is_k ? bars->k_full : bars->v_full;
             uint64_t *empty = is_k ? bars->k_empty : bars->v_empty;
-            uint8_t *ring = smem + (is_k ? kOffK : kOffV);
+            uint8_t *ring = smem + (is_k ? kSOffK : kSOffV);
             prefetch_tmap(map);
             if (is_k) {
                 prefetch_tmap(&qmap);
@@ -141,8 +146,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             int issued = 0;
             for (int j = 0; j < n_kv && !*abort_flag; ++j) {
-                const int st = j % kStages;
-                if (!mbar_wait(&empty[st], ((j / kStages) & 1) ^ 1, p.status, is_k ? 11 : 14)) {
+                const int st = j & 1;
+                if (!mbar_wait(&empty[st], ((j >> 1) & 1) ^ 1, p.status, is_k ? 11 : 14)) {
                     *abort_flag = 1;
                     break;
                 }
@@ -154,160 +159,146 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             // Our copies must land before the CTA can retire.
             if (is_k) mbar_wait(&bars->q_full, 0, p.status, 12);
-            for (int j = max(0, issued - kStages); j < issued; ++j)
-                mbar_wait(&full[j % kStages], (j / kStages) & 1, p.status, 13);
-        }
-    } else if (warp == 1) {
-        // ---------------------------------------------------------- MMA --
-        // the whole warp runs this loop (uniform control flow); umma_* elect
-        // the issuing lane
-        {
-            bool ok = __all_sync(0xffffffffu, mbar_wait(&bars->q_full, 0, p.status, 21));
+            for (int j = max(0, issued - 2); j < issued; ++j)
+                mbar_wait(&full[j & 1], (j >> 1) & 1, p.status, 13);
+        } else if (warp == 1) {
+            // ------------------------------------------------------ MMA --
+            // the whole warp runs the loop; umma_* elect the issuing lane
+            auto wait_all = [&](uint64_t *bar, uint32_t parity, int where) -> bool {
+                return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.status, where));
+            };
             auto issue_s = [&](int j) -> bool {
-                const int st = j % kStages, sb = j & 1;
-                if (!__all_sync(0xffffffffu, mbar_wait(&bars->k_full[st], (j / kStages) & 1, p.status, 22))) return false;
-                if (!__all_sync(0xffffffffu, mbar_wait(&bars->s_empty[sb], ((j >> 1) & 1) ^ 1, p.status, 23))) return false;
+                if (!wait_all(&bars->k_full[j & 1], (j >> 1) & 1, 22)) return false;
                 tc_fence_after();
-                const uint32_t kaddr = sbase + kOffK + st * kTileBytes;
+                const uint32_t kaddr = sbase + kSOffK + (j & 1) * kTileBytes;
 #pragma unroll
                 for (int kk = 0; kk < kDim / 16; ++kk) {
                     const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
-                    umma_bf16(tmem + kColS + sb * 128, umma_desc_sw128(sbase + off, 16, 1024),
+                    umma_bf16(tmem + kColS + (j & 1) * 128, umma_desc_sw128(sbase + off, 16, 1024),
                               umma_desc_sw128(kaddr + off, 16, 1024), kIdescS, kk > 0);
                 }
-                umma_commit(&bars->s_full[sb]);
-                umma_commit(&bars->k_empty[st]);
+                umma_commit(&bars->s_full[j & 1]);
+                umma_commit(&bars->k_empty[j & 1]);
                 return true;
             };
-            auto issue_pv = [&](int i) -> bool {
-                const int st = i % kStages;
-                // P_i stored (and, when needed, O rescaled) by the softmax warps
-                if (!__all_sync(0xffffffffu, mbar_wait(&bars->v_full[st], (i / kStages) & 1, p.status, 26))) return false;
-                if (!__all_sync(0xffffffffu, mbar_wait(&bars->p_full, i & 1, p.status, 24))) return false;
-                tc_fence_after();
-                const uint32_t vaddr = sbase + kOffV + st * kTileBytes;
-                const uint32_t paddr = sbase + kOffP;
-#pragma unroll
-                for (int kk = 0; kk < kKeys / 16; ++kk) {
-                    // A = P (K-major, keys contiguous), B = V (MN-major: 64-dim
-                    // rows of 128 B, 8-key groups 1 KB apart, dim halves one box apart)
-                    const uint64_t a = umma_desc_sw128(paddr + (kk >> 2) * kBox + (kk & 3) * 32, 16, 1024);
-                    const uint64_t b = umma_desc_sw128(vaddr + kk * 16 * 128, kBox, 1024);
-                    umma_bf16(tmem + kColO, a, b, kIdescPV, (i > 0 || kk > 0) ? 1u : 0u);
+            bool ok = wait_all(&bars->q_full, 0, 21) && issue_s(0);
+            for (int j = 0; ok && j < n_kv; ++j) {
+                if (__any_sync(0xffffffffu, *abort_flag != 0)) {
+                    ok = false;
+                    break;
                 }
-                umma_commit(&bars->o_full);
-                umma_commit(&bars->v_empty[st]);
-                return true;
-            };
-            for (int j = 0; ok && j <= n_kv; ++j) {
-                if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
-                if (j < n_kv) ok = __all_sync(0xffffffffu, issue_s(j));
-                if (ok && j >= 1) ok = __all_sync(0xffffffffu, issue_pv(j - 1));
+                if (j + 1 < n_kv) ok = issue_s(j + 1);
+                ok = ok && wait_all(&bars->v_full[j & 1], (j >> 1) & 1, 26) &&
+                     wait_all(&bars->p_full[j & 1], (j >> 1) & 1, 24);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t vaddr = sbase + kSOffV + (j & 1) * kTileBytes;
+#pragma unroll
+                for (int kk = 0; kk < kKeys / 16; ++kk)
+                    umma_bf16_ts(tmem + kColO, tmem + kColS + (j & 1) * 128 + kk * 8,
+                                 umma_desc_sw128(vaddr + kk * 16 * 128, kBox, 1024), kIdescPV,
+                                 (j > 0 || kk > 0) ? 1u : 0u);
+                umma_commit(j + 1 < n_kv ? &bars->o_full : &bars->o_done);
+                umma_commit(&bars->v_empty[j & 1]);
             }
             if (!ok && lane == 0) *abort_flag = 1;
         }
-    } else if (warp >= 2 && warp < 2 + kSoftmaxWarps) {
-        // ------------------------------------------------------ softmax --
-        // Warps 2..9: a warp pair (w, w+4) owns the 32 rows of TMEM lane
-        // quarter w % 4; the first warp of the pair takes columns (keys, and
-        // output dims) 0..63, the second 64..127.
+    } else {
+        // ---------------------------------------------------------- softmax --
         const int quarter = warp & 3;
-        const int half = (warp - 2) >> 2;
+        const int half = (warp >> 2) - 1;              // keys (and dims) 64*half..+63
         const int row = quarter * 32 + lane;
         const int col0 = half * 64;
         const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
         const uint32_t ocol = lane_addr + kColO + col0;
-        const int qpos = p.prior + q0 + row;           // absolute position of this row
+        const int qpos = p.prior + q0 + row;
         const float scale = p.scale_log2;
-        float *xmax = reinterpret_cast<float *>(smem + kOffX);  // [2 parity][2 half][128]
-        float *xsum = xmax + 4 * kRows;                          // [2 half][128]
-        float m_used = -INFINITY, l_part = 0.f;
-        uint8_t *pbox = smem + kOffP + half * kBox + row * 128;
+        float *xmax = reinterpret_cast<float *>(smem + kSOffX);  // [2 parity][2 half][128]
+        float *xsum = xmax + 4 * kRows;                           // [2 half][128]
+        float m_used = -INFINITY, l_run = 0.f;
         bool ok = true;
         for (int j = 0; j < n_kv; ++j) {
-            const int sb = j & 1;
-            // every lane waits; decisions are warp-uniform so the
-            // .sync.aligned TMEM accesses never run divergently
-            const bool got = mbar_wait(&bars->s_full[sb], (j >> 1) & 1, p.status, 31);
+            const int b = j & 1;
+            const bool got = mbar_wait(&bars->s_full[b], (j >> 1) & 1, p.status, 31);
             if (!__all_sync(0xffffffffu, got) || __any_sync(0xffffffffu, *abort_flag != 0)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            float sv[64];
-            tmem_ld64(lane_addr + kColS + sb * 128 + col0, sv);
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->s_empty[sb]);  // S buffer free for S_{j+2}
+            const uint32_t scol = lane_addr + kColS + b * 128;
+            float v[64];
+            tmem_ld64(scol + col0, v);
             const int k0 = j * kKeys + col0;
-            const bool masked = j * kKeys + kKeys - 1 > first_pos;
-            if (masked) {
+            if (j * kKeys + kKeys - 1 > first_pos) {
 #pragma unroll
                 for (int i = 0; i < 64; ++i)
-                    if (k0 + i > qpos) sv[i] = -INFINITY;
+                    if (k0 + i > qpos) v[i] = -INFINITY;
             }
-            // eight independent partial maxima (short dependency chains)
             float m8[8];
 #pragma unroll
-            for (int a = 0; a < 8; ++a) m8[a] = sv[a];
+            for (int a = 0; a < 8; ++a) m8[a] = fmaxf(v[a], v[a + 8]);
 #pragma unroll
-            for (int i = 8; i < 64; ++i) m8[i & 7] = fmaxf(m8[i & 7], sv[i]);
+            for (int i = 16; i < 64; ++i) m8[i & 7] = fmaxf(m8[i & 7], v[i]);
             float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
                              fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
-            xmax[((j & 1) * 2 + half) * kRows + row] = mx;
+            xmax[(b * 2 + half) * kRows + row] = mx;
+            // after this barrier both halves hold their S values in registers,
+            // so P may overwrite the S columns below
             pair_sync(quarter);
-            mx = fmaxf(mx, xmax[((j & 1) * 2 + (half ^ 1)) * kRows + row]) * scale;
-            // move the row max only when this tile exceeds it by > 2^8
+            mx = fmaxf(mx, xmax[(b * 2 + (half ^ 1)) * kRows + row]) * scale;
             const bool move = mx > m_used + kRescaleLog2;
             const float m_new = move ? mx : m_used;
             const float base = (m_new == -INFINITY) ? 0.f : m_new;
             const float alpha = move ? fast_exp2(m_used - base) : 1.f;
-            float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            uint32_t w[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                const float p0 = fast_exp2(fmaf(sv[2 * i], scale, -base));
-                const float p1 = fast_exp2(fmaf(sv[2 * i + 1], scale, -base));
-                s8[i & 7] += p0 + p1;
-                w[i] = pack_bf16x2(p0, p1);
-            }
-            const float ps = ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
-            if (j > 0) {
-                // PV_{j-1} must be done: it reads the P tile and writes O
+            if (j > 0 && __any_sync(0xffffffffu, move)) {
+                // O must hold PV(j-1) before it is rescaled
                 const bool gotc = mbar_wait(&bars->o_full, (j - 1) & 1, p.status, 32);
                 if (!__all_sync(0xffffffffu, gotc)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                if (__any_sync(0xffffffffu, move)) {
 #pragma unroll
-                    for (int c = 0; c < 2; ++c) {
-                        float o[32];
-                        tmem_ld32(ocol + c * 32, o);
+                for (int c = 0; c < 2; ++c) {
+                    float o[32];
+                    tmem_ld32(ocol + c * 32, o);
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) o[i] *= alpha;
-                        tmem_st32(ocol + c * 32, o);
-                    }
+                    for (int i = 0; i < 32; ++i) o[i] *= alpha;
+                    tmem_st32(ocol + c * 32, o);
                 }
             }
+            const uint64_t scale2 = f2_pack(scale, scale);
+            const uint64_t nbase2 = f2_pack(-base, -base);
+            uint64_t sum2[4] = {0, 0, 0, 0};
+            uint32_t w[32];
 #pragma unroll
-            for (int t = 0; t < 8; ++t)
-                *reinterpret_cast<uint4 *>(pbox + ((t ^ (row & 7)) << 4)) =
-                    make_uint4(w[4 * t], w[4 * t + 1], w[4 * t + 2], w[4 * t + 3]);
+            for (int i = 0; i < 32; ++i) {
+                float x0, x1;
+                f2_unpack(f2_fma(f2_pack(v[2 * i], v[2 * i + 1]), scale2, nbase2), x0, x1);
+                const float p0 = MSLIM_EXP_ON_FMA(i) ? exp2_fma(x0) : fast_exp2(x0);
+                const float p1 = MSLIM_EXP_ON_FMA(i) ? exp2_fma(x1) : fast_exp2(x1);
+                sum2[i & 3] = f2_add(sum2[i & 3], f2_pack(p0, p1));
+                w[i] = pack_bf16x2(p0, p1);
+            }
+            // keys 64*half..+63 -> P columns 32*half..+31 of S[b]
+            tmem_st32u_nowait(scol + half * 32, w);
+            tmem_wait_st();
             tc_fence_before();
-            fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->p_full);
-            l_part = l_part * alpha + ps;
+            if (lane == 0) mbar_arrive(&bars->p_full[b]);
+            float s8[8];
+#pragma unroll
+            for (int a = 0; a < 4; ++a) f2_unpack(sum2[a], s8[2 * a], s8[2 * a + 1]);
+            const float ps = ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
+            l_run = l_run * alpha + ps;
             m_used = m_new;
         }
-        const bool last = ok && mbar_wait(&bars->o_full, (n_kv - 1) & 1, p.status, 33);
+        const bool last = ok && mbar_wait(&bars->o_done, 0, p.status, 33);
         if (__all_sync(0xffffffffu, last)) {
             tc_fence_after();
-            xsum[half * kRows + row] = l_part;
+            xsum[half * kRows + row] = l_run;
             pair_sync(quarter);
-            const float inv = 1.0f / (l_part + xsum[(half ^ 1) * kRows + row]);
+            const float inv = 1.0f / (l_run + xsum[(half ^ 1) * kRows + row]);
             const int qrow = q0 + row;
             uint16_t *dst = p.out + ((size_t)qrow * p.qheads + qh) * kDim + col0;
 #pragma unroll
@@ -650,10 +641,10 @@ cudaError_t launch_prefill(const CUtensorMap &qmap, const CUtensorMap &kmap,
         return cudaGetLastError();
     }
     cudaError_t err = cudaFuncSetAttribute(mslim_prefill_causal,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kSSmemBytes);
     if (err != cudaSuccess) return err;
     const unsigned grid = (unsigned)(p.n_qtiles * p.qheads);
-    mslim_prefill_causal<<<grid, kThreads, kSmemBytes, stream>>>(qmap, kmap, vmap, p);
+    mslim_prefill_causal<<<grid, kSThreads, kSSmemBytes, stream>>>(qmap, kmap, vmap, p);
     return cudaGetLastError();
 }
 
