@@ -690,7 +690,7 @@ int mslim_cuda_prefill_causal(const mslim_geometry_t *geometry, const void *q, c
     if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(out, 16))
         return fail(MSLIM_ERR_SHAPE_MISMATCH, "prefill buffers must be 16-byte aligned");
     const uint64_t D = geometry->head_dim;
-    CUtensorMap qmap, kmap, vmap;
+    CUtensorMap qmap, kmap, vmap, omap;
     {
         const uint64_t qd[3] = {D, geometry->query_heads, queries};
         const uint64_t qs[2] = {D * 2, (uint64_t)geometry->query_heads * D * 2};
@@ -699,6 +699,7 @@ int mslim_cuda_prefill_causal(const mslim_geometry_t *geometry, const void *q, c
         const uint32_t box[3] = {64, 1, 128};
         const uint32_t kvbox[3] = {64, 1, 128};
         if (int rc = make_tmap(&qmap, q, 3, qd, qs, box)) return rc;
+        if (int rc = make_tmap(&omap, out, 3, qd, qs, box)) return rc;
         if (int rc = make_tmap(&kmap, k, 3, kd, ks, kvbox)) return rc;
         if (int rc = make_tmap(&vmap, v, 3, kd, ks, kvbox)) return rc;
     }
@@ -714,7 +715,7 @@ int mslim_cuda_prefill_causal(const mslim_geometry_t *geometry, const void *q, c
     p.scale_log2 = scale_log2_for(geometry->head_dim);
     if ((uint64_t)p.n_qtiles * p.qheads > 0x7fffffffull)
         return fail(MSLIM_ERR_SHAPE_MISMATCH, "prefill grid too large");
-    cudaError_t err = mslim::launch_prefill(qmap, kmap, vmap, p, static_cast<cudaStream_t>(stream));
+    cudaError_t err = mslim::launch_prefill(qmap, kmap, vmap, omap, p, static_cast<cudaStream_t>(stream));
     if (err != cudaSuccess) return cuda_fail(err, "prefill launch");
     return MSLIM_OK;
 }

@@ -67,6 +67,11 @@ constexpr int kSSmemBytes = kSOffBar + 512 + 1024;
 constexpr int kSThreads = 12 * 32;
 // Columns in one pair in eight go through the FMA-pipe exp2 (measured best split).
 #define MSLIM_EXP_ON_FMA(i) (((i) & 7) == 7)
+// The same for the two-heads-per-CTA kernel: a bit per (pair index mod 8).
+#ifndef MSLIM_PAIR_POLY_MASK
+#define MSLIM_PAIR_POLY_MASK 0x80
+#endif
+#define MSLIM_PAIR_EXP_ON_FMA(i) ((MSLIM_PAIR_POLY_MASK >> ((i) & 7)) & 1)
 
 struct SingleBars {
     uint64_t q_full;
@@ -350,14 +355,26 @@ constexpr int kPOffV = kPOffK + 2 * kTileBytes;
 constexpr int kPOffBar = kPOffV + 2 * kTileBytes;
 constexpr int kPSmemBytes = kPOffBar + 512 + 1024;
 constexpr int kPThreads = 12 * 32;
+// setmaxnreg split: warpgroup 0 shrinks to kPRegsCtl, the two softmax
+// warpgroups grow to kPRegsSoftmax.  The grown share is drawn from the
+// registers the block was launched with (kPThreads x the per-thread count that
+// __launch_bounds__(kPThreads, 1) allows, 168), so the sum must stay within it
+// or setmaxnreg.inc would never be granted.
+constexpr int kPRegsCtl = 88, kPRegsSoftmax = 200, kPRegsLaunch = 168;
+static_assert(128 * kPRegsCtl + 256 * kPRegsSoftmax <= kPThreads * kPRegsLaunch,
+              "register split exceeds the launch allocation");
+static_assert(kPRegsCtl % 8 == 0 && kPRegsSoftmax % 8 == 0, "setmaxnreg counts are multiples of 8");
+
+// Output staging for head h at the end of the CTA: the slot of Q_h.
+__device__ __forceinline__ uint8_t *stage_base(uint8_t *smem, int h) { return smem + kPOffQ + h * kQBytes; }
 
 struct PairBars {
     uint64_t q_full;
     uint64_t k_full[2], k_empty[2];
     uint64_t v_full[2], v_empty[2];
     uint64_t s_full[2];   // [head], once per key tile
-    uint64_t p_full[2];   // [head], once per key tile (4 warps)
-    uint64_t o_done[2];   // [head], after the last PV
+    uint64_t p_full[2][2];  // [head][half]: P of keys 64*half..+63 written (4 warps)
+    uint64_t o_done[2];   // [head], after the head's last PV
     uint32_t tmem_base;
     int abort;
 };
@@ -365,7 +382,8 @@ struct PairBars {
 __global__ void __launch_bounds__(kPThreads, 1)
     mslim_prefill_pair(const __grid_constant__ CUtensorMap qmap,
                        const __grid_constant__ CUtensorMap kmap,
-                       const __grid_constant__ CUtensorMap vmap, const PrefillParams p) {
+                       const __grid_constant__ CUtensorMap vmap,
+                       const __grid_constant__ CUtensorMap omap, const PrefillParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -392,7 +410,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
             mbar_init(&bars->v_full[b], 1);
             mbar_init(&bars->v_empty[b], 1);
             mbar_init(&bars->s_full[b], 1);
-            mbar_init(&bars->p_full[b], 4);
+            mbar_init(&bars->p_full[b][0], 4);
+            mbar_init(&bars->p_full[b][1], 4);
             mbar_init(&bars->o_done[b], 1);
         }
         bars->abort = 0;
@@ -406,7 +425,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const uint32_t sbase = smem_u32(smem);
 
     if (warp < 4) {
-        warpgroup_reg_dealloc<88>();
+        warpgroup_reg_dealloc<kPRegsCtl>();
         if ((warp == 0 || warp == 2) && lane == 0) {
             // ------------------------------------------------------ TMA --
             const bool is_k = warp == 0;
@@ -473,30 +492,33 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 if (ok && next) ok = wait_all(&bars->k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, 52);
                 const uint32_t vaddr = sbase + kPOffV + (j & 1) * kTileBytes;
                 for (int h = 0; ok && h < 2; ++h) {
-                    ok = wait_all(&bars->p_full[h], j & 1, 55);
-                    if (!ok) break;
-                    tc_fence_after();
+                    // PV over keys 0..63 starts while the softmax still
+                    // writes P for keys 64..127
+                    for (int half = 0; ok && half < 2; ++half) {
+                        ok = wait_all(&bars->p_full[h][half], j & 1, 55);
+                        if (!ok) break;
+                        tc_fence_after();
 #pragma unroll
-                    for (int kk = 0; kk < kKeys / 16; ++kk)
-                        umma_bf16_ts(tmem + kColO + h * 128, tmem + h * 128 + kk * 8,
-                                     umma_desc_sw128(vaddr + kk * 16 * 128, kBox, 1024), kIdescPV,
-                                     (j > 0 || kk > 0) ? 1u : 0u);
+                        for (int kq = 0; kq < kKeys / 32; ++kq) {
+                            const int kk = half * (kKeys / 32) + kq;
+                            umma_bf16_ts(tmem + kColO + h * 128, tmem + h * 128 + kk * 8,
+                                         umma_desc_sw128(vaddr + kk * 16 * 128, kBox, 1024), kIdescPV,
+                                         (j > 0 || kk > 0) ? 1u : 0u);
+                        }
+                    }
+                    if (!ok) break;
                     if (next) issue_s(h, j + 1);
+                    else umma_commit(&bars->o_done[h]);
                 }
                 if (ok) {
                     umma_commit(&bars->v_empty[j & 1]);
                     if (next) umma_commit(&bars->k_empty[(j + 1) & 1]);
                 }
             }
-            if (ok) {
-                umma_commit(&bars->o_done[0]);
-                umma_commit(&bars->o_done[1]);
-            } else if (lane == 0) {
-                *abort_flag = 1;
-            }
+            if (!ok && lane == 0) *abort_flag = 1;
         }
     } else {
-        warpgroup_reg_alloc<200>();
+        warpgroup_reg_alloc<kPRegsSoftmax>();
         // ---------------------------------------------------------- softmax --
         // warpgroup 1 (warps 4-7) owns head qh0, warpgroup 2 (8-11) head qh0 + 1;
         // one thread per query row, all 128 keys of a tile
@@ -519,72 +541,66 @@ __global__ void __launch_bounds__(kPThreads, 1)
             tc_fence_after();
             const int k0 = j * kKeys;
             const bool diag = k0 + kKeys - 1 > first_pos;
-            // pass 1: row max over the two 64-column halves of S (raw scores;
-            // the scale is positive, so it is applied to the max only)
-            float m8[8];
+            // the whole 128-key row of S in registers (one load, one wait)
+            float v[128];
+            tmem_ld128(scol, v);
+            if (diag) {
 #pragma unroll
-            for (int a = 0; a < 8; ++a) m8[a] = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                float v[64];
-                tmem_ld64(scol + c * 64, v);
-                if (diag) {
-#pragma unroll
-                    for (int i = 0; i < 64; ++i)
-                        if (k0 + c * 64 + i > qpos) v[i] = -INFINITY;
-                }
-#pragma unroll
-                for (int i = 0; i < 64; ++i) m8[i & 7] = fmaxf(m8[i & 7], v[i]);
+                for (int i = 0; i < 128; ++i)
+                    if (k0 + i > qpos) v[i] = -INFINITY;
             }
-            const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                                   fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * scale;
+            // row max of the raw scores (the scale is positive, so it is
+            // applied to the max only); four independent three-input chains
+            float m4[4] = {v[0], v[1], v[2], v[3]};
+#pragma unroll
+            for (int i = 4; i + 8 <= 128; i += 8)
+#pragma unroll
+                for (int a = 0; a < 4; ++a) m4[a] = fmax3(m4[a], v[i + a], v[i + 4 + a]);
+#pragma unroll
+            for (int a = 0; a < 4; ++a) m4[a] = fmaxf(m4[a], v[124 + a]);
+            const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * scale;
             const bool move = mx > m_used + kRescaleLog2;
             const float m_new = move ? mx : m_used;
             const float base = (m_new == -INFINITY) ? 0.f : m_new;
             const float alpha = move ? fast_exp2(m_used - base) : 1.f;
-            if (j > 0 && __any_sync(0xffffffffu, move)) {
-                // S_h(j) done implies PV_h(j-1) done: O_h is final for j-1
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    float o[32];
-                    tmem_ld32(ocol + c * 32, o);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] *= alpha;
-                    tmem_st32(ocol + c * 32, o);
-                }
-            }
-            // pass 2: P = 2^(s*scale - base), half by half (S is re-read from
-            // TMEM rather than held, keeping registers low); keys 64c..64c+63
-            // go to columns 32c..32c+31, which hold S values already consumed
+            // P = 2^(s*scale - base); keys 64c..64c+63 go to columns
+            // 32c..32c+31, whose S values are already in registers.  Each half
+            // is announced on its own barrier; O is rescaled before the first.
             const uint64_t scale2 = f2_pack(scale, scale);
             const uint64_t nbase2 = f2_pack(-base, -base);
             uint64_t sum2[4] = {0, 0, 0, 0};
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
-                float v[64];
-                tmem_ld64(scol + c * 64, v);
-                if (diag) {
-#pragma unroll
-                    for (int i = 0; i < 64; ++i)
-                        if (k0 + c * 64 + i > qpos) v[i] = -INFINITY;
-                }
                 uint32_t w[32];
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
+                    const int e = c * 64 + 2 * i;
                     float x0, x1;
-                    f2_unpack(f2_fma(f2_pack(v[2 * i], v[2 * i + 1]), scale2, nbase2), x0, x1);
-                    // one pair in four on the FMA pipe, the rest on MUFU
-                    const float p0 = (i & 3) == 3 ? exp2_fma(x0) : fast_exp2(x0);
-                    const float p1 = (i & 3) == 3 ? exp2_fma(x1) : fast_exp2(x1);
+                    f2_unpack(f2_fma(f2_pack(v[e], v[e + 1]), scale2, nbase2), x0, x1);
+                    const bool poly = MSLIM_PAIR_EXP_ON_FMA(i);
+                    const float p0 = poly ? exp2_fma(x0) : fast_exp2(x0);
+                    const float p1 = poly ? exp2_fma(x1) : fast_exp2(x1);
                     sum2[i & 3] = f2_add(sum2[i & 3], f2_pack(p0, p1));
                     w[i] = pack_bf16x2(p0, p1);
                 }
                 tmem_st32u_nowait(scol + c * 32, w);
+                if (c == 0 && j > 0 && __any_sync(0xffffffffu, move)) {
+                    // S_h(j) done implies PV_h(j-1) done: O_h is final for j-1,
+                    // and PV_h(j) waits for the arrive below
+#pragma unroll
+                    for (int oc = 0; oc < 4; ++oc) {
+                        float o[32];
+                        tmem_ld32(ocol + oc * 32, o);
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) o[i] *= alpha;
+                        tmem_st32(ocol + oc * 32, o);
+                    }
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->p_full[h][c]);
             }
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->p_full[h]);
             float s8[8];
 #pragma unroll
             for (int a = 0; a < 4; ++a) f2_unpack(sum2[a], s8[2 * a], s8[2 * a + 1]);
@@ -593,11 +609,15 @@ __global__ void __launch_bounds__(kPThreads, 1)
             m_used = m_new;
         }
         const bool last = ok && mbar_wait(&bars->o_done[h], 0, p.status, 64);
-        if (__all_sync(0xffffffffu, last)) {
+        const bool good = __all_sync(0xffffffffu, last);
+        if (good) {
             tc_fence_after();
+            // O_h / l -> bf16, staged in Q_h's slot (its last reader, S_h of
+            // the final tile, has completed) in the TMA 128-byte-swizzled
+            // layout, then written by one bulk tensor store per 64 columns;
+            // rows past the last query are clipped by the store.
             const float inv = 1.0f / l_run;
-            const int qrow = q0 + row;
-            uint16_t *dst = p.out + ((size_t)qrow * p.qheads + qh0 + h) * kDim;
+            uint8_t *stage = stage_base(smem, h);
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 float o[32];
@@ -605,15 +625,25 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 uint32_t w[16];
 #pragma unroll
                 for (int i = 0; i < 16; ++i) w[i] = pack_bf16x2(o[2 * i] * inv, o[2 * i + 1] * inv);
-                if (qrow < p.queries) {
+                uint8_t *box_row = stage + (c >> 1) * kBox + row * 128;
 #pragma unroll
-                    for (int t = 0; t < 4; ++t)
-                        reinterpret_cast<uint4 *>(dst + c * 32)[t] =
-                            make_uint4(w[4 * t], w[4 * t + 1], w[4 * t + 2], w[4 * t + 3]);
+                for (int t = 0; t < 4; ++t) {
+                    const int chunk = ((c & 1) * 4 + t) ^ (row & 7);
+                    *reinterpret_cast<uint4 *>(box_row + chunk * 16) =
+                        make_uint4(w[4 * t], w[4 * t + 1], w[4 * t + 2], w[4 * t + 3]);
                 }
             }
+            fence_proxy_async_smem();
         } else {
             *abort_flag = 1;
+        }
+        // every warp of the head's warpgroup reaches this barrier on every path
+        asm volatile("bar.sync %0, 128;" ::"r"(2 + h) : "memory");
+        if (quarter == 0 && lane == 0 && *abort_flag == 0) {
+            tma_store_3d(&omap, stage_base(smem, h), 0, qh0 + h, q0);
+            tma_store_3d(&omap, stage_base(smem, h) + kBox, 64, qh0 + h, q0);
+            bulk_commit_group();
+            bulk_wait_all();
         }
     }
     tc_fence_before();
@@ -631,13 +661,19 @@ bool prefill_supported(unsigned head_dim, unsigned group) { return head_dim == 1
 bool prefill_pairs_heads(unsigned group) { return group % 2 == 0; }
 
 cudaError_t launch_prefill(const CUtensorMap &qmap, const CUtensorMap &kmap,
-                           const CUtensorMap &vmap, const PrefillParams &p, cudaStream_t stream) {
+                           const CUtensorMap &vmap, const CUtensorMap &omap,
+                           const PrefillParams &p, cudaStream_t stream) {
     if (prefill_pairs_heads((unsigned)p.group)) {
         cudaError_t err = cudaFuncSetAttribute(mslim_prefill_pair,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytes);
         if (err != cudaSuccess) return err;
+        // The setmaxnreg split needs the registers it assumes at launch.
+        cudaFuncAttributes fa{};
+        err = cudaFuncGetAttributes(&fa, mslim_prefill_pair);
+        if (err != cudaSuccess) return err;
+        if (fa.numRegs * kPThreads < 128 * kPRegsCtl + 256 * kPRegsSoftmax) return cudaErrorInvalidConfiguration;
         const unsigned grid = (unsigned)(p.n_qtiles * (p.qheads / 2));
-        mslim_prefill_pair<<<grid, kPThreads, kPSmemBytes, stream>>>(qmap, kmap, vmap, p);
+        mslim_prefill_pair<<<grid, kPThreads, kPSmemBytes, stream>>>(qmap, kmap, vmap, omap, p);
         return cudaGetLastError();
     }
     cudaError_t err = cudaFuncSetAttribute(mslim_prefill_causal,

@@ -23,8 +23,10 @@ bool prefill_supported(unsigned head_dim, unsigned group);
 // Even groups run two query heads per CTA (ping-pong kernel).
 bool prefill_pairs_heads(unsigned group);
 
-// q/k/v maps: bf16, dims (D, heads, rows), box (64, 1, 128), 128-byte swizzle.
+// q/k/v/out maps: bf16, dims (D, heads, rows), box (64, 1, 128), 128-byte
+// swizzle; the out map (same shape as q) is written by bulk tensor stores.
 cudaError_t launch_prefill(const CUtensorMap &qmap, const CUtensorMap &kmap,
-                           const CUtensorMap &vmap, const PrefillParams &p, cudaStream_t stream);
+                           const CUtensorMap &vmap, const CUtensorMap &omap,
+                           const PrefillParams &p, cudaStream_t stream);
 
 }  // namespace mslim
