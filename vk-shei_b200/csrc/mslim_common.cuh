@@ -134,6 +134,32 @@ __device__ __forceinline__ void bulk_commit_group() {
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
 
+// Waits until every committed bulk group of this thread has finished reading
+// its shared-memory source (the global writes may still be in flight).
+__device__ __forceinline__ void bulk_wait_read_all() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+// Named barrier over `count` threads.
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Named barrier over `count` threads that also ORs a predicate across them:
+// every participant gets the same result.
+__device__ __forceinline__ bool named_bar_or(int id, int count, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)pred), "r"(id), "r"(count)
+        : "memory");
+    return r != 0;
+}
+
 // Waits until every committed bulk group of this thread has completed
 // (global writes performed), so the CTA may retire.
 __device__ __forceinline__ void bulk_wait_all() {
@@ -451,6 +477,16 @@ __device__ __forceinline__ void tmem_st32u_nowait(uint32_t taddr, const uint32_t
         "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]),
         "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
         "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
+// tcgen05.st of 16 columns without waiting; pair with tmem_wait_st().
+__device__ __forceinline__ void tmem_st16u_nowait(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+        "r"(v[15])
         : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() {

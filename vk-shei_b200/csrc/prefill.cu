@@ -333,27 +333,35 @@ __global__ void __launch_bounds__(kSThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
-// Two heads per CTA (ping-pong), P kept in tensor memory.  A CTA takes one
-// 128-row query tile of two query heads that share a KV head: every K/V byte it
-// loads serves both, both heads have the same causal extent, and while one
-// head's softmax warpgroup works, the tensor core runs the other head's MMAs.
-//   smem: Q_A, Q_B (32 KB each), K ring 2 x 32 KB, V ring 2 x 32 KB (192 KB);
+// Two heads per CTA (ping-pong), P kept in tensor memory, persistent CTAs.  A
+// work item is one 128-row query tile of two query heads that share a KV head:
+// every K/V byte loaded serves both, both heads have the same causal extent,
+// and while one head's softmax warpgroup works, the tensor core runs the other
+// head's MMAs.  One CTA per SM walks the items heaviest first (late query tiles
+// see the most keys) in snake order -- CTA b of G takes ranks b, 2G-1-b,
+// 2G+b, ... -- which pairs heavy items with light ones.
+//   smem: Q_A, Q_B (32 KB each), K ring 2 x 32 KB, V ring 2 x 32 KB, output
+//         staging 16 KB per head (224 KB);
 //   TMEM: S_A (0), S_B (128), O_A (256), O_B (384); P_h is written as bf16
 //         pairs over the first 64 columns of S_h once S_h has been read, and
 //         O_h += P_h V is a TS-MMA (A from TMEM), so P never touches shared
-//         memory and shared-memory operand traffic stays under the tensor
-//         core's rate.
-//   Tensor-core order per key tile j: PV_A(j), S_A(j+1), PV_B(j), S_B(j+1);
-//   S_h(j+1) overwrites P_h(j) only after PV_h(j), which precedes it in the
-//   (in-order) tcgen05 pipe, and S_h(j) done implies PV_h(j-1) done.
-//   Warps: 0 TMA Q+K, 1 MMA, 2 TMA V, 3 idle (warpgroup 0, 88 registers);
-//          4-7 softmax head A, 8-11 softmax head B (200 registers each;
-//          128 x 88 + 256 x 200 <= the 384 x 168 registers of the launch).
+//         memory.
+//   Tensor-core order per item: S_A(0), S_B(0), then per key tile j:
+//         PV_A(j), S_A(j+1), PV_B(j), S_B(j+1).  S_h(j+1) overwrites P_h(j)
+//         only after PV_h(j), which precedes it in the (in-order) tcgen05
+//         pipe, and S_h(j) done implies PV_h(j-1) done.
+//   Across items the K/V rings and the per-tile barriers keep counting; Q of
+//   the next item is loaded as soon as the current item's last S MMAs have
+//   completed, so the next item's S(0) overlaps the current output write.
+//   Warps: 0 TMA K, 1 MMA, 2 TMA V, 3 TMA Q (warpgroup 0, 88 registers);
+//          4-7 softmax head A, 8-11 softmax head B (200 registers each).
 constexpr int kPOffQ = 0;                           // Q_h at h * kQBytes
 constexpr int kPOffK = 2 * kQBytes;                 // K slot s at kPOffK + s * kTileBytes
 constexpr int kPOffV = kPOffK + 2 * kTileBytes;
-constexpr int kPOffBar = kPOffV + 2 * kTileBytes;
+constexpr int kPOffStage = kPOffV + 2 * kTileBytes; // head h's 16 KB output box at + h * kBox
+constexpr int kPOffBar = kPOffStage + 2 * kBox;
 constexpr int kPSmemBytes = kPOffBar + 512 + 1024;
+static_assert(kPSmemBytes <= 227 * 1024, "shared memory per block");
 constexpr int kPThreads = 12 * 32;
 // setmaxnreg split: warpgroup 0 shrinks to kPRegsCtl, the two softmax
 // warpgroups grow to kPRegsSoftmax.  The grown share is drawn from the
@@ -365,19 +373,37 @@ static_assert(128 * kPRegsCtl + 256 * kPRegsSoftmax <= kPThreads * kPRegsLaunch,
               "register split exceeds the launch allocation");
 static_assert(kPRegsCtl % 8 == 0 && kPRegsSoftmax % 8 == 0, "setmaxnreg counts are multiples of 8");
 
-// Output staging for head h at the end of the CTA: the slot of Q_h.
-__device__ __forceinline__ uint8_t *stage_base(uint8_t *smem, int h) { return smem + kPOffQ + h * kQBytes; }
-
 struct PairBars {
-    uint64_t q_full;
+    uint64_t q_full, q_empty;  // once per item
     uint64_t k_full[2], k_empty[2];
     uint64_t v_full[2], v_empty[2];
-    uint64_t s_full[2];   // [head], once per key tile
-    uint64_t p_full[2][2];  // [head][half]: P of keys 64*half..+63 written (4 warps)
-    uint64_t o_done[2];   // [head], after the head's last PV
+    uint64_t s_full[2];        // [head], once per key tile
+    uint64_t p_full[2][2];     // [head][half]: P of keys 64*half..+63 written (4 warps)
+    uint64_t o_done[2];        // [head], once per item, after the head's last PV
     uint32_t tmem_base;
     int abort;
 };
+
+// The item of this CTA's round `round` (false once the CTA is done).
+struct PairItem {
+    int qh0;        // heads qh0, qh0 + 1 share KV head qh0 / group
+    int q0;         // first query row of the tile
+    int n_kv;       // key tiles the tile attends to
+    int first_pos;  // position of the tile's first query row
+};
+__device__ __forceinline__ bool pair_item(const PrefillParams &p, int round, PairItem &it) {
+    const int grid = (int)gridDim.x, b = (int)blockIdx.x;
+    const int pairs = p.qheads / 2;
+    const long long r = (long long)round * grid + ((round & 1) ? (grid - 1 - b) : b);
+    if (r >= (long long)p.n_qtiles * pairs) return false;
+    const int qt = p.n_qtiles - 1 - (int)(r / pairs);
+    it.qh0 = 2 * (int)(r % pairs);
+    it.q0 = qt * kRows;
+    const int last_row = min(it.q0 + kRows, p.queries) - 1;
+    it.n_kv = (p.prior + last_row) / kKeys + 1;
+    it.first_pos = p.prior + it.q0;
+    return true;
+}
 
 __global__ void __launch_bounds__(kPThreads, 1)
     mslim_prefill_pair(const __grid_constant__ CUtensorMap qmap,
@@ -390,20 +416,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
     PairBars *bars = reinterpret_cast<PairBars *>(smem + kPOffBar);
     volatile int *abort_flag = &bars->abort;
 
-    const int pairs = p.qheads / 2;
-    const int bid = blockIdx.x;
-    const int qt = p.n_qtiles - 1 - bid / pairs;  // heavy (late) tiles first
-    const int qh0 = 2 * (bid % pairs);            // heads qh0, qh0 + 1 share a KV head
-    const int kvh = qh0 / p.group;
-    const int q0 = qt * kRows;
-    const int last_row = min(q0 + kRows, p.queries) - 1;
-    const int n_kv = (p.prior + last_row) / kKeys + 1;
-    const int first_pos = p.prior + q0;
-
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         mbar_init(&bars->q_full, 1);
+        mbar_init(&bars->q_empty, 1);
         for (int b = 0; b < 2; ++b) {
             mbar_init(&bars->k_full[b], 1);
             mbar_init(&bars->k_empty[b], 1);
@@ -427,46 +444,65 @@ __global__ void __launch_bounds__(kPThreads, 1)
     if (warp < 4) {
         warpgroup_reg_dealloc<kPRegsCtl>();
         if ((warp == 0 || warp == 2) && lane == 0) {
-            // ------------------------------------------------------ TMA --
+            // -------------------------------------------------- TMA K / V --
             const bool is_k = warp == 0;
             const CUtensorMap *map = is_k ? &kmap : &vmap;
             uint64_t *full = is_k ? bars->k_full : bars->v_full;
             uint64_t *empty = is_k ? bars->k_empty : bars->v_empty;
             uint8_t *ring = smem + (is_k ? kPOffK : kPOffV);
             prefetch_tmap(map);
-            if (is_k) {
-                prefetch_tmap(&qmap);
-                mbar_arrive_expect_tx(&bars->q_full, 2 * kQBytes);
-                for (int h = 0; h < 2; ++h) {
-                    tma_load_3d(smem + kPOffQ + h * kQBytes, &qmap, &bars->q_full, 0, qh0 + h, q0);
-                    tma_load_3d(smem + kPOffQ + h * kQBytes + kBox, &qmap, &bars->q_full, 64, qh0 + h, q0);
+            int g = 0;  // key tiles loaded so far, over all items
+            bool run = true;
+            PairItem it;
+            for (int round = 0; run && pair_item(p, round, it); ++round) {
+                const int kvh = it.qh0 / p.group;
+                for (int j = 0; j < it.n_kv; ++j) {
+                    const int st = g & 1;
+                    if (*abort_flag ||
+                        !mbar_wait(&empty[st], ((g >> 1) & 1) ^ 1, p.status, is_k ? 41 : 42)) {
+                        *abort_flag = 1;
+                        run = false;
+                        break;
+                    }
+                    uint8_t *dst = ring + st * kTileBytes;
+                    mbar_arrive_expect_tx(&full[st], kTileBytes);
+                    tma_load_3d(dst, map, &full[st], 0, kvh, j * kKeys);
+                    tma_load_3d(dst + kBox, map, &full[st], 64, kvh, j * kKeys);
+                    ++g;
                 }
             }
-            int issued = 0;
-            for (int j = 0; j < n_kv && !*abort_flag; ++j) {
-                const int st = j & 1;
-                if (!mbar_wait(&empty[st], ((j >> 1) & 1) ^ 1, p.status, is_k ? 41 : 42)) {
+            // our copies must land before the CTA can retire
+            for (int t = max(0, g - 2); t < g; ++t) mbar_wait(&full[t & 1], (t >> 1) & 1, p.status, 44);
+        } else if (warp == 3 && lane == 0) {
+            // ------------------------------------------------------ TMA Q --
+            prefetch_tmap(&qmap);
+            int loaded = 0;
+            PairItem it;
+            for (int round = 0; pair_item(p, round, it); ++round) {
+                // Q of the previous item is free once its last S MMAs completed
+                if (*abort_flag ||
+                    (round > 0 && !mbar_wait(&bars->q_empty, (round - 1) & 1, p.status, 43))) {
                     *abort_flag = 1;
                     break;
                 }
-                uint8_t *dst = ring + st * kTileBytes;
-                mbar_arrive_expect_tx(&full[st], kTileBytes);
-                tma_load_3d(dst, map, &full[st], 0, kvh, j * kKeys);
-                tma_load_3d(dst + kBox, map, &full[st], 64, kvh, j * kKeys);
-                issued = j + 1;
+                mbar_arrive_expect_tx(&bars->q_full, 2 * kQBytes);
+                for (int h = 0; h < 2; ++h) {
+                    tma_load_3d(smem + kPOffQ + h * kQBytes, &qmap, &bars->q_full, 0, it.qh0 + h, it.q0);
+                    tma_load_3d(smem + kPOffQ + h * kQBytes + kBox, &qmap, &bars->q_full, 64, it.qh0 + h,
+                                it.q0);
+                }
+                ++loaded;
             }
-            if (is_k) mbar_wait(&bars->q_full, 0, p.status, 43);
-            for (int j = max(0, issued - 2); j < issued; ++j)
-                mbar_wait(&full[j & 1], (j >> 1) & 1, p.status, 44);
+            if (loaded > 0) mbar_wait(&bars->q_full, (loaded - 1) & 1, p.status, 45);
         } else if (warp == 1) {
             // ------------------------------------------------------ MMA --
             // the whole warp runs the loop; umma_* elect the issuing lane
             auto wait_all = [&](uint64_t *bar, uint32_t parity, int where) -> bool {
                 return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.status, where));
             };
-            auto issue_s = [&](int h, int j) {
+            auto issue_s = [&](int h, int slot) {
                 const uint32_t qaddr = sbase + kPOffQ + h * kQBytes;
-                const uint32_t kaddr = sbase + kPOffK + (j & 1) * kTileBytes;
+                const uint32_t kaddr = sbase + kPOffK + slot * kTileBytes;
 #pragma unroll
                 for (int kk = 0; kk < kDim / 16; ++kk) {
                     const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
@@ -475,44 +511,52 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 }
                 umma_commit(&bars->s_full[h]);
             };
-            bool ok = wait_all(&bars->q_full, 0, 51) && wait_all(&bars->k_full[0], 0, 52);
-            if (ok) {
+            int g = 0;  // key tiles consumed so far, over all items
+            bool ok = true;
+            PairItem it;
+            for (int round = 0; ok && pair_item(p, round, it); ++round) {
+                ok = wait_all(&bars->q_full, round & 1, 51) && wait_all(&bars->k_full[g & 1], (g >> 1) & 1, 52);
+                if (!ok) break;
                 tc_fence_after();
-                issue_s(0, 0);
-                issue_s(1, 0);
-                umma_commit(&bars->k_empty[0]);
-            }
-            for (int j = 0; ok && j < n_kv; ++j) {
-                if (__any_sync(0xffffffffu, *abort_flag != 0)) {
-                    ok = false;
-                    break;
-                }
-                const bool next = j + 1 < n_kv;
-                ok = wait_all(&bars->v_full[j & 1], (j >> 1) & 1, 54);
-                if (ok && next) ok = wait_all(&bars->k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, 52);
-                const uint32_t vaddr = sbase + kPOffV + (j & 1) * kTileBytes;
-                for (int h = 0; ok && h < 2; ++h) {
-                    // PV over keys 0..63 starts while the softmax still
-                    // writes P for keys 64..127
-                    for (int half = 0; ok && half < 2; ++half) {
-                        ok = wait_all(&bars->p_full[h][half], j & 1, 55);
-                        if (!ok) break;
-                        tc_fence_after();
+                issue_s(0, g & 1);
+                issue_s(1, g & 1);
+                umma_commit(&bars->k_empty[g & 1]);
+                if (it.n_kv == 1) umma_commit(&bars->q_empty);
+                for (int j = 0; ok && j < it.n_kv; ++j, ++g) {
+                    if (__any_sync(0xffffffffu, *abort_flag != 0)) {
+                        ok = false;
+                        break;
+                    }
+                    const bool next = j + 1 < it.n_kv;
+                    ok = wait_all(&bars->v_full[g & 1], (g >> 1) & 1, 54);
+                    if (ok && next) ok = wait_all(&bars->k_full[(g + 1) & 1], ((g + 1) >> 1) & 1, 52);
+                    const uint32_t vaddr = sbase + kPOffV + (g & 1) * kTileBytes;
+                    for (int h = 0; ok && h < 2; ++h) {
+                        // PV over keys 0..63 starts while the softmax still
+                        // writes P for keys 64..127
+                        for (int half = 0; ok && half < 2; ++half) {
+                            ok = wait_all(&bars->p_full[h][half], g & 1, 55);
+                            if (!ok) break;
+                            tc_fence_after();
 #pragma unroll
-                        for (int kq = 0; kq < kKeys / 32; ++kq) {
-                            const int kk = half * (kKeys / 32) + kq;
-                            umma_bf16_ts(tmem + kColO + h * 128, tmem + h * 128 + kk * 8,
-                                         umma_desc_sw128(vaddr + kk * 16 * 128, kBox, 1024), kIdescPV,
-                                         (j > 0 || kk > 0) ? 1u : 0u);
+                            for (int kq = 0; kq < kKeys / 32; ++kq) {
+                                const int kk = half * (kKeys / 32) + kq;
+                                umma_bf16_ts(tmem + kColO + h * 128, tmem + h * 128 + kk * 8,
+                                             umma_desc_sw128(vaddr + kk * 16 * 128, kBox, 1024), kIdescPV,
+                                             (j > 0 || kk > 0) ? 1u : 0u);
+                            }
+                        }
+                        if (!ok) break;
+                        if (next) issue_s(h, (g + 1) & 1);
+                        else umma_commit(&bars->o_done[h]);
+                    }
+                    if (ok) {
+                        umma_commit(&bars->v_empty[g & 1]);
+                        if (next) {
+                            umma_commit(&bars->k_empty[(g + 1) & 1]);
+                            if (j + 2 == it.n_kv) umma_commit(&bars->q_empty);
                         }
                     }
-                    if (!ok) break;
-                    if (next) issue_s(h, j + 1);
-                    else umma_commit(&bars->o_done[h]);
-                }
-                if (ok) {
-                    umma_commit(&bars->v_empty[j & 1]);
-                    if (next) umma_commit(&bars->k_empty[(j + 1) & 1]);
                 }
             }
             if (!ok && lane == 0) *abort_flag = 1;
@@ -528,123 +572,129 @@ __global__ void __launch_bounds__(kPThreads, 1)
         const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
         const uint32_t scol = lane_addr + h * 128;
         const uint32_t ocol = lane_addr + kColO + h * 128;
-        const int qpos = p.prior + q0 + row;
         const float scale = p.scale_log2;
-        float m_used = -INFINITY, l_run = 0.f;
+        const bool issuer = quarter == 0 && lane == 0;
+        uint8_t *stage = smem + kPOffStage + h * kBox;
+        int g = 0;  // key tiles seen so far, over all items
         bool ok = true;
-        for (int j = 0; j < n_kv; ++j) {
-            const bool got = mbar_wait(&bars->s_full[h], j & 1, p.status, 61);
-            if (!__all_sync(0xffffffffu, got) || __any_sync(0xffffffffu, *abort_flag != 0)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            const int k0 = j * kKeys;
-            const bool diag = k0 + kKeys - 1 > first_pos;
-            // the whole 128-key row of S in registers (one load, one wait)
-            float v[128];
-            tmem_ld128(scol, v);
-            if (diag) {
-#pragma unroll
-                for (int i = 0; i < 128; ++i)
-                    if (k0 + i > qpos) v[i] = -INFINITY;
-            }
-            // row max of the raw scores (the scale is positive, so it is
-            // applied to the max only); four independent three-input chains
-            float m4[4] = {v[0], v[1], v[2], v[3]};
-#pragma unroll
-            for (int i = 4; i + 8 <= 128; i += 8)
-#pragma unroll
-                for (int a = 0; a < 4; ++a) m4[a] = fmax3(m4[a], v[i + a], v[i + 4 + a]);
-#pragma unroll
-            for (int a = 0; a < 4; ++a) m4[a] = fmaxf(m4[a], v[124 + a]);
-            const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * scale;
-            const bool move = mx > m_used + kRescaleLog2;
-            const float m_new = move ? mx : m_used;
-            const float base = (m_new == -INFINITY) ? 0.f : m_new;
-            const float alpha = move ? fast_exp2(m_used - base) : 1.f;
-            // P = 2^(s*scale - base); keys 64c..64c+63 go to columns
-            // 32c..32c+31, whose S values are already in registers.  Each half
-            // is announced on its own barrier; O is rescaled before the first.
-            const uint64_t scale2 = f2_pack(scale, scale);
-            const uint64_t nbase2 = f2_pack(-base, -base);
-            uint64_t sum2[4] = {0, 0, 0, 0};
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                uint32_t w[32];
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int e = c * 64 + 2 * i;
-                    float x0, x1;
-                    f2_unpack(f2_fma(f2_pack(v[e], v[e + 1]), scale2, nbase2), x0, x1);
-                    const bool poly = MSLIM_PAIR_EXP_ON_FMA(i);
-                    const float p0 = poly ? exp2_fma(x0) : fast_exp2(x0);
-                    const float p1 = poly ? exp2_fma(x1) : fast_exp2(x1);
-                    sum2[i & 3] = f2_add(sum2[i & 3], f2_pack(p0, p1));
-                    w[i] = pack_bf16x2(p0, p1);
+        PairItem it;
+        for (int round = 0; ok && pair_item(p, round, it); ++round) {
+            const int qpos = p.prior + it.q0 + row;
+            float m_used = -INFINITY, l_run = 0.f;
+            for (int j = 0; j < it.n_kv; ++j, ++g) {
+                const bool got = mbar_wait(&bars->s_full[h], g & 1, p.status, 61);
+                if (!__all_sync(0xffffffffu, got) || __any_sync(0xffffffffu, *abort_flag != 0)) {
+                    ok = false;
+                    break;
                 }
-                tmem_st32u_nowait(scol + c * 32, w);
-                if (c == 0 && j > 0 && __any_sync(0xffffffffu, move)) {
-                    // S_h(j) done implies PV_h(j-1) done: O_h is final for j-1,
-                    // and PV_h(j) waits for the arrive below
+                tc_fence_after();
+                const int k0 = j * kKeys;
+                // the whole 128-key row of S in registers (one load, one wait)
+                float v[128];
+                tmem_ld128(scol, v);
+                if (k0 + kKeys - 1 > it.first_pos) {
 #pragma unroll
-                    for (int oc = 0; oc < 4; ++oc) {
-                        float o[32];
-                        tmem_ld32(ocol + oc * 32, o);
+                    for (int i = 0; i < 128; ++i)
+                        if (k0 + i > qpos) v[i] = -INFINITY;
+                }
+                // row max of the raw scores (the scale is positive, so it is
+                // applied to the max only); four independent three-input chains
+                float m4[4] = {v[0], v[1], v[2], v[3]};
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) o[i] *= alpha;
-                        tmem_st32(ocol + oc * 32, o);
+                for (int i = 4; i + 8 <= 128; i += 8)
+#pragma unroll
+                    for (int a = 0; a < 4; ++a) m4[a] = fmax3(m4[a], v[i + a], v[i + 4 + a]);
+#pragma unroll
+                for (int a = 0; a < 4; ++a) m4[a] = fmaxf(m4[a], v[124 + a]);
+                const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * scale;
+                const bool move = mx > m_used + kRescaleLog2;
+                const float m_new = move ? mx : m_used;
+                const float base = (m_new == -INFINITY) ? 0.f : m_new;
+                const float alpha = move ? fast_exp2(m_used - base) : 1.f;
+                // P = 2^(s*scale - base); keys 64c..64c+63 go to columns
+                // 32c..32c+31, whose S values are already in registers.  Each
+                // half is announced on its own barrier; O is rescaled before
+                // the first.
+                const uint64_t scale2 = f2_pack(scale, scale);
+                const uint64_t nbase2 = f2_pack(-base, -base);
+                uint64_t sum2[4] = {0, 0, 0, 0};
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t w[32];
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const int e = c * 64 + 2 * i;
+                        float x0, x1;
+                        f2_unpack(f2_fma(f2_pack(v[e], v[e + 1]), scale2, nbase2), x0, x1);
+                        const bool poly = MSLIM_PAIR_EXP_ON_FMA(i);
+                        const float p0 = poly ? exp2_fma(x0) : fast_exp2(x0);
+                        const float p1 = poly ? exp2_fma(x1) : fast_exp2(x1);
+                        sum2[i & 3] = f2_add(sum2[i & 3], f2_pack(p0, p1));
+                        w[i] = pack_bf16x2(p0, p1);
                     }
-                }
-                tmem_wait_st();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&bars->p_full[h][c]);
-            }
-            float s8[8];
+                    tmem_st32u_nowait(scol + c * 32, w);
+                    if (c == 0 && j > 0 && __any_sync(0xffffffffu, move)) {
+                        // S_h(j) done implies PV_h(j-1) done: O_h is final for
+                        // j-1, and PV_h(j) waits for the arrive below
 #pragma unroll
-            for (int a = 0; a < 4; ++a) f2_unpack(sum2[a], s8[2 * a], s8[2 * a + 1]);
-            const float ps = ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
-            l_run = l_run * alpha + ps;
-            m_used = m_new;
-        }
-        const bool last = ok && mbar_wait(&bars->o_done[h], 0, p.status, 64);
-        const bool good = __all_sync(0xffffffffu, last);
-        if (good) {
+                        for (int oc = 0; oc < 4; ++oc) {
+                            float o[32];
+                            tmem_ld32(ocol + oc * 32, o);
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) o[i] *= alpha;
+                            tmem_st32(ocol + oc * 32, o);
+                        }
+                    }
+                    tmem_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&bars->p_full[h][c]);
+                }
+                float s8[8];
+#pragma unroll
+                for (int a = 0; a < 4; ++a) f2_unpack(sum2[a], s8[2 * a], s8[2 * a + 1]);
+                const float ps = ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
+                l_run = l_run * alpha + ps;
+                m_used = m_new;
+            }
+            // ---- output of this item: O_h / l -> bf16, one 64-column box at a
+            // time through the head's 16 KB staging buffer (TMA 128-byte
+            // swizzled layout) and a bulk tensor store; rows past the last
+            // query are clipped by the store.
+            const bool good = ok && __all_sync(0xffffffffu, mbar_wait(&bars->o_done[h], round & 1, p.status, 64));
+            if (!good) *abort_flag = 1;
             tc_fence_after();
-            // O_h / l -> bf16, staged in Q_h's slot (its last reader, S_h of
-            // the final tile, has completed) in the TMA 128-byte-swizzled
-            // layout, then written by one bulk tensor store per 64 columns;
-            // rows past the last query are clipped by the store.
             const float inv = 1.0f / l_run;
-            uint8_t *stage = stage_base(smem, h);
+            for (int box = 0; box < 2; ++box) {
+                if (issuer) bulk_wait_read_all();  // the previous store has read the buffer
+                named_bar_sync(1 + h, 128);
+                if (good) {
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                float o[32];
-                tmem_ld32(ocol + c * 32, o);
-                uint32_t w[16];
+                    for (int c = 0; c < 2; ++c) {
+                        float o[32];
+                        tmem_ld32(ocol + box * 64 + c * 32, o);
+                        uint32_t w[16];
 #pragma unroll
-                for (int i = 0; i < 16; ++i) w[i] = pack_bf16x2(o[2 * i] * inv, o[2 * i + 1] * inv);
-                uint8_t *box_row = stage + (c >> 1) * kBox + row * 128;
+                        for (int i = 0; i < 16; ++i) w[i] = pack_bf16x2(o[2 * i] * inv, o[2 * i + 1] * inv);
 #pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    const int chunk = ((c & 1) * 4 + t) ^ (row & 7);
-                    *reinterpret_cast<uint4 *>(box_row + chunk * 16) =
-                        make_uint4(w[4 * t], w[4 * t + 1], w[4 * t + 2], w[4 * t + 3]);
+                        for (int t = 0; t < 4; ++t) {
+                            const int chunk = (c * 4 + t) ^ (row & 7);
+                            *reinterpret_cast<uint4 *>(stage + row * 128 + chunk * 16) =
+                                make_uint4(w[4 * t], w[4 * t + 1], w[4 * t + 2], w[4 * t + 3]);
+                        }
+                    }
+                    fence_proxy_async_smem();
+                }
+                named_bar_sync(1 + h, 128);
+                if (issuer && *abort_flag == 0) {
+                    tma_store_3d(&omap, stage, box * 64, it.qh0 + h, it.q0);
+                    bulk_commit_group();
                 }
             }
-            fence_proxy_async_smem();
-        } else {
-            *abort_flag = 1;
+            // the head's four warps continue or stop together
+            if (named_bar_or(1 + h, 128, !good || *abort_flag != 0)) ok = false;
         }
-        // every warp of the head's warpgroup reaches this barrier on every path
-        asm volatile("bar.sync %0, 128;" ::"r"(2 + h) : "memory");
-        if (quarter == 0 && lane == 0 && *abort_flag == 0) {
-            tma_store_3d(&omap, stage_base(smem, h), 0, qh0 + h, q0);
-            tma_store_3d(&omap, stage_base(smem, h) + kBox, 64, qh0 + h, q0);
-            bulk_commit_group();
-            bulk_wait_all();
-        }
+        if (issuer) bulk_wait_all();
     }
     tc_fence_before();
     __syncthreads();
@@ -672,7 +722,14 @@ cudaError_t launch_prefill(const CUtensorMap &qmap, const CUtensorMap &kmap,
         err = cudaFuncGetAttributes(&fa, mslim_prefill_pair);
         if (err != cudaSuccess) return err;
         if (fa.numRegs * kPThreads < 128 * kPRegsCtl + 256 * kPRegsSoftmax) return cudaErrorInvalidConfiguration;
-        const unsigned grid = (unsigned)(p.n_qtiles * (p.qheads / 2));
+        // persistent: one CTA per SM (at most one per item)
+        int dev = 0, sms = 0;
+        err = cudaGetDevice(&dev);
+        if (err != cudaSuccess) return err;
+        err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (err != cudaSuccess) return err;
+        const long long items = (long long)p.n_qtiles * (p.qheads / 2);
+        const unsigned grid = (unsigned)(items < sms ? items : sms);
         mslim_prefill_pair<<<grid, kPThreads, kPSmemBytes, stream>>>(qmap, kmap, vmap, omap, p);
         return cudaGetLastError();
     }
