@@ -224,50 +224,99 @@ def run_reference(args, rank: int) -> None:
 
 def bench_prefill(m, torch, device, args) -> dict:
     """C2: causal prefill, S = 2048, 32/8 heads,
-    D = 128.  Its 24 MB of inputs fit in L2, so a 256 MB buffer is written
-    between timed iterations and each iteration is timed alone."""
-    S = 2048
+    D = 128, through the C ABI (mslim_cuda_prefill_causal).
+
+    One call's Q/K/V/O (40 MB) fit in the 126 MB L2, so the leg keeps six
+    copies (240 MB) and rotates through them: every call reads inputs last
+    touched five calls (200 MB of traffic) earlier.  The timed calls are
+    captured once into a CUDA graph and replayed back to back between one
+    pair of CUDA events (as consecutive layers' prefill would run), so host
+    jitter (Python, the clock-sampling thread) cannot idle the GPU between
+    them.  The same calls issued from a plain host loop, and one call timed
+    alone (which carries 4-7 us of event/launch latency on top of the
+    kernel), are reported beside it."""
+    S, copies = 2048, 6
     g = m.AttentionGeometry.new(QH, KVH, D)
     gen = torch.Generator(device=device)
     gen.manual_seed(1)
-    q = torch.randn((S, QH, D), generator=gen, device=device, dtype=torch.bfloat16)
-    k = torch.randn((S, KVH, D), generator=gen, device=device, dtype=torch.bfloat16)
-    v = torch.randn((S, KVH, D), generator=gen, device=device, dtype=torch.bfloat16)
-    out = torch.empty_like(q)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    q0 = torch.randn((S, QH, D), generator=gen, device=device, dtype=torch.bfloat16)
+    k0 = torch.randn((S, KVH, D), generator=gen, device=device, dtype=torch.bfloat16)
+    v0 = torch.randn((S, KVH, D), generator=gen, device=device, dtype=torch.bfloat16)
+    sets = [(q0.clone(), k0.clone(), v0.clone(), torch.empty_like(q0)) for _ in range(copies)]
     stream = torch.cuda.current_stream()
-    for _ in range(max(args.warmup, 3)):
-        m.prefill_causal(g, q, k, v, out, S, 0, stream)
+
+    def call(i, st):
+        q, k, v, out = sets[i % copies]
+        m.prefill_causal(g, q, k, v, out, S, 0, st)
+
+    for i in range(max(args.warmup, 3) * copies):
+        call(i, stream)
     torch.cuda.synchronize()
-    steps = max(10, min(args.steps, 100))
-    times = []
+    steps = max(12, min(args.steps, 48))
+    graph = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream()
+    cap.wait_stream(stream)
+    with torch.cuda.graph(graph, stream=cap, capture_error_mode="thread_local"):
+        for i in range(steps):
+            call(i, torch.cuda.current_stream())
+    graph.replay()
+    torch.cuda.synchronize()
+    # an idle gap, so the power limiter's state from the preceding (HBM-bound)
+    # legs does not carry into this burst; the timed block itself is ~2 ms,
+    # a burst, matching the burst GEMM peak it is divided by
+    time.sleep(0.5)
     sampler = ClockSampler(torch.cuda.current_device())
     sampler.start()
-    for _ in range(steps):
-        flush.zero_()
-        a = torch.cuda.Event(enable_timing=True)
-        b = torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        m.prefill_causal(g, q, k, v, out, S, 0, stream)
-        b.record(stream)
-        b.synchronize()
-        times.append(a.elapsed_time(b))
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    graph.replay()
+    b.record(stream)
+    b.synchronize()
+    ms = a.elapsed_time(b) / steps
     clocks = sampler.stop()
+    # the same calls from a plain host loop
+    torch.cuda.synchronize()
+    a.record(stream)
+    for i in range(steps):
+        call(i, stream)
+    b.record(stream)
+    b.synchronize()
+    ms_loop = a.elapsed_time(b) / steps
+    # one call timed alone (events around one launch)
+    alone = []
+    for i in range(10):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        call(i, stream)
+        e1.record(stream)
+        e1.synchronize()
+        alone.append(e0.elapsed_time(e1))
+    del graph
     if m.device_status(torch.cuda.current_device()) != 0:
         raise SystemExit("device status reported an error during the prefill leg")
     flops = 4 * D * QH * S * (S + 1) // 2
-    ms = statistics.mean(times)
     tflops = flops / (ms * 1e-3) / 1e12
     peaks = measured_peaks()
+    kernel = "mslim_prefill_pair" if (QH // KVH) % 2 == 0 else "mslim_prefill_causal"
+    traffic = profile_traffic("prefill_c2_traffic.json")
     return {"metric": "prefill attn TFLOPS (C2 causal, S 2048, 32/8 heads, D 128)", "value": tflops,
-            "unit": "TFLOP/s", "ms_per_step": ms, "ms_min": min(times), "steps": steps,
-            "algorithmic_flops": flops, "l2": "256 MB written between timed iterations",
-            "roofline": {"bound": "tensor", "kernel": "mslim_prefill_causal", "achieved": tflops,
+            "unit": "TFLOP/s", "ms_per_step": ms, "steps": steps,
+            "timing": "calls captured in one CUDA graph, replayed between one pair of CUDA events",
+            "ms_per_call_host_loop": ms_loop,
+            "ms_single_call_events": statistics.median(alone),
+            "algorithmic_flops": flops,
+            "l2": (f"inputs larger than L2: {copies} rotating copies of Q/K/V/O "
+                   f"({copies * 40} MB > 126 MB L2), calls back to back"),
+            "roofline": {"bound": "tensor", "kernel": kernel, "achieved": tflops,
                          "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": tflops / peaks["bf16_tflops"] if peaks["bf16_tflops"] else None,
-                         "peak_source": ("measured (MEASURED_PEAKS.json bf16_tflops, burst: kernel timed alone)"
+                         "peak_source": ("measured (MEASURED_PEAKS.json bf16_tflops, burst)"
                                          if peaks["source"] == "measured" else "fallback 1590 TFLOP/s"),
-                         "traffic": None},
+                         "frac_of_sustained": (tflops / peaks["bf16_tflops_sustained"]
+                                               if peaks.get("bf16_tflops_sustained") else None),
+                         "traffic": traffic["dram_bytes_per_launch"] if traffic else None},
             "gpu_launches": steps, "clocks": clocks}
 
 

@@ -22,6 +22,9 @@
 //              max moves (and its O is rescaled in place) only when a tile's max
 //              exceeds it by more than 2^8.
 // Every mbarrier wait is bounded; the CTA always frees its TMEM.
+#include <atomic>
+#include <mutex>
+
 #include "../../include/mslim_cuda.h"
 #include "prefill.cuh"
 
@@ -710,32 +713,62 @@ bool prefill_supported(unsigned head_dim, unsigned group) { return head_dim == 1
 
 bool prefill_pairs_heads(unsigned group) { return group % 2 == 0; }
 
+namespace {
+
+// Per-device launch setup, done once: shared-memory opt-in for both kernels,
+// the register check of the pair kernel's setmaxnreg split, and the SM count.
+struct PrefillDeviceSetup {
+    std::atomic<int> state{0};  // 0 not yet, 1 ready, 2 failed
+    cudaError_t err = cudaSuccess;
+    int sms = 0;
+};
+constexpr int kMaxDevices = 64;
+PrefillDeviceSetup g_setup[kMaxDevices];
+std::mutex g_setup_mutex;
+
+cudaError_t prefill_setup(int dev, int *sms) {
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    PrefillDeviceSetup &d = g_setup[dev];
+    if (d.state.load(std::memory_order_acquire) == 0) {
+        std::lock_guard<std::mutex> lock(g_setup_mutex);
+        if (d.state.load(std::memory_order_relaxed) == 0) {
+            cudaError_t err = cudaFuncSetAttribute(mslim_prefill_pair,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytes);
+            if (err == cudaSuccess)
+                err = cudaFuncSetAttribute(mslim_prefill_causal,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kSSmemBytes);
+            cudaFuncAttributes fa{};
+            if (err == cudaSuccess) err = cudaFuncGetAttributes(&fa, mslim_prefill_pair);
+            // the setmaxnreg split needs the registers it assumes at launch
+            if (err == cudaSuccess && fa.numRegs * kPThreads < 128 * kPRegsCtl + 256 * kPRegsSoftmax)
+                err = cudaErrorInvalidConfiguration;
+            if (err == cudaSuccess) err = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+            d.err = err;
+            d.state.store(err == cudaSuccess ? 1 : 2, std::memory_order_release);
+        }
+    }
+    if (d.state.load(std::memory_order_acquire) != 1) return d.err;
+    *sms = d.sms;
+    return cudaSuccess;
+}
+
+}  // namespace
+
 cudaError_t launch_prefill(const CUtensorMap &qmap, const CUtensorMap &kmap,
                            const CUtensorMap &vmap, const CUtensorMap &omap,
                            const PrefillParams &p, cudaStream_t stream) {
+    int dev = 0, sms = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return err;
+    err = prefill_setup(dev, &sms);
+    if (err != cudaSuccess) return err;
     if (prefill_pairs_heads((unsigned)p.group)) {
-        cudaError_t err = cudaFuncSetAttribute(mslim_prefill_pair,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytes);
-        if (err != cudaSuccess) return err;
-        // The setmaxnreg split needs the registers it assumes at launch.
-        cudaFuncAttributes fa{};
-        err = cudaFuncGetAttributes(&fa, mslim_prefill_pair);
-        if (err != cudaSuccess) return err;
-        if (fa.numRegs * kPThreads < 128 * kPRegsCtl + 256 * kPRegsSoftmax) return cudaErrorInvalidConfiguration;
         // persistent: one CTA per SM (at most one per item)
-        int dev = 0, sms = 0;
-        err = cudaGetDevice(&dev);
-        if (err != cudaSuccess) return err;
-        err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        if (err != cudaSuccess) return err;
         const long long items = (long long)p.n_qtiles * (p.qheads / 2);
         const unsigned grid = (unsigned)(items < sms ? items : sms);
         mslim_prefill_pair<<<grid, kPThreads, kPSmemBytes, stream>>>(qmap, kmap, vmap, omap, p);
         return cudaGetLastError();
     }
-    cudaError_t err = cudaFuncSetAttribute(mslim_prefill_causal,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kSSmemBytes);
-    if (err != cudaSuccess) return err;
     const unsigned grid = (unsigned)(p.n_qtiles * p.qheads);
     mslim_prefill_causal<<<grid, kSThreads, kSSmemBytes, stream>>>(qmap, kmap, vmap, p);
     return cudaGetLastError();
