@@ -212,6 +212,27 @@ int mslim_cuda_prefill_causal(const mslim_geometry_t *geometry, const void *q, c
                               const void *v, void *out, uint32_t queries, uint32_t prior,
                               void *stream);
 
+/* ------------------------------------------------- layer elementwise -- */
+
+/* GpuEngine::add (src/gpu_llm/gpu_resources.rs:539-559, kernel llm_add) and the
+ * CPU add_residual (src/native_cpu_adapter.rs:186-191): out = bf16(a + b),
+ * n bf16 elements; out may alias a or b. */
+int mslim_cuda_residual_add(const void *a, const void *b, void *out, uint64_t n, void *stream);
+
+/* GpuEngine::swiglu (src/gpu_llm/gpu_resources.rs:561-581, kernel llm_swiglu)
+ * and the CPU MLP (src/native_cpu_adapter.rs:553-560):
+ * out = bf16(bf16(g / (1 + exp(-g))) * u); out may alias gate or up. */
+int mslim_cuda_swiglu(const void *gate, const void *up, void *out, uint64_t n, void *stream);
+
+/* GpuEngine::argmax (src/gpu_llm/gpu_resources.rs:1065, kernel llm_argmax) and
+ * the CPU greedy step (src/native_cpu_adapter.rs:582-587): one int32 token id
+ * per row of `rows` x `vocab` bf16 logits (device pointers).
+ * ties_to_last = 1: f32::total_cmp order, last index among equal maxima (the
+ * CPU path's Iterator::max_by, the parity reference); 0: float order, first
+ * index among equals, NaN never preferred (the OpenCL kernel). */
+int mslim_cuda_argmax(const void *logits, uint32_t rows, uint32_t vocab, int ties_to_last,
+                      int32_t *token_ids, void *stream);
+
 /* ------------------------------------------------------ prologue -- */
 
 /* GpuEngine::norm / BatchKernels::norm (src/gpu_llm/gpu_resources.rs:485-507,

@@ -17,6 +17,10 @@
  *   assets/gpu_llm.cl:72-146           GPU RMSNorm / RoPE formulas
  *   src/cold_store.rs:909-922,763-781  FNV-1a checksum and per-token hashes
  *   src/gpu_region_store.rs:470-483    token-major -> head-major page layout
+ *   src/native_cpu_adapter.rs:129-148  matvec (rows of bf16 weights . f32 x)
+ *   src/native_cpu_adapter.rs:486-591  forward_token: one decoder layer per
+ *                                       token, SwiGLU, residuals, final norm,
+ *                                       lm_head and the greedy argmax
  *
  * Numeric rules kept from the Rust source:
  *   - every f32 sum is a left-to-right fold (Rust `Iterator::sum::<f32>()`
@@ -461,4 +465,144 @@ int mo_openmp_max_threads(void) {
 #else
     return 1;
 #endif
+}
+
+/* ---------------------------------------------------- decoder layer -- */
+
+/* native_cpu_adapter.rs:129-148: out[r] = round_bf16(sum_c bf16(w[r][c]) * x[c]),
+ * the sum a left fold in column order.  Rows in parallel (rayon
+ * par_chunks_exact over rows; no reduction order changes). */
+void mo_matvec_bf16(const uint16_t *w, size_t rows, size_t cols, const float *x, float *out,
+                    int threads) {
+    long r;
+    (void)threads;
+#pragma omp parallel for schedule(static) num_threads(threads > 0 ? threads : 1)
+    for (r = 0; r < (long)rows; ++r) {
+        const uint16_t *row = w + (size_t)r * cols;
+        float sum = -0.0f;
+        for (size_t c = 0; c < cols; ++c) sum = sum + mo_bf16_to_f32(row[c]) * x[c];
+        out[r] = mo_round_bf16(sum);
+    }
+}
+
+/* native_cpu_adapter.rs:186-191 */
+void mo_add_residual(const float *lhs, const float *rhs, float *out, size_t n) {
+    for (size_t i = 0; i < n; ++i) out[i] = mo_round_bf16(lhs[i] + rhs[i]);
+}
+
+/* native_cpu_adapter.rs:553-560: silu = bf16(g / (1 + exp(-g))), out = bf16(silu * u). */
+void mo_swiglu(const float *gate, const float *up, float *out, size_t n) {
+    for (size_t i = 0; i < n; ++i) {
+        float g = gate[i];
+        float silu = mo_round_bf16(g / (1.0f + expf(-g)));
+        out[i] = mo_round_bf16(silu * up[i]);
+    }
+}
+
+/* f32::total_cmp key: a signed-magnitude order over the bits
+ * (-NaN < -inf < ... < -0 < +0 < ... < +inf < +NaN). */
+static inline int32_t total_key(float v) {
+    int32_t b = (int32_t)f32_bits(v);
+    return b ^ (int32_t)(((uint32_t)(b >> 31)) >> 1);
+}
+
+/* native_cpu_adapter.rs:582-587: logits.iter().enumerate().max_by(total_cmp);
+ * Iterator::max_by returns the last of equally maximal elements. */
+long mo_argmax_last(const float *x, size_t n) {
+    if (n == 0) return -1;
+    size_t best = 0;
+    int32_t key = total_key(x[0]);
+    for (size_t i = 1; i < n; ++i) {
+        int32_t k = total_key(x[i]);
+        if (k >= key) { key = k; best = i; }
+    }
+    return (long)best;
+}
+
+/* Weights of one decoder layer, bf16 row-major [out][in] (HF names). */
+typedef struct {
+    const uint16_t *input_norm;   /* [hidden] input_layernorm */
+    const uint16_t *wq;           /* [QH*D][hidden] self_attn.q_proj */
+    const uint16_t *wk;           /* [KVH*D][hidden] */
+    const uint16_t *wv;           /* [KVH*D][hidden] */
+    const uint16_t *wo;           /* [hidden][QH*D] self_attn.o_proj */
+    const uint16_t *post_norm;    /* [hidden] post_attention_layernorm */
+    const uint16_t *wg;           /* [intermediate][hidden] mlp.gate_proj */
+    const uint16_t *wu;           /* [intermediate][hidden] mlp.up_proj */
+    const uint16_t *wd;           /* [hidden][intermediate] mlp.down_proj */
+} mo_layer_weights;
+
+/* One layer of forward_token (native_cpu_adapter.rs:503-577) for the token at
+ * `position`.  k_cache / v_cache: bf16 token-major [>= position+1][KVH][D]
+ * holding positions 0..position-1; this token's K/V are written at
+ * `position` (the hot-dense append, :457-481) and attention runs over
+ * position+1 tokens (dense_attention_bf16).  state: f32 [hidden] holding bf16
+ * values, updated in place.  Optional outputs (NULL skips): q_rope (QH*D),
+ * k_rope (KVH*D), attn (QH*D): the post-RoPE query/key and the attention
+ * output of this token. */
+int mo_layer_forward_token(const mo_layer_weights *w, size_t hidden, size_t intermediate,
+                           size_t query_heads, size_t kv_heads, size_t head_dim, float eps,
+                           float theta, size_t position, uint16_t *k_cache, uint16_t *v_cache,
+                           float *state, float *q_rope, float *k_rope, float *attn_out,
+                           int threads) {
+    if (query_heads == 0 || kv_heads == 0 || head_dim == 0 || query_heads % kv_heads != 0)
+        return MO_ERR_GEOMETRY;
+    const size_t qd = query_heads * head_dim, kd = kv_heads * head_dim;
+    size_t big = hidden > intermediate ? hidden : intermediate;
+    if (qd > big) big = qd;
+    float *wf = (float *)malloc(hidden * sizeof(float));
+    float *normed = (float *)malloc(hidden * sizeof(float));
+    float *q = (float *)malloc(qd * sizeof(float));
+    float *k = (float *)malloc(kd * sizeof(float));
+    float *v = (float *)malloc(kd * sizeof(float));
+    float *att = (float *)malloc(qd * sizeof(float));
+    float *proj = (float *)malloc(big * sizeof(float));
+    float *gate = (float *)malloc(intermediate * sizeof(float));
+    float *up = (float *)malloc(intermediate * sizeof(float));
+    int rc = MO_OK;
+
+    mo_bf16_decode(w->input_norm, wf, hidden);
+    mo_rms_norm(state, wf, hidden, eps, normed);
+    mo_matvec_bf16(w->wq, qd, hidden, normed, q, threads);
+    mo_matvec_bf16(w->wk, kd, hidden, normed, k, threads);
+    mo_matvec_bf16(w->wv, kd, hidden, normed, v, threads);
+    /* round_vec after matvec is the identity on already-rounded values */
+    mo_apply_rope(q, query_heads, head_dim, position, theta);
+    mo_apply_rope(k, kv_heads, head_dim, position, theta);
+    mo_bf16_encode(k, k_cache + position * kd, kd);
+    mo_bf16_encode(v, v_cache + position * kd, kd);
+    rc = mo_dense_attention_bf16(query_heads, kv_heads, head_dim, q, k_cache, v_cache,
+                                 position + 1, att, threads);
+    if (rc == MO_OK) {
+        if (q_rope) memcpy(q_rope, q, qd * sizeof(float));
+        if (k_rope) memcpy(k_rope, k, kd * sizeof(float));
+        if (attn_out) memcpy(attn_out, att, qd * sizeof(float));
+        mo_matvec_bf16(w->wo, hidden, qd, att, proj, threads);
+        mo_add_residual(state, proj, state, hidden);
+        mo_bf16_decode(w->post_norm, wf, hidden);
+        mo_rms_norm(state, wf, hidden, eps, normed);
+        mo_matvec_bf16(w->wg, intermediate, hidden, normed, gate, threads);
+        mo_matvec_bf16(w->wu, intermediate, hidden, normed, up, threads);
+        mo_swiglu(gate, up, gate, intermediate);
+        mo_matvec_bf16(w->wd, hidden, intermediate, gate, proj, threads);
+        mo_add_residual(state, proj, state, hidden);
+    }
+    free(wf); free(normed); free(q); free(k); free(v); free(att); free(proj); free(gate); free(up);
+    return rc;
+}
+
+/* native_cpu_adapter.rs:579-587: final RMSNorm, lm_head matvec and the greedy
+ * token.  logits (optional): f32 [vocab] holding bf16 values. */
+long mo_lm_head_argmax(const float *state, const uint16_t *final_norm, const uint16_t *lm_head,
+                       size_t hidden, size_t vocab, float eps, float *logits, int threads) {
+    float *wf = (float *)malloc(hidden * sizeof(float));
+    float *normed = (float *)malloc(hidden * sizeof(float));
+    float *lg = logits ? logits : (float *)malloc(vocab * sizeof(float));
+    mo_bf16_decode(final_norm, wf, hidden);
+    mo_rms_norm(state, wf, hidden, eps, normed);
+    mo_matvec_bf16(lm_head, vocab, hidden, normed, lg, threads);
+    long next = mo_argmax_last(lg, vocab);
+    if (!logits) free(lg);
+    free(wf); free(normed);
+    return next;
 }

@@ -82,8 +82,26 @@ def lib() -> ctypes.CDLL:
         L.mo_token_hashes.argtypes = [_u8p, _sz, _sz, _sz, _u64p]
         L.mo_page_from_token_major.argtypes = [_u16p, _u16p, _sz, _sz, _sz]
         L.mo_openmp_max_threads.restype = ctypes.c_int
+        L.mo_matvec_bf16.argtypes = [_u16p, _sz, _sz, _f32p, _f32p, ctypes.c_int]
+        L.mo_add_residual.argtypes = [_f32p, _f32p, _f32p, _sz]
+        L.mo_swiglu.argtypes = [_f32p, _f32p, _f32p, _sz]
+        L.mo_argmax_last.argtypes = [_f32p, _sz]
+        L.mo_argmax_last.restype = ctypes.c_long
+        L.mo_layer_forward_token.argtypes = [ctypes.POINTER(LayerWeightsC), _sz, _sz, _sz, _sz, _sz,
+                                             ctypes.c_float, ctypes.c_float, _sz, _u16p, _u16p, _f32p,
+                                             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
+        L.mo_layer_forward_token.restype = ctypes.c_int
+        L.mo_lm_head_argmax.argtypes = [_f32p, _u16p, _u16p, _sz, _sz, ctypes.c_float, ctypes.c_void_p,
+                                        ctypes.c_int]
+        L.mo_lm_head_argmax.restype = ctypes.c_long
         _lib = L
         return L
+
+
+class LayerWeightsC(ctypes.Structure):
+    """mo_layer_weights: pointers to one layer's bf16 weights."""
+    _fields_ = [(n, ctypes.c_void_p) for n in
+                ("input_norm", "wq", "wk", "wv", "wo", "post_norm", "wg", "wu", "wd")]
 
 
 def max_threads() -> int:
@@ -271,3 +289,86 @@ def page_from_token_major(token_major: np.ndarray, kv_heads: int, head_dim: int)
     page = np.empty(kv_heads * n * head_dim, np.uint16)
     lib().mo_page_from_token_major(t, page, n, kv_heads, head_dim)
     return page.reshape(kv_heads, n, head_dim)
+
+
+# ----------------------------------------------------------- decoder layer --
+
+def matvec_bf16(w: np.ndarray, x: np.ndarray, threads: int = 0) -> np.ndarray:
+    """native_cpu_adapter.rs:129-148: bf16-rounded rows of w (bf16 bits [rows][cols]) . x."""
+    w = np.ascontiguousarray(w, np.uint16)
+    rows, cols = w.shape
+    out = np.empty(rows, np.float32)
+    lib().mo_matvec_bf16(w, rows, cols, np.ascontiguousarray(x, np.float32), out, threads or max_threads())
+    return out
+
+
+def add_residual(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """native_cpu_adapter.rs:186-191."""
+    a = np.ascontiguousarray(a, np.float32)
+    out = np.empty_like(a)
+    lib().mo_add_residual(a, np.ascontiguousarray(b, np.float32), out, a.size)
+    return out
+
+
+def swiglu(gate: np.ndarray, up: np.ndarray) -> np.ndarray:
+    """native_cpu_adapter.rs:553-560."""
+    g = np.ascontiguousarray(gate, np.float32)
+    out = np.empty_like(g)
+    lib().mo_swiglu(g, np.ascontiguousarray(up, np.float32), out, g.size)
+    return out
+
+
+def argmax_last(x: np.ndarray) -> int:
+    """native_cpu_adapter.rs:582-587: max_by(total_cmp), last of equal maxima."""
+    return int(lib().mo_argmax_last(np.ascontiguousarray(x, np.float32).reshape(-1), np.size(x)))
+
+
+class LayerOracle:
+    """One decoder layer run token by token as forward_token does
+    (native_cpu_adapter.rs:486-577), with its hot-dense K/V cache.
+
+    `weights` maps the HF-style names input_norm, wq, wk, wv, wo, post_norm,
+    wg, wu, wd to bf16-bit arrays ([out][in] for matrices)."""
+
+    def __init__(self, weights: dict, hidden: int, intermediate: int, query_heads: int, kv_heads: int,
+                 head_dim: int, eps: float, theta: float, capacity: int, threads: int = 0):
+        self.w = {k: np.ascontiguousarray(v, np.uint16) for k, v in weights.items()}
+        self.c = LayerWeightsC(**{k: v.ctypes.data for k, v in self.w.items()})
+        self.dims = (hidden, intermediate, query_heads, kv_heads, head_dim)
+        self.eps, self.theta = float(eps), float(theta)
+        self.k_cache = np.zeros((capacity, kv_heads, head_dim), np.uint16)
+        self.v_cache = np.zeros_like(self.k_cache)
+        self.position = 0
+        self.threads = threads or max_threads()
+
+    def forward(self, state: np.ndarray):
+        """Runs the token whose layer input is `state` (f32, bf16 values) at the
+        next position; returns (new state, post-RoPE q, post-RoPE k, attention)."""
+        hidden, inter, qh, kvh, d = self.dims
+        if self.position >= self.k_cache.shape[0]:
+            raise ValueError("K/V cache capacity exceeded")
+        st = np.array(state, np.float32, copy=True).reshape(-1)
+        if st.size != hidden:
+            raise ValueError(f"state has {st.size} values, the layer takes {hidden}")
+        q = np.empty(qh * d, np.float32)
+        k = np.empty(kvh * d, np.float32)
+        att = np.empty(qh * d, np.float32)
+        rc = lib().mo_layer_forward_token(ctypes.byref(self.c), hidden, inter, qh, kvh, d, self.eps,
+                                          self.theta, self.position, self.k_cache, self.v_cache, st,
+                                          q.ctypes.data, k.ctypes.data, att.ctypes.data, self.threads)
+        if rc != OK:
+            raise ValueError(f"layer oracle error {rc}")
+        self.position += 1
+        return st, q, k, att
+
+
+def lm_head_argmax(state: np.ndarray, final_norm: np.ndarray, lm_head: np.ndarray, eps: float,
+                   threads: int = 0):
+    """native_cpu_adapter.rs:579-587: final norm, lm_head, greedy token; returns (token, logits)."""
+    lm = np.ascontiguousarray(lm_head, np.uint16)
+    vocab, hidden = lm.shape
+    logits = np.empty(vocab, np.float32)
+    tok = lib().mo_lm_head_argmax(np.ascontiguousarray(state, np.float32),
+                                  np.ascontiguousarray(final_norm, np.uint16), lm, hidden, vocab,
+                                  float(eps), logits.ctypes.data, threads or max_threads())
+    return int(tok), logits

@@ -1,0 +1,181 @@
+"""C3: one Llama-3-8B-shaped decoder layer on the
+device, 512-token prefill then 8 forced decode steps, against the CPU
+restatement of forward_token (oracle/mslim_oracle.c, native_cpu_adapter.rs:
+486-577), plus the elementwise layer kernels (residual add, SwiGLU, argmax).
+
+Gates (north star / SURVEY C3): dense KV == ColdStore-exact KV bitwise on the
+device path; attention outputs within max-abs 2e-2 of the CPU path."""
+import numpy as np
+import pytest
+
+from gpu_util import bf16_f32, bf16_ulps, dev, host_u16
+
+
+def u16(t):
+    """bf16 (or int16) device tensor -> numpy bf16 bits."""
+    import torch
+    return host_u16(t.contiguous().view(torch.int16))
+
+
+pytestmark = pytest.mark.gpu
+
+SEED = 2
+PREFILL, DECODE = 512, 8
+VOCAB = 128256
+TOL = 2e-2
+
+
+@pytest.fixture(scope="module")
+def c3(oracle):
+    import torch
+    from mslim_b200 import layer
+    spec = layer.LayerSpec()
+    weights = layer.random_layer_weights(spec, SEED)
+    ids = np.random.default_rng(SEED).integers(0, VOCAB, size=PREFILL + DECODE)
+    emb = layer.embedding_rows(ids, spec.hidden, SEED)
+    x_dev = dev(emb).view(torch.bfloat16)
+    cap = PREFILL + DECODE
+    runs = {}
+    for mode in ("dense", "coldstore"):
+        L = layer.DeviceLayer(spec, weights, cap, kv_mode=mode, page_tokens=256, page_seed=SEED)
+        out, q_r, k_r, v, attn = L.prefill(x_dev[:PREFILL])
+        steps = [L.decode(x_dev[PREFILL + i:PREFILL + i + 1]) for i in range(DECODE)]
+        torch.cuda.synchronize()
+        runs[mode] = {
+            "prefill": [u16(t) for t in (out, q_r, k_r, v, attn)],
+            "decode": [[u16(t) for t in s] for s in steps],
+        }
+        if mode == "dense":
+            runs[mode]["k_cache"] = u16(L.k_cache)
+            runs[mode]["v_cache"] = u16(L.v_cache)
+        del L
+    # the CPU path, token by token (forward_token over one layer)
+    lo = oracle.LayerOracle(weights, spec.hidden, spec.intermediate, spec.query_heads, spec.kv_heads,
+                            spec.head_dim, spec.eps, spec.theta, cap)
+    xf = oracle.bf16_to_f32(emb).reshape(emb.shape)
+    cpu = [lo.forward(xf[t]) for t in range(cap)]
+    return {"spec": spec, "runs": runs, "cpu": cpu}
+
+
+def test_c3_dense_and_coldstore_are_bit_exact(c3):
+    d, c = c3["runs"]["dense"], c3["runs"]["coldstore"]
+    for a, b in zip(d["prefill"], c["prefill"]):
+        assert np.array_equal(a, b)
+    for sd, sc in zip(d["decode"], c["decode"]):
+        for a, b in zip(sd, sc):
+            assert np.array_equal(a, b), "decode step differs between dense and ColdStore KV"
+
+
+def test_c3_attention_matches_cpu_on_the_device_inputs(c3, oracle):
+    """The device attention against the CPU hot-dense attention fed the very
+    same post-RoPE q and K/V (isolates the attention kernels)."""
+    spec = c3["spec"]
+    d = c3["runs"]["dense"]
+    _, q_r, k_r, v, attn = d["prefill"]
+    qh, kvh, hd = spec.query_heads, spec.kv_heads, spec.head_dim
+    ref = oracle.causal_prefill_bf16(qh, kvh, hd, q_r.reshape(PREFILL, qh, hd), k_r.reshape(PREFILL, kvh, hd),
+                                     v.reshape(PREFILL, kvh, hd), PREFILL, 0)
+    err = np.abs(bf16_f32(attn).reshape(ref.shape) - bf16_f32(ref)).max()
+    print(f"C3 prefill attention vs CPU on device inputs: max-abs {err:.3g}")
+    assert err <= TOL, f"prefill attention max-abs {err}"
+    for i, (_, q_step, a_step) in enumerate(d["decode"]):
+        T = PREFILL + i + 1
+        ref = oracle.dense_attention_bf16(qh, kvh, hd, bf16_f32(q_step).reshape(-1),
+                                          d["k_cache"][:T], d["v_cache"][:T])
+        err = np.abs(bf16_f32(a_step).reshape(-1) - ref).max()
+        print(f"C3 decode step {i} attention vs CPU on device inputs: max-abs {err:.3g}")
+        assert err <= TOL, f"decode step {i} attention max-abs {err}"
+
+
+def test_c3_layer_matches_cpu_path(c3):
+    """End to end: every token's attention output of the device layer against
+    the CPU decoder's own (its own projections, RoPE and caches)."""
+    d = c3["runs"]["dense"]
+    cpu = c3["cpu"]
+    attn_dev = np.concatenate([bf16_f32(d["prefill"][4]).reshape(PREFILL, -1)] +
+                              [bf16_f32(s[2]).reshape(1, -1) for s in d["decode"]])
+    attn_cpu = np.stack([c[3] for c in cpu])
+    err = np.abs(attn_dev - attn_cpu).max()
+    print(f"C3 attention outputs vs the CPU path (all 520 tokens): max-abs {err:.3g}")
+    assert err <= TOL, f"attention outputs max-abs {err} against the CPU path"
+    state_dev = np.concatenate([bf16_f32(d["prefill"][0]).reshape(PREFILL, -1)] +
+                               [bf16_f32(s[0]).reshape(1, -1) for s in d["decode"]])
+    state_cpu = np.stack([c[0] for c in cpu])
+    # layer outputs: GEMM vs sequential sums differ in rounding only
+    rel = np.abs(state_dev - state_cpu).max() / np.abs(state_cpu).max()
+    print(f"C3 layer outputs vs the CPU path: max-abs {np.abs(state_dev - state_cpu).max():.3g}, "
+          f"relative to the largest output {rel:.3g}")
+    assert rel < 2e-2, f"layer output relative max-abs {rel}"
+
+
+# ------------------------------------------------------ elementwise ops --
+
+def _rand_bf16(rng, n, scale=1.0):
+    from mslim_b200 import workloads
+    return workloads.bf16_bits(rng.standard_normal(n).astype(np.float32) * np.float32(scale))
+
+
+@pytest.mark.parametrize("n", [1, 7, 8, 4096, 14336 * 3 + 5])
+def test_residual_add_bitwise(n, oracle):
+    import torch
+    import mslim_b200 as m
+    rng = np.random.default_rng(n)
+    a, b = _rand_bf16(rng, n), _rand_bf16(rng, n)
+    ta, tb = dev(a), dev(b)
+    out = torch.empty_like(ta)
+    m.residual_add(ta, tb, out, n)
+    ref = oracle.bf16_from_f32(oracle.add_residual(oracle.bf16_to_f32(a), oracle.bf16_to_f32(b)))
+    assert np.array_equal(u16(out), ref)
+
+
+@pytest.mark.parametrize("n", [1, 9, 14336, 14336 * 8 + 3])
+def test_swiglu_matches_cpu(n, oracle):
+    import torch
+    import mslim_b200 as m
+    rng = np.random.default_rng(n + 1)
+    g, u = _rand_bf16(rng, n, 3.0), _rand_bf16(rng, n)
+    tg, tu = dev(g), dev(u)
+    out = torch.empty_like(tg)
+    m.swiglu(tg, tu, out, n)
+    ref = oracle.bf16_from_f32(oracle.swiglu(oracle.bf16_to_f32(g), oracle.bf16_to_f32(u)))
+    got = u16(out)
+    # expf differs from glibc's in the last f32 bit at most; after the two bf16
+    # roundings almost every output is identical and none is more than 1 ulp off
+    ulps = bf16_ulps(got, ref)
+    assert ulps.max() <= 1
+    assert (ulps == 0).mean() > 0.999
+
+
+def _argmax_case(oracle, logits_u16, ties_to_last):
+    import torch
+    import mslim_b200 as m
+    rows, vocab = logits_u16.shape
+    t = dev(np.ascontiguousarray(logits_u16))
+    ids = torch.full((rows,), -7, dtype=torch.int32, device="cuda:0")
+    m.argmax(t, rows, vocab, ids, ties_to_last=ties_to_last)
+    return ids.cpu().numpy()
+
+
+def test_argmax_last_matches_cpu_max_by(oracle):
+    rng = np.random.default_rng(5)
+    rows = _rand_bf16(rng, 8 * VOCAB, 1.3).reshape(8, VOCAB)
+    got = _argmax_case(oracle, rows, True)
+    want = [oracle.argmax_last(oracle.bf16_to_f32(r)) for r in rows]
+    assert list(got) == want
+
+
+def test_argmax_tie_rules(oracle):
+    one, zero, nzero = 0x3F80, 0x0000, 0x8000
+    nan = 0x7FC0
+    cases = np.array([
+        [0xBF80, one, 0x4000, one, 0x4000, 0xC000],    # 2.0 at 2 and 4
+        [one] * 6,                                      # all equal
+        [nzero, zero, nzero, zero, nzero, nzero],       # -0 vs +0
+        [one, nan, 0x4000, one, 0x3F00, nan],           # NaN present
+    ], np.uint16)
+    last = _argmax_case(oracle, cases, True)
+    first = _argmax_case(oracle, cases, False)
+    # CPU path: f32::total_cmp, last of equal maxima (NaN is the largest)
+    assert list(last) == [oracle.argmax_last(oracle.bf16_to_f32(r)) for r in cases] == [4, 5, 3, 5]
+    # OpenCL llm_argmax: float order, first of equal maxima, NaN never chosen
+    assert list(first) == [2, 0, 0, 2]

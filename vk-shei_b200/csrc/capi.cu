@@ -22,6 +22,7 @@
 #include "../../include/mslim_cuda.h"
 #include "decode.cuh"
 #include "prefill.cuh"
+#include "layer_ops.cuh"
 #include "prologue.cuh"
 
 // One status word per device; kernels record bounded-wait timeouts here.
@@ -718,6 +719,49 @@ int mslim_cuda_prefill_causal(const mslim_geometry_t *geometry, const void *q, c
     cudaError_t err = mslim::launch_prefill(qmap, kmap, vmap, omap, p, static_cast<cudaStream_t>(stream));
     if (err != cudaSuccess) return cuda_fail(err, "prefill launch");
     return MSLIM_OK;
+}
+
+// -------------------------------------------------- layer elementwise --
+
+int mslim_cuda_residual_add(const void *a, const void *b, void *out, uint64_t n, void *stream) {
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    if (!a || !b || !out) return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
+    if (n == 0) return MSLIM_OK;
+    if (!aligned(a, 16) || !aligned(b, 16) || !aligned(out, 16))
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "residual buffers must be 16-byte aligned");
+    cudaError_t err = mslim::launch_residual_add(static_cast<const uint16_t *>(a),
+                                                 static_cast<const uint16_t *>(b),
+                                                 static_cast<uint16_t *>(out), n,
+                                                 static_cast<cudaStream_t>(stream));
+    return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "residual add launch");
+}
+
+int mslim_cuda_swiglu(const void *gate, const void *up, void *out, uint64_t n, void *stream) {
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    if (!gate || !up || !out) return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
+    if (n == 0) return MSLIM_OK;
+    if (!aligned(gate, 16) || !aligned(up, 16) || !aligned(out, 16))
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "SwiGLU buffers must be 16-byte aligned");
+    cudaError_t err = mslim::launch_swiglu(static_cast<const uint16_t *>(gate),
+                                           static_cast<const uint16_t *>(up),
+                                           static_cast<uint16_t *>(out), n,
+                                           static_cast<cudaStream_t>(stream));
+    return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "SwiGLU launch");
+}
+
+int mslim_cuda_argmax(const void *logits, uint32_t rows, uint32_t vocab, int ties_to_last,
+                      int32_t *token_ids, void *stream) {
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    if (!logits || !token_ids) return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
+    if (rows == 0) return MSLIM_OK;
+    if (vocab == 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty vocabulary");
+    if (vocab > 0x7fffffffu || rows > 0x7fffffffu) return fail(MSLIM_ERR_SHAPE_MISMATCH, "argmax too large");
+    cudaError_t err = mslim::launch_argmax(static_cast<const uint16_t *>(logits), rows, vocab,
+                                           ties_to_last, token_ids, static_cast<cudaStream_t>(stream));
+    return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "argmax launch");
 }
 
 // ---------------------------------------------------------- prologue --

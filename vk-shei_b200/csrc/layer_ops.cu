@@ -1,0 +1,171 @@
+// layer_ops.cu -- elementwise decoder-layer kernels around attention.
+//
+//   mslim_residual_add   out = bf16(a + b)                 native_cpu_adapter.rs:186-191,
+//                                                          gpu_llm.cl llm_add
+//   mslim_swiglu         out = bf16(bf16(g / (1 + exp(-g))) * u)
+//                                                          native_cpu_adapter.rs:553-560,
+//                                                          gpu_llm.cl llm_swiglu
+//   mslim_argmax         greedy token per row of logits    native_cpu_adapter.rs:582-587,
+//                                                          gpu_llm.cl llm_argmax
+//
+// All three are HBM-bound streams: 16-byte vector loads, grids of a few waves
+// of 148 SMs, grid-stride loops.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <climits>
+#include <cstdint>
+
+#include "layer_ops.cuh"
+
+namespace mslim {
+
+namespace {
+
+constexpr int kEltThreads = 256;
+
+__device__ __forceinline__ uint32_t add_pair(uint32_t a, uint32_t b) {
+    return pack_bf16x2(bf16lo_f32(a) + bf16lo_f32(b), bf16hi_f32(a) + bf16hi_f32(b));
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u) {
+    const float activated = bf16_round(g / (1.0f + expf(-g)));
+    return activated * u;
+}
+
+__device__ __forceinline__ uint32_t swiglu_pair(uint32_t g, uint32_t u) {
+    return pack_bf16x2(silu_mul(bf16lo_f32(g), bf16lo_f32(u)), silu_mul(bf16hi_f32(g), bf16hi_f32(u)));
+}
+
+// n8 = number of whole 8-element vectors; the tail (< 8) is done by thread 0.
+__global__ void __launch_bounds__(kEltThreads)
+    mslim_residual_add(const uint16_t *__restrict__ a, const uint16_t *__restrict__ b,
+                       uint16_t *__restrict__ out, uint64_t n) {
+    const uint64_t n8 = n / 8;
+    const uint4 *a4 = reinterpret_cast<const uint4 *>(a);
+    const uint4 *b4 = reinterpret_cast<const uint4 *>(b);
+    uint4 *o4 = reinterpret_cast<uint4 *>(out);
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n8;
+         i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint4 x = a4[i], y = b4[i];
+        o4[i] = make_uint4(add_pair(x.x, y.x), add_pair(x.y, y.y), add_pair(x.z, y.z), add_pair(x.w, y.w));
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0)
+        for (uint64_t i = n8 * 8; i < n; ++i)
+            out[i] = bf16_bits_rn(bf16_bits_to_f32(a[i]) + bf16_bits_to_f32(b[i]));
+}
+
+__global__ void __launch_bounds__(kEltThreads)
+    mslim_swiglu(const uint16_t *__restrict__ gate, const uint16_t *__restrict__ up,
+                 uint16_t *__restrict__ out, uint64_t n) {
+    const uint64_t n8 = n / 8;
+    const uint4 *g4 = reinterpret_cast<const uint4 *>(gate);
+    const uint4 *u4 = reinterpret_cast<const uint4 *>(up);
+    uint4 *o4 = reinterpret_cast<uint4 *>(out);
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n8;
+         i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint4 g = g4[i], u = u4[i];
+        o4[i] = make_uint4(swiglu_pair(g.x, u.x), swiglu_pair(g.y, u.y), swiglu_pair(g.z, u.z),
+                           swiglu_pair(g.w, u.w));
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0)
+        for (uint64_t i = n8 * 8; i < n; ++i)
+            out[i] = bf16_bits_rn(silu_mul(bf16_bits_to_f32(gate[i]), bf16_bits_to_f32(up[i])));
+}
+
+// ---------------------------------------------------------------- argmax --
+
+constexpr int kArgThreads = 1024;
+
+// Order key of a bf16 value.  total_cmp: signed-magnitude order of the bits
+// (f32::total_cmp on the widened value orders identically).  Float order:
+// NaN ranks below everything, -0 == +0.
+__device__ __forceinline__ int32_t order_key(uint16_t b, bool total) {
+    if (total) {
+        const int32_t s = (int32_t)(int16_t)b;
+        return s ^ (int32_t)((uint32_t)(s >> 31) >> 17);
+    }
+    const uint32_t mag = b & 0x7fffu;
+    if (mag > 0x7f80u) return INT_MIN;        // NaN
+    if (mag == 0) return 0;                   // +-0 compare equal
+    return (b & 0x8000u) ? -(int32_t)mag : (int32_t)mag;
+}
+
+// (key, index) is better than (k2, i2)
+__device__ __forceinline__ bool better(int32_t k, int32_t i, int32_t k2, int32_t i2, bool last) {
+    return k > k2 || (k == k2 && (last ? i > i2 : i < i2));
+}
+
+// One CTA per row.
+__global__ void __launch_bounds__(kArgThreads)
+    mslim_argmax(const uint16_t *__restrict__ logits, uint32_t n, int ties_to_last,
+                 int32_t *__restrict__ out) {
+    const bool last = ties_to_last != 0;
+    const uint16_t *row = logits + (uint64_t)blockIdx.x * n;
+    int32_t best_k = INT_MIN, best_i = -1;
+    for (uint32_t i = threadIdx.x; i < n; i += kArgThreads) {
+        const int32_t k = order_key(row[i], last);
+        if (best_i < 0 || better(k, (int32_t)i, best_k, best_i, last)) {
+            best_k = k;
+            best_i = (int32_t)i;
+        }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const int32_t k2 = __shfl_xor_sync(0xffffffffu, best_k, off);
+        const int32_t i2 = __shfl_xor_sync(0xffffffffu, best_i, off);
+        if (i2 >= 0 && (best_i < 0 || better(k2, i2, best_k, best_i, last))) {
+            best_k = k2;
+            best_i = i2;
+        }
+    }
+    __shared__ int32_t sk[kArgThreads / 32], si[kArgThreads / 32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        sk[warp] = best_k;
+        si[warp] = best_i;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        best_k = sk[lane];
+        best_i = si[lane];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const int32_t k2 = __shfl_xor_sync(0xffffffffu, best_k, off);
+            const int32_t i2 = __shfl_xor_sync(0xffffffffu, best_i, off);
+            if (i2 >= 0 && (best_i < 0 || better(k2, i2, best_k, best_i, last))) {
+                best_k = k2;
+                best_i = i2;
+            }
+        }
+        if (lane == 0) out[blockIdx.x] = best_i;
+    }
+}
+
+unsigned elt_grid(uint64_t n) {
+    const uint64_t vec = (n / 8 + kEltThreads - 1) / kEltThreads;
+    const uint64_t cap = 148ull * 8;  // a few waves; the loop strides the rest
+    return (unsigned)(vec == 0 ? 1 : (vec < cap ? vec : cap));
+}
+
+}  // namespace
+
+cudaError_t launch_residual_add(const uint16_t *a, const uint16_t *b, uint16_t *out, uint64_t n,
+                                cudaStream_t stream) {
+    mslim_residual_add<<<elt_grid(n), kEltThreads, 0, stream>>>(a, b, out, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_swiglu(const uint16_t *gate, const uint16_t *up, uint16_t *out, uint64_t n,
+                          cudaStream_t stream) {
+    mslim_swiglu<<<elt_grid(n), kEltThreads, 0, stream>>>(gate, up, out, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_argmax(const uint16_t *logits, uint32_t rows, uint32_t n, int ties_to_last,
+                          int32_t *out, cudaStream_t stream) {
+    mslim_argmax<<<rows, kArgThreads, 0, stream>>>(logits, n, ties_to_last, out);
+    return cudaGetLastError();
+}
+
+}  // namespace mslim

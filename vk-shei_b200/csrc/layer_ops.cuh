@@ -1,0 +1,20 @@
+// layer_ops.cuh -- launchers of the decoder-layer elementwise kernels around
+// attention: residual add, SwiGLU, and the greedy argmax over logits.
+#pragma once
+
+#include "mslim_common.cuh"
+
+namespace mslim {
+
+cudaError_t launch_residual_add(const uint16_t *a, const uint16_t *b, uint16_t *out, uint64_t n,
+                                cudaStream_t stream);
+cudaError_t launch_swiglu(const uint16_t *gate, const uint16_t *up, uint16_t *out, uint64_t n,
+                          cudaStream_t stream);
+// rows x n bf16 logits -> int32 index per row.  ties_to_last != 0: the largest
+// value under f32::total_cmp, last index among equals (the CPU path's
+// Iterator::max_by); 0: the largest by float comparison, first index among
+// equals, NaN never chosen unless every entry is NaN (the OpenCL llm_argmax).
+cudaError_t launch_argmax(const uint16_t *logits, uint32_t rows, uint32_t n, int ties_to_last,
+                          int32_t *out, cudaStream_t stream);
+
+}  // namespace mslim

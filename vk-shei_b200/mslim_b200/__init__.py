@@ -10,7 +10,7 @@ from .attention import (AttentionGeometry, AttentionKernelConfig, AttentionKerne
                         InvalidGeometry, NonFinite, PortableError, RopeKernelConfig, ShapeMismatch,
                         TiledAttention, UnsupportedDevice, check, decode_dense, decode_paged, decode_paged_static_scratch,
                         decode_workspace_bytes, device_status, prefill_causal, rmsnorm, rope,
-                        rope_append_decode_paged, rope_append_paged)
+                        rope_append_decode_paged, rope_append_paged, residual_add, swiglu, argmax)
 
 LIB_PATH = _lib.LIB_PATH
 

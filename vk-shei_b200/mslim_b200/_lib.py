@@ -72,6 +72,9 @@ SIGNATURES = {
     "mslim_cuda_decode_paged_static_scratch": (_int, [_G, _vp, _vp, _vp, _u32, _u32, _vp, _u32, _vp, _u32,
                                                       _u32, _vp, _vp]),
     "mslim_cuda_prefill_causal": (_int, [_G, _vp, _vp, _vp, _vp, _u32, _u32, _vp]),
+    "mslim_cuda_residual_add": (_int, [_vp, _vp, _vp, ctypes.c_uint64, _vp]),
+    "mslim_cuda_swiglu": (_int, [_vp, _vp, _vp, ctypes.c_uint64, _vp]),
+    "mslim_cuda_argmax": (_int, [_vp, _u32, _u32, _int, _vp, _vp]),
     "mslim_cuda_rmsnorm": (_int, [_vp, _vp, _vp, _u32, _u32, ctypes.c_float, _vp]),
     "mslim_cuda_rope": (_int, [_vp, _vp, _u32, _u32, _u32, _u32, _R, _vp]),
     "mslim_cuda_rope_append_paged": (_int, [_G, _vp, _vp, _vp, _vp, _u32, _u32, _R, _vp, _vp, _u32, _u32,

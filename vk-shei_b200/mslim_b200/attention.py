@@ -294,6 +294,23 @@ def prefill_causal(geometry: AttentionGeometry, q, k, v, out, queries: int, prio
                                                _ptr(out), queries, prior, _stream(stream)))
 
 
+def residual_add(a, b, out, n: int, stream=None) -> None:
+    """GpuEngine::add (src/gpu_llm/gpu_resources.rs:539-559): out = bf16(a + b)."""
+    check(_lib.lib().mslim_cuda_residual_add(_ptr(a), _ptr(b), _ptr(out), n, _stream(stream)))
+
+
+def swiglu(gate, up, out, n: int, stream=None) -> None:
+    """GpuEngine::swiglu (src/gpu_llm/gpu_resources.rs:561-581)."""
+    check(_lib.lib().mslim_cuda_swiglu(_ptr(gate), _ptr(up), _ptr(out), n, _stream(stream)))
+
+
+def argmax(logits, rows: int, vocab: int, token_ids, ties_to_last: bool = True, stream=None) -> None:
+    """GpuEngine::argmax (src/gpu_llm/gpu_resources.rs:1065) / the CPU greedy
+    step (src/native_cpu_adapter.rs:582-587): int32 token id per row."""
+    check(_lib.lib().mslim_cuda_argmax(_ptr(logits), rows, vocab, int(bool(ties_to_last)), _ptr(token_ids),
+                                       _stream(stream)))
+
+
 def rmsnorm(x, w, y, tokens: int, hidden: int, eps: float, stream=None) -> None:
     check(_lib.lib().mslim_cuda_rmsnorm(_ptr(x), _ptr(w), _ptr(y), tokens, hidden, eps, _stream(stream)))
 
