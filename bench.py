@@ -54,6 +54,15 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-prefill", action="store_true", help="skip the C2 prefill leg")
     ap.add_argument("--prefill-only", action="store_true", help="run only the C2 prefill leg (profiling)")
+    ap.add_argument("--model", action="store_true",
+                    help="C5: the 32-layer decoder, tensor-parallel over the torchrun ranks")
+    ap.add_argument("--model-layers", type=int, default=32)
+    ap.add_argument("--model-batch", type=int, default=8)
+    ap.add_argument("--model-prefill", type=int, default=8192)
+    ap.add_argument("--model-steps", type=int, default=256)
+    ap.add_argument("--mlp", choices=["sharded", "replicated"], default="sharded")
+    ap.add_argument("--kv-mode", choices=["dense", "coldstore"], default="dense")
+    ap.add_argument("--no-graph", action="store_true", help="C5 decode steps issued eagerly (no CUDA graph)")
     return ap.parse_args()
 
 
@@ -320,6 +329,115 @@ def bench_prefill(m, torch, device, args) -> dict:
             "gpu_launches": steps, "clocks": clocks}
 
 
+def bench_model(m, torch, device, args, rank, world, dist) -> dict | None:
+    """C5: a Llama-3-8B-shaped decoder with random
+    weights, batch 8, 8192-token prefill then 256 greedy decode steps,
+    tensor-parallel over the WORLD_SIZE ranks by KV-head group (NCCL
+    all-reduce of the row-parallel o-projection, and of the MLP down
+    projection when the MLP is sharded).  Strong scaling: the model and the
+    batch are fixed, the ranks split them.  Device time by CUDA events,
+    barrier + synchronize around each timed region, max over ranks."""
+    import hashlib
+
+    import numpy as np
+    from mslim_b200 import model as mdl
+
+    B, S, steps = args.model_batch, args.model_prefill, args.model_steps
+    spec = mdl.ModelSpec(layers=args.model_layers)
+    L = spec.layer
+    t0 = time.time()
+    M = mdl.DeviceModel(spec, B, S + steps + 4, seed=5, tp_rank=rank, tp_world=world, mlp=args.mlp,
+                        kv_mode=args.kv_mode)
+    build_s = time.time() - t0
+    ids = torch.from_numpy(np.random.default_rng(5).integers(0, spec.vocab, size=(B, S))).to(device)
+
+    def sync():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        v = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(v, op=dist.ReduceOp.MAX)
+        return float(v.item())
+
+    # warm-up: a short prompt and a few steps through the same kernels
+    tok, _ = M.prefill(ids[:, :min(S, 256)])
+    for _ in range(max(args.warmup, 3)):
+        tok, _ = M.decode_step(tok)
+    graphed = not args.no_graph
+    if graphed:
+        M.capture_decode()
+        for _ in range(2):
+            tok, _ = M.decode_step_graphed(tok)
+    sync()
+    sampler = ClockSampler(torch.cuda.current_device())
+    sampler.start()
+    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    e0.record()
+    tok, _ = M.prefill(ids)
+    e1.record()
+    out = [tok.clone()]
+    step = M.decode_step_graphed if graphed else M.decode_step
+    for _ in range(steps):
+        tok, _ = step(tok)
+        out.append(tok.clone())
+    e2.record()
+    sync()
+    clocks = sampler.stop()
+    prefill_ms = max_over_ranks(e0.elapsed_time(e1))
+    decode_ms = max_over_ranks(e1.elapsed_time(e2))
+    tokens = torch.stack(out, 1).cpu().numpy().astype(np.int32)   # [B][steps + 1]
+    # one more decode step and a one-layer-deep look at the prefill, split by kind
+    M.profile = mdl.SectionTimer(torch)
+    M.decode_step(tok)
+    sync()
+    step_split = M.profile.totals_ms()
+    M.profile = None
+    if graphed:
+        M.release_graph()
+    if m.device_status(torch.cuda.current_device()) != 0:
+        raise SystemExit("device status reported an error during the model leg")
+    if rank != 0:
+        return None
+    peaks = measured_peaks()
+    kvh, qh = L.kv_heads // world, L.query_heads // world
+    inter = L.intermediate if args.mlp == "replicated" else L.intermediate // world
+    params_layer = L.hidden * (qh + 2 * kvh) * L.head_dim + L.hidden * qh * L.head_dim + 3 * L.hidden * inter
+    ctx = S + steps / 2.0
+    return {
+        "metric": "C5 decode tokens/s (32-layer Llama-3-8B-shaped decoder, batch 8, prefill 8192, 256 greedy "
+                  "steps, KV-head tensor parallel)",
+        "value": B * steps / (decode_ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+        "higher_is_better": True, "scaling": "strong", "dtype": "bf16",
+        "data": "synthetic (random-init weights: projections and tied embedding N(0,0.02), norms 1; "
+                "prompt ids uniform [0,128256), seed 5)",
+        "config": {"workload": "C5", "layers": spec.layers, "batch": B, "prefill": S, "decode_steps": steps,
+                   "parallelism": f"tp{world} by KV-head group, MLP {args.mlp}", "kv": args.kv_mode,
+                   "allreduce_per_layer": 1 if args.mlp == "replicated" else 2,
+                   "decode_issue": "one CUDA graph per step" if graphed else "eager"},
+        "prefill_ms": prefill_ms, "prefill_tokens_per_s": B * S / (prefill_ms * 1e-3),
+        "decode_ms_per_step": decode_ms / steps,
+        "decode_step_split_ms": step_split,
+        "decode_step_split_note": "one extra step issued eagerly with CUDA events around every op "
+                                  "(includes launch gaps); the timed steps replay a graph",
+        "per_rank_roofline": {
+            "decode_weight_bytes_per_step": 2 * (params_layer * spec.layers + spec.vocab * L.hidden),
+            "decode_weight_gbs": 2 * (params_layer * spec.layers + spec.vocab * L.hidden)
+            / (step_split.get("gemm", 0.0) * 1e-3) / 1e9 if step_split.get("gemm") else None,
+            "decode_attention_bytes_per_step": int(B * ctx * kvh * L.head_dim * 4 * spec.layers),
+            "decode_attention_gbs": B * ctx * kvh * L.head_dim * 4 * spec.layers
+            / (step_split.get("attention", 0.0) * 1e-3) / 1e9 if step_split.get("attention") else None,
+            "hbm_peak_gbs": peaks["hbm_gbs"],
+        },
+        "tokens_sha256": hashlib.sha256(tokens.tobytes()).hexdigest(),
+        "first_tokens": tokens[:, :8].tolist(),
+        "model_build_s": build_s, "clocks": clocks,
+    }
+
+
 # --------------------------------------------------------------- GPU leg --
 
 def main():
@@ -344,6 +462,14 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device(device))
     m.load()
+    if args.model:
+        line = bench_model(m, torch, device, args, rank, world, dist)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if args.prefill_only:
         print(json.dumps({"prefill": bench_prefill(m, torch, device, args)}), flush=True)
         return

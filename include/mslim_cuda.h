@@ -224,6 +224,12 @@ int mslim_cuda_residual_add(const void *a, const void *b, void *out, uint64_t n,
  * out = bf16(bf16(g / (1 + exp(-g))) * u); out may alias gate or up. */
 int mslim_cuda_swiglu(const void *gate, const void *up, void *out, uint64_t n, void *stream);
 
+/* SwiGLU over a fused gate|up projection (no reference counterpart: the
+ * reference keeps gate and up in separate buffers, GpuEngine::swiglu):
+ * gate_up bf16 [rows][gate (width) | up (width)], out bf16 [rows][width],
+ * out = bf16(bf16(g / (1 + exp(-g))) * u); width a multiple of 8. */
+int mslim_cuda_swiglu_rows(const void *gate_up, void *out, uint32_t rows, uint32_t width, void *stream);
+
 /* GpuEngine::argmax (src/gpu_llm/gpu_resources.rs:1065, kernel llm_argmax) and
  * the CPU greedy step (src/native_cpu_adapter.rs:582-587): one int32 token id
  * per row of `rows` x `vocab` bf16 logits (device pointers).
@@ -240,6 +246,13 @@ int mslim_cuda_argmax(const void *logits, uint32_t rows, uint32_t vocab, int tie
  * s = 1/sqrt(mean(x^2)+eps).  x/y: bf16 [tokens][hidden]; w: bf16 [hidden]. */
 int mslim_cuda_rmsnorm(const void *x, const void *w, void *y, uint32_t tokens, uint32_t hidden,
                        float eps, void *stream);
+
+/* The layer's residual add followed by the next RMSNorm in one pass (the pair
+ * GpuEngine::add + GpuEngine::norm of run_layer, src/gpu_llm/mod.rs:2118-2329):
+ * x = bf16(x + delta) in place, then y = RMSNorm(x, w) exactly as
+ * mslim_cuda_rmsnorm computes it.  y must not alias x or delta. */
+int mslim_cuda_residual_rmsnorm(void *x, const void *delta, const void *w, void *y, uint32_t tokens,
+                                uint32_t hidden, float eps, void *stream);
 
 /* GpuEngine::rope / BatchKernels::rope (src/gpu_llm/gpu_resources.rs:509-537,
  * src/gpu_llm/prefill.rs:322-361): rotate_half RoPE of bf16
@@ -275,6 +288,34 @@ int mslim_cuda_rope_append_decode_paged(const mslim_geometry_t *geometry, const 
                                         void *v_pool, uint32_t n_pages, uint32_t page_tokens,
                                         const int32_t *page_table, uint32_t max_pages,
                                         void *stream);
+
+/* The same decode step for the dense token-major caches of the GPU runtime
+ * (k_cache/v_cache: bf16 [n_seq][max_tokens][KVH][D]): rope(q), rope(k) and
+ * the K/V copies of run_layer (src/gpu_llm/mod.rs:2099-2116) for a batch of
+ * sessions, session s writing row positions[s].  Same RoPE arithmetic as every
+ * other form, so a dense and a paged store hold identical K bits.  A position
+ * outside [0, max_tokens) writes nothing and is reported by
+ * mslim_cuda_device_status. */
+int mslim_cuda_rope_append_decode_dense(const mslim_geometry_t *geometry, const void *q_in,
+                                        void *q_out, const void *k_in, const void *v_in,
+                                        const int32_t *positions, uint32_t n_seq,
+                                        const mslim_rope_config_t *rope, void *k_cache,
+                                        void *v_cache, uint32_t max_tokens, void *stream);
+
+/* The two decode-step appends reading q, k and v straight out of one fused
+ * projection output qkv: bf16 [n_seq][(QH + 2*KVH) * D] holding the q heads,
+ * then the k heads, then the v heads of each session's new token (the
+ * reference projects them into three buffers; the fused GEMM saves two
+ * launches and the copies).  Otherwise as the forms above. */
+int mslim_cuda_rope_append_decode_dense_qkv(const mslim_geometry_t *geometry, const void *qkv,
+                                            void *q_out, const int32_t *positions, uint32_t n_seq,
+                                            const mslim_rope_config_t *rope, void *k_cache,
+                                            void *v_cache, uint32_t max_tokens, void *stream);
+int mslim_cuda_rope_append_decode_paged_qkv(const mslim_geometry_t *geometry, const void *qkv,
+                                            void *q_out, const int32_t *positions, uint32_t n_seq,
+                                            const mslim_rope_config_t *rope, void *k_pool, void *v_pool,
+                                            uint32_t n_pages, uint32_t page_tokens,
+                                            const int32_t *page_table, uint32_t max_pages, void *stream);
 
 /* ------------------------------------------- isolated backend (L3) -- */
 

@@ -179,3 +179,74 @@ def test_argmax_tie_rules(oracle):
     assert list(last) == [oracle.argmax_last(oracle.bf16_to_f32(r)) for r in cases] == [4, 5, 3, 5]
     # OpenCL llm_argmax: float order, first of equal maxima, NaN never chosen
     assert list(first) == [2, 0, 0, 2]
+
+
+# ----------------------------------------------------- fused decode steps --
+
+def test_residual_rmsnorm_is_add_then_norm_bitwise():
+    import torch
+    import mslim_b200 as m
+    rng = np.random.default_rng(11)
+    for tokens, hidden in [(8, 4096), (3, 136), (1, 4000), (5, 12)]:
+        x, d = _rand_bf16(rng, tokens * hidden), _rand_bf16(rng, tokens * hidden, 0.5)
+        w = _rand_bf16(rng, hidden)
+        tx1, tx2, td, tw = dev(x), dev(x), dev(d), dev(w)
+        y1, y2 = torch.empty_like(tx1), torch.empty_like(tx1)
+        m.residual_add(tx1, td, tx1, tokens * hidden)
+        m.rmsnorm(tx1, tw, y1, tokens, hidden, 1e-5)
+        m.residual_rmsnorm(tx2, td, tw, y2, tokens, hidden, 1e-5)
+        assert np.array_equal(u16(tx1), u16(tx2)) and np.array_equal(u16(y1), u16(y2))
+
+
+def test_swiglu_rows_matches_split_buffers_bitwise():
+    import torch
+    import mslim_b200 as m
+    rng = np.random.default_rng(12)
+    rows, width = 8, 14336
+    gu = _rand_bf16(rng, rows * 2 * width, 3.0).reshape(rows, 2 * width)
+    out = torch.empty((rows, width), dtype=torch.int16, device="cuda:0")
+    m.swiglu_rows(dev(gu), out, rows, width)
+    ref = torch.empty_like(out)
+    g, u = dev(np.ascontiguousarray(gu[:, :width])), dev(np.ascontiguousarray(gu[:, width:]))
+    m.swiglu(g, u, ref, rows * width)
+    assert np.array_equal(u16(out), u16(ref))
+
+
+@pytest.mark.parametrize("paged", [False, True])
+def test_fused_qkv_append_matches_separate_inputs(paged):
+    import torch
+    import mslim_b200 as m
+    from mslim_b200 import attention as att
+    rng = np.random.default_rng(13)
+    QH, KVH, D, B, T = 32, 8, 128, 4, 600
+    g = att.AttentionGeometry.new(QH, KVH, D)
+    cfg = att.RopeKernelConfig(theta=500000.0)
+    qkv = _rand_bf16(rng, B * (QH + 2 * KVH) * D).reshape(B, -1)
+    q = np.ascontiguousarray(qkv[:, :QH * D])
+    k = np.ascontiguousarray(qkv[:, QH * D:(QH + KVH) * D])
+    v = np.ascontiguousarray(qkv[:, (QH + KVH) * D:])
+    pos = dev(np.array([0, 17, 255, 599], np.int32))
+    outs = []
+    for fused in (False, True):
+        q_out = torch.empty((B, QH * D), dtype=torch.int16, device="cuda:0")
+        if paged:
+            pt, mp = 256, 3
+            table = dev(np.random.default_rng(1).permutation(B * mp).astype(np.int32).reshape(B, mp))
+            kc = torch.zeros((B * mp, KVH, pt, D), dtype=torch.int16, device="cuda:0")
+            vc = torch.zeros_like(kc)
+            if fused:
+                m.rope_append_decode_paged_qkv(g, dev(qkv), q_out, pos, B, cfg, kc, vc, B * mp, pt, table, mp)
+            else:
+                m.rope_append_decode_paged(g, dev(q), q_out, dev(k), dev(v), pos, B, cfg, kc, vc, B * mp, pt,
+                                           table, mp)
+        else:
+            kc = torch.zeros((B, T, KVH, D), dtype=torch.int16, device="cuda:0")
+            vc = torch.zeros_like(kc)
+            if fused:
+                m.rope_append_decode_dense_qkv(g, dev(qkv), q_out, pos, B, cfg, kc, vc, T)
+            else:
+                m.rope_append_decode_dense(g, dev(q), q_out, dev(k), dev(v), pos, B, cfg, kc, vc, T)
+        outs.append([u16(q_out), u16(kc), u16(vc)])
+    for a, b in zip(*outs):
+        assert np.array_equal(a, b)
+    assert m.device_status(0) == 0

@@ -1,0 +1,91 @@
+"""C5 machinery on one GPU: the tensor-parallel decoder (mslim_b200.model) at
+TP 1, reduced to two full-size layers, against the CPU restatement of
+forward_token (native_cpu_adapter.rs:486-591) teacher-forced with the device's
+own greedy tokens, plus dense == ColdStore KV over the whole model.
+
+A full 32-layer CPU run is ~1 PFLOP and not feasible; the layer and the
+attention are pinned at full size by the C3 tests."""
+import numpy as np
+import pytest
+
+from gpu_util import bf16_f32, host_u16
+
+pytestmark = pytest.mark.gpu
+
+LAYERS, BATCH, PROMPT, STEPS = 2, 2, 32, 6
+
+
+def _u16(t):
+    import torch
+    return host_u16(t.contiguous().view(torch.int16))
+
+
+def _run(kv_mode):
+    import torch
+    from mslim_b200 import model as mdl
+    spec = mdl.ModelSpec(layers=LAYERS)
+    M = mdl.DeviceModel(spec, BATCH, PROMPT + STEPS + 1, seed=7, kv_mode=kv_mode)
+    ids = torch.from_numpy(np.random.default_rng(7).integers(0, spec.vocab, size=(BATCH, PROMPT))).cuda()
+    tok, logits = M.prefill(ids)
+    toks, lgs = [tok.cpu().numpy()], [_u16(logits)]
+    for _ in range(STEPS):
+        tok, logits = M.decode_step(tok)
+        toks.append(tok.cpu().numpy())
+        lgs.append(_u16(logits))
+    torch.cuda.synchronize()
+    return M, spec, ids.cpu().numpy(), np.stack(toks, 1), np.stack(lgs, 1)
+
+
+@pytest.fixture(scope="module")
+def runs():
+    dense = _run("dense")
+    cold = _run("coldstore")
+    return dense, cold
+
+
+def test_model_dense_and_coldstore_agree_bitwise(runs):
+    (_, _, _, t_d, l_d), (_, _, _, t_c, l_c) = runs
+    assert np.array_equal(t_d, t_c)
+    assert np.array_equal(l_d, l_c)
+
+
+def test_model_greedy_tokens_match_cpu_path(runs, oracle):
+    M, spec, prompts, toks, logits = runs[0]
+    L = spec.layer
+    D, qd, kd, inter = L.head_dim, L.q_dim, L.kv_dim, L.intermediate
+    layers = []
+    for W in M.layers:
+        wqkv, wgu = _u16(W["wqkv"]), _u16(W["wgu"])
+        layers.append({"input_norm": _u16(W["in_norm"]), "wq": wqkv[:qd], "wk": wqkv[qd:qd + kd],
+                       "wv": wqkv[qd + kd:], "wo": _u16(W["wo"]), "post_norm": _u16(W["post_norm"]),
+                       "wg": wgu[:inter], "wu": wgu[inter:], "wd": _u16(W["wd"])})
+    emb = _u16(M.embedding)
+    fnorm = _u16(M.final_norm)
+    exact = near = 0
+    worst = 0.0
+    for b in range(BATCH):
+        los = [oracle.LayerOracle(w, L.hidden, inter, L.query_heads, L.kv_heads, D, L.eps, L.theta,
+                                  PROMPT + STEPS + 1) for w in layers]
+        inputs = list(prompts[b]) + list(toks[b, :STEPS])   # teacher-forced with the device's tokens
+        for pos, tid in enumerate(inputs):
+            state = bf16_f32(emb[tid])
+            for lo in los:
+                state, *_ = lo.forward(state)
+            if pos < PROMPT - 1:
+                continue
+            k = pos - (PROMPT - 1)                          # generated step k
+            want, ref = oracle.lm_head_argmax(state, fnorm, emb, L.eps)
+            dev_logits = bf16_f32(logits[b, k])
+            worst = max(worst, float(np.abs(dev_logits - ref).max()))
+            got = int(toks[b, k])
+            if got == want:
+                exact += 1
+                continue
+            # a flip is allowed only between near-equal logits (2 bf16 ulps)
+            ulp = 2.0 ** (np.floor(np.log2(abs(ref[want]))) - 7)
+            assert ref[got] >= ref[want] - 2 * ulp, (b, k, got, want, ref[got], ref[want])
+            near += 1
+    print(f"model greedy tokens: {exact} exact, {near} near-tie flips of {BATCH * (STEPS + 1)}; "
+          f"logits max-abs vs CPU {worst:.3g}")
+    assert exact >= BATCH * (STEPS + 1) - 2
+    assert worst < 0.25

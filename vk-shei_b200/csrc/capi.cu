@@ -751,6 +751,20 @@ int mslim_cuda_swiglu(const void *gate, const void *up, void *out, uint64_t n, v
     return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "SwiGLU launch");
 }
 
+int mslim_cuda_swiglu_rows(const void *gate_up, void *out, uint32_t rows, uint32_t width, void *stream) {
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    if (!gate_up || !out) return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
+    if (rows == 0) return MSLIM_OK;
+    if (width == 0 || width % 8 != 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "SwiGLU width must be a positive multiple of 8");
+    if (!aligned(gate_up, 16) || !aligned(out, 16))
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "SwiGLU buffers must be 16-byte aligned");
+    cudaError_t err = mslim::launch_swiglu_rows(static_cast<const uint16_t *>(gate_up),
+                                                static_cast<uint16_t *>(out), rows, width,
+                                                static_cast<cudaStream_t>(stream));
+    return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "SwiGLU launch");
+}
+
 int mslim_cuda_argmax(const void *logits, uint32_t rows, uint32_t vocab, int ties_to_last,
                       int32_t *token_ids, void *stream) {
     int dev;
@@ -781,6 +795,23 @@ int mslim_cuda_rmsnorm(const void *x, const void *w, void *y, uint32_t tokens, u
                                             static_cast<uint16_t *>(y), tokens, hidden, eps,
                                             static_cast<cudaStream_t>(stream));
     return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "RMSNorm launch");
+}
+
+int mslim_cuda_residual_rmsnorm(void *x, const void *delta, const void *w, void *y, uint32_t tokens,
+                                uint32_t hidden, float eps, void *stream) {
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    if (!x || !delta || !w || !y) return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
+    if (tokens == 0 || hidden == 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty RMSNorm");
+    if (!std::isfinite(eps) || eps < 0.f) return fail(MSLIM_ERR_INVALID_CONFIG, "invalid epsilon");
+    if (hidden % 8 == 0 && (!aligned(x, 16) || !aligned(delta, 16) || !aligned(w, 16) || !aligned(y, 16)))
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "RMSNorm buffers must be 16-byte aligned");
+    if (y == x || y == delta) return fail(MSLIM_ERR_SHAPE_MISMATCH, "RMSNorm output must not alias its inputs");
+    if (tokens > 0x7fffffffu) return fail(MSLIM_ERR_SHAPE_MISMATCH, "too many tokens");
+    cudaError_t err = mslim::launch_residual_rmsnorm(static_cast<uint16_t *>(x), static_cast<const uint16_t *>(delta),
+                                                     static_cast<const uint16_t *>(w), static_cast<uint16_t *>(y),
+                                                     tokens, hidden, eps, static_cast<cudaStream_t>(stream));
+    return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "residual RMSNorm launch");
 }
 
 int mslim_cuda_rope(const void *in, void *out, uint32_t tokens, uint32_t heads, uint32_t head_dim,
@@ -848,6 +879,79 @@ int mslim_cuda_rope_append_decode_paged(const mslim_geometry_t *geometry, const 
         geometry->query_heads, geometry->kv_heads, geometry->head_dim, 0, positions,
         static_cast<uint16_t *>(k_pool), static_cast<uint16_t *>(v_pool), n_pages, page_tokens,
         page_table, max_pages, table, status_ptr(dev), static_cast<cudaStream_t>(stream));
+    return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "RoPE decode append launch");
+}
+
+int mslim_cuda_rope_append_decode_dense(const mslim_geometry_t *geometry, const void *q_in,
+                                        void *q_out, const void *k_in, const void *v_in,
+                                        const int32_t *positions, uint32_t n_seq,
+                                        const mslim_rope_config_t *rope, void *k_cache,
+                                        void *v_cache, uint32_t max_tokens, void *stream) {
+    if (int rc = check_geometry(geometry)) return rc;
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    if (!q_in || !q_out || !k_in || !v_in || !positions || !k_cache || !v_cache)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
+    if (n_seq == 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty batch");
+    if (max_tokens == 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty cache");
+    if (n_seq > 0x7fffffffu) return fail(MSLIM_ERR_SHAPE_MISMATCH, "too many sessions");
+    mslim::RopeTable table;
+    if (int rc = build_rope_table(rope, geometry->head_dim, &table)) return rc;
+    cudaError_t err = mslim::launch_rope_append_dense(
+        static_cast<const uint16_t *>(q_in), static_cast<uint16_t *>(q_out),
+        static_cast<const uint16_t *>(k_in), static_cast<const uint16_t *>(v_in), n_seq,
+        geometry->query_heads, geometry->kv_heads, geometry->head_dim, positions,
+        static_cast<uint16_t *>(k_cache), static_cast<uint16_t *>(v_cache), max_tokens, table,
+        status_ptr(dev), static_cast<cudaStream_t>(stream));
+    return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "RoPE dense append launch");
+}
+
+int mslim_cuda_rope_append_decode_dense_qkv(const mslim_geometry_t *geometry, const void *qkv,
+                                            void *q_out, const int32_t *positions, uint32_t n_seq,
+                                            const mslim_rope_config_t *rope, void *k_cache,
+                                            void *v_cache, uint32_t max_tokens, void *stream) {
+    if (int rc = check_geometry(geometry)) return rc;
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    if (!qkv || !q_out || !positions || !k_cache || !v_cache) return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
+    if (n_seq == 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty batch");
+    if (max_tokens == 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty cache");
+    if (n_seq > 0x7fffffffu) return fail(MSLIM_ERR_SHAPE_MISMATCH, "too many sessions");
+    mslim::RopeTable table;
+    if (int rc = build_rope_table(rope, geometry->head_dim, &table)) return rc;
+    const uint32_t D = geometry->head_dim, QH = geometry->query_heads, KVH = geometry->kv_heads;
+    const uint16_t *base = static_cast<const uint16_t *>(qkv);
+    const uint32_t stride = (QH + 2 * KVH) * D;
+    cudaError_t err = mslim::launch_rope_append_dense(
+        base, static_cast<uint16_t *>(q_out), base + (size_t)QH * D, base + (size_t)(QH + KVH) * D, n_seq,
+        QH, KVH, D, positions, static_cast<uint16_t *>(k_cache), static_cast<uint16_t *>(v_cache), max_tokens,
+        table, status_ptr(dev), static_cast<cudaStream_t>(stream), stride, stride);
+    return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "RoPE dense append launch");
+}
+
+int mslim_cuda_rope_append_decode_paged_qkv(const mslim_geometry_t *geometry, const void *qkv,
+                                            void *q_out, const int32_t *positions, uint32_t n_seq,
+                                            const mslim_rope_config_t *rope, void *k_pool, void *v_pool,
+                                            uint32_t n_pages, uint32_t page_tokens,
+                                            const int32_t *page_table, uint32_t max_pages, void *stream) {
+    if (int rc = check_geometry(geometry)) return rc;
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    if (!qkv || !q_out || !positions || !k_pool || !v_pool || !page_table)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
+    if (n_seq == 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty batch");
+    if (page_tokens == 0 || n_pages == 0 || max_pages == 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty page pool");
+    if (n_seq > 0x7fffffffu) return fail(MSLIM_ERR_SHAPE_MISMATCH, "too many sessions");
+    mslim::RopeTable table;
+    if (int rc = build_rope_table(rope, geometry->head_dim, &table)) return rc;
+    const uint32_t D = geometry->head_dim, QH = geometry->query_heads, KVH = geometry->kv_heads;
+    const uint16_t *base = static_cast<const uint16_t *>(qkv);
+    const uint32_t stride = (QH + 2 * KVH) * D;
+    cudaError_t err = mslim::launch_rope_append_paged(
+        base, static_cast<uint16_t *>(q_out), base + (size_t)QH * D, base + (size_t)(QH + KVH) * D, n_seq, QH,
+        KVH, D, 0, positions, static_cast<uint16_t *>(k_pool), static_cast<uint16_t *>(v_pool), n_pages,
+        page_tokens, page_table, max_pages, table, status_ptr(dev), static_cast<cudaStream_t>(stream), stride,
+        stride);
     return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "RoPE decode append launch");
 }
 

@@ -73,6 +73,24 @@ __global__ void __launch_bounds__(kEltThreads)
             out[i] = bf16_bits_rn(silu_mul(bf16_bits_to_f32(gate[i]), bf16_bits_to_f32(up[i])));
 }
 
+// SwiGLU over rows of a fused gate|up projection: row r of gate_up holds
+// [gate (width) | up (width)]; out is [rows][width].  width % 8 == 0.
+__global__ void __launch_bounds__(kEltThreads)
+    mslim_swiglu_rows(const uint16_t *__restrict__ gate_up, uint16_t *__restrict__ out, uint32_t rows,
+                      uint32_t width) {
+    const uint32_t w8 = width / 8;
+    const uint64_t n8 = (uint64_t)rows * w8;
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n8;
+         i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t r = i / w8, c = i % w8;
+        const uint4 *row = reinterpret_cast<const uint4 *>(gate_up + r * 2ull * width);
+        const uint4 g = row[c], u = row[w8 + c];
+        reinterpret_cast<uint4 *>(out + r * (uint64_t)width)[c] =
+            make_uint4(swiglu_pair(g.x, u.x), swiglu_pair(g.y, u.y), swiglu_pair(g.z, u.z),
+                       swiglu_pair(g.w, u.w));
+    }
+}
+
 // ---------------------------------------------------------------- argmax --
 
 constexpr int kArgThreads = 1024;
@@ -159,6 +177,12 @@ cudaError_t launch_residual_add(const uint16_t *a, const uint16_t *b, uint16_t *
 cudaError_t launch_swiglu(const uint16_t *gate, const uint16_t *up, uint16_t *out, uint64_t n,
                           cudaStream_t stream) {
     mslim_swiglu<<<elt_grid(n), kEltThreads, 0, stream>>>(gate, up, out, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_swiglu_rows(const uint16_t *gate_up, uint16_t *out, uint32_t rows, uint32_t width,
+                               cudaStream_t stream) {
+    mslim_swiglu_rows<<<elt_grid((uint64_t)rows * width), kEltThreads, 0, stream>>>(gate_up, out, rows, width);
     return cudaGetLastError();
 }
 

@@ -10,6 +10,9 @@ cudaError_t launch_residual_add(const uint16_t *a, const uint16_t *b, uint16_t *
                                 cudaStream_t stream);
 cudaError_t launch_swiglu(const uint16_t *gate, const uint16_t *up, uint16_t *out, uint64_t n,
                           cudaStream_t stream);
+// gate_up: [rows][gate (width) | up (width)] -> out [rows][width]; width % 8 == 0.
+cudaError_t launch_swiglu_rows(const uint16_t *gate_up, uint16_t *out, uint32_t rows, uint32_t width,
+                               cudaStream_t stream);
 // rows x n bf16 logits -> int32 index per row.  ties_to_last != 0: the largest
 // value under f32::total_cmp, last index among equals (the CPU path's
 // Iterator::max_by); 0: the largest by float comparison, first index among

@@ -24,28 +24,53 @@ __device__ __forceinline__ float rope_angle(const RopeTable &t, int i, uint32_t 
     return t.multiply ? pos * t.freq[i] : __fdiv_rn(pos, t.freq[i]);
 }
 
-__device__ __forceinline__ void rope_pair(float a, float b, float angle, float &out_a,
-                                          float &out_b) {
+// (cos, sin) of one angle, each rounded to bf16.
+__device__ __forceinline__ float2 rope_cs(float angle) {
     double sd, cd;
     sincos((double)angle, &sd, &cd);
-    const float s = bf16_round((float)sd);
-    const float c = bf16_round((float)cd);
-    out_a = bf16_round(bf16_round(a * c) - bf16_round(b * s));
-    out_b = bf16_round(bf16_round(b * c) + bf16_round(a * s));
+    return make_float2(bf16_round((float)cd), bf16_round((float)sd));
 }
 
-// One 128-thread CTA per token row; 16-byte vector loads.
+__device__ __forceinline__ void rope_rotate(float a, float b, float2 cs, float &out_a, float &out_b) {
+    out_a = bf16_round(bf16_round(a * cs.x) - bf16_round(b * cs.y));
+    out_b = bf16_round(bf16_round(b * cs.x) + bf16_round(a * cs.y));
+}
+
+// The angle depends on (position, i) only, so a CTA that rotates every head
+// of one token evaluates its D/2 (cos, sin) pairs once, into shared memory.
+constexpr int kRopeMaxHalf = 128;
+__device__ __forceinline__ void rope_fill(const RopeTable &t, uint32_t position, uint32_t half,
+                                          float2 *cs) {
+    for (uint32_t i = threadIdx.x; i < half; i += blockDim.x) cs[i] = rope_cs(rope_angle(t, (int)i, position));
+    __syncthreads();
+}
+
+// One 128-thread CTA per token row; 16-byte vector loads.  With kResidual the
+// row is first updated in place, x = bf16(x + delta) (the residual add of the
+// layer, native_cpu_adapter.rs:186-191), and normalised from the updated
+// values with the same reduction order, so the fused form returns the same
+// bits as a residual add followed by RMSNorm.
+template <bool kResidual>
 __global__ void __launch_bounds__(128)
-    mslim_rmsnorm(const uint16_t *__restrict__ x, const uint16_t *__restrict__ w,
-                  uint16_t *__restrict__ y, uint32_t hidden, float eps) {
+    mslim_rmsnorm(uint16_t *__restrict__ x, const uint16_t *__restrict__ delta,
+                  const uint16_t *__restrict__ w, uint16_t *__restrict__ y, uint32_t hidden, float eps) {
     const size_t row = blockIdx.x;
-    const uint16_t *xr = x + row * hidden;
+    uint16_t *xr = x + row * hidden;
+    const uint16_t *dr = kResidual ? delta + row * hidden : nullptr;
     uint16_t *yr = y + row * hidden;
     const bool vec = (hidden % 8 == 0);
     float sum = 0.f;
     if (vec) {
         for (uint32_t i = threadIdx.x * 8; i < hidden; i += 128 * 8) {
-            const uint4 v = *reinterpret_cast<const uint4 *>(xr + i);
+            uint4 v = *reinterpret_cast<const uint4 *>(xr + i);
+            if (kResidual) {
+                const uint4 d = *reinterpret_cast<const uint4 *>(dr + i);
+                v = make_uint4(pack_bf16x2(bf16lo_f32(v.x) + bf16lo_f32(d.x), bf16hi_f32(v.x) + bf16hi_f32(d.x)),
+                               pack_bf16x2(bf16lo_f32(v.y) + bf16lo_f32(d.y), bf16hi_f32(v.y) + bf16hi_f32(d.y)),
+                               pack_bf16x2(bf16lo_f32(v.z) + bf16lo_f32(d.z), bf16hi_f32(v.z) + bf16hi_f32(d.z)),
+                               pack_bf16x2(bf16lo_f32(v.w) + bf16lo_f32(d.w), bf16hi_f32(v.w) + bf16hi_f32(d.w)));
+                *reinterpret_cast<uint4 *>(xr + i) = v;
+            }
             const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
@@ -56,7 +81,12 @@ __global__ void __launch_bounds__(128)
         }
     } else {
         for (uint32_t i = threadIdx.x; i < hidden; i += 128) {
-            const float a = bf16_bits_to_f32(xr[i]);
+            float a = bf16_bits_to_f32(xr[i]);
+            if (kResidual) {
+                const uint16_t nb = bf16_bits_rn(a + bf16_bits_to_f32(dr[i]));
+                xr[i] = nb;
+                a = bf16_bits_to_f32(nb);
+            }
             sum += a * a;
         }
     }
@@ -68,6 +98,7 @@ __global__ void __launch_bounds__(128)
     const float total = (part[0] + part[1]) + (part[2] + part[3]);
     const float mean = __fdiv_rn(total, (float)hidden);
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(mean + eps));
+    // the second pass reads back only elements this thread itself wrote above
     if (vec) {
         for (uint32_t i = threadIdx.x * 8; i < hidden; i += 128 * 8) {
             const uint4 v = *reinterpret_cast<const uint4 *>(xr + i);
@@ -91,23 +122,58 @@ __global__ void __launch_bounds__(128)
     }
 }
 
-// One thread per rotated pair (token, head, i < D/2).
-__global__ void mslim_rope(const uint16_t *__restrict__ in, uint16_t *__restrict__ out,
-                           uint32_t tokens, uint32_t heads, uint32_t dim, uint32_t start_position,
-                           const RopeTable table) {
+// One CTA per token: the token's (cos, sin) table, then every (head, i) pair.
+__global__ void __launch_bounds__(128)
+    mslim_rope(const uint16_t *__restrict__ in, uint16_t *__restrict__ out, uint32_t heads,
+               uint32_t dim, uint32_t start_position, const RopeTable table) {
+    __shared__ float2 cs[kRopeMaxHalf];
+    const uint32_t token = blockIdx.x;
     const uint32_t half = dim / 2;
-    const size_t pairs = (size_t)tokens * heads * half;
-    for (size_t x = (size_t)blockIdx.x * blockDim.x + threadIdx.x; x < pairs;
-         x += (size_t)gridDim.x * blockDim.x) {
-        const uint32_t i = (uint32_t)(x % half);
-        const size_t rowi = x / half;  // token * heads + head
-        const uint32_t token = (uint32_t)(rowi / heads);
-        const size_t base = rowi * dim;
+    rope_fill(table, start_position + token, half, cs);
+    const size_t base = (size_t)token * heads * dim;
+    for (uint32_t x = threadIdx.x; x < heads * half; x += blockDim.x) {
+        const uint32_t head = x / half, i = x % half;
+        const size_t o = base + (size_t)head * dim;
         float oa, ob;
-        rope_pair(bf16_bits_to_f32(in[base + i]), bf16_bits_to_f32(in[base + i + half]),
-                  rope_angle(table, (int)i, start_position + token), oa, ob);
-        out[base + i] = bf16_bits_rn(oa);
-        out[base + i + half] = bf16_bits_rn(ob);
+        rope_rotate(bf16_bits_to_f32(in[o + i]), bf16_bits_to_f32(in[o + i + half]), cs[i], oa, ob);
+        out[o + i] = bf16_bits_rn(oa);
+        out[o + i + half] = bf16_bits_rn(ob);
+    }
+}
+
+// Input rows of the fused appends: q of token t at q_in + t * q_stride, its k
+// and v at k_in / v_in + t * kv_stride (q_stride = QH*D, kv_stride = KVH*D for
+// separate buffers; both (QH+2KVH)*D for one fused q|k|v projection output).
+struct QkvRows {
+    const uint16_t *q, *k, *v;
+    uint32_t q_stride, kv_stride;
+};
+
+// RoPE of one token's q heads into q_out ([token][QH][D]) and of its k heads
+// into k_dst(head) rows, v copied into v_dst(head) rows; (cos, sin) in cs.
+template <typename KDst, typename VDst>
+__device__ __forceinline__ void rope_append_token(const QkvRows &in, uint16_t *q_out, uint32_t token,
+                                                  uint32_t qheads, uint32_t kvheads, uint32_t dim,
+                                                  const float2 *cs, KDst k_dst, VDst v_dst) {
+    const uint32_t half = dim / 2;
+    const uint32_t q_pairs = qheads * half, k_pairs = kvheads * half;
+    const uint16_t *qr = in.q + (size_t)token * in.q_stride;
+    const uint16_t *kr = in.k + (size_t)token * in.kv_stride;
+    const uint16_t *vr = in.v + (size_t)token * in.kv_stride;
+    for (uint32_t x = threadIdx.x; x < q_pairs + k_pairs; x += blockDim.x) {
+        const bool is_q = x < q_pairs;
+        const uint32_t y = is_q ? x : x - q_pairs;
+        const uint32_t head = y / half, i = y % half;
+        const uint16_t *src = (is_q ? qr : kr) + (size_t)head * dim;
+        float oa, ob;
+        rope_rotate(bf16_bits_to_f32(src[i]), bf16_bits_to_f32(src[i + half]), cs[i], oa, ob);
+        uint16_t *dst = is_q ? q_out + ((size_t)token * qheads + head) * dim : k_dst(head);
+        dst[i] = bf16_bits_rn(oa);
+        dst[i + half] = bf16_bits_rn(ob);
+    }
+    for (uint32_t x = threadIdx.x; x < kvheads * dim; x += blockDim.x) {
+        const uint32_t head = x / dim, d = x % dim;
+        v_dst(head)[d] = vr[(size_t)head * dim + d];
     }
 }
 
@@ -119,14 +185,13 @@ __global__ void mslim_rope(const uint16_t *__restrict__ in, uint16_t *__restrict
 //   decode form (positions != null): CTA s is the new token of session s at
 //     position positions[s], pages page_table[s * max_pages ..].
 __global__ void __launch_bounds__(256)
-    mslim_rope_append_paged(const uint16_t *__restrict__ q_in, uint16_t *__restrict__ q_out,
-                            const uint16_t *__restrict__ k_in, const uint16_t *__restrict__ v_in,
-                            uint32_t qheads, uint32_t kvheads, uint32_t dim,
-                            uint32_t start_position, const int32_t *__restrict__ positions,
-                            uint16_t *__restrict__ k_pool, uint16_t *__restrict__ v_pool,
-                            uint32_t n_pages, uint32_t page_tokens,
+    mslim_rope_append_paged(const QkvRows in, uint16_t *__restrict__ q_out, uint32_t qheads,
+                            uint32_t kvheads, uint32_t dim, uint32_t start_position,
+                            const int32_t *__restrict__ positions, uint16_t *__restrict__ k_pool,
+                            uint16_t *__restrict__ v_pool, uint32_t n_pages, uint32_t page_tokens,
                             const int32_t *__restrict__ page_table, uint32_t max_pages,
                             const RopeTable table, int *status) {
+    __shared__ float2 cs[kRopeMaxHalf];
     const uint32_t token = blockIdx.x;
     uint32_t pos;
     const int32_t *row = page_table;
@@ -141,50 +206,64 @@ __global__ void __launch_bounds__(256)
     } else {
         pos = start_position + token;
     }
-    const uint32_t half = dim / 2;
     const int32_t phys = row[pos / page_tokens];
     if (phys < 0 || (uint32_t)phys >= n_pages) {
         // A page id outside the pool: write nothing, record it for the host.
         if (threadIdx.x == 0 && status) atomicExch(status, MSLIM_DEVICE_BAD_PAGE_CODE);
         return;
     }
+    rope_fill(table, pos, dim / 2, cs);
     const uint32_t slot = pos % page_tokens;
-    const uint32_t q_pairs = qheads * half, k_pairs = kvheads * half;
-    for (uint32_t x = threadIdx.x; x < q_pairs + k_pairs; x += blockDim.x) {
-        const bool is_q = x < q_pairs;
-        const uint32_t y = is_q ? x : x - q_pairs;
-        const uint32_t head = y / half, i = y % half;
-        const uint16_t *src = is_q ? q_in + ((size_t)token * qheads + head) * dim
-                                   : k_in + ((size_t)token * kvheads + head) * dim;
-        float oa, ob;
-        rope_pair(bf16_bits_to_f32(src[i]), bf16_bits_to_f32(src[i + half]),
-                  rope_angle(table, (int)i, pos), oa, ob);
-        uint16_t *dst = is_q ? q_out + ((size_t)token * qheads + head) * dim
-                             : k_pool + (((size_t)phys * kvheads + head) * page_tokens + slot) * dim;
-        dst[i] = bf16_bits_rn(oa);
-        dst[i + half] = bf16_bits_rn(ob);
+    auto k_dst = [&](uint32_t head) {
+        return k_pool + (((size_t)phys * kvheads + head) * page_tokens + slot) * dim;
+    };
+    auto v_dst = [&](uint32_t head) {
+        return v_pool + (((size_t)phys * kvheads + head) * page_tokens + slot) * dim;
+    };
+    rope_append_token(in, q_out, token, qheads, kvheads, dim, cs, k_dst, v_dst);
+}
+
+// Dense-cache twin of the decode form above: CTA s is the new token of session
+// s at position positions[s]; q -> RoPE -> q_out, k -> RoPE and v -> copy into
+// the token-major caches [n_seq][max_tokens][KVH][D] at row positions[s].
+__global__ void __launch_bounds__(256)
+    mslim_rope_append_dense(const QkvRows in, uint16_t *__restrict__ q_out, uint32_t qheads,
+                            uint32_t kvheads, uint32_t dim, const int32_t *__restrict__ positions,
+                            uint16_t *__restrict__ k_cache, uint16_t *__restrict__ v_cache,
+                            uint32_t max_tokens, const RopeTable table, int *status) {
+    __shared__ float2 cs[kRopeMaxHalf];
+    const uint32_t token = blockIdx.x;
+    const int32_t p = positions[token];
+    if (p < 0 || (uint32_t)p >= max_tokens) {
+        if (threadIdx.x == 0 && status) atomicExch(status, MSLIM_DEVICE_BAD_PAGE_CODE);
+        return;
     }
-    for (uint32_t x = threadIdx.x; x < kvheads * dim; x += blockDim.x) {
-        const uint32_t head = x / dim, d = x % dim;
-        v_pool[(((size_t)phys * kvheads + head) * page_tokens + slot) * dim + d] =
-            v_in[((size_t)token * kvheads + head) * dim + d];
-    }
+    const uint32_t pos = (uint32_t)p;
+    rope_fill(table, pos, dim / 2, cs);
+    const size_t row = ((size_t)token * max_tokens + pos) * kvheads;  // cache row of this token
+    auto k_dst = [&](uint32_t head) { return k_cache + (row + head) * dim; };
+    auto v_dst = [&](uint32_t head) { return v_cache + (row + head) * dim; };
+    rope_append_token(in, q_out, token, qheads, kvheads, dim, cs, k_dst, v_dst);
 }
 
 }  // namespace
 
 cudaError_t launch_rmsnorm(const uint16_t *x, const uint16_t *w, uint16_t *y, uint32_t tokens,
                            uint32_t hidden, float eps, cudaStream_t stream) {
-    mslim_rmsnorm<<<tokens, 128, 0, stream>>>(x, w, y, hidden, eps);
+    mslim_rmsnorm<false><<<tokens, 128, 0, stream>>>(const_cast<uint16_t *>(x), nullptr, w, y, hidden, eps);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_residual_rmsnorm(uint16_t *x, const uint16_t *delta, const uint16_t *w, uint16_t *y,
+                                    uint32_t tokens, uint32_t hidden, float eps, cudaStream_t stream) {
+    mslim_rmsnorm<true><<<tokens, 128, 0, stream>>>(x, delta, w, y, hidden, eps);
     return cudaGetLastError();
 }
 
 cudaError_t launch_rope(const uint16_t *in, uint16_t *out, uint32_t tokens, uint32_t heads,
                         uint32_t dim, uint32_t start_position, const RopeTable &table,
                         cudaStream_t stream) {
-    const size_t pairs = (size_t)tokens * heads * (dim / 2);
-    const unsigned blocks = (unsigned)std::min<size_t>((pairs + 255) / 256, 148 * 16);
-    mslim_rope<<<blocks, 256, 0, stream>>>(in, out, tokens, heads, dim, start_position, table);
+    mslim_rope<<<tokens, 128, 0, stream>>>(in, out, heads, dim, start_position, table);
     return cudaGetLastError();
 }
 
@@ -194,10 +273,26 @@ cudaError_t launch_rope_append_paged(const uint16_t *q_in, uint16_t *q_out, cons
                                      const int32_t *positions, uint16_t *k_pool,
                                      uint16_t *v_pool, uint32_t n_pages, uint32_t page_tokens,
                                      const int32_t *page_table, uint32_t max_pages,
-                                     const RopeTable &table, int *status, cudaStream_t stream) {
-    mslim_rope_append_paged<<<tokens, 256, 0, stream>>>(
-        q_in, q_out, k_in, v_in, qheads, kvheads, dim, start_position, positions, k_pool, v_pool,
-        n_pages, page_tokens, page_table, max_pages, table, status);
+                                     const RopeTable &table, int *status, cudaStream_t stream,
+                                     uint32_t q_stride, uint32_t kv_stride) {
+    const QkvRows in{q_in, k_in, v_in, q_stride ? q_stride : qheads * dim,
+                     kv_stride ? kv_stride : kvheads * dim};
+    mslim_rope_append_paged<<<tokens, 256, 0, stream>>>(in, q_out, qheads, kvheads, dim, start_position,
+                                                        positions, k_pool, v_pool, n_pages, page_tokens,
+                                                        page_table, max_pages, table, status);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rope_append_dense(const uint16_t *q_in, uint16_t *q_out, const uint16_t *k_in,
+                                     const uint16_t *v_in, uint32_t n_seq, uint32_t qheads,
+                                     uint32_t kvheads, uint32_t dim, const int32_t *positions,
+                                     uint16_t *k_cache, uint16_t *v_cache, uint32_t max_tokens,
+                                     const RopeTable &table, int *status, cudaStream_t stream,
+                                     uint32_t q_stride, uint32_t kv_stride) {
+    const QkvRows in{q_in, k_in, v_in, q_stride ? q_stride : qheads * dim,
+                     kv_stride ? kv_stride : kvheads * dim};
+    mslim_rope_append_dense<<<n_seq, 256, 0, stream>>>(in, q_out, qheads, kvheads, dim, positions, k_cache,
+                                                        v_cache, max_tokens, table, status);
     return cudaGetLastError();
 }
 

@@ -18,6 +18,9 @@ struct RopeTable {
 
 cudaError_t launch_rmsnorm(const uint16_t *x, const uint16_t *w, uint16_t *y, uint32_t tokens,
                            uint32_t hidden, float eps, cudaStream_t stream);
+// x = bf16(x + delta) in place, then y = RMSNorm(x): one pass per row.
+cudaError_t launch_residual_rmsnorm(uint16_t *x, const uint16_t *delta, const uint16_t *w, uint16_t *y,
+                                    uint32_t tokens, uint32_t hidden, float eps, cudaStream_t stream);
 cudaError_t launch_rope(const uint16_t *in, uint16_t *out, uint32_t tokens, uint32_t heads,
                         uint32_t dim, uint32_t start_position, const RopeTable &table,
                         cudaStream_t stream);
@@ -27,6 +30,15 @@ cudaError_t launch_rope_append_paged(const uint16_t *q_in, uint16_t *q_out, cons
                                      const int32_t *positions, uint16_t *k_pool,
                                      uint16_t *v_pool, uint32_t n_pages, uint32_t page_tokens,
                                      const int32_t *page_table, uint32_t max_pages,
-                                     const RopeTable &table, int *status, cudaStream_t stream);
+                                     const RopeTable &table, int *status, cudaStream_t stream,
+                                     uint32_t q_stride = 0, uint32_t kv_stride = 0);
+// q_stride / kv_stride: elements between consecutive tokens' q / k, v rows
+// (0: the rows are packed, QH*D / KVH*D).
+cudaError_t launch_rope_append_dense(const uint16_t *q_in, uint16_t *q_out, const uint16_t *k_in,
+                                     const uint16_t *v_in, uint32_t n_seq, uint32_t qheads,
+                                     uint32_t kvheads, uint32_t dim, const int32_t *positions,
+                                     uint16_t *k_cache, uint16_t *v_cache, uint32_t max_tokens,
+                                     const RopeTable &table, int *status, cudaStream_t stream,
+                                     uint32_t q_stride = 0, uint32_t kv_stride = 0);
 
 }  // namespace mslim

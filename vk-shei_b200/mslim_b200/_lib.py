@@ -74,13 +74,20 @@ SIGNATURES = {
     "mslim_cuda_prefill_causal": (_int, [_G, _vp, _vp, _vp, _vp, _u32, _u32, _vp]),
     "mslim_cuda_residual_add": (_int, [_vp, _vp, _vp, ctypes.c_uint64, _vp]),
     "mslim_cuda_swiglu": (_int, [_vp, _vp, _vp, ctypes.c_uint64, _vp]),
+    "mslim_cuda_swiglu_rows": (_int, [_vp, _vp, _u32, _u32, _vp]),
     "mslim_cuda_argmax": (_int, [_vp, _u32, _u32, _int, _vp, _vp]),
+    "mslim_cuda_residual_rmsnorm": (_int, [_vp, _vp, _vp, _vp, _u32, _u32, ctypes.c_float, _vp]),
+    "mslim_cuda_rope_append_decode_dense_qkv": (_int, [_G, _vp, _vp, _vp, _u32, _R, _vp, _vp, _u32, _vp]),
+    "mslim_cuda_rope_append_decode_paged_qkv": (_int, [_G, _vp, _vp, _vp, _u32, _R, _vp, _vp, _u32, _u32, _vp,
+                                                       _u32, _vp]),
     "mslim_cuda_rmsnorm": (_int, [_vp, _vp, _vp, _u32, _u32, ctypes.c_float, _vp]),
     "mslim_cuda_rope": (_int, [_vp, _vp, _u32, _u32, _u32, _u32, _R, _vp]),
     "mslim_cuda_rope_append_paged": (_int, [_G, _vp, _vp, _vp, _vp, _u32, _u32, _R, _vp, _vp, _u32, _u32,
                                             _vp, _u32, _vp]),
     "mslim_cuda_rope_append_decode_paged": (_int, [_G, _vp, _vp, _vp, _vp, _vp, _u32, _R, _vp, _vp, _u32,
                                                    _u32, _vp, _u32, _vp]),
+    "mslim_cuda_rope_append_decode_dense": (_int, [_G, _vp, _vp, _vp, _vp, _vp, _u32, _R, _vp, _vp, _u32,
+                                                   _vp]),
     "mslim_cuda_backend_create": (_int, [_int, ctypes.POINTER(_vp)]),
     "mslim_cuda_backend_destroy": (None, [_vp]),
     "mslim_cuda_backend_decode": (_int, [_vp, _G, _vp, _vp, _vp, _int, _u32, _vp]),

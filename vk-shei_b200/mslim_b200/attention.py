@@ -294,6 +294,15 @@ def prefill_causal(geometry: AttentionGeometry, q, k, v, out, queries: int, prio
                                                _ptr(out), queries, prior, _stream(stream)))
 
 
+def rope_append_decode_dense(geometry: AttentionGeometry, q_in, q_out, k_in, v_in, positions, n_seq: int,
+                             cfg: RopeKernelConfig, k_cache, v_cache, max_tokens: int, stream=None) -> None:
+    """Decode-step RoPE + K/V write into dense token-major caches
+    [n_seq][max_tokens][KVH][D] at row positions[s] (run_layer, mod.rs:2099-2116)."""
+    check(_lib.lib().mslim_cuda_rope_append_decode_dense(
+        ctypes.byref(geometry.c()), _ptr(q_in), _ptr(q_out), _ptr(k_in), _ptr(v_in), _ptr(positions), n_seq,
+        ctypes.byref(cfg.c()), _ptr(k_cache), _ptr(v_cache), max_tokens, _stream(stream)))
+
+
 def residual_add(a, b, out, n: int, stream=None) -> None:
     """GpuEngine::add (src/gpu_llm/gpu_resources.rs:539-559): out = bf16(a + b)."""
     check(_lib.lib().mslim_cuda_residual_add(_ptr(a), _ptr(b), _ptr(out), n, _stream(stream)))
@@ -302,6 +311,34 @@ def residual_add(a, b, out, n: int, stream=None) -> None:
 def swiglu(gate, up, out, n: int, stream=None) -> None:
     """GpuEngine::swiglu (src/gpu_llm/gpu_resources.rs:561-581)."""
     check(_lib.lib().mslim_cuda_swiglu(_ptr(gate), _ptr(up), _ptr(out), n, _stream(stream)))
+
+
+def swiglu_rows(gate_up, out, rows: int, width: int, stream=None) -> None:
+    """SwiGLU over rows of a fused [gate | up] projection output."""
+    check(_lib.lib().mslim_cuda_swiglu_rows(_ptr(gate_up), _ptr(out), rows, width, _stream(stream)))
+
+
+def residual_rmsnorm(x, delta, w, y, tokens: int, hidden: int, eps: float, stream=None) -> None:
+    """x = bf16(x + delta) in place, then y = RMSNorm(x, w) (one pass)."""
+    check(_lib.lib().mslim_cuda_residual_rmsnorm(_ptr(x), _ptr(delta), _ptr(w), _ptr(y), tokens, hidden, eps,
+                                                 _stream(stream)))
+
+
+def rope_append_decode_dense_qkv(geometry: AttentionGeometry, qkv, q_out, positions, n_seq: int,
+                                 cfg: RopeKernelConfig, k_cache, v_cache, max_tokens: int, stream=None) -> None:
+    """rope_append_decode_dense reading q|k|v from one fused projection output."""
+    check(_lib.lib().mslim_cuda_rope_append_decode_dense_qkv(
+        ctypes.byref(geometry.c()), _ptr(qkv), _ptr(q_out), _ptr(positions), n_seq, ctypes.byref(cfg.c()),
+        _ptr(k_cache), _ptr(v_cache), max_tokens, _stream(stream)))
+
+
+def rope_append_decode_paged_qkv(geometry: AttentionGeometry, qkv, q_out, positions, n_seq: int,
+                                 cfg: RopeKernelConfig, k_pool, v_pool, n_pages: int, page_tokens: int,
+                                 page_table, max_pages: int, stream=None) -> None:
+    """rope_append_decode_paged reading q|k|v from one fused projection output."""
+    check(_lib.lib().mslim_cuda_rope_append_decode_paged_qkv(
+        ctypes.byref(geometry.c()), _ptr(qkv), _ptr(q_out), _ptr(positions), n_seq, ctypes.byref(cfg.c()),
+        _ptr(k_pool), _ptr(v_pool), n_pages, page_tokens, _ptr(page_table), max_pages, _stream(stream)))
 
 
 def argmax(logits, rows: int, vocab: int, token_ids, ties_to_last: bool = True, stream=None) -> None:

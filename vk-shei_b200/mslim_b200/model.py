@@ -1,0 +1,350 @@
+"""A Llama-3-8B-shaped decoder ("C5") on one or
+more B200s, tensor-parallel by KV-head group.
+
+Per layer and rank (TP world W, rank r): the rank owns KV heads
+[r*KVH/W, (r+1)*KVH/W) and their query heads (GQA mapping qh / (QH/KVH) kept),
+so attention needs no exchange; q/k/v projections are column slices, the
+o-projection is row-parallel and its partial sums meet in one NCCL all-reduce
+(sum, bf16, tokens x hidden) over NVLink.  The MLP is either replicated on
+every rank (mlp="replicated": exactly one all-reduce per layer, the MLP's
+FLOPs and weight bytes do not scale) or sharded (mlp="sharded": gate/up
+column-parallel, down row-parallel, a second all-reduce; everything scales).
+
+Sequencing follows the reference GPU runtime: prefill through the batched
+kernels (src/gpu_llm/prefill.rs), decode through run_layer
+(src/gpu_llm/mod.rs:2118-2329), then the final norm, the tied lm_head and the
+greedy argmax with the CPU path's tie rule (native_cpu_adapter.rs:579-587).
+Weights are random: projections and the tied embedding N(0, 0.02), RMSNorm
+weights one; each layer's full tensors come from a device generator seeded by
+(seed, layer), so every rank slices its shard of the same model.
+"""
+from __future__ import annotations
+
+import dataclasses
+
+from . import attention as _att
+from .layer import LayerSpec
+
+
+@dataclasses.dataclass(frozen=True)
+class ModelSpec:
+    layer: LayerSpec = LayerSpec()
+    layers: int = 32
+    vocab: int = 128256
+    std: float = 0.02
+
+
+class SectionTimer:
+    """CUDA events around each step of a forward, summed per kind (gemm,
+    attention, collective, elementwise) once the stream has been synchronised."""
+
+    def __init__(self, torch):
+        self.torch = torch
+        self.marks = []
+
+    def __call__(self, kind):
+        return _Section(self, kind)
+
+    def totals_ms(self) -> dict:
+        out = {}
+        for kind, a, b in self.marks:
+            out[kind] = out.get(kind, 0.0) + a.elapsed_time(b)
+        return out
+
+
+class _Section:
+    def __init__(self, timer, kind):
+        self.timer, self.kind = timer, kind
+
+    def __enter__(self):
+        t = self.timer.torch
+        self.a = t.cuda.Event(enable_timing=True)
+        self.b = t.cuda.Event(enable_timing=True)
+        self.a.record()
+
+    def __exit__(self, *exc):
+        self.b.record()
+        self.timer.marks.append((self.kind, self.a, self.b))
+        return False
+
+
+class _NoSection:
+    def __enter__(self):
+        return None
+
+    def __exit__(self, *exc):
+        return False
+
+
+_NO_SECTION = _NoSection()
+
+
+class DeviceModel:
+    def __init__(self, spec: ModelSpec, batch: int, capacity: int, seed: int = 5, tp_rank: int = 0,
+                 tp_world: int = 1, mlp: str = "sharded", kv_mode: str = "dense", page_tokens: int = 256,
+                 group=None, device=None):
+        import torch
+        L = spec.layer
+        if L.kv_heads % tp_world or L.intermediate % tp_world:
+            raise ValueError("KV heads and the MLP width must divide by the tensor-parallel world")
+        if mlp not in ("sharded", "replicated"):
+            raise ValueError("mlp is 'sharded' or 'replicated'")
+        if kv_mode not in ("dense", "coldstore"):
+            raise ValueError("kv_mode is 'dense' or 'coldstore'")
+        torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = False
+        self.torch, self.spec = torch, spec
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.rank, self.world, self.group = tp_rank, tp_world, group
+        self.mlp, self.kv_mode = mlp, kv_mode
+        self.batch, self.capacity = batch, capacity
+        self.kvh = L.kv_heads // tp_world
+        self.qh = L.query_heads // tp_world
+        self.geometry = _att.AttentionGeometry.new(self.qh, self.kvh, L.head_dim)
+        self.rope_cfg = _att.RopeKernelConfig(theta=L.theta)
+        bf = torch.bfloat16
+        dev = self.device
+        D = L.head_dim
+        q0, q1 = tp_rank * self.qh * D, (tp_rank + 1) * self.qh * D
+        k0, k1 = tp_rank * self.kvh * D, (tp_rank + 1) * self.kvh * D
+        inter = L.intermediate if mlp == "replicated" else L.intermediate // tp_world
+        i0 = 0 if mlp == "replicated" else tp_rank * inter
+
+        def normal(g, shape):
+            return (torch.randn(shape, generator=g, device=dev, dtype=torch.float32) * spec.std).to(bf)
+
+        self.layers = []
+        for li in range(spec.layers):
+            g = torch.Generator(device=dev)
+            g.manual_seed(seed * 1000003 + li)
+            wq = normal(g, (L.q_dim, L.hidden))
+            wk = normal(g, (L.kv_dim, L.hidden))
+            wv = normal(g, (L.kv_dim, L.hidden))
+            wqkv = torch.cat([wq[q0:q1], wk[k0:k1], wv[k0:k1]]).contiguous()
+            del wq, wk, wv
+            wo = normal(g, (L.hidden, L.q_dim))[:, q0:q1].contiguous()
+            wg = normal(g, (L.intermediate, L.hidden))
+            wu = normal(g, (L.intermediate, L.hidden))
+            wgu = torch.cat([wg[i0:i0 + inter], wu[i0:i0 + inter]]).contiguous()
+            del wg, wu
+            wd = normal(g, (L.hidden, L.intermediate))[:, i0:i0 + inter].contiguous()
+            ones = torch.full((L.hidden,), 1.0, dtype=bf, device=dev)
+            self.layers.append({"in_norm": ones, "post_norm": ones.clone(), "wqkv": wqkv, "wo": wo,
+                                "wgu": wgu, "wd": wd})
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed * 1000003 + 999983)
+        self.embedding = normal(g, (spec.vocab, L.hidden))   # tied: lm_head = embedding
+        # the lm_head is split by vocabulary rows; the embedding lookup keeps
+        # the whole table (any token id can come in)
+        per = (spec.vocab + tp_world - 1) // tp_world
+        self.vocab_lo = min(tp_rank * per, spec.vocab)
+        self.vocab_hi = min(self.vocab_lo + per, spec.vocab)
+        self.lm_head = self.embedding[self.vocab_lo:self.vocab_hi]
+        self.final_norm = torch.full((L.hidden,), 1.0, dtype=bf, device=dev)
+        self.inter = inter
+        # K/V of this rank's heads, per layer
+        if kv_mode == "dense":
+            self.k_cache = [torch.zeros((batch, capacity, self.kvh, D), dtype=bf, device=dev)
+                            for _ in range(spec.layers)]
+            self.v_cache = [torch.zeros_like(c) for c in self.k_cache]
+            reach = capacity
+        else:
+            self.page_tokens = page_tokens
+            self.max_pages = (capacity + page_tokens - 1) // page_tokens
+            n_pages = batch * self.max_pages
+            # session s owns pages s*max_pages.. in a fixed random physical order
+            perm = torch.randperm(n_pages, generator=torch.Generator().manual_seed(seed), dtype=torch.int64)
+            self.page_table = perm.to(torch.int32).reshape(batch, self.max_pages).to(dev)
+            self.n_pages = n_pages
+            self.k_pool = [torch.zeros((n_pages, self.kvh, page_tokens, D), dtype=bf, device=dev)
+                           for _ in range(spec.layers)]
+            self.v_pool = [torch.zeros_like(p) for p in self.k_pool]
+            reach = self.max_pages * page_tokens
+        ws = _att.decode_workspace_bytes(self.geometry, batch, reach)
+        self.workspace = torch.empty(max(ws, 16), dtype=torch.uint8, device=dev)
+        self.lengths = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.profile = None   # a SectionTimer splits the device time by kind of step
+
+    # ------------------------------------------------------------ pieces --
+    def _sec(self, kind):
+        return self.profile(kind) if self.profile is not None else _NO_SECTION
+
+    def _all_reduce(self, x):
+        if self.world > 1:
+            import torch.distributed as dist
+            with self._sec("collective"):
+                dist.all_reduce(x, op=dist.ReduceOp.SUM, group=self.group)
+
+    def _norm(self, x, w):
+        out = self.torch.empty_like(x)
+        with self._sec("elementwise"):
+            _att.rmsnorm(x, w, out, x.shape[0], self.spec.layer.hidden, self.spec.layer.eps)
+        return out
+
+    def _gemm(self, x, w):
+        with self._sec("gemm"):
+            return self.torch.matmul(x, w.t())
+
+    def _qkv_split(self, qkv):
+        D = self.spec.layer.head_dim
+        nq, nk = self.qh * D, self.kvh * D
+        with self._sec("elementwise"):
+            return (qkv[:, :nq].contiguous(), qkv[:, nq:nq + nk].contiguous(),
+                    qkv[:, nq + nk:].contiguous())
+
+    def _residual_norm(self, x, delta, w):
+        """x = bf16(x + delta) in place; returns RMSNorm(x, w)."""
+        out = self.torch.empty_like(x)
+        with self._sec("elementwise"):
+            _att.residual_rmsnorm(x, delta, w, out, x.shape[0], self.spec.layer.hidden, self.spec.layer.eps)
+        return out
+
+    def _after_attention(self, li, x, attn):
+        """o-projection (+ all-reduce), residual, MLP (+ all-reduce when
+        sharded), residual; returns the next layer's normalised input (the
+        final norm after the last layer)."""
+        t = self.torch
+        W = self.layers[li]
+        o = self._gemm(attn.reshape(x.shape[0], -1), W["wo"])
+        self._all_reduce(o)
+        n2 = self._residual_norm(x, o, W["post_norm"])
+        gu = self._gemm(n2, W["wgu"])
+        act = t.empty((x.shape[0], self.inter), dtype=x.dtype, device=self.device)
+        with self._sec("elementwise"):
+            _att.swiglu_rows(gu, act, x.shape[0], self.inter)
+        d = self._gemm(act, W["wd"])
+        if self.mlp == "sharded":
+            self._all_reduce(d)
+        nxt = self.layers[li + 1]["in_norm"] if li + 1 < len(self.layers) else self.final_norm
+        return self._residual_norm(x, d, nxt)
+
+    def _lm_head_argmax(self, n_final):
+        """n_final: final-normed bf16 [batch][hidden] -> (int32 ids, bf16 logits
+        of this rank's vocabulary slice).  With several ranks each takes the
+        argmax of its slice and one all-gather of (total-order key, index)
+        pairs picks the winner; equal keys go to the larger index, so the
+        CPU path's tie rule (last maximal index) holds across slices."""
+        t = self.torch
+        B = n_final.shape[0]
+        logits = self._gemm(n_final, self.lm_head)
+        ids = t.empty(B, dtype=t.int32, device=self.device)
+        with self._sec("elementwise"):
+            _att.argmax(logits, B, self.vocab_hi - self.vocab_lo, ids, ties_to_last=True)
+        if self.world == 1:
+            return ids, logits
+        import torch.distributed as dist
+        with self._sec("elementwise"):
+            bits = logits.gather(1, ids.long().view(B, 1)).view(t.int16).to(t.int32).view(B)
+            # f32::total_cmp key of the bf16 value (signed-magnitude flip)
+            key = t.where(bits < 0, bits ^ 0x7FFF, bits)
+            mine = (key.to(t.int64) << 32) | (ids.to(t.int64) + self.vocab_lo)
+            every = t.empty((self.world, B), dtype=t.int64, device=self.device)
+        with self._sec("collective"):
+            dist.all_gather_into_tensor(every, mine, group=self.group)
+        with self._sec("elementwise"):
+            best = (every.max(dim=0).values & 0xFFFFFFFF).to(t.int32)
+        return best, logits
+
+    # ----------------------------------------------------------- prefill --
+    def prefill(self, ids):
+        """ids: int64 [batch][S] prompt tokens (positions 0..S-1 of every
+        session).  Returns the greedy next token per session (and logits)."""
+        t, L = self.torch, self.spec.layer
+        B, S = ids.shape
+        D = L.head_dim
+        if S > self.capacity:
+            raise ValueError("prompt longer than the K/V capacity")
+        with self._sec("elementwise"):
+            x = self.embedding.index_select(0, ids.reshape(-1)).contiguous()   # [B*S][hidden]
+        n = self._norm(x, self.layers[0]["in_norm"])
+        for li, W in enumerate(self.layers):
+            q, k, v = self._qkv_split(self._gemm(n, W["wqkv"]))
+            q_r = t.empty_like(q)
+            k_r = t.empty_like(k)
+            attn = t.empty_like(q)
+            for b in range(B):
+                rows = slice(b * S, (b + 1) * S)
+                with self._sec("elementwise"):
+                    _att.rope(q[rows], q_r[rows], S, self.qh, D, 0, self.rope_cfg)
+                    _att.rope(k[rows], k_r[rows], S, self.kvh, D, 0, self.rope_cfg)
+                    if self.kv_mode == "dense":
+                        self.k_cache[li][b, :S] = k_r[rows].view(S, self.kvh, D)
+                        self.v_cache[li][b, :S] = v[rows].view(S, self.kvh, D)
+                    else:
+                        q_tmp = t.empty((S, self.qh * D), dtype=q.dtype, device=self.device)
+                        _att.rope_append_paged(self.geometry, q[rows], q_tmp, k[rows], v[rows], S, 0,
+                                               self.rope_cfg, self.k_pool[li], self.v_pool[li],
+                                               self.n_pages, self.page_tokens, self.page_table[b:b + 1],
+                                               self.max_pages)
+                with self._sec("attention"):
+                    _att.prefill_causal(self.geometry, q_r[rows], k_r[rows], v[rows], attn[rows], S, 0)
+            n = self._after_attention(li, x, attn)
+        self.lengths.fill_(S)
+        last = n.view(B, S, L.hidden)[:, S - 1].contiguous()
+        return self._lm_head_argmax(last)
+
+    # ------------------------------------------------------------ decode --
+    def decode_step(self, tokens):
+        """tokens: int32 [batch] (this step's input token per session, at
+        position lengths[b]).  Returns (next tokens, logits)."""
+        t = self.torch
+        B = tokens.shape[0]
+        D = self.spec.layer.head_dim
+        with self._sec("elementwise"):
+            x = self.embedding.index_select(0, tokens.long()).contiguous()    # [B][hidden]
+            pos = self.lengths
+            seq = pos + 1
+        n = self._norm(x, self.layers[0]["in_norm"])
+        for li, W in enumerate(self.layers):
+            qkv = self._gemm(n, W["wqkv"])
+            q_r = t.empty((B, self.qh * D), dtype=x.dtype, device=self.device)
+            attn = t.empty_like(q_r)
+            if self.kv_mode == "dense":
+                with self._sec("elementwise"):
+                    _att.rope_append_decode_dense_qkv(self.geometry, qkv, q_r, pos, B, self.rope_cfg,
+                                                      self.k_cache[li], self.v_cache[li], self.capacity)
+                with self._sec("attention"):
+                    _att.decode_dense(self.geometry, q_r, self.k_cache[li], self.v_cache[li], seq, B,
+                                      self.capacity, self.workspace, attn)
+            else:
+                with self._sec("elementwise"):
+                    _att.rope_append_decode_paged_qkv(self.geometry, qkv, q_r, pos, B, self.rope_cfg,
+                                                      self.k_pool[li], self.v_pool[li], self.n_pages,
+                                                      self.page_tokens, self.page_table, self.max_pages)
+                with self._sec("attention"):
+                    _att.decode_paged(self.geometry, q_r, self.k_pool[li], self.v_pool[li], self.n_pages,
+                                      self.page_tokens, self.page_table, self.max_pages, seq, B,
+                                      self.workspace, attn)
+            n = self._after_attention(li, x, attn)
+        with self._sec("elementwise"):
+            self.lengths.add_(1)
+        return self._lm_head_argmax(n)
+
+    # ------------------------------------------------------- graph decode --
+    def capture_decode(self):
+        """Captures one whole decode step (every layer, the all-reduces, the
+        lm_head and the argmax) into a CUDA graph.  decode_step_graphed then
+        replays it: the host issues one launch per step instead of ~20 per
+        layer, and positions advance on the device (lengths += 1 is part of
+        the graph).  Call after at least one eager decode step."""
+        t = self.torch
+        self.g_tokens = t.zeros(self.batch, dtype=t.int32, device=self.device)
+        saved = self.lengths.clone()
+        self.graph = t.cuda.CUDAGraph()
+        side = t.cuda.Stream()
+        side.wait_stream(t.cuda.current_stream())
+        with t.cuda.graph(self.graph, stream=side):
+            self.g_out, self.g_logits = self.decode_step(self.g_tokens)
+        t.cuda.current_stream().wait_stream(side)
+        # capturing ran nothing; keep the lengths the caller had
+        self.lengths.copy_(saved)
+
+    def decode_step_graphed(self, tokens):
+        self.g_tokens.copy_(tokens)
+        self.graph.replay()
+        return self.g_out, self.g_logits
+
+    def release_graph(self):
+        """Drops the captured graph (before the process group goes away)."""
+        self.graph = None
+        self.g_out = self.g_logits = None
+
