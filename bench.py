@@ -396,8 +396,7 @@ def bench_model(m, torch, device, args, rank, world, dist) -> dict | None:
     sync()
     step_split = M.profile.totals_ms()
     M.profile = None
-    if graphed:
-        M.release_graph()
+    M.close()
     if m.device_status(torch.cuda.current_device()) != 0:
         raise SystemExit("device status reported an error during the model leg")
     if rank != 0:

@@ -239,6 +239,41 @@ int mslim_cuda_swiglu_rows(const void *gate_up, void *out, uint32_t rows, uint32
 int mslim_cuda_argmax(const void *logits, uint32_t rows, uint32_t vocab, int ties_to_last,
                       int32_t *token_ids, void *stream);
 
+/* ------------------------------------------- tensor-parallel decode -- */
+
+/* Communicator of one rank of a tensor-parallel group (at most 8 ranks, one
+ * GPU each), built once by the host: every rank allocates its regions with
+ * mslim_cuda_tp_alloc, exports them with mslim_cuda_ipc_handle, and maps the
+ * peers' with mslim_cuda_ipc_open (handles travel over any host channel).
+ *   data[r]:  rank r's bf16 [2][max_rows][hidden] partial-sum slots;
+ *   flags[r]: rank r's uint32 [max_rows][8] ready counters (zeroed);
+ *   epoch:    this rank's uint32 [max_rows] call counters (zeroed).
+ * No reference counterpart: the reference runs on one iGPU; the north star's
+ * KV-head tensor parallelism needs the per-layer reduction. */
+typedef struct {
+    uint32_t world, rank, max_rows, hidden;
+    void *data[8];
+    void *flags[8];
+    void *epoch;
+} mslim_tp_comm_t;
+
+int mslim_cuda_tp_alloc(size_t bytes, void **ptr);   /* zero-filled device memory */
+int mslim_cuda_tp_free(void *ptr);
+int mslim_cuda_ipc_handle(const void *ptr, void *handle /* 64 bytes */);
+int mslim_cuda_ipc_open(const void *handle /* 64 bytes */, void **ptr);
+int mslim_cuda_ipc_close(void *ptr);
+
+/* The collective after a row-parallel projection of the decode step, fused
+ * with what run_layer does next (residual add, RMSNorm): for rows [0, rows),
+ * x = bf16(x + bf16(sum over ranks r of data[r][slot][row])) and
+ * y = RMSNorm(x, w), every rank computing identical bits (fp32 sum in rank
+ * order).  The caller writes its own partial into data[rank][slot] first and
+ * alternates slot 0/1 from call to call.  Waits on peers are bounded; a rank
+ * that never arrives is reported by mslim_cuda_device_status and leaves x, y
+ * untouched. */
+int mslim_cuda_tp_allreduce_rmsnorm(const mslim_tp_comm_t *comm, uint32_t slot, void *x, const void *w,
+                                    void *y, uint32_t rows, float eps, void *stream);
+
 /* ------------------------------------------------------ prologue -- */
 
 /* GpuEngine::norm / BatchKernels::norm (src/gpu_llm/gpu_resources.rs:485-507,

@@ -23,6 +23,7 @@
 #include "decode.cuh"
 #include "prefill.cuh"
 #include "layer_ops.cuh"
+#include "tp_allreduce.cuh"
 #include "prologue.cuh"
 
 // One status word per device; kernels record bounded-wait timeouts here.
@@ -776,6 +777,90 @@ int mslim_cuda_argmax(const void *logits, uint32_t rows, uint32_t vocab, int tie
     cudaError_t err = mslim::launch_argmax(static_cast<const uint16_t *>(logits), rows, vocab,
                                            ties_to_last, token_ids, static_cast<cudaStream_t>(stream));
     return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "argmax launch");
+}
+
+// ------------------------------------------------ tensor-parallel decode --
+
+int mslim_cuda_tp_alloc(size_t bytes, void **ptr) {
+    if (!ptr) return fail(MSLIM_ERR_SHAPE_MISMATCH, "null pointer slot");
+    *ptr = nullptr;
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    if (bytes == 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty allocation");
+    cudaError_t err = cudaMalloc(ptr, bytes);
+    if (err != cudaSuccess) return cuda_fail(err, "tensor-parallel buffer allocation");
+    err = cudaMemset(*ptr, 0, bytes);
+    if (err != cudaSuccess) {
+        cudaFree(*ptr);
+        *ptr = nullptr;
+        return cuda_fail(err, "tensor-parallel buffer clear");
+    }
+    return MSLIM_OK;
+}
+
+int mslim_cuda_tp_free(void *ptr) {
+    if (!ptr) return MSLIM_OK;
+    cudaError_t err = cudaFree(ptr);
+    return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "tensor-parallel buffer free");
+}
+
+int mslim_cuda_ipc_handle(const void *ptr, void *handle) {
+    if (!ptr || !handle) return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    cudaIpcMemHandle_t h;
+    cudaError_t err = cudaIpcGetMemHandle(&h, const_cast<void *>(ptr));
+    if (err != cudaSuccess) return cuda_fail(err, "IPC handle export");
+    std::memcpy(handle, &h, sizeof(h));
+    return MSLIM_OK;
+}
+
+int mslim_cuda_ipc_open(const void *handle, void **ptr) {
+    if (!handle || !ptr) return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
+    *ptr = nullptr;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    cudaError_t err = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "IPC handle open");
+}
+
+int mslim_cuda_ipc_close(void *ptr) {
+    if (!ptr) return MSLIM_OK;
+    cudaError_t err = cudaIpcCloseMemHandle(ptr);
+    return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "IPC handle close");
+}
+
+int mslim_cuda_tp_allreduce_rmsnorm(const mslim_tp_comm_t *comm, uint32_t slot, void *x, const void *w,
+                                    void *y, uint32_t rows, float eps, void *stream) {
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    if (!comm || !x || !w || !y) return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
+    if (comm->world == 0 || comm->world > (uint32_t)mslim::kTpMaxWorld || comm->rank >= comm->world)
+        return fail(MSLIM_ERR_INVALID_CONFIG, "tensor-parallel world of 1..8 ranks");
+    if (slot > 1) return fail(MSLIM_ERR_SHAPE_MISMATCH, "slot is 0 or 1");
+    if (rows == 0) return MSLIM_OK;
+    if (rows > comm->max_rows) return fail(MSLIM_ERR_SHAPE_MISMATCH, "more rows than the communicator holds");
+    if (comm->hidden == 0 || comm->hidden % 8 != 0)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "hidden size must be a positive multiple of 8");
+    if (!std::isfinite(eps) || eps < 0.f) return fail(MSLIM_ERR_INVALID_CONFIG, "invalid epsilon");
+    if (!aligned(x, 16) || !aligned(w, 16) || !aligned(y, 16) || !comm->epoch)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "buffers must be 16-byte aligned");
+    mslim::TpCommDev d{};
+    d.world = comm->world;
+    d.rank = comm->rank;
+    d.max_rows = comm->max_rows;
+    d.hidden = comm->hidden;
+    for (uint32_t r = 0; r < comm->world; ++r) {
+        if (!comm->data[r] || !comm->flags[r] || !aligned(comm->data[r], 16))
+            return fail(MSLIM_ERR_SHAPE_MISMATCH, "rank %u of the communicator is not mapped", r);
+        d.data[r] = static_cast<const uint16_t *>(comm->data[r]);
+        d.flags[r] = static_cast<uint32_t *>(comm->flags[r]);
+    }
+    d.epoch = static_cast<uint32_t *>(comm->epoch);
+    cudaError_t err = mslim::launch_tp_allreduce_rmsnorm(d, slot, static_cast<uint16_t *>(x),
+                                                         static_cast<const uint16_t *>(w),
+                                                         static_cast<uint16_t *>(y), rows, eps, status_ptr(dev),
+                                                         static_cast<cudaStream_t>(stream));
+    return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "tensor-parallel all-reduce launch");
 }
 
 // ---------------------------------------------------------- prologue --

@@ -33,6 +33,12 @@ class KernelConfig(ctypes.Structure):
                 ("splits", ctypes.c_uint32)]
 
 
+class TpComm(ctypes.Structure):
+    _fields_ = [("world", ctypes.c_uint32), ("rank", ctypes.c_uint32), ("max_rows", ctypes.c_uint32),
+                ("hidden", ctypes.c_uint32), ("data", ctypes.c_void_p * 8), ("flags", ctypes.c_void_p * 8),
+                ("epoch", ctypes.c_void_p)]
+
+
 class RopeConfig(ctypes.Structure):
     _fields_ = [("theta", ctypes.c_float), ("llama3_scaling", ctypes.c_uint32),
                 ("factor", ctypes.c_float), ("low_freq_factor", ctypes.c_float),
@@ -88,6 +94,13 @@ SIGNATURES = {
                                                    _u32, _vp, _u32, _vp]),
     "mslim_cuda_rope_append_decode_dense": (_int, [_G, _vp, _vp, _vp, _vp, _vp, _u32, _R, _vp, _vp, _u32,
                                                    _vp]),
+    "mslim_cuda_tp_alloc": (_int, [_sz, ctypes.POINTER(_vp)]),
+    "mslim_cuda_tp_free": (_int, [_vp]),
+    "mslim_cuda_ipc_handle": (_int, [_vp, _vp]),
+    "mslim_cuda_ipc_open": (_int, [_vp, ctypes.POINTER(_vp)]),
+    "mslim_cuda_ipc_close": (_int, [_vp]),
+    "mslim_cuda_tp_allreduce_rmsnorm": (_int, [ctypes.POINTER(TpComm), _u32, _vp, _vp, _vp, _u32, ctypes.c_float,
+                                               _vp]),
     "mslim_cuda_backend_create": (_int, [_int, ctypes.POINTER(_vp)]),
     "mslim_cuda_backend_destroy": (None, [_vp]),
     "mslim_cuda_backend_decode": (_int, [_vp, _G, _vp, _vp, _vp, _int, _u32, _vp]),

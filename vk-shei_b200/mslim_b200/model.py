@@ -163,6 +163,12 @@ class DeviceModel:
         self.workspace = torch.empty(max(ws, 16), dtype=torch.uint8, device=dev)
         self.lengths = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.profile = None   # a SectionTimer splits the device time by kind of step
+        # decode-step reductions over NVLink peer memory (fused with the
+        # residual add and RMSNorm); prefill reduces through NCCL
+        self.comm = None
+        if tp_world > 1:
+            from .tp import TpComm
+            self.comm = TpComm(tp_world, tp_rank, batch, L.hidden, group)
 
     # ------------------------------------------------------------ pieces --
     def _sec(self, kind):
@@ -198,24 +204,38 @@ class DeviceModel:
             _att.residual_rmsnorm(x, delta, w, out, x.shape[0], self.spec.layer.hidden, self.spec.layer.eps)
         return out
 
-    def _after_attention(self, li, x, attn):
-        """o-projection (+ all-reduce), residual, MLP (+ all-reduce when
+    def _reduce_residual_norm(self, inp, w_proj, x, w_norm, reduce: bool, fused: bool):
+        """x += (sum over ranks of) inp @ w_proj^T; returns RMSNorm(x, w_norm).
+        fused: the GEMM writes this rank's partial into the communicator slot
+        and one kernel reduces over NVLink, adds and normalises (decode);
+        otherwise NCCL all-reduce then the fused residual + RMSNorm."""
+        rows = x.shape[0]
+        if reduce and fused and self.comm is not None:
+            slot = self.comm.next_slot()
+            with self._sec("gemm"):
+                self.torch.matmul(inp, w_proj.t(), out=self.comm.slot(slot, rows))
+            out = self.torch.empty_like(x)
+            with self._sec("collective"):
+                self.comm.allreduce_rmsnorm(slot, x, w_norm, out, rows, self.spec.layer.eps)
+            return out
+        y = self._gemm(inp, w_proj)
+        if reduce:
+            self._all_reduce(y)
+        return self._residual_norm(x, y, w_norm)
+
+    def _after_attention(self, li, x, attn, fused: bool = False):
+        """o-projection (+ reduction), residual, MLP (+ reduction when
         sharded), residual; returns the next layer's normalised input (the
         final norm after the last layer)."""
         t = self.torch
         W = self.layers[li]
-        o = self._gemm(attn.reshape(x.shape[0], -1), W["wo"])
-        self._all_reduce(o)
-        n2 = self._residual_norm(x, o, W["post_norm"])
+        n2 = self._reduce_residual_norm(attn.reshape(x.shape[0], -1), W["wo"], x, W["post_norm"], True, fused)
         gu = self._gemm(n2, W["wgu"])
         act = t.empty((x.shape[0], self.inter), dtype=x.dtype, device=self.device)
         with self._sec("elementwise"):
             _att.swiglu_rows(gu, act, x.shape[0], self.inter)
-        d = self._gemm(act, W["wd"])
-        if self.mlp == "sharded":
-            self._all_reduce(d)
         nxt = self.layers[li + 1]["in_norm"] if li + 1 < len(self.layers) else self.final_norm
-        return self._residual_norm(x, d, nxt)
+        return self._reduce_residual_norm(act, W["wd"], x, nxt, self.mlp == "sharded", fused)
 
     def _lm_head_argmax(self, n_final):
         """n_final: final-normed bf16 [batch][hidden] -> (int32 ids, bf16 logits
@@ -314,7 +334,7 @@ class DeviceModel:
                     _att.decode_paged(self.geometry, q_r, self.k_pool[li], self.v_pool[li], self.n_pages,
                                       self.page_tokens, self.page_table, self.max_pages, seq, B,
                                       self.workspace, attn)
-            n = self._after_attention(li, x, attn)
+            n = self._after_attention(li, x, attn, fused=True)
         with self._sec("elementwise"):
             self.lengths.add_(1)
         return self._lm_head_argmax(n)
@@ -347,4 +367,16 @@ class DeviceModel:
         """Drops the captured graph (before the process group goes away)."""
         self.graph = None
         self.g_out = self.g_logits = None
+
+    def close(self):
+        """Releases the graph and the communicator's peer mappings (call on
+        every rank, before the process group is destroyed)."""
+        self.release_graph()
+        if self.comm is not None:
+            if self.world > 1:
+                import torch.distributed as dist
+                self.torch.cuda.synchronize()
+                dist.barrier(group=self.group)
+            self.comm.close()
+            self.comm = None
 
