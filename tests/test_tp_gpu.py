@@ -119,3 +119,43 @@ def test_two_ranks_agree_and_sum_in_rank_order(oracle):
     delta = oracle.bf16_from_f32(f(parts[0]) + f(parts[1]))
     xn = oracle.bf16_from_f32(f(x) + f(delta))
     assert np.array_equal(outs0[0][0].reshape(-1), xn)
+
+
+def test_a_peer_that_never_arrives_times_out_and_the_context_survives():
+    """Failure detection without a fault: a two-rank communicator whose second
+    rank is never run (its slots alias this rank's, its ready counter is never
+    written).  The kernel's bounded wait gives up (~2 s), records a timeout in
+    the status word, leaves x and y untouched, and the context stays usable."""
+    import ctypes
+
+    import torch
+    import mslim_b200 as m
+    from gpu_util import dev
+    from mslim_b200 import _lib
+    from mslim_b200.tp import TpComm
+    rng = np.random.default_rng(31)
+    comm = TpComm(1, 0, ROWS, HIDDEN)
+    try:
+        c = _lib.TpComm()
+        ctypes.memmove(ctypes.byref(c), ctypes.byref(comm.c), ctypes.sizeof(c))
+        c.world = 2
+        c.data[1], c.flags[1] = comm.c.data[0], comm.c.flags[0]
+        x = dev(_bf16(rng, ROWS * HIDDEN).reshape(ROWS, HIDDEN))
+        x_before = _u16(x)
+        y = torch.zeros_like(x)
+        w = dev(_bf16(rng, HIDDEN))
+        assert m.device_status(0) == 0
+        m.check(_lib.lib().mslim_cuda_tp_allreduce_rmsnorm(ctypes.byref(c), 0, x.data_ptr(), w.data_ptr(),
+                                                           y.data_ptr(), ROWS, EPS,
+                                                           torch.cuda.current_stream().cuda_stream))
+        assert m.device_status(0) == _lib.ERR_DEVICE_TIMEOUT
+        assert np.array_equal(_u16(x), x_before) and not _u16(y).any()
+        # the context is intact: other kernels still run and the status is clear
+        a = dev(_bf16(rng, 1024))
+        out = torch.empty_like(a)
+        m.residual_add(a, a, out, 1024)
+        torch.cuda.synchronize()
+        assert m.device_status(0) == 0
+    finally:
+        torch.cuda.synchronize()
+        comm.close()

@@ -79,6 +79,21 @@ class _NoSection:
 _NO_SECTION = _NoSection()
 
 
+def shard_argmax_key(torch, bits, local_ids, vocab_lo: int):
+    """One int64 per row ordering a vocabulary shard's maximum: the
+    f32::total_cmp key of its bf16 value (bits, int16) above its global index,
+    so the largest key wins and, among equal values, the larger index (the CPU
+    path's last-maximal-index rule, native_cpu_adapter.rs:582-587)."""
+    b = bits.to(torch.int32)
+    key = torch.where(b < 0, b ^ 0x7FFF, b)
+    return (key.to(torch.int64) << 32) | (local_ids.to(torch.int64) + vocab_lo)
+
+
+def pick_shard_argmax(torch, every):
+    """every: int64 [ranks][rows] of shard_argmax_key -> int32 global token ids."""
+    return (every.max(dim=0).values & 0xFFFFFFFF).to(torch.int32)
+
+
 class DeviceModel:
     def __init__(self, spec: ModelSpec, batch: int, capacity: int, seed: int = 5, tp_rank: int = 0,
                  tp_world: int = 1, mlp: str = "sharded", kv_mode: str = "dense", page_tokens: int = 256,
@@ -253,15 +268,13 @@ class DeviceModel:
             return ids, logits
         import torch.distributed as dist
         with self._sec("elementwise"):
-            bits = logits.gather(1, ids.long().view(B, 1)).view(t.int16).to(t.int32).view(B)
-            # f32::total_cmp key of the bf16 value (signed-magnitude flip)
-            key = t.where(bits < 0, bits ^ 0x7FFF, bits)
-            mine = (key.to(t.int64) << 32) | (ids.to(t.int64) + self.vocab_lo)
+            bits = logits.gather(1, ids.long().view(B, 1)).view(t.int16).view(B)
+            mine = shard_argmax_key(t, bits, ids, self.vocab_lo)
             every = t.empty((self.world, B), dtype=t.int64, device=self.device)
         with self._sec("collective"):
             dist.all_gather_into_tensor(every, mine, group=self.group)
         with self._sec("elementwise"):
-            best = (every.max(dim=0).values & 0xFFFFFFFF).to(t.int32)
+            best = pick_shard_argmax(t, every)
         return best, logits
 
     # ----------------------------------------------------------- prefill --
