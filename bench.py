@@ -63,6 +63,8 @@ def parse():
     ap.add_argument("--mlp", choices=["sharded", "replicated"], default="sharded")
     ap.add_argument("--kv-mode", choices=["dense", "coldstore"], default="dense")
     ap.add_argument("--no-graph", action="store_true", help="C5 decode steps issued eagerly (no CUDA graph)")
+    ap.add_argument("--layer", action="store_true",
+                    help="C3: one Llama-3-8B layer, 512-token prefill + 8 decode steps, CPU path beside it")
     return ap.parse_args()
 
 
@@ -329,6 +331,69 @@ def bench_prefill(m, torch, device, args) -> dict:
             "gpu_launches": steps, "clocks": clocks}
 
 
+def bench_layer(m, torch, device, args) -> dict:
+    """C3: one Llama-3-8B-shaped layer, 512-token
+    prefill then 8 forced decode steps, dense KV and ColdStore-exact KV, device
+    time by CUDA events; the CPU decoder (oracle forward_token, one layer) is
+    timed beside it on a bounded sample of the same tokens."""
+    import hashlib
+
+    import numpy as np
+    from mslim_b200 import layer as lay
+    sys.path.insert(0, ROOT)
+    from oracle import oracle as orc
+
+    P, steps, seed = 512, 8, 2
+    spec = lay.LayerSpec()
+    weights = lay.random_layer_weights(spec, seed)
+    ids = np.random.default_rng(seed).integers(0, 128256, size=P + steps)
+    emb = lay.embedding_rows(ids, spec.hidden, seed)
+    x = torch.from_numpy(emb.view(np.int16)).to(device).view(torch.bfloat16)
+    out = {}
+    for mode in ("dense", "coldstore"):
+        times = []
+        for rep in range(max(args.warmup, 3) + 5):
+            L = lay.DeviceLayer(spec, weights, P + steps, kv_mode=mode, page_tokens=256, page_seed=seed)
+            torch.cuda.synchronize()
+            e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            e0.record()
+            y, *_ = L.prefill(x[:P])
+            e1.record()
+            ys = [L.decode(x[P + i:P + i + 1])[0] for i in range(steps)]
+            e2.record()
+            torch.cuda.synchronize()
+            if rep >= max(args.warmup, 3):
+                times.append((e0.elapsed_time(e1), e1.elapsed_time(e2)))
+            last = torch.cat([y] + ys).view(torch.int16).cpu().numpy()
+            del L
+        pf = statistics.median(t[0] for t in times)
+        dc = statistics.median(t[1] for t in times)
+        out[mode] = {"prefill_ms": pf, "prefill_tokens_per_s": P / (pf * 1e-3),
+                     "decode_ms_per_step": dc / steps, "decode_tokens_per_s": steps / (dc * 1e-3),
+                     "outputs_sha256": hashlib.sha256(last.tobytes()).hexdigest()}
+    # the CPU decoder on the first tokens of the same prompt (all host threads)
+    lo = orc.LayerOracle(weights, spec.hidden, spec.intermediate, spec.query_heads, spec.kv_heads,
+                         spec.head_dim, spec.eps, spec.theta, P + steps)
+    xf = orc.bf16_to_f32(emb).reshape(emb.shape)
+    t0 = time.time()
+    n = 0
+    while n < P and (n < 8 or time.time() - t0 < args.cpu_seconds):
+        lo.forward(xf[n])
+        n += 1
+    cpu_s = time.time() - t0
+    return {
+        "metric": "C3 one-layer tokens/s (Llama-3-8B layer, 512-token prefill + 8 decode steps)",
+        "value": out["dense"]["prefill_tokens_per_s"], "unit": "tokens/s", "n_gpus": 1,
+        "dtype": "bf16", "data": "synthetic (seed 2: N(0,0.02) projections, norms 1, N(0,1) embedding rows)",
+        "config": {"workload": "C3", "prefill": P, "decode_steps": steps},
+        "dense": out["dense"], "coldstore": out["coldstore"],
+        "dense_equals_coldstore": out["dense"]["outputs_sha256"] == out["coldstore"]["outputs_sha256"],
+        "cpu_baseline": {"value": n / cpu_s, "unit": "tokens/s", "cores": orc.max_threads(), "kind": "port",
+                         "sample": f"the first {n} prompt tokens through oracle forward_token (one layer), "
+                                   f"{cpu_s:.1f} s"},
+    }
+
+
 def bench_model(m, torch, device, args, rank, world, dist) -> dict | None:
     """C5: a Llama-3-8B-shaped decoder with random
     weights, batch 8, 8192-token prefill then 256 greedy decode steps,
@@ -461,6 +526,9 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device(device))
     m.load()
+    if args.layer:
+        print(json.dumps(bench_layer(m, torch, device, args)), flush=True)
+        return
     if args.model:
         line = bench_model(m, torch, device, args, rank, world, dist)
         if line is not None:
