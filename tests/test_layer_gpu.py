@@ -3,7 +3,7 @@ device, 512-token prefill then 8 forced decode steps, against the CPU
 restatement of forward_token (oracle/mslim_oracle.c, native_cpu_adapter.rs:
 486-577), plus the elementwise layer kernels (residual add, SwiGLU, argmax).
 
-Gates (north star / SURVEY C3): dense KV == ColdStore-exact KV bitwise on the
+Gates (the north star for C3): dense KV == ColdStore-exact KV bitwise on the
 device path; attention outputs within max-abs 2e-2 of the CPU path."""
 import numpy as np
 import pytest
