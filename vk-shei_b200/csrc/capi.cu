@@ -189,11 +189,14 @@ int decode_shape(const mslim_geometry_t *g, uint32_t nq, DecodeShapeInfo *s) {
 
 // Split policy: aim for about eight waves of two CTAs per SM, with splits of
 // 64..2048 tokens (multiples of the 64-token TMA stage).
+// Tokens per split: about eight waves of two CTAs per SM over all (session,
+// KV-head chunk) items, at least 256 tokens (four pipeline stages, so a CTA's
+// setup is amortised and the merge combines few partials) and at most 2048.
 uint32_t policy_split_tokens(uint64_t work_items, uint64_t max_tokens) {
     const uint64_t target = 148ull * 2 * 8;
     uint64_t st = (work_items * max_tokens + target - 1) / target;
     st = (st + 63) / 64 * 64;
-    return (uint32_t)std::min<uint64_t>(std::max<uint64_t>(st, 64), 2048);
+    return (uint32_t)std::min<uint64_t>(std::max<uint64_t>(st, 256), 2048);
 }
 
 // The kernel runs at the next head_dim in {64, 128, 256}; the caller's

@@ -387,7 +387,27 @@ __global__ void __launch_bounds__(128) mslim_decode_merge(const DecodeParams p, 
     float acc[kPer];
 #pragma unroll
     for (int k = 0; k < kPer; ++k) acc[k] = 0.f;
-    for (int s = 0; s < splits; ++s) {
+    // splits in order; four at a time have their loads in flight together
+    int s = 0;
+    for (; s + 4 <= splits; s += 4) {
+        float mv[4], lv[4], pv[4][kPer];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const float *part = src + (s + u) * kRowF;
+            mv[u] = part[D];
+            lv[u] = part[D + 1];
+#pragma unroll
+            for (int k = 0; k < kPer; ++k) pv[u][k] = part[lane + 32 * k];
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const float w = fast_exp2(mv[u] - mb);
+            l += w * lv[u];
+#pragma unroll
+            for (int k = 0; k < kPer; ++k) acc[k] += w * pv[u][k];
+        }
+    }
+    for (; s < splits; ++s) {
         const float *part = src + s * kRowF;
         const float w = fast_exp2(part[D] - mb);
         l += w * part[D + 1];

@@ -3,10 +3,10 @@
 // run_layer split over KV-head groups) reduced over NVLink peer memory inside
 // the kernel that applies the residual add and the next RMSNorm.
 //
-// One CTA per row (decode: one row per session).  Thread 0 makes this rank's
-// partial visible at system scope, publishes the row's call number into every
-// rank's flag slot for this rank, and waits (bounded by %globaltimer) until
-// every rank's number has arrived in its own flags.  Then the CTA reads the row
+// One CTA per row (decode: one row per session).  Lane r of warp 0 makes this
+// rank's partial visible at system scope, publishes the row's call number into
+// rank r's flag slot for this rank, and waits (bounded by %globaltimer) until
+// rank r's number has arrived in this rank's flags.  Then the CTA reads the row
 // from every rank with plain 16-byte loads that fetch afresh (ld.cv: the slot
 // addresses repeat every second call), sums in fp32 in rank
 // order (so every rank computes identical bits), rounds once to bf16, adds the
@@ -38,6 +38,11 @@ __device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" 
 
 __device__ __forceinline__ void nano_sleep(uint32_t ns) { asm volatile("nanosleep.u32 %0;" ::"r"(ns)); }
 
+__device__ __forceinline__ void st_relaxed_sys(uint32_t *p, uint32_t v) {
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+template <int W>
 __global__ void __launch_bounds__(kTpThreads)
     mslim_tp_allreduce_rmsnorm(const TpCommDev c, uint32_t slot, uint16_t *__restrict__ x,
                                const uint16_t *__restrict__ w, uint16_t *__restrict__ y, float eps,
@@ -45,25 +50,32 @@ __global__ void __launch_bounds__(kTpThreads)
     const uint32_t row = blockIdx.x;
     const uint32_t hidden = c.hidden;
     __shared__ int s_ok;
-    if (threadIdx.x == 0) {
+    // warp 0: lane r (< W) publishes this rank's call number into rank r's
+    // flags, then waits for rank r's number in this rank's flags; the lanes
+    // work in parallel, each behind its own system-scope fence
+    if (threadIdx.x < 32) {
+        const uint32_t lane = threadIdx.x;
         const uint32_t e = c.epoch[row] + 1;
-        fence_sys();  // this rank's partial (written by earlier kernels) before its flag
-        for (uint32_t r = 0; r < c.world; ++r) st_release_sys(c.flags[r] + row * kTpMaxWorld + c.rank, e);
         int ok = 1;
-        const uint64_t start = globaltimer();
-        for (uint32_t r = 0; r < c.world && ok; ++r) {
-            const uint32_t *f = c.flags[c.rank] + row * kTpMaxWorld + r;
-            while (ld_acquire_sys(f) < e) {  // counters only grow; a peer may be one call ahead
+        if (lane < W) {
+            fence_sys();   // this rank's partial (written by earlier kernels) before its number
+            st_relaxed_sys(c.flags[lane] + row * kTpMaxWorld + c.rank, e);
+            const uint32_t *f = c.flags[c.rank] + row * kTpMaxWorld + lane;
+            const uint64_t start = globaltimer();
+            while (ld_acquire_sys(f) < e) {   // counters only grow; a peer may be one call ahead
                 if (globaltimer() - start > kTpWaitBoundNs) {
-                    record_timeout(status, 80 + (int)r);
+                    record_timeout(status, 80 + (int)lane);
                     ok = 0;
                     break;
                 }
-                nano_sleep(32);
+                nano_sleep(20);
             }
         }
-        c.epoch[row] = e;
-        s_ok = ok;
+        ok = __all_sync(0xffffffffu, ok);
+        if (lane == 0) {
+            c.epoch[row] = e;
+            s_ok = ok;
+        }
     }
     __syncthreads();
     if (!s_ok) return;   // reported through the status word; x and y untouched
@@ -73,10 +85,14 @@ __global__ void __launch_bounds__(kTpThreads)
     uint16_t *yr = y + (size_t)row * hidden;
     float sum = 0.f;
     for (uint32_t i = threadIdx.x * 8; i < hidden; i += kTpThreads * 8) {
+        // every rank's chunk in flight at once, summed in rank order
+        uint4 p[W];
+#pragma unroll
+        for (int r = 0; r < W; ++r) p[r] = __ldcv(reinterpret_cast<const uint4 *>(c.data[r] + off + i));
         float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        for (uint32_t r = 0; r < c.world; ++r) {
-            const uint4 p = __ldcv(reinterpret_cast<const uint4 *>(c.data[r] + off + i));
-            const uint32_t pv[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+        for (int r = 0; r < W; ++r) {
+            const uint32_t pv[4] = {p[r].x, p[r].y, p[r].z, p[r].w};
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 acc[2 * k] += bf16lo_f32(pv[k]);
@@ -127,7 +143,17 @@ __global__ void __launch_bounds__(kTpThreads)
 cudaError_t launch_tp_allreduce_rmsnorm(const TpCommDev &comm, uint32_t slot, uint16_t *x,
                                         const uint16_t *w, uint16_t *y, uint32_t rows, float eps,
                                         int *status, cudaStream_t stream) {
-    mslim_tp_allreduce_rmsnorm<<<rows, kTpThreads, 0, stream>>>(comm, slot, x, w, y, eps, status);
+    switch (comm.world) {
+    case 1: mslim_tp_allreduce_rmsnorm<1><<<rows, kTpThreads, 0, stream>>>(comm, slot, x, w, y, eps, status); break;
+    case 2: mslim_tp_allreduce_rmsnorm<2><<<rows, kTpThreads, 0, stream>>>(comm, slot, x, w, y, eps, status); break;
+    case 3: mslim_tp_allreduce_rmsnorm<3><<<rows, kTpThreads, 0, stream>>>(comm, slot, x, w, y, eps, status); break;
+    case 4: mslim_tp_allreduce_rmsnorm<4><<<rows, kTpThreads, 0, stream>>>(comm, slot, x, w, y, eps, status); break;
+    case 5: mslim_tp_allreduce_rmsnorm<5><<<rows, kTpThreads, 0, stream>>>(comm, slot, x, w, y, eps, status); break;
+    case 6: mslim_tp_allreduce_rmsnorm<6><<<rows, kTpThreads, 0, stream>>>(comm, slot, x, w, y, eps, status); break;
+    case 7: mslim_tp_allreduce_rmsnorm<7><<<rows, kTpThreads, 0, stream>>>(comm, slot, x, w, y, eps, status); break;
+    case 8: mslim_tp_allreduce_rmsnorm<8><<<rows, kTpThreads, 0, stream>>>(comm, slot, x, w, y, eps, status); break;
+    default: return cudaErrorInvalidValue;
+    }
     return cudaGetLastError();
 }
 
