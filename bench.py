@@ -63,6 +63,8 @@ def parse():
     ap.add_argument("--mlp", choices=["sharded", "replicated"], default="sharded")
     ap.add_argument("--kv-mode", choices=["dense", "coldstore"], default="dense")
     ap.add_argument("--no-graph", action="store_true", help="C5 decode steps issued eagerly (no CUDA graph)")
+    ap.add_argument("--decode-gemm", choices=["own", "cublas"], default="cublas",
+                    help="C5 decode projections: cuBLAS (default) or mslim_cuda_gemv")
     ap.add_argument("--layer", action="store_true",
                     help="C3: one Llama-3-8B layer, 512-token prefill + 8 decode steps, CPU path beside it")
     return ap.parse_args()
@@ -412,7 +414,7 @@ def bench_model(m, torch, device, args, rank, world, dist) -> dict | None:
     L = spec.layer
     t0 = time.time()
     M = mdl.DeviceModel(spec, B, S + steps + 4, seed=5, tp_rank=rank, tp_world=world, mlp=args.mlp,
-                        kv_mode=args.kv_mode)
+                        kv_mode=args.kv_mode, decode_gemm=args.decode_gemm)
     build_s = time.time() - t0
     ids = torch.from_numpy(np.random.default_rng(5).integers(0, spec.vocab, size=(B, S))).to(device)
 
@@ -481,7 +483,8 @@ def bench_model(m, torch, device, args, rank, world, dist) -> dict | None:
         "config": {"workload": "C5", "layers": spec.layers, "batch": B, "prefill": S, "decode_steps": steps,
                    "parallelism": f"tp{world} by KV-head group, MLP {args.mlp}", "kv": args.kv_mode,
                    "allreduce_per_layer": 1 if args.mlp == "replicated" else 2,
-                   "decode_issue": "one CUDA graph per step" if graphed else "eager"},
+                   "decode_issue": "one CUDA graph per step" if graphed else "eager",
+                   "decode_projections": "mslim_cuda_gemv" if args.decode_gemm == "own" else "cuBLAS"},
         "prefill_ms": prefill_ms, "prefill_tokens_per_s": B * S / (prefill_ms * 1e-3),
         "decode_ms_per_step": decode_ms / steps,
         "decode_step_split_ms": step_split,

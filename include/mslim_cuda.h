@@ -224,6 +224,13 @@ int mslim_cuda_residual_add(const void *a, const void *b, void *out, uint64_t n,
  * out = bf16(bf16(g / (1 + exp(-g))) * u); out may alias gate or up. */
 int mslim_cuda_swiglu(const void *gate, const void *up, void *out, uint64_t n, void *stream);
 
+/* A projection of the decode step (GpuEngine's GEMVs, llm_gemv_bf16*,
+ * assets/gpu_llm.cl:38-68, for a few sessions at once): y[m][n] =
+ * bf16(sum_k x[m][k] * w[n][k]), fp32 accumulation, the weights streamed once.
+ * x: bf16 [m][k], w: bf16 [n][k] (the HF [out][in] layout), y: bf16 [m][n];
+ * 1 <= m <= 16, n % 8 == 0, k % 128 == 0, 16-byte aligned. */
+int mslim_cuda_gemv(const void *x, const void *w, void *y, uint32_t m, uint32_t n, uint32_t k, void *stream);
+
 /* SwiGLU over a fused gate|up projection (no reference counterpart: the
  * reference keeps gate and up in separate buffers, GpuEngine::swiglu):
  * gate_up bf16 [rows][gate (width) | up (width)], out bf16 [rows][width],

@@ -250,3 +250,20 @@ def test_fused_qkv_append_matches_separate_inputs(paged):
     for a, b in zip(*outs):
         assert np.array_equal(a, b)
     assert m.device_status(0) == 0
+
+
+@pytest.mark.parametrize("m,n,k", [(8, 6144, 4096), (8, 4096, 512), (8, 28672, 4096), (8, 4096, 14336),
+                                   (3, 1024, 1792), (16, 520, 256), (1, 8, 128)])
+def test_gemv_matches_fp32_reference(m, n, k):
+    import torch
+    import mslim_b200 as mm
+    rng = np.random.default_rng(m * 7 + n + k)
+    x = _rand_bf16(rng, m * k).reshape(m, k)
+    w = _rand_bf16(rng, n * k, 0.02).reshape(n, k)
+    y = torch.empty((m, n), dtype=torch.int16, device="cuda:0")
+    mm.gemv(dev(x), dev(w), y, m, n, k)
+    ref = bf16_f32(x).astype(np.float64) @ bf16_f32(w).astype(np.float64).T
+    got = bf16_f32(u16(y))
+    # one bf16 rounding of an fp32 sum: within ~1 ulp of the exact value
+    tol = np.abs(ref) * 2.0 ** -7 + 1e-6 * np.sqrt(k)
+    assert (np.abs(got - ref) <= tol).all(), np.abs(got - ref).max()

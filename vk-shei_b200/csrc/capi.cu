@@ -755,6 +755,21 @@ int mslim_cuda_swiglu(const void *gate, const void *up, void *out, uint64_t n, v
     return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "SwiGLU launch");
 }
 
+int mslim_cuda_gemv(const void *x, const void *w, void *y, uint32_t m, uint32_t n, uint32_t k, void *stream) {
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    if (!x || !w || !y) return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
+    if (m == 0 || m > 16) return fail(MSLIM_ERR_SHAPE_MISMATCH, "the decode projection takes 1..16 rows");
+    if (n == 0 || n % 8 != 0 || k == 0 || k % 128 != 0)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "n must be a multiple of 8 and k of 128");
+    if (!aligned(x, 16) || !aligned(w, 16) || !aligned(y, 16))
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "projection buffers must be 16-byte aligned");
+    if (y == x || y == w) return fail(MSLIM_ERR_SHAPE_MISMATCH, "the output must not alias an input");
+    cudaError_t err = mslim::launch_gemv(static_cast<const uint16_t *>(x), static_cast<const uint16_t *>(w),
+                                         static_cast<uint16_t *>(y), m, n, k, static_cast<cudaStream_t>(stream));
+    return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "projection launch");
+}
+
 int mslim_cuda_swiglu_rows(const void *gate_up, void *out, uint32_t rows, uint32_t width, void *stream) {
     int dev;
     if (int rc = current_device(&dev)) return rc;

@@ -313,6 +313,11 @@ def swiglu(gate, up, out, n: int, stream=None) -> None:
     check(_lib.lib().mslim_cuda_swiglu(_ptr(gate), _ptr(up), _ptr(out), n, _stream(stream)))
 
 
+def gemv(x, w, y, m: int, n: int, k: int, stream=None) -> None:
+    """y[m][n] = bf16(x[m][k] . w[n][k]) for 1..16 rows (the decode projections)."""
+    check(_lib.lib().mslim_cuda_gemv(_ptr(x), _ptr(w), _ptr(y), m, n, k, _stream(stream)))
+
+
 def swiglu_rows(gate_up, out, rows: int, width: int, stream=None) -> None:
     """SwiGLU over rows of a fused [gate | up] projection output."""
     check(_lib.lib().mslim_cuda_swiglu_rows(_ptr(gate_up), _ptr(out), rows, width, _stream(stream)))

@@ -97,7 +97,7 @@ def pick_shard_argmax(torch, every):
 class DeviceModel:
     def __init__(self, spec: ModelSpec, batch: int, capacity: int, seed: int = 5, tp_rank: int = 0,
                  tp_world: int = 1, mlp: str = "sharded", kv_mode: str = "dense", page_tokens: int = 256,
-                 group=None, device=None):
+                 group=None, device=None, decode_gemm: str = "cublas"):
         import torch
         L = spec.layer
         if L.kv_heads % tp_world or L.intermediate % tp_world:
@@ -111,6 +111,9 @@ class DeviceModel:
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         self.rank, self.world, self.group = tp_rank, tp_world, group
         self.mlp, self.kv_mode = mlp, kv_mode
+        if decode_gemm not in ("own", "cublas"):
+            raise ValueError("decode_gemm is 'own' (mslim_cuda_gemv) or 'cublas'")
+        self.decode_gemm = decode_gemm
         self.batch, self.capacity = batch, capacity
         self.kvh = L.kv_heads // tp_world
         self.qh = L.query_heads // tp_world
@@ -201,9 +204,20 @@ class DeviceModel:
             _att.rmsnorm(x, w, out, x.shape[0], self.spec.layer.hidden, self.spec.layer.eps)
         return out
 
-    def _gemm(self, x, w):
+    def _gemm(self, x, w, out=None):
+        """x @ w^T through cuBLAS, or, with decode_gemm="own", the decode
+        step's few rows through mslim_cuda_gemv (measured slower than cuBLAS
+        at these shapes; the option serves hosts without cuBLAS)."""
+        t = self.torch
+        rows, (n, k) = x.shape[0], w.shape
         with self._sec("gemm"):
-            return self.torch.matmul(x, w.t())
+            if self.decode_gemm == "own" and rows <= 16 and n % 8 == 0 and k % 128 == 0:
+                y = out if out is not None else t.empty((rows, n), dtype=x.dtype, device=self.device)
+                _att.gemv(x.contiguous(), w, y, rows, n, k)
+                return y
+            if out is not None:
+                return t.matmul(x, w.t(), out=out)
+            return t.matmul(x, w.t())
 
     def _qkv_split(self, qkv):
         D = self.spec.layer.head_dim
@@ -227,8 +241,7 @@ class DeviceModel:
         rows = x.shape[0]
         if reduce and fused and self.comm is not None:
             slot = self.comm.next_slot()
-            with self._sec("gemm"):
-                self.torch.matmul(inp, w_proj.t(), out=self.comm.slot(slot, rows))
+            self._gemm(inp, w_proj, out=self.comm.slot(slot, rows))
             out = self.torch.empty_like(x)
             with self._sec("collective"):
                 self.comm.allreduce_rmsnorm(slot, x, w_norm, out, rows, self.spec.layer.eps)
