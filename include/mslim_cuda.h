@@ -212,6 +212,21 @@ int mslim_cuda_prefill_causal(const mslim_geometry_t *geometry, const void *q, c
                               const void *v, void *out, uint32_t queries, uint32_t prior,
                               void *stream);
 
+/* ColdStore page sealing from device pages: the per-token FNV-1a 64 hashes of
+ * a page record (src/cold_store.rs:725-742 token_hashes; computed by the
+ * writer in GpuRegionStore::append_batch, src/gpu_region_store.rs:391-522)
+ * taken directly from the device page pool that the appends fill, so the host
+ * receives head-major pages and their hashes with no transpose.
+ * pool: bf16 [n_pool_pages][kv_heads][page_tokens][head_dim] (K or V);
+ * page_ids: device int32 [n_pages]; hashes: device uint64 [n_pages][tokens],
+ * tokens <= page_tokens (a partly filled page hashes like its compact record).
+ * A page id outside the pool yields 0 hashes and is reported by
+ * mslim_cuda_device_status.  The record's whole-payload checksums are
+ * sequential FNV over each payload and stay with the host writer. */
+int mslim_cuda_page_token_hashes(const void *pool, uint32_t n_pool_pages, uint32_t kv_heads,
+                                 uint32_t page_tokens, uint32_t head_dim, const int32_t *page_ids,
+                                 uint32_t n_pages, uint32_t tokens, uint64_t *hashes, void *stream);
+
 /* ------------------------------------------------- layer elementwise -- */
 
 /* GpuEngine::add (src/gpu_llm/gpu_resources.rs:539-559, kernel llm_add) and the

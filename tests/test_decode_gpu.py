@@ -193,3 +193,22 @@ def test_rejects_bad_arguments(m):
         m.decode_dense(m.AttentionGeometry.new(4, 1, 12), b, b, b, seq, 1, 1, ws, b.clone())
     with pytest.raises(m.ShapeMismatch):  # page size not a multiple of 64
         m.decode_paged(g, b, b, b, 1, 48, seq, 1, seq, 1, ws, b.clone())
+
+
+@pytest.mark.parametrize("tokens", [256, 100, 1])
+def test_page_token_hashes_match_the_coldstore_record(m, oracle, tokens):
+    """ColdStore page sealing from device pages (cold_store.rs:725-742): the
+    per-token FNV-1a of pool pages equal the record hashes of their compact
+    head-major payloads, full or partly filled."""
+    import torch
+    rng = np.random.default_rng(tokens)
+    n_pool, kvh, pt, d = 12, 8, 256, 128
+    pool = rng.integers(0, 1 << 16, size=(n_pool, kvh, pt, d), dtype=np.uint16)
+    ids = np.array([7, 0, 11, 3], np.int32)
+    hashes = torch.zeros((len(ids), tokens), dtype=torch.int64, device="cuda:0")
+    m.page_token_hashes(dev(pool), n_pool, kvh, pt, d, dev(ids), len(ids), tokens, hashes)
+    got = hashes.cpu().numpy().view(np.uint64)
+    for i, p in enumerate(ids):
+        payload = np.ascontiguousarray(pool[p][:, :tokens, :])
+        assert np.array_equal(got[i], oracle.token_hashes(payload, kvh, tokens))
+    assert m.device_status(0) == 0

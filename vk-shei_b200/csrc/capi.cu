@@ -755,6 +755,24 @@ int mslim_cuda_swiglu(const void *gate, const void *up, void *out, uint64_t n, v
     return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "SwiGLU launch");
 }
 
+int mslim_cuda_page_token_hashes(const void *pool, uint32_t n_pool_pages, uint32_t kv_heads,
+                                 uint32_t page_tokens, uint32_t head_dim, const int32_t *page_ids,
+                                 uint32_t n_pages, uint32_t tokens, uint64_t *hashes, void *stream) {
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    if (!pool || !page_ids || !hashes) return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
+    if (n_pages == 0 || tokens == 0) return MSLIM_OK;
+    if (kv_heads == 0 || head_dim == 0 || head_dim % 8 != 0 || page_tokens == 0 || n_pool_pages == 0)
+        return fail(MSLIM_ERR_INVALID_GEOMETRY, "page geometry (head_dim a multiple of 8)");
+    if (tokens > page_tokens) return fail(MSLIM_ERR_SHAPE_MISMATCH, "more tokens than a page holds");
+    if (n_pages > 65535) return fail(MSLIM_ERR_SHAPE_MISMATCH, "at most 65535 pages per call");
+    if (!aligned(pool, 16) || !aligned(hashes, 8)) return fail(MSLIM_ERR_SHAPE_MISMATCH, "misaligned buffer");
+    cudaError_t err = mslim::launch_page_token_hashes(static_cast<const uint16_t *>(pool), n_pool_pages, kv_heads,
+                                                      page_tokens, head_dim, page_ids, n_pages, tokens, hashes,
+                                                      status_ptr(dev), static_cast<cudaStream_t>(stream));
+    return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "page hash launch");
+}
+
 int mslim_cuda_gemv(const void *x, const void *w, void *y, uint32_t m, uint32_t n, uint32_t k, void *stream) {
     int dev;
     if (int rc = current_device(&dev)) return rc;

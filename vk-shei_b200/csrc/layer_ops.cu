@@ -166,6 +166,45 @@ __global__ void __launch_bounds__(kGemvThreads)
         *reinterpret_cast<uint32_t *>(y + (size_t)(g + 8) * n + n0 + 2 * t) = pack_bf16x2(c[2], c[3]);
 }
 
+// ------------------------------------------------------------ page seal --
+// Per-token FNV-1a 64 of ColdStore pages straight from the device page pool
+// (src/cold_store.rs:725-742 token_hashes over a record payload): token t's
+// hash runs over the D*2 bytes of token t of head 0, then head 1, ... in
+// memory order.  One thread per token; the hash only depends on each token's
+// bytes, so a partly filled page hashes like its compact record payload.
+__global__ void __launch_bounds__(128)
+    mslim_page_token_hashes(const uint16_t *__restrict__ pool, uint32_t n_pool_pages, uint32_t kv_heads,
+                            uint32_t page_tokens, uint32_t head_dim, const int32_t *__restrict__ page_ids,
+                            uint32_t tokens, uint64_t *__restrict__ hashes, int *status) {
+    const uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t pi = blockIdx.y;
+    if (t >= tokens) return;
+    const int32_t page = page_ids[pi];
+    uint64_t *out = hashes + (size_t)pi * tokens + t;
+    if (page < 0 || (uint32_t)page >= n_pool_pages) {
+        if (t == 0 && status) atomicExch(status, MSLIM_DEVICE_BAD_PAGE_CODE);
+        *out = 0;
+        return;
+    }
+    uint64_t state = 0xcbf29ce484222325ull;
+    for (uint32_t h = 0; h < kv_heads; ++h) {
+        const uint4 *row =
+            reinterpret_cast<const uint4 *>(pool + (((size_t)page * kv_heads + h) * page_tokens + t) * head_dim);
+        for (uint32_t c = 0; c < head_dim / 8; ++c) {
+            const uint4 v = __ldg(row + c);
+            const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int wd = 0; wd < 4; ++wd)
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    state ^= (words[wd] >> (8 * b)) & 0xffu;
+                    state *= 0x100000001b3ull;
+                }
+        }
+    }
+    *out = state;
+}
+
 // ---------------------------------------------------------------- argmax --
 
 constexpr int kArgThreads = 1024;
@@ -271,6 +310,16 @@ cudaError_t launch_gemv(const uint16_t *x, const uint16_t *w, uint16_t *y, uint3
         mslim_gemv<2><<<n / 16, kGemvThreads, 0, stream>>>(x, w, y, m, n, k);
     else
         mslim_gemv<4><<<n / 8, kGemvThreads, 0, stream>>>(x, w, y, m, n, k);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_page_token_hashes(const uint16_t *pool, uint32_t n_pool_pages, uint32_t kv_heads,
+                                     uint32_t page_tokens, uint32_t head_dim, const int32_t *page_ids,
+                                     uint32_t n_pages, uint32_t tokens, uint64_t *hashes, int *status,
+                                     cudaStream_t stream) {
+    dim3 grid((tokens + 127) / 128, n_pages);
+    mslim_page_token_hashes<<<grid, 128, 0, stream>>>(pool, n_pool_pages, kv_heads, page_tokens, head_dim,
+                                                      page_ids, tokens, hashes, status);
     return cudaGetLastError();
 }
 

@@ -17,6 +17,12 @@ cudaError_t launch_swiglu_rows(const uint16_t *gate_up, uint16_t *out, uint32_t 
 // m <= 16 rows; n % 8 == 0, k % 128 == 0, 16-byte aligned rows.
 cudaError_t launch_gemv(const uint16_t *x, const uint16_t *w, uint16_t *y, uint32_t m, uint32_t n, uint32_t k,
                         cudaStream_t stream);
+// hashes[p][t] = FNV-1a 64 of token t (t < tokens) of pool page page_ids[p]
+// over its heads in order; pool: bf16 [n_pool_pages][kv_heads][page_tokens][head_dim].
+cudaError_t launch_page_token_hashes(const uint16_t *pool, uint32_t n_pool_pages, uint32_t kv_heads,
+                                     uint32_t page_tokens, uint32_t head_dim, const int32_t *page_ids,
+                                     uint32_t n_pages, uint32_t tokens, uint64_t *hashes, int *status,
+                                     cudaStream_t stream);
 // rows x n bf16 logits -> int32 index per row.  ties_to_last != 0: the largest
 // value under f32::total_cmp, last index among equals (the CPU path's
 // Iterator::max_by); 0: the largest by float comparison, first index among

@@ -313,6 +313,13 @@ def swiglu(gate, up, out, n: int, stream=None) -> None:
     check(_lib.lib().mslim_cuda_swiglu(_ptr(gate), _ptr(up), _ptr(out), n, _stream(stream)))
 
 
+def page_token_hashes(pool, n_pool_pages: int, kv_heads: int, page_tokens: int, head_dim: int, page_ids,
+                      n_pages: int, tokens: int, hashes, stream=None) -> None:
+    """Per-token FNV-1a of ColdStore pages from the device pool (cold_store.rs:725-742)."""
+    check(_lib.lib().mslim_cuda_page_token_hashes(_ptr(pool), n_pool_pages, kv_heads, page_tokens, head_dim,
+                                                  _ptr(page_ids), n_pages, tokens, _ptr(hashes), _stream(stream)))
+
+
 def gemv(x, w, y, m: int, n: int, k: int, stream=None) -> None:
     """y[m][n] = bf16(x[m][k] . w[n][k]) for 1..16 rows (the decode projections)."""
     check(_lib.lib().mslim_cuda_gemv(_ptr(x), _ptr(w), _ptr(y), m, n, k, _stream(stream)))
