@@ -33,9 +33,6 @@ struct DecodeParams {
     float *out_f32;              // if set, the merge writes f32 here instead of bf16
 };
 
-// Tokens per TMA stage (the split and page granularity).
-constexpr int kDecodeTileTokens = 64;
-
 // Enqueues the split kernel and the merge kernel on `stream`.
 cudaError_t launch_decode(int head_dim, bool paged, const CUtensorMap &kmap,
                           const CUtensorMap &vmap, const DecodeParams &p, uint16_t *out,

@@ -103,15 +103,6 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
 
 // Tiled TMA loads from this GPU's own global memory into this CTA's shared
 // memory, completing on `bar`.  No multicast.
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar,
-                                            int32_t x, int32_t y) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
-        : "memory");
-}
-
 __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar,
                                             int32_t x, int32_t y, int32_t z) {
     asm volatile(
@@ -405,14 +396,6 @@ __device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, u
         : "memory");
 }
 
-// 32 consecutive 32-bit TMEM columns of this thread's lane from raw words.
-__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t (&v)[32]) {
-    float f[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]);
-    tmem_st32(taddr, f);
-}
-
 // Register budget moves between warpgroups (all four warps of a warpgroup
 // execute the same instruction).
 template <uint32_t N>
@@ -477,16 +460,6 @@ __device__ __forceinline__ void tmem_st32u_nowait(uint32_t taddr, const uint32_t
         "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]),
         "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
         "r"(v[29]), "r"(v[30]), "r"(v[31])
-        : "memory");
-}
-// tcgen05.st of 16 columns without waiting; pair with tmem_wait_st().
-__device__ __forceinline__ void tmem_st16u_nowait(uint32_t taddr, const uint32_t (&v)[16]) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-        "%11, %12, %13, %14, %15, %16};" ::"r"(taddr),
-        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
-        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
-        "r"(v[15])
         : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() {

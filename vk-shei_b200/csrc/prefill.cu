@@ -68,13 +68,10 @@ constexpr int kSOffX = kSOffV + 2 * kTileBytes;     // row-max / row-sum exchang
 constexpr int kSOffBar = kSOffX + 6 * kRows * 4;
 constexpr int kSSmemBytes = kSOffBar + 512 + 1024;
 constexpr int kSThreads = 12 * 32;
-// Columns in one pair in eight go through the FMA-pipe exp2 (measured best split).
+// One pair of P columns in eight goes through the FMA-pipe exp2, the rest
+// through MUFU (the measured best split); both prefill kernels use the same
+// pairs, so for the same inputs they return the same bits.
 #define MSLIM_EXP_ON_FMA(i) (((i) & 7) == 7)
-// The same for the two-heads-per-CTA kernel: a bit per (pair index mod 8).
-#ifndef MSLIM_PAIR_POLY_MASK
-#define MSLIM_PAIR_POLY_MASK 0x80
-#endif
-#define MSLIM_PAIR_EXP_ON_FMA(i) ((MSLIM_PAIR_POLY_MASK >> ((i) & 7)) & 1)
 
 struct SingleBars {
     uint64_t q_full;
@@ -629,7 +626,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
                         const int e = c * 64 + 2 * i;
                         float x0, x1;
                         f2_unpack(f2_fma(f2_pack(v[e], v[e + 1]), scale2, nbase2), x0, x1);
-                        const bool poly = MSLIM_PAIR_EXP_ON_FMA(i);
+                        const bool poly = MSLIM_EXP_ON_FMA(i);
                         const float p0 = poly ? exp2_fma(x0) : fast_exp2(x0);
                         const float p1 = poly ? exp2_fma(x1) : fast_exp2(x1);
                         sum2[i & 3] = f2_add(sum2[i & 3], f2_pack(p0, p1));
