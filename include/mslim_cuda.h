@@ -387,11 +387,15 @@ void mslim_cuda_backend_destroy(mslim_backend_t *backend);
 /* AttentionBackend::decode as GpuBackend implements it
  * (src/gpu_backend.rs:149-377): host query f32 [QH*D] (any finite f32; it is
  * carried as a bf16 hi + lo pair), host K/V frames concatenated token-major
- * [tokens][KVH][D] of dtype 1 = bf16 (2 = f16 and 3 = f32 return
- * MSLIM_ERR_UNSUPPORTED_DEVICE: the B200 path is a bf16 path), host output
- * f32 [QH*D].  Uploads, runs the dense decode, reads back and synchronises,
- * like the reference's blocking dispatch.  tokens == 0 gives zeros; a
- * non-finite query or output gives MSLIM_ERR_NON_FINITE. */
+ * [tokens][KVH][D] of dtype 1 = bf16, 2 = f16 or 3 = f32, host output
+ * f32 [QH*D].  The kernels read bf16: f16/f32 frames whose values are all
+ * exact bf16 values are carried bit for bit; otherwise each value becomes a
+ * bf16 hi + lo pair laid side by side along the head dimension (kernel
+ * head_dim 2*D, so D <= 128 there, else MSLIM_ERR_UNSUPPORTED_DEVICE) with
+ * the query duplicated, and the two output halves are added on the host.
+ * Uploads, runs the dense decode, reads back and synchronises, like the
+ * reference's blocking dispatch.  tokens == 0 gives zeros; a non-finite
+ * query, frame value or output gives MSLIM_ERR_NON_FINITE. */
 int mslim_cuda_backend_decode(mslim_backend_t *backend, const mslim_geometry_t *geometry,
                               const float *query_host, const void *keys_host,
                               const void *values_host, int dtype, uint32_t tokens,

@@ -62,13 +62,56 @@ def test_geometry_roundtrips_f32_frames(m, backend, oracle, qh, kvh):
     assert np.max(np.abs(cpu - gpu)) < 1e-4
 
 
-def test_lossy_formats_are_rejected_not_quantized(m, backend):
+def test_values_off_the_bf16_grid_are_carried_not_quantized(m, backend, oracle):
+    """0.1 is not a bf16 value: the frame goes up as a bf16 hi + lo pair and
+    the result still meets the reference's 1e-4 against f64."""
     from mslim_b200 import workloads as wl
     g = m.AttentionGeometry.new(4, 2, 4)
-    k = np.full((4, 2, 4), 0.1, np.float32)  # 0.1 is not a bf16 value
-    cache, _, _ = frames(m, wl, g, k, k, "f32")
+    k = np.full((4, 2, 4), 0.1, np.float32)
+    v = np.arange(32, dtype=np.float32).reshape(4, 2, 4) * np.float32(0.0371)
+    cache, kb, vb = frames(m, wl, g, k, v, "f32")
+    q = np.linspace(-1.3, 0.7, 16).astype(np.float32)
+    cpu = oracle.cpu_reference_decode_f64(4, 2, 4, q, kb, vb, "f32", "f32")
+    gpu = cache.decode(backend, q)
+    assert np.max(np.abs(cpu - gpu)) < 1e-4, (cpu, gpu)
+    assert backend.last_timings()["input_kv_bytes"] == 2 * 32 * 4
+
+
+@pytest.mark.parametrize("dtype", ["f16", "f32"])
+@pytest.mark.parametrize("qh,kvh,d,t", [(32, 8, 128, 700), (8, 2, 64, 129), (4, 4, 40, 33)])
+def test_general_f16_f32_frames_against_f64(m, backend, oracle, dtype, qh, kvh, d, t):
+    from mslim_b200 import workloads as wl
+    rng = np.random.default_rng(d + t)
+    g = m.AttentionGeometry.new(qh, kvh, d)
+    k = rng.standard_normal((t, kvh, d)).astype(np.float32)
+    v = rng.standard_normal((t, kvh, d)).astype(np.float32)
+    cache, kb, vb = frames(m, wl, g, k, v, dtype)
+    q = (rng.standard_normal(qh * d) * 0.5).astype(np.float32)
+    cpu = oracle.cpu_reference_decode_f64(qh, kvh, d, q, kb, vb, dtype, dtype)
+    gpu = cache.decode(backend, q)
+    err = np.max(np.abs(cpu - gpu))
+    print(f"{dtype} frames qh={qh} kvh={kvh} d={d} t={t}: max-abs vs f64 {err:.3g}")
+    assert err < 1e-4, err
+
+
+def test_split_frames_need_head_dim_at_most_128(m, backend):
+    from mslim_b200 import workloads as wl
+    g = m.AttentionGeometry.new(2, 1, 256)
+    k = np.full((3, 1, 256), 0.1, np.float32)
+    cache, _, _ = frames(m, wl, g, k, k, "f16")
     with pytest.raises(m.UnsupportedDevice):
-        cache.decode(backend, np.zeros(16, np.float32))
+        cache.decode(backend, np.zeros(512, np.float32))
+
+
+def test_non_finite_frame_values_are_refused(m, backend):
+    from mslim_b200 import workloads as wl
+    g = m.AttentionGeometry.new(4, 2, 8)
+    k = np.ones((2, 2, 8), np.float32)
+    v = k.copy()
+    v[1, 1, 3] = np.inf
+    cache, _, _ = frames(m, wl, g, k, v, "f32")
+    with pytest.raises(m.NonFinite):
+        cache.decode(backend, np.ones(32, np.float32))
 
 
 def test_long_history_and_large_head_dim(m, backend, oracle):

@@ -345,6 +345,13 @@ int build_rope_table(const mslim_rope_config_t *rope, uint32_t dim, mslim::RopeT
     return MSLIM_OK;
 }
 
+// binary32 -> bf16 bits, round to nearest even (finite inputs).
+uint16_t bf16_bits_rne(float f) {
+    uint32_t bits;
+    memcpy(&bits, &f, 4);
+    return (uint16_t)((bits + 0x7fffu + ((bits >> 16) & 1u)) >> 16);
+}
+
 // IEEE binary16 -> binary32 (exact).
 float half_bits_to_float(uint16_t h) {
     const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
@@ -1282,33 +1289,65 @@ int mslim_cuda_backend_decode(mslim_backend_t *b, const mslim_geometry_t *geomet
     }
     if (dtype < 1 || dtype > 3) return fail(MSLIM_ERR_UNSUPPORTED_DEVICE, "unknown frame format %d", dtype);
     if (!keys_host || !values_host) return fail(MSLIM_ERR_SHAPE_MISMATCH, "null KV frames");
-    // The sm_100a path is a bf16 path.  FP16/FP32 frames are carried only when
-    // every value is exactly a bf16 value (bits preserved, no quantization).
+    // The sm_100a kernels read bf16.  FP16/FP32 frames whose values are all
+    // exact bf16 values are carried bit for bit.  Otherwise every value is
+    // split into two bf16 terms, hi = bf16(f), lo = bf16(f - hi) (exact for
+    // FP16, 16 significant bits for FP32), laid side by side along the head
+    // dimension ([k_hi | k_lo], [v_hi | v_lo]) with the query duplicated
+    // ([q | q]): q'.k' = q.k_hi + q.k_lo, and the two output halves add up to
+    // the attention output.  The scale stays 1/sqrt(D) of the caller.
     std::vector<uint16_t> conv_k, conv_v;
+    uint32_t DE = D;          // head dimension the kernel sees
+    bool split = false;
     if (dtype != 1) {
         const size_t n = (size_t)tokens * KVH * D;
-        conv_k.resize(n);
-        conv_v.resize(n);
+        auto value = [&](const void *src, size_t i) {
+            float f;
+            if (dtype == 3) {
+                memcpy(&f, static_cast<const uint8_t *>(src) + 4 * i, 4);
+            } else {
+                uint16_t h;
+                memcpy(&h, static_cast<const uint8_t *>(src) + 2 * i, 2);
+                f = half_bits_to_float(h);
+            }
+            return f;
+        };
+        for (int which = 0; which < 2 && !split; ++which) {
+            const void *src = which ? values_host : keys_host;
+            for (size_t i = 0; i < n; ++i) {
+                const float f = value(src, i);
+                if (!std::isfinite(f)) return fail(MSLIM_ERR_NON_FINITE, "non-finite computation: KV frame");
+                uint32_t bits;
+                memcpy(&bits, &f, 4);
+                if ((bits & 0xffffu) != 0) {
+                    split = true;
+                    break;
+                }
+            }
+        }
+        if (split && 2 * D > 256)
+            return fail(MSLIM_ERR_UNSUPPORTED_DEVICE,
+                        "%s frames with values that are not exact bf16 values need head_dim <= 128",
+                        dtype == 2 ? "FP16" : "FP32");
+        DE = split ? 2 * D : D;
+        conv_k.resize((size_t)tokens * KVH * DE);
+        conv_v.resize((size_t)tokens * KVH * DE);
         for (int which = 0; which < 2; ++which) {
             const void *src = which ? values_host : keys_host;
             uint16_t *dst = which ? conv_v.data() : conv_k.data();
-            for (size_t i = 0; i < n; ++i) {
-                float f;
-                if (dtype == 3) {
-                    memcpy(&f, static_cast<const uint8_t *>(src) + 4 * i, 4);
-                } else {
-                    uint16_t h;
-                    memcpy(&h, static_cast<const uint8_t *>(src) + 2 * i, 2);
-                    f = half_bits_to_float(h);
+            for (size_t row = 0; row < (size_t)tokens * KVH; ++row) {
+                for (uint32_t d = 0; d < D; ++d) {
+                    const float f = value(src, row * D + d);
+                    if (!std::isfinite(f)) return fail(MSLIM_ERR_NON_FINITE, "non-finite computation: KV frame");
+                    const uint16_t hi = bf16_bits_rne(f);
+                    dst[row * DE + d] = hi;
+                    if (split) {
+                        uint32_t hb = (uint32_t)hi << 16;
+                        float hf;
+                        memcpy(&hf, &hb, 4);
+                        dst[row * DE + D + d] = bf16_bits_rne(f - hf);
+                    }
                 }
-                uint32_t bits;
-                memcpy(&bits, &f, 4);
-                if (!std::isfinite(f) || (bits & 0xffffu) != 0)
-                    return fail(MSLIM_ERR_UNSUPPORTED_DEVICE,
-                                "no native kernel registered for %s frames whose values are not "
-                                "exact bf16 values (sm_100a path is bf16)",
-                                dtype == 2 ? "FP16" : "FP32");
-                dst[i] = (uint16_t)(bits >> 16);
             }
         }
         keys_host = conv_k.data();
@@ -1318,7 +1357,7 @@ int mslim_cuda_backend_decode(mslim_backend_t *b, const mslim_geometry_t *geomet
     if (tokens > 0x7fffffffu) return fail(MSLIM_ERR_INVALID_GEOMETRY, "GPU token count > i32");
     // The kernel runs at the next supported head_dim; pad with zeros (zero
     // query/key lanes add nothing to q.k and padded value lanes are dropped).
-    const uint32_t KD = D <= 64 ? 64 : D <= 128 ? 128 : 256;
+    const uint32_t KD = DE <= 64 ? 64 : DE <= 128 ? 128 : 256;
     DecodeShapeInfo sh;
     if (int rc = decode_shape(geometry, 1, &sh)) return rc;
     const uint32_t st = policy_split_tokens((uint64_t)KVH * sh.head_chunks, tokens);
@@ -1355,19 +1394,24 @@ int mslim_cuda_backend_decode(mslim_backend_t *b, const mslim_geometry_t *geomet
     const auto t0 = std::chrono::steady_clock::now();
     // Host staging with zero padding of the head dimension.
     std::vector<float> qpad((size_t)QH * KD, 0.0f);
-    for (uint32_t h = 0; h < QH; ++h) memcpy(&qpad[(size_t)h * KD], query_host + (size_t)h * D, D * 4);
+    for (uint32_t h = 0; h < QH; ++h) {
+        memcpy(&qpad[(size_t)h * KD], query_host + (size_t)h * D, D * 4);
+        if (split) memcpy(&qpad[(size_t)h * KD + D], query_host + (size_t)h * D, D * 4);
+    }
     err = cudaMemcpyAsync(dq, qpad.data(), q_bytes, cudaMemcpyHostToDevice, b->stream);
-    if (err == cudaSuccess && KD == D) {
+    if (err == cudaSuccess && KD == DE) {
         err = cudaMemcpyAsync(dk, keys_host, kv_bytes, cudaMemcpyHostToDevice, b->stream);
         if (err == cudaSuccess) err = cudaMemcpyAsync(dv, values_host, kv_bytes, cudaMemcpyHostToDevice, b->stream);
     } else if (err == cudaSuccess) {
-        err = cudaMemcpy2DAsync(dk, KD * 2, keys_host, D * 2, D * 2, (size_t)tokens * KVH,
+        err = cudaMemcpy2DAsync(dk, KD * 2, keys_host, DE * 2, DE * 2, (size_t)tokens * KVH,
                                 cudaMemcpyHostToDevice, b->stream);
         if (err == cudaSuccess)
-            err = cudaMemcpy2DAsync(dv, KD * 2, values_host, D * 2, D * 2, (size_t)tokens * KVH,
+            err = cudaMemcpy2DAsync(dv, KD * 2, values_host, DE * 2, DE * 2, (size_t)tokens * KVH,
                                     cudaMemcpyHostToDevice, b->stream);
-        if (err == cudaSuccess) err = cudaMemset2DAsync(dk + D, KD * 2, 0, (KD - D) * 2, (size_t)tokens * KVH, b->stream);
-        if (err == cudaSuccess) err = cudaMemset2DAsync(dv + D, KD * 2, 0, (KD - D) * 2, (size_t)tokens * KVH, b->stream);
+        if (err == cudaSuccess)
+            err = cudaMemset2DAsync(dk + DE, KD * 2, 0, (KD - DE) * 2, (size_t)tokens * KVH, b->stream);
+        if (err == cudaSuccess)
+            err = cudaMemset2DAsync(dv + DE, KD * 2, 0, (KD - DE) * 2, (size_t)tokens * KVH, b->stream);
     }
     if (err != cudaSuccess) return done(cuda_fail(err, "write KV"));
     DecodeCall c{};
@@ -1400,10 +1444,13 @@ int mslim_cuda_backend_decode(mslim_backend_t *b, const mslim_geometry_t *geomet
     if (status) return done(fail(MSLIM_ERR_DEVICE_TIMEOUT, "device wait bound hit during decode"));
     float kernel_ms = 0.f;
     cudaEventElapsedTime(&kernel_ms, b->ev0, b->ev1);
-    for (uint32_t h = 0; h < QH; ++h) memcpy(out_host + (size_t)h * D, &opad[(size_t)h * KD], D * 4);
+    for (uint32_t h = 0; h < QH; ++h) {
+        const float *o = &opad[(size_t)h * KD];
+        for (uint32_t d = 0; d < D; ++d) out_host[(size_t)h * D + d] = split ? o[d] + o[D + d] : o[d];
+    }
     b->dispatch_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
     b->kernel_ms = kernel_ms;
-    b->input_kv_bytes = 2 * (size_t)tokens * KVH * D * 2;
+    b->input_kv_bytes = 2 * (size_t)tokens * KVH * D * (dtype == 3 ? 4 : 2);
     b->scratch_bytes = ws_bytes;
     b->output_bytes = qn * 4;
     b->have_timings = true;
