@@ -266,23 +266,8 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr, uint32_t lbo
     return d;
 }
 
-// D[tmem] (+)= A[smem] * B[smem]^T, bf16 inputs, fp32 accumulate.  Called by
-// all 32 lanes of the MMA warp in warp-uniform control flow; elect.sync picks
-// the one lane that issues.  (Issued from a lone divergent lane, each MMA was
-// measured at 97-250 cycles instead of its 64-cycle (N=128) pipe time.)
-__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                          uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred e, p;\n\t"
-        "elect.sync _|e, 0xffffffff;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
 // Arrives on `bar` once every tcgen05 operation the issuing lane issued so far is
-// done.  Warp-collective like umma_bf16 (one elected lane commits).
+// done.  Warp-collective like the MMA groups below (one elected lane commits).
 __device__ __forceinline__ void umma_commit(uint64_t *bar) {
     asm volatile(
         "{\n\t.reg .pred e;\n\t"
@@ -382,19 +367,72 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 
 namespace mslim {
 
-// D[tmem] (+)= A[tmem] * B[smem]: A (M=128 rows on the 128 lanes, K packed two
-// bf16 per 32-bit column) comes from tensor memory.  Warp-collective like
-// umma_bf16.
-__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                             uint32_t idesc, uint32_t accumulate) {
+// tcgen05.mma issue.  All 32 lanes of the MMA warp call these in warp-uniform
+// control flow and elect.sync picks the lane that issues; one elect covers a
+// whole group of K steps, which keeps the MMA warp's instruction count (it
+// shares its SM sub-partition with two softmax warps) low.  (Issued from a lone
+// divergent lane, each MMA was measured at 97-250 cycles instead of its
+// 64-cycle N=128 pipe time.)
+//
+// Eight K=16 steps of one 128 x N x 128 product from a single elect: step k
+// reads A at a_desc + a_off(k) and B at b_desc + b_off(k), where the offsets (in
+// the descriptors' 16-byte units) advance by 2 (32 bytes, the next 16 columns
+// of a 128-byte swizzled row) within a 64-column box and by `box16` across the
+// two boxes.  Descriptor start addresses are the low 14 bits and the summed
+// addresses stay inside shared memory, so the adds never carry out of the
+// field.  Step 0 accumulates when `accumulate` is set, steps 1..7 always do.
+__device__ __forceinline__ void umma_bf16_ss_k128(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                  uint32_t idesc, uint32_t accumulate, uint32_t box16) {
     asm volatile(
-        "{\n\t.reg .pred e, p;\n\t"
-        "elect.sync _|e, 0xffffffff;\n\t"
+        "{\n\t.reg .pred e, p, t;\n\t.reg .b64 a1, a2, a3, a4, a5, a6, a7, b1, b2, b3, b4, b5, b6, b7, bx;\n\t"
+        "cvt.u64.u32 bx, %5;\n\t"
+        "add.s64 a1, %1, 2;\n\tadd.s64 a2, %1, 4;\n\tadd.s64 a3, %1, 6;\n\t"
+        "add.s64 a4, %1, bx;\n\tadd.s64 a5, a4, 2;\n\tadd.s64 a6, a4, 4;\n\tadd.s64 a7, a4, 6;\n\t"
+        "add.s64 b1, %2, 2;\n\tadd.s64 b2, %2, 4;\n\tadd.s64 b3, %2, 6;\n\t"
+        "add.s64 b4, %2, bx;\n\tadd.s64 b5, b4, 2;\n\tadd.s64 b6, b4, 4;\n\tadd.s64 b7, b4, 6;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        "setp.eq.b32 t, %4, %4;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a1, b1, %3, t;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a2, b2, %3, t;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a3, b3, %3, t;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a4, b4, %3, t;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a5, b5, %3, t;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a6, b6, %3, t;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a7, b7, %3, t;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(box16)
         : "memory");
 }
+
+// Four K=16 steps of O += P V with P in tensor memory: step k reads A at
+// a_tmem + 8k (sixteen bf16 keys packed into eight 32-bit columns) and B at
+// b_desc + k * b_step16.  Step 0 accumulates when `accumulate` is set.
+__device__ __forceinline__ void umma_bf16_ts_k64(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                                 uint32_t idesc, uint32_t accumulate, uint32_t b_step16) {
+    asm volatile(
+        "{\n\t.reg .pred e, p, t;\n\t.reg .b32 a1, a2, a3;\n\t.reg .b64 b1, b2, b3, bs;\n\t"
+        "cvt.u64.u32 bs, %5;\n\t"
+        "add.s32 a1, %1, 8;\n\tadd.s32 a2, %1, 16;\n\tadd.s32 a3, %1, 24;\n\t"
+        "add.s64 b1, %2, bs;\n\tadd.s64 b2, b1, bs;\n\tadd.s64 b3, b2, bs;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "setp.eq.b32 t, %4, %4;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a1], b1, %3, t;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a2], b2, %3, t;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a3], b3, %3, t;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(b_step16)
+        : "memory");
+}
+
+// Programmatic dependent launch (no-ops when the launch did not ask for it):
+// allow the next grid of the stream to start launching; wait until every
+// prerequisite grid has completed and its memory is visible.
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // Register budget moves between warpgroups (all four warps of a warpgroup
 // execute the same instruction).

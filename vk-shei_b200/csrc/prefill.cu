@@ -176,12 +176,8 @@ __global__ void __launch_bounds__(kSThreads, 1)
                 if (!wait_all(&bars->k_full[j & 1], (j >> 1) & 1, 22)) return false;
                 tc_fence_after();
                 const uint32_t kaddr = sbase + kSOffK + (j & 1) * kTileBytes;
-#pragma unroll
-                for (int kk = 0; kk < kDim / 16; ++kk) {
-                    const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
-                    umma_bf16(tmem + kColS + (j & 1) * 128, umma_desc_sw128(sbase + off, 16, 1024),
-                              umma_desc_sw128(kaddr + off, 16, 1024), kIdescS, kk > 0);
-                }
+                umma_bf16_ss_k128(tmem + kColS + (j & 1) * 128, umma_desc_sw128(sbase, 16, 1024),
+                                  umma_desc_sw128(kaddr, 16, 1024), kIdescS, 0u, kBox >> 4);
                 umma_commit(&bars->s_full[j & 1]);
                 umma_commit(&bars->k_empty[j & 1]);
                 return true;
@@ -199,10 +195,10 @@ __global__ void __launch_bounds__(kSThreads, 1)
                 tc_fence_after();
                 const uint32_t vaddr = sbase + kSOffV + (j & 1) * kTileBytes;
 #pragma unroll
-                for (int kk = 0; kk < kKeys / 16; ++kk)
-                    umma_bf16_ts(tmem + kColO, tmem + kColS + (j & 1) * 128 + kk * 8,
-                                 umma_desc_sw128(vaddr + kk * 16 * 128, kBox, 1024), kIdescPV,
-                                 (j > 0 || kk > 0) ? 1u : 0u);
+                for (int half = 0; half < 2; ++half)
+                    umma_bf16_ts_k64(tmem + kColO, tmem + kColS + (j & 1) * 128 + half * 32,
+                                     umma_desc_sw128(vaddr + half * 4 * 16 * 128, kBox, 1024), kIdescPV,
+                                     (j > 0 || half > 0) ? 1u : 0u, (16 * 128) >> 4);
                 umma_commit(j + 1 < n_kv ? &bars->o_full : &bars->o_done);
                 umma_commit(&bars->v_empty[j & 1]);
             }
@@ -440,6 +436,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
     tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
     const uint32_t sbase = smem_u32(smem);
+    // Programmatic dependent launch: the next kernel of the stream may begin
+    // launching (its CTAs take SMs as ours retire), and nothing below reads an
+    // input or writes the output before the previous kernel's memory is visible.
+    griddep_launch_dependents();
+    griddep_wait();
 
     if (warp < 4) {
         warpgroup_reg_dealloc<kPRegsCtl>();
@@ -503,12 +504,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
             auto issue_s = [&](int h, int slot) {
                 const uint32_t qaddr = sbase + kPOffQ + h * kQBytes;
                 const uint32_t kaddr = sbase + kPOffK + slot * kTileBytes;
-#pragma unroll
-                for (int kk = 0; kk < kDim / 16; ++kk) {
-                    const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
-                    umma_bf16(tmem + h * 128, umma_desc_sw128(qaddr + off, 16, 1024),
-                              umma_desc_sw128(kaddr + off, 16, 1024), kIdescS, kk > 0);
-                }
+                // the eight K=16 steps from one elect (see umma_bf16_ss_k128)
+                umma_bf16_ss_k128(tmem + h * 128, umma_desc_sw128(qaddr, 16, 1024),
+                                  umma_desc_sw128(kaddr, 16, 1024), kIdescS, 0u, kBox >> 4);
                 umma_commit(&bars->s_full[h]);
             };
             int g = 0;  // key tiles consumed so far, over all items
@@ -538,13 +536,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
                             ok = wait_all(&bars->p_full[h][half], g & 1, 55);
                             if (!ok) break;
                             tc_fence_after();
-#pragma unroll
-                            for (int kq = 0; kq < kKeys / 32; ++kq) {
-                                const int kk = half * (kKeys / 32) + kq;
-                                umma_bf16_ts(tmem + kColO + h * 128, tmem + h * 128 + kk * 8,
-                                             umma_desc_sw128(vaddr + kk * 16 * 128, kBox, 1024), kIdescPV,
-                                             (j > 0 || kk > 0) ? 1u : 0u);
-                            }
+                            // keys 64*half .. +63: four K=16 steps from one elect
+                            umma_bf16_ts_k64(tmem + kColO + h * 128, tmem + h * 128 + half * 32,
+                                             umma_desc_sw128(vaddr + half * 4 * 16 * 128, kBox, 1024),
+                                             kIdescPV, (j > 0 || half > 0) ? 1u : 0u, (16 * 128) >> 4);
                         }
                         if (!ok) break;
                         if (next) issue_s(h, (g + 1) & 1);
@@ -763,8 +758,17 @@ cudaError_t launch_prefill(const CUtensorMap &qmap, const CUtensorMap &kmap,
         // persistent: one CTA per SM (at most one per item)
         const long long items = (long long)p.n_qtiles * (p.qheads / 2);
         const unsigned grid = (unsigned)(items < sms ? items : sms);
-        mslim_prefill_pair<<<grid, kPThreads, kPSmemBytes, stream>>>(qmap, kmap, vmap, omap, p);
-        return cudaGetLastError();
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(grid);
+        cfg.blockDim = dim3(kPThreads);
+        cfg.dynamicSmemBytes = kPSmemBytes;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelEx(&cfg, mslim_prefill_pair, qmap, kmap, vmap, omap, p);
     }
     const unsigned grid = (unsigned)(p.n_qtiles * p.qheads);
     mslim_prefill_causal<<<grid, kSThreads, kSSmemBytes, stream>>>(qmap, kmap, vmap, p);
