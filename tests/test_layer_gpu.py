@@ -252,6 +252,45 @@ def test_fused_qkv_append_matches_separate_inputs(paged):
     assert m.device_status(0) == 0
 
 
+@pytest.mark.parametrize("paged", [False, True])
+@pytest.mark.parametrize("qh,kvh,d", [(32, 8, 128), (4, 1, 128), (8, 2, 80), (2, 2, 256)])
+def test_rope_append_vector_and_scalar_forms_agree(paged, qh, kvh, d):
+    """The launcher takes the 16-byte form when head_dim % 16 == 0 and every
+    row is 16-byte aligned; an input view one element into its buffer forces
+    the element-wise form.  Both must write the same bits."""
+    import torch
+    import mslim_b200 as m
+    from mslim_b200 import attention as att
+    rng = np.random.default_rng(qh * 31 + d)
+    B, T = 5, 300
+    g = att.AttentionGeometry.new(qh, kvh, d)
+    cfg = att.RopeKernelConfig(theta=500000.0)
+    width = (qh + 2 * kvh) * d
+    qkv = _rand_bf16(rng, B * width).reshape(B, width)
+    pos = dev(np.array([0, 1, 77, 255, 299], np.int32))
+    outs = []
+    for misaligned in (False, True):
+        buf = torch.zeros(B * width + 8, dtype=torch.int16, device="cuda:0")
+        off = 1 if misaligned else 0
+        buf[off:off + B * width].copy_(dev(qkv).view(-1))
+        src = buf[off:off + B * width].view(B, width)
+        q_out = torch.empty((B, qh * d), dtype=torch.int16, device="cuda:0")
+        if paged:
+            pt, mp = 64, 5
+            table = dev(np.random.default_rng(3).permutation(B * mp).astype(np.int32).reshape(B, mp))
+            kc = torch.zeros((B * mp, kvh, pt, d), dtype=torch.int16, device="cuda:0")
+            vc = torch.zeros_like(kc)
+            m.rope_append_decode_paged_qkv(g, src, q_out, pos, B, cfg, kc, vc, B * mp, pt, table, mp)
+        else:
+            kc = torch.zeros((B, T, kvh, d), dtype=torch.int16, device="cuda:0")
+            vc = torch.zeros_like(kc)
+            m.rope_append_decode_dense_qkv(g, src, q_out, pos, B, cfg, kc, vc, T)
+        outs.append([u16(q_out), u16(kc), u16(vc)])
+    for a, b in zip(*outs):
+        assert np.array_equal(a, b)
+    assert m.device_status(0) == 0
+
+
 @pytest.mark.parametrize("m,n,k", [(8, 6144, 4096), (8, 4096, 512), (8, 28672, 4096), (8, 4096, 14336),
                                    (3, 1024, 1792), (16, 520, 256), (1, 8, 128)])
 def test_gemv_matches_fp32_reference(m, n, k):

@@ -64,6 +64,10 @@ __global__ void __launch_bounds__(kThreads)
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * S::kStageBytes);
     uint64_t *empty = full + STAGES;
 
+    // launched with programmatic dependent launch: inputs (and the partials a
+    // previous merge may still read) are touched only after the predecessor
+    griddep_launch_dependents();
+    griddep_wait();
     const int split = blockIdx.x;
     const int kvh = blockIdx.y / p.head_chunks;
     const int hchunk = blockIdx.y % p.head_chunks;
@@ -362,6 +366,8 @@ __global__ void __launch_bounds__(kThreads)
 // One warp per (sequence, query row, query head): fixed split-order combine.
 template <int D>
 __global__ void __launch_bounds__(128) mslim_decode_merge(const DecodeParams p, uint16_t *out) {
+    griddep_launch_dependents();
+    griddep_wait();  // the split kernel's partials
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const size_t item = (size_t)blockIdx.x * 4 + warp;
     const size_t items = (size_t)p.n_seq * p.nq * p.qheads;
@@ -437,12 +443,10 @@ cudaError_t launch_impl(const CUtensorMap &kmap, const CUtensorMap &vmap, const 
         cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess) return err;
     dim3 grid(p.max_splits, p.kvheads * p.head_chunks, p.n_seq * p.q_blocks);
-    kernel<<<grid, kThreads, smem, stream>>>(kmap, vmap, p);
-    err = cudaGetLastError();
+    err = launch_pdl(kernel, grid, dim3(kThreads), smem, stream, kmap, vmap, p);
     if (err != cudaSuccess) return err;
     const size_t items = (size_t)p.n_seq * p.nq * p.qheads;
-    mslim_decode_merge<D><<<(unsigned)((items + 3) / 4), 128, 0, stream>>>(p, out);
-    return cudaGetLastError();
+    return launch_pdl(mslim_decode_merge<D>, dim3((unsigned)((items + 3) / 4)), dim3(128), 0, stream, p, out);
 }
 
 }  // namespace

@@ -758,17 +758,8 @@ cudaError_t launch_prefill(const CUtensorMap &qmap, const CUtensorMap &kmap,
         // persistent: one CTA per SM (at most one per item)
         const long long items = (long long)p.n_qtiles * (p.qheads / 2);
         const unsigned grid = (unsigned)(items < sms ? items : sms);
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(grid);
-        cfg.blockDim = dim3(kPThreads);
-        cfg.dynamicSmemBytes = kPSmemBytes;
-        cfg.stream = stream;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        return cudaLaunchKernelEx(&cfg, mslim_prefill_pair, qmap, kmap, vmap, omap, p);
+        return launch_pdl(mslim_prefill_pair, dim3(grid), dim3(kPThreads), kPSmemBytes, stream, qmap, kmap,
+                          vmap, omap, p);
     }
     const unsigned grid = (unsigned)(p.n_qtiles * p.qheads);
     mslim_prefill_causal<<<grid, kSThreads, kSSmemBytes, stream>>>(qmap, kmap, vmap, p);

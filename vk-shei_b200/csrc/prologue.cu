@@ -177,6 +177,52 @@ __device__ __forceinline__ void rope_append_token(const QkvRows &in, uint16_t *q
     }
 }
 
+// The same work in 16-byte groups, spread over gridDim.y CTAs per token: item
+// x < (QH + KVH) * D/16 rotates eight consecutive pairs (i0..i0+7 with
+// i0+D/2..i0+D/2+7) of one q or k head; the remaining items copy one 16-byte
+// chunk of a v head.  Every load of a thread is independent of its stores, so
+// the loads of all items are in flight together.  Needs D % 16 == 0 and 16-byte
+// aligned rows (checked by the launcher); same arithmetic, same bits.
+template <typename KDst, typename VDst>
+__device__ __forceinline__ void rope_append_token_vec(const QkvRows &in, uint16_t *q_out, uint32_t token,
+                                                      uint32_t qheads, uint32_t kvheads, uint32_t dim,
+                                                      const float2 *cs, KDst k_dst, VDst v_dst) {
+    const uint32_t half = dim / 2, groups = half / 8;
+    const uint32_t rot = (qheads + kvheads) * groups, total = rot + kvheads * (dim / 8);
+    const uint16_t *qr = in.q + (size_t)token * in.q_stride;
+    const uint16_t *kr = in.k + (size_t)token * in.kv_stride;
+    const uint16_t *vr = in.v + (size_t)token * in.kv_stride;
+    for (uint32_t x = blockIdx.y * blockDim.x + threadIdx.x; x < total; x += gridDim.y * blockDim.x) {
+        if (x < rot) {
+            const bool is_q = x < qheads * groups;
+            const uint32_t y = is_q ? x : x - qheads * groups;
+            const uint32_t head = y / groups, i0 = (y % groups) * 8;
+            const uint16_t *src = (is_q ? qr : kr) + (size_t)head * dim;
+            const uint4 a4 = *reinterpret_cast<const uint4 *>(src + i0);
+            const uint4 b4 = *reinterpret_cast<const uint4 *>(src + i0 + half);
+            const uint32_t a[4] = {a4.x, a4.y, a4.z, a4.w}, b[4] = {b4.x, b4.y, b4.z, b4.w};
+            uint32_t oa[4], ob[4];
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+                float r0, r1, s0, s1;
+                rope_rotate(bf16_bits_to_f32((uint16_t)(a[w] & 0xffffu)), bf16_bits_to_f32((uint16_t)(b[w] & 0xffffu)),
+                            cs[i0 + 2 * w], r0, s0);
+                rope_rotate(bf16_bits_to_f32((uint16_t)(a[w] >> 16)), bf16_bits_to_f32((uint16_t)(b[w] >> 16)),
+                            cs[i0 + 2 * w + 1], r1, s1);
+                oa[w] = (uint32_t)bf16_bits_rn(r0) | ((uint32_t)bf16_bits_rn(r1) << 16);
+                ob[w] = (uint32_t)bf16_bits_rn(s0) | ((uint32_t)bf16_bits_rn(s1) << 16);
+            }
+            uint16_t *dst = is_q ? q_out + ((size_t)token * qheads + head) * dim : k_dst(head);
+            *reinterpret_cast<uint4 *>(dst + i0) = make_uint4(oa[0], oa[1], oa[2], oa[3]);
+            *reinterpret_cast<uint4 *>(dst + i0 + half) = make_uint4(ob[0], ob[1], ob[2], ob[3]);
+        } else {
+            const uint32_t c = x - rot, head = c / (dim / 8), d0 = (c % (dim / 8)) * 8;
+            *reinterpret_cast<uint4 *>(v_dst(head) + d0) =
+                *reinterpret_cast<const uint4 *>(vr + (size_t)head * dim + d0);
+        }
+    }
+}
+
 // One CTA per new token: RoPE of its q heads into q_out, RoPE of its k heads
 // and a copy of its v heads into the ColdStore-exact page that holds the
 // token (head-major [KVH][page_tokens][D] inside the page).
@@ -184,6 +230,7 @@ __device__ __forceinline__ void rope_append_token(const QkvRows &in, uint16_t *q
 //     position start_position + t, pages page_table[0..max_pages);
 //   decode form (positions != null): CTA s is the new token of session s at
 //     position positions[s], pages page_table[s * max_pages ..].
+template <bool kVec>
 __global__ void __launch_bounds__(256)
     mslim_rope_append_paged(const QkvRows in, uint16_t *__restrict__ q_out, uint32_t qheads,
                             uint32_t kvheads, uint32_t dim, uint32_t start_position,
@@ -191,6 +238,8 @@ __global__ void __launch_bounds__(256)
                             uint16_t *__restrict__ v_pool, uint32_t n_pages, uint32_t page_tokens,
                             const int32_t *__restrict__ page_table, uint32_t max_pages,
                             const RopeTable table, int *status) {
+    griddep_launch_dependents();
+    griddep_wait();  // programmatic dependent launch: the predecessor's writes are visible
     __shared__ float2 cs[kRopeMaxHalf];
     const uint32_t token = blockIdx.x;
     uint32_t pos;
@@ -220,17 +269,21 @@ __global__ void __launch_bounds__(256)
     auto v_dst = [&](uint32_t head) {
         return v_pool + (((size_t)phys * kvheads + head) * page_tokens + slot) * dim;
     };
-    rope_append_token(in, q_out, token, qheads, kvheads, dim, cs, k_dst, v_dst);
+    if constexpr (kVec) rope_append_token_vec(in, q_out, token, qheads, kvheads, dim, cs, k_dst, v_dst);
+    else rope_append_token(in, q_out, token, qheads, kvheads, dim, cs, k_dst, v_dst);
 }
 
 // Dense-cache twin of the decode form above: CTA s is the new token of session
 // s at position positions[s]; q -> RoPE -> q_out, k -> RoPE and v -> copy into
 // the token-major caches [n_seq][max_tokens][KVH][D] at row positions[s].
+template <bool kVec>
 __global__ void __launch_bounds__(256)
     mslim_rope_append_dense(const QkvRows in, uint16_t *__restrict__ q_out, uint32_t qheads,
                             uint32_t kvheads, uint32_t dim, const int32_t *__restrict__ positions,
                             uint16_t *__restrict__ k_cache, uint16_t *__restrict__ v_cache,
                             uint32_t max_tokens, const RopeTable table, int *status) {
+    griddep_launch_dependents();
+    griddep_wait();  // programmatic dependent launch: the predecessor's writes are visible
     __shared__ float2 cs[kRopeMaxHalf];
     const uint32_t token = blockIdx.x;
     const int32_t p = positions[token];
@@ -243,7 +296,23 @@ __global__ void __launch_bounds__(256)
     const size_t row = ((size_t)token * max_tokens + pos) * kvheads;  // cache row of this token
     auto k_dst = [&](uint32_t head) { return k_cache + (row + head) * dim; };
     auto v_dst = [&](uint32_t head) { return v_cache + (row + head) * dim; };
-    rope_append_token(in, q_out, token, qheads, kvheads, dim, cs, k_dst, v_dst);
+    if constexpr (kVec) rope_append_token_vec(in, q_out, token, qheads, kvheads, dim, cs, k_dst, v_dst);
+    else rope_append_token(in, q_out, token, qheads, kvheads, dim, cs, k_dst, v_dst);
+}
+
+// The 16-byte form: head_dim a multiple of 16 and every row start 16-byte
+// aligned (bases, and the q / kv row strides in elements a multiple of 8).
+bool rope_vec_ok(const QkvRows &in, const void *q_out, const void *k_dst, const void *v_dst, uint32_t dim) {
+    auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+    return dim % 16 == 0 && al(in.q) && al(in.k) && al(in.v) && al(q_out) && al(k_dst) && al(v_dst) &&
+           in.q_stride % 8 == 0 && in.kv_stride % 8 == 0;
+}
+
+// CTAs per token for the 16-byte form: about one 16-byte item per thread of a
+// 128-thread CTA, at most eight CTAs.
+unsigned rope_vec_ctas(uint32_t qheads, uint32_t kvheads, uint32_t dim) {
+    const uint64_t items = (uint64_t)(qheads + kvheads) * (dim / 16) + (uint64_t)kvheads * (dim / 8);
+    return (unsigned)std::min<uint64_t>(8, std::max<uint64_t>(1, (items + 127) / 128));
 }
 
 }  // namespace
@@ -277,10 +346,14 @@ cudaError_t launch_rope_append_paged(const uint16_t *q_in, uint16_t *q_out, cons
                                      uint32_t q_stride, uint32_t kv_stride) {
     const QkvRows in{q_in, k_in, v_in, q_stride ? q_stride : qheads * dim,
                      kv_stride ? kv_stride : kvheads * dim};
-    mslim_rope_append_paged<<<tokens, 256, 0, stream>>>(in, q_out, qheads, kvheads, dim, start_position,
-                                                        positions, k_pool, v_pool, n_pages, page_tokens,
-                                                        page_table, max_pages, table, status);
-    return cudaGetLastError();
+    if (rope_vec_ok(in, q_out, k_pool, v_pool, dim)) {
+        return launch_pdl(mslim_rope_append_paged<true>, dim3(tokens, rope_vec_ctas(qheads, kvheads, dim)),
+                          dim3(128), 0, stream, in, q_out, qheads, kvheads, dim, start_position, positions, k_pool,
+                          v_pool, n_pages, page_tokens, page_table, max_pages, table, status);
+    }
+    return launch_pdl(mslim_rope_append_paged<false>, dim3(tokens), dim3(256), 0, stream, in, q_out, qheads,
+                      kvheads, dim, start_position, positions, k_pool, v_pool, n_pages, page_tokens, page_table,
+                      max_pages, table, status);
 }
 
 cudaError_t launch_rope_append_dense(const uint16_t *q_in, uint16_t *q_out, const uint16_t *k_in,
@@ -291,9 +364,13 @@ cudaError_t launch_rope_append_dense(const uint16_t *q_in, uint16_t *q_out, cons
                                      uint32_t q_stride, uint32_t kv_stride) {
     const QkvRows in{q_in, k_in, v_in, q_stride ? q_stride : qheads * dim,
                      kv_stride ? kv_stride : kvheads * dim};
-    mslim_rope_append_dense<<<n_seq, 256, 0, stream>>>(in, q_out, qheads, kvheads, dim, positions, k_cache,
-                                                        v_cache, max_tokens, table, status);
-    return cudaGetLastError();
+    if (rope_vec_ok(in, q_out, k_cache, v_cache, dim)) {
+        return launch_pdl(mslim_rope_append_dense<true>, dim3(n_seq, rope_vec_ctas(qheads, kvheads, dim)),
+                          dim3(128), 0, stream, in, q_out, qheads, kvheads, dim, positions, k_cache, v_cache,
+                          max_tokens, table, status);
+    }
+    return launch_pdl(mslim_rope_append_dense<false>, dim3(n_seq), dim3(256), 0, stream, in, q_out, qheads,
+                      kvheads, dim, positions, k_cache, v_cache, max_tokens, table, status);
 }
 
 }  // namespace mslim
