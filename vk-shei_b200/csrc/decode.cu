@@ -386,19 +386,25 @@ __global__ void __launch_bounds__(128) mslim_decode_merge(const DecodeParams p, 
                            ? 0
                            : min((int)p.max_splits, (cta_end + p.split_tokens - 1) / p.split_tokens);
     const float *src = p.partials + item * p.max_splits * kRowF;
+    // the maximum over the splits: lane s reads split s (32 per round), then a
+    // warp max (exact, so the order does not matter)
     float m = -INFINITY;
-    for (int s = 0; s < splits; ++s) m = fmaxf(m, src[s * kRowF + D]);
+    for (int s0 = 0; s0 < splits; s0 += 32)
+        if (s0 + lane < splits) m = fmaxf(m, src[(s0 + lane) * kRowF + D]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     const float mb = (m == -INFINITY) ? 0.f : m;
     float l = 0.f;
     float acc[kPer];
 #pragma unroll
     for (int k = 0; k < kPer; ++k) acc[k] = 0.f;
-    // splits in order; four at a time have their loads in flight together
+    // splits accumulated in order; eight at a time have their loads in flight
+    constexpr int kBatch = 8;
     int s = 0;
-    for (; s + 4 <= splits; s += 4) {
-        float mv[4], lv[4], pv[4][kPer];
+    for (; s + kBatch <= splits; s += kBatch) {
+        float mv[kBatch], lv[kBatch], pv[kBatch][kPer];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < kBatch; ++u) {
             const float *part = src + (s + u) * kRowF;
             mv[u] = part[D];
             lv[u] = part[D + 1];
@@ -406,7 +412,7 @@ __global__ void __launch_bounds__(128) mslim_decode_merge(const DecodeParams p, 
             for (int k = 0; k < kPer; ++k) pv[u][k] = part[lane + 32 * k];
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < kBatch; ++u) {
             const float w = fast_exp2(mv[u] - mb);
             l += w * lv[u];
 #pragma unroll

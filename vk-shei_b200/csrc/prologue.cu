@@ -50,6 +50,22 @@ __device__ __forceinline__ void rope_fill(const RopeTable &t, uint32_t position,
 // layer, native_cpu_adapter.rs:186-191), and normalised from the updated
 // values with the same reduction order, so the fused form returns the same
 // bits as a residual add followed by RMSNorm.
+// 1 / sqrt(mean(x^2) + eps) from each thread's partial sum of squares: warp
+// xor-tree, then the four warps' sums in a fixed order.
+__device__ __forceinline__ float rms_scale(float sum, uint32_t hidden, float eps) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    __shared__ float part[4];
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = sum;
+    __syncthreads();
+    const float total = (part[0] + part[1]) + (part[2] + part[3]);
+    const float mean = __fdiv_rn(total, (float)hidden);
+    return __fdiv_rn(1.0f, __fsqrt_rn(mean + eps));
+}
+
+// Rows up to 128 * 8 * kNormRegIters elements stay in registers.
+constexpr int kNormRegIters = 8;
+
 template <bool kResidual>
 __global__ void __launch_bounds__(128)
     mslim_rmsnorm(uint16_t *__restrict__ x, const uint16_t *__restrict__ delta,
@@ -60,6 +76,61 @@ __global__ void __launch_bounds__(128)
     uint16_t *yr = y + row * hidden;
     const bool vec = (hidden % 8 == 0);
     float sum = 0.f;
+    if (vec && hidden <= 128 * 8 * kNormRegIters) {
+        // The whole row in registers: every load (x, delta, w) is issued before
+        // the first use, and the second pass does not read x back.  Same
+        // element order and sums as the loops below, so the same bits.
+        uint4 xv[kNormRegIters], wt[kNormRegIters];
+#pragma unroll
+        for (int it = 0; it < kNormRegIters; ++it) {
+            const uint32_t i = (threadIdx.x + it * 128) * 8;
+            if (i < hidden) {
+                xv[it] = *reinterpret_cast<const uint4 *>(xr + i);
+                wt[it] = *reinterpret_cast<const uint4 *>(w + i);
+                if (kResidual) {
+                    const uint4 v = xv[it];
+                    const uint4 d = *reinterpret_cast<const uint4 *>(dr + i);
+                    xv[it] = make_uint4(
+                        pack_bf16x2(bf16lo_f32(v.x) + bf16lo_f32(d.x), bf16hi_f32(v.x) + bf16hi_f32(d.x)),
+                        pack_bf16x2(bf16lo_f32(v.y) + bf16lo_f32(d.y), bf16hi_f32(v.y) + bf16hi_f32(d.y)),
+                        pack_bf16x2(bf16lo_f32(v.z) + bf16lo_f32(d.z), bf16hi_f32(v.z) + bf16hi_f32(d.z)),
+                        pack_bf16x2(bf16lo_f32(v.w) + bf16lo_f32(d.w), bf16hi_f32(v.w) + bf16hi_f32(d.w)));
+                }
+            }
+        }
+#pragma unroll
+        for (int it = 0; it < kNormRegIters; ++it) {
+            const uint32_t i = (threadIdx.x + it * 128) * 8;
+            if (i < hidden) {
+                if (kResidual) *reinterpret_cast<uint4 *>(xr + i) = xv[it];
+                const uint32_t v4[4] = {xv[it].x, xv[it].y, xv[it].z, xv[it].w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float a = bf16lo_f32(v4[k]), b = bf16hi_f32(v4[k]);
+                    sum += a * a;
+                    sum += b * b;
+                }
+            }
+        }
+        const float scale = rms_scale(sum, hidden, eps);
+#pragma unroll
+        for (int it = 0; it < kNormRegIters; ++it) {
+            const uint32_t i = (threadIdx.x + it * 128) * 8;
+            if (i < hidden) {
+                const uint32_t v4[4] = {xv[it].x, xv[it].y, xv[it].z, xv[it].w};
+                const uint32_t w4[4] = {wt[it].x, wt[it].y, wt[it].z, wt[it].w};
+                uint32_t ov[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float a = bf16_round(bf16lo_f32(v4[k]) * scale) * bf16lo_f32(w4[k]);
+                    const float b = bf16_round(bf16hi_f32(v4[k]) * scale) * bf16hi_f32(w4[k]);
+                    ov[k] = pack_bf16x2(a, b);
+                }
+                *reinterpret_cast<uint4 *>(yr + i) = make_uint4(ov[0], ov[1], ov[2], ov[3]);
+            }
+        }
+        return;
+    }
     if (vec) {
         for (uint32_t i = threadIdx.x * 8; i < hidden; i += 128 * 8) {
             uint4 v = *reinterpret_cast<const uint4 *>(xr + i);
@@ -90,14 +161,7 @@ __global__ void __launch_bounds__(128)
             sum += a * a;
         }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    __shared__ float part[4];
-    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = sum;
-    __syncthreads();
-    const float total = (part[0] + part[1]) + (part[2] + part[3]);
-    const float mean = __fdiv_rn(total, (float)hidden);
-    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(mean + eps));
+    const float scale = rms_scale(sum, hidden, eps);
     // the second pass reads back only elements this thread itself wrote above
     if (vec) {
         for (uint32_t i = threadIdx.x * 8; i < hidden; i += 128 * 8) {

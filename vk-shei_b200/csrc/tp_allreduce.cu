@@ -38,13 +38,75 @@ __device__ __forceinline__ void st_relaxed_sys(uint32_t *p, uint32_t v) {
     asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// One 16-byte chunk of the row: every rank's partial summed in rank order in
+// fp32, rounded once, added to the residual; returns the new x chunk and adds
+// its squares to `sum` (element order fixed, so every rank gets the same bits).
 template <int W>
+__device__ __forceinline__ uint4 tp_reduce_chunk(const TpCommDev &c, size_t off, uint32_t i, uint4 xv,
+                                                 float &sum) {
+    uint4 p[W];
+#pragma unroll
+    for (int r = 0; r < W; ++r) p[r] = __ldcv(reinterpret_cast<const uint4 *>(c.data[r] + off + i));
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int r = 0; r < W; ++r) {
+        const uint32_t pv[4] = {p[r].x, p[r].y, p[r].z, p[r].w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            acc[2 * k] += bf16lo_f32(pv[k]);
+            acc[2 * k + 1] += bf16hi_f32(pv[k]);
+        }
+    }
+    const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+    uint32_t nw[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float a = bf16lo_f32(xw[k]) + bf16_round(acc[2 * k]);
+        const float b = bf16hi_f32(xw[k]) + bf16_round(acc[2 * k + 1]);
+        nw[k] = pack_bf16x2(a, b);
+        const float na = bf16lo_f32(nw[k]), nb = bf16hi_f32(nw[k]);
+        sum += na * na;
+        sum += nb * nb;
+    }
+    return make_uint4(nw[0], nw[1], nw[2], nw[3]);
+}
+
+__device__ __forceinline__ uint4 tp_norm_chunk(uint4 v, uint4 wt, float scale) {
+    const uint32_t xv[4] = {v.x, v.y, v.z, v.w};
+    const uint32_t wv[4] = {wt.x, wt.y, wt.z, wt.w};
+    uint32_t ov[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+        ov[k] = pack_bf16x2(bf16_round(bf16lo_f32(xv[k]) * scale) * bf16lo_f32(wv[k]),
+                            bf16_round(bf16hi_f32(xv[k]) * scale) * bf16hi_f32(wv[k]));
+    return make_uint4(ov[0], ov[1], ov[2], ov[3]);
+}
+
+// Rows up to kTpThreads * 8 * kTpRegIters elements are held in registers: this
+// rank's x and the norm weights are loaded before the wait for the peers (they
+// do not depend on them) and x is not read back for the second pass.
+constexpr int kTpRegIters = 4;
+
+template <int W, bool kReg>
 __global__ void __launch_bounds__(kTpThreads)
     mslim_tp_allreduce_rmsnorm(const TpCommDev c, uint32_t slot, uint16_t *__restrict__ x,
                                const uint16_t *__restrict__ w, uint16_t *__restrict__ y, float eps,
                                int *status) {
     const uint32_t row = blockIdx.x;
     const uint32_t hidden = c.hidden;
+    uint16_t *xr = x + (size_t)row * hidden;
+    uint16_t *yr = y + (size_t)row * hidden;
+    uint4 xv[kReg ? kTpRegIters : 1], wt[kReg ? kTpRegIters : 1];
+    if constexpr (kReg) {
+#pragma unroll
+        for (int it = 0; it < kTpRegIters; ++it) {
+            const uint32_t i = (threadIdx.x + it * kTpThreads) * 8;
+            if (i < hidden) {
+                xv[it] = *reinterpret_cast<const uint4 *>(xr + i);
+                wt[it] = *reinterpret_cast<const uint4 *>(w + i);
+            }
+        }
+    }
     __shared__ int s_ok;
     // warp 0: lane r (< W) publishes this rank's call number into rank r's
     // flags, then waits for rank r's number in this rank's flags; the lanes
@@ -77,37 +139,21 @@ __global__ void __launch_bounds__(kTpThreads)
     if (!s_ok) return;   // reported through the status word; x and y untouched
     fence_sys();
     const size_t off = ((size_t)slot * c.max_rows + row) * hidden;
-    uint16_t *xr = x + (size_t)row * hidden;
-    uint16_t *yr = y + (size_t)row * hidden;
     float sum = 0.f;
-    for (uint32_t i = threadIdx.x * 8; i < hidden; i += kTpThreads * 8) {
-        // every rank's chunk in flight at once, summed in rank order
-        uint4 p[W];
+    if constexpr (kReg) {
 #pragma unroll
-        for (int r = 0; r < W; ++r) p[r] = __ldcv(reinterpret_cast<const uint4 *>(c.data[r] + off + i));
-        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int r = 0; r < W; ++r) {
-            const uint32_t pv[4] = {p[r].x, p[r].y, p[r].z, p[r].w};
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                acc[2 * k] += bf16lo_f32(pv[k]);
-                acc[2 * k + 1] += bf16hi_f32(pv[k]);
+        for (int it = 0; it < kTpRegIters; ++it) {
+            const uint32_t i = (threadIdx.x + it * kTpThreads) * 8;
+            if (i < hidden) {
+                xv[it] = tp_reduce_chunk<W>(c, off, i, xv[it], sum);
+                *reinterpret_cast<uint4 *>(xr + i) = xv[it];
             }
         }
-        const uint4 xv = *reinterpret_cast<const uint4 *>(xr + i);
-        const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
-        uint32_t nw[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const float a = bf16lo_f32(xw[k]) + bf16_round(acc[2 * k]);
-            const float b = bf16hi_f32(xw[k]) + bf16_round(acc[2 * k + 1]);
-            nw[k] = pack_bf16x2(a, b);
-            const float na = bf16lo_f32(nw[k]), nb = bf16hi_f32(nw[k]);
-            sum += na * na;
-            sum += nb * nb;
+    } else {
+        for (uint32_t i = threadIdx.x * 8; i < hidden; i += kTpThreads * 8) {
+            const uint4 nv = tp_reduce_chunk<W>(c, off, i, *reinterpret_cast<const uint4 *>(xr + i), sum);
+            *reinterpret_cast<uint4 *>(xr + i) = nv;
         }
-        *reinterpret_cast<uint4 *>(xr + i) = make_uint4(nw[0], nw[1], nw[2], nw[3]);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
@@ -119,19 +165,28 @@ __global__ void __launch_bounds__(kTpThreads)
     for (int k = 0; k < kTpThreads / 32; ++k) total += part[k];
     const float mean = __fdiv_rn(total, (float)hidden);
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(mean + eps));
-    // reads back only the elements this thread wrote above
-    for (uint32_t i = threadIdx.x * 8; i < hidden; i += kTpThreads * 8) {
-        const uint4 v = *reinterpret_cast<const uint4 *>(xr + i);
-        const uint4 wt = *reinterpret_cast<const uint4 *>(w + i);
-        const uint32_t xv[4] = {v.x, v.y, v.z, v.w};
-        const uint32_t wv[4] = {wt.x, wt.y, wt.z, wt.w};
-        uint32_t ov[4];
+    if constexpr (kReg) {
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-            ov[k] = pack_bf16x2(bf16_round(bf16lo_f32(xv[k]) * scale) * bf16lo_f32(wv[k]),
-                                bf16_round(bf16hi_f32(xv[k]) * scale) * bf16hi_f32(wv[k]));
-        *reinterpret_cast<uint4 *>(yr + i) = make_uint4(ov[0], ov[1], ov[2], ov[3]);
+        for (int it = 0; it < kTpRegIters; ++it) {
+            const uint32_t i = (threadIdx.x + it * kTpThreads) * 8;
+            if (i < hidden) *reinterpret_cast<uint4 *>(yr + i) = tp_norm_chunk(xv[it], wt[it], scale);
+        }
+    } else {
+        // reads back only the elements this thread wrote above
+        for (uint32_t i = threadIdx.x * 8; i < hidden; i += kTpThreads * 8)
+            *reinterpret_cast<uint4 *>(yr + i) = tp_norm_chunk(*reinterpret_cast<const uint4 *>(xr + i),
+                                                               *reinterpret_cast<const uint4 *>(w + i), scale);
     }
+}
+
+template <int W>
+cudaError_t launch_w(const TpCommDev &comm, uint32_t slot, uint16_t *x, const uint16_t *w, uint16_t *y,
+                     uint32_t rows, float eps, int *status, cudaStream_t stream) {
+    if (comm.hidden <= (uint32_t)kTpThreads * 8 * kTpRegIters)
+        mslim_tp_allreduce_rmsnorm<W, true><<<rows, kTpThreads, 0, stream>>>(comm, slot, x, w, y, eps, status);
+    else
+        mslim_tp_allreduce_rmsnorm<W, false><<<rows, kTpThreads, 0, stream>>>(comm, slot, x, w, y, eps, status);
+    return cudaGetLastError();
 }
 
 }  // namespace
@@ -140,17 +195,16 @@ cudaError_t launch_tp_allreduce_rmsnorm(const TpCommDev &comm, uint32_t slot, ui
                                         const uint16_t *w, uint16_t *y, uint32_t rows, float eps,
                                         int *status, cudaStream_t stream) {
     switch (comm.world) {
-    case 1: mslim_tp_allreduce_rmsnorm<1><<<rows, kTpThreads, 0, stream>>>(comm, slot, x, w, y, eps, status); break;
-    case 2: mslim_tp_allreduce_rmsnorm<2><<<rows, kTpThreads, 0, stream>>>(comm, slot, x, w, y, eps, status); break;
-    case 3: mslim_tp_allreduce_rmsnorm<3><<<rows, kTpThreads, 0, stream>>>(comm, slot, x, w, y, eps, status); break;
-    case 4: mslim_tp_allreduce_rmsnorm<4><<<rows, kTpThreads, 0, stream>>>(comm, slot, x, w, y, eps, status); break;
-    case 5: mslim_tp_allreduce_rmsnorm<5><<<rows, kTpThreads, 0, stream>>>(comm, slot, x, w, y, eps, status); break;
-    case 6: mslim_tp_allreduce_rmsnorm<6><<<rows, kTpThreads, 0, stream>>>(comm, slot, x, w, y, eps, status); break;
-    case 7: mslim_tp_allreduce_rmsnorm<7><<<rows, kTpThreads, 0, stream>>>(comm, slot, x, w, y, eps, status); break;
-    case 8: mslim_tp_allreduce_rmsnorm<8><<<rows, kTpThreads, 0, stream>>>(comm, slot, x, w, y, eps, status); break;
+    case 1: return launch_w<1>(comm, slot, x, w, y, rows, eps, status, stream);
+    case 2: return launch_w<2>(comm, slot, x, w, y, rows, eps, status, stream);
+    case 3: return launch_w<3>(comm, slot, x, w, y, rows, eps, status, stream);
+    case 4: return launch_w<4>(comm, slot, x, w, y, rows, eps, status, stream);
+    case 5: return launch_w<5>(comm, slot, x, w, y, rows, eps, status, stream);
+    case 6: return launch_w<6>(comm, slot, x, w, y, rows, eps, status, stream);
+    case 7: return launch_w<7>(comm, slot, x, w, y, rows, eps, status, stream);
+    case 8: return launch_w<8>(comm, slot, x, w, y, rows, eps, status, stream);
     default: return cudaErrorInvalidValue;
     }
-    return cudaGetLastError();
 }
 
 }  // namespace mslim
