@@ -454,17 +454,6 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
     return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args &&>(args)...);
 }
 
-// Register budget moves between warpgroups (all four warps of a warpgroup
-// execute the same instruction).
-template <uint32_t N>
-__device__ __forceinline__ void warpgroup_reg_dealloc() {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
-}
-template <uint32_t N>
-__device__ __forceinline__ void warpgroup_reg_alloc() {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
-}
-
 // 2^x on the FMA/ALU pipes only (offloads the MUFU unit): n = round(x) by
 // adding 1.5 * 2^23 (the integer lands in the low mantissa bits, no
 // float->int conversion, which would itself use the MUFU/XU pipe), f = x - n in

@@ -349,8 +349,10 @@ __global__ void __launch_bounds__(kSThreads, 1)
 //   Across items the K/V rings and the per-tile barriers keep counting; Q of
 //   the next item is loaded as soon as the current item's last S MMAs have
 //   completed, so the next item's S(0) overlaps the current output write.
-//   Warps: 0 TMA K, 1 MMA, 2 TMA V, 3 TMA Q (warpgroup 0, 88 registers);
-//          4-7 softmax head A, 8-11 softmax head B (200 registers each).
+//   Warps: 0 TMA K, 1 MMA, 2 TMA V, 3 TMA Q; 4-7 softmax head A, 8-11
+//          softmax head B.  ptxas compiles every path within the registers the
+//          launch allows (__launch_bounds__(384, 1): 168 per thread), and one CTA
+//          fills the SM, so the kernel moves no registers between warpgroups.
 constexpr int kPOffQ = 0;                           // Q_h at h * kQBytes
 constexpr int kPOffK = 2 * kQBytes;                 // K slot s at kPOffK + s * kTileBytes
 constexpr int kPOffV = kPOffK + 2 * kTileBytes;
@@ -359,15 +361,6 @@ constexpr int kPOffBar = kPOffStage + 2 * kBox;
 constexpr int kPSmemBytes = kPOffBar + 512 + 1024;
 static_assert(kPSmemBytes <= 227 * 1024, "shared memory per block");
 constexpr int kPThreads = 12 * 32;
-// setmaxnreg split: warpgroup 0 shrinks to kPRegsCtl, the two softmax
-// warpgroups grow to kPRegsSoftmax.  The grown share is drawn from the
-// registers the block was launched with (kPThreads x the per-thread count that
-// __launch_bounds__(kPThreads, 1) allows, 168), so the sum must stay within it
-// or setmaxnreg.inc would never be granted.
-constexpr int kPRegsCtl = 88, kPRegsSoftmax = 200, kPRegsLaunch = 168;
-static_assert(128 * kPRegsCtl + 256 * kPRegsSoftmax <= kPThreads * kPRegsLaunch,
-              "register split exceeds the launch allocation");
-static_assert(kPRegsCtl % 8 == 0 && kPRegsSoftmax % 8 == 0, "setmaxnreg counts are multiples of 8");
 
 struct PairBars {
     uint64_t q_full, q_empty;  // once per item
@@ -443,7 +436,6 @@ __global__ void __launch_bounds__(kPThreads, 1)
     griddep_wait();
 
     if (warp < 4) {
-        warpgroup_reg_dealloc<kPRegsCtl>();
         if ((warp == 0 || warp == 2) && lane == 0) {
             // -------------------------------------------------- TMA K / V --
             const bool is_k = warp == 0;
@@ -557,7 +549,6 @@ __global__ void __launch_bounds__(kPThreads, 1)
             if (!ok && lane == 0) *abort_flag = 1;
         }
     } else {
-        warpgroup_reg_alloc<kPRegsSoftmax>();
         // ---------------------------------------------------------- softmax --
         // warpgroup 1 (warps 4-7) owns head qh0, warpgroup 2 (8-11) head qh0 + 1;
         // one thread per query row, all 128 keys of a tile
@@ -708,7 +699,7 @@ bool prefill_pairs_heads(unsigned group) { return group % 2 == 0; }
 namespace {
 
 // Per-device launch setup, done once: shared-memory opt-in for both kernels,
-// the register check of the pair kernel's setmaxnreg split, and the SM count.
+// and the SM count.
 struct PrefillDeviceSetup {
     std::atomic<int> state{0};  // 0 not yet, 1 ready, 2 failed
     cudaError_t err = cudaSuccess;
@@ -729,11 +720,6 @@ cudaError_t prefill_setup(int dev, int *sms) {
             if (err == cudaSuccess)
                 err = cudaFuncSetAttribute(mslim_prefill_causal,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, kSSmemBytes);
-            cudaFuncAttributes fa{};
-            if (err == cudaSuccess) err = cudaFuncGetAttributes(&fa, mslim_prefill_pair);
-            // the setmaxnreg split needs the registers it assumes at launch
-            if (err == cudaSuccess && fa.numRegs * kPThreads < 128 * kPRegsCtl + 256 * kPRegsSoftmax)
-                err = cudaErrorInvalidConfiguration;
             if (err == cudaSuccess) err = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
             d.err = err;
             d.state.store(err == cudaSuccess ? 1 : 2, std::memory_order_release);
