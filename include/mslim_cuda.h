@@ -212,6 +212,28 @@ int mslim_cuda_prefill_causal(const mslim_geometry_t *geometry, const void *q, c
                               const void *v, void *out, uint32_t queries, uint32_t prior,
                               void *stream);
 
+/* Logical K/V serialisation of one session and layer, for the validation
+ * digest `logical_kv_sha256` (GpuLlm::logical_kv_sha256,
+ * src/gpu_llm/mod.rs:1981-2023, dense caches; GpuRegionStore::logical_kv_sha256,
+ * src/gpu_region_store.rs:338-371, ColdStore pages; both hash
+ * "mslim-dense-kv-state-v1", the token count as u64 LE, then per layer K and
+ * V, each ordered [kv_heads][tokens][head_dim]).  These write one such
+ * tensor, out: bf16 [kv_heads][tokens][head_dim] on the device, from
+ *   dense: cache = one session's token-major rows [>= tokens][kv_heads][head_dim];
+ *   paged: pool [n_pages][kv_heads][page_tokens][head_dim] (the ColdStore-exact
+ *          page layout) and page_row = the session's device page table row
+ *          (logical page -> physical page, max_pages entries), i.e. the
+ *          GpuRegionStore::read_keys / read_values gather
+ *          (src/gpu_region_store.rs:828-931) in head-major order.
+ * The host hashes the stream (the reference does the same after its
+ * read-back).  A page id outside the pool leaves its rows unwritten and is
+ * reported by mslim_cuda_device_status. */
+int mslim_cuda_kv_canonical_dense(const void *cache, uint32_t kv_heads, uint32_t head_dim, uint32_t tokens,
+                                  void *out, void *stream);
+int mslim_cuda_kv_canonical_paged(const void *pool, uint32_t n_pages, uint32_t kv_heads, uint32_t page_tokens,
+                                  uint32_t head_dim, const int32_t *page_row, uint32_t max_pages,
+                                  uint32_t tokens, void *out, void *stream);
+
 /* ColdStore page sealing from device pages: the per-token FNV-1a 64 hashes of
  * a page record (src/cold_store.rs:725-742 token_hashes; computed by the
  * writer in GpuRegionStore::append_batch, src/gpu_region_store.rs:391-522)

@@ -282,6 +282,45 @@ def token_hashes(page_payload: np.ndarray, heads: int, tokens: int) -> np.ndarra
     return out
 
 
+def logical_kv_sha256(tokens: int, layers, kv_heads: int, head_dim: int) -> str:
+    """The validation digest of the logical K/V state, restated row by row
+    from GpuLlm::logical_kv_sha256 (src/gpu_llm/mod.rs:1981-2023) and
+    GpuRegionStore::logical_kv_sha256 (src/gpu_region_store.rs:338-371):
+    "mslim-dense-kv-state-v1", tokens as u64 LE, then for each layer (K, V)
+    its token-major rows [tokens][kv_heads][head_dim] visited head-major
+    (for head: for token: the head_dim bf16 values of that row).
+    layers: list of (k, v) uint16 arrays shaped [>= tokens][kv_heads][head_dim].
+    SHA-256 is Python's hashlib (FIPS 180-4), as the reference uses the sha2
+    crate."""
+    import hashlib
+    import struct
+    h = hashlib.sha256()
+    h.update(b"mslim-dense-kv-state-v1")
+    h.update(struct.pack("<Q", int(tokens)))
+    for k, v in layers:
+        for tm in (k, v):
+            a = np.ascontiguousarray(tm, np.uint16).reshape(-1, kv_heads, head_dim)[:tokens]
+            for head in range(kv_heads):
+                for token in range(tokens):
+                    h.update(a[token, head].tobytes())
+    return h.hexdigest()
+
+
+def logical_kv_sha256_fast(tokens: int, layers, kv_heads: int, head_dim: int) -> str:
+    """logical_kv_sha256 with each tensor transposed to [kv_heads][tokens][head_dim]
+    first (the same bytes in the same order; for large states)."""
+    import hashlib
+    import struct
+    h = hashlib.sha256()
+    h.update(b"mslim-dense-kv-state-v1")
+    h.update(struct.pack("<Q", int(tokens)))
+    for k, v in layers:
+        for tm in (k, v):
+            a = np.ascontiguousarray(tm, np.uint16).reshape(-1, kv_heads, head_dim)[:tokens]
+            h.update(np.ascontiguousarray(a.transpose(1, 0, 2)).tobytes())
+    return h.hexdigest()
+
+
 def page_from_token_major(token_major: np.ndarray, kv_heads: int, head_dim: int) -> np.ndarray:
     """src/gpu_region_store.rs:470-483 for one page."""
     t = np.ascontiguousarray(token_major, np.uint16).reshape(-1)

@@ -212,3 +212,29 @@ def test_page_token_hashes_match_the_coldstore_record(m, oracle, tokens):
         payload = np.ascontiguousarray(pool[p][:, :tokens, :])
         assert np.array_equal(got[i], oracle.token_hashes(payload, kvh, tokens))
     assert m.device_status(0) == 0
+
+
+def test_kv_canonical_paged_reads_pages_in_order_and_rejects_bad_ids():
+    """mslim_cuda_kv_canonical_paged: the session's pages, listed by its page
+    table row, come out head-major [kv_heads][tokens][head_dim]; a page id
+    outside the pool writes nothing for its rows and sets the status word."""
+    import torch
+    import mslim_b200 as m
+    from gpu_util import dev, host_u16
+    rng = np.random.default_rng(17)
+    kvh, pt, d, n_pages, tokens = 3, 16, 24, 6, 70
+    pool = rng.integers(0, 65536, size=(n_pages, kvh, pt, d), dtype=np.uint16)
+    row = np.array([4, 0, 5, 2, 1], np.int32)          # 5 logical pages for 70 tokens
+    out = torch.zeros((kvh, tokens, d), dtype=torch.int16, device="cuda:0")
+    m.kv_canonical_paged(dev(pool), n_pages, kvh, pt, d, dev(row), len(row), tokens, out)
+    assert m.device_status(0) == 0
+    want = np.stack([np.concatenate([pool[row[t // pt], h, t % pt][None] for t in range(tokens)])
+                     for h in range(kvh)])
+    assert np.array_equal(host_u16(out), want)
+    bad = row.copy()
+    bad[2] = n_pages                                     # outside the pool
+    out.zero_()
+    m.kv_canonical_paged(dev(pool), n_pages, kvh, pt, d, dev(bad), len(bad), tokens, out)
+    assert m.device_status(0) == 2                       # MSLIM_ERR_SHAPE_MISMATCH
+    got = host_u16(out)
+    assert not got[:, 2 * pt:3 * pt].any() and np.array_equal(got[:, :2 * pt], want[:, :2 * pt])

@@ -48,6 +48,7 @@ def c3(oracle):
         if mode == "dense":
             runs[mode]["k_cache"] = u16(L.k_cache)
             runs[mode]["v_cache"] = u16(L.v_cache)
+        runs[mode]["kv_sha256"] = L.logical_kv_sha256()
         del L
     # the CPU path, token by token (forward_token over one layer)
     lo = oracle.LayerOracle(weights, spec.hidden, spec.intermediate, spec.query_heads, spec.kv_heads,
@@ -64,6 +65,19 @@ def test_c3_dense_and_coldstore_are_bit_exact(c3):
     for sd, sc in zip(d["decode"], c["decode"]):
         for a, b in zip(sd, sc):
             assert np.array_equal(a, b), "decode step differs between dense and ColdStore KV"
+
+
+def test_c3_logical_kv_digest_dense_equals_coldstore(c3, oracle):
+    """The adapters' validation digest (src/gpu_llm/mod.rs:1981-2023,
+    src/gpu_region_store.rs:338-371) over the 520 committed tokens: the dense
+    caches and the ColdStore-exact pages hold the same bf16 K/V, and the
+    device-ordered bytes hash like the CPU restatement of the serialisation."""
+    d, c = c3["runs"]["dense"], c3["runs"]["coldstore"]
+    spec = c3["spec"]
+    T = PREFILL + DECODE
+    assert d["kv_sha256"] == c["kv_sha256"]
+    want = oracle.logical_kv_sha256_fast(T, [(d["k_cache"], d["v_cache"])], spec.kv_heads, spec.head_dim)
+    assert d["kv_sha256"] == want
 
 
 def test_c3_attention_matches_cpu_on_the_device_inputs(c3, oracle):

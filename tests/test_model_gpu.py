@@ -89,3 +89,17 @@ def test_model_greedy_tokens_match_cpu_path(runs, oracle):
           f"logits max-abs vs CPU {worst:.3g}")
     assert exact >= BATCH * (STEPS + 1) - 2
     assert worst < 0.25
+
+
+def test_model_logical_kv_digest_dense_equals_coldstore(runs, oracle):
+    """Per session, over every layer: the dense caches and the ColdStore-exact
+    pages give the same logical K/V digest, equal to the CPU restatement's over
+    the dense caches read back (src/gpu_llm/mod.rs:1981-2023)."""
+    (Md, spec, *_), (Mc, *_) = runs
+    L = spec.layer
+    for b in range(BATCH):
+        sd = Md.logical_kv_sha256(b)
+        assert sd == Mc.logical_kv_sha256(b), b
+        T = int(Md.lengths[b].item())
+        layers = [(_u16(Md.k_cache[li][b]), _u16(Md.v_cache[li][b])) for li in range(spec.layers)]
+        assert sd == oracle.logical_kv_sha256_fast(T, layers, L.kv_heads, L.head_dim), b

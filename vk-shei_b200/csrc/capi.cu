@@ -780,6 +780,38 @@ int mslim_cuda_page_token_hashes(const void *pool, uint32_t n_pool_pages, uint32
     return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "page hash launch");
 }
 
+int mslim_cuda_kv_canonical_dense(const void *cache, uint32_t kv_heads, uint32_t head_dim, uint32_t tokens,
+                                  void *out, void *stream) {
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    if (!cache || !out) return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
+    if (kv_heads == 0 || head_dim == 0) return fail(MSLIM_ERR_INVALID_GEOMETRY, "empty KV geometry");
+    if (tokens == 0) return MSLIM_OK;
+    if (out == cache) return fail(MSLIM_ERR_SHAPE_MISMATCH, "output must not alias the cache");
+    cudaError_t err = mslim::launch_kv_canonical(static_cast<const uint16_t *>(cache), static_cast<uint16_t *>(out),
+                                                 kv_heads, tokens, head_dim, nullptr, 0, 0, status_ptr(dev),
+                                                 static_cast<cudaStream_t>(stream));
+    return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "canonical KV launch");
+}
+
+int mslim_cuda_kv_canonical_paged(const void *pool, uint32_t n_pages, uint32_t kv_heads, uint32_t page_tokens,
+                                  uint32_t head_dim, const int32_t *page_row, uint32_t max_pages, uint32_t tokens,
+                                  void *out, void *stream) {
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    if (!pool || !page_row || !out) return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
+    if (kv_heads == 0 || head_dim == 0 || page_tokens == 0 || n_pages == 0)
+        return fail(MSLIM_ERR_INVALID_GEOMETRY, "empty page geometry");
+    if (tokens == 0) return MSLIM_OK;
+    if ((uint64_t)tokens > (uint64_t)max_pages * page_tokens)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "more tokens than the session's pages hold");
+    if (out == pool) return fail(MSLIM_ERR_SHAPE_MISMATCH, "output must not alias the pool");
+    cudaError_t err = mslim::launch_kv_canonical(static_cast<const uint16_t *>(pool), static_cast<uint16_t *>(out),
+                                                 kv_heads, tokens, head_dim, page_row, page_tokens, n_pages,
+                                                 status_ptr(dev), static_cast<cudaStream_t>(stream));
+    return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "canonical KV launch");
+}
+
 int mslim_cuda_gemv(const void *x, const void *w, void *y, uint32_t m, uint32_t n, uint32_t k, void *stream) {
     int dev;
     if (int rc = current_device(&dev)) return rc;

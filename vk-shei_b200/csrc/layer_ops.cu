@@ -13,6 +13,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <climits>
 #include <cstdint>
 
@@ -280,7 +281,65 @@ unsigned elt_grid(uint64_t n) {
     return (unsigned)(vec == 0 ? 1 : (vec < cap ? vec : cap));
 }
 
+// Canonical logical K (or V) rows of one session and layer: out[h][t][0..D)
+// for h < kv_heads, t < tokens, the per-tensor byte order of the logical KV
+// digest (K then V, layer-major, each [kv_heads][tokens][head_dim]).  Source
+// rows: a token-major dense cache (page_row == null: row (t, h) at
+// src + (t * kv_heads + h) * D) or ColdStore-exact pool pages (logical page
+// t / page_tokens -> physical page page_row[..], head-major inside the page).
+// One thread per eight-element chunk (D % 8 == 0, 16-byte aligned) or per
+// element otherwise.  A page id outside the pool writes nothing for that row
+// and is recorded in the status word.
+template <bool kVec>
+__global__ void __launch_bounds__(256)
+    mslim_kv_canonical(const uint16_t *__restrict__ src, uint16_t *__restrict__ out, uint32_t kv_heads,
+                       uint32_t tokens, uint32_t dim, const int32_t *__restrict__ page_row,
+                       uint32_t page_tokens, uint32_t n_pages, int *status) {
+    constexpr uint32_t kW = kVec ? 8 : 1;
+    const uint32_t per_row = dim / kW;
+    const uint64_t total = (uint64_t)kv_heads * tokens * per_row;
+    for (uint64_t x = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; x < total;
+         x += (uint64_t)gridDim.x * blockDim.x) {
+        const uint32_t c = (uint32_t)(x % per_row);
+        const uint64_t ht = x / per_row;
+        const uint32_t t = (uint32_t)(ht % tokens), h = (uint32_t)(ht / tokens);
+        const uint16_t *row;
+        if (page_row) {
+            const int32_t phys = page_row[t / page_tokens];
+            if (phys < 0 || (uint32_t)phys >= n_pages) {
+                if (status) atomicExch(status, MSLIM_DEVICE_BAD_PAGE_CODE);
+                continue;
+            }
+            row = src + (((size_t)phys * kv_heads + h) * page_tokens + t % page_tokens) * dim;
+        } else {
+            row = src + ((size_t)t * kv_heads + h) * dim;
+        }
+        uint16_t *dst = out + ((size_t)h * tokens + t) * dim;
+        if constexpr (kVec)
+            *reinterpret_cast<uint4 *>(dst + c * 8) = *reinterpret_cast<const uint4 *>(row + c * 8);
+        else
+            dst[c] = row[c];
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_kv_canonical(const uint16_t *src, uint16_t *out, uint32_t kv_heads, uint32_t tokens,
+                                uint32_t dim, const int32_t *page_row, uint32_t page_tokens, uint32_t n_pages,
+                                int *status, cudaStream_t stream) {
+    if (tokens == 0) return cudaSuccess;
+    auto al = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    const bool vec = dim % 8 == 0 && al(src) && al(out);
+    const uint64_t total = (uint64_t)kv_heads * tokens * (vec ? dim / 8 : dim);
+    const unsigned grid = (unsigned)std::min<uint64_t>((total + 255) / 256, 148ull * 16);
+    if (vec)
+        mslim_kv_canonical<true><<<grid, 256, 0, stream>>>(src, out, kv_heads, tokens, dim, page_row, page_tokens,
+                                                            n_pages, status);
+    else
+        mslim_kv_canonical<false><<<grid, 256, 0, stream>>>(src, out, kv_heads, tokens, dim, page_row, page_tokens,
+                                                             n_pages, status);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_residual_add(const uint16_t *a, const uint16_t *b, uint16_t *out, uint64_t n,
                                 cudaStream_t stream) {

@@ -29,5 +29,12 @@ cudaError_t launch_page_token_hashes(const uint16_t *pool, uint32_t n_pool_pages
 // equals, NaN never chosen unless every entry is NaN (the OpenCL llm_argmax).
 cudaError_t launch_argmax(const uint16_t *logits, uint32_t rows, uint32_t n, int ties_to_last,
                           int32_t *out, cudaStream_t stream);
+// out [kv_heads][tokens][dim] bf16: one session's K (or V) rows in the logical
+// KV digest order, from a token-major dense cache (page_row == null) or from
+// ColdStore-exact pool pages [n_pages][kv_heads][page_tokens][dim] listed by
+// page_row (logical page -> physical page).
+cudaError_t launch_kv_canonical(const uint16_t *src, uint16_t *out, uint32_t kv_heads, uint32_t tokens,
+                                uint32_t dim, const int32_t *page_row, uint32_t page_tokens, uint32_t n_pages,
+                                int *status, cudaStream_t stream);
 
 }  // namespace mslim

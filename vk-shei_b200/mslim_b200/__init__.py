@@ -11,7 +11,8 @@ from .attention import (AttentionGeometry, AttentionKernelConfig, AttentionKerne
                         TiledAttention, UnsupportedDevice, check, decode_dense, decode_paged, decode_paged_static_scratch,
                         decode_workspace_bytes, device_status, prefill_causal, rmsnorm, rope,
                         rope_append_decode_dense, rope_append_decode_paged, rope_append_paged, residual_add, swiglu,
-                        argmax, swiglu_rows, residual_rmsnorm, gemv, page_token_hashes, rope_append_decode_dense_qkv,
+                        argmax, swiglu_rows, residual_rmsnorm, gemv, page_token_hashes, kv_canonical_dense, kv_canonical_paged,
+                        rope_append_decode_dense_qkv,
                         rope_append_decode_paged_qkv)
 
 LIB_PATH = _lib.LIB_PATH

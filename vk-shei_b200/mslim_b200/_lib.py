@@ -82,6 +82,8 @@ SIGNATURES = {
     "mslim_cuda_swiglu": (_int, [_vp, _vp, _vp, ctypes.c_uint64, _vp]),
     "mslim_cuda_gemv": (_int, [_vp, _vp, _vp, _u32, _u32, _u32, _vp]),
     "mslim_cuda_page_token_hashes": (_int, [_vp, _u32, _u32, _u32, _u32, _vp, _u32, _u32, _vp, _vp]),
+    "mslim_cuda_kv_canonical_dense": (_int, [_vp, _u32, _u32, _u32, _vp, _vp]),
+    "mslim_cuda_kv_canonical_paged": (_int, [_vp, _u32, _u32, _u32, _u32, _vp, _u32, _u32, _vp, _vp]),
     "mslim_cuda_swiglu_rows": (_int, [_vp, _vp, _u32, _u32, _vp]),
     "mslim_cuda_argmax": (_int, [_vp, _u32, _u32, _int, _vp, _vp]),
     "mslim_cuda_residual_rmsnorm": (_int, [_vp, _vp, _vp, _vp, _u32, _u32, ctypes.c_float, _vp]),

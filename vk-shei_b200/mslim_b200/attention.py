@@ -320,6 +320,21 @@ def page_token_hashes(pool, n_pool_pages: int, kv_heads: int, page_tokens: int, 
                                                   _ptr(page_ids), n_pages, tokens, _ptr(hashes), _stream(stream)))
 
 
+def kv_canonical_dense(cache, kv_heads: int, head_dim: int, tokens: int, out, stream=None) -> None:
+    """One session's token-major K (or V) rows -> out [kv_heads][tokens][head_dim]
+    (the logical KV digest order, src/gpu_llm/mod.rs:1981-2023)."""
+    check(_lib.lib().mslim_cuda_kv_canonical_dense(_ptr(cache), kv_heads, head_dim, tokens, _ptr(out),
+                                                   _stream(stream)))
+
+
+def kv_canonical_paged(pool, n_pages: int, kv_heads: int, page_tokens: int, head_dim: int, page_row,
+                       max_pages: int, tokens: int, out, stream=None) -> None:
+    """One session's ColdStore-exact pages -> out [kv_heads][tokens][head_dim]
+    (src/gpu_region_store.rs:338-371, the read_keys/read_values gather)."""
+    check(_lib.lib().mslim_cuda_kv_canonical_paged(_ptr(pool), n_pages, kv_heads, page_tokens, head_dim,
+                                                   _ptr(page_row), max_pages, tokens, _ptr(out), _stream(stream)))
+
+
 def gemv(x, w, y, m: int, n: int, k: int, stream=None) -> None:
     """y[m][n] = bf16(x[m][k] . w[n][k]) for 1..16 rows (the decode projections)."""
     check(_lib.lib().mslim_cuda_gemv(_ptr(x), _ptr(w), _ptr(y), m, n, k, _stream(stream)))

@@ -203,3 +203,30 @@ class DeviceLayer:
         x = self._mlp_residual(x, attn)
         self.position = p + 1
         return x, q_r, attn
+
+    def canonical_kv(self):
+        """(K, V) of the committed tokens as device tensors [kv_heads][tokens][head_dim],
+        the logical KV digest order, read from whichever store this layer uses."""
+        t, s, T = self.torch, self.spec, self.position
+        k = t.empty((s.kv_heads, T, s.head_dim), dtype=t.bfloat16, device=self.device)
+        v = t.empty_like(k)
+        if self.kv_mode == "dense":
+            _att.kv_canonical_dense(self.k_cache, s.kv_heads, s.head_dim, T, k)
+            _att.kv_canonical_dense(self.v_cache, s.kv_heads, s.head_dim, T, v)
+        else:
+            for pool, dst in ((self.k_pool, k), (self.v_pool, v)):
+                _att.kv_canonical_paged(pool, self.max_pages, s.kv_heads, self.page_tokens, s.head_dim,
+                                        self.page_table[0], self.max_pages, T, dst)
+        return k, v
+
+    def logical_kv_sha256(self) -> str:
+        """The adapters' validation digest over this one layer's K/V state
+        (src/gpu_llm/mod.rs:1981-2023): equal for the dense and the
+        ColdStore-exact store when they hold the same bf16 K/V."""
+        from .digest import LogicalKvHasher, device_tensor_bytes
+        hasher = LogicalKvHasher(self.position)
+        k, v = self.canonical_kv()
+        hasher.add(device_tensor_bytes(self.torch, k), device_tensor_bytes(self.torch, v))
+        if _att.device_status(self.device.index or 0) != 0:
+            raise _att.ShapeMismatch("a page id outside the pool while reading the K/V state")
+        return hasher.hexdigest()

@@ -365,6 +365,35 @@ class DeviceModel:
             self.lengths.add_(1)
         return self._lm_head_argmax(n)
 
+    # --------------------------------------------------- validation digest --
+    def logical_kv_sha256(self, session: int = 0) -> str:
+        """The adapters' validation digest of one session's K/V state over
+        all layers (GpuLlm::logical_kv_sha256, src/gpu_llm/mod.rs:1981-2023):
+        "mslim-dense-kv-state-v1", the session's token count, then per layer K
+        and V ordered [kv_heads][tokens][head_dim] (this rank's KV heads).
+        Equal for the dense and the ColdStore-exact store when they hold the
+        same bf16 K/V."""
+        from .digest import LogicalKvHasher, device_tensor_bytes
+        t, D = self.torch, self.spec.layer.head_dim
+        T = int(self.lengths[session].item())
+        hasher = LogicalKvHasher(T)
+        k = t.empty((self.kvh, T, D), dtype=t.bfloat16, device=self.device)
+        v = t.empty_like(k)
+        for li in range(self.spec.layers):
+            if self.kv_mode == "dense":
+                _att.kv_canonical_dense(self.k_cache[li][session], self.kvh, D, T, k)
+                _att.kv_canonical_dense(self.v_cache[li][session], self.kvh, D, T, v)
+            else:
+                row = self.page_table[session]
+                _att.kv_canonical_paged(self.k_pool[li], self.n_pages, self.kvh, self.page_tokens, D, row,
+                                        self.max_pages, T, k)
+                _att.kv_canonical_paged(self.v_pool[li], self.n_pages, self.kvh, self.page_tokens, D, row,
+                                        self.max_pages, T, v)
+            hasher.add(device_tensor_bytes(t, k), device_tensor_bytes(t, v))
+        if _att.device_status(self.device.index or 0) != 0:
+            raise _att.ShapeMismatch("a page id outside the pool while reading the K/V state")
+        return hasher.hexdigest()
+
     # ------------------------------------------------------- graph decode --
     def capture_decode(self):
         """Captures one whole decode step (every layer, the all-reduces, the
