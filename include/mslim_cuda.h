@@ -431,6 +431,17 @@ int mslim_cuda_backend_last_timings(const mslim_backend_t *backend, char *out, s
 /* Library version string (for diagnostics). */
 const char *mslim_cuda_version(void);
 
+/* Hex SHA-256 of the sources this library was built from (every CUDA source,
+ * device header, this header and the build recipe, each hashed as its length
+ * u64 LE then its bytes, then the target architecture flags).  The reference's
+ * calibration profile identity, implementation_digest
+ * (src/calibration_profile.rs:90-125), hashes its kernel sources
+ * (assets/gpu_llm.cl, assets/tiled_attention.cl, src/gpu_llm/...) the same
+ * way; with this library in their place it folds this string in instead, so a
+ * profile recorded against one build of the kernels is not reused with
+ * another.  "unknown" when built without the recipe. */
+const char *mslim_cuda_implementation_digest(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -41,6 +41,19 @@ def test_static_archive_and_shared_library_built():
     assert os.path.exists(os.path.join(base, "libmslim_cuda.a"))
 
 
+def test_implementation_digest_names_the_sources_the_library_was_built_from(m):
+    """mslim_cuda_implementation_digest, the library's share of the
+    calibration profile identity (src/calibration_profile.rs:90-125): the
+    digest the build recipe computes over the current sources."""
+    import sys
+    from mslim_b200 import _lib
+    sys.path.insert(0, os.path.join(ROOT, "vk-shei_b200"))
+    import build
+    got = _lib.lib().mslim_cuda_implementation_digest().decode()
+    assert re.fullmatch(r"[0-9a-f]{64}", got)
+    assert got == build.source_digest(), "the loaded library was built from other sources"
+
+
 def test_default_is_reference_and_experimental_opt_in_is_mandatory(m):
     # src/attention_kernel.rs:145-158
     assert m.AttentionKernelConfig.from_json("{}") == m.AttentionKernelConfig()

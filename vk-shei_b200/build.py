@@ -30,6 +30,30 @@ SO = os.path.join(OUT_DIR, "libmslim_cuda.so")
 AR = os.path.join(OUT_DIR, "libmslim_cuda.a")
 
 
+def digest_files() -> list[str]:
+    """The files whose bytes define the library: the CUDA sources in build
+    order, the device headers (sorted), the C ABI header and this recipe."""
+    heads = sorted(f for f in os.listdir(CSRC) if f.endswith((".cuh", ".h")))
+    return ([os.path.join(CSRC, f) for f in SOURCES] + [os.path.join(CSRC, f) for f in heads] +
+            [os.path.join(INCLUDE, "mslim_cuda.h"), os.path.abspath(__file__)])
+
+
+def source_digest() -> str:
+    """SHA-256 over every digest file as (length u64 LE, bytes), then the
+    target architecture flags -- the library's counterpart of the reference's
+    implementation_digest (src/calibration_profile.rs:90-125), which hashes
+    its kernel and runtime sources the same way."""
+    import hashlib
+    import struct
+    h = hashlib.sha256()
+    for f in digest_files():
+        data = open(f, "rb").read()
+        h.update(struct.pack("<Q", len(data)))
+        h.update(data)
+    h.update(" ".join(ARCH).encode())
+    return h.hexdigest()
+
+
 def _headers() -> list[str]:
     hs = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cuh", ".h"))]
     return hs + [os.path.join(INCLUDE, f) for f in os.listdir(INCLUDE) if f.endswith(".h")]
@@ -45,8 +69,13 @@ def _stale(target: str, deps: list[str]) -> bool:
 def _compile(src: str, force: bool) -> str:
     obj = os.path.join(OBJ_DIR, os.path.splitext(src)[0] + ".o")
     path = os.path.join(CSRC, src)
-    if force or _stale(obj, [path] + _headers()):
-        cmd = [NVCC, *ARCH, *FLAGS, "-c", path, "-o", obj]
+    extra, deps = [], [path] + _headers()
+    if src == "capi.cu":
+        # the C ABI carries the digest of every source, so it follows all of them
+        extra = [f"-DMSLIM_SOURCE_DIGEST=\"{source_digest()}\""]
+        deps = digest_files()
+    if force or _stale(obj, deps):
+        cmd = [NVCC, *ARCH, *FLAGS, *extra, "-c", path, "-o", obj]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"nvcc failed for {src}:\n{r.stdout}\n{r.stderr}")

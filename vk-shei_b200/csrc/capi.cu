@@ -431,6 +431,11 @@ const char *mslim_cuda_last_error(void) { return g_last_error.c_str(); }
 
 const char *mslim_cuda_version(void) { return "mslim-cuda 0.1.0 (sm_100a)"; }
 
+#ifndef MSLIM_SOURCE_DIGEST
+#define MSLIM_SOURCE_DIGEST "unknown"  // built outside vk-shei_b200/build.py
+#endif
+const char *mslim_cuda_implementation_digest(void) { return MSLIM_SOURCE_DIGEST; }
+
 int mslim_cuda_device_status(int device, int reset, int *status) {
     if (!status) return fail(MSLIM_ERR_SHAPE_MISMATCH, "status pointer is null");
     int prev;

@@ -60,6 +60,7 @@ _R = ctypes.POINTER(RopeConfig)
 SIGNATURES = {
     "mslim_cuda_last_error": (ctypes.c_char_p, []),
     "mslim_cuda_version": (ctypes.c_char_p, []),
+    "mslim_cuda_implementation_digest": (ctypes.c_char_p, []),
     "mslim_cuda_device_status": (_int, [_int, _int, ctypes.POINTER(_int)]),
     "mslim_cuda_geometry_validate": (_int, [_G]),
     "mslim_cuda_config_default": (KernelConfig, []),
