@@ -427,6 +427,9 @@ class TiledAttention:
         g = geometry or self.geometry
         if g != self.geometry:
             raise ShapeMismatch("kernel specialization does not match geometry")
+        if queries < 0 or prior < 0 or queries + prior > 0x7fffffff:
+            # checked_add and the indexing bound (tiled_attention.rs:182-188; the kernels index in i32)
+            raise ShapeMismatch("attention history exceeds the indexing bound")
         check(_lib.lib().mslim_cuda_plan_run(self._h, _ptr(q), _nbytes(q), _ptr(k), _nbytes(k), _ptr(v),
                                              _nbytes(v), _ptr(output), _nbytes(output), queries, prior,
                                              _stream(stream)))
