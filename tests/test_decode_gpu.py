@@ -149,6 +149,29 @@ def test_dense_and_coldstore_pages_bit_exact(m, wl, oracle, page_tokens, split_t
         assert max_abs(bf16_f32(paged[s]).reshape(-1), ref) <= TOL
 
 
+def test_dense_and_coldstore_bit_exact_for_many_context_lengths(m, wl, oracle):
+    """The reference's exact-hot parity sweep (src/gpu_llm/mod.rs:4311-4415,
+    T in 1..2048): every context length around the 64-token tile and
+    256-token page edges, one session each, dense caches against
+    ColdStore-exact pages in one batched call, bitwise; each within the
+    tolerance of the CPU path."""
+    g = m.AttentionGeometry.new(32, 8, 128)
+    rng = np.random.default_rng(4311)
+    edges = [1, 2, 3, 7, 31, 32, 33, 63, 64, 65, 127, 128, 129, 191, 255, 256, 257, 383, 511, 512, 513,
+             767, 1023, 1024, 1025, 1279, 1535, 1791, 2047, 2048]
+    for page_tokens in (64, 256):
+        pool = build_pool(wl, rng, edges, 8, 128, page_tokens)
+        q = rand_bf16(wl, rng, (len(edges), 32, 128))
+        paged = run_paged(m, g, q, pool, edges, page_tokens)
+        dense = run_dense(m, g, q, pool["k_dense"], pool["v_dense"], edges)
+        assert paged.tobytes() == dense.tobytes(), page_tokens
+        for s in (0, 8, 15, 29):
+            L = edges[s]
+            ref = oracle.dense_attention_bf16(32, 8, 128, oracle.bf16_to_f32(q[s].reshape(-1)),
+                                              pool["k_dense"][s, :L], pool["v_dense"][s, :L])
+            assert max_abs(bf16_f32(paged[s]).reshape(-1), ref) <= TOL
+
+
 def test_split_size_changes_only_rounding(m, wl, oracle):
     g = m.AttentionGeometry.new(32, 8, 128)
     rng = np.random.default_rng(3)

@@ -68,6 +68,27 @@ def test_c2_full_size_matches_cpu_path(m, oracle):
     assert same > 0.5, same
 
 
+@pytest.mark.parametrize("chunk", [64, 128, 192, 256])
+def test_chunked_prefill_equals_one_shot(m, chunk):
+    """Prefill in batches of 64/128/192/256 tokens (each chunk at prior =
+    tokens so far, over the keys written so far; src/gpu_llm/mod.rs:5435)
+    gives the same bits as one call over all 640 tokens: every row runs the
+    same key tiles in the same order wherever its query tile starts."""
+    from mslim_b200 import workloads as wl
+    qh, kvh, d, S = 32, 8, 128, 640
+    g = m.AttentionGeometry.new(qh, kvh, d)
+    rng = np.random.default_rng(5435)
+    q = wl.normal_bf16(rng, (S, qh, d))
+    k = wl.normal_bf16(rng, (S, kvh, d))
+    v = wl.normal_bf16(rng, (S, kvh, d))
+    whole = run_prefill(m, g, q, k, v, S, 0)
+    parts = []
+    for start in range(0, S, chunk):
+        n = min(chunk, S - start)
+        parts.append(run_prefill(m, g, q[start:start + n], k[:start + n], v[:start + n], n, start))
+    assert np.concatenate(parts).tobytes() == whole.tobytes()
+
+
 def test_prefill_rejects_unsupported(m):
     torch = torch_mod()
     b = torch.zeros(64, dtype=torch.int16, device="cuda:0")
