@@ -165,6 +165,35 @@ int mslim_cuda_decode_dense(const mslim_geometry_t *geometry, const void *q, con
                             uint32_t max_tokens, uint32_t split_tokens, void *workspace,
                             size_t workspace_bytes, void *out, void *stream);
 
+/* Certified sparse decode (epsilon > 0): attention of one query per session
+ * restricted to a certified set of token positions, the GPU side of the
+ * micro-region path -- GpuEngine::micro_sparse_scores followed by the
+ * ordinary softmax / PV (src/gpu_llm/gpu_resources.rs:656-729;
+ * llm_micro_clear_scores + llm_micro_sparse_qk, assets/gpu_llm.cl:847-882:
+ * every omitted score -inf) and GpuEngine::micro_hot_attention (:736-771,
+ * llm_micro_hot_fused_attention, gpu_llm.cl:899-964: softmax over the
+ * selected positions only).  The certificate that authorises the omission
+ * (gpu_micro_regions.rs, attention_certificate.rs) stays with the host.
+ * q: bf16 [n_seq][QH][D]; k_cache/v_cache: dense token-major
+ * [n_seq][max_tokens][KVH][D]; seq_tokens: device int32 [n_seq] committed
+ * lengths; selected: device int32 [n_seq][max_selected] positions, strictly
+ * increasing, each below the session's committed length (the reference checks
+ * this on the host before its upload, gpu_resources.rs:664-671,838-845; here a
+ * violation is recorded in the device status word, reported as
+ * MSLIM_ERR_SHAPE_MISMATCH by mslim_cuda_device_status, and that session's
+ * output is unspecified); selected_counts: device int32 [n_seq], 0 gives zeros.
+ * The selected K/V rows are gathered into the workspace and the split-KV
+ * decode runs over them, so selecting every position gives the bits of
+ * mslim_cuda_decode_dense with the same split_tokens.  workspace: 256-byte
+ * aligned, >= mslim_cuda_decode_selected_workspace_bytes. */
+int mslim_cuda_decode_selected_workspace_bytes(const mslim_geometry_t *geometry, uint32_t n_seq,
+                                               uint32_t max_selected, uint32_t split_tokens, size_t *bytes);
+int mslim_cuda_decode_selected(const mslim_geometry_t *geometry, const void *q, const void *k_cache,
+                               const void *v_cache, uint32_t max_tokens, const int32_t *seq_tokens,
+                               const int32_t *selected, const int32_t *selected_counts, uint32_t max_selected,
+                               uint32_t n_seq, uint32_t split_tokens, void *workspace, size_t workspace_bytes,
+                               void *out, void *stream);
+
 /* Paged decode over ColdStore-exact pages: the device-resident replacement of
  * GpuEngine::attention_gpu_region (src/gpu_llm/gpu_resources.rs:883-1063),
  * which staged V from the ColdStore through the host.  k_pool/v_pool: bf16

@@ -282,6 +282,25 @@ def token_hashes(page_payload: np.ndarray, heads: int, tokens: int) -> np.ndarra
     return out
 
 
+def selected_attention_bf16(query_heads: int, kv_heads: int, head_dim: int, q: np.ndarray,
+                            k: np.ndarray, v: np.ndarray, positions) -> np.ndarray:
+    """Certified sparse decode (epsilon > 0): llm_micro_clear_scores +
+    llm_micro_sparse_qk (assets/gpu_llm.cl:847-882) leave every omitted score
+    at -inf, so the softmax and PV that follow weigh only the selected
+    positions; llm_micro_hot_fused_attention (gpu_llm.cl:899-964) computes the
+    same over the selected list directly.  Restated as the CPU hot-dense
+    attention over the selected token-major rows, in increasing position
+    order (positions must be strictly increasing)."""
+    pos = np.asarray(positions, np.int64)
+    if pos.size and (np.any(np.diff(pos) <= 0) or pos[0] < 0):
+        raise ValueError("selected positions must be strictly increasing")
+    if pos.size == 0:
+        return np.zeros(query_heads * head_dim, np.float32)
+    kk = np.ascontiguousarray(np.asarray(k, np.uint16).reshape(-1, kv_heads, head_dim)[pos])
+    vv = np.ascontiguousarray(np.asarray(v, np.uint16).reshape(-1, kv_heads, head_dim)[pos])
+    return dense_attention_bf16(query_heads, kv_heads, head_dim, q, kk, vv)
+
+
 def logical_kv_sha256(tokens: int, layers, kv_heads: int, head_dim: int) -> str:
     """The validation digest of the logical K/V state, restated row by row
     from GpuLlm::logical_kv_sha256 (src/gpu_llm/mod.rs:1981-2023) and

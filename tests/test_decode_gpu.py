@@ -261,3 +261,73 @@ def test_kv_canonical_paged_reads_pages_in_order_and_rejects_bad_ids():
     assert m.device_status(0) == 2                       # MSLIM_ERR_SHAPE_MISMATCH
     got = host_u16(out)
     assert not got[:, 2 * pt:3 * pt].any() and np.array_equal(got[:, :2 * pt], want[:, :2 * pt])
+
+
+def _selected_case(m, wl, rng, lengths, counts, max_selected, qh=32, kvh=8, d=128, split_tokens=0, sel=None):
+    torch = torch_mod()
+    g = m.AttentionGeometry.new(qh, kvh, d)
+    n_seq, cap = len(lengths), max(lengths)
+    k = np.full((n_seq, cap, kvh, d), 0x7FC1, np.uint16)      # NaN past each end
+    v = np.full_like(k, 0x7FC1)
+    for s_, L in enumerate(lengths):
+        k[s_, :L] = rand_bf16(wl, rng, (L, kvh, d))
+        v[s_, :L] = rand_bf16(wl, rng, (L, kvh, d))
+    if sel is None:
+        sel = np.zeros((n_seq, max_selected), np.int32)
+        for s_, (L, c) in enumerate(zip(lengths, counts)):
+            sel[s_, :c] = np.sort(rng.choice(L, size=c, replace=False))
+    q = rand_bf16(wl, rng, (n_seq, qh, d))
+    ws = torch.empty(m.decode_selected_workspace_bytes(g, n_seq, max_selected, split_tokens), dtype=torch.uint8,
+                     device="cuda:0")
+    out = empty_u16((n_seq, qh, d))
+    kd, vd = dev(k), dev(v)
+    m.decode_selected(g, dev(q), kd, vd, cap, dev(np.asarray(lengths, np.int32)), dev(sel),
+                      dev(np.asarray(counts, np.int32)), max_selected, n_seq, ws, out, split_tokens)
+    torch.cuda.synchronize()
+    assert np.array_equal(host_u16(kd), k) and np.array_equal(host_u16(vd), v), "K/V modified"
+    return g, q, k, v, sel, host_u16(out)
+
+
+def test_selected_decode_matches_cpu_over_the_certified_rows(m, wl, oracle):
+    """epsilon > 0 path (gpu_resources.rs:656-771): attention over the
+    selected positions only, against the CPU attention over those rows."""
+    rng = np.random.default_rng(847)
+    lengths, counts = [300, 2049, 65, 1000, 8], [1, 17, 64, 999, 8]
+    g, q, k, v, sel, out = _selected_case(m, wl, rng, lengths, counts, 1024)
+    assert m.device_status(0) == 0
+    for s, c in enumerate(counts):
+        ref = oracle.selected_attention_bf16(32, 8, 128, oracle.bf16_to_f32(q[s].reshape(-1)), k[s], v[s],
+                                             sel[s, :c])
+        assert max_abs(bf16_f32(out[s]).reshape(-1), ref) <= TOL, (s, c)
+
+
+def test_selecting_every_position_gives_the_dense_decode_bits(m, wl):
+    torch = torch_mod()
+    rng = np.random.default_rng(964)
+    lengths = [1, 77, 512, 700]
+    sel = np.zeros((4, 768), np.int32)
+    for s, L in enumerate(lengths):
+        sel[s, :L] = np.arange(L)
+    g, q, k, v, _, out = _selected_case(m, wl, rng, lengths, lengths, 768, split_tokens=128, sel=sel)
+    assert m.device_status(0) == 0
+    dense = run_dense(m, g, q, k, v, lengths, 128)
+    assert dense.tobytes() == out.tobytes()
+
+
+def test_selected_decode_empty_and_invalid_selections(m, wl):
+    rng = np.random.default_rng(965)
+    # count 0 -> zeros, no error
+    _, _, _, _, _, out = _selected_case(m, wl, rng, [40, 50], [0, 3], 8)
+    assert m.device_status(0) == 0 and not out[0].any() and out[1].any()
+    # not strictly increasing
+    sel = np.array([[3, 9, 9, 20], [0, 1, 2, 3]], np.int32)
+    _selected_case(m, wl, rng, [40, 50], [4, 4], 4, sel=sel)
+    assert m.device_status(0) == 2
+    # a position at or past the committed length
+    sel = np.array([[3, 9, 40, 0], [0, 1, 2, 3]], np.int32)
+    _selected_case(m, wl, rng, [40, 50], [3, 4], 4, sel=sel)
+    assert m.device_status(0) == 2
+    # more selected than the capacity
+    sel = np.zeros((2, 4), np.int32)
+    _selected_case(m, wl, rng, [40, 50], [5, 1], 4, sel=sel)
+    assert m.device_status(0) == 2

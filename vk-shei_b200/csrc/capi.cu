@@ -608,6 +608,78 @@ int mslim_cuda_decode_dense(const mslim_geometry_t *geometry, const void *q, con
     return run_decode(c);
 }
 
+// Certified sparse decode: the gathered K and V rows, then the split partials,
+// each section 256-byte aligned.
+struct SelectedLayout {
+    size_t kv_bytes, partial_bytes, total;
+};
+static int selected_layout(const mslim_geometry_t *geometry, uint32_t n_seq, uint32_t max_selected,
+                           uint32_t split_tokens, SelectedLayout *l) {
+    size_t part = 0;
+    if (int rc = mslim_cuda_decode_workspace_bytes(geometry, n_seq, max_selected, split_tokens, &part)) return rc;
+    auto up = [](size_t x) { return (x + 255) / 256 * 256; };
+    l->kv_bytes = up((size_t)n_seq * max_selected * geometry->kv_heads * geometry->head_dim * 2);
+    l->partial_bytes = part;
+    l->total = 2 * l->kv_bytes + up(part);
+    return MSLIM_OK;
+}
+
+int mslim_cuda_decode_selected_workspace_bytes(const mslim_geometry_t *geometry, uint32_t n_seq,
+                                               uint32_t max_selected, uint32_t split_tokens, size_t *bytes) {
+    if (!bytes) return fail(MSLIM_ERR_SHAPE_MISMATCH, "bytes pointer is null");
+    SelectedLayout l;
+    if (int rc = selected_layout(geometry, n_seq, max_selected, split_tokens, &l)) return rc;
+    *bytes = l.total;
+    return MSLIM_OK;
+}
+
+int mslim_cuda_decode_selected(const mslim_geometry_t *geometry, const void *q, const void *k_cache,
+                               const void *v_cache, uint32_t max_tokens, const int32_t *seq_tokens,
+                               const int32_t *selected, const int32_t *selected_counts, uint32_t max_selected,
+                               uint32_t n_seq, uint32_t split_tokens, void *workspace, size_t workspace_bytes,
+                               void *out, void *stream) {
+    if (max_tokens == 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty cache");
+    if (max_selected == 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty selection capacity");
+    uint32_t st = split_tokens;
+    if (int rc = decode_common_checks(geometry, n_seq, &st, max_selected)) return rc;
+    if (!q || !k_cache || !v_cache || !seq_tokens || !selected || !selected_counts || !out || !workspace)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
+    SelectedLayout l;
+    if (int rc = selected_layout(geometry, n_seq, max_selected, st, &l)) return rc;
+    if (workspace_bytes < l.total)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "workspace holds %zu bytes, needs %zu", workspace_bytes, l.total);
+    if (!aligned(workspace, 256)) return fail(MSLIM_ERR_SHAPE_MISMATCH, "workspace must be 256-byte aligned");
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    uint8_t *base = static_cast<uint8_t *>(workspace);
+    uint16_t *gk = reinterpret_cast<uint16_t *>(base);
+    uint16_t *gv = reinterpret_cast<uint16_t *>(base + l.kv_bytes);
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t err = mslim::launch_gather_selected(
+        static_cast<const uint16_t *>(k_cache), static_cast<const uint16_t *>(v_cache), max_tokens,
+        geometry->kv_heads, geometry->head_dim, seq_tokens, selected, selected_counts, max_selected, n_seq, gk, gv,
+        status_ptr(dev), s);
+    if (err != cudaSuccess) return cuda_fail(err, "selection gather launch");
+    DecodeCall c{};
+    c.g = geometry;
+    c.q = q;
+    c.k = gk;
+    c.v = gv;
+    c.seq_tokens = selected_counts;  // the gathered rows are the whole attended set
+    c.fixed_tokens = -1;
+    c.n_seq = n_seq;
+    c.nq = 1;
+    c.max_tokens = max_selected;
+    c.split_tokens = st;
+    c.workspace = base + 2 * l.kv_bytes;
+    c.workspace_bytes = l.partial_bytes;
+    c.out = out;
+    c.scale_log2 = scale_log2_for(geometry->head_dim);
+    c.kernel_dim = kernel_dim_for(geometry->head_dim);
+    c.stream = s;
+    return run_decode(c);
+}
+
 int mslim_cuda_decode_paged(const mslim_geometry_t *geometry, const void *q, const void *k_pool,
                             const void *v_pool, uint32_t n_pages, uint32_t page_tokens,
                             const int32_t *page_table, uint32_t max_pages_per_seq,

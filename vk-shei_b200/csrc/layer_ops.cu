@@ -322,7 +322,74 @@ __global__ void __launch_bounds__(256)
     }
 }
 
+// Certified-selection gather: for session s, the count[s] token positions
+// selected[s][0..count) (strictly increasing, each below the session's
+// committed length seq_tokens[s]) have their K and V rows copied from the
+// token-major dense caches [n_seq][max_tokens][kv_heads][dim] to rows 0..count
+// of gk/gv [n_seq][max_selected][kv_heads][dim], so a dense decode over count
+// tokens attends to exactly the selected set.  A count above max_selected or
+// above the committed length, a position out of range or not above its
+// predecessor is recorded in the status word and its row is not copied.
+// One thread per 16-byte chunk (kvh * dim % 8 == 0) or per element.
+template <bool kVec>
+__global__ void __launch_bounds__(256)
+    mslim_gather_selected(const uint16_t *__restrict__ k_cache, const uint16_t *__restrict__ v_cache,
+                          uint32_t max_tokens, uint32_t row_elems, const int32_t *__restrict__ seq_tokens,
+                          const int32_t *__restrict__ selected, const int32_t *__restrict__ counts,
+                          uint32_t max_selected, uint16_t *__restrict__ gk, uint16_t *__restrict__ gv,
+                          int *status) {
+    constexpr uint32_t kW = kVec ? 8 : 1;
+    const uint32_t s = blockIdx.x;
+    const int32_t committed = seq_tokens[s];
+    int32_t count = counts[s];
+    if (count < 0 || (uint32_t)count > max_selected || count > committed) {
+        if (threadIdx.x == 0 && blockIdx.y == 0 && status) atomicExch(status, MSLIM_DEVICE_BAD_PAGE_CODE);
+        return;
+    }
+    const int32_t *sel = selected + (size_t)s * max_selected;
+    const uint32_t per_row = row_elems / kW;
+    const uint64_t total = (uint64_t)count * per_row;
+    for (uint64_t x = (uint64_t)blockIdx.y * blockDim.x + threadIdx.x; x < total;
+         x += (uint64_t)gridDim.y * blockDim.x) {
+        const uint32_t e = (uint32_t)(x / per_row), c = (uint32_t)(x % per_row);
+        const int32_t pos = sel[e];
+        if (pos < 0 || pos >= committed || (uint32_t)pos >= max_tokens || (e > 0 && sel[e - 1] >= pos)) {
+            if (c == 0 && status) atomicExch(status, MSLIM_DEVICE_BAD_PAGE_CODE);
+            continue;
+        }
+        const size_t src = ((size_t)s * max_tokens + (uint32_t)pos) * row_elems + (size_t)c * kW;
+        const size_t dst = ((size_t)s * max_selected + e) * row_elems + (size_t)c * kW;
+        if constexpr (kVec) {
+            *reinterpret_cast<uint4 *>(gk + dst) = *reinterpret_cast<const uint4 *>(k_cache + src);
+            *reinterpret_cast<uint4 *>(gv + dst) = *reinterpret_cast<const uint4 *>(v_cache + src);
+        } else {
+            gk[dst] = k_cache[src];
+            gv[dst] = v_cache[src];
+        }
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_gather_selected(const uint16_t *k_cache, const uint16_t *v_cache, uint32_t max_tokens,
+                                   uint32_t kv_heads, uint32_t dim, const int32_t *seq_tokens,
+                                   const int32_t *selected, const int32_t *counts, uint32_t max_selected,
+                                   uint32_t n_seq, uint16_t *gk, uint16_t *gv, int *status, cudaStream_t stream) {
+    auto al = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    const uint32_t row_elems = kv_heads * dim;
+    const bool vec = row_elems % 8 == 0 && al(k_cache) && al(v_cache) && al(gk) && al(gv);
+    const uint64_t per_session = (uint64_t)max_selected * (vec ? row_elems / 8 : row_elems);
+    const unsigned chunks = (unsigned)std::min<uint64_t>(std::max<uint64_t>(1, (per_session + 255) / 256), 64);
+    const dim3 grid(n_seq, chunks);
+    if (vec)
+        mslim_gather_selected<true><<<grid, 256, 0, stream>>>(k_cache, v_cache, max_tokens, row_elems, seq_tokens,
+                                                               selected, counts, max_selected, gk, gv, status);
+    else
+        mslim_gather_selected<false><<<grid, 256, 0, stream>>>(k_cache, v_cache, max_tokens, row_elems,
+                                                                seq_tokens, selected, counts, max_selected, gk, gv,
+                                                                status);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_kv_canonical(const uint16_t *src, uint16_t *out, uint32_t kv_heads, uint32_t tokens,
                                 uint32_t dim, const int32_t *page_row, uint32_t page_tokens, uint32_t n_pages,

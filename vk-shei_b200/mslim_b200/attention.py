@@ -263,6 +263,26 @@ def decode_dense(geometry: AttentionGeometry, q, k_cache, v_cache, seq_tokens, n
         max_tokens, split_tokens, _ptr(workspace), _nbytes(workspace), _ptr(out), _stream(stream)))
 
 
+def decode_selected_workspace_bytes(geometry: AttentionGeometry, n_seq: int, max_selected: int,
+                                    split_tokens: int = 0) -> int:
+    out = ctypes.c_size_t()
+    check(_lib.lib().mslim_cuda_decode_selected_workspace_bytes(ctypes.byref(geometry.c()), n_seq, max_selected,
+                                                                split_tokens, ctypes.byref(out)))
+    return out.value
+
+
+def decode_selected(geometry: AttentionGeometry, q, k_cache, v_cache, max_tokens: int, seq_tokens, selected,
+                    selected_counts, max_selected: int, n_seq: int, workspace, out, split_tokens: int = 0,
+                    stream=None) -> None:
+    """Certified sparse decode (epsilon > 0): attention restricted to the
+    selected positions, GpuEngine::micro_sparse_scores / micro_hot_attention
+    (src/gpu_llm/gpu_resources.rs:656-771)."""
+    check(_lib.lib().mslim_cuda_decode_selected(
+        ctypes.byref(geometry.c()), _ptr(q), _ptr(k_cache), _ptr(v_cache), max_tokens, _ptr(seq_tokens),
+        _ptr(selected), _ptr(selected_counts), max_selected, n_seq, split_tokens, _ptr(workspace),
+        _nbytes(workspace), _ptr(out), _stream(stream)))
+
+
 def decode_paged(geometry: AttentionGeometry, q, k_pool, v_pool, n_pages: int, page_tokens: int,
                  page_table, max_pages_per_seq: int, seq_tokens, n_seq: int, workspace, out,
                  split_tokens: int = 0, stream=None) -> None:
