@@ -615,6 +615,11 @@ struct SelectedLayout {
 };
 static int selected_layout(const mslim_geometry_t *geometry, uint32_t n_seq, uint32_t max_selected,
                            uint32_t split_tokens, SelectedLayout *l) {
+    if (int rc = check_geometry(geometry)) return rc;
+    // the gathered rows are indexed like a dense cache (i32 token counts)
+    if ((uint64_t)n_seq * max_selected > 0x7fffffffull ||
+        (uint64_t)n_seq * max_selected * geometry->kv_heads * geometry->head_dim > (1ull << 40))
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "selection capacity too large");
     size_t part = 0;
     if (int rc = mslim_cuda_decode_workspace_bytes(geometry, n_seq, max_selected, split_tokens, &part)) return rc;
     auto up = [](size_t x) { return (x + 255) / 256 * 256; };
