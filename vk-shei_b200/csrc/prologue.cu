@@ -287,13 +287,14 @@ __device__ __forceinline__ void rope_append_token_vec(const QkvRows &in, uint16_
     }
 }
 
-// One CTA per new token: RoPE of its q heads into q_out, RoPE of its k heads
-// and a copy of its v heads into the ColdStore-exact page that holds the
-// token (head-major [KVH][page_tokens][D] inside the page).
-//   prefill form (positions == null): CTA t is token t of one sequence at
-//     position start_position + t, pages page_table[0..max_pages);
-//   decode form (positions != null): CTA s is the new token of session s at
-//     position positions[s], pages page_table[s * max_pages ..].
+// Per new token (blockIdx.x; with kVec its work spread over gridDim.y CTAs):
+// RoPE of its q heads into q_out, RoPE of its k heads and a copy of its v
+// heads into the ColdStore-exact page that holds the token (head-major
+// [KVH][page_tokens][D] inside the page).
+//   prefill form (positions == null): token t of one sequence at position
+//     start_position + t, pages page_table[0..max_pages);
+//   decode form (positions != null): the new token of session s at position
+//     positions[s], pages page_table[s * max_pages ..].
 template <bool kVec>
 __global__ void __launch_bounds__(256)
     mslim_rope_append_paged(const QkvRows in, uint16_t *__restrict__ q_out, uint32_t qheads,
@@ -337,9 +338,10 @@ __global__ void __launch_bounds__(256)
     else rope_append_token(in, q_out, token, qheads, kvheads, dim, cs, k_dst, v_dst);
 }
 
-// Dense-cache twin of the decode form above: CTA s is the new token of session
-// s at position positions[s]; q -> RoPE -> q_out, k -> RoPE and v -> copy into
-// the token-major caches [n_seq][max_tokens][KVH][D] at row positions[s].
+// Dense-cache twin of the decode form above: blockIdx.x = s is the new token
+// of session s at position positions[s]; q -> RoPE -> q_out, k -> RoPE and
+// v -> copy into the token-major caches [n_seq][max_tokens][KVH][D] at row
+// positions[s].
 template <bool kVec>
 __global__ void __launch_bounds__(256)
     mslim_rope_append_dense(const QkvRows in, uint16_t *__restrict__ q_out, uint32_t qheads,
