@@ -209,8 +209,7 @@ int mslim_cuda_decode_paged(const mslim_geometry_t *geometry, const void *q, con
 
 /* Paged decode that allocates nothing and takes no workspace.  No counterpart
  * in the reference: it is for callers that cannot allocate device memory --
- * code running while a stream is being captured into a CUDA graph, a serving
- * loop that must never hit the implicit device synchronisation of
+ * a serving loop that must never hit the implicit device synchronisation of
  * cudaMalloc/cudaFree, or a host (e.g. a Rust FFI caller) that holds only the
  * K/V, page-table and output pointers and has no device allocator bound.
  * Same arguments and results as mslim_cuda_decode_paged minus the workspace;

@@ -1,9 +1,9 @@
 """The allocation-free paged decode entry point.
 
 mslim_cuda_decode_paged_static_scratch serves callers that cannot allocate
-device memory (a stream being captured into a CUDA graph, a serving loop that
-must not pay cudaMalloc/cudaFree's implicit device synchronisation, an FFI
-host that only holds the K/V, page-table and output pointers).  Its split
+device memory (a serving loop that must not pay cudaMalloc/cudaFree's
+implicit device synchronisation, an FFI host that only holds the K/V,
+page-table and output pointers and has no device allocator).  Its split
 partials live in the library's static 16 MiB device array instead of a
 caller workspace.  These tests call it through the C ABI twice in a row and
 compare with mslim_cuda_decode_paged, which takes a workspace.  This file is
