@@ -159,3 +159,77 @@ def test_a_peer_that_never_arrives_times_out_and_the_context_survives():
     finally:
         torch.cuda.synchronize()
         comm.close()
+
+
+def _set_call_numbers(comm, value: int):
+    """Writes every row's call counter of a communicator (uint32, set here as
+    its int32 bit pattern) so a test can start next to the wrap."""
+    import torch
+    from mslim_b200.tp import _DeviceArray
+    ep = torch.as_tensor(_DeviceArray(comm.c.epoch, (comm.max_rows,), "<i4"), device="cuda")
+    ep.fill_(value)
+    torch.cuda.synchronize()
+
+
+def test_one_rank_across_the_call_number_wrap():
+    """Call numbers are uint32 per row and wrap after 2^32 calls; the
+    reduction compares them as serial numbers and skips 0, so calls on either
+    side of the wrap still equal the residual add + RMSNorm bitwise."""
+    import torch
+    import mslim_b200 as m
+    from gpu_util import dev
+    from mslim_b200.tp import TpComm
+    rng = np.random.default_rng(22)
+    comm = TpComm(1, 0, ROWS, HIDDEN)
+    try:
+        _set_call_numbers(comm, -3)          # 0xFFFFFFFD: the next calls are ..FE, ..FF, 1, 2
+        w = dev(_bf16(rng, HIDDEN))
+        x0 = _bf16(rng, ROWS * HIDDEN).reshape(ROWS, HIDDEN)
+        for call in range(4):
+            part = _bf16(rng, ROWS * HIDDEN, 0.5).reshape(ROWS, HIDDEN)
+            slot = comm.next_slot()
+            comm.slot(slot, ROWS).view(torch.int16).copy_(dev(part))
+            xa, xb = dev(x0), dev(x0)
+            ya, yb = torch.empty_like(xa), torch.empty_like(xa)
+            comm.allreduce_rmsnorm(slot, xa, w, ya, ROWS, EPS)
+            m.residual_rmsnorm(xb, dev(part), w, yb, ROWS, HIDDEN, EPS)
+            torch.cuda.synchronize()
+            assert np.array_equal(_u16(xa), _u16(xb)) and np.array_equal(_u16(ya), _u16(yb)), call
+        assert m.device_status(0) == 0
+    finally:
+        torch.cuda.synchronize()
+        comm.close()
+
+
+def test_a_missing_peer_still_times_out_at_the_call_number_wrap():
+    """At the wrap the next call number would be 0, the value of a flag no peer
+    has written; it is skipped, so a peer that never arrives is still waited
+    for (and the bounded wait gives up) instead of being taken as arrived."""
+    import ctypes
+
+    import torch
+    import mslim_b200 as m
+    from gpu_util import dev
+    from mslim_b200 import _lib
+    from mslim_b200.tp import TpComm
+    rng = np.random.default_rng(32)
+    comm = TpComm(1, 0, ROWS, HIDDEN)
+    try:
+        _set_call_numbers(comm, -1)          # 0xFFFFFFFF: the next call number wraps
+        c = _lib.TpComm()
+        ctypes.memmove(ctypes.byref(c), ctypes.byref(comm.c), ctypes.sizeof(c))
+        c.world = 2
+        c.data[1], c.flags[1] = comm.c.data[0], comm.c.flags[0]
+        x = dev(_bf16(rng, ROWS * HIDDEN).reshape(ROWS, HIDDEN))
+        x_before = _u16(x)
+        y = torch.zeros_like(x)
+        w = dev(_bf16(rng, HIDDEN))
+        assert m.device_status(0) == 0
+        m.check(_lib.lib().mslim_cuda_tp_allreduce_rmsnorm(ctypes.byref(c), 0, x.data_ptr(), w.data_ptr(),
+                                                           y.data_ptr(), ROWS, EPS,
+                                                           torch.cuda.current_stream().cuda_stream))
+        assert m.device_status(0) == _lib.ERR_DEVICE_TIMEOUT
+        assert np.array_equal(_u16(x), x_before) and not _u16(y).any()
+    finally:
+        torch.cuda.synchronize()
+        comm.close()

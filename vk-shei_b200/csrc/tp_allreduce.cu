@@ -113,14 +113,19 @@ __global__ void __launch_bounds__(kTpThreads)
     // work in parallel, each behind its own system-scope fence
     if (threadIdx.x < 32) {
         const uint32_t lane = threadIdx.x;
-        const uint32_t e = c.epoch[row] + 1;
+        // Call numbers wrap after 2^32 calls of a row (hours of serving at
+        // batch-8 decode rates): they are compared as serial numbers, and 0 --
+        // the value of a flag no peer has written -- is never used.
+        uint32_t e = c.epoch[row] + 1;
+        if (e == 0) e = 1;
         int ok = 1;
         if (lane < W) {
             fence_sys();   // this rank's partial (written by earlier kernels) before its number
             st_relaxed_sys(c.flags[lane] + row * kTpMaxWorld + c.rank, e);
             const uint32_t *f = c.flags[c.rank] + row * kTpMaxWorld + lane;
             const uint64_t start = globaltimer();
-            while (ld_acquire_sys(f) < e) {   // counters only grow; a peer may be one call ahead
+            // a peer may be one call ahead (its number e + 1)
+            while ((int32_t)(ld_acquire_sys(f) - e) < 0) {
                 if (globaltimer() - start > kTpWaitBoundNs) {
                     record_timeout(status, 80 + (int)lane);
                     ok = 0;
