@@ -667,7 +667,9 @@ def main():
         e2e_graph = torch.cuda.CUDAGraph()
         cap = torch.cuda.Stream()
         cap.wait_stream(stream)
-        with torch.cuda.graph(e2e_graph, stream=cap):
+        # thread-local capture: other threads of the process (the process
+        # group's) may touch CUDA while this thread captures
+        with torch.cuda.graph(e2e_graph, stream=cap, capture_error_mode="thread_local"):
             e2e_calls(torch.cuda.current_stream())
         torch.cuda.synchronize()
 
