@@ -32,7 +32,8 @@ def run_prefill(m, g, q, k, v, queries, prior):
 CASES = [(1, 0), (5, 0), (128, 0), (129, 0), (200, 37), (256, 256), (64, 1000), (300, 129)]
 
 
-@pytest.mark.parametrize("geom", [(32, 8, 128), (8, 2, 128), (4, 1, 128), (4, 4, 128)])
+@pytest.mark.parametrize("geom", [(32, 8, 128), (8, 2, 128), (4, 1, 128), (4, 4, 128), (32, 8, 64), (8, 4, 64),
+                                  (16, 8, 64)])
 def test_prefill_matches_cpu_path(m, oracle, geom):
     from mslim_b200 import workloads as wl
     qh, kvh, d = geom
@@ -68,14 +69,14 @@ def test_c2_full_size_matches_cpu_path(m, oracle):
     assert same > 0.5, same
 
 
-@pytest.mark.parametrize("chunk", [64, 128, 192, 256])
-def test_chunked_prefill_equals_one_shot(m, chunk):
+@pytest.mark.parametrize("chunk,d", [(64, 128), (128, 128), (192, 128), (256, 128), (192, 64)])
+def test_chunked_prefill_equals_one_shot(m, chunk, d):
     """Prefill in batches of 64/128/192/256 tokens (each chunk at prior =
     tokens so far, over the keys written so far; src/gpu_llm/mod.rs:5435)
     gives the same bits as one call over all 640 tokens: every row runs the
     same key tiles in the same order wherever its query tile starts."""
     from mslim_b200 import workloads as wl
-    qh, kvh, d, S = 32, 8, 128, 640
+    qh, kvh, S = 32, 8, 640
     g = m.AttentionGeometry.new(qh, kvh, d)
     rng = np.random.default_rng(5435)
     q = wl.normal_bf16(rng, (S, qh, d))
@@ -92,7 +93,10 @@ def test_chunked_prefill_equals_one_shot(m, chunk):
 def test_prefill_rejects_unsupported(m):
     torch = torch_mod()
     b = torch.zeros(64, dtype=torch.int16, device="cuda:0")
+    # head_dim 64 runs in the two-head kernel only (an even group); 80 has no kernel
     with pytest.raises(m.InvalidGeometry):
-        m.prefill_causal(m.AttentionGeometry.new(4, 1, 64), b, b, b, b.clone(), 1, 0)
+        m.prefill_causal(m.AttentionGeometry.new(4, 4, 64), b, b, b, b.clone(), 1, 0)
+    with pytest.raises(m.InvalidGeometry):
+        m.prefill_causal(m.AttentionGeometry.new(4, 2, 80), b, b, b, b.clone(), 1, 0)
     with pytest.raises(m.ShapeMismatch):
         m.prefill_causal(m.AttentionGeometry.new(4, 1, 128), b, b, b, b, 1, 0)

@@ -779,8 +779,10 @@ int mslim_cuda_prefill_causal(const mslim_geometry_t *geometry, const void *q, c
     if (out == q || out == k || out == v)
         return fail(MSLIM_ERR_SHAPE_MISMATCH, "output must not alias read-only Q/K/V");
     if (!mslim::prefill_supported(geometry->head_dim, geometry->query_heads / geometry->kv_heads))
-        return fail(MSLIM_ERR_INVALID_GEOMETRY, "head_dim %u has no sm_100a prefill kernel (128)",
-                    geometry->head_dim);
+        return fail(MSLIM_ERR_INVALID_GEOMETRY,
+                    "head_dim %u with %u query heads per KV head has no sm_100a prefill kernel "
+                    "(head_dim 128, or 64 with an even group)",
+                    geometry->head_dim, geometry->query_heads / geometry->kv_heads);
     if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(out, 16))
         return fail(MSLIM_ERR_SHAPE_MISMATCH, "prefill buffers must be 16-byte aligned");
     const uint64_t D = geometry->head_dim;
@@ -806,6 +808,7 @@ int mslim_cuda_prefill_causal(const mslim_geometry_t *geometry, const void *q, c
     p.queries = (int)queries;
     p.prior = (int)prior;
     p.n_qtiles = (int)((queries + 127) / 128);
+    p.head_dim = (int)geometry->head_dim;
     p.scale_log2 = scale_log2_for(geometry->head_dim);
     if ((uint64_t)p.n_qtiles * p.qheads > 0x7fffffffull)
         return fail(MSLIM_ERR_SHAPE_MISMATCH, "prefill grid too large");

@@ -405,6 +405,27 @@ __device__ __forceinline__ void umma_bf16_ss_k128(uint32_t d_tmem, uint64_t a_de
         : "memory");
 }
 
+// Four K=16 steps of a 128 x N x 64 product (head_dim 64: A and B each one
+// 64-column box) from a single elect: step k reads A at a_desc + 2k and B at
+// b_desc + 2k (the next 32 bytes of each 128-byte swizzled row).  Step 0
+// accumulates when `accumulate` is set, steps 1..3 always do.
+__device__ __forceinline__ void umma_bf16_ss_k64(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred e, p, t;\n\t.reg .b64 a1, a2, a3, b1, b2, b3;\n\t"
+        "add.s64 a1, %1, 2;\n\tadd.s64 a2, %1, 4;\n\tadd.s64 a3, %1, 6;\n\t"
+        "add.s64 b1, %2, 2;\n\tadd.s64 b2, %2, 4;\n\tadd.s64 b3, %2, 6;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "setp.eq.b32 t, %4, %4;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a1, b1, %3, t;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a2, b2, %3, t;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a3, b3, %3, t;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // Four K=16 steps of O += P V with P in tensor memory: step k reads A at
 // a_tmem + 8k (sixteen bf16 keys packed into eight 32-bit columns) and B at
 // b_desc + k * b_step16.  Step 0 accumulates when `accumulate` is set.

@@ -353,13 +353,26 @@ __global__ void __launch_bounds__(kSThreads, 1)
 //          softmax head B.  ptxas compiles every path within the registers the
 //          launch allows (__launch_bounds__(384, 1): 168 per thread), and one CTA
 //          fills the SM, so the kernel moves no registers between warpgroups.
-constexpr int kPOffQ = 0;                           // Q_h at h * kQBytes
-constexpr int kPOffK = 2 * kQBytes;                 // K slot s at kPOffK + s * kTileBytes
-constexpr int kPOffV = kPOffK + 2 * kTileBytes;
-constexpr int kPOffStage = kPOffV + 2 * kTileBytes; // head h's 16 KB output box at + h * kBox
-constexpr int kPOffBar = kPOffStage + 2 * kBox;
-constexpr int kPSmemBytes = kPOffBar + 512 + 1024;
-static_assert(kPSmemBytes <= 227 * 1024, "shared memory per block");
+//   head_dim: 128 (two 64-column boxes per Q/K/V/O row) or 64 (one box; the S
+//   product then has four K=16 steps and O_h uses 64 of its 128 columns).
+template <int D>
+struct PairShape {
+    static_assert(D == 64 || D == 128, "pair prefill head_dim");
+    static constexpr int kBoxes = D / 64;                // 64-column boxes per row
+    static constexpr int kQBytes = kBoxes * kBox;        // one head's Q tile
+    static constexpr int kTileBytes = kBoxes * kBox;     // one K or V tile
+    static constexpr int kOffQ = 0;                      // Q_h at h * kQBytes
+    static constexpr int kOffK = 2 * kQBytes;            // K slot s at kOffK + s * kTileBytes
+    static constexpr int kOffV = kOffK + 2 * kTileBytes;
+    static constexpr int kOffStage = kOffV + 2 * kTileBytes;  // head h's 16 KB output box at + h * kBox
+    static constexpr int kOffBar = kOffStage + 2 * kBox;
+    static constexpr int kSmemBytes = kOffBar + 512 + 1024;
+    // PV: M 128 query rows, N = head_dim, B (V) MN-major
+    static constexpr uint32_t kIdescPV =
+        (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((uint32_t)(D >> 3) << 17) | ((kRows >> 4) << 24);
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory per block");
+};
+static_assert(PairShape<128>::kIdescPV == kIdescPV, "head_dim 128 keeps the single-head kernel's PV shape");
 constexpr int kPThreads = 12 * 32;
 
 struct PairBars {
@@ -394,15 +407,17 @@ __device__ __forceinline__ bool pair_item(const PrefillParams &p, int round, Pai
     return true;
 }
 
+template <int D>
 __global__ void __launch_bounds__(kPThreads, 1)
     mslim_prefill_pair(const __grid_constant__ CUtensorMap qmap,
                        const __grid_constant__ CUtensorMap kmap,
                        const __grid_constant__ CUtensorMap vmap,
                        const __grid_constant__ CUtensorMap omap, const PrefillParams p) {
+    using PS = PairShape<D>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    PairBars *bars = reinterpret_cast<PairBars *>(smem + kPOffBar);
+    PairBars *bars = reinterpret_cast<PairBars *>(smem + PS::kOffBar);
     volatile int *abort_flag = &bars->abort;
 
     const int warp = threadIdx.x >> 5;
@@ -442,7 +457,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
             const CUtensorMap *map = is_k ? &kmap : &vmap;
             uint64_t *full = is_k ? bars->k_full : bars->v_full;
             uint64_t *empty = is_k ? bars->k_empty : bars->v_empty;
-            uint8_t *ring = smem + (is_k ? kPOffK : kPOffV);
+            uint8_t *ring = smem + (is_k ? PS::kOffK : PS::kOffV);
             prefetch_tmap(map);
             int g = 0;  // key tiles loaded so far, over all items
             bool run = true;
@@ -457,10 +472,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
                         run = false;
                         break;
                     }
-                    uint8_t *dst = ring + st * kTileBytes;
-                    mbar_arrive_expect_tx(&full[st], kTileBytes);
-                    tma_load_3d(dst, map, &full[st], 0, kvh, j * kKeys);
-                    tma_load_3d(dst + kBox, map, &full[st], 64, kvh, j * kKeys);
+                    uint8_t *dst = ring + st * PS::kTileBytes;
+                    mbar_arrive_expect_tx(&full[st], PS::kTileBytes);
+#pragma unroll
+                    for (int b = 0; b < PS::kBoxes; ++b)
+                        tma_load_3d(dst + b * kBox, map, &full[st], b * 64, kvh, j * kKeys);
                     ++g;
                 }
             }
@@ -478,12 +494,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
                     *abort_flag = 1;
                     break;
                 }
-                mbar_arrive_expect_tx(&bars->q_full, 2 * kQBytes);
-                for (int h = 0; h < 2; ++h) {
-                    tma_load_3d(smem + kPOffQ + h * kQBytes, &qmap, &bars->q_full, 0, it.qh0 + h, it.q0);
-                    tma_load_3d(smem + kPOffQ + h * kQBytes + kBox, &qmap, &bars->q_full, 64, it.qh0 + h,
-                                it.q0);
-                }
+                mbar_arrive_expect_tx(&bars->q_full, 2 * PS::kQBytes);
+                for (int h = 0; h < 2; ++h)
+#pragma unroll
+                    for (int b = 0; b < PS::kBoxes; ++b)
+                        tma_load_3d(smem + PS::kOffQ + h * PS::kQBytes + b * kBox, &qmap, &bars->q_full, b * 64,
+                                    it.qh0 + h, it.q0);
                 ++loaded;
             }
             if (loaded > 0) mbar_wait(&bars->q_full, (loaded - 1) & 1, p.status, 45);
@@ -494,11 +510,15 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.status, where));
             };
             auto issue_s = [&](int h, int slot) {
-                const uint32_t qaddr = sbase + kPOffQ + h * kQBytes;
-                const uint32_t kaddr = sbase + kPOffK + slot * kTileBytes;
+                const uint32_t qaddr = sbase + PS::kOffQ + h * PS::kQBytes;
+                const uint32_t kaddr = sbase + PS::kOffK + slot * PS::kTileBytes;
                 // the eight K=16 steps from one elect (see umma_bf16_ss_k128)
-                umma_bf16_ss_k128(tmem + h * 128, umma_desc_sw128(qaddr, 16, 1024),
-                                  umma_desc_sw128(kaddr, 16, 1024), kIdescS, 0u, kBox >> 4);
+                if constexpr (D == 128)
+                    umma_bf16_ss_k128(tmem + h * 128, umma_desc_sw128(qaddr, 16, 1024),
+                                      umma_desc_sw128(kaddr, 16, 1024), kIdescS, 0u, kBox >> 4);
+                else
+                    umma_bf16_ss_k64(tmem + h * 128, umma_desc_sw128(qaddr, 16, 1024),
+                                     umma_desc_sw128(kaddr, 16, 1024), kIdescS, 0u);
                 umma_commit(&bars->s_full[h]);
             };
             int g = 0;  // key tiles consumed so far, over all items
@@ -520,7 +540,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
                     const bool next = j + 1 < it.n_kv;
                     ok = wait_all(&bars->v_full[g & 1], (g >> 1) & 1, 54);
                     if (ok && next) ok = wait_all(&bars->k_full[(g + 1) & 1], ((g + 1) >> 1) & 1, 52);
-                    const uint32_t vaddr = sbase + kPOffV + (g & 1) * kTileBytes;
+                    const uint32_t vaddr = sbase + PS::kOffV + (g & 1) * PS::kTileBytes;
                     for (int h = 0; ok && h < 2; ++h) {
                         // PV over keys 0..63 starts while the softmax still
                         // writes P for keys 64..127
@@ -531,7 +551,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
                             // keys 64*half .. +63: four K=16 steps from one elect
                             umma_bf16_ts_k64(tmem + kColO + h * 128, tmem + h * 128 + half * 32,
                                              umma_desc_sw128(vaddr + half * 4 * 16 * 128, kBox, 1024),
-                                             kIdescPV, (j > 0 || half > 0) ? 1u : 0u, (16 * 128) >> 4);
+                                             PS::kIdescPV, (j > 0 || half > 0) ? 1u : 0u, (16 * 128) >> 4);
                         }
                         if (!ok) break;
                         if (next) issue_s(h, (g + 1) & 1);
@@ -560,7 +580,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
         const uint32_t ocol = lane_addr + kColO + h * 128;
         const float scale = p.scale_log2;
         const bool issuer = quarter == 0 && lane == 0;
-        uint8_t *stage = smem + kPOffStage + h * kBox;
+        uint8_t *stage = smem + PS::kOffStage + h * kBox;
         int g = 0;  // key tiles seen so far, over all items
         bool ok = true;
         PairItem it;
@@ -623,7 +643,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
                         // S_h(j) done implies PV_h(j-1) done: O_h is final for
                         // j-1, and PV_h(j) waits for the arrive below
 #pragma unroll
-                        for (int oc = 0; oc < 4; ++oc) {
+                        for (int oc = 0; oc < D / 32; ++oc) {
                             float o[32];
                             tmem_ld32(ocol + oc * 32, o);
 #pragma unroll
@@ -651,7 +671,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
             if (!good) *abort_flag = 1;
             tc_fence_after();
             const float inv = 1.0f / l_run;
-            for (int box = 0; box < 2; ++box) {
+            for (int box = 0; box < PS::kBoxes; ++box) {
                 if (issuer) bulk_wait_read_all();  // the previous store has read the buffer
                 named_bar_sync(1 + h, 128);
                 if (good) {
@@ -692,7 +712,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
 
 }  // namespace
 
-bool prefill_supported(unsigned head_dim, unsigned group) { return head_dim == 128 && group >= 1; }
+bool prefill_supported(unsigned head_dim, unsigned group) {
+    // head_dim 64 runs only in the two-head kernel (even groups)
+    return group >= 1 && (head_dim == 128 || (head_dim == 64 && group % 2 == 0));
+}
 
 bool prefill_pairs_heads(unsigned group) { return group % 2 == 0; }
 
@@ -715,8 +738,12 @@ cudaError_t prefill_setup(int dev, int *sms) {
     if (d.state.load(std::memory_order_acquire) == 0) {
         std::lock_guard<std::mutex> lock(g_setup_mutex);
         if (d.state.load(std::memory_order_relaxed) == 0) {
-            cudaError_t err = cudaFuncSetAttribute(mslim_prefill_pair,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytes);
+            cudaError_t err = cudaFuncSetAttribute(mslim_prefill_pair<128>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   PairShape<128>::kSmemBytes);
+            if (err == cudaSuccess)
+                err = cudaFuncSetAttribute(mslim_prefill_pair<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           PairShape<64>::kSmemBytes);
             if (err == cudaSuccess)
                 err = cudaFuncSetAttribute(mslim_prefill_causal,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, kSSmemBytes);
@@ -744,8 +771,11 @@ cudaError_t launch_prefill(const CUtensorMap &qmap, const CUtensorMap &kmap,
         // persistent: one CTA per SM (at most one per item)
         const long long items = (long long)p.n_qtiles * (p.qheads / 2);
         const unsigned grid = (unsigned)(items < sms ? items : sms);
-        return launch_pdl(mslim_prefill_pair, dim3(grid), dim3(kPThreads), kPSmemBytes, stream, qmap, kmap,
-                          vmap, omap, p);
+        if (p.head_dim == 64)
+            return launch_pdl(mslim_prefill_pair<64>, dim3(grid), dim3(kPThreads), PairShape<64>::kSmemBytes,
+                              stream, qmap, kmap, vmap, omap, p);
+        return launch_pdl(mslim_prefill_pair<128>, dim3(grid), dim3(kPThreads), PairShape<128>::kSmemBytes,
+                          stream, qmap, kmap, vmap, omap, p);
     }
     const unsigned grid = (unsigned)(p.n_qtiles * p.qheads);
     mslim_prefill_causal<<<grid, kSThreads, kSSmemBytes, stream>>>(qmap, kmap, vmap, p);

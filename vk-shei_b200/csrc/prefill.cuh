@@ -15,6 +15,7 @@ struct PrefillParams {
     int qheads, kvheads, group;
     int queries, prior; // rows prior..prior+queries-1 attend to keys 0..=row
     int n_qtiles;       // ceil(queries / 128)
+    int head_dim;       // 128, or 64 with an even GQA group
     float scale_log2;   // log2(e) / sqrt(D)
 };
 
