@@ -114,3 +114,29 @@ def test_plan_rejects_bad_geometry_and_buffers(m):
         assert m.device_status(0) == 0
     finally:
         plan.close()
+
+
+@pytest.mark.parametrize("qh,kh,dim", [(8, 2, 128), (8, 2, 64), (4, 4, 64)])
+def test_long_runs_take_the_prefill_kernel_where_it_exists(m, oracle, qh, kh, dim):
+    """Runs of >= 64 queries go to the tcgen05 prefill kernel when it takes the
+    shape (head_dim 128, or 64 with an even group) and to the split-KV kernel
+    otherwise; both within tolerance of the CPU path."""
+    cfg = m.AttentionKernelConfig(mode=m.AttentionKernelMode.STRICT_TILED)
+    g = m.AttentionGeometry.new(qh, kh, dim)
+    plan = m.TiledAttention.build(cfg, g)
+    try:
+        queries, prior = 200, 57
+        n = prior + queries
+        q = modular_input(queries * qh * dim, 3).reshape(queries, qh, dim)
+        k = modular_input(n * kh * dim, 7).reshape(n, kh, dim)
+        v = modular_input(n * kh * dim, 11).reshape(n, kh, dim)
+        out = empty_u16((queries, qh, dim))
+        plan.run(dev(q), dev(k), dev(v), out, queries, prior)
+        torch_mod().cuda.synchronize()
+        ref = oracle.causal_prefill_bf16(qh, kh, dim, q, k, v, queries, prior)
+        assert max_abs(bf16_f32(host_u16(out)), bf16_f32(ref)) <= TOL
+        took_prefill = plan.diagnostics()["prefill_dispatches_since_configuration"] == 1
+        assert took_prefill == ((qh // kh) % 2 == 0 or dim == 128)
+        assert m.device_status(0) == 0
+    finally:
+        plan.close()
