@@ -244,9 +244,10 @@ def bench_prefill(m, torch, device, args) -> dict:
     touched five calls (200 MB of traffic) earlier.  The timed calls are
     captured once into a CUDA graph and replayed back to back (as consecutive
     layers' prefill would run), so host jitter (Python, the clock-sampling
-    thread) cannot idle the GPU between them; after three warm replays, three
-    replays are timed, each between a pair of CUDA events, and the median is
-    the figure.  Consecutive calls overlap launch and setup through
+    thread) cannot idle the GPU between them; after a one-second idle (the
+    power limiter recovers from the HBM-bound decode legs) and three warm
+    replays, three replays are timed, each between a pair of CUDA events, and
+    the median is the figure.  Consecutive calls overlap launch and setup through
     programmatic dependent launch; each waits for its predecessor's memory
     before it reads an input.  The same calls issued from a plain host loop,
     and one call timed alone (which carries 4-7 us of event/launch latency on
@@ -275,8 +276,10 @@ def bench_prefill(m, torch, device, args) -> dict:
     with torch.cuda.graph(graph, stream=cap, capture_error_mode="thread_local"):
         for i in range(steps):
             call(i, torch.cuda.current_stream())
-    # warm replays: the clocks and the power limiter settle into this leg's
-    # regime (the preceding legs are HBM-bound) before anything is timed
+    # a one-second idle lets the power limiter recover from the preceding
+    # HBM-bound legs, then warm replays settle the clocks into this leg's
+    # regime before anything is timed
+    time.sleep(1.0)
     for _ in range(3):
         graph.replay()
     torch.cuda.synchronize()
