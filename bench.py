@@ -13,9 +13,18 @@ needed between steps.
 
 Multi-GPU: one process per GPU (torchrun); each rank owns its own sessions
 (independent objects, no data-path collective); NCCL is used only for the
-barrier and the max-over-ranks step time.  --scaling weak (default) gives
-every rank the 64 C4 sessions; --scaling strong shards the 64 sessions of one
-C4 draw across ranks by longest-processing-time.
+barrier and the max-over-ranks step time.  --scaling strong (default) shards
+the 64 sessions of the one C4 draw across the ranks by longest-processing-
+time, as configuration C4 defines the multi-GPU case; the line carries every
+rank's token sum and split count.  At N > 1 the weak figure (every rank
+decoding its own 64 sessions) is reported beside it under "weak", and
+--scaling weak makes it the headline.
+
+The C5 leg (key "model", --no-model skips it) runs the 32-layer
+Llama-3-8B-shaped decoder tensor-parallel over the same ranks (KV-head
+groups, the fused NVLink reduction in the decode step) with a stated number
+of decode steps, so every N of a scaling run carries the tensor-parallel
+decode figures and the SHA-256 of its greedy tokens.
 
 --impl reference times the reference's CPU hot-dense path (its C
 restatement in oracle/, OpenMP across query heads like the reference's rayon
@@ -46,8 +55,13 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="strong")
     ap.add_argument("--sessions", type=int, default=64, help="sessions per GPU (small profiling cases)")
+    ap.add_argument("--shard-of", default="",
+                    help="R/N: on one GPU, time the sessions that rank R of an N-rank strong-scaling "
+                         "run owns (per-rank behaviour of the multi-GPU split)")
+    ap.add_argument("--no-model", action="store_true", help="skip the C5 tensor-parallel model leg")
+    ap.add_argument("--no-weak", action="store_true", help="skip the weak-scaling figure at N > 1")
     ap.add_argument("--split-tokens", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
@@ -60,6 +74,8 @@ def parse():
     ap.add_argument("--model-batch", type=int, default=8)
     ap.add_argument("--model-prefill", type=int, default=8192)
     ap.add_argument("--model-steps", type=int, default=256)
+    ap.add_argument("--model-leg-steps", type=int, default=64,
+                    help="decode steps of the C5 leg inside the default (C4) run")
     ap.add_argument("--mlp", choices=["sharded", "replicated"], default="sharded")
     ap.add_argument("--kv-mode", choices=["dense", "coldstore"], default="dense")
     ap.add_argument("--no-graph", action="store_true", help="C5 decode steps issued eagerly (no CUDA graph)")
@@ -105,7 +121,7 @@ class ClockSampler:
                 self.reasons |= int(p.nvmlDeviceGetCurrentClocksEventReasons(self._h))
             except Exception:
                 pass
-            time.sleep(0.005)
+            time.sleep(0.001)
 
     def start(self):
         if self._nvml:
@@ -144,6 +160,17 @@ def profile_traffic(name: str):
     return None
 
 
+def host_threads() -> int:
+    """Every host thread this process may run on.  torchrun sets
+    OMP_NUM_THREADS=1 in each rank; the CPU legs size OpenMP from the
+    affinity mask instead, so the reference arm runs on the same cores at
+    every N."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def lpt_shard(lengths, world: int, rank: int) -> list[int]:
     """Longest-processing-time assignment of sessions to ranks."""
     order = sorted(range(len(lengths)), key=lambda i: (-int(lengths[i]), i))
@@ -166,7 +193,7 @@ def cpu_sample_gbs(lengths, seconds: float, seed: int = 3) -> dict:
     from oracle import oracle
     from mslim_b200 import workloads
     rng = np.random.default_rng(seed)
-    threads = oracle.max_threads()
+    threads = host_threads()
     sample = []
     for L in lengths:
         L = int(L)
@@ -187,6 +214,7 @@ def cpu_sample_gbs(lengths, seconds: float, seed: int = 3) -> dict:
         if el >= seconds or passes >= 1000:
             break
     return {"value": done_bytes / el / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "omp_num_threads_env": os.environ.get("OMP_NUM_THREADS"),
             "sample": f"{len(sample)} C4 sessions (L={','.join(str(int(x)) for x in lengths)}) x {passes} passes, "
                       f"{el:.1f} s, oracle/mslim_oracle.c paged_attention_bf16 with {threads} OpenMP threads"}
 
@@ -200,7 +228,7 @@ def run_reference(args, rank: int) -> None:
     from oracle import oracle
     lengths = layout.lengths[:4]
     rng = np.random.default_rng(3)
-    threads = oracle.max_threads()
+    threads = host_threads()
     data = []
     for L in lengths:
         npg = (int(L) + PAGE - 1) // PAGE
@@ -228,7 +256,8 @@ def run_reference(args, rank: int) -> None:
             "data": "synthetic (seeded N(0,1) bf16)",
             "config": {"workload": "C4 batched long-context decode (bounded CPU sample)", "page_tokens": PAGE,
                        "query_heads": QH, "kv_heads": KVH, "head_dim": D},
-            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
+            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample,
+                             "omp_num_threads_env": os.environ.get("OMP_NUM_THREADS")},
             "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -339,7 +368,9 @@ def bench_prefill(m, torch, device, args) -> dict:
                                          if peaks["source"] == "measured" else "fallback 1590 TFLOP/s"),
                          "frac_of_sustained": (tflops / peaks["bf16_tflops_sustained"]
                                                if peaks.get("bf16_tflops_sustained") else None),
-                         "traffic": traffic["dram_bytes_per_launch"] if traffic else None},
+                         "traffic": traffic["dram_bytes_per_launch"] if traffic else None,
+                         "traffic_source": ("profiles/prefill_c2_traffic.json (one ncu capture of this C2 call), "
+                                            "not measured in this run" if traffic else None)},
             "gpu_launches": steps, "clocks": clocks}
 
 
@@ -555,129 +586,270 @@ def main():
         return
 
     layout = workloads.c4_layout(seed=3)
-    if args.scaling == "strong" and world > 1:
-        mine = lpt_shard(layout.lengths, world, rank)
+    all_sessions = list(range(min(args.sessions, len(layout.lengths))))
+    shard_world, shard_rank = world, rank
+    if args.shard_of:
+        shard_rank, shard_world = (int(x) for x in args.shard_of.split("/"))
+    strong = args.scaling == "strong" and shard_world > 1
+    if strong:
+        mine = lpt_shard(layout.lengths[all_sessions], shard_world, shard_rank)
     else:
-        mine = list(range(min(args.sessions, len(layout.lengths))))
-    lengths = layout.lengths[mine].astype(np.int32)
-    n_seq = len(mine)
-    # pages for L + 1 tokens: the e2e leg appends the step's new token at L
-    pages = (lengths + 1 + PAGE - 1) // PAGE
-    n_pages = int(pages.sum())
-    rng = np.random.default_rng(3 + rank)
-    perm = rng.permutation(n_pages).astype(np.int32)
-    max_pages = int(pages.max())
-    table = np.zeros((n_seq, max_pages), np.int32)
-    cur = 0
-    for s in range(n_seq):
-        table[s, :pages[s]] = perm[cur:cur + pages[s]]
-        cur += pages[s]
-
-    gen = torch.Generator(device=device)
-    gen.manual_seed(3 + rank)
-    k_pool = torch.randn((n_pages, KVH, PAGE, D), generator=gen, device=device, dtype=torch.bfloat16)
-    v_pool = torch.randn((n_pages, KVH, PAGE, D), generator=gen, device=device, dtype=torch.bfloat16)
-    q = torch.randn((n_seq, QH, D), generator=gen, device=device, dtype=torch.bfloat16)
-    out = torch.empty((n_seq, QH, D), device=device, dtype=torch.bfloat16)
-    table_d = torch.from_numpy(table).to(device)
-    seq_d = torch.from_numpy(lengths).to(device)
-    g = m.AttentionGeometry.new(QH, KVH, D)
-    max_tokens = max_pages * PAGE
-    ws = torch.empty(m.decode_workspace_bytes(g, n_seq, max_tokens, args.split_tokens), dtype=torch.uint8,
-                     device=device)
-    stream = torch.cuda.current_stream()
-
-    def step():
-        m.decode_paged(g, q, k_pool, v_pool, n_pages, PAGE, table_d, max_pages, seq_d, n_seq, ws, out,
-                       args.split_tokens, stream)
-
-    step_bytes = int(lengths.astype(np.int64).sum()) * KVH * D * 4 + n_seq * QH * D * 4 + int(
-        ((lengths + PAGE - 1) // PAGE).sum()) * 4
-
-    for _ in range(max(args.warmup, 3)):
-        step()
-    torch.cuda.synchronize()
-    if m.device_status(local) != 0:
-        raise SystemExit("device status reported a bounded wait timeout during warm-up")
+        mine = all_sessions
+    c4 = C4Pages(np, torch, device, m, layout.lengths[mine].astype(np.int32), seed=3 + rank,
+                 split_tokens=args.split_tokens)
 
     def barrier():
         if dist is not None:
             dist.barrier()
 
-    # ---- device-timed region (CUDA events on the launching stream) ----
-    sampler = ClockSampler(local)
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    barrier()
-    torch.cuda.synchronize()
-    sampler.start()
-    t_start = torch.cuda.Event(enable_timing=True)
-    t_end = torch.cuda.Event(enable_timing=True)
-    t_start.record(stream)
-    for i in range(args.steps):
-        evs[i][0].record(stream)
-        step()
-        evs[i][1].record(stream)
-    t_end.record(stream)
-    torch.cuda.synchronize()
-    barrier()
-    clocks = sampler.stop()
-    elapsed_ms = t_start.elapsed_time(t_end)
-    launch_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
-    if dist is not None:
-        t = torch.tensor([elapsed_ms], device=device, dtype=torch.float64)
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], device=device, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed_ms = float(t.item())
-        tb = torch.tensor([step_bytes, n_seq], device=device, dtype=torch.float64)
-        dist.all_reduce(tb, op=dist.ReduceOp.SUM)
-        total_bytes, total_seq = float(tb[0].item()), int(tb[1].item())
-    else:
-        total_bytes, total_seq = float(step_bytes), n_seq
+        return float(t.item())
+
+    def sum_over_ranks(*xs):
+        if dist is None:
+            return [float(x) for x in xs]
+        t = torch.tensor(list(xs), device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return [float(x) for x in t.tolist()]
+
+    def per_rank(*xs):
+        """[world][len(xs)] of every rank's values (rank order)."""
+        t = torch.tensor([list(xs)], device=device, dtype=torch.float64)
+        if dist is None:
+            return t.tolist()
+        every = torch.empty((world, len(xs)), device=device, dtype=torch.float64)
+        dist.all_gather_into_tensor(every, t)
+        return every.tolist()
+
+    # ---- device-timed region (CUDA events on the launching stream) ----
+    timed = c4.time_steps(args.steps, max(args.warmup, 3), local, barrier)
+    elapsed_ms = max_over_ranks(timed["elapsed_ms"])
+    total_bytes, total_seq, total_tokens = sum_over_ranks(c4.step_bytes, c4.n_seq, c4.tokens)
+    total_seq = int(total_seq)
     ms_per_step = elapsed_ms / args.steps
     value = total_bytes / (ms_per_step * 1e-3) / 1e9
+    ranks = per_rank(c4.tokens, c4.n_seq, c4.split_tokens, c4.ctas, timed["elapsed_ms"] / args.steps)
     status = m.device_status(local)
 
     # ---- end-to-end leg: the C-ABI calls a decode step makes, host buffers ----
     e2e = None
     if not args.no_e2e:
+        e = c4.time_e2e(args.steps, barrier)
+        e_ms = max_over_ranks(e["ms"])
+        e_bytes, = sum_over_ranks(e["bytes"])
+        e2e = {"value": e_bytes / (e_ms / args.steps * 1e-3) / 1e9, "unit": "GB/s",
+               "h2d_bytes_per_step": e["h2d"] * world, "d2h_bytes_per_step": e["d2h"] * world,
+               "ms_per_step": e_ms / args.steps,
+               "path": "pinned host q/k/v -> mslim_cuda_rope_append_decode_paged -> mslim_cuda_decode_paged "
+                       "-> host output; the step's copies and launches replayed as one CUDA graph, the "
+                       "host waits for every step's result"}
+        if m.device_status(local) != 0:
+            raise SystemExit("device status reported an error during the e2e leg")
+    c4_local = {"step_bytes": c4.step_bytes, "launch_ms": timed["launch_ms"], "n_seq": c4.n_seq,
+                "lengths": c4.lengths}
+    c4.close()
+    del c4
+    torch.cuda.empty_cache()
+
+    # ---- weak scaling beside the strong headline (N > 1): every rank its own 64 sessions ----
+    weak = None
+    if strong and world > 1 and not args.no_weak:
+        w4 = C4Pages(np, torch, device, m, layout.lengths[all_sessions].astype(np.int32), seed=3 + rank,
+                     split_tokens=args.split_tokens)
+        wt = w4.time_steps(args.steps, max(args.warmup, 3), local, barrier)
+        w_ms = max_over_ranks(wt["elapsed_ms"]) / args.steps
+        w_bytes, w_seq = sum_over_ranks(w4.step_bytes, w4.n_seq)
+        weak = {"value": w_bytes / (w_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": w_ms,
+                "global_sessions": int(w_seq), "sessions_per_gpu": w4.n_seq,
+                "note": "every rank decodes its own copy of the 64 C4 sessions (weak scaling)"}
+        w4.close()
+        del w4
+        torch.cuda.empty_cache()
+
+    prefill = None
+    if rank == 0 and not args.no_prefill:
+        prefill = bench_prefill(m, torch, device, args)
+        torch.cuda.empty_cache()
+
+    # ---- C5 leg: the tensor-parallel decoder over the same ranks ----
+    model = None
+    if not args.no_model:
+        margs = argparse.Namespace(**vars(args))
+        margs.model_steps = args.model_leg_steps
+        barrier()
+        model = bench_model(m, torch, device, margs, rank, world, dist)
+        torch.cuda.empty_cache()
+
+    if rank != 0:
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+
+    peaks = measured_peaks()
+    step_bytes = c4_local["step_bytes"]
+    achieved = step_bytes / (c4_local["launch_ms"] * 1e-3) / 1e9
+    traffic = profile_traffic("decode_c4_traffic.json")
+    roofline = {"bound": "hbm", "kernel": "mslim_decode_split + mslim_decode_merge",
+                "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"] if peaks["hbm_gbs"] else None,
+                "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)" if peaks["source"] == "measured"
+                else "fallback 6650 GB/s",
+                "traffic": (int(traffic["traffic_over_algorithmic"] * step_bytes) if traffic else None),
+                "traffic_source": ("scaled from profiles/decode_c4_traffic.json, not measured in this run: one "
+                                   "ncu capture of 8 C4 sessions gave DRAM bytes / algorithmic bytes = "
+                                   f"{traffic['traffic_over_algorithmic']:.4f}, applied to this launch's "
+                                   "algorithmic bytes" if traffic else None),
+                "algorithmic_bytes_per_launch": step_bytes,
+                "achieved_note": "rank 0's algorithmic bytes / its mean per-step CUDA-event time"}
+    cpu = None
+    if not args.no_cpu and world == 1:
+        cpu = cpu_sample_gbs(c4_local["lengths"][:4], args.cpu_seconds)
+    rank_tokens = [r[0] for r in ranks]
+    mean_tokens = sum(rank_tokens) / len(rank_tokens)
+    line = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "strong" if (strong or world == 1) and args.scaling == "strong" else "weak",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) bf16 K/V/Q; no dataset)",
+            "config": {"workload": "C4 batched long-context decode: 64 sessions with L ~ U[4096,32768] (seed 3), "
+                                   "256-token ColdStore-exact pages in a random physical permutation, "
+                                   "QH 32 / KVH 8 / D 128, one query per session",
+                       "sessions_per_gpu": c4_local["n_seq"], "global_sessions": total_seq, "page_tokens": PAGE,
+                       "split_tokens": args.split_tokens or "policy",
+                       "l2": "no flush: inputs larger than L2 (%.2f GB per GPU per step)" % (step_bytes / 1e9),
+                       "parallelism": (f"sessions LPT-sharded over {world} GPUs (strong: one 64-session C4 draw)"
+                                       if strong else
+                                       f"session-sharded x{world} ({args.scaling})"),
+                       **({"shard_of": args.shard_of} if args.shard_of else {})},
+            "tokens_per_s": total_seq / (ms_per_step * 1e-3),
+            "per_rank": {"tokens": rank_tokens, "sessions": [int(r[1]) for r in ranks],
+                         "split_tokens": [int(r[2]) for r in ranks], "split_ctas": [int(r[3]) for r in ranks],
+                         "ms_per_step": [r[4] for r in ranks],
+                         "token_imbalance_max_over_mean": max(rank_tokens) / mean_tokens if mean_tokens else None},
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "prefill": prefill,
+            "weak": weak, "model": model,
+            "gpu_launches": 2 * args.steps, "clocks": timed["clocks"], "device_status": status}
+    print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+class C4Pages:
+    """One rank's C4 sessions in 256-token ColdStore-exact pages (random
+    physical permutation) with the decode's query, output and workspace."""
+
+    def __init__(self, np, torch, device, m, lengths, seed: int, split_tokens: int = 0):
+        self.np, self.torch, self.device, self.m = np, torch, device, m
+        self.lengths = lengths
+        self.n_seq = n_seq = len(lengths)
+        # pages for L + 1 tokens: the e2e leg appends the step's new token at L
+        pages = (lengths + 1 + PAGE - 1) // PAGE
+        self.n_pages = n_pages = int(pages.sum())
+        rng = np.random.default_rng(seed)
+        perm = rng.permutation(n_pages).astype(np.int32)
+        self.max_pages = max_pages = int(pages.max())
+        table = np.zeros((n_seq, max_pages), np.int32)
+        cur = 0
+        for s in range(n_seq):
+            table[s, :pages[s]] = perm[cur:cur + pages[s]]
+            cur += pages[s]
+        gen = torch.Generator(device=device)
+        gen.manual_seed(seed)
+        self.k_pool = torch.randn((n_pages, KVH, PAGE, D), generator=gen, device=device, dtype=torch.bfloat16)
+        self.v_pool = torch.randn((n_pages, KVH, PAGE, D), generator=gen, device=device, dtype=torch.bfloat16)
+        self.q = torch.randn((n_seq, QH, D), generator=gen, device=device, dtype=torch.bfloat16)
+        self.out = torch.empty((n_seq, QH, D), device=device, dtype=torch.bfloat16)
+        self.table_d = torch.from_numpy(table).to(device)
+        self.seq_d = torch.from_numpy(lengths).to(device)
+        self.g = m.AttentionGeometry.new(QH, KVH, D)
+        max_tokens = max_pages * PAGE
+        self.split_tokens = split_tokens or m.decode_split_tokens(self.g, n_seq, max_tokens)
+        self.ws = torch.empty(m.decode_workspace_bytes(self.g, n_seq, max_tokens, self.split_tokens),
+                              dtype=torch.uint8, device=device)
+        self.ctas = int(sum(-(-int(L) // self.split_tokens) for L in lengths)) * KVH
+        self.tokens = int(lengths.astype(np.int64).sum())
+        self.step_bytes = self.tokens * KVH * D * 4 + n_seq * QH * D * 4 + int(((lengths + PAGE - 1) // PAGE).sum()) * 4
+        self.stream = torch.cuda.current_stream()
+
+    def step(self):
+        self.m.decode_paged(self.g, self.q, self.k_pool, self.v_pool, self.n_pages, PAGE, self.table_d,
+                            self.max_pages, self.seq_d, self.n_seq, self.ws, self.out, self.split_tokens,
+                            self.stream)
+
+    def time_steps(self, steps: int, warmup: int, local: int, barrier) -> dict:
+        torch = self.torch
+        for _ in range(warmup):
+            self.step()
+        torch.cuda.synchronize()
+        if self.m.device_status(local) != 0:
+            raise SystemExit("device status reported a bounded wait timeout during warm-up")
+        sampler = ClockSampler(local)
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        barrier()
+        torch.cuda.synchronize()
+        sampler.start()
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record(self.stream)
+        for i in range(steps):
+            evs[i][0].record(self.stream)
+            self.step()
+            evs[i][1].record(self.stream)
+        t_end.record(self.stream)
+        torch.cuda.synchronize()
+        barrier()
+        clocks = sampler.stop()
+        return {"elapsed_ms": t_start.elapsed_time(t_end),
+                "launch_ms": statistics.mean(a.elapsed_time(b) for a, b in evs), "clocks": clocks}
+
+    def time_e2e(self, steps: int, barrier) -> dict:
+        """Per step: the new token's q, k and v of every session from one
+        pinned host buffer -> RoPE + paged append -> split-KV decode -> the
+        output back in pinned host memory, captured once as a CUDA graph and
+        replayed; the host waits for every step's result."""
+        torch, np, m = self.torch, self.np, self.m
+        n_seq, lengths, stream = self.n_seq, self.lengths, self.stream
         rope_cfg = m.RopeKernelConfig(theta=500000.0)
-        # the step's inputs (the new token's q, k and v of every session) in one
-        # pinned host buffer, so one host-to-device copy carries them
         nq_el, nkv_el = n_seq * QH * D, 2 * n_seq * KVH * D
         in_host = torch.empty(nq_el + nkv_el, dtype=torch.bfloat16).pin_memory()
         in_host[:nq_el].copy_(torch.randn(nq_el, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16))
         in_host[nq_el:].copy_(torch.randn(nkv_el, generator=torch.Generator().manual_seed(6)).to(torch.bfloat16))
         out_host = torch.empty((n_seq, QH, D), dtype=torch.bfloat16).pin_memory()
-        in_dev = torch.empty(nq_el + nkv_el, device=device, dtype=torch.bfloat16)
+        in_dev = torch.empty(nq_el + nkv_el, device=self.device, dtype=torch.bfloat16)
         q_in = in_dev[:nq_el].view(n_seq, QH, D)
         kv_in = in_dev[nq_el:].view(2, n_seq, KVH, D)
-        q_rot = torch.empty_like(q)
-        pos_d = torch.from_numpy(lengths).to(device)          # new token at position L
-        seq1_d = torch.from_numpy(lengths + 1).to(device)     # then attend over L + 1
+        q_rot = torch.empty_like(self.q)
+        pos_d = torch.from_numpy(lengths).to(self.device)          # new token at position L
+        seq1_d = torch.from_numpy(lengths + 1).to(self.device)     # then attend over L + 1
 
-        def e2e_calls(st):
+        def calls(st):
             in_dev.copy_(in_host, non_blocking=True)
-            m.rope_append_decode_paged(g, q_in, q_rot, kv_in[0], kv_in[1], pos_d, n_seq, rope_cfg, k_pool,
-                                       v_pool, n_pages, PAGE, table_d, max_pages, st)
-            m.decode_paged(g, q_rot, k_pool, v_pool, n_pages, PAGE, table_d, max_pages, seq1_d, n_seq, ws,
-                           out, args.split_tokens, st)
-            out_host.copy_(out, non_blocking=True)
+            m.rope_append_decode_paged(self.g, q_in, q_rot, kv_in[0], kv_in[1], pos_d, n_seq, rope_cfg,
+                                       self.k_pool, self.v_pool, self.n_pages, PAGE, self.table_d,
+                                       self.max_pages, st)
+            m.decode_paged(self.g, q_rot, self.k_pool, self.v_pool, self.n_pages, PAGE, self.table_d,
+                           self.max_pages, seq1_d, n_seq, self.ws, self.out, self.split_tokens, st)
+            out_host.copy_(self.out, non_blocking=True)
 
-        # one decode step = copy in, RoPE + append, split-KV decode, copy out,
-        # captured once as a CUDA graph; every step replays it and waits for
-        # its result on the host (a blocking dispatch, as the reference's)
-        e2e_calls(stream)
+        calls(stream)
         stream.synchronize()
-        e2e_graph = torch.cuda.CUDAGraph()
+        graph = torch.cuda.CUDAGraph()
         cap = torch.cuda.Stream()
         cap.wait_stream(stream)
         # thread-local capture: other threads of the process (the process
         # group's) may touch CUDA while this thread captures
-        with torch.cuda.graph(e2e_graph, stream=cap, capture_error_mode="thread_local"):
-            e2e_calls(torch.cuda.current_stream())
+        with torch.cuda.graph(graph, stream=cap, capture_error_mode="thread_local"):
+            calls(torch.cuda.current_stream())
         torch.cuda.synchronize()
 
         def e2e_step():
-            e2e_graph.replay()
+            graph.replay()
             stream.synchronize()
 
         for _ in range(3):
@@ -689,68 +861,17 @@ def main():
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             e2e_step()
         b.record(stream)
         torch.cuda.synchronize()
-        e_ms = a.elapsed_time(b)
-        if dist is not None:
-            t = torch.tensor([e_ms], device=device, dtype=torch.float64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e_ms = float(t.item())
-            tb = torch.tensor([e_bytes], device=device, dtype=torch.float64)
-            dist.all_reduce(tb, op=dist.ReduceOp.SUM)
-            e_bytes = float(tb[0].item())
-        e2e = {"value": e_bytes / (e_ms / args.steps * 1e-3) / 1e9, "unit": "GB/s",
-               "h2d_bytes_per_step": int(in_host.numel() * 2) * world,
-               "d2h_bytes_per_step": int(out_host.numel() * 2) * world,
-               "ms_per_step": e_ms / args.steps,
-               "path": "pinned host q/k/v -> mslim_cuda_rope_append_decode_paged -> mslim_cuda_decode_paged "
-                       "-> host output; the step's copies and launches replayed as one CUDA graph, the "
-                       "host waits for every step's result"}
-        del e2e_graph
-        if m.device_status(local) != 0:
-            raise SystemExit("device status reported an error during the e2e leg")
+        ms = a.elapsed_time(b)
+        del graph
+        return {"ms": ms, "bytes": e_bytes, "h2d": int(in_host.numel() * 2), "d2h": int(out_host.numel() * 2)}
 
-    prefill = None
-    if rank == 0 and not args.no_prefill:
-        prefill = bench_prefill(m, torch, device, args)
-
-    if rank != 0:
-        if dist is not None:
-            dist.destroy_process_group()
-        return
-
-    peaks = measured_peaks()
-    achieved = step_bytes / (launch_ms * 1e-3) / 1e9
-    traffic = profile_traffic("decode_c4_traffic.json")
-    roofline = {"bound": "hbm", "kernel": "mslim_decode_split + mslim_decode_merge",
-                "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / peaks["hbm_gbs"] if peaks["hbm_gbs"] else None,
-                "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)" if peaks["source"] == "measured"
-                else "fallback 6650 GB/s",
-                "traffic": (traffic["dram_bytes_per_launch_scaled"] if traffic and n_seq == 64 else None),
-                "algorithmic_bytes_per_launch": step_bytes}
-    cpu = None
-    if not args.no_cpu and world == 1:
-        cpu = cpu_sample_gbs(lengths[:4], args.cpu_seconds)
-    line = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-            "scaling": args.scaling, "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded N(0,1) bf16 K/V/Q; no dataset)",
-            "config": {"workload": "C4 batched long-context decode: sessions with L ~ U[4096,32768] (seed 3), "
-                                   "256-token ColdStore-exact pages in a random physical permutation, "
-                                   "QH 32 / KVH 8 / D 128, one query per session",
-                       "sessions_per_gpu": n_seq, "global_sessions": total_seq, "page_tokens": PAGE,
-                       "split_tokens": args.split_tokens or "policy",
-                       "l2": "no flush: inputs larger than L2 (%.2f GB per GPU per step)" % (step_bytes / 1e9),
-                       "parallelism": f"session-sharded x{world} ({args.scaling})"},
-            "tokens_per_s": total_seq / (ms_per_step * 1e-3),
-            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "prefill": prefill,
-            "gpu_launches": 2 * args.steps, "clocks": clocks, "device_status": status}
-    print(json.dumps(line), flush=True)
-    if dist is not None:
-        dist.destroy_process_group()
+    def close(self):
+        for name in ("k_pool", "v_pool", "q", "out", "ws", "table_d", "seq_d"):
+            setattr(self, name, None)
 
 
 if __name__ == "__main__":

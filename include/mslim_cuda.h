@@ -16,7 +16,11 @@
  *   - work is enqueued on the caller's stream (`stream` is a cudaStream_t,
  *     NULL = legacy default stream); no host synchronisation inside decode;
  *   - inputs are read-only and must not alias the output
- *     (src/gpu_llm/tiled_attention.rs:204-207).
+ *     (src/gpu_llm/tiled_attention.rs:204-207);
+ *   - the device addresses of the library's own device globals (the status
+ *     word, the static decode scratch) are looked up once per device and
+ *     kept for the life of the process: do not call the library on a device
+ *     after cudaDeviceReset or any other teardown of its primary context.
  *
  * Data formats: "bf16" is raw little-endian uint16 bits.  K/V are either
  * token-major [tokens][kv_heads][head_dim] (the reference's dense GPU caches,
@@ -90,8 +94,10 @@ const char *mslim_cuda_last_error(void);
 /* Reads (and with reset != 0 clears) the device status word that kernels set
  * when a bounded device-side wait gives up (*status = MSLIM_ERR_DEVICE_TIMEOUT,
  * same return code) or a page-table entry lies outside the page pool
- * (*status = MSLIM_ERR_SHAPE_MISMATCH, same return code, nothing written);
- * synchronises `device`.  No reference counterpart: the
+ * (*status = MSLIM_ERR_SHAPE_MISMATCH, same return code; the pool is never
+ * addressed through such an entry: appends and gathers write nothing for it,
+ * a paged decode leaves that session's output undefined); synchronises
+ * `device`.  No reference counterpart: the
  * reference relies on the OpenCL queue timeout (docs/validation/
  * tiled-attention.json:790-796). */
 int mslim_cuda_device_status(int device, int reset, int *status);
@@ -154,6 +160,14 @@ int mslim_cuda_plan_diagnostics(const mslim_plan_t *plan, char *out, size_t len)
 int mslim_cuda_decode_workspace_bytes(const mslim_geometry_t *geometry, uint32_t n_seq,
                                       uint32_t max_tokens, uint32_t split_tokens, size_t *bytes);
 
+/* The split size (tokens, a multiple of 64) that split_tokens == 0 selects
+ * for n_seq sequences of at most max_tokens tokens.  Outputs depend on the
+ * split size only through rounding; a caller that needs the same bits from
+ * two calls passes the same explicit value.  Counterpart of the split count
+ * that AttentionKernelConfig carries (src/attention_kernel.rs:6-42). */
+int mslim_cuda_decode_split_tokens(const mslim_geometry_t *geometry, uint32_t n_seq,
+                                   uint32_t max_tokens, uint32_t *split_tokens);
+
 /* Dense decode: GpuEngine::attention / exact_hot_fused_attention
  * (src/gpu_llm/gpu_resources.rs:583-643,783-828) for a batch of sequences.
  * q: bf16 [n_seq][QH][D] (post-RoPE); k_cache/v_cache: bf16 token-major
@@ -200,7 +214,10 @@ int mslim_cuda_decode_selected(const mslim_geometry_t *geometry, const void *q, 
  * [n_pages][KVH][page_tokens][D]; page_table: device int32
  * [n_seq][max_pages_per_seq] of physical page ids; seq_tokens: device int32
  * [n_seq].  page_tokens must be a multiple of 64.  Results are bit-identical
- * to mslim_cuda_decode_dense on the same K/V bytes. */
+ * to mslim_cuda_decode_dense on the same K/V bytes.  A table entry outside
+ * [0, n_pages) is not loaded; it is reported by mslim_cuda_device_status and
+ * the output rows of its session are undefined (other sessions are
+ * unaffected). */
 int mslim_cuda_decode_paged(const mslim_geometry_t *geometry, const void *q, const void *k_pool,
                             const void *v_pool, uint32_t n_pages, uint32_t page_tokens,
                             const int32_t *page_table, uint32_t max_pages_per_seq,
@@ -215,14 +232,16 @@ int mslim_cuda_decode_paged(const mslim_geometry_t *geometry, const void *q, con
  * Same arguments and results as mslim_cuda_decode_paged minus the workspace;
  * with the same split_tokens the output is bit-identical to it.
  * The split partials live in a library-owned static device array of
- * MSLIM_STATIC_SCRATCH_BYTES (16 MiB, the reference's split-scratch bound,
- * src/attention_kernel.rs:124-138), held by every GPU that loads the library
- * until the process exits.  A request whose partials exceed it fails with
+ * MSLIM_STATIC_SCRATCH_BYTES (16 MiB, a fixed limit of this library), held by
+ * every GPU that loads the library until the process exits.  A request whose partials exceed it fails with
  * MSLIM_ERR_SHAPE_MISMATCH; split_tokens == 0 picks the library's split size
  * and, if needed, larger splits until the partials fit.  The first call on a
  * device looks up the array's device address (no allocation); make that first
- * call before any stream capture.  Every call shares the one array: calls
- * that can overlap on the GPU (different streams, no ordering) race on it. */
+ * call before any stream capture.  That address is kept for the life of the
+ * process, so the library must not be used on a device after
+ * cudaDeviceReset (or any other teardown of its primary context).  Every
+ * call shares the one array: calls that can overlap on the GPU (different
+ * streams, no ordering) race on it. */
 #define MSLIM_STATIC_SCRATCH_BYTES (16u << 20)
 int mslim_cuda_decode_paged_static_scratch(const mslim_geometry_t *geometry, const void *q,
                                            const void *k_pool, const void *v_pool,
@@ -312,6 +331,14 @@ int mslim_cuda_swiglu_rows(const void *gate_up, void *out, uint32_t rows, uint32
  * index among equals, NaN never preferred (the OpenCL kernel). */
 int mslim_cuda_argmax(const void *logits, uint32_t rows, uint32_t vocab, int ties_to_last,
                       int32_t *token_ids, void *stream);
+
+/* Diagnostic of the prefill softmax's exponentials, no reference counterpart:
+ * for device f32 arrays of n values, y_poly = the FMA-pipe polynomial 2^x the
+ * prefill kernels evaluate for one pair in eight, y_mufu = the MUFU ex2.approx
+ * they use for the rest, y_ref = CUDA's exp2f.  Lets a test measure the
+ * polynomial's stated error bound on the device. */
+int mslim_cuda_exp2_eval(const float *x, float *y_poly, float *y_mufu, float *y_ref, uint32_t n,
+                         void *stream);
 
 /* ------------------------------------------- tensor-parallel decode -- */
 

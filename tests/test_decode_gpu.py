@@ -218,6 +218,43 @@ def test_rejects_bad_arguments(m):
         m.decode_paged(g, b, b, b, 1, 48, seq, 1, seq, 1, ws, b.clone())
 
 
+def test_paged_decode_reports_page_ids_outside_the_pool(m, wl):
+    """A page-table entry outside [0, n_pages) is never loaded: the decode
+    records it in the device status word (mslim_cuda_device_status returns
+    MSLIM_ERR_SHAPE_MISMATCH), and sessions whose rows are intact keep their
+    exact outputs.  The reference rejects bad buffers before dispatch
+    (src/gpu_llm/tiled_attention.rs:172-207); here the table lives on the
+    device, so the check runs where the entry is read."""
+    import ctypes
+    from mslim_b200 import _lib
+    torch = torch_mod()
+    rng = np.random.default_rng(41)
+    qh, kvh, d, pt = 32, 8, 128, 64
+    lengths = [300, 200, 130, 64]
+    pool = build_pool(wl, rng, lengths, kvh, d, pt)
+    g = m.AttentionGeometry.new(qh, kvh, d)
+    q = rand_bf16(wl, rng, (len(lengths), qh, d))
+    want = run_paged(m, g, q, pool, lengths, pt)
+    bad = dict(pool)
+    bad["table"] = pool["table"].copy()
+    bad["table"][0, 2] = pool["n_pages"]      # one past the pool
+    bad["table"][2, 1] = -1                   # negative
+    n_seq = len(lengths)
+    ws = torch.empty(m.decode_workspace_bytes(g, n_seq, pool["max_tokens"]), dtype=torch.uint8, device="cuda:0")
+    out = empty_u16((n_seq, qh, d))
+    m.decode_paged(g, dev(q), dev(pool["k_pool"]), dev(pool["v_pool"]), pool["n_pages"], pt, dev(bad["table"]),
+                   pool["max_pages"], dev(np.asarray(lengths, np.int32)), n_seq, ws, out)
+    st = ctypes.c_int(0)
+    rc = _lib.lib().mslim_cuda_device_status(0, 1, ctypes.byref(st))
+    assert rc == _lib.ERR_SHAPE_MISMATCH and st.value == 2, (rc, st.value)
+    assert "outside the page pool" in _lib.last_error()
+    got = host_u16(out)
+    for s in (1, 3):                          # untouched table rows: same bits
+        assert np.array_equal(got[s], want[s]), s
+    # the status word was cleared; a good table decodes cleanly again
+    assert np.array_equal(run_paged(m, g, q, pool, lengths, pt), want)
+
+
 @pytest.mark.parametrize("tokens", [256, 100, 1])
 def test_page_token_hashes_match_the_coldstore_record(m, oracle, tokens):
     """ColdStore page sealing from device pages (cold_store.rs:725-742): the
@@ -331,3 +368,33 @@ def test_selected_decode_empty_and_invalid_selections(m, wl):
     sel = np.zeros((2, 4), np.int32)
     _selected_case(m, wl, rng, [40, 50], [5, 1], 4, sel=sel)
     assert m.device_status(0) == 2
+
+
+def test_gpu_engine_reserves_its_workspace_when_built(m, wl, oracle):
+    """GpuEngine::attention (src/gpu_llm/gpu_resources.rs:583-643) through the
+    Python mirror: the decode workspace is reserved when the engine is built
+    (like the reference's Workspace), attention() allocates nothing, its
+    output equals the dense entry point's, and a history beyond the reserved
+    capacity is a ShapeMismatch."""
+    torch = torch_mod()
+    rng = np.random.default_rng(43)
+    qh, kvh, d, cap = 32, 8, 128, 1024
+    g = m.AttentionGeometry.new(qh, kvh, d)
+    eng = m.GpuEngine(0, g, cap)
+    ws_ptr = eng._workspace.data_ptr()
+    k = rand_bf16(wl, rng, (cap, kvh, d))
+    v = rand_bf16(wl, rng, (cap, kvh, d))
+    q = rand_bf16(wl, rng, (qh, d))
+    kd, vd, qd = dev(k), dev(v), dev(q)
+    for T in (1, 300, cap):
+        out = empty_u16((qh, d))
+        eng.attention(qd, (kd, vd), out, T, g)
+        torch.cuda.synchronize()
+        assert eng._workspace.data_ptr() == ws_ptr
+        want = run_dense(m, g, q[None], k[None, :T], v[None, :T])[0]
+        ref = oracle.dense_attention_bf16(qh, kvh, d, bf16_f32(q).reshape(-1), k[:T], v[:T])
+        got = host_u16(out)
+        assert max_abs(bf16_f32(got).reshape(-1), ref) <= TOL
+        assert got.tobytes() == want.tobytes()        # same call, same split policy
+    with pytest.raises(m.ShapeMismatch):
+        eng.attention(qd, (kd, vd), empty_u16((qh, d)), cap + 1, g)

@@ -100,3 +100,40 @@ def test_prefill_rejects_unsupported(m):
         m.prefill_causal(m.AttentionGeometry.new(4, 2, 80), b, b, b, b.clone(), 1, 0)
     with pytest.raises(m.ShapeMismatch):
         m.prefill_causal(m.AttentionGeometry.new(4, 1, 128), b, b, b, b, 1, 0)
+
+
+def test_fma_pipe_exp2_meets_its_stated_error_bound():
+    """The prefill softmax evaluates one exponential pair in eight with a
+    polynomial on the FMA pipe (exp2_fma: round-to-integer split, the Remez
+    minimax cubic for 2^f on [-1/2, 1/2], exponent-field add).  Over (-126, 0],
+    the argument range of a softmax that subtracts the row maximum, its
+    relative error against CUDA's exp2f (and against float64) stays within the
+    stated 7.5e-5; at -126 and below it returns about 2^-126."""
+    import ctypes
+    import torch
+    from mslim_b200 import _lib
+    _lib.lib()
+    grid = -126.0 + np.arange(126 * 4096 + 1, dtype=np.float64) / 4096.0      # every 2^-12 step
+    rng = np.random.default_rng(9)
+    x = np.concatenate([grid[1:], rng.uniform(-126.0, 0.0, 1 << 20), [-1e-30, -0.5, 0.5 - 1.0, -125.5]])
+    x = x.astype(np.float32)
+    xd = torch.from_numpy(x).cuda()
+    outs = [torch.empty_like(xd) for _ in range(3)]
+    rc = _lib.lib().mslim_cuda_exp2_eval(xd.data_ptr(), outs[0].data_ptr(), outs[1].data_ptr(),
+                                         outs[2].data_ptr(), x.size, None)
+    assert rc == 0, _lib.last_error()
+    torch.cuda.synchronize()
+    poly, mufu, ref = (o.cpu().numpy().astype(np.float64) for o in outs)
+    rel = np.abs(poly / ref - 1.0)
+    assert rel.max() <= 7.5e-5, (rel.max(), x[np.argmax(rel)])
+    exact = np.exp2(x.astype(np.float64))
+    assert np.abs(poly / exact - 1.0).max() <= 7.5e-5 + 2e-7
+    assert np.abs(mufu / exact - 1.0).max() <= 1e-6          # the MUFU path, for scale
+    low = np.array([-126.0, -130.0, -1000.0], np.float32)
+    xl = torch.from_numpy(low).cuda()
+    outl = [torch.empty_like(xl) for _ in range(3)]
+    assert _lib.lib().mslim_cuda_exp2_eval(xl.data_ptr(), outl[0].data_ptr(), outl[1].data_ptr(),
+                                           outl[2].data_ptr(), low.size, None) == 0
+    torch.cuda.synchronize()
+    got = outl[0].cpu().numpy().astype(np.float64)
+    assert np.all(np.abs(got / 2.0 ** -126 - 1.0) <= 2e-4), got

@@ -102,3 +102,40 @@ def test_static_scratch_rejects_oversized_requests(m):
     rc = call_static(m, g, case, out, 64)
     assert rc == m._lib.ERR_SHAPE_MISMATCH
     assert "static scratch" in m._lib.last_error()
+
+
+def test_static_scratch_takes_larger_splits_when_the_policy_split_overflows(m):
+    """64 sessions of 32768 tokens: at the library's own split size the
+    partials need more than the 16 MiB array, so split_tokens == 0 doubles the
+    split until they fit.  The result equals the workspace entry point at that
+    doubled split, bit for bit, on two calls in a row."""
+    torch = torch_mod()
+    g = m.AttentionGeometry.new(32, 8, 128)
+    n_seq, L, pt = 64, 32768, 256
+    limit = 16 << 20
+    policy = m.decode_split_tokens(g, n_seq, L)
+    assert m.decode_workspace_bytes(g, n_seq, L, policy) > limit     # the case overflows
+    st = policy
+    while m.decode_workspace_bytes(g, n_seq, L, st) > limit and st < L:
+        st *= 2
+    assert st > policy and m.decode_workspace_bytes(g, n_seq, L, st) <= limit
+    pages = L // pt
+    n_pages = n_seq * pages
+    gen = torch.Generator(device="cuda:0")
+    gen.manual_seed(23)
+    k = torch.randn((n_pages, 8, pt, 128), generator=gen, device="cuda:0", dtype=torch.bfloat16)
+    v = torch.randn((n_pages, 8, pt, 128), generator=gen, device="cuda:0", dtype=torch.bfloat16)
+    q = torch.randn((n_seq, 32, 128), generator=gen, device="cuda:0", dtype=torch.bfloat16)
+    table = torch.randperm(n_pages, generator=gen, device="cuda:0").to(torch.int32).view(n_seq, pages)
+    seq = torch.full((n_seq,), L, dtype=torch.int32, device="cuda:0")
+    case = dict(q=q, k=k, v=v, table=table, n_pages=n_pages, max_pages=pages, seq=seq, n_seq=n_seq,
+                page_tokens=pt)
+    want = call_workspace(m, g, case, st)
+    for _ in range(2):
+        out = empty_u16((n_seq, 32, 128))
+        out.fill_(0x7FC1)
+        rc = call_static(m, g, case, out, 0)
+        assert rc == 0, m._lib.last_error()
+        torch.cuda.synchronize()
+        assert host_u16(out).tobytes() == want.tobytes()
+    assert m.device_status(0) == 0

@@ -95,6 +95,8 @@ int *status_ptr(int dev) {
 // Device address of g_static_decode_scratch, looked up once per device with
 // that device current (host code may not take the address of a __device__
 // array directly: that would be a host-side stand-in, not device memory).
+// Like g_status_ptr it is kept for the life of the process; the C ABI states
+// that the library is not used on a device after a reset of its context.
 void *g_static_scratch_ptr[kMaxDevices] = {};
 
 int static_scratch_ptr(int dev, void **ptr) {
@@ -291,6 +293,7 @@ int run_decode(const DecodeCall &c) {
     p.max_splits = (int)max_splits;
     p.page_tokens = (int)c.page_tokens;
     p.max_pages = (int)c.max_pages;
+    p.n_pages = (int)std::min<uint64_t>(c.n_pages, 0x7fffffff);
     p.n_seq = (int)c.n_seq;
     p.head_dim = (int)g->head_dim;
     p.token_cap = c.paged ? (int)std::min<uint64_t>((uint64_t)c.max_pages * c.page_tokens, 0x7fffffff)
@@ -562,6 +565,17 @@ int mslim_cuda_decode_workspace_bytes(const mslim_geometry_t *geometry, uint32_t
         return fail(MSLIM_ERR_SHAPE_MISMATCH, "split_tokens must be a multiple of 64");
     const uint64_t splits = (max_tokens + split_tokens - 1) / split_tokens;
     *bytes = partial_bytes(geometry, n_seq, 1, splits);
+    return MSLIM_OK;
+}
+
+int mslim_cuda_decode_split_tokens(const mslim_geometry_t *geometry, uint32_t n_seq,
+                                   uint32_t max_tokens, uint32_t *split_tokens) {
+    if (int rc = check_geometry(geometry)) return rc;
+    if (!split_tokens) return fail(MSLIM_ERR_SHAPE_MISMATCH, "split_tokens pointer is null");
+    if (n_seq == 0 || max_tokens == 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty batch");
+    DecodeShapeInfo sh;
+    if (int rc = decode_shape(geometry, 1, &sh)) return rc;
+    *split_tokens = policy_split_tokens((uint64_t)n_seq * geometry->kv_heads * sh.head_chunks, max_tokens);
     return MSLIM_OK;
 }
 
@@ -937,6 +951,16 @@ int mslim_cuda_argmax(const void *logits, uint32_t rows, uint32_t vocab, int tie
     cudaError_t err = mslim::launch_argmax(static_cast<const uint16_t *>(logits), rows, vocab,
                                            ties_to_last, token_ids, static_cast<cudaStream_t>(stream));
     return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "argmax launch");
+}
+
+int mslim_cuda_exp2_eval(const float *x, float *y_poly, float *y_mufu, float *y_ref, uint32_t n,
+                         void *stream) {
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    if (n == 0) return MSLIM_OK;
+    if (!x || !y_poly || !y_mufu || !y_ref) return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
+    cudaError_t err = mslim::launch_exp2_eval(x, y_poly, y_mufu, y_ref, n, static_cast<cudaStream_t>(stream));
+    return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "exp2 evaluation launch");
 }
 
 // ------------------------------------------------ tensor-parallel decode --

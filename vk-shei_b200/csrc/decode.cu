@@ -109,11 +109,21 @@ __global__ void __launch_bounds__(kThreads)
                 const int t0 = t_begin + i * kTileT;
                 uint8_t *kdst = smem + s * S::kStageBytes;
                 uint8_t *vdst = kdst + S::kTensorBytes;
-                mbar_arrive_expect_tx(&full[s], S::kStageBytes);
                 if constexpr (PAGED) {
                     const int lp = t0 / p.page_tokens;
                     const int off = t0 - lp * p.page_tokens;
                     const int phys = p.page_table[(size_t)seq * p.max_pages + lp];
+                    if (phys < 0 || phys >= p.n_pages) {
+                        // A table entry outside the pool: report it and load
+                        // nothing; the stage completes without bytes so the
+                        // consumers do not wait (the output is then undefined
+                        // and the status word says so).
+                        if (p.status) atomicExch(p.status, MSLIM_DEVICE_BAD_PAGE_CODE);
+                        mbar_arrive(&full[s]);
+                        issued = i + 1;
+                        continue;
+                    }
+                    mbar_arrive_expect_tx(&full[s], S::kStageBytes);
                     const int z = phys * p.kvheads + kvh;
 #pragma unroll
                     for (int b = 0; b < S::kBoxes; ++b) {
@@ -121,6 +131,7 @@ __global__ void __launch_bounds__(kThreads)
                         tma_load_3d(vdst + b * kBoxBytes, &vmap, &full[s], b * 64, off, z);
                     }
                 } else {
+                    mbar_arrive_expect_tx(&full[s], S::kStageBytes);
 #pragma unroll
                     for (int b = 0; b < S::kBoxes; ++b) {
                         tma_load_4d(kdst + b * kBoxBytes, &kmap, &full[s], b * 64, kvh, t0, seq);

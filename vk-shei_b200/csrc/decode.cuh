@@ -22,6 +22,8 @@ struct DecodeParams {
     int max_splits;
     int page_tokens;             // paged only, multiple of 64
     int max_pages;               // paged only
+    int n_pages;                 // paged only: pool size; table entries outside
+                                 // [0, n_pages) are reported, never loaded
     int n_seq;
     int head_dim;                // caller's head_dim (<= kernel D, multiple of 8); TMA
                                  // zero-fills K/V columns past it

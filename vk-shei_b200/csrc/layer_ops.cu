@@ -455,4 +455,22 @@ cudaError_t launch_argmax(const uint16_t *logits, uint32_t rows, uint32_t n, int
     return cudaGetLastError();
 }
 
+// ------------------------------------------------------ exp2 diagnostic --
+
+__global__ void mslim_exp2_eval(const float *x, float *y_poly, float *y_mufu, float *y_ref, uint32_t n) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const float v = x[i];
+        y_poly[i] = exp2_fma(v);
+        y_mufu[i] = fast_exp2(v);
+        y_ref[i] = exp2f(v);
+    }
+}
+
+cudaError_t launch_exp2_eval(const float *x, float *y_poly, float *y_mufu, float *y_ref, uint32_t n,
+                             cudaStream_t stream) {
+    const uint32_t blocks = (uint32_t)std::min<uint64_t>((n + 255) / 256, 148u * 8);
+    mslim_exp2_eval<<<blocks, 256, 0, stream>>>(x, y_poly, y_mufu, y_ref, n);
+    return cudaGetLastError();
+}
+
 }  // namespace mslim

@@ -44,4 +44,9 @@ cudaError_t launch_kv_canonical(const uint16_t *src, uint16_t *out, uint32_t kv_
                                 uint32_t dim, const int32_t *page_row, uint32_t page_tokens, uint32_t n_pages,
                                 int *status, cudaStream_t stream);
 
+// y_poly[i] = exp2_fma(x[i]), y_mufu[i] = fast_exp2(x[i]) (the two 2^x
+// evaluations of the prefill softmax), y_ref[i] = exp2f(x[i]).
+cudaError_t launch_exp2_eval(const float *x, float *y_poly, float *y_mufu, float *y_ref, uint32_t n,
+                             cudaStream_t stream);
+
 }  // namespace mslim

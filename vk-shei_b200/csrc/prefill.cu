@@ -6,21 +6,31 @@
 // assets/tiled_attention.cl:9-130 for queries > 1): query row i (absolute
 // position prior + i) attends to keys 0..=prior+i.
 //
-// One CTA per (128-row query tile, query head); heavy tiles (more keys)
-// launch first.  Warp roles:
-//   warps 0,10 TMA producers: the Q tile once and 128-key K tiles (warp 0),
-//              V tiles (warp 10), each through its own two-slot ring (128-byte
-//              swizzle, this GPU's HBM, no multicast); a K slot is released as
-//              soon as S_j is computed, a V slot after PV_j;
-//   warp 1     allocates 512 TMEM columns (S double buffer + O) and, from one
-//              lane, issues tcgen05.mma: S_j = Q K_j^T (K-major operands) and
-//              O_j = P_j V_j (P from shared memory, V as an MN-major operand);
-//   warps 2-9  two threads per query row (the row's TMEM lane, 64 columns
-//              each; the pair shares the row max through shared memory): read
-//              S_j once, causal mask, online softmax in exp2, P_j as bf16 into a
-//              swizzled shared tile.  O accumulates in TMEM across tiles; a row's
-//              max moves (and its O is rescaled in place) only when a tile's max
-//              exceeds it by more than 2^8.
+// Two kernels share one numeric contract (S = Q K^T and O += P V as
+// tcgen05.mma kind::f16, M 128 x N 128, fp32 accumulators in TMEM; an online
+// softmax in exp2 whose running max moves only by more than 2^8; P written
+// back into TMEM as bf16 and consumed by a TS-MMA, A from TMEM -- P never goes
+// through shared memory), so for the same inputs they return the same bits:
+//
+//   mslim_prefill_pair    even GQA groups (C2: group 4).  Persistent: one CTA
+//       per SM walks (128-row query tile, pair of query heads sharing a KV
+//       head) items, heaviest first in snake order; every staged K/V byte
+//       serves both heads.  TMEM: S_A, S_B, O_A, O_B (128 columns each).
+//       Tensor-core order per key tile: PV_A(j), S_A(j+1), PV_B(j), S_B(j+1),
+//       so one head's MMAs run while the other head's softmax works.  Warps:
+//       TMA K, MMA (one elected lane issues each group of MMAs), TMA V, TMA Q
+//       (the next item's Q is prefetched as soon as the current item's last S
+//       completes), then a softmax warpgroup per head, one thread per query
+//       row, which also rescales O in TMEM and writes the output through a
+//       swizzled staging buffer and bulk tensor stores.
+//   mslim_prefill_causal  odd groups: one head per CTA, S double-buffered in
+//       TMEM (S(j+1) issued before PV(j)), eight softmax warps taking 64 keys
+//       each and exchanging row maxima through shared memory.
+//
+// TMA loads read this GPU's HBM only (128-byte swizzle, no multicast); K and
+// V have separate rings, a K slot is released once S_j is computed, a V slot
+// after PV_j.  Consecutive calls overlap through programmatic dependent
+// launch: a call waits for its predecessor's memory before reading an input.
 // Every mbarrier wait is bounded; the CTA always frees its TMEM.
 #include <atomic>
 #include <mutex>

@@ -255,6 +255,14 @@ def decode_workspace_bytes(geometry: AttentionGeometry, n_seq: int, max_tokens: 
     return out.value
 
 
+def decode_split_tokens(geometry: AttentionGeometry, n_seq: int, max_tokens: int) -> int:
+    """The split size the library picks when split_tokens is 0."""
+    out = ctypes.c_uint32()
+    check(_lib.lib().mslim_cuda_decode_split_tokens(ctypes.byref(geometry.c()), n_seq, max_tokens,
+                                                    ctypes.byref(out)))
+    return out.value
+
+
 def decode_dense(geometry: AttentionGeometry, q, k_cache, v_cache, seq_tokens, n_seq: int,
                  max_tokens: int, workspace, out, split_tokens: int = 0, stream=None) -> None:
     """GpuEngine::attention for a batch of token-major caches."""
@@ -476,16 +484,25 @@ class TiledAttention:
 class GpuEngine:
     """The attention/prologue slice of src/gpu_llm/gpu_resources.rs::GpuEngine.
 
-    Holds its decode workspace (grown when a longer history arrives, like the
-    reference's Workspace buffers) and the installed TiledAttention plan."""
+    The decode workspace is reserved when the engine is built, for histories
+    of up to `max_tokens` tokens of `geometry` (the reference sizes its
+    Workspace buffers from the model's context capacity when it creates the
+    engine, src/gpu_llm/kernels.rs:272-293), so attention() never allocates;
+    a longer history is a ShapeMismatch.  set_attention_kernel installs a
+    TiledAttention plan, which owns its own scratch."""
 
-    def __init__(self, device: int = 0):
+    def __init__(self, device: int = 0, geometry: AttentionGeometry | None = None, max_tokens: int = 0):
         import torch
         self.device = device
         self._torch = torch
-        self._workspace = None
         self._seq = torch.zeros(1, dtype=torch.int32, device=f"cuda:{device}")
         self.tiled_attention: TiledAttention | None = None
+        self.geometry = geometry
+        self.max_tokens = max_tokens
+        self._workspace = None
+        if geometry is not None and max_tokens > 0:
+            self._workspace = torch.empty(max(decode_workspace_bytes(geometry, 1, max_tokens), 16),
+                                          dtype=torch.uint8, device=f"cuda:{device}")
 
     def set_attention_kernel(self, config: AttentionKernelConfig, geometry: AttentionGeometry,
                              allow_experimental: bool = False) -> None:
@@ -493,12 +510,6 @@ class GpuEngine:
         config.validate_activation(allow_experimental)
         self.tiled_attention = None if config.mode == AttentionKernelMode.REFERENCE else \
             TiledAttention.build(config, geometry, self.device)
-
-    def _ws(self, nbytes: int):
-        if self._workspace is None or _nbytes(self._workspace) < nbytes:
-            self._workspace = self._torch.empty(max(nbytes, 1 << 20), dtype=self._torch.uint8,
-                                                device=f"cuda:{self.device}")
-        return self._workspace
 
     def norm(self, inp, weight, output, hidden: int, eps: float, tokens: int = 1, stream=None) -> None:
         rmsnorm(inp, weight, output, tokens, hidden, eps, stream)
@@ -519,9 +530,11 @@ class GpuEngine:
         cap = _nbytes(kv[0]) // (geometry.kv_elements_per_token() * 2)
         if tokens > cap or _nbytes(kv[1]) < tokens * geometry.kv_elements_per_token() * 2:
             raise ShapeMismatch("KV cache smaller than the token count")
-        ws = self._ws(decode_workspace_bytes(geometry, 1, tokens))
+        if self._workspace is None or tokens > self.max_tokens or \
+                _nbytes(self._workspace) < decode_workspace_bytes(geometry, 1, tokens):
+            raise ShapeMismatch("history beyond the decode workspace reserved when the engine was built")
         self._seq.fill_(tokens)
-        decode_dense(geometry, query, kv[0], kv[1], self._seq, 1, tokens, ws, output, 0, stream)
+        decode_dense(geometry, query, kv[0], kv[1], self._seq, 1, tokens, self._workspace, output, 0, stream)
 
     exact_hot_fused_attention = attention
 
