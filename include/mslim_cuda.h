@@ -311,11 +311,17 @@ int mslim_cuda_residual_add(const void *a, const void *b, void *out, uint64_t n,
 int mslim_cuda_swiglu(const void *gate, const void *up, void *out, uint64_t n, void *stream);
 
 /* A projection of the decode step (GpuEngine's GEMVs, llm_gemv_bf16*,
- * assets/gpu_llm.cl:38-68, for a few sessions at once): y[m][n] =
- * bf16(sum_k x[m][k] * w[n][k]), fp32 accumulation, the weights streamed once.
- * x: bf16 [m][k], w: bf16 [n][k] (the HF [out][in] layout), y: bf16 [m][n];
- * 1 <= m <= 16, n % 8 == 0, k % 128 == 0, 16-byte aligned. */
-int mslim_cuda_gemv(const void *x, const void *w, void *y, uint32_t m, uint32_t n, uint32_t k, void *stream);
+ * assets/gpu_llm.cl:38-68, for a few sessions at once) on the tcgen05 tensor
+ * cores: y[r][n] = bf16(sum_k x[r][k] * w[n][k]) for r < m, fp32
+ * accumulation, every weight byte read once.  x: bf16 [m][k], w: bf16 [n][k]
+ * (the HF [out][in] layout), both 16-byte aligned; y: bf16 rows of ldy >= n
+ * elements; 1 <= m <= 16, k a multiple of 8.  Long K is cut into up to eight
+ * splits combined in a fixed order on the chip (no workspace), so repeated
+ * calls return the same bits.  The kernel starts streaming w before the
+ * preceding kernel in the stream has finished (programmatic dependent
+ * launch): w must not be written by that kernel. */
+int mslim_cuda_gemv(const void *x, const void *w, void *y, uint32_t m, uint32_t n, uint32_t k, uint32_t ldy,
+                    void *stream);
 
 /* SwiGLU over a fused gate|up projection (no reference counterpart: the
  * reference keeps gate and up in separate buffers, GpuEngine::swiglu):

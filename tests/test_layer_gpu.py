@@ -306,17 +306,48 @@ def test_rope_append_vector_and_scalar_forms_agree(paged, qh, kvh, d):
 
 
 @pytest.mark.parametrize("m,n,k", [(8, 6144, 4096), (8, 4096, 512), (8, 28672, 4096), (8, 4096, 14336),
-                                   (3, 1024, 1792), (16, 520, 256), (1, 8, 128)])
+                                   (8, 16032, 4096), (8, 768, 4096), (3, 1024, 1792), (16, 520, 256),
+                                   (1, 8, 128), (5, 200, 72)])
 def test_gemv_matches_fp32_reference(m, n, k):
+    """The tcgen05 projection against a float64 product of the same bf16
+    values: one bf16 rounding of an fp32 sum, and the same bits on a second
+    call (fixed split order)."""
     import torch
     import mslim_b200 as mm
     rng = np.random.default_rng(m * 7 + n + k)
     x = _rand_bf16(rng, m * k).reshape(m, k)
     w = _rand_bf16(rng, n * k, 0.02).reshape(n, k)
-    y = torch.empty((m, n), dtype=torch.int16, device="cuda:0")
-    mm.gemv(dev(x), dev(w), y, m, n, k)
+    y = torch.full((m, n), 0x7FC1, dtype=torch.int16, device="cuda:0")
+    xd, wd = dev(x), dev(w)
+    mm.gemv(xd, wd, y, m, n, k)
     ref = bf16_f32(x).astype(np.float64) @ bf16_f32(w).astype(np.float64).T
     got = bf16_f32(u16(y))
-    # one bf16 rounding of an fp32 sum: within ~1 ulp of the exact value
     tol = np.abs(ref) * 2.0 ** -7 + 1e-6 * np.sqrt(k)
     assert (np.abs(got - ref) <= tol).all(), np.abs(got - ref).max()
+    y2 = torch.empty_like(y)
+    mm.gemv(xd, wd, y2, m, n, k)
+    assert torch.equal(y, y2)
+    assert mm.device_status(0) == 0
+
+
+def test_gemv_writes_strided_rows_and_rejects_bad_arguments():
+    """ldy > n writes into a wider row (e.g. one slice of a fused output) and
+    leaves the rest untouched; bad shapes are refused before any launch."""
+    import torch
+    import mslim_b200 as mm
+    rng = np.random.default_rng(5)
+    m, n, k, ldy = 4, 256, 4096, 384
+    x = _rand_bf16(rng, m * k).reshape(m, k)
+    w = _rand_bf16(rng, n * k, 0.02).reshape(n, k)
+    y = torch.full((m, ldy), 0x1234, dtype=torch.int16, device="cuda:0")
+    mm.gemv(dev(x), dev(w), y, m, n, k, ldy=ldy)
+    dense = torch.empty((m, n), dtype=torch.int16, device="cuda:0")
+    mm.gemv(dev(x), dev(w), dense, m, n, k)
+    got = u16(y)
+    assert np.array_equal(got[:, :n], u16(dense)) and (got[:, n:] == 0x1234).all()
+    with pytest.raises(mm.ShapeMismatch):
+        mm.gemv(dev(x), dev(w), dense, 17, n, k)
+    with pytest.raises(mm.ShapeMismatch):
+        mm.gemv(dev(x), dev(w), dense, m, n, 100)
+    with pytest.raises(mm.ShapeMismatch):
+        mm.gemv(dev(x), dev(w), dense, m, n, k, ldy=n - 1)

@@ -20,11 +20,11 @@ def _u16(t):
     return host_u16(t.contiguous().view(torch.int16))
 
 
-def _run(kv_mode):
+def _run(kv_mode, decode_gemm="cublas"):
     import torch
     from mslim_b200 import model as mdl
     spec = mdl.ModelSpec(layers=LAYERS)
-    M = mdl.DeviceModel(spec, BATCH, PROMPT + STEPS + 1, seed=7, kv_mode=kv_mode)
+    M = mdl.DeviceModel(spec, BATCH, PROMPT + STEPS + 1, seed=7, kv_mode=kv_mode, decode_gemm=decode_gemm)
     ids = torch.from_numpy(np.random.default_rng(7).integers(0, spec.vocab, size=(BATCH, PROMPT))).cuda()
     tok, logits = M.prefill(ids)
     toks, lgs = [tok.cpu().numpy()], [_u16(logits)]
@@ -43,14 +43,27 @@ def runs():
     return dense, cold
 
 
+@pytest.fixture(scope="module")
+def runs_own_gemv():
+    """The same model with the decode projections on mslim_cuda_gemv."""
+    return _run("dense", "own"), _run("coldstore", "own")
+
+
 def test_model_dense_and_coldstore_agree_bitwise(runs):
     (_, _, _, t_d, l_d), (_, _, _, t_c, l_c) = runs
     assert np.array_equal(t_d, t_c)
     assert np.array_equal(l_d, l_c)
 
 
-def test_model_greedy_tokens_match_cpu_path(runs, oracle):
-    M, spec, prompts, toks, logits = runs[0]
+def test_model_own_gemv_dense_and_coldstore_agree_bitwise(runs_own_gemv):
+    (_, _, _, t_d, l_d), (_, _, _, t_c, l_c) = runs_own_gemv
+    assert np.array_equal(t_d, t_c)
+    assert np.array_equal(l_d, l_c)
+
+
+@pytest.mark.parametrize("gemm", ["cublas", "own"])
+def test_model_greedy_tokens_match_cpu_path(runs, runs_own_gemv, oracle, gemm):
+    M, spec, prompts, toks, logits = (runs if gemm == "cublas" else runs_own_gemv)[0]
     L = spec.layer
     D, qd, kd, inter = L.head_dim, L.q_dim, L.kv_dim, L.intermediate
     layers = []

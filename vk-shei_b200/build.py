@@ -20,7 +20,7 @@ CSRC = os.path.join(HERE, "csrc")
 OUT_DIR = os.path.join(HERE, "mslim_b200")
 OBJ_DIR = os.path.join(HERE, "_build")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
-SOURCES = ["capi.cu", "decode.cu", "prologue.cu", "prefill.cu", "layer_ops.cu", "tp_allreduce.cu"]
+SOURCES = ["capi.cu", "decode.cu", "prologue.cu", "prefill.cu", "layer_ops.cu", "tp_allreduce.cu", "gemv.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 HOST_CXX = "/usr/bin/g++" if os.path.exists("/usr/bin/g++") else "g++"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -23,6 +23,7 @@
 #include "decode.cuh"
 #include "prefill.cuh"
 #include "layer_ops.cuh"
+#include "gemv.cuh"
 #include "tp_allreduce.cuh"
 #include "prologue.cuh"
 
@@ -911,18 +912,31 @@ int mslim_cuda_kv_canonical_paged(const void *pool, uint32_t n_pages, uint32_t k
     return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "canonical KV launch");
 }
 
-int mslim_cuda_gemv(const void *x, const void *w, void *y, uint32_t m, uint32_t n, uint32_t k, void *stream) {
+int mslim_cuda_gemv(const void *x, const void *w, void *y, uint32_t m, uint32_t n, uint32_t k, uint32_t ldy,
+                    void *stream) {
     int dev;
     if (int rc = current_device(&dev)) return rc;
     if (!x || !w || !y) return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
     if (m == 0 || m > 16) return fail(MSLIM_ERR_SHAPE_MISMATCH, "the decode projection takes 1..16 rows");
-    if (n == 0 || n % 8 != 0 || k == 0 || k % 128 != 0)
-        return fail(MSLIM_ERR_SHAPE_MISMATCH, "n must be a multiple of 8 and k of 128");
-    if (!aligned(x, 16) || !aligned(w, 16) || !aligned(y, 16))
-        return fail(MSLIM_ERR_SHAPE_MISMATCH, "projection buffers must be 16-byte aligned");
+    if (n == 0 || k == 0 || k % 8 != 0)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "n must be positive and k a positive multiple of 8");
+    if (n > 0x7fffff80u || k > 0x7fffffc0u) return fail(MSLIM_ERR_SHAPE_MISMATCH, "projection too large");
+    if (ldy < n) return fail(MSLIM_ERR_SHAPE_MISMATCH, "ldy must be at least n");
+    if (!aligned(x, 16) || !aligned(w, 16) || !aligned(y, 2))
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "x and w must be 16-byte aligned");
     if (y == x || y == w) return fail(MSLIM_ERR_SHAPE_MISMATCH, "the output must not alias an input");
-    cudaError_t err = mslim::launch_gemv(static_cast<const uint16_t *>(x), static_cast<const uint16_t *>(w),
-                                         static_cast<uint16_t *>(y), m, n, k, static_cast<cudaStream_t>(stream));
+    const mslim::GemvPlan plan = mslim::gemv_plan(m, n, k);
+    CUtensorMap xmap, wmap;
+    {
+        const uint64_t xd[2] = {k, m}, xs[1] = {(uint64_t)k * 2};
+        const uint32_t xbox[2] = {64, 16};
+        const uint64_t wd[2] = {k, n}, ws[1] = {(uint64_t)k * 2};
+        const uint32_t wbox[2] = {64, 128};
+        if (int rc = make_tmap(&xmap, x, 2, xd, xs, xbox)) return rc;
+        if (int rc = make_tmap(&wmap, w, 2, wd, ws, wbox)) return rc;
+    }
+    cudaError_t err = mslim::launch_gemv_tc(xmap, wmap, plan, m, n, static_cast<uint16_t *>(y), ldy,
+                                            status_ptr(dev), static_cast<cudaStream_t>(stream));
     return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "projection launch");
 }
 

@@ -12,7 +12,10 @@
 //                       warps each own 16 tokens of every tile.  Rows of the
 //                       MMA are the (query, head) pairs that share the KV
 //                       head, so K/V bytes are read once per group.
-//   mslim_decode_merge  fixed split-order combine of {m, l, acc[D]} partials.
+//   mslim_decode_merge_row / mslim_decode_merge  fixed split-order combine of
+//                       {m, l, acc[D]} partials (one CTA per row with every
+//                       partial requested at once, up to 64 splits; one warp
+//                       per row in batches of eight splits beyond that).
 //
 // Numeric contract (same code for dense and paged K/V, so the two layouts are
 // bit-identical by construction, and run-to-run deterministic):
@@ -374,7 +377,71 @@ __global__ void __launch_bounds__(kThreads)
     }
 }
 
-// One warp per (sequence, query row, query head): fixed split-order combine.
+// Splits whose partials feed (sequence, query row qg): the same count the
+// split kernel's grid produced for the row's query block.
+__device__ __forceinline__ int merge_splits(const DecodeParams &p, int seq, int qg) {
+    const int ntok = min(p.token_cap, p.fixed_tokens >= 0 ? p.fixed_tokens : p.seq_tokens[seq]);
+    const int prior = ntok - p.nq;
+    const int qblock = qg / p.q_per_cta;
+    const int qg_last = min(p.nq, (qblock + 1) * p.q_per_cta) - 1;
+    const int cta_end = prior + qg_last + 1;
+    return (ntok <= 0 || cta_end <= 0) ? 0
+                                       : min((int)p.max_splits, (cta_end + p.split_tokens - 1) / p.split_tokens);
+}
+
+// One CTA per (sequence, query row, query head), thread d = output dim d, for
+// rows of at most MAXS splits: every partial of the row is requested at once
+// (the split maxima and sums through shared memory, thread d's acc[d] of
+// every split in registers), so the combine costs one memory round trip
+// instead of one per batch of splits.  Same arithmetic and order as
+// mslim_decode_merge: m = max_s m_s, w_s = 2^(m_s - m), l and acc summed in
+// split order, out = bf16(acc * (1 / l)).
+template <int D, int MAXS>
+__global__ void __launch_bounds__(D) mslim_decode_merge_row(const DecodeParams p, uint16_t *out) {
+    griddep_launch_dependents();
+    griddep_wait();  // the split kernel's partials
+    __shared__ float ms[MAXS], ls[MAXS];
+    const size_t item = blockIdx.x;
+    const size_t sq = item / p.qheads;  // seq * nq + qg
+    const int qg = (int)(sq % p.nq);
+    const int seq = (int)(sq / p.nq);
+    constexpr int kRowF = D + 2;
+    const int splits = merge_splits(p, seq, qg);
+    const float *src = p.partials + item * p.max_splits * kRowF;
+    const int d = threadIdx.x;
+    float av[MAXS];
+#pragma unroll
+    for (int s = 0; s < MAXS; ++s) av[s] = (s < splits) ? src[s * kRowF + d] : 0.f;
+    for (int s = d; s < splits; s += D) {
+        ms[s] = src[s * kRowF + D];
+        ls[s] = src[s * kRowF + D + 1];
+    }
+    __syncthreads();
+    float m = -INFINITY;
+#pragma unroll
+    for (int s = 0; s < MAXS; ++s)
+        if (s < splits) m = fmaxf(m, ms[s]);
+    const float mb = (m == -INFINITY) ? 0.f : m;
+    float l = 0.f, acc = 0.f;
+#pragma unroll
+    for (int s = 0; s < MAXS; ++s) {
+        if (s < splits) {
+            const float w = fast_exp2(ms[s] - mb);
+            l += w * ls[s];
+            acc += w * av[s];
+        }
+    }
+    const float inv = (l > 0.f) ? 1.0f / l : 0.f;
+    if (d < p.head_dim) {
+        if (p.out_f32)
+            p.out_f32[item * p.head_dim + d] = acc * inv;
+        else
+            out[item * p.head_dim + d] = bf16_bits_rn(acc * inv);
+    }
+}
+
+// One warp per (sequence, query row, query head): fixed split-order combine
+// for rows of any number of splits.
 template <int D>
 __global__ void __launch_bounds__(128) mslim_decode_merge(const DecodeParams p, uint16_t *out) {
     griddep_launch_dependents();
@@ -388,14 +455,7 @@ __global__ void __launch_bounds__(128) mslim_decode_merge(const DecodeParams p, 
     const int seq = (int)(sq / p.nq);
     constexpr int kRowF = D + 2;
     constexpr int kPer = D / 32;
-    const int ntok = min(p.token_cap, p.fixed_tokens >= 0 ? p.fixed_tokens : p.seq_tokens[seq]);
-    const int prior = ntok - p.nq;
-    const int qblock = qg / p.q_per_cta;
-    const int qg_last = min(p.nq, (qblock + 1) * p.q_per_cta) - 1;
-    const int cta_end = prior + qg_last + 1;
-    const int splits = (ntok <= 0 || cta_end <= 0)
-                           ? 0
-                           : min((int)p.max_splits, (cta_end + p.split_tokens - 1) / p.split_tokens);
+    const int splits = merge_splits(p, seq, qg);
     const float *src = p.partials + item * p.max_splits * kRowF;
     // the maximum over the splits: lane s reads split s (32 per round), then a
     // warp max (exact, so the order does not matter)
@@ -463,6 +523,13 @@ cudaError_t launch_impl(const CUtensorMap &kmap, const CUtensorMap &vmap, const 
     err = launch_pdl(kernel, grid, dim3(kThreads), smem, stream, kmap, vmap, p);
     if (err != cudaSuccess) return err;
     const size_t items = (size_t)p.n_seq * p.nq * p.qheads;
+    if (items <= 0x7fffffffull) {
+        const dim3 rows((unsigned)items);
+        if (p.max_splits <= 8) return launch_pdl(mslim_decode_merge_row<D, 8>, rows, dim3(D), 0, stream, p, out);
+        if (p.max_splits <= 16) return launch_pdl(mslim_decode_merge_row<D, 16>, rows, dim3(D), 0, stream, p, out);
+        if (p.max_splits <= 32) return launch_pdl(mslim_decode_merge_row<D, 32>, rows, dim3(D), 0, stream, p, out);
+        if (p.max_splits <= 64) return launch_pdl(mslim_decode_merge_row<D, 64>, rows, dim3(D), 0, stream, p, out);
+    }
     return launch_pdl(mslim_decode_merge<D>, dim3((unsigned)((items + 3) / 4)), dim3(128), 0, stream, p, out);
 }
 

@@ -1,0 +1,274 @@
+// gemv.cu -- the decode step's projections (a few rows against a weight
+// matrix) on the tcgen05 tensor cores.
+//
+// Replaces the reference's decode GEMVs (llm_gemv_bf16*, assets/gpu_llm.cl:
+// 38-68, and the prefill-reuse forms of :553-733) for 1..16 activation rows:
+// Y[m][n] = bf16(sum_k X[m][k] * W[n][k]), W in the [out][in] layout.
+//
+// The weight matrix is the A operand ("swap AB"): a CTA owns 128 output
+// features, which are the 128 rows of one tcgen05.mma (kind::f16, M 128), and
+// the activation rows are its N = 16 columns (rows past m are TMA zero fill).
+// Every weight byte is read from HBM exactly once; the few activation rows
+// are re-read per CTA from L2.  Warp roles, 128 threads:
+//   warp 0  one lane issues TMA loads of [128 x 64] weight boxes and [16 x 64]
+//           activation boxes (128-byte swizzle, this GPU's HBM, no multicast)
+//           into a four-stage mbarrier ring.  The weights do not depend on
+//           the preceding kernel, so the first four weight boxes are issued
+//           before griddepcontrol.wait (programmatic dependent launch) and
+//           stream while the predecessor finishes; the activations follow it;
+//   warp 1  allocates 32 TMEM columns and, from one elected lane, issues four
+//           K=16 MMAs per stage into the 128 x 16 fp32 accumulator, each
+//           stage's commit releasing its ring slot;
+//   all     read the accumulator with tcgen05.ld (thread t = output feature
+//           t of the tile) and write bf16 rows.
+// Long K is cut into up to eight splits so that about three CTAs per SM
+// stream at once.  The splits of one tile form a thread-block cluster: each
+// CTA leaves its fp32 partial in its own shared memory, and after a cluster
+// barrier the first CTA of the cluster reads them over distributed shared
+// memory, adds them in split order and rounds once, so the result does not
+// depend on which CTA finished first, and nothing goes through global
+// memory (no workspace).
+#include "gemv.cuh"
+
+namespace mslim {
+
+namespace {
+
+constexpr int kStages = 4;
+constexpr int kWBytes = 128 * 128;              // [128 rows][64 bf16] swizzled: 16 KB
+constexpr int kXBytes = 16 * 128;               // [16 rows][64 bf16]: 2 KB
+constexpr int kStageBytes = kWBytes + kXBytes;  // 18 KB, a multiple of 1024
+constexpr int kThreads = 128;
+constexpr uint32_t kTmemCols = 32;
+constexpr uint32_t kCtasPerSm = 3;
+constexpr uint32_t kMinKTiles = 4;  // 64-wide K steps per CTA at least
+constexpr uint32_t kMaxSplits = 8;  // portable cluster size
+// kind::f16 instruction descriptor: D f32, A = W and B = X bf16, both
+// K-major, N = 16, M = 128.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((16u >> 3) << 17) | ((128u >> 4) << 24);
+
+struct GemvParams {
+    uint32_t m, n, ldy;
+    uint32_t k_steps, k_tiles, splits;
+    uint16_t *y;
+    int *status;
+};
+
+struct Bars {
+    uint64_t full[kStages];
+    uint64_t empty[kStages];
+    uint64_t acc;
+    uint32_t tmem_base;
+};
+
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// f32 at shared-memory address `saddr` of CTA `rank` of this cluster.
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t saddr, uint32_t rank) {
+    uint32_t remote;
+    float v;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(saddr), "r"(rank));
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int32_t x,
+                                            int32_t y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+
+// 16 consecutive fp32 columns of this thread's TMEM lane (wait in the same
+// asm block, so no use of the registers is scheduled before the load lands).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15}, [%16];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__global__ void __launch_bounds__(kThreads)
+    mslim_gemv_tc(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
+                  const GemvParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Bars *bars = reinterpret_cast<Bars *>(smem + kStages * kStageBytes);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t tile = blockIdx.x, split = blockIdx.y;
+    const uint32_t ks0 = split * p.k_tiles;
+    const int nk = (int)min(p.k_tiles, p.k_steps - ks0);  // >= 1 by the plan
+
+    griddep_launch_dependents();
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&bars->full[s], 1);
+            mbar_init(&bars->empty[s], 1);
+        }
+        mbar_init(&bars->acc, 1);
+        fence_mbarrier_init();
+    }
+    if (warp == 1) tmem_alloc(&bars->tmem_base, kTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            prefetch_tmap(&wmap);
+            prefetch_tmap(&xmap);
+            const int pre = min(kStages, nk);
+            const int32_t n0 = (int32_t)(tile * 128);
+            for (int i = 0; i < pre; ++i) {
+                mbar_arrive_expect_tx(&bars->full[i], kStageBytes);
+                tma_load_2d(smem + i * kStageBytes, &wmap, &bars->full[i], (int32_t)((ks0 + i) * 64), n0);
+            }
+            griddep_wait();  // the activation rows come from the preceding kernel
+            for (int i = 0; i < pre; ++i)
+                tma_load_2d(smem + i * kStageBytes + kWBytes, &xmap, &bars->full[i], (int32_t)((ks0 + i) * 64), 0);
+            int issued = pre;
+            for (int i = pre; i < nk; ++i) {
+                const int s = i % kStages;
+                if (!mbar_wait(&bars->empty[s], ((i / kStages) & 1) ^ 1, p.status, 21)) break;
+                uint8_t *dst = smem + s * kStageBytes;
+                const int32_t kx = (int32_t)((ks0 + i) * 64);
+                mbar_arrive_expect_tx(&bars->full[s], kStageBytes);
+                tma_load_2d(dst, &wmap, &bars->full[s], kx, n0);
+                tma_load_2d(dst + kWBytes, &xmap, &bars->full[s], kx, 0);
+                issued = i + 1;
+            }
+            // the copies still in flight land before the CTA may retire
+            for (int i = max(0, issued - kStages); i < issued; ++i)
+                mbar_wait(&bars->full[i % kStages], (i / kStages) & 1, p.status, 22);
+        }
+    } else if (warp == 1) {
+        for (int i = 0; i < nk; ++i) {
+            const int s = i % kStages;
+            if (!mbar_wait(&bars->full[s], (i / kStages) & 1, p.status, 23)) break;
+            tc_fence_after();
+            const uint32_t wa = smem_u32(smem + s * kStageBytes);
+            umma_bf16_ss_k64(tmem, umma_desc_sw128(wa, 16, 1024), umma_desc_sw128(wa + kWBytes, 16, 1024),
+                             kIdesc, i > 0 ? 1u : 0u);
+            umma_commit(&bars->empty[s]);
+        }
+        umma_commit(&bars->acc);
+    }
+
+    // ---- epilogue: thread t holds output feature tile*128 + t, rows 0..15 ----
+    __syncwarp();  // warp 0's producer lane rejoins before the warp-wide loads
+    mbar_wait(&bars->acc, 0, p.status, 24);
+    tc_fence_after();
+    float acc[16];
+    tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16), acc);
+    griddep_wait();  // outputs are written only once the predecessor is done
+    const uint32_t n = tile * 128 + threadIdx.x;
+    const uint32_t M = p.m;
+    if (p.splits == 1) {
+        if (n < p.n) {
+#pragma unroll
+            for (uint32_t r = 0; r < 16; ++r)
+                if (r < M) p.y[(size_t)r * p.ldy + n] = bf16_bits_rn(acc[r]);
+        }
+    } else {
+        // the ring is idle (every stage was consumed by an MMA that has
+        // completed): this CTA's partial goes to red[r][t] at its start
+        float *red = reinterpret_cast<float *>(smem);
+#pragma unroll
+        for (uint32_t r = 0; r < 16; ++r)
+            if (r < M) red[r * 128 + threadIdx.x] = acc[r];
+        cluster_sync();  // every split's partial is in place
+        if (cluster_ctarank() == 0) {
+            const uint32_t base = smem_u32(red) + threadIdx.x * 4;
+            float sum[16];
+#pragma unroll
+            for (uint32_t r = 0; r < 16; ++r) sum[r] = acc[r];
+            for (uint32_t s = 1; s < p.splits; ++s) {
+                float v[16];
+#pragma unroll
+                for (uint32_t r = 0; r < 16; ++r)
+                    if (r < M) v[r] = ld_dsmem_f32(base + r * 512, s);
+#pragma unroll
+                for (uint32_t r = 0; r < 16; ++r)
+                    if (r < M) sum[r] += v[r];
+            }
+            if (n < p.n) {
+#pragma unroll
+                for (uint32_t r = 0; r < 16; ++r)
+                    if (r < M) p.y[(size_t)r * p.ldy + n] = bf16_bits_rn(sum[r]);
+            }
+        }
+        cluster_sync();  // no CTA leaves while its partial may still be read
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+}
+
+}  // namespace
+
+GemvPlan gemv_plan(uint32_t m, uint32_t n, uint32_t k) {
+    (void)m;
+    GemvPlan pl{};
+    pl.n_tiles = (n + 127) / 128;
+    pl.k_steps = (k + 63) / 64;
+    const uint64_t total = (uint64_t)pl.n_tiles * pl.k_steps;
+    const uint64_t target = 148ull * kCtasPerSm;
+    uint64_t kt = std::max<uint64_t>(kMinKTiles, (total + target - 1) / target);
+    kt = std::min<uint64_t>(kt, pl.k_steps);
+    pl.splits = (uint32_t)std::min<uint64_t>(kMaxSplits, (pl.k_steps + kt - 1) / kt);
+    pl.k_tiles = (pl.k_steps + pl.splits - 1) / pl.splits;
+    pl.splits = (pl.k_steps + pl.k_tiles - 1) / pl.k_tiles;  // no empty split
+    return pl;
+}
+
+cudaError_t launch_gemv_tc(const CUtensorMap &xmap, const CUtensorMap &wmap, const GemvPlan &plan, uint32_t m,
+                           uint32_t n, uint16_t *y, uint32_t ldy, int *status, cudaStream_t stream) {
+    GemvParams p{};
+    p.m = m;
+    p.n = n;
+    p.ldy = ldy;
+    p.k_steps = plan.k_steps;
+    p.k_tiles = plan.k_tiles;
+    p.splits = plan.splits;
+    p.y = y;
+    p.status = status;
+    const size_t smem = (size_t)kStages * kStageBytes + sizeof(Bars) + 1024;
+    cudaError_t err = cudaFuncSetAttribute(mslim_gemv_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (err != cudaSuccess) return err;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(plan.n_tiles, plan.splits);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = plan.splits;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, mslim_gemv_tc, xmap, wmap, p);
+}
+
+}  // namespace mslim

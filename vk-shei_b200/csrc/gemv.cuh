@@ -1,0 +1,27 @@
+// gemv.cuh -- the decode-step projections on the 5th-generation tensor cores.
+#pragma once
+
+#include "mslim_common.cuh"
+
+namespace mslim {
+
+// How one projection is cut into CTAs: 128 output features (weight rows) per
+// tile, the K dimension in `splits` (<= 8, one cluster) chunks of `k_tiles`
+// 64-wide steps.
+struct GemvPlan {
+    uint32_t n_tiles;  // ceil(n / 128)
+    uint32_t k_steps;  // ceil(k / 64)
+    uint32_t k_tiles;  // 64-wide K steps per split
+    uint32_t splits;   // K chunks = CTAs per cluster
+};
+
+GemvPlan gemv_plan(uint32_t m, uint32_t n, uint32_t k);
+
+// Y[m][n] (row stride ldy elements) = bf16(sum_k X[m][k] * W[n][k]), fp32
+// accumulation in TMEM, the splits combined in order over distributed shared
+// memory.  xmap: 2-D bf16 map over X (K, m) with a 64 x 16 box; wmap: over W
+// (K, n) with a 64 x 128 box; both 128-byte swizzle.
+cudaError_t launch_gemv_tc(const CUtensorMap &xmap, const CUtensorMap &wmap, const GemvPlan &plan, uint32_t m,
+                           uint32_t n, uint16_t *y, uint32_t ldy, int *status, cudaStream_t stream);
+
+}  // namespace mslim

@@ -92,81 +92,6 @@ __global__ void __launch_bounds__(kEltThreads)
     }
 }
 
-// ------------------------------------------------------------------ gemv --
-// Y[m][n] = bf16(sum_k X[m][k] * W[n][k]) for the decode step's few rows
-// (m < 16): the projection as a weight stream.  mma.sync m16n8k16 (bf16, fp32
-// accumulate) with the rows as M (padded to 16) and 8 output columns as N.
-// Inside every 32-wide K chunk, lane (g, t) loads W[n0 + g][k + 8t .. 8t + 7]
-// and X[g][k + 8t .. 8t + 7] (and X[g + 8][..]) as one 16-byte vector each and
-// feeds them as two k16 steps; the k order inside the chunk is permuted
-// identically for A and B, so the products and the set of sums are unchanged.
-// A CTA has four warps: KSPLIT warps share 8 output columns and split K
-// (partials combined in shared memory), 4 / KSPLIT column groups per CTA.
-constexpr int kGemvThreads = 128;
-
-template <int KSPLIT>
-__global__ void __launch_bounds__(kGemvThreads)
-    mslim_gemv(const uint16_t *__restrict__ x, const uint16_t *__restrict__ w, uint16_t *__restrict__ y,
-               uint32_t m, uint32_t n, uint32_t k) {
-    constexpr int kGroups = 4 / KSPLIT;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int grp = warp / KSPLIT, part = warp % KSPLIT;
-    const uint32_t n0 = (blockIdx.x * kGroups + grp) * 8;
-    const int g = lane >> 2, t = lane & 3;
-    const uint32_t kpart = k / KSPLIT;
-    const uint32_t kb = part * kpart, ke = kb + kpart;
-    const bool row_lo = (uint32_t)g < m, row_hi = (uint32_t)(g + 8) < m;
-    const uint16_t *wr = w + (size_t)(n0 + g) * k + 8 * t;
-    const uint16_t *x_lo = x + (size_t)g * k + 8 * t;
-    const uint16_t *x_hi = x + (size_t)(g + 8) * k + 8 * t;
-    float c[4] = {0.f, 0.f, 0.f, 0.f};
-    const uint4 zero = make_uint4(0, 0, 0, 0);
-    constexpr int U = 4;  // chunks with loads in flight together
-    uint32_t kk = kb;
-    for (; kk + 32 * U <= ke; kk += 32 * U) {
-        uint4 bw[U], al[U], ah[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            bw[u] = __ldg(reinterpret_cast<const uint4 *>(wr + kk + 32 * u));
-            al[u] = row_lo ? __ldg(reinterpret_cast<const uint4 *>(x_lo + kk + 32 * u)) : zero;
-            ah[u] = row_hi ? __ldg(reinterpret_cast<const uint4 *>(x_hi + kk + 32 * u)) : zero;
-        }
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const uint32_t a0[4] = {al[u].x, ah[u].x, al[u].y, ah[u].y};
-            mma_bf16_16816(c, a0, bw[u].x, bw[u].y);
-            const uint32_t a1[4] = {al[u].z, ah[u].z, al[u].w, ah[u].w};
-            mma_bf16_16816(c, a1, bw[u].z, bw[u].w);
-        }
-    }
-    for (; kk < ke; kk += 32) {
-        const uint4 bw = __ldg(reinterpret_cast<const uint4 *>(wr + kk));
-        const uint4 al = row_lo ? __ldg(reinterpret_cast<const uint4 *>(x_lo + kk)) : zero;
-        const uint4 ah = row_hi ? __ldg(reinterpret_cast<const uint4 *>(x_hi + kk)) : zero;
-        const uint32_t a0[4] = {al.x, ah.x, al.y, ah.y};
-        mma_bf16_16816(c, a0, bw.x, bw.y);
-        const uint32_t a1[4] = {al.z, ah.z, al.w, ah.w};
-        mma_bf16_16816(c, a1, bw.z, bw.w);
-    }
-    if (KSPLIT > 1) {
-        // fixed order over the K parts: part 0 + part 1 (+ 2 + 3)
-        __shared__ float red[4][32][4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) red[warp][lane][i] = c[i];
-        __syncthreads();
-        if (part != 0) return;
-#pragma unroll
-        for (int q = 1; q < KSPLIT; ++q)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) c[i] += red[warp + q][lane][i];
-    }
-    // C fragment: c0, c1 row g, columns 2t, 2t+1; c2, c3 row g + 8
-    if (row_lo)
-        *reinterpret_cast<uint32_t *>(y + (size_t)g * n + n0 + 2 * t) = pack_bf16x2(c[0], c[1]);
-    if (row_hi)
-        *reinterpret_cast<uint32_t *>(y + (size_t)(g + 8) * n + n0 + 2 * t) = pack_bf16x2(c[2], c[3]);
-}
-
 // ------------------------------------------------------------ page seal --
 // Per-token FNV-1a 64 of ColdStore pages straight from the device page pool
 // (src/cold_store.rs:725-742 token_hashes over a record payload): token t's
@@ -423,19 +348,6 @@ cudaError_t launch_swiglu(const uint16_t *gate, const uint16_t *up, uint16_t *ou
 cudaError_t launch_swiglu_rows(const uint16_t *gate_up, uint16_t *out, uint32_t rows, uint32_t width,
                                cudaStream_t stream) {
     mslim_swiglu_rows<<<elt_grid((uint64_t)rows * width), kEltThreads, 0, stream>>>(gate_up, out, rows, width);
-    return cudaGetLastError();
-}
-
-cudaError_t launch_gemv(const uint16_t *x, const uint16_t *w, uint16_t *y, uint32_t m, uint32_t n, uint32_t k,
-                        cudaStream_t stream) {
-    // about four waves of CTAs: 32 columns per CTA when N allows, else split K
-    const uint32_t want = 148u * 4;
-    if (n / 32 >= want && n % 32 == 0 && k % 32 == 0)
-        mslim_gemv<1><<<n / 32, kGemvThreads, 0, stream>>>(x, w, y, m, n, k);
-    else if (n / 16 >= want && n % 16 == 0 && k % 64 == 0)
-        mslim_gemv<2><<<n / 16, kGemvThreads, 0, stream>>>(x, w, y, m, n, k);
-    else
-        mslim_gemv<4><<<n / 8, kGemvThreads, 0, stream>>>(x, w, y, m, n, k);
     return cudaGetLastError();
 }
 

@@ -13,10 +13,6 @@ cudaError_t launch_swiglu(const uint16_t *gate, const uint16_t *up, uint16_t *ou
 // gate_up: [rows][gate (width) | up (width)] -> out [rows][width]; width % 8 == 0.
 cudaError_t launch_swiglu_rows(const uint16_t *gate_up, uint16_t *out, uint32_t rows, uint32_t width,
                                cudaStream_t stream);
-// Y[m][n] = X[m][k] . W[n][k]^T, bf16 in and out, fp32 accumulation, for
-// m <= 16 rows; n % 8 == 0, k % 128 == 0, 16-byte aligned rows.
-cudaError_t launch_gemv(const uint16_t *x, const uint16_t *w, uint16_t *y, uint32_t m, uint32_t n, uint32_t k,
-                        cudaStream_t stream);
 // hashes[p][t] = FNV-1a 64 of token t (t < tokens) of pool page page_ids[p]
 // over its heads in order; pool: bf16 [n_pool_pages][kv_heads][page_tokens][head_dim].
 cudaError_t launch_page_token_hashes(const uint16_t *pool, uint32_t n_pool_pages, uint32_t kv_heads,

@@ -363,9 +363,10 @@ def kv_canonical_paged(pool, n_pages: int, kv_heads: int, page_tokens: int, head
                                                    _ptr(page_row), max_pages, tokens, _ptr(out), _stream(stream)))
 
 
-def gemv(x, w, y, m: int, n: int, k: int, stream=None) -> None:
-    """y[m][n] = bf16(x[m][k] . w[n][k]) for 1..16 rows (the decode projections)."""
-    check(_lib.lib().mslim_cuda_gemv(_ptr(x), _ptr(w), _ptr(y), m, n, k, _stream(stream)))
+def gemv(x, w, y, m: int, n: int, k: int, ldy: int = 0, stream=None) -> None:
+    """y[m][n] = bf16(x[m][k] . w[n][k]) for 1..16 rows (the decode
+    projections) on the tensor cores; ldy: y's row stride (default n)."""
+    check(_lib.lib().mslim_cuda_gemv(_ptr(x), _ptr(w), _ptr(y), m, n, k, ldy or n, _stream(stream)))
 
 
 def swiglu_rows(gate_up, out, rows: int, width: int, stream=None) -> None:

@@ -205,13 +205,13 @@ class DeviceModel:
         return out
 
     def _gemm(self, x, w, out=None):
-        """x @ w^T through cuBLAS, or, with decode_gemm="own", the decode
-        step's few rows through mslim_cuda_gemv (measured slower than cuBLAS
-        at these shapes; the option serves hosts without cuBLAS)."""
+        """x @ w^T: the decode step's few rows (decode_gemm="own") through
+        mslim_cuda_gemv, the tcgen05 weight-streaming projection; prefill rows
+        (and decode_gemm="cublas") through cuBLAS."""
         t = self.torch
         rows, (n, k) = x.shape[0], w.shape
         with self._sec("gemm"):
-            if self.decode_gemm == "own" and rows <= 16 and n % 8 == 0 and k % 128 == 0:
+            if self.decode_gemm == "own" and rows <= 16 and k % 8 == 0:
                 y = out if out is not None else t.empty((rows, n), dtype=x.dtype, device=self.device)
                 _att.gemv(x.contiguous(), w, y, rows, n, k)
                 return y
