@@ -208,6 +208,23 @@ int mslim_cuda_decode_selected(const mslim_geometry_t *geometry, const void *q, 
                                uint32_t n_seq, uint32_t split_tokens, void *workspace, size_t workspace_bytes,
                                void *out, void *stream);
 
+/* The same certified sparse decode over ColdStore-exact pages: the selected
+ * rows are gathered straight out of the page pool (k_pool/v_pool bf16
+ * [n_pages][KVH][page_tokens][D], page_table device int32
+ * [n_seq][max_pages_per_seq]), so an epsilon > 0 decode needs no dense copy
+ * of the cache (the reference's micro path reads its dense GPU caches,
+ * src/gpu_llm/gpu_resources.rs:656-771).  Workspace and results as
+ * mslim_cuda_decode_selected: selecting every position gives the bits of
+ * mslim_cuda_decode_paged with the same split_tokens.  A page id outside the
+ * pool is reported by mslim_cuda_device_status. */
+int mslim_cuda_decode_selected_paged(const mslim_geometry_t *geometry, const void *q, const void *k_pool,
+                                     const void *v_pool, uint32_t n_pages, uint32_t page_tokens,
+                                     const int32_t *page_table, uint32_t max_pages_per_seq,
+                                     const int32_t *seq_tokens, const int32_t *selected,
+                                     const int32_t *selected_counts, uint32_t max_selected, uint32_t n_seq,
+                                     uint32_t split_tokens, void *workspace, size_t workspace_bytes, void *out,
+                                     void *stream);
+
 /* Paged decode over ColdStore-exact pages: the device-resident replacement of
  * GpuEngine::attention_gpu_region (src/gpu_llm/gpu_resources.rs:883-1063),
  * which staged V from the ColdStore through the host.  k_pool/v_pool: bf16

@@ -370,6 +370,58 @@ def test_selected_decode_empty_and_invalid_selections(m, wl):
     assert m.device_status(0) == 2
 
 
+@pytest.mark.parametrize("page_tokens", [64, 256])
+def test_selected_decode_over_coldstore_pages(m, wl, oracle, page_tokens):
+    """epsilon > 0 over ColdStore-exact pages: the selected rows come straight
+    out of the page pool (random physical order, NaN in unused slots) and give
+    the bits of the dense-cache selection over the same K/V; selecting every
+    position gives the paged decode's bits; a page id outside the pool is
+    reported."""
+    torch = torch_mod()
+    rng = np.random.default_rng(1063 + page_tokens)
+    qh, kvh, d = 32, 8, 128
+    g = m.AttentionGeometry.new(qh, kvh, d)
+    lengths, counts = [300, 1025, 64, 700], [5, 333, 64, 700]
+    pool = build_pool(wl, rng, lengths, kvh, d, page_tokens)
+    n_seq, cap = len(lengths), 768
+    sel = np.zeros((n_seq, cap), np.int32)
+    for s_, (L, c) in enumerate(zip(lengths, counts)):
+        sel[s_, :c] = np.sort(rng.choice(L, size=c, replace=False))
+    sel[3, :700] = np.arange(700)                            # every position of session 3
+    q = rand_bf16(wl, rng, (n_seq, qh, d))
+    st = 128
+    ws = torch.empty(m.decode_selected_workspace_bytes(g, n_seq, cap, st), dtype=torch.uint8, device="cuda:0")
+    seq = dev(np.asarray(lengths, np.int32))
+    cnt = dev(np.asarray(counts, np.int32))
+    kp, vp = dev(pool["k_pool"]), dev(pool["v_pool"])
+
+    def paged_sel(table):
+        out = empty_u16((n_seq, qh, d))
+        m.decode_selected_paged(g, dev(q), kp, vp, pool["n_pages"], page_tokens, dev(table), pool["max_pages"],
+                                seq, dev(sel), cnt, cap, n_seq, ws, out, st)
+        torch.cuda.synchronize()
+        return host_u16(out)
+
+    got = paged_sel(pool["table"])
+    assert m.device_status(0) == 0
+    dense_out = empty_u16((n_seq, qh, d))
+    m.decode_selected(g, dev(q), dev(pool["k_dense"]), dev(pool["v_dense"]), pool["max_tokens"], seq, dev(sel), cnt,
+                      cap, n_seq, ws, dense_out, st)
+    torch.cuda.synchronize()
+    assert got.tobytes() == host_u16(dense_out).tobytes()
+    full = run_paged(m, g, q, pool, lengths, page_tokens, st)
+    assert got[3].tobytes() == full[3].tobytes()
+    for s_, c in enumerate(counts):
+        ref = oracle.selected_attention_bf16(qh, kvh, d, oracle.bf16_to_f32(q[s_].reshape(-1)),
+                                             pool["k_dense"][s_], pool["v_dense"][s_], sel[s_, :c])
+        assert max_abs(bf16_f32(got[s_]).reshape(-1), ref) <= TOL, s_
+    assert np.array_equal(host_u16(kp), pool["k_pool"]) and np.array_equal(host_u16(vp), pool["v_pool"])
+    bad = pool["table"].copy()
+    bad[1, 0] = pool["n_pages"] + 3
+    paged_sel(bad)
+    assert m.device_status(0) == 2
+
+
 def test_gpu_engine_reserves_its_workspace_when_built(m, wl, oracle):
     """GpuEngine::attention (src/gpu_llm/gpu_resources.rs:583-643) through the
     Python mirror: the decode workspace is reserved when the engine is built

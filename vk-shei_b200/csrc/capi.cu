@@ -653,16 +653,19 @@ int mslim_cuda_decode_selected_workspace_bytes(const mslim_geometry_t *geometry,
     return MSLIM_OK;
 }
 
-int mslim_cuda_decode_selected(const mslim_geometry_t *geometry, const void *q, const void *k_cache,
-                               const void *v_cache, uint32_t max_tokens, const int32_t *seq_tokens,
-                               const int32_t *selected, const int32_t *selected_counts, uint32_t max_selected,
-                               uint32_t n_seq, uint32_t split_tokens, void *workspace, size_t workspace_bytes,
-                               void *out, void *stream) {
+// The gather into the workspace, then the dense split-KV decode over the
+// gathered rows (shared by the dense-cache and the page-pool forms).
+static int run_decode_selected(const mslim_geometry_t *geometry, const void *q, const void *k_src,
+                               const void *v_src, uint32_t max_tokens, const int32_t *page_table,
+                               uint32_t max_pages, uint32_t page_tokens, uint32_t n_pages,
+                               const int32_t *seq_tokens, const int32_t *selected, const int32_t *selected_counts,
+                               uint32_t max_selected, uint32_t n_seq, uint32_t split_tokens, void *workspace,
+                               size_t workspace_bytes, void *out, void *stream) {
     if (max_tokens == 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty cache");
     if (max_selected == 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty selection capacity");
     uint32_t st = split_tokens;
     if (int rc = decode_common_checks(geometry, n_seq, &st, max_selected)) return rc;
-    if (!q || !k_cache || !v_cache || !seq_tokens || !selected || !selected_counts || !out || !workspace)
+    if (!q || !k_src || !v_src || !seq_tokens || !selected || !selected_counts || !out || !workspace)
         return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
     SelectedLayout l;
     if (int rc = selected_layout(geometry, n_seq, max_selected, st, &l)) return rc;
@@ -676,9 +679,9 @@ int mslim_cuda_decode_selected(const mslim_geometry_t *geometry, const void *q, 
     uint16_t *gv = reinterpret_cast<uint16_t *>(base + l.kv_bytes);
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaError_t err = mslim::launch_gather_selected(
-        static_cast<const uint16_t *>(k_cache), static_cast<const uint16_t *>(v_cache), max_tokens,
-        geometry->kv_heads, geometry->head_dim, seq_tokens, selected, selected_counts, max_selected, n_seq, gk, gv,
-        status_ptr(dev), s);
+        static_cast<const uint16_t *>(k_src), static_cast<const uint16_t *>(v_src), max_tokens, page_table,
+        max_pages, page_tokens, n_pages, geometry->kv_heads, geometry->head_dim, seq_tokens, selected,
+        selected_counts, max_selected, n_seq, gk, gv, status_ptr(dev), s);
     if (err != cudaSuccess) return cuda_fail(err, "selection gather launch");
     DecodeCall c{};
     c.g = geometry;
@@ -698,6 +701,32 @@ int mslim_cuda_decode_selected(const mslim_geometry_t *geometry, const void *q, 
     c.kernel_dim = kernel_dim_for(geometry->head_dim);
     c.stream = s;
     return run_decode(c);
+}
+
+int mslim_cuda_decode_selected(const mslim_geometry_t *geometry, const void *q, const void *k_cache,
+                               const void *v_cache, uint32_t max_tokens, const int32_t *seq_tokens,
+                               const int32_t *selected, const int32_t *selected_counts, uint32_t max_selected,
+                               uint32_t n_seq, uint32_t split_tokens, void *workspace, size_t workspace_bytes,
+                               void *out, void *stream) {
+    return run_decode_selected(geometry, q, k_cache, v_cache, max_tokens, nullptr, 0, 0, 0, seq_tokens, selected,
+                               selected_counts, max_selected, n_seq, split_tokens, workspace, workspace_bytes, out,
+                               stream);
+}
+
+int mslim_cuda_decode_selected_paged(const mslim_geometry_t *geometry, const void *q, const void *k_pool,
+                                     const void *v_pool, uint32_t n_pages, uint32_t page_tokens,
+                                     const int32_t *page_table, uint32_t max_pages_per_seq,
+                                     const int32_t *seq_tokens, const int32_t *selected,
+                                     const int32_t *selected_counts, uint32_t max_selected, uint32_t n_seq,
+                                     uint32_t split_tokens, void *workspace, size_t workspace_bytes, void *out,
+                                     void *stream) {
+    if (page_tokens == 0 || n_pages == 0 || max_pages_per_seq == 0 || !page_table)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty page pool or page table");
+    const uint64_t reach = (uint64_t)max_pages_per_seq * page_tokens;
+    if (reach > 0x7fffffffull) return fail(MSLIM_ERR_SHAPE_MISMATCH, "page table spans too many tokens");
+    return run_decode_selected(geometry, q, k_pool, v_pool, (uint32_t)reach, page_table, max_pages_per_seq,
+                               page_tokens, n_pages, seq_tokens, selected, selected_counts, max_selected, n_seq,
+                               split_tokens, workspace, workspace_bytes, out, stream);
 }
 
 int mslim_cuda_decode_paged(const mslim_geometry_t *geometry, const void *q, const void *k_pool,

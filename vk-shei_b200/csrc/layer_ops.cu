@@ -249,20 +249,30 @@ __global__ void __launch_bounds__(256)
 
 // Certified-selection gather: for session s, the count[s] token positions
 // selected[s][0..count) (strictly increasing, each below the session's
-// committed length seq_tokens[s]) have their K and V rows copied from the
-// token-major dense caches [n_seq][max_tokens][kv_heads][dim] to rows 0..count
-// of gk/gv [n_seq][max_selected][kv_heads][dim], so a dense decode over count
-// tokens attends to exactly the selected set.  A count above max_selected or
-// above the committed length, a position out of range or not above its
-// predecessor is recorded in the status word and its row is not copied.
-// One thread per 16-byte chunk (kvh * dim % 8 == 0) or per element.
+// committed length seq_tokens[s]) have their K and V rows copied to rows
+// 0..count of gk/gv [n_seq][max_selected][kv_heads][dim], so a dense decode
+// over count tokens attends to exactly the selected set.  The source is the
+// token-major dense caches [n_seq][max_tokens][kv_heads][dim] or, with a page
+// table, ColdStore-exact pool pages [n_pages][kv_heads][page_tokens][dim]
+// (position t of session s is token t % page_tokens of page
+// page_table[s][t / page_tokens]; head h's row of it is contiguous).  A count
+// above max_selected or above the committed length, a position out of range
+// or not above its predecessor, or a page id outside the pool is recorded in
+// the status word and its row is not copied.  One thread per 16-byte chunk
+// (dim % 8 == 0) or per element.
+struct GatherSrc {
+    const uint16_t *k, *v;
+    uint32_t max_tokens;        // dense: rows per session; paged: max_pages * page_tokens
+    const int32_t *page_table;  // null: dense
+    uint32_t max_pages, page_tokens, n_pages;
+};
+
 template <bool kVec>
 __global__ void __launch_bounds__(256)
-    mslim_gather_selected(const uint16_t *__restrict__ k_cache, const uint16_t *__restrict__ v_cache,
-                          uint32_t max_tokens, uint32_t row_elems, const int32_t *__restrict__ seq_tokens,
-                          const int32_t *__restrict__ selected, const int32_t *__restrict__ counts,
-                          uint32_t max_selected, uint16_t *__restrict__ gk, uint16_t *__restrict__ gv,
-                          int *status) {
+    mslim_gather_selected(const GatherSrc src, uint32_t kv_heads, uint32_t dim,
+                          const int32_t *__restrict__ seq_tokens, const int32_t *__restrict__ selected,
+                          const int32_t *__restrict__ counts, uint32_t max_selected, uint16_t *__restrict__ gk,
+                          uint16_t *__restrict__ gv, int *status) {
     constexpr uint32_t kW = kVec ? 8 : 1;
     const uint32_t s = blockIdx.x;
     const int32_t committed = seq_tokens[s];
@@ -272,47 +282,62 @@ __global__ void __launch_bounds__(256)
         return;
     }
     const int32_t *sel = selected + (size_t)s * max_selected;
+    const uint32_t row_elems = kv_heads * dim;
+    const uint32_t per_head = dim / kW;
     const uint32_t per_row = row_elems / kW;
     const uint64_t total = (uint64_t)count * per_row;
     for (uint64_t x = (uint64_t)blockIdx.y * blockDim.x + threadIdx.x; x < total;
          x += (uint64_t)gridDim.y * blockDim.x) {
         const uint32_t e = (uint32_t)(x / per_row), c = (uint32_t)(x % per_row);
         const int32_t pos = sel[e];
-        if (pos < 0 || pos >= committed || (uint32_t)pos >= max_tokens || (e > 0 && sel[e - 1] >= pos)) {
+        if (pos < 0 || pos >= committed || (uint32_t)pos >= src.max_tokens || (e > 0 && sel[e - 1] >= pos)) {
             if (c == 0 && status) atomicExch(status, MSLIM_DEVICE_BAD_PAGE_CODE);
             continue;
         }
-        const size_t src = ((size_t)s * max_tokens + (uint32_t)pos) * row_elems + (size_t)c * kW;
+        size_t from;
+        if (src.page_table) {
+            const int32_t phys = src.page_table[(size_t)s * src.max_pages + (uint32_t)pos / src.page_tokens];
+            if (phys < 0 || (uint32_t)phys >= src.n_pages) {
+                if (c == 0 && status) atomicExch(status, MSLIM_DEVICE_BAD_PAGE_CODE);
+                continue;
+            }
+            const uint32_t h = c / per_head, within = c % per_head;
+            from = (((size_t)phys * kv_heads + h) * src.page_tokens + (uint32_t)pos % src.page_tokens) * dim +
+                   (size_t)within * kW;
+        } else {
+            from = ((size_t)s * src.max_tokens + (uint32_t)pos) * row_elems + (size_t)c * kW;
+        }
         const size_t dst = ((size_t)s * max_selected + e) * row_elems + (size_t)c * kW;
         if constexpr (kVec) {
-            *reinterpret_cast<uint4 *>(gk + dst) = *reinterpret_cast<const uint4 *>(k_cache + src);
-            *reinterpret_cast<uint4 *>(gv + dst) = *reinterpret_cast<const uint4 *>(v_cache + src);
+            *reinterpret_cast<uint4 *>(gk + dst) = *reinterpret_cast<const uint4 *>(src.k + from);
+            *reinterpret_cast<uint4 *>(gv + dst) = *reinterpret_cast<const uint4 *>(src.v + from);
         } else {
-            gk[dst] = k_cache[src];
-            gv[dst] = v_cache[src];
+            gk[dst] = src.k[from];
+            gv[dst] = src.v[from];
         }
     }
 }
 
 }  // namespace
 
-cudaError_t launch_gather_selected(const uint16_t *k_cache, const uint16_t *v_cache, uint32_t max_tokens,
-                                   uint32_t kv_heads, uint32_t dim, const int32_t *seq_tokens,
+cudaError_t launch_gather_selected(const uint16_t *k_src, const uint16_t *v_src, uint32_t max_tokens,
+                                   const int32_t *page_table, uint32_t max_pages, uint32_t page_tokens,
+                                   uint32_t n_pages, uint32_t kv_heads, uint32_t dim, const int32_t *seq_tokens,
                                    const int32_t *selected, const int32_t *counts, uint32_t max_selected,
                                    uint32_t n_seq, uint16_t *gk, uint16_t *gv, int *status, cudaStream_t stream) {
     auto al = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
     const uint32_t row_elems = kv_heads * dim;
-    const bool vec = row_elems % 8 == 0 && al(k_cache) && al(v_cache) && al(gk) && al(gv);
+    const bool vec = dim % 8 == 0 && al(k_src) && al(v_src) && al(gk) && al(gv);
     const uint64_t per_session = (uint64_t)max_selected * (vec ? row_elems / 8 : row_elems);
     const unsigned chunks = (unsigned)std::min<uint64_t>(std::max<uint64_t>(1, (per_session + 255) / 256), 64);
     const dim3 grid(n_seq, chunks);
+    const GatherSrc src{k_src, v_src, max_tokens, page_table, max_pages, page_tokens, n_pages};
     if (vec)
-        mslim_gather_selected<true><<<grid, 256, 0, stream>>>(k_cache, v_cache, max_tokens, row_elems, seq_tokens,
-                                                               selected, counts, max_selected, gk, gv, status);
+        mslim_gather_selected<true><<<grid, 256, 0, stream>>>(src, kv_heads, dim, seq_tokens, selected, counts,
+                                                               max_selected, gk, gv, status);
     else
-        mslim_gather_selected<false><<<grid, 256, 0, stream>>>(k_cache, v_cache, max_tokens, row_elems,
-                                                                seq_tokens, selected, counts, max_selected, gk, gv,
-                                                                status);
+        mslim_gather_selected<false><<<grid, 256, 0, stream>>>(src, kv_heads, dim, seq_tokens, selected, counts,
+                                                                max_selected, gk, gv, status);
     return cudaGetLastError();
 }
 

@@ -25,11 +25,15 @@ cudaError_t launch_page_token_hashes(const uint16_t *pool, uint32_t n_pool_pages
 // equals, NaN never chosen unless every entry is NaN (the OpenCL llm_argmax).
 cudaError_t launch_argmax(const uint16_t *logits, uint32_t rows, uint32_t n, int ties_to_last,
                           int32_t *out, cudaStream_t stream);
-// Rows selected[s][0..counts[s]) of the dense caches [n_seq][max_tokens][kv_heads][dim]
-// -> rows 0..counts[s] of gk/gv [n_seq][max_selected][kv_heads][dim] (positions
-// strictly increasing and below seq_tokens[s]; violations go to the status word).
-cudaError_t launch_gather_selected(const uint16_t *k_cache, const uint16_t *v_cache, uint32_t max_tokens,
-                                   uint32_t kv_heads, uint32_t dim, const int32_t *seq_tokens,
+// Rows selected[s][0..counts[s]) of session s -> rows 0..counts[s] of gk/gv
+// [n_seq][max_selected][kv_heads][dim] (positions strictly increasing and
+// below seq_tokens[s]; violations go to the status word).  Source: dense
+// caches [n_seq][max_tokens][kv_heads][dim] (page_table null) or pool pages
+// [n_pages][kv_heads][page_tokens][dim] listed by page_table [n_seq][max_pages]
+// (max_tokens = max_pages * page_tokens).
+cudaError_t launch_gather_selected(const uint16_t *k_src, const uint16_t *v_src, uint32_t max_tokens,
+                                   const int32_t *page_table, uint32_t max_pages, uint32_t page_tokens,
+                                   uint32_t n_pages, uint32_t kv_heads, uint32_t dim, const int32_t *seq_tokens,
                                    const int32_t *selected, const int32_t *counts, uint32_t max_selected,
                                    uint32_t n_seq, uint16_t *gk, uint16_t *gv, int *status, cudaStream_t stream);
 // out [kv_heads][tokens][dim] bf16: one session's K (or V) rows in the logical

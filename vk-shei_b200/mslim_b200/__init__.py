@@ -12,7 +12,7 @@ from .attention import (AttentionGeometry, AttentionKernelConfig, AttentionKerne
                         decode_workspace_bytes, decode_split_tokens, device_status, prefill_causal, rmsnorm, rope,
                         rope_append_decode_dense, rope_append_decode_paged, rope_append_paged, residual_add, swiglu,
                         argmax, swiglu_rows, residual_rmsnorm, gemv, page_token_hashes, kv_canonical_dense, kv_canonical_paged,
-                        decode_selected, decode_selected_workspace_bytes,
+                        decode_selected, decode_selected_paged, decode_selected_workspace_bytes,
                         rope_append_decode_dense_qkv,
                         rope_append_decode_paged_qkv)
 

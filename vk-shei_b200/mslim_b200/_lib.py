@@ -89,6 +89,8 @@ SIGNATURES = {
     "mslim_cuda_decode_selected_workspace_bytes": (_int, [_vp, _u32, _u32, _u32, _vp]),
     "mslim_cuda_decode_selected": (_int, [_vp, _vp, _vp, _vp, _u32, _vp, _vp, _vp, _u32, _u32, _u32, _vp,
                                           ctypes.c_size_t, _vp, _vp]),
+    "mslim_cuda_decode_selected_paged": (_int, [_vp, _vp, _vp, _vp, _u32, _u32, _vp, _u32, _vp, _vp, _vp, _u32,
+                                                _u32, _u32, _vp, ctypes.c_size_t, _vp, _vp]),
     "mslim_cuda_kv_canonical_paged": (_int, [_vp, _u32, _u32, _u32, _u32, _vp, _u32, _u32, _vp, _vp]),
     "mslim_cuda_swiglu_rows": (_int, [_vp, _vp, _u32, _u32, _vp]),
     "mslim_cuda_argmax": (_int, [_vp, _u32, _u32, _int, _vp, _vp]),

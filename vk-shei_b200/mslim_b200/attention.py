@@ -291,6 +291,17 @@ def decode_selected(geometry: AttentionGeometry, q, k_cache, v_cache, max_tokens
         _nbytes(workspace), _ptr(out), _stream(stream)))
 
 
+def decode_selected_paged(geometry: AttentionGeometry, q, k_pool, v_pool, n_pages: int, page_tokens: int,
+                          page_table, max_pages_per_seq: int, seq_tokens, selected, selected_counts,
+                          max_selected: int, n_seq: int, workspace, out, split_tokens: int = 0, stream=None) -> None:
+    """Certified sparse decode with the selected rows gathered straight out
+    of ColdStore-exact pages."""
+    check(_lib.lib().mslim_cuda_decode_selected_paged(
+        ctypes.byref(geometry.c()), _ptr(q), _ptr(k_pool), _ptr(v_pool), n_pages, page_tokens, _ptr(page_table),
+        max_pages_per_seq, _ptr(seq_tokens), _ptr(selected), _ptr(selected_counts), max_selected, n_seq,
+        split_tokens, _ptr(workspace), _nbytes(workspace), _ptr(out), _stream(stream)))
+
+
 def decode_paged(geometry: AttentionGeometry, q, k_pool, v_pool, n_pages: int, page_tokens: int,
                  page_table, max_pages_per_seq: int, seq_tokens, n_seq: int, workspace, out,
                  split_tokens: int = 0, stream=None) -> None:
