@@ -190,13 +190,17 @@ int decode_shape(const mslim_geometry_t *g, uint32_t nq, DecodeShapeInfo *s) {
     return MSLIM_OK;
 }
 
-// Split policy: aim for about eight waves of two CTAs per SM, with splits of
-// 64..2048 tokens (multiples of the 64-token TMA stage).
-// Tokens per split: about eight waves of two CTAs per SM over all (session,
-// KV-head chunk) items, at least 256 tokens (four pipeline stages, so a CTA's
-// setup is amortised and the merge combines few partials) and at most 2048.
+// Split policy (tokens per split, a multiple of the 64-token TMA stage):
+// about seven CTAs per SM (3.5 waves of two) if every (session, KV-head
+// chunk) item held max_tokens tokens, at least 256 tokens (four pipeline
+// stages, so a CTA's setup is amortised and the merge combines few partials)
+// and at most 2048.  Sessions shorter than max_tokens make fewer CTAs, so the
+// real count is lower; splits this long were measured faster than shorter
+// ones both for 64 C4 sessions on one GPU and for the 8-session shards of an
+// 8-GPU run (per-CTA setup and the merge cost more than the last wave's
+// imbalance).
 uint32_t policy_split_tokens(uint64_t work_items, uint64_t max_tokens) {
-    const uint64_t target = 148ull * 2 * 8;
+    const uint64_t target = 148ull * 7;
     uint64_t st = (work_items * max_tokens + target - 1) / target;
     st = (st + 63) / 64 * 64;
     return (uint32_t)std::min<uint64_t>(std::max<uint64_t>(st, 256), 2048);
