@@ -720,7 +720,10 @@ def main():
                                    "256-token ColdStore-exact pages in a random physical permutation, "
                                    "QH 32 / KVH 8 / D 128, one query per session",
                        "sessions_per_gpu": c4_local["n_seq"], "global_sessions": total_seq, "page_tokens": PAGE,
-                       "split_tokens": args.split_tokens or "policy",
+                       "split_tokens": [int(r[2]) for r in ranks],
+                       "split_tokens_source": ("--split-tokens" if args.split_tokens else
+                                               "mslim_cuda_decode_split_tokens_for_lengths on each rank's "
+                                               "host-side session lengths"),
                        "l2": "no flush: inputs larger than L2 (%.2f GB per GPU per step)" % (step_bytes / 1e9),
                        "parallelism": (f"sessions LPT-sharded over {world} GPUs (strong: one 64-session C4 draw)"
                                        if strong else
@@ -769,7 +772,10 @@ class C4Pages:
         self.seq_d = torch.from_numpy(lengths).to(device)
         self.g = m.AttentionGeometry.new(QH, KVH, D)
         max_tokens = max_pages * PAGE
-        self.split_tokens = split_tokens or m.decode_split_tokens(self.g, n_seq, max_tokens)
+        # the split size for this rank's sessions from their host-side lengths
+        # (fewest waves of split CTAs), as a serving host that tracks its
+        # sessions' lengths would choose it
+        self.split_tokens = split_tokens or m.decode_split_tokens_for_lengths(self.g, lengths)
         self.ws = torch.empty(m.decode_workspace_bytes(self.g, n_seq, max_tokens, self.split_tokens),
                               dtype=torch.uint8, device=device)
         self.ctas = int(sum(-(-int(L) // self.split_tokens) for L in lengths)) * KVH

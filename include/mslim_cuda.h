@@ -168,6 +168,16 @@ int mslim_cuda_decode_workspace_bytes(const mslim_geometry_t *geometry, uint32_t
 int mslim_cuda_decode_split_tokens(const mslim_geometry_t *geometry, uint32_t n_seq,
                                    uint32_t max_tokens, uint32_t *split_tokens);
 
+/* A split size for one batch whose token counts the host knows (host int32
+ * lengths[n_seq], as the runtime tracks them): the split CTAs of a decode
+ * run in waves of the GPU's resident CTAs, so the size is chosen for the
+ * fewest waves times the split length rather than from the longest session
+ * alone; pass it to the decode calls of that batch (bits are identical for
+ * every call with the same split size).  No reference counterpart: the
+ * reference's split-KV plan takes a fixed split count. */
+int mslim_cuda_decode_split_tokens_for_lengths(const mslim_geometry_t *geometry, uint32_t n_seq,
+                                               const int32_t *lengths, uint32_t *split_tokens);
+
 /* Dense decode: GpuEngine::attention / exact_hot_fused_attention
  * (src/gpu_llm/gpu_resources.rs:583-643,783-828) for a batch of sequences.
  * q: bf16 [n_seq][QH][D] (post-RoPE); k_cache/v_cache: bf16 token-major

@@ -137,3 +137,20 @@ def test_decode_workspace_bytes(m):
     assert m.decode_workspace_bytes(g, 64, 32768, 2048) == 64 * 32 * 16 * 130 * 4
     with pytest.raises(m.ShapeMismatch):
         m.decode_workspace_bytes(g, 1, 100, 100)
+
+
+def test_split_tokens_for_host_lengths(m):
+    """mslim_cuda_decode_split_tokens_for_lengths: a multiple of 64 in
+    [256, 4096], deterministic, and for one rank's share of an 8-GPU C4 run
+    (eight sessions, about 139 K tokens) it keeps the split CTAs within two
+    waves of the 296 resident CTAs, where the longest-session policy alone
+    would start a nearly empty third wave."""
+    import numpy as np
+    g = m.AttentionGeometry.new(32, 8, 128)
+    lengths = np.array([32000, 5100, 27000, 9000, 14000, 21000, 4200, 26000], np.int32)
+    st = m.decode_split_tokens_for_lengths(g, lengths)
+    assert st % 64 == 0 and 256 <= st <= 4096
+    assert st == m.decode_split_tokens_for_lengths(g, lengths)
+    ctas = sum(-(-int(L) // st) for L in lengths) * 8
+    assert ctas <= 2 * 296, (st, ctas)
+    assert m.decode_split_tokens_for_lengths(g, np.zeros(3, np.int32)) % 64 == 0

@@ -584,6 +584,38 @@ int mslim_cuda_decode_split_tokens(const mslim_geometry_t *geometry, uint32_t n_
     return MSLIM_OK;
 }
 
+int mslim_cuda_decode_split_tokens_for_lengths(const mslim_geometry_t *geometry, uint32_t n_seq,
+                                               const int32_t *lengths, uint32_t *split_tokens) {
+    if (int rc = check_geometry(geometry)) return rc;
+    if (!split_tokens || !lengths) return fail(MSLIM_ERR_SHAPE_MISMATCH, "null pointer");
+    if (n_seq == 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty batch");
+    DecodeShapeInfo sh;
+    if (int rc = decode_shape(geometry, 1, &sh)) return rc;
+    // resident split CTAs: shared memory allows three per SM at head_dim 64,
+    // two at 128 and one at 256 (the kernel's stage rings)
+    const uint32_t kd = kernel_dim_for(geometry->head_dim);
+    const uint64_t slots = 148ull * (kd <= 64 ? 3 : kd <= 128 ? 2 : 1);
+    const uint64_t per_seq = (uint64_t)geometry->kv_heads * sh.head_chunks;
+    // Every wave of CTAs lasts about one full split (plus a fixed per-CTA cost
+    // of about three 64-token stages), so the step takes about
+    // ceil(CTAs / slots) * (split + 192) token-times: pick the split that
+    // minimises it, the longer split on a tie.
+    uint64_t best = ~0ull;
+    uint32_t best_st = 2048;
+    for (uint32_t st = 256; st <= 4096; st += 64) {
+        uint64_t ctas = 0;
+        for (uint32_t i = 0; i < n_seq; ++i)
+            if (lengths[i] > 0) ctas += ((uint64_t)lengths[i] + st - 1) / st * per_seq;
+        const uint64_t cost = ((ctas + slots - 1) / slots) * (st + 192);
+        if (cost <= best) {
+            best = cost;
+            best_st = st;
+        }
+    }
+    *split_tokens = best_st;
+    return MSLIM_OK;
+}
+
 static int decode_common_checks(const mslim_geometry_t *geometry, uint32_t n_seq,
                                 uint32_t *split_tokens, uint32_t max_tokens) {
     if (int rc = check_geometry(geometry)) return rc;

@@ -21,13 +21,14 @@
 //           stage's commit releasing its ring slot;
 //   all     read the accumulator with tcgen05.ld (thread t = output feature
 //           t of the tile) and write bf16 rows.
-// Long K is cut into up to eight splits so that about three CTAs per SM
-// stream at once.  The splits of one tile form a thread-block cluster: each
-// CTA leaves its fp32 partial in its own shared memory, and after a cluster
-// barrier the first CTA of the cluster reads them over distributed shared
-// memory, adds them in split order and rounds once, so the result does not
-// depend on which CTA finished first, and nothing goes through global
-// memory (no workspace).
+// Long K is cut into up to eight splits so that the CTAs of a projection fill
+// the GPU in one wave (three per SM).  The splits of one tile form a
+// thread-block cluster: once the first CTA's own MMAs are done its ring is
+// free, it signals its partners, they store their fp32 partials straight
+// into its shared memory (distributed shared memory, no round trip) and
+// arrive on its barrier, and it adds them in split order and rounds once, so
+// the result does not depend on which CTA finished first, and nothing goes
+// through global memory (no workspace).
 #include "gemv.cuh"
 
 namespace mslim {
@@ -58,26 +59,72 @@ struct Bars {
     uint64_t full[kStages];
     uint64_t empty[kStages];
     uint64_t acc;
+    uint64_t go;        // rank > 0: rank 0's ring is free for this CTA's partial
+    uint64_t red_full;  // rank 0: every partner's partial has landed (S - 1 arrivals)
     uint32_t tmem_base;
 };
 
-__device__ __forceinline__ void cluster_sync() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+// Remote (distributed shared memory) access within the cluster.
+__device__ __forceinline__ uint32_t mapa(uint32_t saddr, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(saddr), "r"(rank));
+    return remote;
+}
+
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
+// Arrives (release, cluster scope) on the mbarrier at `bar` of CTA `rank`.
+__device__ __forceinline__ void mbar_arrive_remote(uint64_t *bar, uint32_t rank) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(mapa(smem_u32(bar), rank))
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait (acquire at cluster scope) for a phase completed by another
+// CTA's remote arrival.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, int *status, int where) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const uint64_t start = globaltimer();
+    uint32_t spins = 0;
+    while (!mbar_try_wait_cluster(bar, parity)) {
+        if (++spins >= 64) {
+            spins = 0;
+            if (globaltimer() - start > kWaitBoundNs) {
+                record_timeout(status, where);
+                return false;
+            }
+        }
+    }
+    return true;
+}
+
+// Split cluster barrier: every thread arrives once right after set-up and
+// waits once before its first remote access, so the barrier's latency hides
+// behind the K stream.
+__device__ __forceinline__ void cluster_arrive() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
     uint32_t r;
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
     return r;
-}
-
-// f32 at shared-memory address `saddr` of CTA `rank` of this cluster.
-__device__ __forceinline__ float ld_dsmem_f32(uint32_t saddr, uint32_t rank) {
-    uint32_t remote;
-    float v;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(saddr), "r"(rank));
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
-    return v;
 }
 
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int32_t x,
@@ -106,7 +153,7 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
     mslim_gemv_tc(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
                   const GemvParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -124,11 +171,14 @@ __global__ void __launch_bounds__(kThreads)
             mbar_init(&bars->empty[s], 1);
         }
         mbar_init(&bars->acc, 1);
+        mbar_init(&bars->go, 1);
+        mbar_init(&bars->red_full, p.splits > 1 ? p.splits - 1 : 1);
         fence_mbarrier_init();
     }
     if (warp == 1) tmem_alloc(&bars->tmem_base, kTmemCols);
     tc_fence_before();
     __syncthreads();
+    cluster_arrive();  // this CTA's barriers exist; partners may signal them after the wait
     tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
 
@@ -182,6 +232,7 @@ __global__ void __launch_bounds__(kThreads)
     griddep_wait();  // outputs are written only once the predecessor is done
     const uint32_t n = tile * 128 + threadIdx.x;
     const uint32_t M = p.m;
+    cluster_wait();  // every CTA of the cluster has its barriers initialised
     if (p.splits == 1) {
         if (n < p.n) {
 #pragma unroll
@@ -189,34 +240,40 @@ __global__ void __launch_bounds__(kThreads)
                 if (r < M) p.y[(size_t)r * p.ldy + n] = bf16_bits_rn(acc[r]);
         }
     } else {
-        // the ring is idle (every stage was consumed by an MMA that has
-        // completed): this CTA's partial goes to red[r][t] at its start
+        // Partners push their fp32 partials into rank 0's ring, which is idle
+        // once rank 0's own MMAs completed (every stage was consumed):
+        // partner r's rows at red[r - 1][row][feature].  Rank 0 says "go"
+        // when its ring is free, adds the partials in rank order when all
+        // have landed, and writes the row.  Partners leave after their push;
+        // rank 0, whose memory they write, leaves last.
+        const uint32_t rank = cluster_ctarank();
         float *red = reinterpret_cast<float *>(smem);
-#pragma unroll
-        for (uint32_t r = 0; r < 16; ++r)
-            if (r < M) red[r * 128 + threadIdx.x] = acc[r];
-        cluster_sync();  // every split's partial is in place
-        if (cluster_ctarank() == 0) {
-            const uint32_t base = smem_u32(red) + threadIdx.x * 4;
+        if (rank == 0) {
+            if (threadIdx.x >= 1 && threadIdx.x < p.splits) mbar_arrive_remote(&bars->go, threadIdx.x);
+            mbar_wait_cluster(&bars->red_full, 0, p.status, 26);
             float sum[16];
 #pragma unroll
             for (uint32_t r = 0; r < 16; ++r) sum[r] = acc[r];
             for (uint32_t s = 1; s < p.splits; ++s) {
-                float v[16];
 #pragma unroll
                 for (uint32_t r = 0; r < 16; ++r)
-                    if (r < M) v[r] = ld_dsmem_f32(base + r * 512, s);
-#pragma unroll
-                for (uint32_t r = 0; r < 16; ++r)
-                    if (r < M) sum[r] += v[r];
+                    if (r < M) sum[r] += red[((s - 1) * 16 + r) * 128 + threadIdx.x];
             }
             if (n < p.n) {
 #pragma unroll
                 for (uint32_t r = 0; r < 16; ++r)
                     if (r < M) p.y[(size_t)r * p.ldy + n] = bf16_bits_rn(sum[r]);
             }
+        } else {
+            mbar_wait_cluster(&bars->go, 0, p.status, 25);
+            const uint32_t dst = mapa(smem_u32(red + ((rank - 1) * 16) * 128 + threadIdx.x), 0);
+#pragma unroll
+            for (uint32_t r = 0; r < 16; ++r)
+                if (r < M) st_cluster_f32(dst + r * 512, acc[r]);
+            asm volatile("fence.acq_rel.cluster;" ::: "memory");
+            __syncthreads();
+            if (threadIdx.x == 0) mbar_arrive_remote(&bars->red_full, 0);
         }
-        cluster_sync();  // no CTA leaves while its partial may still be read
     }
     tc_fence_before();
     __syncthreads();
@@ -230,13 +287,21 @@ GemvPlan gemv_plan(uint32_t m, uint32_t n, uint32_t k) {
     GemvPlan pl{};
     pl.n_tiles = (n + 127) / 128;
     pl.k_steps = (k + 63) / 64;
-    const uint64_t total = (uint64_t)pl.n_tiles * pl.k_steps;
-    const uint64_t target = 148ull * kCtasPerSm;
-    uint64_t kt = std::max<uint64_t>(kMinKTiles, (total + target - 1) / target);
-    kt = std::min<uint64_t>(kt, pl.k_steps);
-    pl.splits = (uint32_t)std::min<uint64_t>(kMaxSplits, (pl.k_steps + kt - 1) / kt);
+    // One wave of CTAs (kCtasPerSm per SM) when the tiles allow: the largest
+    // split count (at most eight, at least kMinKTiles K steps per CTA) whose
+    // CTAs all fit at once, so they start together and finish together; a
+    // second, nearly empty wave would stream its few CTAs with the HBM idle.
+    // Tiles beyond one wave already fill the GPU unsplit.
+    const uint32_t slots = 148u * kCtasPerSm;
+    pl.splits = 1;
+    for (uint32_t s = 2; s <= kMaxSplits; ++s) {
+        const uint32_t kt = (pl.k_steps + s - 1) / s;
+        const uint32_t splits = (pl.k_steps + kt - 1) / kt;  // no empty split
+        if (kt < kMinKTiles || (uint64_t)pl.n_tiles * splits > slots) break;
+        pl.splits = splits;
+    }
     pl.k_tiles = (pl.k_steps + pl.splits - 1) / pl.splits;
-    pl.splits = (pl.k_steps + pl.k_tiles - 1) / pl.k_tiles;  // no empty split
+    pl.splits = (pl.k_steps + pl.k_tiles - 1) / pl.k_tiles;
     return pl;
 }
 

@@ -74,6 +74,7 @@ SIGNATURES = {
     "mslim_cuda_plan_diagnostics": (_int, [_vp, ctypes.c_char_p, _sz]),
     "mslim_cuda_decode_workspace_bytes": (_int, [_G, _u32, _u32, _u32, ctypes.POINTER(_sz)]),
     "mslim_cuda_decode_split_tokens": (_int, [_G, _u32, _u32, ctypes.POINTER(_u32)]),
+    "mslim_cuda_decode_split_tokens_for_lengths": (_int, [_G, _u32, _vp, ctypes.POINTER(_u32)]),
     "mslim_cuda_exp2_eval": (_int, [_vp, _vp, _vp, _vp, _u32, _vp]),
     "mslim_cuda_decode_dense": (_int, [_G, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _vp, _sz, _vp, _vp]),
     "mslim_cuda_decode_paged": (_int, [_G, _vp, _vp, _vp, _u32, _u32, _vp, _u32, _vp, _u32, _u32, _vp,

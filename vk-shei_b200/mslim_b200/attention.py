@@ -263,6 +263,16 @@ def decode_split_tokens(geometry: AttentionGeometry, n_seq: int, max_tokens: int
     return out.value
 
 
+def decode_split_tokens_for_lengths(geometry: AttentionGeometry, lengths) -> int:
+    """The split size for a batch whose token counts are known on the host
+    (fewest waves of split CTAs times the split length)."""
+    arr = np.ascontiguousarray(np.asarray(lengths, dtype=np.int32))
+    out = ctypes.c_uint32()
+    check(_lib.lib().mslim_cuda_decode_split_tokens_for_lengths(ctypes.byref(geometry.c()), arr.size,
+                                                                arr.ctypes.data, ctypes.byref(out)))
+    return out.value
+
+
 def decode_dense(geometry: AttentionGeometry, q, k_cache, v_cache, seq_tokens, n_seq: int,
                  max_tokens: int, workspace, out, split_tokens: int = 0, stream=None) -> None:
     """GpuEngine::attention for a batch of token-major caches."""
