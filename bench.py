@@ -776,7 +776,7 @@ class C4Pages:
         # (fewest waves of split CTAs), as a serving host that tracks its
         # sessions' lengths would choose it
         self.split_tokens = split_tokens or m.decode_split_tokens_for_lengths(self.g, lengths)
-        self.ws = torch.empty(m.decode_workspace_bytes(self.g, n_seq, max_tokens, self.split_tokens),
+        self.ws = torch.zeros(m.decode_workspace_bytes(self.g, n_seq, max_tokens, self.split_tokens),
                               dtype=torch.uint8, device=device)
         self.ctas = int(sum(-(-int(L) // self.split_tokens) for L in lengths)) * KVH
         self.tokens = int(lengths.astype(np.int64).sum())

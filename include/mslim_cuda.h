@@ -156,7 +156,11 @@ int mslim_cuda_plan_diagnostics(const mslim_plan_t *plan, char *out, size_t len)
 /* Bytes of split scratch that mslim_cuda_decode_* need for n_seq sequences
  * of at most max_tokens tokens split every split_tokens tokens
  * (split_tokens 0 = library policy).  Counterpart of
- * AttentionKernelConfig::decode_scratch_bytes (src/attention_kernel.rs:124-138). */
+ * AttentionKernelConfig::decode_scratch_bytes (src/attention_kernel.rs:124-138).
+ * A decode workspace must be zero-filled once before its first use: its
+ * first 256 bytes hold the counter from which the split kernel's resident
+ * CTAs take their work, and every call leaves them zero again.  One
+ * workspace serves any later calls that fit it, on one stream at a time. */
 int mslim_cuda_decode_workspace_bytes(const mslim_geometry_t *geometry, uint32_t n_seq,
                                       uint32_t max_tokens, uint32_t split_tokens, size_t *bytes);
 
@@ -173,8 +177,8 @@ int mslim_cuda_decode_split_tokens(const mslim_geometry_t *geometry, uint32_t n_
  * run in waves of the GPU's resident CTAs, so the size is chosen for the
  * fewest waves times the split length rather than from the longest session
  * alone; pass it to the decode calls of that batch (bits are identical for
- * every call with the same split size).  No reference counterpart: the
- * reference's split-KV plan takes a fixed split count. */
+ * every call with the same split size); 256..3072 tokens.  No reference
+ * counterpart: the reference's split-KV plan takes a fixed split count. */
 int mslim_cuda_decode_split_tokens_for_lengths(const mslim_geometry_t *geometry, uint32_t n_seq,
                                                const int32_t *lengths, uint32_t *split_tokens);
 
@@ -209,7 +213,8 @@ int mslim_cuda_decode_dense(const mslim_geometry_t *geometry, const void *q, con
  * The selected K/V rows are gathered into the workspace and the split-KV
  * decode runs over them, so selecting every position gives the bits of
  * mslim_cuda_decode_dense with the same split_tokens.  workspace: 256-byte
- * aligned, >= mslim_cuda_decode_selected_workspace_bytes. */
+ * aligned, >= mslim_cuda_decode_selected_workspace_bytes, zero-filled once
+ * before its first use (calls leave its counter at zero). */
 int mslim_cuda_decode_selected_workspace_bytes(const mslim_geometry_t *geometry, uint32_t n_seq,
                                                uint32_t max_selected, uint32_t split_tokens, size_t *bytes);
 int mslim_cuda_decode_selected(const mslim_geometry_t *geometry, const void *q, const void *k_cache,
@@ -240,7 +245,9 @@ int mslim_cuda_decode_selected_paged(const mslim_geometry_t *geometry, const voi
  * which staged V from the ColdStore through the host.  k_pool/v_pool: bf16
  * [n_pages][KVH][page_tokens][D]; page_table: device int32
  * [n_seq][max_pages_per_seq] of physical page ids; seq_tokens: device int32
- * [n_seq].  page_tokens must be a multiple of 64.  Results are bit-identical
+ * [n_seq].  page_tokens must be a multiple of 64.  A session of L tokens is
+ * decoded as ceil(L / split_tokens) splits of equal length (rounded up to 64
+ * tokens), whose partials are combined in order.  Results are bit-identical
  * to mslim_cuda_decode_dense on the same K/V bytes.  A table entry outside
  * [0, n_pages) is not loaded; it is reported by mslim_cuda_device_status and
  * the output rows of its session are undefined (other sessions are

@@ -134,14 +134,14 @@ def test_geometry_rules(m):
 
 def test_decode_workspace_bytes(m):
     g = m.AttentionGeometry.new(32, 8, 128)
-    assert m.decode_workspace_bytes(g, 64, 32768, 2048) == 64 * 32 * 16 * 130 * 4
+    assert m.decode_workspace_bytes(g, 64, 32768, 2048) == 256 + 64 * 32 * 16 * 130 * 4
     with pytest.raises(m.ShapeMismatch):
         m.decode_workspace_bytes(g, 1, 100, 100)
 
 
 def test_split_tokens_for_host_lengths(m):
     """mslim_cuda_decode_split_tokens_for_lengths: a multiple of 64 in
-    [256, 4096], deterministic, and for one rank's share of an 8-GPU C4 run
+    [256, 3072], deterministic, and for one rank's share of an 8-GPU C4 run
     (eight sessions, about 139 K tokens) it keeps the split CTAs within two
     waves of the 296 resident CTAs, where the longest-session policy alone
     would start a nearly empty third wave."""
@@ -149,7 +149,7 @@ def test_split_tokens_for_host_lengths(m):
     g = m.AttentionGeometry.new(32, 8, 128)
     lengths = np.array([32000, 5100, 27000, 9000, 14000, 21000, 4200, 26000], np.int32)
     st = m.decode_split_tokens_for_lengths(g, lengths)
-    assert st % 64 == 0 and 256 <= st <= 4096
+    assert st % 64 == 0 and 256 <= st <= 3072
     assert st == m.decode_split_tokens_for_lengths(g, lengths)
     ctas = sum(-(-int(L) // st) for L in lengths) * 8
     assert ctas <= 2 * 296, (st, ctas)

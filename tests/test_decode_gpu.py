@@ -30,7 +30,7 @@ def run_dense(m, g, q_bits, k_bits, v_bits, lengths=None, split_tokens=0):
     n_seq, max_tokens = k_bits.shape[0], k_bits.shape[1]
     if lengths is None:
         lengths = np.full(n_seq, max_tokens, np.int32)
-    ws = torch.empty(m.decode_workspace_bytes(g, n_seq, max_tokens, split_tokens), dtype=torch.uint8,
+    ws = torch.zeros(m.decode_workspace_bytes(g, n_seq, max_tokens, split_tokens), dtype=torch.uint8,
                      device="cuda:0")
     out = empty_u16((n_seq, g.query_heads, g.head_dim))
     m.decode_dense(g, dev(q_bits), dev(k_bits), dev(v_bits), dev(np.asarray(lengths, np.int32)), n_seq,
@@ -112,7 +112,7 @@ def build_pool(wl, rng, lengths, kvh, d, page_tokens, spare_pages=5, garbage=Tru
 def run_paged(m, g, q, pool, lengths, page_tokens, split_tokens=0):
     torch = torch_mod()
     n_seq = len(lengths)
-    ws = torch.empty(m.decode_workspace_bytes(g, n_seq, pool["max_tokens"], split_tokens), dtype=torch.uint8,
+    ws = torch.zeros(m.decode_workspace_bytes(g, n_seq, pool["max_tokens"], split_tokens), dtype=torch.uint8,
                      device="cuda:0")
     out = empty_u16((n_seq, g.query_heads, g.head_dim))
     kp, vp = dev(pool["k_pool"]), dev(pool["v_pool"])
@@ -240,7 +240,7 @@ def test_paged_decode_reports_page_ids_outside_the_pool(m, wl):
     bad["table"][0, 2] = pool["n_pages"]      # one past the pool
     bad["table"][2, 1] = -1                   # negative
     n_seq = len(lengths)
-    ws = torch.empty(m.decode_workspace_bytes(g, n_seq, pool["max_tokens"]), dtype=torch.uint8, device="cuda:0")
+    ws = torch.zeros(m.decode_workspace_bytes(g, n_seq, pool["max_tokens"]), dtype=torch.uint8, device="cuda:0")
     out = empty_u16((n_seq, qh, d))
     m.decode_paged(g, dev(q), dev(pool["k_pool"]), dev(pool["v_pool"]), pool["n_pages"], pt, dev(bad["table"]),
                    pool["max_pages"], dev(np.asarray(lengths, np.int32)), n_seq, ws, out)
@@ -314,7 +314,7 @@ def _selected_case(m, wl, rng, lengths, counts, max_selected, qh=32, kvh=8, d=12
         for s_, (L, c) in enumerate(zip(lengths, counts)):
             sel[s_, :c] = np.sort(rng.choice(L, size=c, replace=False))
     q = rand_bf16(wl, rng, (n_seq, qh, d))
-    ws = torch.empty(m.decode_selected_workspace_bytes(g, n_seq, max_selected, split_tokens), dtype=torch.uint8,
+    ws = torch.zeros(m.decode_selected_workspace_bytes(g, n_seq, max_selected, split_tokens), dtype=torch.uint8,
                      device="cuda:0")
     out = empty_u16((n_seq, qh, d))
     kd, vd = dev(k), dev(v)
@@ -390,7 +390,7 @@ def test_selected_decode_over_coldstore_pages(m, wl, oracle, page_tokens):
     sel[3, :700] = np.arange(700)                            # every position of session 3
     q = rand_bf16(wl, rng, (n_seq, qh, d))
     st = 128
-    ws = torch.empty(m.decode_selected_workspace_bytes(g, n_seq, cap, st), dtype=torch.uint8, device="cuda:0")
+    ws = torch.zeros(m.decode_selected_workspace_bytes(g, n_seq, cap, st), dtype=torch.uint8, device="cuda:0")
     seq = dev(np.asarray(lengths, np.int32))
     cnt = dev(np.asarray(counts, np.int32))
     kp, vp = dev(pool["k_pool"]), dev(pool["v_pool"])

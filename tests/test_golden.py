@@ -46,7 +46,7 @@ def test_cuda_decode_matches_golden():
     f = load("decode_small.npz")
     qh, kvh, d, t = (int(x) for x in f["geometry"])
     g = m.AttentionGeometry.new(qh, kvh, d)
-    ws = torch.empty(m.decode_workspace_bytes(g, 1, t), dtype=torch.uint8, device="cuda:0")
+    ws = torch.zeros(m.decode_workspace_bytes(g, 1, t), dtype=torch.uint8, device="cuda:0")
     out = empty_u16((1, qh, d))
     m.decode_dense(g, dev(f["q"][None]), dev(f["k"][None]), dev(f["v"][None]), dev(np.array([t], np.int32)),
                    1, t, ws, out)

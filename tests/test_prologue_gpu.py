@@ -114,7 +114,7 @@ def test_rope_append_paged_then_decode_c1(m, wl, oracle, page_tokens):
     q_ref = oracle.rope_rows_bf16(case.q_raw[None], T - 1, case.theta)[0]
     qd = host_u16(q_out)[T - 1]
     assert np.mean(ulps(qd, q_ref) == 0) > 0.99
-    ws = torch.empty(m.decode_workspace_bytes(g, 1, T), dtype=torch.uint8, device="cuda:0")
+    ws = torch.zeros(m.decode_workspace_bytes(g, 1, T), dtype=torch.uint8, device="cuda:0")
     out = empty_u16((1, 32, 128))
     m.decode_paged(g, q_out[T - 1:T], k_pool, v_pool, n_pages, page_tokens,
                    dev(table[None].copy()), len(table), dev(np.array([T], np.int32)), 1, ws, out)

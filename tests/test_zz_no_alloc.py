@@ -61,7 +61,7 @@ def call_static(m, g, c, out, split_tokens):
 
 def call_workspace(m, g, c, split_tokens):
     torch = torch_mod()
-    ws = torch.empty(m.decode_workspace_bytes(g, c["n_seq"], c["max_pages"] * c["page_tokens"], split_tokens),
+    ws = torch.zeros(m.decode_workspace_bytes(g, c["n_seq"], c["max_pages"] * c["page_tokens"], split_tokens),
                      dtype=torch.uint8, device="cuda:0")
     out = empty_u16((c["n_seq"], g.query_heads, g.head_dim))
     m.decode_paged(g, c["q"], c["k"], c["v"], c["n_pages"], c["page_tokens"], c["table"], c["max_pages"],

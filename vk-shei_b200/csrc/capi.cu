@@ -210,8 +210,13 @@ uint32_t policy_split_tokens(uint64_t work_items, uint64_t max_tokens) {
 // head_dim must be a multiple of 8 (16-byte TMA row strides) and at most 256.
 uint32_t kernel_dim_for(uint32_t d) { return d <= 64 ? 64 : d <= 128 ? 128 : 256; }
 
+// Decode workspace: a 256-byte head holding the persistent split kernel's
+// work counter (zero before the first call, left zero by every call), then
+// the split partials.
+constexpr uint64_t kDecodeCounterBytes = 256;
+
 uint64_t partial_bytes(const mslim_geometry_t *g, uint64_t n_seq, uint64_t nq, uint64_t splits) {
-    return n_seq * nq * g->query_heads * splits * (kernel_dim_for(g->head_dim) + 2) * sizeof(float);
+    return kDecodeCounterBytes + n_seq * nq * g->query_heads * splits * (kernel_dim_for(g->head_dim) + 2) * sizeof(float);
 }
 
 struct DecodeCall {
@@ -284,7 +289,8 @@ int run_decode(const DecodeCall &c) {
     p.q_f32 = c.q_f32;
     p.seq_tokens = c.seq_tokens;
     p.page_table = c.page_table;
-    p.partials = static_cast<float *>(c.workspace);
+    p.work_counter = static_cast<unsigned *>(c.workspace);
+    p.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(c.workspace) + kDecodeCounterBytes);
     p.status = status_ptr(dev);
     p.qheads = (int)g->query_heads;
     p.kvheads = (int)g->kv_heads;
@@ -596,17 +602,30 @@ int mslim_cuda_decode_split_tokens_for_lengths(const mslim_geometry_t *geometry,
     const uint32_t kd = kernel_dim_for(geometry->head_dim);
     const uint64_t slots = 148ull * (kd <= 64 ? 3 : kd <= 128 ? 2 : 1);
     const uint64_t per_seq = (uint64_t)geometry->kv_heads * sh.head_chunks;
-    // Every wave of CTAs lasts about one full split (plus a fixed per-CTA cost
-    // of about three 64-token stages), so the step takes about
-    // ceil(CTAs / slots) * (split + 192) token-times: pick the split that
-    // minimises it, the longer split on a tie.
+    // A session of L tokens becomes ceil(L / split) CTAs of equal length
+    // (rounded up to 64 tokens).  Every wave of CTAs lasts about the longest
+    // of them (plus a fixed per-CTA cost of about three 64-token stages), so
+    // the step takes about ceil(CTAs / slots) * (longest + 192) token-times:
+    // pick the split that minimises it, the longer split on a tie.  Splits
+    // above 3072 tokens, and single waves of long CTAs, measured slower than
+    // the model says (no wave left to even out the SMs): at least two waves
+    // are kept whenever the batch has the tokens for them.
     uint64_t best = ~0ull;
     uint32_t best_st = 2048;
-    for (uint32_t st = 256; st <= 4096; st += 64) {
-        uint64_t ctas = 0;
-        for (uint32_t i = 0; i < n_seq; ++i)
-            if (lengths[i] > 0) ctas += ((uint64_t)lengths[i] + st - 1) / st * per_seq;
-        const uint64_t cost = ((ctas + slots - 1) / slots) * (st + 192);
+    uint64_t total = 0;
+    for (uint32_t i = 0; i < n_seq; ++i)
+        if (lengths[i] > 0) total += (uint64_t)lengths[i] * per_seq;
+    const bool two_waves = total >= 2 * slots * 256;
+    for (uint32_t st = 256; st <= 3072; st += 64) {
+        uint64_t ctas = 0, longest = 0;
+        for (uint32_t i = 0; i < n_seq; ++i) {
+            if (lengths[i] <= 0) continue;
+            const uint64_t L = (uint64_t)lengths[i], n = (L + st - 1) / st;
+            ctas += n * per_seq;
+            longest = std::max<uint64_t>(longest, ((L + n - 1) / n + 63) / 64 * 64);
+        }
+        if (two_waves && ctas <= slots) continue;
+        const uint64_t cost = ((ctas + slots - 1) / slots) * (longest + 192);
         if (cost <= best) {
             best = cost;
             best_st = st;
@@ -1330,6 +1349,9 @@ int mslim_cuda_plan_build(const mslim_kernel_config_t *config, const mslim_geome
     if (rc == MSLIM_OK) {
         cudaError_t err = cudaMalloc(&scratch, kPlanScratchBytes);
         if (err != cudaSuccess) rc = cuda_fail(err, "allocate plan split scratch");
+        // the decode work counter at its head starts at zero (calls leave it there)
+        else if ((err = cudaMemset(scratch, 0, kPlanScratchBytes)) != cudaSuccess)
+            rc = cuda_fail(err, "clear plan split scratch");
     }
     cudaSetDevice(prev);
     if (rc) return rc;
@@ -1611,6 +1633,10 @@ int mslim_cuda_backend_decode(mslim_backend_t *b, const mslim_geometry_t *geomet
     uint16_t *dv = reinterpret_cast<uint16_t *>(base + up(q_bytes) + up(kv_bytes));
     float *dout = reinterpret_cast<float *>(base + up(q_bytes) + 2 * up(kv_bytes));
     void *dws = base + up(q_bytes) + 2 * up(kv_bytes) + up(out_bytes);
+    // the buffer is re-cut per call: the decode workspace's counter head is
+    // cleared each time
+    err = cudaMemsetAsync(dws, 0, 256, b->stream);
+    if (err != cudaSuccess) return done(cuda_fail(err, "clear decode workspace"));
     const auto t0 = std::chrono::steady_clock::now();
     // Host staging with zero padding of the head dimension.
     std::vector<float> qpad((size_t)QH * KD, 0.0f);

@@ -6,7 +6,8 @@
 // ColdStore-staged PV of gpu_llm.cl:280-323) with one B200 kernel pair:
 //
 //   mslim_decode_split  one CTA per (split, KV-head chunk, sequence x query
-//                       block).  A producer warp streams 64-token K and V
+//                       block); a sequence's keys are cut into
+//                       ceil(L / split_tokens) splits of equal length.  A producer warp streams 64-token K and V
 //                       tiles with TMA (128-byte swizzle, this GPU's HBM, no
 //                       multicast) through an mbarrier ring; four consumer
 //                       warps each own 16 tokens of every tile.  Rows of the
@@ -24,6 +25,8 @@
 //   acc += p_hi * v + p_lo * v                p split into two bf16 terms, so
 //                                             the PV product keeps ~16 bits of p
 //   out = bf16(sum_s w_s acc_s / sum_s w_s l_s)   fixed split order.
+#include <algorithm>
+
 #include "decode.cuh"
 
 namespace mslim {
@@ -56,6 +59,328 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk) {
     return (uint32_t)((chunk >> 3) * kBoxBytes + row * 128 + (((chunk & 7) ^ (row & 7)) << 4));
 }
 
+// Tokens per split of a run of `tokens` keys: the run is cut into
+// ceil(tokens / split_tokens) splits of equal length (rounded up to the
+// 64-token stage), so no split is a short remainder and the CTAs of a decode
+// take about the same time.  The last split may be shorter by < 64 tokens
+// per split.  0 for an empty run.
+__device__ __forceinline__ int split_len(int tokens, int split_tokens) {
+    if (tokens <= 0) return 0;
+    const int n = (tokens + split_tokens - 1) / split_tokens;
+    return ((tokens + n - 1) / n + kTileT - 1) / kTileT * kTileT;
+}
+
+// Loads the K and V tile at token t0 of (seq, kvh) into stage buffers kdst /
+// vdst, completing on `bar`.  Paged: a page-table entry outside the pool is
+// reported and nothing is loaded; the stage completes without bytes so the
+// consumers do not wait (that session's output is then undefined and the
+// status word says so).
+template <int D, bool PAGED>
+__device__ __forceinline__ void issue_tile(const CUtensorMap *kmap, const CUtensorMap *vmap, const DecodeParams &p,
+                                           uint64_t *bar, uint8_t *kdst, uint8_t *vdst, int seq, int kvh, int t0) {
+    using S = Shape<D>;
+    if constexpr (PAGED) {
+        const int lp = t0 / p.page_tokens;
+        const int off = t0 - lp * p.page_tokens;
+        const int phys = p.page_table[(size_t)seq * p.max_pages + lp];
+        if (phys < 0 || phys >= p.n_pages) {
+            if (p.status) atomicExch(p.status, MSLIM_DEVICE_BAD_PAGE_CODE);
+            mbar_arrive(bar);
+            return;
+        }
+        mbar_arrive_expect_tx(bar, S::kStageBytes);
+        const int z = phys * p.kvheads + kvh;
+#pragma unroll
+        for (int b = 0; b < S::kBoxes; ++b) {
+            tma_load_3d(kdst + b * kBoxBytes, kmap, bar, b * 64, off, z);
+            tma_load_3d(vdst + b * kBoxBytes, vmap, bar, b * 64, off, z);
+        }
+    } else {
+        mbar_arrive_expect_tx(bar, S::kStageBytes);
+#pragma unroll
+        for (int b = 0; b < S::kBoxes; ++b) {
+            tma_load_4d(kdst + b * kBoxBytes, kmap, bar, b * 64, kvh, t0, seq);
+            tma_load_4d(vdst + b * kBoxBytes, vmap, bar, b * 64, kvh, t0, seq);
+        }
+    }
+}
+
+// The (query, head) rows of one CTA's work item and where they sit: rows
+// r = query (qg_first + r / hc) x head (kvh * group + hchunk * hc + r % hc).
+struct DecodeItem {
+    int seq, kvh, hchunk, qg_first, qg_last, prior, split;
+};
+
+// One consumer warp's share of a work item: MMA rows are the item's (query,
+// head) rows, the warp owns 16 tokens of every 64-token tile, keeps its own
+// online-softmax state, and the four warps are combined in warp order at the
+// end of the item.
+template <int D, bool QSPLIT>
+struct DecodeConsumer {
+    using S = Shape<D>;
+    uint32_t qa[S::kKSteps][4];
+    uint32_t qb[QSPLIT ? S::kKSteps : 1][4];
+    int row_limit[2];
+    bool row_ok[2];
+    int row_q[2];
+    float o[S::kNTiles][4];
+    float m_run[2], l_run[2];
+
+    // A fragments of Q (16 rows x 16 dims per k-step) and a fresh state.
+    // With QSPLIT the query arrives as f32 and is carried as qa (bf16 of q) +
+    // qb (bf16 of the remainder), two MMAs per k-step.
+    __device__ __forceinline__ void begin(const DecodeParams &p, const DecodeItem &it, int lane) {
+        const int g = lane >> 2, c = lane & 3;
+        const int hc = p.heads_per_cta;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int r = g + 8 * h;
+            row_q[h] = it.qg_first + r / hc;
+            row_ok[h] = (r < p.q_per_cta * hc) && (row_q[h] <= it.qg_last);
+            row_limit[h] = row_ok[h] ? it.prior + row_q[h] : -1;  // last visible token
+        }
+#pragma unroll
+        for (int ks = 0; ks < S::kKSteps; ++ks) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int r = g + 8 * h;
+                uint32_t k0 = 0, k8 = 0, k0r = 0, k8r = 0;
+                if (row_ok[h]) {
+                    const int qh = it.kvh * p.group + it.hchunk * hc + r % hc;
+                    const int d0 = ks * 16 + 2 * c;  // dims d0, d0+1 and d0+8, d0+9
+                    const size_t off = (((size_t)it.seq * p.nq + row_q[h]) * p.qheads + qh) * p.head_dim + d0;
+                    if constexpr (QSPLIT) {
+                        const float2 f0 = d0 < p.head_dim ? *reinterpret_cast<const float2 *>(p.q_f32 + off)
+                                                          : make_float2(0.f, 0.f);
+                        const float2 f8 = d0 + 8 < p.head_dim ? *reinterpret_cast<const float2 *>(p.q_f32 + off + 8)
+                                                              : make_float2(0.f, 0.f);
+                        k0 = pack_bf16x2(f0.x, f0.y);
+                        k8 = pack_bf16x2(f8.x, f8.y);
+                        k0r = pack_bf16x2(f0.x - bf16lo_f32(k0), f0.y - bf16hi_f32(k0));
+                        k8r = pack_bf16x2(f8.x - bf16lo_f32(k8), f8.y - bf16hi_f32(k8));
+                    } else {
+                        k0 = d0 < p.head_dim ? ld_u32(p.q + off) : 0u;
+                        k8 = d0 + 8 < p.head_dim ? ld_u32(p.q + off + 8) : 0u;
+                    }
+                }
+                qa[ks][h] = k0;      // a0 (row g) / a1 (row g+8): k = 2c, 2c+1
+                qa[ks][2 + h] = k8;  // a2 / a3: k = 2c+8, 2c+9
+                if constexpr (QSPLIT) {
+                    qb[ks][h] = k0r;
+                    qb[ks][2 + h] = k8r;
+                }
+            }
+        }
+#pragma unroll
+        for (int n = 0; n < S::kNTiles; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+        m_run[0] = m_run[1] = -INFINITY;
+        l_run[0] = l_run[1] = 0.f;
+    }
+
+    // This warp's 16 tokens of the 64-token tile at token tile_t0 (stage s),
+    // keys below t_end.
+    __device__ __forceinline__ void tile(uint8_t *stage, int tile_t0, int t_end, float scale, int warp, int lane) {
+        const int g = lane >> 2, c = lane & 3;
+        const int row0 = warp * kWarpTokens;
+        const int t0 = tile_t0 + row0;
+        const int valid = min(kWarpTokens, t_end - t0);
+        if (valid <= 0) return;
+        const uint32_t kt = smem_u32(stage);
+        const uint32_t vt = kt + S::kTensorBytes;
+        if (valid < kWarpTokens) {
+            // Rows past the sequence end hold whatever the page or cache held;
+            // zero their V so p == 0 cannot meet a NaN/Inf payload.
+            uint8_t *vrow = stage + S::kTensorBytes;
+            for (int x = lane; x < (kWarpTokens - valid) * S::kBoxes * 8; x += 32) {
+                const int r = row0 + valid + x / (S::kBoxes * 8);
+                const int ch = x % (S::kBoxes * 8);
+                *reinterpret_cast<uint4 *>(vrow + swz(r, ch)) = make_uint4(0, 0, 0, 0);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+        }
+        // ---- S = Q K^T for this warp's 16 tokens (two n-tiles of 8) ----
+        float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+        for (int j = 0; j < D / 32; ++j) {
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+                const int r = row0 + nt * 8 + (lane & 7);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4(kt + swz(r, 4 * j + (lane >> 3)), b0, b1, b2, b3);
+                mma_bf16_16816(sc[nt], qa[2 * j], b0, b1);
+                mma_bf16_16816(sc[nt], qa[2 * j + 1], b2, b3);
+                if constexpr (QSPLIT) {
+                    mma_bf16_16816(sc[nt], qb[2 * j], b0, b1);
+                    mma_bf16_16816(sc[nt], qb[2 * j + 1], b2, b3);
+                }
+            }
+        }
+        // ---- online softmax over the 16 tokens (rows g, g+8) ----
+        float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int h = e >> 1;
+                const int tok = t0 + nt * 8 + 2 * c + (e & 1);
+                const float v = (tok <= row_limit[h]) ? sc[nt][e] * scale : -INFINITY;
+                sc[nt][e] = v;
+                mx[h] = fmaxf(mx[h], v);
+            }
+        float alpha[2], base[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+            mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+            const float m_new = fmaxf(m_run[h], mx[h]);
+            base[h] = (m_new == -INFINITY) ? 0.f : m_new;
+            alpha[h] = fast_exp2(m_run[h] - base[h]);
+            m_run[h] = m_new;
+        }
+        float ps[2] = {0.f, 0.f};
+        uint32_t phi[4], plo[4];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const float p0 = fast_exp2(sc[nt][2 * h] - base[h]);
+                const float p1 = fast_exp2(sc[nt][2 * h + 1] - base[h]);
+                ps[h] += p0 + p1;
+                const uint32_t hi = pack_bf16x2(p0, p1);
+                const uint32_t lo = pack_bf16x2(p0 - bf16lo_f32(hi), p1 - bf16hi_f32(hi));
+                // A fragment of P (16 rows x 16 tokens): a0 = (g, 2c..), a1 = (g+8, 2c..),
+                // a2 = (g, 2c+8..), a3 = (g+8, 2c+8..).
+                phi[nt * 2 + h] = hi;
+                plo[nt * 2 + h] = lo;
+            }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) l_run[h] = l_run[h] * alpha[h] + ps[h];
+#pragma unroll
+        for (int n = 0; n < S::kNTiles; ++n) {
+            o[n][0] *= alpha[0];
+            o[n][1] *= alpha[0];
+            o[n][2] *= alpha[1];
+            o[n][3] *= alpha[1];
+        }
+        // ---- O += P V (V^T fragments via transposed ldmatrix) ----
+        const uint32_t pa_hi[4] = {phi[0], phi[1], phi[2], phi[3]};
+        const uint32_t pa_lo[4] = {plo[0], plo[1], plo[2], plo[3]};
+#pragma unroll
+        for (int j = 0; j < D / 16; ++j) {
+            const int mtx = lane >> 3;
+            const int r = row0 + (mtx & 1) * 8 + (lane & 7);
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4_trans(vt + swz(r, 2 * j + (mtx >> 1)), b0, b1, b2, b3);
+            mma_bf16_16816(o[2 * j], pa_hi, b0, b1);
+            mma_bf16_16816(o[2 * j], pa_lo, b0, b1);
+            mma_bf16_16816(o[2 * j + 1], pa_hi, b2, b3);
+            mma_bf16_16816(o[2 * j + 1], pa_lo, b2, b3);
+        }
+    }
+
+    // The four warps' states combined in warp order into the item's split
+    // partial {acc[D], m, l}.  Warps 1-3 hand their states over through
+    // `scratch` ([3][16 rows][D + 2] floats, a stage buffer every consumer is
+    // done with); warp 0 combines them with its own, which it keeps in
+    // registers.  Same arithmetic and order for every row and dim, whatever
+    // kernel runs the item.
+    __device__ __forceinline__ void finish(const DecodeParams &p, const DecodeItem &it, float *scratch, int warp,
+                                           int lane) {
+        constexpr int kRowF = D + 2;
+        const int g = lane >> 2, c = lane & 3;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 1);
+            l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 2);
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");  // the stage is read
+        if (warp > 0) {
+            float *mine = scratch + (warp - 1) * 16 * kRowF;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int r = g + 8 * h;
+                if (c == 0) {
+                    mine[r * kRowF + D] = m_run[h];
+                    mine[r * kRowF + D + 1] = l_run[h];
+                }
+#pragma unroll
+                for (int n = 0; n < S::kNTiles; ++n) {
+                    mine[r * kRowF + n * 8 + 2 * c] = o[n][2 * h];
+                    mine[r * kRowF + n * 8 + 2 * c + 1] = o[n][2 * h + 1];
+                }
+            }
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+        if (warp == 0) {
+            const int hc = p.heads_per_cta;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                if (!row_ok[h]) continue;
+                const int r = g + 8 * h;
+                float mw[kConsumerWarps], lw[kConsumerWarps], wgt[kConsumerWarps];
+                mw[0] = m_run[h];
+                lw[0] = l_run[h];
+#pragma unroll
+                for (int w = 1; w < kConsumerWarps; ++w) {
+                    mw[w] = scratch[((w - 1) * 16 + r) * kRowF + D];
+                    lw[w] = scratch[((w - 1) * 16 + r) * kRowF + D + 1];
+                }
+                float m = -INFINITY;
+#pragma unroll
+                for (int w = 0; w < kConsumerWarps; ++w) m = fmaxf(m, mw[w]);
+                const float mb = (m == -INFINITY) ? 0.f : m;
+                float l = 0.f;
+#pragma unroll
+                for (int w = 0; w < kConsumerWarps; ++w) {
+                    wgt[w] = fast_exp2(mw[w] - mb);
+                    l += wgt[w] * lw[w];
+                }
+                const int qh = it.kvh * p.group + it.hchunk * hc + r % hc;
+                float *dst = p.partials +
+                             ((((size_t)it.seq * p.nq + row_q[h]) * p.qheads + qh) * p.max_splits + it.split) * kRowF;
+#pragma unroll
+                for (int n = 0; n < S::kNTiles; ++n) {
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const int d = n * 8 + 2 * c + e;
+                        float a = 0.f;
+                        a += wgt[0] * o[n][2 * h + e];
+#pragma unroll
+                        for (int w = 1; w < kConsumerWarps; ++w) a += wgt[w] * scratch[((w - 1) * 16 + r) * kRowF + d];
+                        dst[d] = a;
+                    }
+                }
+                if (c == 0) {
+                    dst[D] = m;
+                    dst[D + 1] = l;
+                }
+            }
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");  // scratch is free again
+    }
+};
+
+// Causal extent of the query block `qblock` of sequence `seq`: query row qg
+// (0-based among the nq new rows) sees tokens [0, prior + qg]; cta_end is the
+// exclusive token bound of the block; 0 splits for an empty block.
+struct UnitExtent {
+    int ntok, prior, qg_first, qg_last, cta_end, slen, splits;
+};
+__device__ __forceinline__ UnitExtent unit_extent(const DecodeParams &p, int seq, int qblock) {
+    UnitExtent u;
+    u.ntok = min(p.token_cap, p.fixed_tokens >= 0 ? p.fixed_tokens : p.seq_tokens[seq]);
+    u.prior = u.ntok - p.nq;
+    u.qg_first = qblock * p.q_per_cta;
+    u.qg_last = min(p.nq, u.qg_first + p.q_per_cta) - 1;
+    u.cta_end = u.prior + u.qg_last + 1;
+    const bool empty = u.ntok <= 0 || u.cta_end <= 0;
+    u.slen = empty ? 0 : split_len(u.cta_end, p.split_tokens);
+    u.splits = empty ? 0 : min((int)p.max_splits, (u.cta_end + u.slen - 1) / u.slen);
+    return u;
+}
+
+// One CTA per (split, KV-head chunk, sequence x query block).
 template <int D, int STAGES, bool PAGED, bool QSPLIT>
 __global__ void __launch_bounds__(kThreads)
     mslim_decode_split(const __grid_constant__ CUtensorMap kmap,
@@ -71,22 +396,18 @@ __global__ void __launch_bounds__(kThreads)
     // previous merge may still read) are touched only after the predecessor
     griddep_launch_dependents();
     griddep_wait();
-    const int split = blockIdx.x;
-    const int kvh = blockIdx.y / p.head_chunks;
-    const int hchunk = blockIdx.y % p.head_chunks;
-    const int seq = blockIdx.z / p.q_blocks;
-    const int qblock = blockIdx.z % p.q_blocks;
-
-    // Causal extent of this CTA: query row qg (0-based among the nq new rows)
-    // sees tokens [0, prior + qg], prior = tokens - nq.
-    const int ntok = min(p.token_cap, p.fixed_tokens >= 0 ? p.fixed_tokens : p.seq_tokens[seq]);
-    const int prior = ntok - p.nq;
-    const int qg_first = qblock * p.q_per_cta;
-    const int qg_last = min(p.nq, qg_first + p.q_per_cta) - 1;
-    const int cta_end = prior + qg_last + 1;  // exclusive token bound of the block
-    const int t_begin = split * p.split_tokens;
-    if (ntok <= 0 || cta_end <= 0 || t_begin >= cta_end) return;  // CTA-uniform
-    const int t_end = min(cta_end, t_begin + p.split_tokens);
+    DecodeItem it;
+    it.split = blockIdx.x;
+    it.kvh = blockIdx.y / p.head_chunks;
+    it.hchunk = blockIdx.y % p.head_chunks;
+    it.seq = blockIdx.z / p.q_blocks;
+    const UnitExtent u = unit_extent(p, it.seq, blockIdx.z % p.q_blocks);
+    it.prior = u.prior;
+    it.qg_first = u.qg_first;
+    it.qg_last = u.qg_last;
+    if (it.split >= u.splits) return;  // CTA-uniform
+    const int t_begin = it.split * u.slen;
+    const int t_end = min(u.cta_end, t_begin + u.slen);
     const int ntiles = (t_end - t_begin + kTileT - 1) / kTileT;
 
     const int warp = threadIdx.x >> 5;
@@ -109,38 +430,9 @@ __global__ void __launch_bounds__(kThreads)
             for (int i = 0; i < ntiles; ++i) {
                 const int s = i % STAGES;
                 if (!mbar_wait(&empty[s], ((i / STAGES) & 1) ^ 1, p.status, 1)) break;
-                const int t0 = t_begin + i * kTileT;
                 uint8_t *kdst = smem + s * S::kStageBytes;
-                uint8_t *vdst = kdst + S::kTensorBytes;
-                if constexpr (PAGED) {
-                    const int lp = t0 / p.page_tokens;
-                    const int off = t0 - lp * p.page_tokens;
-                    const int phys = p.page_table[(size_t)seq * p.max_pages + lp];
-                    if (phys < 0 || phys >= p.n_pages) {
-                        // A table entry outside the pool: report it and load
-                        // nothing; the stage completes without bytes so the
-                        // consumers do not wait (the output is then undefined
-                        // and the status word says so).
-                        if (p.status) atomicExch(p.status, MSLIM_DEVICE_BAD_PAGE_CODE);
-                        mbar_arrive(&full[s]);
-                        issued = i + 1;
-                        continue;
-                    }
-                    mbar_arrive_expect_tx(&full[s], S::kStageBytes);
-                    const int z = phys * p.kvheads + kvh;
-#pragma unroll
-                    for (int b = 0; b < S::kBoxes; ++b) {
-                        tma_load_3d(kdst + b * kBoxBytes, &kmap, &full[s], b * 64, off, z);
-                        tma_load_3d(vdst + b * kBoxBytes, &vmap, &full[s], b * 64, off, z);
-                    }
-                } else {
-                    mbar_arrive_expect_tx(&full[s], S::kStageBytes);
-#pragma unroll
-                    for (int b = 0; b < S::kBoxes; ++b) {
-                        tma_load_4d(kdst + b * kBoxBytes, &kmap, &full[s], b * 64, kvh, t0, seq);
-                        tma_load_4d(vdst + b * kBoxBytes, &vmap, &full[s], b * 64, kvh, t0, seq);
-                    }
-                }
+                issue_tile<D, PAGED>(&kmap, &vmap, p, &full[s], kdst, kdst + S::kTensorBytes, it.seq, it.kvh,
+                                     t_begin + i * kTileT);
                 issued = i + 1;
             }
             // Do not retire while our copies may still be landing in this CTA's
@@ -152,241 +444,181 @@ __global__ void __launch_bounds__(kThreads)
     }
 
     // ----------------------------------------------------------- consumers --
-    const int g = lane >> 2;  // fragment row (and row + 8)
-    const int c = lane & 3;   // fragment column pair
-    const int hc = p.heads_per_cta;
-    // MMA row r <-> (query qg_first + r / hc, head kvh*group + hchunk*hc + r % hc)
-    int row_q[2], row_limit[2];
-    bool row_ok[2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const int r = g + 8 * h;
-        const int qi = r / hc;
-        row_q[h] = qg_first + qi;
-        row_ok[h] = (r < p.q_per_cta * hc) && (row_q[h] <= qg_last);
-        row_limit[h] = row_ok[h] ? prior + row_q[h] : -1;  // last visible token
-    }
-
-    // A fragments of Q (16 rows x 16 dims per k-step).  With QSPLIT the query
-    // arrives as f32 and is carried as qa (bf16 of q) + qb (bf16 of the
-    // remainder), two MMAs per k-step.
-    uint32_t qa[S::kKSteps][4];
-    uint32_t qb[QSPLIT ? S::kKSteps : 1][4];
-#pragma unroll
-    for (int ks = 0; ks < S::kKSteps; ++ks) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int r = g + 8 * h;
-            uint32_t k0 = 0, k8 = 0, k0r = 0, k8r = 0;
-            if (row_ok[h]) {
-                const int qh = kvh * p.group + hchunk * hc + r % hc;
-                const int d0 = ks * 16 + 2 * c;  // dims d0, d0+1 and d0+8, d0+9
-                const size_t off =
-                    (((size_t)seq * p.nq + row_q[h]) * p.qheads + qh) * p.head_dim + d0;
-                if constexpr (QSPLIT) {
-                    const float2 f0 = d0 < p.head_dim
-                                          ? *reinterpret_cast<const float2 *>(p.q_f32 + off)
-                                          : make_float2(0.f, 0.f);
-                    const float2 f8 = d0 + 8 < p.head_dim
-                                          ? *reinterpret_cast<const float2 *>(p.q_f32 + off + 8)
-                                          : make_float2(0.f, 0.f);
-                    k0 = pack_bf16x2(f0.x, f0.y);
-                    k8 = pack_bf16x2(f8.x, f8.y);
-                    k0r = pack_bf16x2(f0.x - bf16lo_f32(k0), f0.y - bf16hi_f32(k0));
-                    k8r = pack_bf16x2(f8.x - bf16lo_f32(k8), f8.y - bf16hi_f32(k8));
-                } else {
-                    k0 = d0 < p.head_dim ? ld_u32(p.q + off) : 0u;
-                    k8 = d0 + 8 < p.head_dim ? ld_u32(p.q + off + 8) : 0u;
-                }
-            }
-            qa[ks][h] = k0;      // a0 (row g) / a1 (row g+8): k = 2c, 2c+1
-            qa[ks][2 + h] = k8;  // a2 / a3: k = 2c+8, 2c+9
-            if constexpr (QSPLIT) {
-                qb[ks][h] = k0r;
-                qb[ks][2 + h] = k8r;
-            }
-        }
-    }
-
-    float o[S::kNTiles][4];
-#pragma unroll
-    for (int n = 0; n < S::kNTiles; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-    float m_run[2] = {-INFINITY, -INFINITY};
-    float l_run[2] = {0.f, 0.f};
-    const float scale = p.scale_log2;
-    const uint32_t smem_base = smem_u32(smem);
-
+    DecodeConsumer<D, QSPLIT> cs;
+    cs.begin(p, it, lane);
     for (int i = 0; i < ntiles; ++i) {
         const int s = i % STAGES;
         if (!mbar_wait(&full[s], (i / STAGES) & 1, p.status, 3)) break;
-        const int row0 = warp * kWarpTokens;
-        const int t0 = t_begin + i * kTileT + row0;
-        const int valid = min(kWarpTokens, t_end - t0);
-        if (valid > 0) {
-            const uint32_t kt = smem_base + s * S::kStageBytes;
-            const uint32_t vt = kt + S::kTensorBytes;
-            if (valid < kWarpTokens) {
-                // Rows past the sequence end hold whatever the page or cache held;
-                // zero their V so p == 0 cannot meet a NaN/Inf payload.
-                uint8_t *vrow = smem + s * S::kStageBytes + S::kTensorBytes;
-                for (int x = lane; x < (kWarpTokens - valid) * S::kBoxes * 8; x += 32) {
-                    const int r = row0 + valid + x / (S::kBoxes * 8);
-                    const int ch = x % (S::kBoxes * 8);
-                    *reinterpret_cast<uint4 *>(vrow + swz(r, ch)) = make_uint4(0, 0, 0, 0);
-                }
-                fence_proxy_async_smem();
-                __syncwarp();
-            }
-            // ---- S = Q K^T for this warp's 16 tokens (two n-tiles of 8) ----
-            float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-#pragma unroll
-            for (int j = 0; j < D / 32; ++j) {
-#pragma unroll
-                for (int nt = 0; nt < 2; ++nt) {
-                    const int r = row0 + nt * 8 + (lane & 7);
-                    uint32_t b0, b1, b2, b3;
-                    ldsm_x4(kt + swz(r, 4 * j + (lane >> 3)), b0, b1, b2, b3);
-                    mma_bf16_16816(sc[nt], qa[2 * j], b0, b1);
-                    mma_bf16_16816(sc[nt], qa[2 * j + 1], b2, b3);
-                    if constexpr (QSPLIT) {
-                        mma_bf16_16816(sc[nt], qb[2 * j], b0, b1);
-                        mma_bf16_16816(sc[nt], qb[2 * j + 1], b2, b3);
-                    }
-                }
-            }
-            // ---- online softmax over the 16 tokens (rows g, g+8) ----
-            float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int h = e >> 1;
-                    const int tok = t0 + nt * 8 + 2 * c + (e & 1);
-                    const float v = (tok <= row_limit[h]) ? sc[nt][e] * scale : -INFINITY;
-                    sc[nt][e] = v;
-                    mx[h] = fmaxf(mx[h], v);
-                }
-            float alpha[2], base[2];
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
-                mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
-                const float m_new = fmaxf(m_run[h], mx[h]);
-                base[h] = (m_new == -INFINITY) ? 0.f : m_new;
-                alpha[h] = fast_exp2(m_run[h] - base[h]);
-                m_run[h] = m_new;
-            }
-            float ps[2] = {0.f, 0.f};
-            uint32_t phi[4], plo[4];
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const float p0 = fast_exp2(sc[nt][2 * h] - base[h]);
-                    const float p1 = fast_exp2(sc[nt][2 * h + 1] - base[h]);
-                    ps[h] += p0 + p1;
-                    const uint32_t hi = pack_bf16x2(p0, p1);
-                    const uint32_t lo = pack_bf16x2(p0 - bf16lo_f32(hi), p1 - bf16hi_f32(hi));
-                    // A fragment of P (16 rows x 16 tokens): a0 = (g, 2c..), a1 = (g+8, 2c..),
-                    // a2 = (g, 2c+8..), a3 = (g+8, 2c+8..).
-                    phi[nt * 2 + h] = hi;
-                    plo[nt * 2 + h] = lo;
-                }
-#pragma unroll
-            for (int h = 0; h < 2; ++h) l_run[h] = l_run[h] * alpha[h] + ps[h];
-#pragma unroll
-            for (int n = 0; n < S::kNTiles; ++n) {
-                o[n][0] *= alpha[0];
-                o[n][1] *= alpha[0];
-                o[n][2] *= alpha[1];
-                o[n][3] *= alpha[1];
-            }
-            // ---- O += P V (V^T fragments via transposed ldmatrix) ----
-            const uint32_t pa_hi[4] = {phi[0], phi[1], phi[2], phi[3]};
-            const uint32_t pa_lo[4] = {plo[0], plo[1], plo[2], plo[3]};
-#pragma unroll
-            for (int j = 0; j < D / 16; ++j) {
-                const int mtx = lane >> 3;
-                const int r = row0 + (mtx & 1) * 8 + (lane & 7);
-                uint32_t b0, b1, b2, b3;
-                ldsm_x4_trans(vt + swz(r, 2 * j + (mtx >> 1)), b0, b1, b2, b3);
-                mma_bf16_16816(o[2 * j], pa_hi, b0, b1);
-                mma_bf16_16816(o[2 * j], pa_lo, b0, b1);
-                mma_bf16_16816(o[2 * j + 1], pa_hi, b2, b3);
-                mma_bf16_16816(o[2 * j + 1], pa_lo, b2, b3);
-            }
-        }
+        cs.tile(smem + s * S::kStageBytes, t_begin + i * kTileT, t_end, p.scale_log2, warp, lane);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }
-
-    // ---- combine the four warps' states (fixed warp order) ----
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 1);
-        l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 2);
-    }
     // All consumers are done with the ring (the producer has issued nothing
-    // further), so its first stage is reused as [warp][16 rows][D + 2] floats.
-    asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
-    float *st = reinterpret_cast<float *>(smem);
-    constexpr int kRowF = D + 2;
-    float *mine = st + warp * 16 * kRowF;
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const int r = g + 8 * h;
-        if (c == 0) {
-            mine[r * kRowF + D] = m_run[h];
-            mine[r * kRowF + D + 1] = l_run[h];
+    // further), so its first stage is the combine's scratch.
+    cs.finish(p, it, reinterpret_cast<float *>(smem), warp, lane);
+}
+
+// What the producer of the persistent kernel tells the consumers about each
+// stage it fills: the work item, the tile and whether it opens or closes the
+// item's split (or ends the CTA's work).
+struct StageMeta {
+    int seq, kvh, hchunk, split, prior, qg_first, qg_last;
+    int t0, t_end, flags;
+};
+constexpr int kMetaFirst = 1, kMetaLast = 2, kMetaDone = 4;
+constexpr int kMaxUnits = 256;  // (sequence, query block) pairs the persistent kernel takes
+
+// Persistent form: a fixed grid of resident CTAs takes (item, split) work
+// units from a counter in the workspace (the merge puts it back to zero), so
+// fast SMs take more splits and no wave leaves SMs idle; each split is
+// computed exactly as mslim_decode_split computes it (same tiles, same warp
+// order), so the partials -- and the outputs -- are the same bits.  The
+// producer numbers the work: the splits of every (sequence, query block)
+// unit (a prefix sum over at most kMaxUnits units, in shared memory) times
+// the KV-head chunks.
+template <int D, int STAGES, bool PAGED>
+__global__ void __launch_bounds__(kThreads)
+    mslim_decode_persist(const __grid_constant__ CUtensorMap kmap,
+                         const __grid_constant__ CUtensorMap vmap, const DecodeParams p) {
+    using S = Shape<D>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * S::kStageBytes);
+    uint64_t *empty = full + STAGES;
+    StageMeta *meta = reinterpret_cast<StageMeta *>(empty + STAGES);
+    int *prefix = reinterpret_cast<int *>(meta + STAGES);  // [kMaxUnits + 1]
+
+    griddep_launch_dependents();
+    griddep_wait();  // inputs, and the counter the previous merge reset
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
         }
-#pragma unroll
-        for (int n = 0; n < S::kNTiles; ++n) {
-            mine[r * kRowF + n * 8 + 2 * c] = o[n][2 * h];
-            mine[r * kRowF + n * 8 + 2 * c + 1] = o[n][2 * h + 1];
-        }
+        fence_mbarrier_init();
     }
-    asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
-    const int rows = p.q_per_cta * hc;
-    for (int x = threadIdx.x; x < rows * (D / 2); x += kConsumerWarps * 32) {
-        const int r = x / (D / 2);
-        const int d = (x % (D / 2)) * 2;
-        const int qg = qg_first + r / hc;
-        if (qg > qg_last) continue;
-        float m = -INFINITY;
+    __syncthreads();
+
+    if (warp == kConsumerWarps) {
+        // ------------------------------------------------------ producer --
+        // splits per unit, eight units per lane, then a warp-wide prefix sum
+        const int units = p.n_seq * p.q_blocks;
+        int cnt[kMaxUnits / 32];
+        int local = 0;
 #pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) m = fmaxf(m, st[(w * 16 + r) * kRowF + D]);
-        const float mb = (m == -INFINITY) ? 0.f : m;
-        float l = 0.f, a0 = 0.f, a1 = 0.f;
+        for (int k = 0; k < kMaxUnits / 32; ++k) {
+            const int uix = lane * (kMaxUnits / 32) + k;
+            cnt[k] = uix < units ? unit_extent(p, uix / p.q_blocks, uix % p.q_blocks).splits : 0;
+            local += cnt[k];
+        }
+        int incl = local;
 #pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) {
-            const float *src = st + (w * 16 + r) * kRowF;
-            const float wgt = fast_exp2(src[D] - mb);
-            l += wgt * src[D + 1];
-            a0 += wgt * src[d];
-            a1 += wgt * src[d + 1];
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
         }
-        const int qh = kvh * p.group + hchunk * hc + r % hc;
-        float *dst = p.partials +
-                     ((((size_t)seq * p.nq + qg) * p.qheads + qh) * p.max_splits + split) * kRowF;
-        dst[d] = a0;
-        dst[d + 1] = a1;
-        if (d == 0) {
-            dst[D] = m;
-            dst[D + 1] = l;
+        int run = incl - local;
+#pragma unroll
+        for (int k = 0; k < kMaxUnits / 32; ++k) {
+            prefix[lane * (kMaxUnits / 32) + k] = run;
+            run += cnt[k];
         }
+        if (lane == 31) prefix[kMaxUnits] = incl;
+        __syncwarp();
+        if (lane == 0) {
+            prefetch_tmap(&kmap);
+            prefetch_tmap(&vmap);
+            const int H = p.kvheads * p.head_chunks;
+            const long long total = (long long)prefix[kMaxUnits] * H;
+            int i = 0;  // stages filled so far
+            bool ok = true;
+            long long g = atomicAdd(p.work_counter, 1u);
+            while (ok && g < total) {
+                const int w = (int)(g / H), hcid = (int)(g % H);
+                int lo = 0, hi = units;  // the last unit whose prefix is <= w
+                while (hi - lo > 1) {
+                    const int mid = (lo + hi) >> 1;
+                    if (prefix[mid] <= w) lo = mid;
+                    else hi = mid;
+                }
+                const int seq = lo / p.q_blocks;
+                const UnitExtent u = unit_extent(p, seq, lo % p.q_blocks);
+                const int split = w - prefix[lo];
+                const int t_begin = split * u.slen;
+                const int t_end = min(u.cta_end, t_begin + u.slen);
+                const int ntiles = (t_end - t_begin + kTileT - 1) / kTileT;
+                const long long g_next = atomicAdd(p.work_counter, 1u);  // in flight during the loads
+                for (int t = 0; t < ntiles; ++t, ++i) {
+                    const int s = i % STAGES;
+                    if (!mbar_wait(&empty[s], ((i / STAGES) & 1) ^ 1, p.status, 4)) {
+                        ok = false;
+                        break;
+                    }
+                    StageMeta &m = meta[s];
+                    m.seq = seq;
+                    m.kvh = hcid / p.head_chunks;
+                    m.hchunk = hcid % p.head_chunks;
+                    m.split = split;
+                    m.prior = u.prior;
+                    m.qg_first = u.qg_first;
+                    m.qg_last = u.qg_last;
+                    m.t0 = t_begin + t * kTileT;
+                    m.t_end = t_end;
+                    m.flags = (t == 0 ? kMetaFirst : 0) | (t == ntiles - 1 ? kMetaLast : 0);
+                    uint8_t *kdst = smem + s * S::kStageBytes;
+                    issue_tile<D, PAGED>(&kmap, &vmap, p, &full[s], kdst, kdst + S::kTensorBytes, seq, m.kvh, m.t0);
+                }
+                g = g_next;
+            }
+            if (ok) {  // the end of this CTA's work: a stage with no bytes
+                const int s = i % STAGES;
+                if (mbar_wait(&empty[s], ((i / STAGES) & 1) ^ 1, p.status, 4)) {
+                    meta[s].flags = kMetaDone;
+                    mbar_arrive(&full[s]);
+                    ++i;
+                }
+            }
+            // Do not retire while our copies may still be landing in this CTA's
+            // shared memory: wait (bounded) for the last stages filled.
+            for (int k = max(0, i - STAGES); k < i; ++k) mbar_wait(&full[k % STAGES], (k / STAGES) & 1, p.status, 2);
+        }
+        return;
+    }
+
+    // ----------------------------------------------------------- consumers --
+    DecodeConsumer<D, false> cs;
+    DecodeItem it{};
+    for (int i = 0;; ++i) {
+        const int s = i % STAGES;
+        if (!mbar_wait(&full[s], (i / STAGES) & 1, p.status, 3)) break;
+        const StageMeta m = meta[s];
+        if (m.flags & kMetaDone) break;
+        uint8_t *stage = smem + s * S::kStageBytes;
+        if (m.flags & kMetaFirst) {
+            it.seq = m.seq;
+            it.kvh = m.kvh;
+            it.hchunk = m.hchunk;
+            it.split = m.split;
+            it.prior = m.prior;
+            it.qg_first = m.qg_first;
+            it.qg_last = m.qg_last;
+            cs.begin(p, it, lane);
+        }
+        cs.tile(stage, m.t0, m.t_end, p.scale_log2, warp, lane);
+        // the split's last stage is the combine's scratch before it is released
+        if (m.flags & kMetaLast) cs.finish(p, it, reinterpret_cast<float *>(stage), warp, lane);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
     }
 }
 
 // Splits whose partials feed (sequence, query row qg): the same count the
-// split kernel's grid produced for the row's query block.
+// split kernels produce for the row's query block.
 __device__ __forceinline__ int merge_splits(const DecodeParams &p, int seq, int qg) {
-    const int ntok = min(p.token_cap, p.fixed_tokens >= 0 ? p.fixed_tokens : p.seq_tokens[seq]);
-    const int prior = ntok - p.nq;
-    const int qblock = qg / p.q_per_cta;
-    const int qg_last = min(p.nq, (qblock + 1) * p.q_per_cta) - 1;
-    const int cta_end = prior + qg_last + 1;
-    return (ntok <= 0 || cta_end <= 0) ? 0
-                                       : min((int)p.max_splits, (cta_end + p.split_tokens - 1) / p.split_tokens);
+    return unit_extent(p, seq, qg / p.q_per_cta).splits;
 }
 
 // One CTA per (sequence, query row, query head), thread d = output dim d, for
@@ -400,6 +632,7 @@ template <int D, int MAXS>
 __global__ void __launch_bounds__(D) mslim_decode_merge_row(const DecodeParams p, uint16_t *out) {
     griddep_launch_dependents();
     griddep_wait();  // the split kernel's partials
+    if (blockIdx.x == 0 && threadIdx.x == 0 && p.work_counter) *p.work_counter = 0u;  // for the next call
     __shared__ float ms[MAXS], ls[MAXS];
     const size_t item = blockIdx.x;
     const size_t sq = item / p.qheads;  // seq * nq + qg
@@ -446,6 +679,7 @@ template <int D>
 __global__ void __launch_bounds__(128) mslim_decode_merge(const DecodeParams p, uint16_t *out) {
     griddep_launch_dependents();
     griddep_wait();  // the split kernel's partials
+    if (blockIdx.x == 0 && threadIdx.x == 0 && p.work_counter) *p.work_counter = 0u;  // for the next call
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const size_t item = (size_t)blockIdx.x * 4 + warp;
     const size_t items = (size_t)p.n_seq * p.nq * p.qheads;
@@ -514,13 +748,39 @@ template <int D, int STAGES, bool PAGED, bool QSPLIT>
 cudaError_t launch_impl(const CUtensorMap &kmap, const CUtensorMap &vmap, const DecodeParams &p,
                         uint16_t *out, cudaStream_t stream) {
     using S = Shape<D>;
-    const size_t smem = (size_t)STAGES * S::kStageBytes + 2 * STAGES * sizeof(uint64_t) + 1024;
-    auto kernel = mslim_decode_split<D, STAGES, PAGED, QSPLIT>;
-    cudaError_t err =
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (err != cudaSuccess) return err;
-    dim3 grid(p.max_splits, p.kvheads * p.head_chunks, p.n_seq * p.q_blocks);
-    err = launch_pdl(kernel, grid, dim3(kThreads), smem, stream, kmap, vmap, p);
+    cudaError_t err;
+    const uint64_t units = (uint64_t)p.n_seq * p.q_blocks;
+    if (!QSPLIT && p.work_counter && units <= (uint64_t)kMaxUnits) {
+        // persistent: as many CTAs as stay resident, at most one per work unit
+        const size_t smem = (size_t)STAGES * S::kStageBytes + 2 * STAGES * sizeof(uint64_t) +
+                            STAGES * sizeof(StageMeta) + (kMaxUnits + 1) * sizeof(int) + 1024;
+        auto kernel = mslim_decode_persist<D, STAGES, PAGED>;
+        static int per_sm = 0, sms = 0;  // resident CTAs of this form (same on every B200)
+        if (!per_sm) {
+            err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (err != cudaSuccess) return err;
+            int dev = 0, n = 0, b = 0;
+            if ((err = cudaGetDevice(&dev)) != cudaSuccess) return err;
+            if ((err = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return err;
+            if ((err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, kThreads, smem)) != cudaSuccess)
+                return err;
+            sms = n;
+            per_sm = b > 0 ? b : 1;
+        } else if ((err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) !=
+                   cudaSuccess) {
+            return err;
+        }
+        const uint64_t work = units * p.kvheads * p.head_chunks * p.max_splits;
+        const unsigned ctas = (unsigned)std::min<uint64_t>(work, (uint64_t)per_sm * sms);
+        err = launch_pdl(kernel, dim3(ctas), dim3(kThreads), smem, stream, kmap, vmap, p);
+    } else {
+        const size_t smem = (size_t)STAGES * S::kStageBytes + 2 * STAGES * sizeof(uint64_t) + 1024;
+        auto kernel = mslim_decode_split<D, STAGES, PAGED, QSPLIT>;
+        err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (err != cudaSuccess) return err;
+        dim3 grid(p.max_splits, p.kvheads * p.head_chunks, p.n_seq * p.q_blocks);
+        err = launch_pdl(kernel, grid, dim3(kThreads), smem, stream, kmap, vmap, p);
+    }
     if (err != cudaSuccess) return err;
     const size_t items = (size_t)p.n_seq * p.nq * p.qheads;
     if (items <= 0x7fffffffull) {

@@ -11,6 +11,8 @@ struct DecodeParams {
     const int32_t *seq_tokens;   // [n_seq] tokens in each sequence's cache
     const int32_t *page_table;   // [n_seq][max_pages] physical page ids (paged only)
     float *partials;             // [n_seq][nq][QH][max_splits][D + 2] (kernel D)
+    unsigned *work_counter;      // zero on entry, left zero (the merge resets it); null:
+                                 // one CTA per split instead of the persistent form
     int *status;                 // device status word
     int qheads, kvheads, group;  // group = QH / KVH
     int head_chunks;             // CTAs per KV head along the group

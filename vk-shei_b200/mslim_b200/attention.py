@@ -523,7 +523,7 @@ class GpuEngine:
         self.max_tokens = max_tokens
         self._workspace = None
         if geometry is not None and max_tokens > 0:
-            self._workspace = torch.empty(max(decode_workspace_bytes(geometry, 1, max_tokens), 16),
+            self._workspace = torch.zeros(max(decode_workspace_bytes(geometry, 1, max_tokens), 16),
                                           dtype=torch.uint8, device=f"cuda:{device}")
 
     def set_attention_kernel(self, config: AttentionKernelConfig, geometry: AttentionGeometry,

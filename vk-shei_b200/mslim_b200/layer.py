@@ -118,7 +118,7 @@ class DeviceLayer:
         # the paged decode sizes its split partials by the page table's reach
         reach = capacity if kv_mode == "dense" else self.max_pages * self.page_tokens
         ws = _att.decode_workspace_bytes(self.geometry, 1, reach)
-        self.workspace = torch.empty(max(ws, 16), dtype=torch.uint8, device=self.device)
+        self.workspace = torch.zeros(max(ws, 16), dtype=torch.uint8, device=self.device)
         self.position = 0
 
     # ---- the steps shared by prefill and decode

@@ -178,7 +178,7 @@ class DeviceModel:
             self.v_pool = [torch.zeros_like(p) for p in self.k_pool]
             reach = self.max_pages * page_tokens
         ws = _att.decode_workspace_bytes(self.geometry, batch, reach)
-        self.workspace = torch.empty(max(ws, 16), dtype=torch.uint8, device=dev)
+        self.workspace = torch.zeros(max(ws, 16), dtype=torch.uint8, device=dev)
         self.lengths = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.profile = None   # a SectionTimer splits the device time by kind of step
         # decode-step reductions over NVLink peer memory (fused with the
