@@ -705,7 +705,8 @@ def main():
                                    f"{traffic['traffic_over_algorithmic']:.4f}, applied to this launch's "
                                    "algorithmic bytes" if traffic else None),
                 "algorithmic_bytes_per_launch": step_bytes,
-                "achieved_note": "rank 0's algorithmic bytes / its mean per-step CUDA-event time"}
+                "achieved_note": "rank 0's algorithmic bytes / its per-step time (the graph replay of the K steps "
+                                 "between CUDA events, divided by K): the split and merge kernels of a step"}
     cpu = None
     if not args.no_cpu and world == 1:
         cpu = cpu_sample_gbs(c4_local["lengths"][:4], args.cpu_seconds)
@@ -725,11 +726,13 @@ def main():
                                                "mslim_cuda_decode_split_tokens_for_lengths on each rank's "
                                                "host-side session lengths"),
                        "l2": "no flush: inputs larger than L2 (%.2f GB per GPU per step)" % (step_bytes / 1e9),
+                       "issue": "the K timed steps captured as one CUDA graph and replayed once",
                        "parallelism": (f"sessions LPT-sharded over {world} GPUs (strong: one 64-session C4 draw)"
                                        if strong else
                                        f"session-sharded x{world} ({args.scaling})"),
                        **({"shard_of": args.shard_of} if args.shard_of else {})},
             "tokens_per_s": total_seq / (ms_per_step * 1e-3),
+            "eager_ms_per_step": timed["eager_ms"],
             "per_rank": {"tokens": rank_tokens, "sessions": [int(r[1]) for r in ranks],
                          "split_tokens": [int(r[2]) for r in ranks], "split_ctas": [int(r[3]) for r in ranks],
                          "ms_per_step": [r[4] for r in ranks],
@@ -789,30 +792,51 @@ class C4Pages:
                             self.stream)
 
     def time_steps(self, steps: int, warmup: int, local: int, barrier) -> dict:
+        """The K timed decode steps are captured once as a CUDA graph (the way a
+        serving loop issues its decode steps) and replayed once between two
+        CUDA events; the same K steps issued one by one from the host are
+        timed beside it (`eager_ms`)."""
         torch = self.torch
         for _ in range(warmup):
             self.step()
         torch.cuda.synchronize()
         if self.m.device_status(local) != 0:
             raise SystemExit("device status reported a bounded wait timeout during warm-up")
+        graph = torch.cuda.CUDAGraph()
+        cap = torch.cuda.Stream()
+        cap.wait_stream(self.stream)
+        main_stream = self.stream
+        self.stream = cap
+        with torch.cuda.graph(graph, stream=cap, capture_error_mode="thread_local"):
+            for _ in range(steps):
+                self.step()
+        self.stream = main_stream
+        torch.cuda.synchronize()
+        graph.replay()  # one untimed replay: the graph's first launch uploads it
+        torch.cuda.synchronize()
         sampler = ClockSampler(local)
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
         barrier()
         torch.cuda.synchronize()
         sampler.start()
         t_start = torch.cuda.Event(enable_timing=True)
         t_end = torch.cuda.Event(enable_timing=True)
         t_start.record(self.stream)
-        for i in range(steps):
-            evs[i][0].record(self.stream)
-            self.step()
-            evs[i][1].record(self.stream)
+        graph.replay()
         t_end.record(self.stream)
         torch.cuda.synchronize()
         barrier()
         clocks = sampler.stop()
-        return {"elapsed_ms": t_start.elapsed_time(t_end),
-                "launch_ms": statistics.mean(a.elapsed_time(b) for a, b in evs), "clocks": clocks}
+        elapsed = t_start.elapsed_time(t_end)
+        del graph
+        # the same steps issued one by one
+        torch.cuda.synchronize()
+        t_start.record(self.stream)
+        for _ in range(steps):
+            self.step()
+        t_end.record(self.stream)
+        torch.cuda.synchronize()
+        return {"elapsed_ms": elapsed, "launch_ms": elapsed / steps, "eager_ms": t_start.elapsed_time(t_end) / steps,
+                "clocks": clocks}
 
     def time_e2e(self, steps: int, barrier) -> dict:
         """Per step: the new token's q, k and v of every session from one

@@ -210,10 +210,13 @@ uint32_t policy_split_tokens(uint64_t work_items, uint64_t max_tokens) {
 // head_dim must be a multiple of 8 (16-byte TMA row strides) and at most 256.
 uint32_t kernel_dim_for(uint32_t d) { return d <= 64 ? 64 : d <= 128 ? 128 : 256; }
 
-// Decode workspace: a 256-byte head holding the persistent split kernel's
-// work counter (zero before the first call, left zero by every call), then
-// the split partials.
-constexpr uint64_t kDecodeCounterBytes = 256;
+// Decode workspace: a head of counters for the persistent split kernel (the
+// work counter and its CTAs-done counter, then one arrival counter per
+// (sequence x query block, KV-head chunk) item, at most kMaxDecodeItems;
+// zero before the first call, left zero by every call), then the split
+// partials.
+constexpr uint64_t kMaxDecodeItems = 16384;
+constexpr uint64_t kDecodeCounterBytes = 256 + 4 * kMaxDecodeItems;
 
 uint64_t partial_bytes(const mslim_geometry_t *g, uint64_t n_seq, uint64_t nq, uint64_t splits) {
     return kDecodeCounterBytes + n_seq * nq * g->query_heads * splits * (kernel_dim_for(g->head_dim) + 2) * sizeof(float);
@@ -290,6 +293,8 @@ int run_decode(const DecodeCall &c) {
     p.seq_tokens = c.seq_tokens;
     p.page_table = c.page_table;
     p.work_counter = static_cast<unsigned *>(c.workspace);
+    p.item_counters = reinterpret_cast<unsigned *>(static_cast<uint8_t *>(c.workspace) + 256);
+    p.out = static_cast<uint16_t *>(c.out);
     p.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(c.workspace) + kDecodeCounterBytes);
     p.status = status_ptr(dev);
     p.qheads = (int)g->query_heads;

@@ -129,7 +129,10 @@ struct DecodeConsumer {
     // A fragments of Q (16 rows x 16 dims per k-step) and a fresh state.
     // With QSPLIT the query arrives as f32 and is carried as qa (bf16 of q) +
     // qb (bf16 of the remainder), two MMAs per k-step.
-    __device__ __forceinline__ void begin(const DecodeParams &p, const DecodeItem &it, int lane) {
+    // q_smem: the item's rows (r = query x head, head_dim elements each) staged
+    // in shared memory, or null to read them from global memory.
+    __device__ __forceinline__ void begin(const DecodeParams &p, const DecodeItem &it, int lane,
+                                          const uint16_t *q_smem = nullptr) {
         const int g = lane >> 2, c = lane & 3;
         const int hc = p.heads_per_cta;
 #pragma unroll
@@ -158,6 +161,10 @@ struct DecodeConsumer {
                         k8 = pack_bf16x2(f8.x, f8.y);
                         k0r = pack_bf16x2(f0.x - bf16lo_f32(k0), f0.y - bf16hi_f32(k0));
                         k8r = pack_bf16x2(f8.x - bf16lo_f32(k8), f8.y - bf16hi_f32(k8));
+                    } else if (q_smem) {
+                        const uint16_t *row = q_smem + r * p.head_dim + d0;
+                        k0 = d0 < p.head_dim ? *reinterpret_cast<const uint32_t *>(row) : 0u;
+                        k8 = d0 + 8 < p.head_dim ? *reinterpret_cast<const uint32_t *>(row + 8) : 0u;
                     } else {
                         k0 = d0 < p.head_dim ? ld_u32(p.q + off) : 0u;
                         k8 = d0 + 8 < p.head_dim ? ld_u32(p.q + off + 8) : 0u;
@@ -180,7 +187,7 @@ struct DecodeConsumer {
     // This warp's 16 tokens of the 64-token tile at token tile_t0 (stage s),
     // keys below t_end.
     __device__ __forceinline__ void tile(uint8_t *stage, int tile_t0, int t_end, float scale, int warp, int lane) {
-        const int g = lane >> 2, c = lane & 3;
+        const int c = lane & 3;
         const int row0 = warp * kWarpTokens;
         const int t0 = tile_t0 + row0;
         const int valid = min(kWarpTokens, t_end - t0);
@@ -464,30 +471,103 @@ __global__ void __launch_bounds__(kThreads)
 struct StageMeta {
     int seq, kvh, hchunk, split, prior, qg_first, qg_last;
     int t0, t_end, flags;
+    int item, nsplits;  // the (unit, KV-head chunk) item and its split count
 };
+constexpr int kMaxFusedSplits = 64;  // splits per item the in-kernel merge takes
+
+// The last CTA to finish a split of an item merges the item's partials (the
+// other splits' from global memory) in split order -- the arithmetic and
+// order of mslim_decode_merge_row, so the output bits are the same -- and
+// writes its bf16 rows.  Run by the four consumer warps; `scratch` holds the
+// split maxima and sums ([16 rows][kMaxFusedSplits] each).
+template <int D>
+__device__ __forceinline__ void merge_item(const DecodeParams &p, const DecodeItem &it, int nsplits,
+                                           float *scratch) {
+    constexpr int kRowF = D + 2;
+    constexpr int kThr = kConsumerWarps * 32;
+    const int hc = p.heads_per_cta;
+    const int rows = p.q_per_cta * hc;
+    float *ms = scratch, *ls = scratch + 16 * kMaxFusedSplits;
+    auto part = [&](int r, int s) -> const float * {
+        const int qg = it.qg_first + r / hc;
+        const int qh = it.kvh * p.group + it.hchunk * hc + r % hc;
+        return p.partials + ((((size_t)it.seq * p.nq + qg) * p.qheads + qh) * p.max_splits + s) * kRowF;
+    };
+    for (int x = threadIdx.x; x < rows * nsplits; x += kThr) {
+        const int r = x / nsplits, s = x % nsplits;
+        if (it.qg_first + r / hc > it.qg_last) continue;
+        const float *src = part(r, s);
+        ms[r * kMaxFusedSplits + s] = __ldcg(src + D);
+        ls[r * kMaxFusedSplits + s] = __ldcg(src + D + 1);
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kThr) : "memory");
+    for (int x = threadIdx.x; x < rows * D; x += kThr) {
+        const int r = x / D, d = x % D;
+        const int qg = it.qg_first + r / hc;
+        if (qg > it.qg_last) continue;
+        const float *mr = ms + r * kMaxFusedSplits, *lr = ls + r * kMaxFusedSplits;
+        float m = -INFINITY;
+        for (int s = 0; s < nsplits; ++s) m = fmaxf(m, mr[s]);
+        const float mb = (m == -INFINITY) ? 0.f : m;
+        float l = 0.f, acc = 0.f;
+        const float *src = part(r, 0) + d;
+        int s = 0;
+        for (; s + 8 <= nsplits; s += 8) {
+            float av[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) av[u] = __ldcg(src + (size_t)(s + u) * kRowF);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const float w = fast_exp2(mr[s + u] - mb);
+                l += w * lr[s + u];
+                acc += w * av[u];
+            }
+        }
+        for (; s < nsplits; ++s) {
+            const float w = fast_exp2(mr[s] - mb);
+            l += w * lr[s];
+            acc += w * __ldcg(src + (size_t)s * kRowF);
+        }
+        const float inv = (l > 0.f) ? 1.0f / l : 0.f;
+        if (d < p.head_dim) {
+            const int qh = it.kvh * p.group + it.hchunk * hc + r % hc;
+            p.out[(((size_t)it.seq * p.nq + qg) * p.qheads + qh) * p.head_dim + d] = bf16_bits_rn(acc * inv);
+        }
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kThr) : "memory");  // scratch is free again
+}
 constexpr int kMetaFirst = 1, kMetaLast = 2, kMetaDone = 4;
 constexpr int kMaxUnits = 256;  // (sequence, query block) pairs the persistent kernel takes
+constexpr uint64_t kMaxDecodeItems = 16384;  // items whose counters the workspace head holds
 
 // Persistent form: a fixed grid of resident CTAs takes (item, split) work
-// units from a counter in the workspace (the merge puts it back to zero), so
-// fast SMs take more splits and no wave leaves SMs idle; each split is
-// computed exactly as mslim_decode_split computes it (same tiles, same warp
-// order), so the partials -- and the outputs -- are the same bits.  The
-// producer numbers the work: the splits of every (sequence, query block)
-// unit (a prefix sum over at most kMaxUnits units, in shared memory) times
-// the KV-head chunks.
+// units -- CTA b unit b first, then the next free unit from a counter in the
+// workspace (the merge puts it back to zero) -- so fast SMs take more splits
+// and no wave leaves SMs idle; each split is computed exactly as
+// mslim_decode_split computes it (same tiles, same warp order), so the
+// partials -- and the outputs -- are the same bits.  The producer numbers the
+// work: the splits of every (sequence, query block) unit (a prefix sum over
+// at most kMaxUnits units, kept in shared memory with each unit's extent, so
+// a chunk boundary reads nothing from global memory) times the KV-head
+// chunks.  A unit's query rows come into a per-stage shared-memory slot by a
+// bulk copy that completes with the unit's first K/V stage, so the consumers
+// never wait on global memory for Q.
 template <int D, int STAGES, bool PAGED>
 __global__ void __launch_bounds__(kThreads)
     mslim_decode_persist(const __grid_constant__ CUtensorMap kmap,
                          const __grid_constant__ CUtensorMap vmap, const DecodeParams p) {
     using S = Shape<D>;
+    constexpr int kQSlot = 16 * D * 2;  // up to 16 (query, head) rows
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * S::kStageBytes);
+    uint16_t *qslot = reinterpret_cast<uint16_t *>(smem + STAGES * S::kStageBytes);  // [STAGES][16 x D]
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * (S::kStageBytes + kQSlot));
     uint64_t *empty = full + STAGES;
     StageMeta *meta = reinterpret_cast<StageMeta *>(empty + STAGES);
     int *prefix = reinterpret_cast<int *>(meta + STAGES);  // [kMaxUnits + 1]
+    int *unit_end = prefix + kMaxUnits + 1;                 // [kMaxUnits] cta_end
+    int *unit_prior = unit_end + kMaxUnits;                 // [kMaxUnits] prior
 
     griddep_launch_dependents();
     griddep_wait();  // inputs, and the counter the previous merge reset
@@ -511,7 +591,13 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
         for (int k = 0; k < kMaxUnits / 32; ++k) {
             const int uix = lane * (kMaxUnits / 32) + k;
-            cnt[k] = uix < units ? unit_extent(p, uix / p.q_blocks, uix % p.q_blocks).splits : 0;
+            cnt[k] = 0;
+            if (uix < units) {
+                const UnitExtent u = unit_extent(p, uix / p.q_blocks, uix % p.q_blocks);
+                cnt[k] = u.splits;
+                unit_end[uix] = u.cta_end;
+                unit_prior[uix] = u.prior;
+            }
             local += cnt[k];
         }
         int incl = local;
@@ -533,10 +619,12 @@ __global__ void __launch_bounds__(kThreads)
             prefetch_tmap(&vmap);
             const int H = p.kvheads * p.head_chunks;
             const long long total = (long long)prefix[kMaxUnits] * H;
+            const int hc = p.heads_per_cta;
             int i = 0;  // stages filled so far
             bool ok = true;
-            long long g = atomicAdd(p.work_counter, 1u);
+            long long g = blockIdx.x;  // the first unit needs no counter
             while (ok && g < total) {
+                const long long g_next = (long long)gridDim.x + atomicAdd(p.work_counter, 1u);
                 const int w = (int)(g / H), hcid = (int)(g % H);
                 int lo = 0, hi = units;  // the last unit whose prefix is <= w
                 while (hi - lo > 1) {
@@ -545,12 +633,15 @@ __global__ void __launch_bounds__(kThreads)
                     else hi = mid;
                 }
                 const int seq = lo / p.q_blocks;
-                const UnitExtent u = unit_extent(p, seq, lo % p.q_blocks);
+                const int qg_first = (lo % p.q_blocks) * p.q_per_cta;
+                const int qg_last = min(p.nq, qg_first + p.q_per_cta) - 1;
+                const int cta_end = unit_end[lo];
+                const int slen = split_len(cta_end, p.split_tokens);
                 const int split = w - prefix[lo];
-                const int t_begin = split * u.slen;
-                const int t_end = min(u.cta_end, t_begin + u.slen);
+                const int t_begin = split * slen;
+                const int t_end = min(cta_end, t_begin + slen);
                 const int ntiles = (t_end - t_begin + kTileT - 1) / kTileT;
-                const long long g_next = atomicAdd(p.work_counter, 1u);  // in flight during the loads
+                const int kvh = hcid / p.head_chunks, hchunk = hcid % p.head_chunks;
                 for (int t = 0; t < ntiles; ++t, ++i) {
                     const int s = i % STAGES;
                     if (!mbar_wait(&empty[s], ((i / STAGES) & 1) ^ 1, p.status, 4)) {
@@ -559,17 +650,30 @@ __global__ void __launch_bounds__(kThreads)
                     }
                     StageMeta &m = meta[s];
                     m.seq = seq;
-                    m.kvh = hcid / p.head_chunks;
-                    m.hchunk = hcid % p.head_chunks;
+                    m.kvh = kvh;
+                    m.hchunk = hchunk;
                     m.split = split;
-                    m.prior = u.prior;
-                    m.qg_first = u.qg_first;
-                    m.qg_last = u.qg_last;
+                    m.prior = unit_prior[lo];
+                    m.qg_first = qg_first;
+                    m.qg_last = qg_last;
                     m.t0 = t_begin + t * kTileT;
                     m.t_end = t_end;
                     m.flags = (t == 0 ? kMetaFirst : 0) | (t == ntiles - 1 ? kMetaLast : 0);
+                    m.item = lo * H + hcid;
+                    m.nsplits = prefix[lo + 1] - prefix[lo];
+                    if (t == 0) {
+                        // the unit's query rows, hc heads of each query row side by side
+                        const uint32_t row_bytes = (uint32_t)(hc * p.head_dim * 2);
+                        const int nrows = qg_last - qg_first + 1;
+                        mbar_expect_tx(&full[s], row_bytes * nrows);
+                        for (int qi = 0; qi < nrows; ++qi)
+                            bulk_load(qslot + (size_t)s * (kQSlot / 2) + (size_t)qi * hc * p.head_dim,
+                                      p.q + (((size_t)seq * p.nq + qg_first + qi) * p.qheads + kvh * p.group +
+                                             hchunk * hc) * p.head_dim,
+                                      row_bytes, &full[s]);
+                    }
                     uint8_t *kdst = smem + s * S::kStageBytes;
-                    issue_tile<D, PAGED>(&kmap, &vmap, p, &full[s], kdst, kdst + S::kTensorBytes, seq, m.kvh, m.t0);
+                    issue_tile<D, PAGED>(&kmap, &vmap, p, &full[s], kdst, kdst + S::kTensorBytes, seq, kvh, m.t0);
                 }
                 g = g_next;
             }
@@ -581,14 +685,33 @@ __global__ void __launch_bounds__(kThreads)
                     ++i;
                 }
             }
+            // this CTA takes no more work; the last CTA to get here puts the
+            // counters back to zero for the next call
+            __threadfence();
+            if (atomicAdd(&p.work_counter[1], 1u) == gridDim.x - 1) {
+                p.work_counter[0] = 0u;
+                p.work_counter[1] = 0u;
+            }
             // Do not retire while our copies may still be landing in this CTA's
             // shared memory: wait (bounded) for the last stages filled.
             for (int k = max(0, i - STAGES); k < i; ++k) mbar_wait(&full[k % STAGES], (k / STAGES) & 1, p.status, 2);
+        }
+        // units without keys (empty sessions) have no split to merge: their
+        // rows are written as zeros by CTA u % grid
+        for (int uix = 0; uix < units; ++uix) {
+            if (prefix[uix + 1] != prefix[uix] || uix % (int)gridDim.x != (int)blockIdx.x) continue;
+            const int seq = uix / p.q_blocks;
+            const int qg_first = (uix % p.q_blocks) * p.q_per_cta;
+            const int qg_last = min(p.nq, qg_first + p.q_per_cta) - 1;
+            const size_t first = ((size_t)seq * p.nq + qg_first) * p.qheads * p.head_dim;
+            const size_t n = (size_t)(qg_last - qg_first + 1) * p.qheads * p.head_dim;
+            for (size_t x = lane; x < n; x += 32) p.out[first + x] = 0;
         }
         return;
     }
 
     // ----------------------------------------------------------- consumers --
+    volatile int *is_last = unit_prior + kMaxUnits;
     DecodeConsumer<D, false> cs;
     DecodeItem it{};
     for (int i = 0;; ++i) {
@@ -605,11 +728,25 @@ __global__ void __launch_bounds__(kThreads)
             it.prior = m.prior;
             it.qg_first = m.qg_first;
             it.qg_last = m.qg_last;
-            cs.begin(p, it, lane);
+            cs.begin(p, it, lane, qslot + (size_t)s * (kQSlot / 2));
         }
         cs.tile(stage, m.t0, m.t_end, p.scale_log2, warp, lane);
-        // the split's last stage is the combine's scratch before it is released
-        if (m.flags & kMetaLast) cs.finish(p, it, reinterpret_cast<float *>(stage), warp, lane);
+        if (m.flags & kMetaLast) {
+            // the split's last stage is the combine's (and the merge's)
+            // scratch before it is released
+            cs.finish(p, it, reinterpret_cast<float *>(stage), warp, lane);
+            // the partial is out (warp 0 wrote it); the last split of the item
+            // merges it
+            if (warp == 0) __threadfence();
+            asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+            if (threadIdx.x == 0) *is_last = atomicAdd(&p.item_counters[m.item], 1u) + 1 == (unsigned)m.nsplits;
+            asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+            if (*is_last) {
+                __threadfence();
+                merge_item<D>(p, it, m.nsplits, reinterpret_cast<float *>(stage));
+                if (threadIdx.x == 0) p.item_counters[m.item] = 0u;
+            }
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }
@@ -750,10 +887,12 @@ cudaError_t launch_impl(const CUtensorMap &kmap, const CUtensorMap &vmap, const 
     using S = Shape<D>;
     cudaError_t err;
     const uint64_t units = (uint64_t)p.n_seq * p.q_blocks;
-    if (!QSPLIT && p.work_counter && units <= (uint64_t)kMaxUnits) {
+    if (!QSPLIT && p.work_counter && p.item_counters && !p.out_f32 && units <= (uint64_t)kMaxUnits &&
+        units * p.kvheads * p.head_chunks <= (uint64_t)kMaxDecodeItems && p.max_splits <= kMaxFusedSplits &&
+        (reinterpret_cast<uintptr_t>(p.q) & 15u) == 0) {
         // persistent: as many CTAs as stay resident, at most one per work unit
-        const size_t smem = (size_t)STAGES * S::kStageBytes + 2 * STAGES * sizeof(uint64_t) +
-                            STAGES * sizeof(StageMeta) + (kMaxUnits + 1) * sizeof(int) + 1024;
+        const size_t smem = (size_t)STAGES * (S::kStageBytes + 16 * D * 2) + 2 * STAGES * sizeof(uint64_t) +
+                            STAGES * sizeof(StageMeta) + (3 * kMaxUnits + 2) * sizeof(int) + 1024;
         auto kernel = mslim_decode_persist<D, STAGES, PAGED>;
         static int per_sm = 0, sms = 0;  // resident CTAs of this form (same on every B200)
         if (!per_sm) {
@@ -772,7 +911,7 @@ cudaError_t launch_impl(const CUtensorMap &kmap, const CUtensorMap &vmap, const 
         }
         const uint64_t work = units * p.kvheads * p.head_chunks * p.max_splits;
         const unsigned ctas = (unsigned)std::min<uint64_t>(work, (uint64_t)per_sm * sms);
-        err = launch_pdl(kernel, dim3(ctas), dim3(kThreads), smem, stream, kmap, vmap, p);
+        return launch_pdl(kernel, dim3(ctas), dim3(kThreads), smem, stream, kmap, vmap, p);  // merges in-kernel
     } else {
         const size_t smem = (size_t)STAGES * S::kStageBytes + 2 * STAGES * sizeof(uint64_t) + 1024;
         auto kernel = mslim_decode_split<D, STAGES, PAGED, QSPLIT>;

@@ -11,8 +11,12 @@ struct DecodeParams {
     const int32_t *seq_tokens;   // [n_seq] tokens in each sequence's cache
     const int32_t *page_table;   // [n_seq][max_pages] physical page ids (paged only)
     float *partials;             // [n_seq][nq][QH][max_splits][D + 2] (kernel D)
-    unsigned *work_counter;      // zero on entry, left zero (the merge resets it); null:
-                                 // one CTA per split instead of the persistent form
+    unsigned *work_counter;      // [2]: work taken and CTAs done, zero on entry, left zero;
+                                 // null: one CTA per split and a merge kernel instead of
+                                 // the persistent form
+    unsigned *item_counters;     // persistent form: splits finished per (unit, KV-head
+                                 // chunk) item, zero on entry, left zero
+    uint16_t *out;               // bf16 [n_seq][nq][QH][head_dim]
     int *status;                 // device status word
     int qheads, kvheads, group;  // group = QH / KVH
     int head_chunks;             // CTAs per KV head along the group
