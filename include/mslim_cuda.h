@@ -275,7 +275,9 @@ int mslim_cuda_decode_paged(const mslim_geometry_t *geometry, const void *q, con
  * call before any stream capture.  That address is kept for the life of the
  * process, so the library must not be used on a device after
  * cudaDeviceReset (or any other teardown of its primary context).  Every
- * call shares the one array: calls that can overlap on the GPU (different
+ * call shares the one array and finds the previous call's contents there;
+ * each call first clears the array's head of work counters on its stream
+ * (a memset, no allocation).  Calls that can overlap on the GPU (different
  * streams, no ordering) race on it. */
 #define MSLIM_STATIC_SCRATCH_BYTES (16u << 20)
 int mslim_cuda_decode_paged_static_scratch(const mslim_geometry_t *geometry, const void *q,

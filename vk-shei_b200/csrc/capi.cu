@@ -32,8 +32,10 @@ __device__ int g_mslim_status_word;
 
 // Split partials of mslim_cuda_decode_paged_static_scratch: a fixed device
 // array, so that entry point never allocates.  Its contents persist between
-// calls; every partial the merge reads is written by the split kernel of the
-// same call first, so nothing in it has to start at zero.
+// calls.  Every partial the merge reads is written by the split kernel of the
+// same call first; only the head of work counters has to start at zero, and
+// the entry point clears it on its stream before each call (so a call that
+// gave up on a bounded wait cannot leave the next one a stale count).
 static __device__ __align__(256) float g_static_decode_scratch[MSLIM_STATIC_SCRATCH_BYTES / sizeof(float)];
 
 namespace {
@@ -863,6 +865,8 @@ int mslim_cuda_decode_paged_static_scratch(const mslim_geometry_t *geometry, con
     if (int rc = current_device(&dev)) return rc;
     void *scratch = nullptr;
     if (int rc = static_scratch_ptr(dev, &scratch)) return rc;
+    cudaError_t err = cudaMemsetAsync(scratch, 0, kDecodeCounterBytes, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail(err, "clearing the static scratch counters");
     return mslim_cuda_decode_paged(geometry, q, k_pool, v_pool, n_pages, page_tokens, page_table,
                                    max_pages_per_seq, seq_tokens, n_seq, st, scratch,
                                    MSLIM_STATIC_SCRATCH_BYTES, out, stream);
