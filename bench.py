@@ -302,9 +302,11 @@ def bench_prefill(m, torch, device, args) -> dict:
     graph = torch.cuda.CUDAGraph()
     cap = torch.cuda.Stream()
     cap.wait_stream(stream)
+    launches0 = m.kernel_launches()
     with torch.cuda.graph(graph, stream=cap, capture_error_mode="thread_local"):
         for i in range(steps):
             call(i, torch.cuda.current_stream())
+    captured = m.kernel_launches() - launches0  # per replay
     # a one-second idle lets the power limiter recover from the preceding
     # HBM-bound legs, then warm replays settle the clocks into this leg's
     # regime before anything is timed
@@ -371,7 +373,7 @@ def bench_prefill(m, torch, device, args) -> dict:
                          "traffic": traffic["dram_bytes_per_launch"] if traffic else None,
                          "traffic_source": ("profiles/prefill_c2_traffic.json (one ncu capture of this C2 call), "
                                             "not measured in this run" if traffic else None)},
-            "gpu_launches": steps, "clocks": clocks}
+            "gpu_launches": captured, "clocks": clocks}
 
 
 def bench_layer(m, torch, device, args) -> dict:
@@ -649,6 +651,7 @@ def main():
                        "host waits for every step's result"}
         if m.device_status(local) != 0:
             raise SystemExit("device status reported an error during the e2e leg")
+    timed_launches_per_step = timed["launches"] / args.steps
     c4_local = {"step_bytes": c4.step_bytes, "launch_ms": timed["launch_ms"], "n_seq": c4.n_seq,
                 "lengths": c4.lengths}
     c4.close()
@@ -694,7 +697,9 @@ def main():
     step_bytes = c4_local["step_bytes"]
     achieved = step_bytes / (c4_local["launch_ms"] * 1e-3) / 1e9
     traffic = profile_traffic("decode_c4_traffic.json")
-    roofline = {"bound": "hbm", "kernel": "mslim_decode_split + mslim_decode_merge",
+    roofline = {"bound": "hbm", "kernel": ("mslim_decode_persist (split-KV with the merge in-kernel)"
+                                           if timed_launches_per_step == 1 else
+                                           "mslim_decode_split + mslim_decode_merge"),
                 "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": achieved / peaks["hbm_gbs"] if peaks["hbm_gbs"] else None,
                 "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)" if peaks["source"] == "measured"
@@ -706,7 +711,7 @@ def main():
                                    "algorithmic bytes" if traffic else None),
                 "algorithmic_bytes_per_launch": step_bytes,
                 "achieved_note": "rank 0's algorithmic bytes / its per-step time (the graph replay of the K steps "
-                                 "between CUDA events, divided by K): the split and merge kernels of a step"}
+                                 "between CUDA events, divided by K): every kernel of a step"}
     cpu = None
     if not args.no_cpu and world == 1:
         cpu = cpu_sample_gbs(c4_local["lengths"][:4], args.cpu_seconds)
@@ -739,7 +744,10 @@ def main():
                          "token_imbalance_max_over_mean": max(rank_tokens) / mean_tokens if mean_tokens else None},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "prefill": prefill,
             "weak": weak, "model": model,
-            "gpu_launches": 2 * args.steps, "clocks": timed["clocks"], "device_status": status}
+            "gpu_launches": timed["launches"],
+            "gpu_launches_note": "the library's kernel launches recorded into the timed graph "
+                                 "(mslim_cuda_kernel_launches before and after its capture)",
+            "clocks": timed["clocks"], "device_status": status}
     print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
@@ -807,9 +815,11 @@ class C4Pages:
         cap.wait_stream(self.stream)
         main_stream = self.stream
         self.stream = cap
+        launches0 = self.m.kernel_launches()
         with torch.cuda.graph(graph, stream=cap, capture_error_mode="thread_local"):
             for _ in range(steps):
                 self.step()
+        captured = self.m.kernel_launches() - launches0  # the library's kernels in the timed graph
         self.stream = main_stream
         torch.cuda.synchronize()
         graph.replay()  # one untimed replay: the graph's first launch uploads it
@@ -836,7 +846,7 @@ class C4Pages:
         t_end.record(self.stream)
         torch.cuda.synchronize()
         return {"elapsed_ms": elapsed, "launch_ms": elapsed / steps, "eager_ms": t_start.elapsed_time(t_end) / steps,
-                "clocks": clocks}
+                "clocks": clocks, "launches": captured}
 
     def time_e2e(self, steps: int, barrier) -> dict:
         """Per step: the new token's q, k and v of every session from one

@@ -102,6 +102,12 @@ const char *mslim_cuda_last_error(void);
  * tiled-attention.json:790-796). */
 int mslim_cuda_device_status(int device, int reset, int *status);
 
+/* Kernels this library has launched in the process so far (every device and
+ * stream; a launch recorded into a stream capture counts once, at capture).
+ * A host that replays a captured step K times ran K x the launches the
+ * capture added.  No reference counterpart (an accounting aid). */
+uint64_t mslim_cuda_kernel_launches(void);
+
 /* ------------------------------------------- configuration contract -- */
 
 /* AttentionGeometry::new (src/portable.rs:421-443). */

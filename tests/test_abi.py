@@ -156,3 +156,11 @@ def test_split_tokens_for_host_lengths(m):
     ctas = sum(-(-int(L) // st) for L in lengths) * 8
     assert ctas <= 2 * 296, (st, ctas)
     assert m.decode_split_tokens_for_lengths(g, np.zeros(3, np.int32)) % 64 == 0
+
+
+def test_kernel_launch_counter_reads_without_a_gpu(m):
+    """mslim_cuda_kernel_launches is a host counter: it reads without a
+    device and only grows."""
+    a = m.kernel_launches()
+    b = m.kernel_launches()
+    assert 0 <= a <= b

@@ -39,6 +39,12 @@ __device__ int g_mslim_status_word;
 static __device__ __align__(256) float g_static_decode_scratch[MSLIM_STATIC_SCRATCH_BYTES / sizeof(float)];
 
 namespace {
+std::atomic<uint64_t> g_kernel_launches{0};
+}  // namespace
+
+void mslim::note_launch() { g_kernel_launches.fetch_add(1, std::memory_order_relaxed); }
+
+namespace {
 
 thread_local std::string g_last_error;
 
@@ -456,6 +462,8 @@ const char *mslim_cuda_version(void) { return "mslim-cuda 0.1.0 (sm_100a)"; }
 #define MSLIM_SOURCE_DIGEST "unknown"  // built outside vk-shei_b200/build.py
 #endif
 const char *mslim_cuda_implementation_digest(void) { return MSLIM_SOURCE_DIGEST; }
+
+uint64_t mslim_cuda_kernel_launches(void) { return g_kernel_launches.load(std::memory_order_relaxed); }
 
 int mslim_cuda_device_status(int device, int reset, int *status) {
     if (!status) return fail(MSLIM_ERR_SHAPE_MISMATCH, "status pointer is null");

@@ -333,7 +333,7 @@ cudaError_t launch_gemv_tc(const CUtensorMap &xmap, const CUtensorMap &wmap, con
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, mslim_gemv_tc, xmap, wmap, p);
+    return counted(cudaLaunchKernelEx(&cfg, mslim_gemv_tc, xmap, wmap, p));
 }
 
 }  // namespace mslim

@@ -338,7 +338,7 @@ cudaError_t launch_gather_selected(const uint16_t *k_src, const uint16_t *v_src,
     else
         mslim_gather_selected<false><<<grid, 256, 0, stream>>>(src, kv_heads, dim, seq_tokens, selected, counts,
                                                                 max_selected, gk, gv, status);
-    return cudaGetLastError();
+    return counted(cudaGetLastError());
 }
 
 cudaError_t launch_kv_canonical(const uint16_t *src, uint16_t *out, uint32_t kv_heads, uint32_t tokens,
@@ -355,25 +355,25 @@ cudaError_t launch_kv_canonical(const uint16_t *src, uint16_t *out, uint32_t kv_
     else
         mslim_kv_canonical<false><<<grid, 256, 0, stream>>>(src, out, kv_heads, tokens, dim, page_row, page_tokens,
                                                              n_pages, status);
-    return cudaGetLastError();
+    return counted(cudaGetLastError());
 }
 
 cudaError_t launch_residual_add(const uint16_t *a, const uint16_t *b, uint16_t *out, uint64_t n,
                                 cudaStream_t stream) {
     mslim_residual_add<<<elt_grid(n), kEltThreads, 0, stream>>>(a, b, out, n);
-    return cudaGetLastError();
+    return counted(cudaGetLastError());
 }
 
 cudaError_t launch_swiglu(const uint16_t *gate, const uint16_t *up, uint16_t *out, uint64_t n,
                           cudaStream_t stream) {
     mslim_swiglu<<<elt_grid(n), kEltThreads, 0, stream>>>(gate, up, out, n);
-    return cudaGetLastError();
+    return counted(cudaGetLastError());
 }
 
 cudaError_t launch_swiglu_rows(const uint16_t *gate_up, uint16_t *out, uint32_t rows, uint32_t width,
                                cudaStream_t stream) {
     mslim_swiglu_rows<<<elt_grid((uint64_t)rows * width), kEltThreads, 0, stream>>>(gate_up, out, rows, width);
-    return cudaGetLastError();
+    return counted(cudaGetLastError());
 }
 
 cudaError_t launch_page_token_hashes(const uint16_t *pool, uint32_t n_pool_pages, uint32_t kv_heads,
@@ -383,13 +383,13 @@ cudaError_t launch_page_token_hashes(const uint16_t *pool, uint32_t n_pool_pages
     dim3 grid((tokens + 127) / 128, n_pages);
     mslim_page_token_hashes<<<grid, 128, 0, stream>>>(pool, n_pool_pages, kv_heads, page_tokens, head_dim,
                                                       page_ids, tokens, hashes, status);
-    return cudaGetLastError();
+    return counted(cudaGetLastError());
 }
 
 cudaError_t launch_argmax(const uint16_t *logits, uint32_t rows, uint32_t n, int ties_to_last,
                           int32_t *out, cudaStream_t stream) {
     mslim_argmax<<<rows, kArgThreads, 0, stream>>>(logits, n, ties_to_last, out);
-    return cudaGetLastError();
+    return counted(cudaGetLastError());
 }
 
 // ------------------------------------------------------ exp2 diagnostic --
@@ -407,7 +407,7 @@ cudaError_t launch_exp2_eval(const float *x, float *y_poly, float *y_mufu, float
                              cudaStream_t stream) {
     const uint32_t blocks = (uint32_t)std::min<uint64_t>((n + 255) / 256, 148u * 8);
     mslim_exp2_eval<<<blocks, 256, 0, stream>>>(x, y_poly, y_mufu, y_ref, n);
-    return cudaGetLastError();
+    return counted(cudaGetLastError());
 }
 
 }  // namespace mslim

@@ -471,6 +471,16 @@ __device__ __forceinline__ void griddep_launch_dependents() {
 }
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// Every kernel launch the library issues (eager or into a stream capture)
+// is counted; mslim_cuda_kernel_launches() reads the total.
+void note_launch();
+
+// Counts a launch that returned `err` == cudaSuccess; passes `err` through.
+inline cudaError_t counted(cudaError_t err) {
+    if (err == cudaSuccess) note_launch();
+    return err;
+}
+
 // Host side: launch with programmatic stream serialization, so the kernel may
 // begin launching while its predecessor in the stream still runs (once the
 // predecessor triggers or retires).  Kernels launched this way call
@@ -488,7 +498,7 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args &&>(args)...);
+    return counted(cudaLaunchKernelEx(&cfg, kernel, static_cast<Args &&>(args)...));
 }
 
 // 2^x on the FMA/ALU pipes only (offloads the MUFU unit): n = round(x) by

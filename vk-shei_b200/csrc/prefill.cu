@@ -789,7 +789,7 @@ cudaError_t launch_prefill(const CUtensorMap &qmap, const CUtensorMap &kmap,
     }
     const unsigned grid = (unsigned)(p.n_qtiles * p.qheads);
     mslim_prefill_causal<<<grid, kSThreads, kSSmemBytes, stream>>>(qmap, kmap, vmap, p);
-    return cudaGetLastError();
+    return counted(cudaGetLastError());
 }
 
 }  // namespace mslim

@@ -386,20 +386,20 @@ unsigned rope_vec_ctas(uint32_t qheads, uint32_t kvheads, uint32_t dim) {
 cudaError_t launch_rmsnorm(const uint16_t *x, const uint16_t *w, uint16_t *y, uint32_t tokens,
                            uint32_t hidden, float eps, cudaStream_t stream) {
     mslim_rmsnorm<false><<<tokens, 128, 0, stream>>>(const_cast<uint16_t *>(x), nullptr, w, y, hidden, eps);
-    return cudaGetLastError();
+    return counted(cudaGetLastError());
 }
 
 cudaError_t launch_residual_rmsnorm(uint16_t *x, const uint16_t *delta, const uint16_t *w, uint16_t *y,
                                     uint32_t tokens, uint32_t hidden, float eps, cudaStream_t stream) {
     mslim_rmsnorm<true><<<tokens, 128, 0, stream>>>(x, delta, w, y, hidden, eps);
-    return cudaGetLastError();
+    return counted(cudaGetLastError());
 }
 
 cudaError_t launch_rope(const uint16_t *in, uint16_t *out, uint32_t tokens, uint32_t heads,
                         uint32_t dim, uint32_t start_position, const RopeTable &table,
                         cudaStream_t stream) {
     mslim_rope<<<tokens, 128, 0, stream>>>(in, out, heads, dim, start_position, table);
-    return cudaGetLastError();
+    return counted(cudaGetLastError());
 }
 
 cudaError_t launch_rope_append_paged(const uint16_t *q_in, uint16_t *q_out, const uint16_t *k_in,

@@ -191,7 +191,7 @@ cudaError_t launch_w(const TpCommDev &comm, uint32_t slot, uint16_t *x, const ui
         mslim_tp_allreduce_rmsnorm<W, true><<<rows, kTpThreads, 0, stream>>>(comm, slot, x, w, y, eps, status);
     else
         mslim_tp_allreduce_rmsnorm<W, false><<<rows, kTpThreads, 0, stream>>>(comm, slot, x, w, y, eps, status);
-    return cudaGetLastError();
+    return counted(cudaGetLastError());
 }
 
 }  // namespace

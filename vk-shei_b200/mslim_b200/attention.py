@@ -247,6 +247,11 @@ def device_status(device: int = 0, reset: bool = True) -> int:
     return st.value
 
 
+def kernel_launches() -> int:
+    """Kernels the library has launched in this process (captures count once)."""
+    return int(_lib.lib().mslim_cuda_kernel_launches())
+
+
 def decode_workspace_bytes(geometry: AttentionGeometry, n_seq: int, max_tokens: int,
                            split_tokens: int = 0) -> int:
     out = ctypes.c_size_t()
