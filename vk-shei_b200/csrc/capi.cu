@@ -897,7 +897,7 @@ int mslim_cuda_prefill_causal(const mslim_geometry_t *geometry, const void *q, c
     if (!mslim::prefill_supported(geometry->head_dim, geometry->query_heads / geometry->kv_heads))
         return fail(MSLIM_ERR_INVALID_GEOMETRY,
                     "head_dim %u with %u query heads per KV head has no sm_100a prefill kernel "
-                    "(head_dim 128, or 64 with an even group)",
+                    "(head_dim 64..128, a multiple of 8)",
                     geometry->head_dim, geometry->query_heads / geometry->kv_heads);
     if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(out, 16))
         return fail(MSLIM_ERR_SHAPE_MISMATCH, "prefill buffers must be 16-byte aligned");

@@ -311,7 +311,9 @@ __global__ void __launch_bounds__(kSThreads, 1)
             pair_sync(quarter);
             const float inv = 1.0f / (l_run + xsum[(half ^ 1) * kRows + row]);
             const int qrow = q0 + row;
-            uint16_t *dst = p.out + ((size_t)qrow * p.qheads + qh) * kDim + col0;
+            // rows are head_dim elements apart; columns past head_dim (zero
+            // padding of a head_dim below 128) are not written
+            uint16_t *dst = p.out + ((size_t)qrow * p.qheads + qh) * p.head_dim + col0;
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 float o[32];
@@ -322,8 +324,9 @@ __global__ void __launch_bounds__(kSThreads, 1)
                 if (qrow < p.queries) {
 #pragma unroll
                     for (int t = 0; t < 4; ++t)
-                        reinterpret_cast<uint4 *>(dst + c * 32)[t] =
-                            make_uint4(w[4 * t], w[4 * t + 1], w[4 * t + 2], w[4 * t + 3]);
+                        if (col0 + c * 32 + t * 8 < p.head_dim)
+                            reinterpret_cast<uint4 *>(dst + c * 32)[t] =
+                                make_uint4(w[4 * t], w[4 * t + 1], w[4 * t + 2], w[4 * t + 3]);
                 }
             }
         } else {
@@ -723,8 +726,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
 }  // namespace
 
 bool prefill_supported(unsigned head_dim, unsigned group) {
-    // head_dim 64 runs only in the two-head kernel (even groups)
-    return group >= 1 && (head_dim == 128 || (head_dim == 64 && group % 2 == 0));
+    // The kernels run at head_dim 64 (two-head kernel) or 128 (both); a
+    // smaller multiple of 8 runs zero-padded: the tensor maps describe the
+    // caller's head_dim, the TMA fills the columns past it with zeros (they
+    // add nothing to S, and their O columns are zero), and the output stores
+    // stop at head_dim.
+    return group >= 1 && head_dim >= 64 && head_dim <= 128 && head_dim % 8 == 0;
 }
 
 bool prefill_pairs_heads(unsigned group) { return group % 2 == 0; }
@@ -781,7 +788,7 @@ cudaError_t launch_prefill(const CUtensorMap &qmap, const CUtensorMap &kmap,
         // persistent: one CTA per SM (at most one per item)
         const long long items = (long long)p.n_qtiles * (p.qheads / 2);
         const unsigned grid = (unsigned)(items < sms ? items : sms);
-        if (p.head_dim == 64)
+        if (p.head_dim <= 64)
             return launch_pdl(mslim_prefill_pair<64>, dim3(grid), dim3(kPThreads), PairShape<64>::kSmemBytes,
                               stream, qmap, kmap, vmap, omap, p);
         return launch_pdl(mslim_prefill_pair<128>, dim3(grid), dim3(kPThreads), PairShape<128>::kSmemBytes,

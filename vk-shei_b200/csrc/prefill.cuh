@@ -15,7 +15,8 @@ struct PrefillParams {
     int qheads, kvheads, group;
     int queries, prior; // rows prior..prior+queries-1 attend to keys 0..=row
     int n_qtiles;       // ceil(queries / 128)
-    int head_dim;       // 128, or 64 with an even GQA group
+    int head_dim;       // the caller's head_dim, 64..128 (a multiple of 8); the
+                        // kernel runs at 64 (even groups, head_dim 64) or 128
     float scale_log2;   // log2(e) / sqrt(D)
 };
 
