@@ -297,10 +297,10 @@ int mslim_cuda_decode_paged_static_scratch(const mslim_geometry_t *geometry, con
 
 /* BatchKernels::attention (src/gpu_llm/prefill.rs:363-435): chunked causal
  * prefill, tcgen05/TMEM tensor cores.  q/out: bf16 [queries][QH][D];
- * k/v: bf16 token-major [prior+queries][KVH][D].  head_dim 64..128, a
- * multiple of 8, any GQA group (a head_dim below the kernel's 64 or 128 runs
- * zero-padded on the chip); other shapes return MSLIM_ERR_INVALID_GEOMETRY
- * (mslim_cuda_plan_run serves them). */
+ * k/v: bf16 token-major [prior+queries][KVH][D].  head_dim 64..256, a
+ * multiple of 8, any GQA group (the kernels run at 64, 128 or 256; a head_dim
+ * between runs zero-padded on the chip); other shapes return
+ * MSLIM_ERR_INVALID_GEOMETRY (mslim_cuda_plan_run serves them). */
 int mslim_cuda_prefill_causal(const mslim_geometry_t *geometry, const void *q, const void *k,
                               const void *v, void *out, uint32_t queries, uint32_t prior,
                               void *stream);

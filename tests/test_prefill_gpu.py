@@ -37,7 +37,10 @@ CASES = [(1, 0), (5, 0), (128, 0), (129, 0), (200, 37), (256, 256), (64, 1000), 
                                   # zero-padded head dims (the reference validates 80,
                                   # tiled_attention.rs:414-421) and head_dim 64 with an
                                   # odd group (the single-head kernel at 128)
-                                  (4, 2, 80), (12, 4, 80), (4, 4, 64), (6, 2, 64), (8, 8, 96), (4, 2, 120)])
+                                  (4, 2, 80), (12, 4, 80), (4, 4, 64), (6, 2, 64), (8, 8, 96), (4, 2, 120),
+                                  # head_dim 256 (64-key tiles; tiled_attention.rs:414-421) and
+                                  # 192, zero-padded to it
+                                  (4, 1, 256), (8, 2, 256), (6, 2, 256), (4, 2, 192)])
 def test_prefill_matches_cpu_path(m, oracle, geom):
     from mslim_b200 import workloads as wl
     qh, kvh, d = geom
@@ -73,7 +76,8 @@ def test_c2_full_size_matches_cpu_path(m, oracle):
     assert same > 0.5, same
 
 
-@pytest.mark.parametrize("chunk,d", [(64, 128), (128, 128), (192, 128), (256, 128), (192, 64), (128, 80)])
+@pytest.mark.parametrize("chunk,d", [(64, 128), (128, 128), (192, 128), (256, 128), (192, 64), (128, 80),
+                                     (192, 256)])
 def test_chunked_prefill_equals_one_shot(m, chunk, d):
     """Prefill in batches of 64/128/192/256 tokens (each chunk at prior =
     tokens so far, over the keys written so far; src/gpu_llm/mod.rs:5435)
@@ -97,7 +101,7 @@ def test_chunked_prefill_equals_one_shot(m, chunk, d):
 def test_prefill_rejects_unsupported(m):
     torch = torch_mod()
     b = torch.zeros(64, dtype=torch.int16, device="cuda:0")
-    # head dims outside 64..128 or not a multiple of 8 have no prefill kernel
+    # head dims outside 64..256 or not a multiple of 8 have no prefill kernel
     with pytest.raises(m.InvalidGeometry):
         m.prefill_causal(m.AttentionGeometry.new(4, 4, 32), b, b, b, b.clone(), 1, 0)
     with pytest.raises(m.InvalidGeometry):

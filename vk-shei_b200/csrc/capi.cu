@@ -897,7 +897,7 @@ int mslim_cuda_prefill_causal(const mslim_geometry_t *geometry, const void *q, c
     if (!mslim::prefill_supported(geometry->head_dim, geometry->query_heads / geometry->kv_heads))
         return fail(MSLIM_ERR_INVALID_GEOMETRY,
                     "head_dim %u with %u query heads per KV head has no sm_100a prefill kernel "
-                    "(head_dim 64..128, a multiple of 8)",
+                    "(head_dim 64..256, a multiple of 8)",
                     geometry->head_dim, geometry->query_heads / geometry->kv_heads);
     if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(out, 16))
         return fail(MSLIM_ERR_SHAPE_MISMATCH, "prefill buffers must be 16-byte aligned");
@@ -909,7 +909,7 @@ int mslim_cuda_prefill_causal(const mslim_geometry_t *geometry, const void *q, c
         const uint64_t kd[3] = {D, geometry->kv_heads, history};
         const uint64_t ks[2] = {D * 2, (uint64_t)geometry->kv_heads * D * 2};
         const uint32_t box[3] = {64, 1, 128};
-        const uint32_t kvbox[3] = {64, 1, 128};
+        const uint32_t kvbox[3] = {64, 1, mslim::prefill_kv_box_rows(geometry->head_dim)};
         if (int rc = make_tmap(&qmap, q, 3, qd, qs, box)) return rc;
         if (int rc = make_tmap(&omap, out, 3, qd, qs, box)) return rc;
         if (int rc = make_tmap(&kmap, k, 3, kd, ks, kvbox)) return rc;

@@ -23,9 +23,15 @@
 //       completes), then a softmax warpgroup per head, one thread per query
 //       row, which also rescales O in TMEM and writes the output through a
 //       swizzled staging buffer and bulk tensor stores.
-//   mslim_prefill_causal  odd groups: one head per CTA, S double-buffered in
-//       TMEM (S(j+1) issued before PV(j)), eight softmax warps taking 64 keys
-//       each and exchanging row maxima through shared memory.
+//   mslim_prefill_causal  odd groups, and head_dim 256: one head per CTA, S
+//       double-buffered in TMEM (S(j+1) issued before PV(j)), eight softmax
+//       warps taking half a key tile each and exchanging row maxima through
+//       shared memory; 128-key tiles, or 64-key tiles at head_dim 256 (O then
+//       takes 256 TMEM columns).
+//
+// head_dim: the kernels run at 64, 128 or 256; a smaller multiple of 8 (from
+// 64) runs zero-padded by the TMA (columns past head_dim read as zeros, the
+// stores stop at head_dim).
 //
 // TMA loads read this GPU's HBM only (128-byte swizzle, no multicast); K and
 // V have separate rings, a K slot is released once S_j is computed, a V slot
@@ -44,10 +50,7 @@ namespace {
 
 constexpr int kRows = 128;                 // query rows per CTA = TMEM lanes
 constexpr int kKeys = 128;                 // keys per tile
-constexpr int kDim = 128;                  // head_dim
 constexpr int kBox = kRows * 128;          // one [128 rows][64 bf16] swizzled box: 16 KB
-constexpr int kQBytes = 2 * kBox;          // Q tile (two 64-column boxes)
-constexpr int kTileBytes = 2 * kBox;       // one K or V tile
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColO = 256;     // S[2] at 0/128, O (accumulating) at 256
 // A row's running max is only moved (and O rescaled in TMEM) when a tile's
@@ -60,23 +63,48 @@ constexpr float kRescaleLog2 = 8.0f;
 constexpr uint32_t kIdescS = (1u << 4) | (1u << 7) | (1u << 10) | ((kKeys >> 3) << 17) | ((kRows >> 4) << 24);
 constexpr uint32_t kIdescPV = kIdescS | (1u << 16);
 
-// One head per CTA, S double-buffered in TMEM.
-//   TMEM: S[0] (0), S[1] (128), O (256, accumulating).  P(j) is written as bf16
-//         pairs over the first 64 columns of S[j & 1] once S(j) sits in
-//         registers, and O += P V is a TS-MMA (A from TMEM).
+// One head per CTA, S double-buffered in TMEM (any GQA group; head_dim 128,
+// or 256 with 64-key tiles).
+//   TMEM: S[0], S[1] (kKeys columns each), then O (head_dim columns,
+//         accumulating).  P(j) is written as bf16 pairs over the first
+//         kKeys / 2 columns of S[j & 1] once S(j) sits in registers, and
+//         O += P V is a TS-MMA (A from TMEM).
 //   Tensor-core order: S(0), then per tile j: S(j+1), PV(j).  S(j+1) goes to
 //         the other buffer, so the softmax of tile j+1 overlaps PV(j) and
 //         S(j+2); S(j+2) reuses buffer j & 1 only after PV(j) (in-order pipe).
-//   smem: Q (32 KB), K ring 2 x 32 KB, V ring 2 x 32 KB (160 KB).
+//   smem: Q (128 rows x head_dim), K ring 2 x 32 KB, V ring 2 x 32 KB
+//         (160 KB at head_dim 128, 192 KB at 256).
 //   Warps: 0 TMA Q+K, 1 MMA, 2 TMA V, 3 idle; 4-11 softmax, a warp pair
-//         (w, w+4) per 32 TMEM lanes (rows): warps 4-7 keys 0..63 of a tile
-//         (and output dims 0..63), warps 8-11 keys 64..127 (dims 64..127); the
-//         pair exchanges row maxima through shared memory.
-constexpr int kSOffK = kQBytes;
-constexpr int kSOffV = kSOffK + 2 * kTileBytes;
-constexpr int kSOffX = kSOffV + 2 * kTileBytes;     // row-max / row-sum exchange
-constexpr int kSOffBar = kSOffX + 6 * kRows * 4;
-constexpr int kSSmemBytes = kSOffBar + 512 + 1024;
+//         (w, w+4) per 32 TMEM lanes (rows): warps 4-7 the first half of a
+//         tile's keys (and of the output dims), warps 8-11 the second half;
+//         the pair exchanges row maxima through shared memory.
+template <int D>
+struct SingleShape {
+    static_assert(D == 128 || D == 256, "single-head prefill head_dim");
+    static constexpr int kKeysT = D == 256 ? 64 : 128;  // keys per tile
+    static constexpr int kBoxes = D / 64;               // 64-column boxes per row
+    static constexpr int kQBytes = kBoxes * kBox;       // Q: 128 rows
+    static constexpr int kKVBox = kKeysT * 128;         // one [kKeysT rows][64 bf16] box
+    static constexpr int kTileBytes = kBoxes * kKVBox;  // one K or V tile (32 KB)
+    static constexpr int kHalfKeys = kKeysT / 2;        // keys of one softmax half
+    static constexpr int kHalfDims = D / 2;             // output dims of one softmax half
+    static constexpr uint32_t kColO = 2 * kKeysT;       // O after S[0], S[1]
+    static constexpr int kOffK = kQBytes;
+    static constexpr int kOffV = kOffK + 2 * kTileBytes;
+    static constexpr int kOffX = kOffV + 2 * kTileBytes;  // row-max / row-sum exchange
+    static constexpr int kOffBar = kOffX + 6 * kRows * 4;
+    static constexpr int kSmemBytes = kOffBar + 512 + 1024;
+    // S: M 128, N kKeysT, A and B K-major; PV: N = D, B (V) MN-major
+    static constexpr uint32_t kIdescS =
+        (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kKeysT >> 3) << 17) | ((kRows >> 4) << 24);
+    static constexpr uint32_t kIdescPV =
+        (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((uint32_t)(D >> 3) << 17) | ((kRows >> 4) << 24);
+    static_assert(kColO + D <= kTmemCols, "TMEM columns");
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory per block");
+};
+static_assert(SingleShape<128>::kColO == kColO && SingleShape<128>::kIdescS == kIdescS &&
+                  SingleShape<128>::kIdescPV == kIdescPV,
+              "head_dim 128 keeps the single-head layout");
 constexpr int kSThreads = 12 * 32;
 // One pair of P columns in eight goes through the FMA-pipe exp2, the rest
 // through MUFU (the measured best split); both prefill kernels use the same
@@ -101,14 +129,17 @@ __device__ __forceinline__ void pair_sync(int quarter) {
     asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
 }
 
+template <int D>
 __global__ void __launch_bounds__(kSThreads, 1)
     mslim_prefill_causal(const __grid_constant__ CUtensorMap qmap,
                          const __grid_constant__ CUtensorMap kmap,
                          const __grid_constant__ CUtensorMap vmap, const PrefillParams p) {
     extern __shared__ uint8_t smem_raw[];
+    using SS = SingleShape<D>;
+    constexpr int kKeysT = SS::kKeysT;
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    SingleBars *bars = reinterpret_cast<SingleBars *>(smem + kSOffBar);
+    SingleBars *bars = reinterpret_cast<SingleBars *>(smem + SS::kOffBar);
     volatile int *abort_flag = &bars->abort;
 
     const int bid = blockIdx.x;
@@ -117,7 +148,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
     const int kvh = qh / p.group;
     const int q0 = qt * kRows;
     const int last_row = min(q0 + kRows, p.queries) - 1;
-    const int n_kv = (p.prior + last_row) / kKeys + 1;  // key tiles this CTA needs
+    const int n_kv = (p.prior + last_row) / kKeysT + 1;  // key tiles this CTA needs
     const int first_pos = p.prior + q0;                 // smallest query position here
 
     const int warp = threadIdx.x >> 5;
@@ -151,13 +182,14 @@ __global__ void __launch_bounds__(kSThreads, 1)
             const CUtensorMap *map = is_k ? &kmap : &vmap;
             uint64_t *full = is_k ? bars->k_full : bars->v_full;
             uint64_t *empty = is_k ? bars->k_empty : bars->v_empty;
-            uint8_t *ring = smem + (is_k ? kSOffK : kSOffV);
+            uint8_t *ring = smem + (is_k ? SS::kOffK : SS::kOffV);
             prefetch_tmap(map);
             if (is_k) {
                 prefetch_tmap(&qmap);
-                mbar_arrive_expect_tx(&bars->q_full, kQBytes);
-                tma_load_3d(smem, &qmap, &bars->q_full, 0, qh, q0);
-                tma_load_3d(smem + kBox, &qmap, &bars->q_full, 64, qh, q0);
+                mbar_arrive_expect_tx(&bars->q_full, SS::kQBytes);
+#pragma unroll
+                for (int bx = 0; bx < SS::kBoxes; ++bx)
+                    tma_load_3d(smem + bx * kBox, &qmap, &bars->q_full, bx * 64, qh, q0);
             }
             int issued = 0;
             for (int j = 0; j < n_kv && !*abort_flag; ++j) {
@@ -166,10 +198,11 @@ __global__ void __launch_bounds__(kSThreads, 1)
                     *abort_flag = 1;
                     break;
                 }
-                uint8_t *dst = ring + st * kTileBytes;
-                mbar_arrive_expect_tx(&full[st], kTileBytes);
-                tma_load_3d(dst, map, &full[st], 0, kvh, j * kKeys);
-                tma_load_3d(dst + kBox, map, &full[st], 64, kvh, j * kKeys);
+                uint8_t *dst = ring + st * SS::kTileBytes;
+                mbar_arrive_expect_tx(&full[st], SS::kTileBytes);
+#pragma unroll
+                for (int bx = 0; bx < SS::kBoxes; ++bx)
+                    tma_load_3d(dst + bx * SS::kKVBox, map, &full[st], bx * 64, kvh, j * kKeysT);
                 issued = j + 1;
             }
             // Our copies must land before the CTA can retire.
@@ -185,9 +218,20 @@ __global__ void __launch_bounds__(kSThreads, 1)
             auto issue_s = [&](int j) -> bool {
                 if (!wait_all(&bars->k_full[j & 1], (j >> 1) & 1, 22)) return false;
                 tc_fence_after();
-                const uint32_t kaddr = sbase + kSOffK + (j & 1) * kTileBytes;
-                umma_bf16_ss_k128(tmem + kColS + (j & 1) * 128, umma_desc_sw128(sbase, 16, 1024),
-                                  umma_desc_sw128(kaddr, 16, 1024), kIdescS, 0u, kBox >> 4);
+                const uint32_t kaddr = sbase + SS::kOffK + (j & 1) * SS::kTileBytes;
+                const uint32_t sdst = tmem + kColS + (j & 1) * kKeysT;
+                if constexpr (D == 128) {
+                    umma_bf16_ss_k128(sdst, umma_desc_sw128(sbase, 16, 1024), umma_desc_sw128(kaddr, 16, 1024),
+                                      SS::kIdescS, 0u, kBox >> 4);
+                } else {
+                    // one group of four K=16 steps per 64-column box (Q and K
+                    // boxes have different row counts, so different strides)
+#pragma unroll
+                    for (int bx = 0; bx < SS::kBoxes; ++bx)
+                        umma_bf16_ss_k64(sdst, umma_desc_sw128(sbase + bx * kBox, 16, 1024),
+                                         umma_desc_sw128(kaddr + bx * SS::kKVBox, 16, 1024), SS::kIdescS,
+                                         bx > 0 ? 1u : 0u);
+                }
                 umma_commit(&bars->s_full[j & 1]);
                 umma_commit(&bars->k_empty[j & 1]);
                 return true;
@@ -203,12 +247,15 @@ __global__ void __launch_bounds__(kSThreads, 1)
                      wait_all(&bars->p_full[j & 1], (j >> 1) & 1, 24);
                 if (!ok) break;
                 tc_fence_after();
-                const uint32_t vaddr = sbase + kSOffV + (j & 1) * kTileBytes;
+                const uint32_t vaddr = sbase + SS::kOffV + (j & 1) * SS::kTileBytes;
+                // 64 keys (four K=16 steps) per call: P columns advance 32 per
+                // 64 keys, V rows 64 per 64 keys; V's 64-column boxes are
+                // kKVBox bytes apart along N
 #pragma unroll
-                for (int half = 0; half < 2; ++half)
-                    umma_bf16_ts_k64(tmem + kColO, tmem + kColS + (j & 1) * 128 + half * 32,
-                                     umma_desc_sw128(vaddr + half * 4 * 16 * 128, kBox, 1024), kIdescPV,
-                                     (j > 0 || half > 0) ? 1u : 0u, (16 * 128) >> 4);
+                for (int kc = 0; kc < kKeysT / 64; ++kc)
+                    umma_bf16_ts_k64(tmem + SS::kColO, tmem + kColS + (j & 1) * kKeysT + kc * 32,
+                                     umma_desc_sw128(vaddr + kc * 4 * 16 * 128, SS::kKVBox, 1024), SS::kIdescPV,
+                                     (j > 0 || kc > 0) ? 1u : 0u, (16 * 128) >> 4);
                 umma_commit(j + 1 < n_kv ? &bars->o_full : &bars->o_done);
                 umma_commit(&bars->v_empty[j & 1]);
             }
@@ -217,14 +264,16 @@ __global__ void __launch_bounds__(kSThreads, 1)
     } else {
         // ---------------------------------------------------------- softmax --
         const int quarter = warp & 3;
-        const int half = (warp >> 2) - 1;              // keys (and dims) 64*half..+63
+        constexpr int kHK = SS::kHalfKeys, kHD = SS::kHalfDims;
+        const int half = (warp >> 2) - 1;  // keys kHK*half..+kHK-1 of a tile, output dims kHD*half..
         const int row = quarter * 32 + lane;
-        const int col0 = half * 64;
+        const int col0 = half * kHK;       // this half's first S column (key)
+        const int dim0 = half * kHD;       // this half's first output dim
         const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
-        const uint32_t ocol = lane_addr + kColO + col0;
+        const uint32_t ocol = lane_addr + SS::kColO + dim0;
         const int qpos = p.prior + q0 + row;
         const float scale = p.scale_log2;
-        float *xmax = reinterpret_cast<float *>(smem + kSOffX);  // [2 parity][2 half][128]
+        float *xmax = reinterpret_cast<float *>(smem + SS::kOffX);  // [2 parity][2 half][128]
         float *xsum = xmax + 4 * kRows;                           // [2 half][128]
         float m_used = -INFINITY, l_run = 0.f;
         bool ok = true;
@@ -236,20 +285,21 @@ __global__ void __launch_bounds__(kSThreads, 1)
                 break;
             }
             tc_fence_after();
-            const uint32_t scol = lane_addr + kColS + b * 128;
-            float v[64];
-            tmem_ld64(scol + col0, v);
-            const int k0 = j * kKeys + col0;
-            if (j * kKeys + kKeys - 1 > first_pos) {
+            const uint32_t scol = lane_addr + kColS + b * kKeysT;
+            float v[kHK];
+            if constexpr (kHK == 64) tmem_ld64(scol + col0, v);
+            else tmem_ld32(scol + col0, v);
+            const int k0 = j * kKeysT + col0;
+            if (j * kKeysT + kKeysT - 1 > first_pos) {
 #pragma unroll
-                for (int i = 0; i < 64; ++i)
+                for (int i = 0; i < kHK; ++i)
                     if (k0 + i > qpos) v[i] = -INFINITY;
             }
             float m8[8];
 #pragma unroll
             for (int a = 0; a < 8; ++a) m8[a] = fmaxf(v[a], v[a + 8]);
 #pragma unroll
-            for (int i = 16; i < 64; ++i) m8[i & 7] = fmaxf(m8[i & 7], v[i]);
+            for (int i = 16; i < kHK; ++i) m8[i & 7] = fmaxf(m8[i & 7], v[i]);
             float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
                              fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
             xmax[(b * 2 + half) * kRows + row] = mx;
@@ -270,7 +320,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
                 }
                 tc_fence_after();
 #pragma unroll
-                for (int c = 0; c < 2; ++c) {
+                for (int c = 0; c < kHD / 32; ++c) {
                     float o[32];
                     tmem_ld32(ocol + c * 32, o);
 #pragma unroll
@@ -281,9 +331,9 @@ __global__ void __launch_bounds__(kSThreads, 1)
             const uint64_t scale2 = f2_pack(scale, scale);
             const uint64_t nbase2 = f2_pack(-base, -base);
             uint64_t sum2[4] = {0, 0, 0, 0};
-            uint32_t w[32];
+            uint32_t w[kHK / 2];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
+            for (int i = 0; i < kHK / 2; ++i) {
                 float x0, x1;
                 f2_unpack(f2_fma(f2_pack(v[2 * i], v[2 * i + 1]), scale2, nbase2), x0, x1);
                 const float p0 = MSLIM_EXP_ON_FMA(i) ? exp2_fma(x0) : fast_exp2(x0);
@@ -291,8 +341,9 @@ __global__ void __launch_bounds__(kSThreads, 1)
                 sum2[i & 3] = f2_add(sum2[i & 3], f2_pack(p0, p1));
                 w[i] = pack_bf16x2(p0, p1);
             }
-            // keys 64*half..+63 -> P columns 32*half..+31 of S[b]
-            tmem_st32u_nowait(scol + half * 32, w);
+            // this half's keys -> P columns (kHK/2)*half.. of S[b]
+            if constexpr (kHK == 64) tmem_st32u_nowait(scol + half * 32, w);
+            else tmem_st16u_nowait(scol + half * 16, w);
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
@@ -312,10 +363,10 @@ __global__ void __launch_bounds__(kSThreads, 1)
             const float inv = 1.0f / (l_run + xsum[(half ^ 1) * kRows + row]);
             const int qrow = q0 + row;
             // rows are head_dim elements apart; columns past head_dim (zero
-            // padding of a head_dim below 128) are not written
-            uint16_t *dst = p.out + ((size_t)qrow * p.qheads + qh) * p.head_dim + col0;
+            // padding of a head_dim below the kernel's) are not written
+            uint16_t *dst = p.out + ((size_t)qrow * p.qheads + qh) * p.head_dim + dim0;
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
+            for (int c = 0; c < kHD / 32; ++c) {
                 float o[32];
                 tmem_ld32(ocol + c * 32, o);
                 uint32_t w[16];
@@ -324,7 +375,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
                 if (qrow < p.queries) {
 #pragma unroll
                     for (int t = 0; t < 4; ++t)
-                        if (col0 + c * 32 + t * 8 < p.head_dim)
+                        if (dim0 + c * 32 + t * 8 < p.head_dim)
                             reinterpret_cast<uint4 *>(dst + c * 32)[t] =
                                 make_uint4(w[4 * t], w[4 * t + 1], w[4 * t + 2], w[4 * t + 3]);
                 }
@@ -726,15 +777,17 @@ __global__ void __launch_bounds__(kPThreads, 1)
 }  // namespace
 
 bool prefill_supported(unsigned head_dim, unsigned group) {
-    // The kernels run at head_dim 64 (two-head kernel) or 128 (both); a
-    // smaller multiple of 8 runs zero-padded: the tensor maps describe the
-    // caller's head_dim, the TMA fills the columns past it with zeros (they
-    // add nothing to S, and their O columns are zero), and the output stores
-    // stop at head_dim.
-    return group >= 1 && head_dim >= 64 && head_dim <= 128 && head_dim % 8 == 0;
+    // The kernels run at head_dim 64 (two-head kernel), 128 (both) or 256
+    // (single-head kernel, 64-key tiles); a smaller multiple of 8 runs
+    // zero-padded: the tensor maps describe the caller's head_dim, the TMA
+    // fills the columns past it with zeros (they add nothing to S, and their
+    // O columns are zero), and the output stores stop at head_dim.
+    return group >= 1 && head_dim >= 64 && head_dim <= 256 && head_dim % 8 == 0;
 }
 
-bool prefill_pairs_heads(unsigned group) { return group % 2 == 0; }
+bool prefill_pairs_heads(unsigned group, unsigned head_dim) { return group % 2 == 0 && head_dim <= 128; }
+
+unsigned prefill_kv_box_rows(unsigned head_dim) { return head_dim > 128 ? 64 : 128; }
 
 namespace {
 
@@ -762,8 +815,11 @@ cudaError_t prefill_setup(int dev, int *sms) {
                 err = cudaFuncSetAttribute(mslim_prefill_pair<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            PairShape<64>::kSmemBytes);
             if (err == cudaSuccess)
-                err = cudaFuncSetAttribute(mslim_prefill_causal,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kSSmemBytes);
+                err = cudaFuncSetAttribute(mslim_prefill_causal<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           SingleShape<128>::kSmemBytes);
+            if (err == cudaSuccess)
+                err = cudaFuncSetAttribute(mslim_prefill_causal<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           SingleShape<256>::kSmemBytes);
             if (err == cudaSuccess) err = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
             d.err = err;
             d.state.store(err == cudaSuccess ? 1 : 2, std::memory_order_release);
@@ -784,7 +840,7 @@ cudaError_t launch_prefill(const CUtensorMap &qmap, const CUtensorMap &kmap,
     if (err != cudaSuccess) return err;
     err = prefill_setup(dev, &sms);
     if (err != cudaSuccess) return err;
-    if (prefill_pairs_heads((unsigned)p.group)) {
+    if (prefill_pairs_heads((unsigned)p.group, (unsigned)p.head_dim)) {
         // persistent: one CTA per SM (at most one per item)
         const long long items = (long long)p.n_qtiles * (p.qheads / 2);
         const unsigned grid = (unsigned)(items < sms ? items : sms);
@@ -795,7 +851,10 @@ cudaError_t launch_prefill(const CUtensorMap &qmap, const CUtensorMap &kmap,
                           stream, qmap, kmap, vmap, omap, p);
     }
     const unsigned grid = (unsigned)(p.n_qtiles * p.qheads);
-    mslim_prefill_causal<<<grid, kSThreads, kSSmemBytes, stream>>>(qmap, kmap, vmap, p);
+    if (p.head_dim > 128)
+        mslim_prefill_causal<256><<<grid, kSThreads, SingleShape<256>::kSmemBytes, stream>>>(qmap, kmap, vmap, p);
+    else
+        mslim_prefill_causal<128><<<grid, kSThreads, SingleShape<128>::kSmemBytes, stream>>>(qmap, kmap, vmap, p);
     return counted(cudaGetLastError());
 }
 
