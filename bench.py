@@ -81,6 +81,8 @@ def parse():
     ap.add_argument("--no-graph", action="store_true", help="C5 decode steps issued eagerly (no CUDA graph)")
     ap.add_argument("--decode-gemm", choices=["own", "cublas"], default="cublas",
                     help="C5 decode projections: cuBLAS (default) or mslim_cuda_gemv")
+    ap.add_argument("--gemv", action="store_true",
+                    help="the C5 decode projections: mslim_cuda_gemv against cuBLAS, per shape")
     ap.add_argument("--layer", action="store_true",
                     help="C3: one Llama-3-8B layer, 512-token prefill + 8 decode steps, CPU path beside it")
     return ap.parse_args()
@@ -376,6 +378,71 @@ def bench_prefill(m, torch, device, args) -> dict:
             "gpu_launches": captured, "clocks": clocks}
 
 
+GEMV_SHAPES = [("tp1_qkv", 6144, 4096), ("tp1_o", 4096, 4096), ("tp1_gate_up", 28672, 4096),
+               ("tp1_down", 4096, 14336), ("tp1_lm_head", 128256, 4096), ("tp8_qkv", 768, 4096),
+               ("tp8_o", 4096, 512), ("tp8_gate_up", 3584, 4096), ("tp8_down", 4096, 1792),
+               ("tp8_lm_head", 16032, 4096)]
+
+
+def bench_gemv(m, torch, device, args) -> dict:
+    """The C5 decode step's projections (batch 8 rows; TP 1 and per-rank TP 8
+    shapes) through mslim_cuda_gemv (the tcgen05 weight stream) and through
+    cuBLAS (torch.matmul), each as 40 calls captured in one CUDA graph, best
+    of five replays between CUDA events.  Weight copies rotate so that every
+    call streams its weights from HBM (> 400 MB of weights per replay)."""
+    from mslim_b200 import attention as att
+    torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = False
+    rows, reps = args.model_batch, 40
+    out = []
+    for name, n, k in GEMV_SHAPES:
+        wbytes = n * k * 2
+        copies = max(1, min(16, (400 << 20) // wbytes + 1))
+        gen = torch.Generator(device=device)
+        gen.manual_seed(11)
+        ws = [torch.randn((n, k), generator=gen, device=device, dtype=torch.bfloat16) * 0.02 for _ in range(copies)]
+        x = torch.randn((rows, k), generator=gen, device=device, dtype=torch.bfloat16)
+        y = torch.empty((rows, n), device=device, dtype=torch.bfloat16)
+        res = {"shape": name, "n": n, "k": k, "rows": rows, "weight_bytes": wbytes}
+        for kind in ("own", "cublas"):
+            def call(i, st):
+                w = ws[i % copies]
+                if kind == "own":
+                    att.gemv(x, w, y, rows, n, k, stream=st)
+                else:
+                    torch.matmul(x, w.t(), out=y)
+            stream = torch.cuda.current_stream()
+            for i in range(6):
+                call(i, stream)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            cap = torch.cuda.Stream()
+            cap.wait_stream(stream)
+            with torch.cuda.graph(graph, stream=cap, capture_error_mode="thread_local"):
+                for i in range(reps):
+                    call(i, torch.cuda.current_stream())
+            graph.replay()
+            torch.cuda.synchronize()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            best = float("inf")
+            for _ in range(5):
+                a.record(stream)
+                graph.replay()
+                b.record(stream)
+                b.synchronize()
+                best = min(best, a.elapsed_time(b) / reps)
+            del graph
+            res[f"{kind}_us"] = best * 1e3
+            res[f"{kind}_gbs"] = wbytes / (best * 1e-3) / 1e9
+        out.append(res)
+        del ws
+        torch.cuda.empty_cache()
+    if m.device_status(torch.cuda.current_device()) != 0:
+        raise SystemExit("device status reported an error during the GEMV leg")
+    return {"metric": "decode projection time (C5 shapes, batch rows)", "unit": "us", "shapes": out,
+            "peak_hbm_gbs": measured_peaks()["hbm_gbs"]}
+
+
 def bench_layer(m, torch, device, args) -> dict:
     """C3: one Llama-3-8B-shaped layer, 512-token
     prefill then 8 forced decode steps, dense KV and ColdStore-exact KV, device
@@ -574,6 +641,9 @@ def main():
     m.load()
     if args.layer:
         print(json.dumps(bench_layer(m, torch, device, args)), flush=True)
+        return
+    if args.gemv:
+        print(json.dumps(bench_gemv(m, torch, device, args)), flush=True)
         return
     if args.model:
         line = bench_model(m, torch, device, args, rank, world, dist)

@@ -286,6 +286,26 @@ struct DecodeConsumer {
         }
     }
 
+    // Drops the state of a finished split (the next stage always opens a new
+    // split, whose begin() sets all of it): constants are not held in
+    // registers across the code that runs between splits.
+    __device__ __forceinline__ void clear() {
+#pragma unroll
+        for (int ks = 0; ks < S::kKSteps; ++ks)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                qa[ks][e] = 0u;
+                if constexpr (QSPLIT) qb[ks][e] = 0u;
+            }
+#pragma unroll
+        for (int n = 0; n < S::kNTiles; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+        m_run[0] = m_run[1] = -INFINITY;
+        l_run[0] = l_run[1] = 0.f;
+        row_limit[0] = row_limit[1] = -1;
+        row_ok[0] = row_ok[1] = false;
+        row_q[0] = row_q[1] = 0;
+    }
+
     // The four warps' states combined in warp order into the item's split
     // partial {acc[D], m, l}.  Warps 1-3 hand their states over through
     // `scratch` ([3][16 rows][D + 2] floats, a stage buffer every consumer is
@@ -374,9 +394,14 @@ struct DecodeConsumer {
 struct UnitExtent {
     int ntok, prior, qg_first, qg_last, cta_end, slen, splits;
 };
-__device__ __forceinline__ UnitExtent unit_extent(const DecodeParams &p, int seq, int qblock) {
+// The session's token count as the caller gave it (before the cap).
+__device__ __forceinline__ int unit_tokens(const DecodeParams &p, int seq) {
+    return p.fixed_tokens >= 0 ? p.fixed_tokens : p.seq_tokens[seq];
+}
+// Extent of query block `qblock` of a session holding `tokens` tokens.
+__device__ __forceinline__ UnitExtent unit_extent_of(const DecodeParams &p, int tokens, int qblock) {
     UnitExtent u;
-    u.ntok = min(p.token_cap, p.fixed_tokens >= 0 ? p.fixed_tokens : p.seq_tokens[seq]);
+    u.ntok = min(p.token_cap, tokens);
     u.prior = u.ntok - p.nq;
     u.qg_first = qblock * p.q_per_cta;
     u.qg_last = min(p.nq, u.qg_first + p.q_per_cta) - 1;
@@ -385,6 +410,9 @@ __device__ __forceinline__ UnitExtent unit_extent(const DecodeParams &p, int seq
     u.slen = empty ? 0 : split_len(u.cta_end, p.split_tokens);
     u.splits = empty ? 0 : min((int)p.max_splits, (u.cta_end + u.slen - 1) / u.slen);
     return u;
+}
+__device__ __forceinline__ UnitExtent unit_extent(const DecodeParams &p, int seq, int qblock) {
+    return unit_extent_of(p, unit_tokens(p, seq), qblock);
 }
 
 // One CTA per (split, KV-head chunk, sequence x query block).
@@ -501,43 +529,54 @@ __device__ __forceinline__ void merge_item(const DecodeParams &p, const DecodeIt
         ls[r * kMaxFusedSplits + s] = __ldcg(src + D + 1);
     }
     asm volatile("bar.sync 1, %0;" ::"n"(kThr) : "memory");
-    for (int x = threadIdx.x; x < rows * D; x += kThr) {
-        const int r = x / D, d = x % D;
+    // A thread takes one row's two adjacent dims at a time (the partial rows
+    // are 8-byte aligned) with the loads of kBatch splits in flight, so an
+    // item of <= kBatch splits costs one round trip per pair; the sums run in
+    // split order, one split at a time (the arithmetic of
+    // mslim_decode_merge_row, so the bits are the same).
+    constexpr int kBatch = D >= 256 ? 4 : 8;  // (more would cost registers: at head_dim 128 the second CTA per SM)
+    constexpr int kPairs = D / 2;
+#pragma unroll 1
+    for (int x = threadIdx.x; x < rows * kPairs; x += kThr) {
+        const int r = x / kPairs, d = 2 * (x % kPairs);
         const int qg = it.qg_first + r / hc;
-        if (qg > it.qg_last) continue;
+        if (qg > it.qg_last || d >= p.head_dim) continue;
         const float *mr = ms + r * kMaxFusedSplits, *lr = ls + r * kMaxFusedSplits;
         float m = -INFINITY;
         for (int s = 0; s < nsplits; ++s) m = fmaxf(m, mr[s]);
         const float mb = (m == -INFINITY) ? 0.f : m;
-        float l = 0.f, acc = 0.f;
+        float l = 0.f, acc0 = 0.f, acc1 = 0.f;
         const float *src = part(r, 0) + d;
-        int s = 0;
-        for (; s + 8 <= nsplits; s += 8) {
-            float av[8];
+#pragma unroll 1
+        for (int s0 = 0; s0 < nsplits; s0 += kBatch) {
+            float2 av[kBatch];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) av[u] = __ldcg(src + (size_t)(s + u) * kRowF);
+            for (int u = 0; u < kBatch; ++u)
+                if (s0 + u < nsplits) av[u] = __ldcg(reinterpret_cast<const float2 *>(src + (size_t)(s0 + u) * kRowF));
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const float w = fast_exp2(mr[s + u] - mb);
-                l += w * lr[s + u];
-                acc += w * av[u];
+            for (int u = 0; u < kBatch; ++u) {
+                if (s0 + u < nsplits) {
+                    const float w = fast_exp2(mr[s0 + u] - mb);
+                    l += w * lr[s0 + u];
+                    acc0 += w * av[u].x;
+                    acc1 += w * av[u].y;
+                }
             }
         }
-        for (; s < nsplits; ++s) {
-            const float w = fast_exp2(mr[s] - mb);
-            l += w * lr[s];
-            acc += w * __ldcg(src + (size_t)s * kRowF);
-        }
         const float inv = (l > 0.f) ? 1.0f / l : 0.f;
-        if (d < p.head_dim) {
-            const int qh = it.kvh * p.group + it.hchunk * hc + r % hc;
-            p.out[(((size_t)it.seq * p.nq + qg) * p.qheads + qh) * p.head_dim + d] = bf16_bits_rn(acc * inv);
-        }
+        const int qh = it.kvh * p.group + it.hchunk * hc + r % hc;
+        *reinterpret_cast<uint32_t *>(p.out + (((size_t)it.seq * p.nq + qg) * p.qheads + qh) * p.head_dim + d) =
+            (uint32_t)bf16_bits_rn(acc0 * inv) | ((uint32_t)bf16_bits_rn(acc1 * inv) << 16);
     }
     asm volatile("bar.sync 1, %0;" ::"n"(kThr) : "memory");  // scratch is free again
 }
-constexpr int kMetaFirst = 1, kMetaLast = 2, kMetaDone = 4;
+// kMetaLate: the split is among the launch's last two waves of work, where a
+// merge would delay this CTA's remaining split past the others' (merges of
+// such items wait until the CTA has no more work).
+constexpr int kMetaFirst = 1, kMetaLast = 2, kMetaDone = 4, kMetaLate = 8;
 constexpr int kMaxUnits = 256;  // (sequence, query block) pairs the persistent kernel takes
+constexpr int kLenBuckets = 64;  // split-length buckets of the unit order (64 tokens each)
+constexpr int kMaxPending = 16;  // merges a CTA defers to the end of its work
 constexpr uint64_t kMaxDecodeItems = 16384;  // items whose counters the workspace head holds
 
 // Persistent form: a fixed grid of resident CTAs takes (item, split) work
@@ -565,9 +604,13 @@ __global__ void __launch_bounds__(kThreads)
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * (S::kStageBytes + kQSlot));
     uint64_t *empty = full + STAGES;
     StageMeta *meta = reinterpret_cast<StageMeta *>(empty + STAGES);
-    int *prefix = reinterpret_cast<int *>(meta + STAGES);  // [kMaxUnits + 1]
-    int *unit_end = prefix + kMaxUnits + 1;                 // [kMaxUnits] cta_end
-    int *unit_prior = unit_end + kMaxUnits;                 // [kMaxUnits] prior
+    int *prefix = reinterpret_cast<int *>(meta + STAGES);  // [kMaxUnits + 1] first split of each position
+    int *utok = prefix + kMaxUnits + 1;                     // [kMaxUnits] token count of each unit
+    int *order = utok + kMaxUnits;                          // [kMaxUnits] unit at each position
+    int *hist = order + kMaxUnits;                          // [kLenBuckets] positions per split length
+    volatile int *is_last = hist + kLenBuckets;             // consumers: merge the item now
+    volatile int *pend_n = is_last + 1;                     // consumers: merges deferred so far
+    volatile int *pend = pend_n + 1;                        // [kMaxPending] (item | nsplits << 16)
 
     griddep_launch_dependents();
     griddep_wait();  // inputs, and the counter the previous merge reset
@@ -578,26 +621,80 @@ __global__ void __launch_bounds__(kThreads)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kConsumerWarps);
         }
+        *pend_n = 0;
         fence_mbarrier_init();
     }
     __syncthreads();
 
     if (warp == kConsumerWarps) {
         // ------------------------------------------------------ producer --
-        // splits per unit, eight units per lane, then a warp-wide prefix sum
+        // Units are taken longest split first (a counting sort on the split
+        // length, 64-token buckets), so the last units of the launch are the
+        // shortest and the CTAs finish close together; the order decides only
+        // which CTA computes a split, never its arithmetic.
         const int units = p.n_seq * p.q_blocks;
-        int cnt[kMaxUnits / 32];
+        constexpr int kPer = kMaxUnits / 32;
+        // this lane's token counts first, all loads in flight together (the
+        // shared-memory stores below would otherwise order them one by one)
+        int toks[kPer];
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const int uix = lane * kPer + k;
+            toks[k] = uix < units ? unit_tokens(p, uix / p.q_blocks) : 0;
+        }
+        for (int b = lane; b < kLenBuckets; b += 32) hist[b] = 0;
+        __syncwarp();
+        int key[kPer], rank[kPer];  // split-length bucket (kLenBuckets: no unit), place in it
+        int nspl[kPer];
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const int uix = lane * kPer + k;
+            key[k] = kLenBuckets;  // no unit
+            nspl[k] = 0;
+            if (uix < units) {
+                utok[uix] = toks[k];
+                const UnitExtent u = unit_extent_of(p, toks[k], uix % p.q_blocks);
+                nspl[k] = u.splits;
+                key[k] = u.splits ? kLenBuckets - 1 - min(kLenBuckets - 1, u.slen / kTileT) : kLenBuckets - 1;
+            }
+            // rank within the bucket: the lanes holding the same key this round
+            // share one shared-memory atomic (most units of a batch fall in a
+            // few buckets, and colliding atomics would serialise)
+            const unsigned peers = __match_any_sync(0xffffffffu, key[k]);
+            const int leader = __ffs(peers) - 1;
+            int base = 0;
+            if (lane == leader && key[k] < kLenBuckets) base = atomicAdd(&hist[key[k]], __popc(peers));
+            base = __shfl_sync(0xffffffffu, base, leader);
+            rank[k] = base + __popc(peers & ((1u << lane) - 1u));
+        }
+        __syncwarp();
+        {
+            // exclusive scan of the bucket counts, two buckets per lane
+            static_assert(kLenBuckets == 64, "two buckets per lane");
+            const int h0 = hist[2 * lane], h1 = hist[2 * lane + 1];
+            int incl = h0 + h1;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += v;
+            }
+            __syncwarp();
+            hist[2 * lane] = incl - h0 - h1;
+            hist[2 * lane + 1] = incl - h1;
+        }
+        __syncwarp();
+        // order entry: unit index (low 16 bits) and its split count
+#pragma unroll
+        for (int k = 0; k < kPer; ++k)
+            if (key[k] < kLenBuckets) order[hist[key[k]] + rank[k]] = (lane * kPer + k) | (nspl[k] << 16);
+        __syncwarp();
+        // splits per position, then a warp-wide prefix sum over positions
+        int cnt[kPer];
         int local = 0;
 #pragma unroll
-        for (int k = 0; k < kMaxUnits / 32; ++k) {
-            const int uix = lane * (kMaxUnits / 32) + k;
-            cnt[k] = 0;
-            if (uix < units) {
-                const UnitExtent u = unit_extent(p, uix / p.q_blocks, uix % p.q_blocks);
-                cnt[k] = u.splits;
-                unit_end[uix] = u.cta_end;
-                unit_prior[uix] = u.prior;
-            }
+        for (int k = 0; k < kPer; ++k) {
+            const int pk = lane * kPer + k;
+            cnt[k] = pk < units ? (order[pk] >> 16) : 0;
             local += cnt[k];
         }
         int incl = local;
@@ -608,8 +705,8 @@ __global__ void __launch_bounds__(kThreads)
         }
         int run = incl - local;
 #pragma unroll
-        for (int k = 0; k < kMaxUnits / 32; ++k) {
-            prefix[lane * (kMaxUnits / 32) + k] = run;
+        for (int k = 0; k < kPer; ++k) {
+            prefix[lane * kPer + k] = run;
             run += cnt[k];
         }
         if (lane == 31) prefix[kMaxUnits] = incl;
@@ -626,17 +723,19 @@ __global__ void __launch_bounds__(kThreads)
             while (ok && g < total) {
                 const long long g_next = (long long)gridDim.x + atomicAdd(p.work_counter, 1u);
                 const int w = (int)(g / H), hcid = (int)(g % H);
-                int lo = 0, hi = units;  // the last unit whose prefix is <= w
+                int lo = 0, hi = units;  // the last position whose prefix is <= w
                 while (hi - lo > 1) {
                     const int mid = (lo + hi) >> 1;
                     if (prefix[mid] <= w) lo = mid;
                     else hi = mid;
                 }
-                const int seq = lo / p.q_blocks;
-                const int qg_first = (lo % p.q_blocks) * p.q_per_cta;
-                const int qg_last = min(p.nq, qg_first + p.q_per_cta) - 1;
-                const int cta_end = unit_end[lo];
-                const int slen = split_len(cta_end, p.split_tokens);
+                const int unit = order[lo] & 0xffff;
+                const int seq = unit / p.q_blocks;
+                const UnitExtent ue = unit_extent_of(p, utok[unit], unit % p.q_blocks);
+                const int qg_first = ue.qg_first;
+                const int qg_last = ue.qg_last;
+                const int cta_end = ue.cta_end;
+                const int slen = ue.slen;
                 const int split = w - prefix[lo];
                 const int t_begin = split * slen;
                 const int t_end = min(cta_end, t_begin + slen);
@@ -653,13 +752,14 @@ __global__ void __launch_bounds__(kThreads)
                     m.kvh = kvh;
                     m.hchunk = hchunk;
                     m.split = split;
-                    m.prior = unit_prior[lo];
+                    m.prior = ue.prior;
                     m.qg_first = qg_first;
                     m.qg_last = qg_last;
                     m.t0 = t_begin + t * kTileT;
                     m.t_end = t_end;
-                    m.flags = (t == 0 ? kMetaFirst : 0) | (t == ntiles - 1 ? kMetaLast : 0);
-                    m.item = lo * H + hcid;
+                    m.flags = (t == 0 ? kMetaFirst : 0) | (t == ntiles - 1 ? kMetaLast : 0) |
+                              (g + 2LL * gridDim.x >= total ? kMetaLate : 0);
+                    m.item = unit * H + hcid;
                     m.nsplits = prefix[lo + 1] - prefix[lo];
                     if (t == 0) {
                         // the unit's query rows, hc heads of each query row side by side
@@ -699,7 +799,8 @@ __global__ void __launch_bounds__(kThreads)
         // units without keys (empty sessions) have no split to merge: their
         // rows are written as zeros by CTA u % grid
         for (int uix = 0; uix < units; ++uix) {
-            if (prefix[uix + 1] != prefix[uix] || uix % (int)gridDim.x != (int)blockIdx.x) continue;
+            if (uix % (int)gridDim.x != (int)blockIdx.x || unit_extent_of(p, utok[uix], uix % p.q_blocks).splits != 0)
+                continue;
             const int seq = uix / p.q_blocks;
             const int qg_first = (uix % p.q_blocks) * p.q_per_cta;
             const int qg_last = min(p.nq, qg_first + p.q_per_cta) - 1;
@@ -711,14 +812,17 @@ __global__ void __launch_bounds__(kThreads)
     }
 
     // ----------------------------------------------------------- consumers --
-    volatile int *is_last = unit_prior + kMaxUnits;
     DecodeConsumer<D, false> cs;
     DecodeItem it{};
+    bool streamed = false;  // the loop ended on the producer's end-of-work stage
     for (int i = 0;; ++i) {
         const int s = i % STAGES;
         if (!mbar_wait(&full[s], (i / STAGES) & 1, p.status, 3)) break;
         const StageMeta m = meta[s];
-        if (m.flags & kMetaDone) break;
+        if (m.flags & kMetaDone) {
+            streamed = true;
+            break;
+        }
         uint8_t *stage = smem + s * S::kStageBytes;
         if (m.flags & kMetaFirst) {
             it.seq = m.seq;
@@ -735,11 +839,24 @@ __global__ void __launch_bounds__(kThreads)
             // the split's last stage is the combine's (and the merge's)
             // scratch before it is released
             cs.finish(p, it, reinterpret_cast<float *>(stage), warp, lane);
-            // the partial is out (warp 0 wrote it); the last split of the item
-            // merges it
+            cs.clear();
+            // The partial is out (warp 0 wrote it).  The CTA whose split
+            // completes the item merges it: at once while plenty of work is
+            // left (other CTAs take up the slack), and in the launch's last
+            // two waves after its own last split, from the queue of pending
+            // merges (a merge under full HBM load costs several L2 round trips
+            // and would make this CTA's remaining split finish last), or at
+            // once when that queue is full.
             if (warp == 0) __threadfence();
             asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
-            if (threadIdx.x == 0) *is_last = atomicAdd(&p.item_counters[m.item], 1u) + 1 == (unsigned)m.nsplits;
+            if (threadIdx.x == 0) {
+                int now = 0;
+                if (atomicAdd(&p.item_counters[m.item], 1u) + 1 == (unsigned)m.nsplits) {
+                    if ((m.flags & kMetaLate) && *pend_n < kMaxPending) pend[(*pend_n)++] = m.item | (m.nsplits << 16);
+                    else now = 1;
+                }
+                *is_last = now;
+            }
             asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
             if (*is_last) {
                 __threadfence();
@@ -749,6 +866,28 @@ __global__ void __launch_bounds__(kThreads)
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    // The deferred merges, once this CTA has no more splits to compute (every
+    // stage is consumed, so stage 0 is the merge's scratch).  Skipped after a
+    // wait that gave up: copies may still be landing in the stages.
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+    const int npend = streamed ? *pend_n : 0;
+    if (npend > 0) {
+        __threadfence();
+        const int H = p.kvheads * p.head_chunks;
+        for (int k = 0; k < npend; ++k) {
+            const int e = pend[k];
+            const int item = e & 0xffff, nsplits = e >> 16;
+            const int unit = item / H, hcid = item % H;
+            DecodeItem mi{};
+            mi.seq = unit / p.q_blocks;
+            mi.qg_first = (unit % p.q_blocks) * p.q_per_cta;
+            mi.qg_last = min(p.nq, mi.qg_first + p.q_per_cta) - 1;
+            mi.kvh = hcid / p.head_chunks;
+            mi.hchunk = hcid % p.head_chunks;
+            merge_item<D>(p, mi, nsplits, reinterpret_cast<float *>(smem));
+            if (threadIdx.x == 0) p.item_counters[item] = 0u;
+        }
     }
 }
 
@@ -892,7 +1031,8 @@ cudaError_t launch_impl(const CUtensorMap &kmap, const CUtensorMap &vmap, const 
         (reinterpret_cast<uintptr_t>(p.q) & 15u) == 0) {
         // persistent: as many CTAs as stay resident, at most one per work unit
         const size_t smem = (size_t)STAGES * (S::kStageBytes + 16 * D * 2) + 2 * STAGES * sizeof(uint64_t) +
-                            STAGES * sizeof(StageMeta) + (3 * kMaxUnits + 2) * sizeof(int) + 1024;
+                            STAGES * sizeof(StageMeta) + (3 * kMaxUnits + 1 + kLenBuckets + 2 + kMaxPending) * sizeof(int) +
+                            1024;
         auto kernel = mslim_decode_persist<D, STAGES, PAGED>;
         static int per_sm = 0, sms = 0;  // resident CTAs of this form (same on every B200)
         if (!per_sm) {
