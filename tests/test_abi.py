@@ -135,8 +135,8 @@ def test_geometry_rules(m):
 def test_decode_workspace_bytes(m):
     g = m.AttentionGeometry.new(32, 8, 128)
     # a head of work counters (two words, then one arrival counter per item,
-    # 16384 items) and the split partials {acc[128], m, l} in f32
-    assert m.decode_workspace_bytes(g, 64, 32768, 2048) == 256 + 4 * 16384 + 64 * 32 * 16 * 130 * 4
+    # 16384 items) and the split partials {acc[128], m, l, 2 pad} in f32
+    assert m.decode_workspace_bytes(g, 64, 32768, 2048) == 256 + 4 * 16384 + 64 * 32 * 16 * 132 * 4
     with pytest.raises(m.ShapeMismatch):
         m.decode_workspace_bytes(g, 1, 100, 100)
 

@@ -98,7 +98,7 @@ def test_static_scratch_rejects_oversized_requests(m):
     rng = np.random.default_rng(22)
     case = make_case(m, rng, [32768] * 4)
     out = empty_u16((4, 32, 128))
-    # 4 sessions x 32 heads x 512 splits of 64 tokens x 130 floats > 16 MiB
+    # 4 sessions x 32 heads x 512 splits of 64 tokens x 132 floats > 16 MiB
     rc = call_static(m, g, case, out, 64)
     assert rc == m._lib.ERR_SHAPE_MISMATCH
     assert "static scratch" in m._lib.last_error()

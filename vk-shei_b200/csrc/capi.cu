@@ -227,7 +227,8 @@ constexpr uint64_t kMaxDecodeItems = 16384;
 constexpr uint64_t kDecodeCounterBytes = 256 + 4 * kMaxDecodeItems;
 
 uint64_t partial_bytes(const mslim_geometry_t *g, uint64_t n_seq, uint64_t nq, uint64_t splits) {
-    return kDecodeCounterBytes + n_seq * nq * g->query_heads * splits * (kernel_dim_for(g->head_dim) + 2) * sizeof(float);
+    // split partials {acc[D], m, l, 2 pad} (D + 4 floats: 16-byte records)
+    return kDecodeCounterBytes + n_seq * nq * g->query_heads * splits * (kernel_dim_for(g->head_dim) + 4) * sizeof(float);
 }
 
 struct DecodeCall {

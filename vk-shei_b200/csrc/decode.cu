@@ -34,6 +34,9 @@ namespace mslim {
 namespace {
 
 constexpr int kTileT = 64;       // tokens per pipeline stage
+// A split partial in global memory is {acc[D], m, l} and two pad floats:
+// D + 4 floats, a multiple of 16 bytes, so any run of partials is one bulk copy.
+constexpr int kPartPad = 4;
 constexpr int kWarpTokens = 16;  // tokens per consumer warp per stage
 constexpr int kConsumerWarps = kTileT / kWarpTokens;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
@@ -364,8 +367,8 @@ struct DecodeConsumer {
                     l += wgt[w] * lw[w];
                 }
                 const int qh = it.kvh * p.group + it.hchunk * hc + r % hc;
-                float *dst = p.partials +
-                             ((((size_t)it.seq * p.nq + row_q[h]) * p.qheads + qh) * p.max_splits + it.split) * kRowF;
+                float *dst = p.partials + ((((size_t)it.seq * p.nq + row_q[h]) * p.qheads + qh) * p.max_splits +
+                                           it.split) * (D + kPartPad);
 #pragma unroll
                 for (int n = 0; n < S::kNTiles; ++n) {
 #pragma unroll
@@ -511,7 +514,7 @@ constexpr int kMaxFusedSplits = 64;  // splits per item the in-kernel merge take
 template <int D>
 __device__ __forceinline__ void merge_item(const DecodeParams &p, const DecodeItem &it, int nsplits,
                                            float *scratch) {
-    constexpr int kRowF = D + 2;
+    constexpr int kRowF = D + kPartPad;
     constexpr int kThr = kConsumerWarps * 32;
     const int hc = p.heads_per_cta;
     const int rows = p.q_per_cta * hc;
@@ -570,6 +573,61 @@ __device__ __forceinline__ void merge_item(const DecodeParams &p, const DecodeIt
     }
     asm volatile("bar.sync 1, %0;" ::"n"(kThr) : "memory");  // scratch is free again
 }
+// merge_item from shared memory: every valid row's first `nsplits` partials
+// (contiguous 16-byte records) come in by one bulk copy per row, completing on
+// `bar`, so the merge costs one round trip instead of a few dependent ones;
+// `scratch` (free shared memory) holds them.  Same arithmetic and order as
+// merge_item, so the bits are the same.
+template <int D>
+__device__ __forceinline__ void merge_item_bulk(const DecodeParams &p, const DecodeItem &it, int nsplits,
+                                                float *scratch, uint64_t *bar, uint32_t parity) {
+    constexpr int kRowF = D + kPartPad;
+    constexpr int kThr = kConsumerWarps * 32;
+    const int hc = p.heads_per_cta;
+    const int nrows = (it.qg_last - it.qg_first + 1) * hc;  // row r: query r / hc, head r % hc
+    // the stage's generic-proxy accesses are ordered before the copies' writes
+    fence_proxy_async_smem();
+    asm volatile("bar.sync 1, %0;" ::"n"(kThr) : "memory");
+    if (threadIdx.x == 0) {
+        const uint32_t row_bytes = (uint32_t)(nsplits * kRowF * sizeof(float));
+        mbar_arrive_expect_tx(bar, row_bytes * (uint32_t)nrows);
+        for (int r = 0; r < nrows; ++r) {
+            const int qg = it.qg_first + r / hc;
+            const int qh = it.kvh * p.group + it.hchunk * hc + r % hc;
+            bulk_load(scratch + (size_t)r * nsplits * kRowF,
+                      p.partials + (((size_t)it.seq * p.nq + qg) * p.qheads + qh) * p.max_splits * kRowF, row_bytes,
+                      bar);
+        }
+    }
+    mbar_wait(bar, parity, p.status, 5);
+    constexpr int kPairs = D / 2;
+#pragma unroll 1
+    for (int x = threadIdx.x; x < nrows * kPairs; x += kThr) {
+        const int r = x / kPairs, d = 2 * (x % kPairs);
+        if (d >= p.head_dim) continue;
+        const float *rec = scratch + (size_t)r * nsplits * kRowF;
+        float m = -INFINITY;
+#pragma unroll 1
+        for (int s = 0; s < nsplits; ++s) m = fmaxf(m, rec[s * kRowF + D]);
+        const float mb = (m == -INFINITY) ? 0.f : m;
+        float l = 0.f, acc0 = 0.f, acc1 = 0.f;
+#pragma unroll 1
+        for (int s = 0; s < nsplits; ++s) {
+            const float w = fast_exp2(rec[s * kRowF + D] - mb);
+            l += w * rec[s * kRowF + D + 1];
+            const float2 a = *reinterpret_cast<const float2 *>(rec + s * kRowF + d);
+            acc0 += w * a.x;
+            acc1 += w * a.y;
+        }
+        const float inv = (l > 0.f) ? 1.0f / l : 0.f;
+        const int qg = it.qg_first + r / hc;
+        const int qh = it.kvh * p.group + it.hchunk * hc + r % hc;
+        *reinterpret_cast<uint32_t *>(p.out + (((size_t)it.seq * p.nq + qg) * p.qheads + qh) * p.head_dim + d) =
+            (uint32_t)bf16_bits_rn(acc0 * inv) | ((uint32_t)bf16_bits_rn(acc1 * inv) << 16);
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kThr) : "memory");  // scratch is free again
+}
+
 // kMetaLate: the split is among the launch's last two waves of work, where a
 // merge would delay this CTA's remaining split past the others' (merges of
 // such items wait until the CTA has no more work).
@@ -603,7 +661,8 @@ __global__ void __launch_bounds__(kThreads)
     uint16_t *qslot = reinterpret_cast<uint16_t *>(smem + STAGES * S::kStageBytes);  // [STAGES][16 x D]
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * (S::kStageBytes + kQSlot));
     uint64_t *empty = full + STAGES;
-    StageMeta *meta = reinterpret_cast<StageMeta *>(empty + STAGES);
+    uint64_t *merge_bar = empty + STAGES;  // bulk copies of a merge's partials
+    StageMeta *meta = reinterpret_cast<StageMeta *>(merge_bar + 1);
     int *prefix = reinterpret_cast<int *>(meta + STAGES);  // [kMaxUnits + 1] first split of each position
     int *utok = prefix + kMaxUnits + 1;                     // [kMaxUnits] token count of each unit
     int *order = utok + kMaxUnits;                          // [kMaxUnits] unit at each position
@@ -621,6 +680,7 @@ __global__ void __launch_bounds__(kThreads)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kConsumerWarps);
         }
+        mbar_init(merge_bar, 1);
         *pend_n = 0;
         fence_mbarrier_init();
     }
@@ -634,13 +694,16 @@ __global__ void __launch_bounds__(kThreads)
         // which CTA computes a split, never its arithmetic.
         const int units = p.n_seq * p.q_blocks;
         constexpr int kPer = kMaxUnits / 32;
-        // this lane's token counts first, all loads in flight together (the
-        // shared-memory stores below would otherwise order them one by one)
+        // Units go round-robin over the lanes (unit k * 32 + lane), so a batch
+        // of up to 32 units is ranked in one round.  This lane's token counts
+        // first, all loads in flight together (the shared-memory stores below
+        // would otherwise order them one by one).
+        const int rounds = (units + 31) / 32;
         int toks[kPer];
 #pragma unroll
         for (int k = 0; k < kPer; ++k) {
-            const int uix = lane * kPer + k;
-            toks[k] = uix < units ? unit_tokens(p, uix / p.q_blocks) : 0;
+            const int uix = k * 32 + lane;
+            toks[k] = (k < rounds && uix < units) ? unit_tokens(p, uix / p.q_blocks) : 0;
         }
         for (int b = lane; b < kLenBuckets; b += 32) hist[b] = 0;
         __syncwarp();
@@ -648,9 +711,11 @@ __global__ void __launch_bounds__(kThreads)
         int nspl[kPer];
 #pragma unroll
         for (int k = 0; k < kPer; ++k) {
-            const int uix = lane * kPer + k;
             key[k] = kLenBuckets;  // no unit
             nspl[k] = 0;
+            rank[k] = 0;
+            if (k >= rounds) continue;  // warp-uniform
+            const int uix = k * 32 + lane;
             if (uix < units) {
                 utok[uix] = toks[k];
                 const UnitExtent u = unit_extent_of(p, toks[k], uix % p.q_blocks);
@@ -686,7 +751,7 @@ __global__ void __launch_bounds__(kThreads)
         // order entry: unit index (low 16 bits) and its split count
 #pragma unroll
         for (int k = 0; k < kPer; ++k)
-            if (key[k] < kLenBuckets) order[hist[key[k]] + rank[k]] = (lane * kPer + k) | (nspl[k] << 16);
+            if (key[k] < kLenBuckets) order[hist[key[k]] + rank[k]] = (k * 32 + lane) | (nspl[k] << 16);
         __syncwarp();
         // splits per position, then a warp-wide prefix sum over positions
         int cnt[kPer];
@@ -812,9 +877,22 @@ __global__ void __launch_bounds__(kThreads)
     }
 
     // ----------------------------------------------------------- consumers --
+    if constexpr (PAGED) {
+        // While the producer numbers the units, the grid's consumer threads
+        // pull the page table into L2 (one 128-byte line each, within the
+        // table), so the first tiles' page lookups do not wait on DRAM.
+        const size_t lines = ((size_t)p.n_seq * p.max_pages * sizeof(int32_t) + 127) / 128;
+        const size_t line = (size_t)blockIdx.x * (kConsumerWarps * 32) + threadIdx.x;
+        if (line < lines) prefetch_l2(reinterpret_cast<const uint8_t *>(p.page_table) + line * 128);
+    }
     DecodeConsumer<D, false> cs;
     DecodeItem it{};
     bool streamed = false;  // the loop ended on the producer's end-of-work stage
+    uint32_t merges = 0;    // merges this CTA ran from bulk copies (merge_bar's phase)
+    // one item's partials: rows x splits records
+    auto bulk_fits = [&](int nsplits, size_t bytes) {
+        return (size_t)p.q_per_cta * p.heads_per_cta * nsplits * (D + kPartPad) * sizeof(float) <= bytes;
+    };
     for (int i = 0;; ++i) {
         const int s = i % STAGES;
         if (!mbar_wait(&full[s], (i / STAGES) & 1, p.status, 3)) break;
@@ -860,7 +938,10 @@ __global__ void __launch_bounds__(kThreads)
             asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
             if (*is_last) {
                 __threadfence();
-                merge_item<D>(p, it, m.nsplits, reinterpret_cast<float *>(stage));
+                if (bulk_fits(m.nsplits, S::kStageBytes))
+                    merge_item_bulk<D>(p, it, m.nsplits, reinterpret_cast<float *>(stage), merge_bar, (merges++) & 1);
+                else
+                    merge_item<D>(p, it, m.nsplits, reinterpret_cast<float *>(stage));
                 if (threadIdx.x == 0) p.item_counters[m.item] = 0u;
             }
         }
@@ -885,7 +966,10 @@ __global__ void __launch_bounds__(kThreads)
             mi.qg_last = min(p.nq, mi.qg_first + p.q_per_cta) - 1;
             mi.kvh = hcid / p.head_chunks;
             mi.hchunk = hcid % p.head_chunks;
-            merge_item<D>(p, mi, nsplits, reinterpret_cast<float *>(smem));
+            if (bulk_fits(nsplits, (size_t)STAGES * S::kStageBytes))
+                merge_item_bulk<D>(p, mi, nsplits, reinterpret_cast<float *>(smem), merge_bar, (merges++) & 1);
+            else
+                merge_item<D>(p, mi, nsplits, reinterpret_cast<float *>(smem));
             if (threadIdx.x == 0) p.item_counters[item] = 0u;
         }
     }
@@ -914,7 +998,7 @@ __global__ void __launch_bounds__(D) mslim_decode_merge_row(const DecodeParams p
     const size_t sq = item / p.qheads;  // seq * nq + qg
     const int qg = (int)(sq % p.nq);
     const int seq = (int)(sq / p.nq);
-    constexpr int kRowF = D + 2;
+    constexpr int kRowF = D + kPartPad;
     const int splits = merge_splits(p, seq, qg);
     const float *src = p.partials + item * p.max_splits * kRowF;
     const int d = threadIdx.x;
@@ -963,7 +1047,7 @@ __global__ void __launch_bounds__(128) mslim_decode_merge(const DecodeParams p, 
     const size_t sq = item / p.qheads;  // seq * nq + qg
     const int qg = (int)(sq % p.nq);
     const int seq = (int)(sq / p.nq);
-    constexpr int kRowF = D + 2;
+    constexpr int kRowF = D + kPartPad;
     constexpr int kPer = D / 32;
     const int splits = merge_splits(p, seq, qg);
     const float *src = p.partials + item * p.max_splits * kRowF;
@@ -1030,7 +1114,7 @@ cudaError_t launch_impl(const CUtensorMap &kmap, const CUtensorMap &vmap, const 
         units * p.kvheads * p.head_chunks <= (uint64_t)kMaxDecodeItems && p.max_splits <= kMaxFusedSplits &&
         (reinterpret_cast<uintptr_t>(p.q) & 15u) == 0) {
         // persistent: as many CTAs as stay resident, at most one per work unit
-        const size_t smem = (size_t)STAGES * (S::kStageBytes + 16 * D * 2) + 2 * STAGES * sizeof(uint64_t) +
+        const size_t smem = (size_t)STAGES * (S::kStageBytes + 16 * D * 2) + (2 * STAGES + 1) * sizeof(uint64_t) +
                             STAGES * sizeof(StageMeta) + (3 * kMaxUnits + 1 + kLenBuckets + 2 + kMaxPending) * sizeof(int) +
                             1024;
         auto kernel = mslim_decode_persist<D, STAGES, PAGED>;

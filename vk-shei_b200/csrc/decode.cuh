@@ -10,7 +10,7 @@ struct DecodeParams {
     const float *q_f32;          // f32 query of the same shape (dense only), or null
     const int32_t *seq_tokens;   // [n_seq] tokens in each sequence's cache
     const int32_t *page_table;   // [n_seq][max_pages] physical page ids (paged only)
-    float *partials;             // [n_seq][nq][QH][max_splits][D + 2] (kernel D)
+    float *partials;             // [n_seq][nq][QH][max_splits][D + 4] (kernel D): acc, m, l, 2 pad
     unsigned *work_counter;      // [2]: work taken and CTAs done, zero on entry, left zero;
                                  // null: one CTA per split and a merge kernel instead of
                                  // the persistent form
