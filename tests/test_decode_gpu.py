@@ -450,3 +450,55 @@ def test_gpu_engine_reserves_its_workspace_when_built(m, wl, oracle):
         assert got.tobytes() == want.tobytes()        # same call, same split policy
     with pytest.raises(m.ShapeMismatch):
         eng.attention(qd, (kd, vd), empty_u16((qh, d)), cap + 1, g)
+
+
+@pytest.mark.parametrize("split_tokens", [1024, 256, 64])
+def test_persistent_kernel_and_split_merge_pair_give_the_same_bits(m, wl, oracle, split_tokens):
+    """The persistent decode (one launch: splits taken from a work counter,
+    units longest split first, each item merged in-kernel by the CTA whose
+    split completes it -- from a bulk copy of its partials, at once or after
+    that CTA's last split, or from plain loads when the partials do not fit
+    shared memory) returns the bits of the one-CTA-per-split kernel and its
+    separate merge.  A query buffer that is 4-byte but not 16-byte aligned
+    makes the library take the two-kernel form (the persistent kernel brings
+    query rows in by bulk copies) on the same bytes; the launch counter shows
+    which form ran.  Split sizes 1024, 256 and 64 give items of up to 4, 16
+    and 64 splits (every merge form)."""
+    torch = torch_mod()
+    g = m.AttentionGeometry.new(32, 8, 128)
+    rng = np.random.default_rng(1000 + split_tokens)
+    pt = 256
+    lengths = [4096, 1, 3000, 0, 777, 2500, 64, 4000]
+    pool = build_pool(wl, rng, lengths, 8, 128, pt)
+    q = rand_bf16(wl, rng, (len(lengths), 32, 128))
+    n_seq = len(lengths)
+    ws = torch.zeros(m.decode_workspace_bytes(g, n_seq, pool["max_tokens"], split_tokens), dtype=torch.uint8,
+                     device="cuda:0")
+    kp, vp, table = dev(pool["k_pool"]), dev(pool["v_pool"]), dev(pool["table"])
+    seq = dev(np.asarray(lengths, np.int32))
+    q_al = dev(q)
+    buf = torch.zeros(q.size + 8, dtype=torch.int16, device="cuda:0")
+    q_mis = buf[2:2 + q.size].view(q.shape)            # 4 bytes past a 16-byte boundary
+    q_mis.copy_(q_al)
+    assert q_al.data_ptr() % 16 == 0 and q_mis.data_ptr() % 16 == 4
+    outs, launches = [], []
+    for qd in (q_al, q_mis, q_al):
+        out = empty_u16((n_seq, 32, 128))
+        out.fill_(0x7FC1)
+        before = m.kernel_launches()
+        m.decode_paged(g, qd, kp, vp, pool["n_pages"], pt, table, pool["max_pages"], seq, n_seq, ws, out,
+                       split_tokens)
+        launches.append(m.kernel_launches() - before)
+        torch.cuda.synchronize()
+        assert m.device_status(0) == 0
+        outs.append(host_u16(out))
+    assert launches == [1, 2, 1], launches
+    assert outs[0].tobytes() == outs[1].tobytes()        # persistent == split + merge
+    assert outs[0].tobytes() == outs[2].tobytes()        # and again (counters left at zero)
+    for s, L in enumerate(lengths):
+        if L == 0:
+            assert not np.any(outs[0][s]), s
+            continue
+        ref = oracle.paged_attention_bf16(32, 8, 128, bf16_f32(q[s].reshape(-1)), pool["k_pool"], pool["v_pool"],
+                                          pool["table"][s], pt, L, 1)
+        assert max_abs(bf16_f32(outs[0][s].reshape(-1)), ref) <= TOL, s
