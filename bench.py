@@ -63,6 +63,8 @@ def parse():
     ap.add_argument("--no-model", action="store_true", help="skip the C5 tensor-parallel model leg")
     ap.add_argument("--no-weak", action="store_true", help="skip the weak-scaling figure at N > 1")
     ap.add_argument("--split-tokens", type=int, default=0)
+    ap.add_argument("--decode-schedule", choices=["split-merge", "persistent"], default="split-merge",
+                    help="mslim_cuda_set_decode_schedule for the run (same bits either way)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -639,6 +641,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device(device))
     m.load()
+    m.set_decode_schedule(m.DECODE_PERSISTENT if args.decode_schedule == "persistent" else m.DECODE_SPLIT_MERGE)
     if args.layer:
         print(json.dumps(bench_layer(m, torch, device, args)), flush=True)
         return
@@ -769,7 +772,7 @@ def main():
     traffic = profile_traffic("decode_c4_traffic.json")
     roofline = {"bound": "hbm", "kernel": ("mslim_decode_persist (split-KV with the merge in-kernel)"
                                            if timed_launches_per_step == 1 else
-                                           "mslim_decode_split + mslim_decode_merge"),
+                                           "mslim_decode_split + mslim_decode_merge_row"),
                 "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": achieved / peaks["hbm_gbs"] if peaks["hbm_gbs"] else None,
                 "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)" if peaks["source"] == "measured"
@@ -802,6 +805,8 @@ def main():
                                                "host-side session lengths"),
                        "l2": "no flush: inputs larger than L2 (%.2f GB per GPU per step)" % (step_bytes / 1e9),
                        "issue": "the K timed steps captured as one CUDA graph and replayed once",
+                       "decode_schedule": ("persistent" if m.get_decode_schedule() == m.DECODE_PERSISTENT
+                                           else "split + merge"),
                        "parallelism": (f"sessions LPT-sharded over {world} GPUs (strong: one 64-session C4 draw)"
                                        if strong else
                                        f"session-sharded x{world} ({args.scaling})"),

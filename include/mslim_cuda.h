@@ -189,6 +189,22 @@ int mslim_cuda_decode_split_tokens(const mslim_geometry_t *geometry, uint32_t n_
 int mslim_cuda_decode_split_tokens_for_lengths(const mslim_geometry_t *geometry, uint32_t n_seq,
                                                const int32_t *lengths, uint32_t *split_tokens);
 
+/* Decode schedule, process-wide: every decode entry point follows it.
+ * MSLIM_DECODE_SPLIT_MERGE (the default): one CTA per (split, KV-head chunk,
+ * sequence), then a merge kernel -- two launches per decode.
+ * MSLIM_DECODE_PERSISTENT: resident CTAs take splits from a work counter in
+ * the workspace head and merge each item in-kernel -- one launch -- where the
+ * shape allows (up to 256 sequence x query blocks, 64 splits, 16384 items, a
+ * 16-byte aligned bf16 query), the split + merge form otherwise.  Both return
+ * the same bits.  Measured on B200 at the C4 shapes (the shares of 1, 2, 4
+ * and 8 GPUs, splits from mslim_cuda_decode_split_tokens_for_lengths): split
+ * + merge 5-7 % faster.  Returns MSLIM_ERR_SHAPE_MISMATCH for another value.
+ * No reference counterpart. */
+#define MSLIM_DECODE_SPLIT_MERGE 0
+#define MSLIM_DECODE_PERSISTENT 1
+int mslim_cuda_set_decode_schedule(int schedule);
+int mslim_cuda_get_decode_schedule(void);
+
 /* Dense decode: GpuEngine::attention / exact_hot_fused_attention
  * (src/gpu_llm/gpu_resources.rs:583-643,783-828) for a batch of sequences.
  * q: bf16 [n_seq][QH][D] (post-RoPE); k_cache/v_cache: bf16 token-major

@@ -141,20 +141,59 @@ def test_decode_workspace_bytes(m):
         m.decode_workspace_bytes(g, 1, 100, 100)
 
 
+def _fluid_step_time(lengths, per_seq, slots, st, cap=2.5, fixed=300.0, exit_cost=8.0):
+    """The split kernel's step time as the library models it: CTAs start in
+    grid order as resident places free up; n running CTAs each stream at
+    min(cap, slots / n) times their full-load rate."""
+    import heapq
+    lens = [int(x) for x in lengths if x > 0]
+    max_splits = max([1] + [-(-L // st) for L in lens])
+    running, level, t = [], 0.0, 0.0
+
+    def finish():
+        nonlocal level, t
+        rate = min(cap, slots / len(running))
+        top = heapq.heappop(running)
+        t += (top - level) / rate
+        level = top
+
+    for L in [max(int(x), 0) for x in lengths]:
+        n = -(-L // st) if L else 0
+        slen = -(-(-(-L // n)) // 64) * 64 if n else 0
+        for _ in range(per_seq):
+            for k in range(max_splits):
+                work = (min(slen, L - k * slen) + fixed) if k < n else exit_cost
+                if len(running) == slots:
+                    finish()
+                heapq.heappush(running, level + work)
+    while running:
+        finish()
+    return t
+
+
 def test_split_tokens_for_host_lengths(m):
-    """mslim_cuda_decode_split_tokens_for_lengths: a multiple of 64 in
-    [256, 3072], deterministic, and for one rank's share of an 8-GPU C4 run
-    (eight sessions, about 139 K tokens) it keeps the split CTAs within two
-    waves of the 296 resident CTAs, where the longest-session policy alone
-    would start a nearly empty third wave."""
+    """mslim_cuda_decode_split_tokens_for_lengths runs the model of the split
+    kernel's CTAs on the GPU over the split sizes 3072, 2688, 2048, 1536, 1024
+    and keeps the fastest (the longer split within 0.5 %): it equals this
+    restatement of the model for the C4 draw and its shards of 2, 4 and 8
+    GPUs, and is deterministic."""
     import numpy as np
+    import bench
+    from mslim_b200 import workloads
     g = m.AttentionGeometry.new(32, 8, 128)
-    lengths = np.array([32000, 5100, 27000, 9000, 14000, 21000, 4200, 26000], np.int32)
-    st = m.decode_split_tokens_for_lengths(g, lengths)
-    assert st % 64 == 0 and 256 <= st <= 3072
-    assert st == m.decode_split_tokens_for_lengths(g, lengths)
-    ctas = sum(-(-int(L) // st) for L in lengths) * 8
-    assert ctas <= 2 * 296, (st, ctas)
+    L = workloads.c4_layout(seed=3).lengths[:64]
+    for world in (1, 2, 4, 8):
+        for rank in sorted({0, world - 1}):
+            lengths = L[bench.lpt_shard(L, world, rank)].astype(np.int32)
+            st = m.decode_split_tokens_for_lengths(g, lengths)
+            assert st in (3072, 2688, 2048, 1536, 1024)
+            assert st == m.decode_split_tokens_for_lengths(g, lengths)
+            best, best_st = 0.0, None
+            for cand in (3072, 2688, 2048, 1536, 1024):
+                t = _fluid_step_time(lengths, 8, 296, cand)
+                if best_st is None or t < best * 0.995:
+                    best, best_st = t, cand
+            assert st == best_st, (world, rank, st, best_st)
     assert m.decode_split_tokens_for_lengths(g, np.zeros(3, np.int32)) % 64 == 0
 
 
@@ -164,3 +203,18 @@ def test_kernel_launch_counter_reads_without_a_gpu(m):
     a = m.kernel_launches()
     b = m.kernel_launches()
     assert 0 <= a <= b
+
+
+def test_decode_schedule_setting(m):
+    """mslim_cuda_set_decode_schedule: split + merge by default, persistent on
+    request, anything else rejected (host state only, no device needed)."""
+    assert m.get_decode_schedule() == m.DECODE_SPLIT_MERGE
+    try:
+        m.set_decode_schedule(m.DECODE_PERSISTENT)
+        assert m.get_decode_schedule() == m.DECODE_PERSISTENT
+        with pytest.raises(m.ShapeMismatch):
+            m.set_decode_schedule(7)
+        assert m.get_decode_schedule() == m.DECODE_PERSISTENT
+    finally:
+        m.set_decode_schedule(m.DECODE_SPLIT_MERGE)
+    assert m.get_decode_schedule() == m.DECODE_SPLIT_MERGE

@@ -454,16 +454,16 @@ def test_gpu_engine_reserves_its_workspace_when_built(m, wl, oracle):
 
 @pytest.mark.parametrize("split_tokens", [1024, 256, 64])
 def test_persistent_kernel_and_split_merge_pair_give_the_same_bits(m, wl, oracle, split_tokens):
-    """The persistent decode (one launch: splits taken from a work counter,
-    units longest split first, each item merged in-kernel by the CTA whose
-    split completes it -- from a bulk copy of its partials, at once or after
-    that CTA's last split, or from plain loads when the partials do not fit
-    shared memory) returns the bits of the one-CTA-per-split kernel and its
-    separate merge.  A query buffer that is 4-byte but not 16-byte aligned
-    makes the library take the two-kernel form (the persistent kernel brings
-    query rows in by bulk copies) on the same bytes; the launch counter shows
-    which form ran.  Split sizes 1024, 256 and 64 give items of up to 4, 16
-    and 64 splits (every merge form)."""
+    """The persistent decode schedule (one launch: splits taken from a work
+    counter, units longest split first, each item merged in-kernel by the CTA
+    whose split completes it -- from a bulk copy of its partials, at once or
+    after that CTA's last split, or from plain loads when the partials do not
+    fit shared memory) returns the bits of the default schedule, one CTA per
+    split and a separate merge.  Under the persistent schedule a query buffer
+    that is 4-byte but not 16-byte aligned falls back to the two-kernel form
+    (the persistent kernel brings query rows in by bulk copies); the launch
+    counter shows which form ran.  Split sizes 1024, 256 and 64 give items of
+    up to 4, 16 and 64 splits (every merge form)."""
     torch = torch_mod()
     g = m.AttentionGeometry.new(32, 8, 128)
     rng = np.random.default_rng(1000 + split_tokens)
@@ -482,19 +482,26 @@ def test_persistent_kernel_and_split_merge_pair_give_the_same_bits(m, wl, oracle
     q_mis.copy_(q_al)
     assert q_al.data_ptr() % 16 == 0 and q_mis.data_ptr() % 16 == 4
     outs, launches = [], []
-    for qd in (q_al, q_mis, q_al):
-        out = empty_u16((n_seq, 32, 128))
-        out.fill_(0x7FC1)
-        before = m.kernel_launches()
-        m.decode_paged(g, qd, kp, vp, pool["n_pages"], pt, table, pool["max_pages"], seq, n_seq, ws, out,
-                       split_tokens)
-        launches.append(m.kernel_launches() - before)
-        torch.cuda.synchronize()
-        assert m.device_status(0) == 0
-        outs.append(host_u16(out))
-    assert launches == [1, 2, 1], launches
-    assert outs[0].tobytes() == outs[1].tobytes()        # persistent == split + merge
+    runs = [(m.DECODE_PERSISTENT, q_al), (m.DECODE_PERSISTENT, q_mis), (m.DECODE_PERSISTENT, q_al),
+            (m.DECODE_SPLIT_MERGE, q_al)]
+    try:
+        for schedule, qd in runs:
+            m.set_decode_schedule(schedule)
+            out = empty_u16((n_seq, 32, 128))
+            out.fill_(0x7FC1)
+            before = m.kernel_launches()
+            m.decode_paged(g, qd, kp, vp, pool["n_pages"], pt, table, pool["max_pages"], seq, n_seq, ws, out,
+                           split_tokens)
+            launches.append(m.kernel_launches() - before)
+            torch.cuda.synchronize()
+            assert m.device_status(0) == 0
+            outs.append(host_u16(out))
+    finally:
+        m.set_decode_schedule(m.DECODE_SPLIT_MERGE)
+    assert launches == [1, 2, 1, 2], launches
+    assert outs[0].tobytes() == outs[1].tobytes()        # persistent == split + merge (unaligned query)
     assert outs[0].tobytes() == outs[2].tobytes()        # and again (counters left at zero)
+    assert outs[0].tobytes() == outs[3].tobytes()        # the default schedule
     for s, L in enumerate(lengths):
         if L == 0:
             assert not np.any(outs[0][s]), s

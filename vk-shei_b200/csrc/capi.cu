@@ -17,6 +17,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <queue>
 #include <vector>
 
 #include "../../include/mslim_cuda.h"
@@ -40,6 +41,7 @@ static __device__ __align__(256) float g_static_decode_scratch[MSLIM_STATIC_SCRA
 
 namespace {
 std::atomic<uint64_t> g_kernel_launches{0};
+std::atomic<int> g_decode_schedule{MSLIM_DECODE_SPLIT_MERGE};
 }  // namespace
 
 void mslim::note_launch() { g_kernel_launches.fetch_add(1, std::memory_order_relaxed); }
@@ -301,6 +303,7 @@ int run_decode(const DecodeCall &c) {
     p.q_f32 = c.q_f32;
     p.seq_tokens = c.seq_tokens;
     p.page_table = c.page_table;
+    p.persistent = g_decode_schedule.load(std::memory_order_relaxed) == MSLIM_DECODE_PERSISTENT ? 1 : 0;
     p.work_counter = static_cast<unsigned *>(c.workspace);
     p.item_counters = reinterpret_cast<unsigned *>(static_cast<uint8_t *>(c.workspace) + 256);
     p.out = static_cast<uint16_t *>(c.out);
@@ -466,6 +469,15 @@ const char *mslim_cuda_implementation_digest(void) { return MSLIM_SOURCE_DIGEST;
 
 uint64_t mslim_cuda_kernel_launches(void) { return g_kernel_launches.load(std::memory_order_relaxed); }
 
+int mslim_cuda_set_decode_schedule(int schedule) {
+    if (schedule != MSLIM_DECODE_SPLIT_MERGE && schedule != MSLIM_DECODE_PERSISTENT)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "unknown decode schedule %d", schedule);
+    g_decode_schedule.store(schedule, std::memory_order_relaxed);
+    return MSLIM_OK;
+}
+
+int mslim_cuda_get_decode_schedule(void) { return g_decode_schedule.load(std::memory_order_relaxed); }
+
 int mslim_cuda_device_status(int device, int reset, int *status) {
     if (!status) return fail(MSLIM_ERR_SHAPE_MISMATCH, "status pointer is null");
     int prev;
@@ -606,6 +618,50 @@ int mslim_cuda_decode_split_tokens(const mslim_geometry_t *geometry, uint32_t n_
     return MSLIM_OK;
 }
 
+namespace {
+
+// Step time of the split kernel with split size `st`, in token-times of one CTA
+// streaming at its share of HBM under full load.  CTAs start in grid order
+// (split fastest, then KV-head chunk, then session) as the `slots` resident
+// places free up.  While n CTAs run, each streams at min(kCap, slots / n)
+// times its full-load rate: HBM is shared, and a CTA alone is limited by its
+// own pipeline (about 2.5x its full-load share, so the last CTAs of a step
+// speed up only that much).  A CTA costs its tokens plus kFixed (filling its
+// pipeline, combining its warps); a CTA past its session's splits exits at
+// once (kExit).  Every running CTA receives the same service, so the next one
+// to finish is the one with the least service left: a heap of completion
+// levels, O(CTAs log slots).
+double fluid_step_time(const int32_t *lengths, uint32_t n_seq, uint64_t per_seq, uint64_t slots, uint32_t st) {
+    constexpr double kCap = 2.5, kFixed = 300.0, kExit = 8.0;
+    uint64_t max_splits = 1;
+    for (uint32_t i = 0; i < n_seq; ++i)
+        if (lengths[i] > 0) max_splits = std::max<uint64_t>(max_splits, ((uint64_t)lengths[i] + st - 1) / st);
+    std::priority_queue<double, std::vector<double>, std::greater<double>> running;  // completion levels
+    double level = 0.0, t = 0.0;
+    auto finish = [&]() {  // advance to the next completion
+        const double n = (double)running.size();
+        const double rate = std::min(kCap, (double)slots / n);
+        t += (running.top() - level) / rate;
+        level = running.top();
+        running.pop();
+    };
+    for (uint32_t i = 0; i < n_seq; ++i) {
+        const uint64_t L = lengths[i] > 0 ? (uint64_t)lengths[i] : 0;
+        const uint64_t n = L ? (L + st - 1) / st : 0;
+        const uint64_t slen = n ? ((L + n - 1) / n + 63) / 64 * 64 : 0;
+        for (uint64_t h = 0; h < per_seq; ++h)
+            for (uint64_t k = 0; k < max_splits; ++k) {
+                const double work = k < n ? (double)std::min<uint64_t>(slen, L - k * slen) + kFixed : kExit;
+                if (running.size() == slots) finish();
+                running.push(level + work);
+            }
+    }
+    while (!running.empty()) finish();
+    return t;
+}
+
+}  // namespace
+
 int mslim_cuda_decode_split_tokens_for_lengths(const mslim_geometry_t *geometry, uint32_t n_seq,
                                                const int32_t *lengths, uint32_t *split_tokens) {
     if (int rc = check_geometry(geometry)) return rc;
@@ -618,32 +674,18 @@ int mslim_cuda_decode_split_tokens_for_lengths(const mslim_geometry_t *geometry,
     const uint32_t kd = kernel_dim_for(geometry->head_dim);
     const uint64_t slots = 148ull * (kd <= 64 ? 3 : kd <= 128 ? 2 : 1);
     const uint64_t per_seq = (uint64_t)geometry->kv_heads * sh.head_chunks;
-    // A session of L tokens becomes ceil(L / split) CTAs of equal length
-    // (rounded up to 64 tokens).  Every wave of CTAs lasts about the longest
-    // of them (plus a fixed per-CTA cost of about three 64-token stages), so
-    // the step takes about ceil(CTAs / slots) * (longest + 192) token-times:
-    // pick the split that minimises it, the longer split on a tie.  Splits
-    // above 3072 tokens, and single waves of long CTAs, measured slower than
-    // the model says (no wave left to even out the SMs): at least two waves
-    // are kept whenever the batch has the tokens for them.
-    uint64_t best = ~0ull;
+    // Every candidate split runs through fluid_step_time (a model of the split
+    // kernel's CTAs on the GPU, above); the fastest wins, the longer split when
+    // two are within 0.5 %.  The candidates are the sizes the model was checked
+    // against on the C4 shards of 1, 2, 4 and 8 GPUs (its choice within 2 % of
+    // the best measured; sizes in between can land the last wave badly).
+    static const uint32_t kCandidates[] = {3072, 2688, 2048, 1536, 1024};
+    double best = 0.0;
     uint32_t best_st = 2048;
-    uint64_t total = 0;
-    for (uint32_t i = 0; i < n_seq; ++i)
-        if (lengths[i] > 0) total += (uint64_t)lengths[i] * per_seq;
-    const bool two_waves = total >= 2 * slots * 256;
-    for (uint32_t st = 256; st <= 3072; st += 64) {
-        uint64_t ctas = 0, longest = 0;
-        for (uint32_t i = 0; i < n_seq; ++i) {
-            if (lengths[i] <= 0) continue;
-            const uint64_t L = (uint64_t)lengths[i], n = (L + st - 1) / st;
-            ctas += n * per_seq;
-            longest = std::max<uint64_t>(longest, ((L + n - 1) / n + 63) / 64 * 64);
-        }
-        if (two_waves && ctas <= slots) continue;
-        const uint64_t cost = ((ctas + slots - 1) / slots) * (longest + 192);
-        if (cost <= best) {
-            best = cost;
+    for (uint32_t st : kCandidates) {
+        const double t = fluid_step_time(lengths, n_seq, per_seq, slots, st);
+        if (best == 0.0 || t < best * 0.995) {
+            best = t;
             best_st = st;
         }
     }

@@ -1110,7 +1110,7 @@ cudaError_t launch_impl(const CUtensorMap &kmap, const CUtensorMap &vmap, const 
     using S = Shape<D>;
     cudaError_t err;
     const uint64_t units = (uint64_t)p.n_seq * p.q_blocks;
-    if (!QSPLIT && p.work_counter && p.item_counters && !p.out_f32 && units <= (uint64_t)kMaxUnits &&
+    if (p.persistent && !QSPLIT && p.work_counter && p.item_counters && !p.out_f32 && units <= (uint64_t)kMaxUnits &&
         units * p.kvheads * p.head_chunks <= (uint64_t)kMaxDecodeItems && p.max_splits <= kMaxFusedSplits &&
         (reinterpret_cast<uintptr_t>(p.q) & 15u) == 0) {
         // persistent: as many CTAs as stay resident, at most one per work unit

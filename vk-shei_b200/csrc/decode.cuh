@@ -11,6 +11,7 @@ struct DecodeParams {
     const int32_t *seq_tokens;   // [n_seq] tokens in each sequence's cache
     const int32_t *page_table;   // [n_seq][max_pages] physical page ids (paged only)
     float *partials;             // [n_seq][nq][QH][max_splits][D + 4] (kernel D): acc, m, l, 2 pad
+    int persistent;              // 1: the persistent form where the shape allows (the decode schedule)
     unsigned *work_counter;      // [2]: work taken and CTAs done, zero on entry, left zero;
                                  // null: one CTA per split and a merge kernel instead of
                                  // the persistent form

@@ -63,6 +63,8 @@ SIGNATURES = {
     "mslim_cuda_implementation_digest": (ctypes.c_char_p, []),
     "mslim_cuda_device_status": (_int, [_int, _int, ctypes.POINTER(_int)]),
     "mslim_cuda_kernel_launches": (ctypes.c_uint64, []),
+    "mslim_cuda_set_decode_schedule": (_int, [_int]),
+    "mslim_cuda_get_decode_schedule": (_int, []),
     "mslim_cuda_geometry_validate": (_int, [_G]),
     "mslim_cuda_config_default": (KernelConfig, []),
     "mslim_cuda_config_validate": (_int, [_C, _int]),

@@ -247,6 +247,20 @@ def device_status(device: int = 0, reset: bool = True) -> int:
     return st.value
 
 
+DECODE_SPLIT_MERGE = 0
+DECODE_PERSISTENT = 1
+
+
+def set_decode_schedule(schedule: int) -> None:
+    """Process-wide decode schedule: DECODE_SPLIT_MERGE (default) or
+    DECODE_PERSISTENT (same bits)."""
+    check(_lib.lib().mslim_cuda_set_decode_schedule(int(schedule)))
+
+
+def get_decode_schedule() -> int:
+    return int(_lib.lib().mslim_cuda_get_decode_schedule())
+
+
 def kernel_launches() -> int:
     """Kernels the library has launched in this process (captures count once)."""
     return int(_lib.lib().mslim_cuda_kernel_launches())
