@@ -954,7 +954,8 @@ int mslim_cuda_prefill_causal(const mslim_geometry_t *geometry, const void *q, c
         const uint32_t box[3] = {64, 1, 128};
         const uint32_t kvbox[3] = {64, 1, mslim::prefill_kv_box_rows(geometry->head_dim)};
         if (int rc = make_tmap(&qmap, q, 3, qd, qs, box)) return rc;
-        if (int rc = make_tmap(&omap, out, 3, qd, qs, box)) return rc;
+        const uint32_t obox[3] = {64, 1, 32};  // the pair kernel stores 32 rows per warp
+        if (int rc = make_tmap(&omap, out, 3, qd, qs, obox)) return rc;
         if (int rc = make_tmap(&kmap, k, 3, kd, ks, kvbox)) return rc;
         if (int rc = make_tmap(&vmap, v, 3, kd, ks, kvbox)) return rc;
     }

@@ -22,7 +22,8 @@
 //       (the next item's Q is prefetched as soon as the current item's last S
 //       completes), then a softmax warpgroup per head, one thread per query
 //       row, which also rescales O in TMEM and writes the output through a
-//       swizzled staging buffer and bulk tensor stores.
+//       swizzled staging buffer, each warp its own 32 rows with its own bulk
+//       tensor stores.
 //   mslim_prefill_causal  odd groups, and head_dim 256: one head per CTA, S
 //       double-buffered in TMEM (S(j+1) issued before PV(j)), eight softmax
 //       warps taking half a key tile each and exchanging row maxima through
@@ -643,7 +644,6 @@ __global__ void __launch_bounds__(kPThreads, 1)
         const uint32_t scol = lane_addr + h * 128;
         const uint32_t ocol = lane_addr + kColO + h * 128;
         const float scale = p.scale_log2;
-        const bool issuer = quarter == 0 && lane == 0;
         uint8_t *stage = smem + PS::kOffStage + h * kBox;
         int g = 0;  // key tiles seen so far, over all items
         bool ok = true;
@@ -728,16 +728,19 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 m_used = m_new;
             }
             // ---- output of this item: O_h / l -> bf16, one 64-column box at a
-            // time through the head's 16 KB staging buffer (TMA 128-byte
-            // swizzled layout) and a bulk tensor store; rows past the last
-            // query are clipped by the store.
+            // time.  Each warp stages its own 32 rows (a 4 KB slice of the head's
+            // 16 KB staging buffer, TMA 128-byte swizzled layout) and stores them
+            // with its own bulk tensor store (32-row box), so no warp waits for
+            // another's rows or for another's store to release the buffer; rows
+            // past the last query are clipped by the store.
             const bool good = ok && __all_sync(0xffffffffu, mbar_wait(&bars->o_done[h], round & 1, p.status, 64));
             if (!good) *abort_flag = 1;
             tc_fence_after();
             const float inv = 1.0f / l_run;
+            uint8_t *wstage = stage + quarter * 32 * 128;
             for (int box = 0; box < PS::kBoxes; ++box) {
-                if (issuer) bulk_wait_read_all();  // the previous store has read the buffer
-                named_bar_sync(1 + h, 128);
+                if (lane == 0) bulk_wait_read_all();  // this warp's previous store has read its slice
+                __syncwarp();
                 if (good) {
 #pragma unroll
                     for (int c = 0; c < 2; ++c) {
@@ -748,23 +751,23 @@ __global__ void __launch_bounds__(kPThreads, 1)
                         for (int i = 0; i < 16; ++i) w[i] = pack_bf16x2(o[2 * i] * inv, o[2 * i + 1] * inv);
 #pragma unroll
                         for (int t = 0; t < 4; ++t) {
-                            const int chunk = (c * 4 + t) ^ (row & 7);
-                            *reinterpret_cast<uint4 *>(stage + row * 128 + chunk * 16) =
+                            const int chunk = (c * 4 + t) ^ (lane & 7);
+                            *reinterpret_cast<uint4 *>(wstage + lane * 128 + chunk * 16) =
                                 make_uint4(w[4 * t], w[4 * t + 1], w[4 * t + 2], w[4 * t + 3]);
                         }
                     }
                     fence_proxy_async_smem();
                 }
-                named_bar_sync(1 + h, 128);
-                if (issuer && *abort_flag == 0) {
-                    tma_store_3d(&omap, stage, box * 64, it.qh0 + h, it.q0);
+                __syncwarp();
+                if (lane == 0 && good && *abort_flag == 0) {
+                    tma_store_3d(&omap, wstage, box * 64, it.qh0 + h, it.q0 + quarter * 32);
                     bulk_commit_group();
                 }
             }
             // the head's four warps continue or stop together
             if (named_bar_or(1 + h, 128, !good || *abort_flag != 0)) ok = false;
         }
-        if (issuer) bulk_wait_all();
+        if (lane == 0) bulk_wait_all();
     }
     tc_fence_before();
     __syncthreads();

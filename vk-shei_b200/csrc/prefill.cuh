@@ -29,9 +29,9 @@ bool prefill_pairs_heads(unsigned group, unsigned head_dim);
 // Rows of the k/v maps' boxes: 128 (one key tile), 64 above head_dim 128.
 unsigned prefill_kv_box_rows(unsigned head_dim);
 
-// q/k/v/out maps: bf16, dims (head_dim, heads, rows), 128-byte swizzle; q and
-// out boxes (64, 1, 128), k and v boxes (64, 1, prefill_kv_box_rows); the out
-// map (same shape as q) is written by bulk tensor stores.
+// q/k/v/out maps: bf16, dims (head_dim, heads, rows), 128-byte swizzle; q box
+// (64, 1, 128), k and v boxes (64, 1, prefill_kv_box_rows); the out map (same
+// shape as q, box (64, 1, 32): one warp's rows) is written by bulk tensor stores.
 cudaError_t launch_prefill(const CUtensorMap &qmap, const CUtensorMap &kmap,
                            const CUtensorMap &vmap, const CUtensorMap &omap,
                            const PrefillParams &p, cudaStream_t stream);
