@@ -81,8 +81,9 @@ def parse():
     ap.add_argument("--mlp", choices=["sharded", "replicated"], default="sharded")
     ap.add_argument("--kv-mode", choices=["dense", "coldstore"], default="dense")
     ap.add_argument("--no-graph", action="store_true", help="C5 decode steps issued eagerly (no CUDA graph)")
-    ap.add_argument("--decode-gemm", choices=["own", "cublas"], default="cublas",
-                    help="C5 decode projections: cuBLAS (default) or mslim_cuda_gemv")
+    ap.add_argument("--decode-gemm", choices=["auto", "own", "cublas"], default="auto",
+                    help="C5 decode projections: auto (mslim_cuda_gemv at TP > 1, cuBLAS at TP 1), "
+                         "own (mslim_cuda_gemv) or cublas")
     ap.add_argument("--gemv", action="store_true",
                     help="the C5 decode projections: mslim_cuda_gemv against cuBLAS, per shape")
     ap.add_argument("--layer", action="store_true",
@@ -525,8 +526,12 @@ def bench_model(m, torch, device, args, rank, world, dist) -> dict | None:
     spec = mdl.ModelSpec(layers=args.model_layers)
     L = spec.layer
     t0 = time.time()
+    # decode projections: the own tcgen05 GEMV where the ranks' shards are
+    # small (measured faster per step at TP 2 and per shape at TP 8), cuBLAS
+    # at TP 1 (measured 2-3 % faster there); profiles/gemv_c5_shapes.md
+    gemm = args.decode_gemm if args.decode_gemm != "auto" else ("own" if world > 1 else "cublas")
     M = mdl.DeviceModel(spec, B, S + steps + 4, seed=5, tp_rank=rank, tp_world=world, mlp=args.mlp,
-                        kv_mode=args.kv_mode, decode_gemm=args.decode_gemm)
+                        kv_mode=args.kv_mode, decode_gemm=gemm)
     build_s = time.time() - t0
     ids = torch.from_numpy(np.random.default_rng(5).integers(0, spec.vocab, size=(B, S))).to(device)
 
@@ -596,7 +601,7 @@ def bench_model(m, torch, device, args, rank, world, dist) -> dict | None:
                    "parallelism": f"tp{world} by KV-head group, MLP {args.mlp}", "kv": args.kv_mode,
                    "allreduce_per_layer": 1 if args.mlp == "replicated" else 2,
                    "decode_issue": "one CUDA graph per step" if graphed else "eager",
-                   "decode_projections": "mslim_cuda_gemv" if args.decode_gemm == "own" else "cuBLAS"},
+                   "decode_projections": "mslim_cuda_gemv" if gemm == "own" else "cuBLAS"},
         "prefill_ms": prefill_ms, "prefill_tokens_per_s": B * S / (prefill_ms * 1e-3),
         "decode_ms_per_step": decode_ms / steps,
         "decode_step_split_ms": step_split,
