@@ -42,6 +42,8 @@ __device__ __forceinline__ uint32_t swiglu_pair(uint32_t g, uint32_t u) {
 __global__ void __launch_bounds__(kEltThreads)
     mslim_residual_add(const uint16_t *__restrict__ a, const uint16_t *__restrict__ b,
                        uint16_t *__restrict__ out, uint64_t n) {
+    griddep_launch_dependents();
+    griddep_wait();  // programmatic dependent launch: inputs after the predecessor
     const uint64_t n8 = n / 8;
     const uint4 *a4 = reinterpret_cast<const uint4 *>(a);
     const uint4 *b4 = reinterpret_cast<const uint4 *>(b);
@@ -59,6 +61,8 @@ __global__ void __launch_bounds__(kEltThreads)
 __global__ void __launch_bounds__(kEltThreads)
     mslim_swiglu(const uint16_t *__restrict__ gate, const uint16_t *__restrict__ up,
                  uint16_t *__restrict__ out, uint64_t n) {
+    griddep_launch_dependents();
+    griddep_wait();
     const uint64_t n8 = n / 8;
     const uint4 *g4 = reinterpret_cast<const uint4 *>(gate);
     const uint4 *u4 = reinterpret_cast<const uint4 *>(up);
@@ -79,6 +83,8 @@ __global__ void __launch_bounds__(kEltThreads)
 __global__ void __launch_bounds__(kEltThreads)
     mslim_swiglu_rows(const uint16_t *__restrict__ gate_up, uint16_t *__restrict__ out, uint32_t rows,
                       uint32_t width) {
+    griddep_launch_dependents();
+    griddep_wait();
     const uint32_t w8 = width / 8;
     const uint64_t n8 = (uint64_t)rows * w8;
     for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n8;
@@ -158,6 +164,8 @@ __device__ __forceinline__ bool better(int32_t k, int32_t i, int32_t k2, int32_t
 __global__ void __launch_bounds__(kArgThreads)
     mslim_argmax(const uint16_t *__restrict__ logits, uint32_t n, int ties_to_last,
                  int32_t *__restrict__ out) {
+    griddep_launch_dependents();
+    griddep_wait();
     const bool last = ties_to_last != 0;
     const uint16_t *row = logits + (uint64_t)blockIdx.x * n;
     int32_t best_k = INT_MIN, best_i = -1;
@@ -360,20 +368,18 @@ cudaError_t launch_kv_canonical(const uint16_t *src, uint16_t *out, uint32_t kv_
 
 cudaError_t launch_residual_add(const uint16_t *a, const uint16_t *b, uint16_t *out, uint64_t n,
                                 cudaStream_t stream) {
-    mslim_residual_add<<<elt_grid(n), kEltThreads, 0, stream>>>(a, b, out, n);
-    return counted(cudaGetLastError());
+    return launch_pdl(mslim_residual_add, dim3(elt_grid(n)), dim3(kEltThreads), 0, stream, a, b, out, n);
 }
 
 cudaError_t launch_swiglu(const uint16_t *gate, const uint16_t *up, uint16_t *out, uint64_t n,
                           cudaStream_t stream) {
-    mslim_swiglu<<<elt_grid(n), kEltThreads, 0, stream>>>(gate, up, out, n);
-    return counted(cudaGetLastError());
+    return launch_pdl(mslim_swiglu, dim3(elt_grid(n)), dim3(kEltThreads), 0, stream, gate, up, out, n);
 }
 
 cudaError_t launch_swiglu_rows(const uint16_t *gate_up, uint16_t *out, uint32_t rows, uint32_t width,
                                cudaStream_t stream) {
-    mslim_swiglu_rows<<<elt_grid((uint64_t)rows * width), kEltThreads, 0, stream>>>(gate_up, out, rows, width);
-    return counted(cudaGetLastError());
+    return launch_pdl(mslim_swiglu_rows, dim3(elt_grid((uint64_t)rows * width)), dim3(kEltThreads), 0, stream,
+                      gate_up, out, rows, width);
 }
 
 cudaError_t launch_page_token_hashes(const uint16_t *pool, uint32_t n_pool_pages, uint32_t kv_heads,
@@ -388,8 +394,7 @@ cudaError_t launch_page_token_hashes(const uint16_t *pool, uint32_t n_pool_pages
 
 cudaError_t launch_argmax(const uint16_t *logits, uint32_t rows, uint32_t n, int ties_to_last,
                           int32_t *out, cudaStream_t stream) {
-    mslim_argmax<<<rows, kArgThreads, 0, stream>>>(logits, n, ties_to_last, out);
-    return counted(cudaGetLastError());
+    return launch_pdl(mslim_argmax, dim3(rows), dim3(kArgThreads), 0, stream, logits, n, ties_to_last, out);
 }
 
 // ------------------------------------------------------ exp2 diagnostic --

@@ -70,6 +70,8 @@ template <bool kResidual>
 __global__ void __launch_bounds__(128)
     mslim_rmsnorm(uint16_t *__restrict__ x, const uint16_t *__restrict__ delta,
                   const uint16_t *__restrict__ w, uint16_t *__restrict__ y, uint32_t hidden, float eps) {
+    griddep_launch_dependents();
+    griddep_wait();  // programmatic dependent launch: inputs after the predecessor
     const size_t row = blockIdx.x;
     uint16_t *xr = x + row * hidden;
     const uint16_t *dr = kResidual ? delta + row * hidden : nullptr;
@@ -385,14 +387,13 @@ unsigned rope_vec_ctas(uint32_t qheads, uint32_t kvheads, uint32_t dim) {
 
 cudaError_t launch_rmsnorm(const uint16_t *x, const uint16_t *w, uint16_t *y, uint32_t tokens,
                            uint32_t hidden, float eps, cudaStream_t stream) {
-    mslim_rmsnorm<false><<<tokens, 128, 0, stream>>>(const_cast<uint16_t *>(x), nullptr, w, y, hidden, eps);
-    return counted(cudaGetLastError());
+    return launch_pdl(mslim_rmsnorm<false>, dim3(tokens), dim3(128), 0, stream, const_cast<uint16_t *>(x),
+                      static_cast<const uint16_t *>(nullptr), w, y, hidden, eps);
 }
 
 cudaError_t launch_residual_rmsnorm(uint16_t *x, const uint16_t *delta, const uint16_t *w, uint16_t *y,
                                     uint32_t tokens, uint32_t hidden, float eps, cudaStream_t stream) {
-    mslim_rmsnorm<true><<<tokens, 128, 0, stream>>>(x, delta, w, y, hidden, eps);
-    return counted(cudaGetLastError());
+    return launch_pdl(mslim_rmsnorm<true>, dim3(tokens), dim3(128), 0, stream, x, delta, w, y, hidden, eps);
 }
 
 cudaError_t launch_rope(const uint16_t *in, uint16_t *out, uint32_t tokens, uint32_t heads,

@@ -92,6 +92,10 @@ __global__ void __launch_bounds__(kTpThreads)
     mslim_tp_allreduce_rmsnorm(const TpCommDev c, uint32_t slot, uint16_t *__restrict__ x,
                                const uint16_t *__restrict__ w, uint16_t *__restrict__ y, float eps,
                                int *status) {
+    // programmatic dependent launch: the partials, x and the flags are touched
+    // only after the preceding projection has completed
+    griddep_launch_dependents();
+    griddep_wait();
     const uint32_t row = blockIdx.x;
     const uint32_t hidden = c.hidden;
     uint16_t *xr = x + (size_t)row * hidden;
@@ -188,10 +192,10 @@ template <int W>
 cudaError_t launch_w(const TpCommDev &comm, uint32_t slot, uint16_t *x, const uint16_t *w, uint16_t *y,
                      uint32_t rows, float eps, int *status, cudaStream_t stream) {
     if (comm.hidden <= (uint32_t)kTpThreads * 8 * kTpRegIters)
-        mslim_tp_allreduce_rmsnorm<W, true><<<rows, kTpThreads, 0, stream>>>(comm, slot, x, w, y, eps, status);
-    else
-        mslim_tp_allreduce_rmsnorm<W, false><<<rows, kTpThreads, 0, stream>>>(comm, slot, x, w, y, eps, status);
-    return counted(cudaGetLastError());
+        return launch_pdl(mslim_tp_allreduce_rmsnorm<W, true>, dim3(rows), dim3(kTpThreads), 0, stream, comm, slot,
+                          x, w, y, eps, status);
+    return launch_pdl(mslim_tp_allreduce_rmsnorm<W, false>, dim3(rows), dim3(kTpThreads), 0, stream, comm, slot, x,
+                      w, y, eps, status);
 }
 
 }  // namespace
