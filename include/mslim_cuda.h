@@ -164,10 +164,10 @@ int mslim_cuda_plan_diagnostics(const mslim_plan_t *plan, char *out, size_t len)
  * (split_tokens 0 = library policy).  Counterpart of
  * AttentionKernelConfig::decode_scratch_bytes (src/attention_kernel.rs:124-138).
  * A decode workspace must be zero-filled once before its first use: its
- * head holds the counters from which the split kernel's resident CTAs take
- * their work and find the last split of each item, and every call leaves
- * them zero again.  One
- * workspace serves any later calls that fit it, on one stream at a time. */
+ * head holds the counters from which the persistent schedule's resident CTAs
+ * take their work and find the last split of each item (see
+ * mslim_cuda_set_decode_schedule), and every call leaves them zero again.
+ * One workspace serves any later calls that fit it, on one stream at a time. */
 int mslim_cuda_decode_workspace_bytes(const mslim_geometry_t *geometry, uint32_t n_seq,
                                       uint32_t max_tokens, uint32_t split_tokens, size_t *bytes);
 
