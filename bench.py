@@ -146,6 +146,11 @@ class ClockSampler:
 
 # -------------------------------------------------------------- utilities --
 
+# Peer-to-peer copy over NVLink, per direction per GPU, measured on this pool's
+# B200s (900 GB/s nominal): the denominator for bytes a kernel pulls from peers.
+NVLINK_PEER_GBS = 770.0
+
+
 def measured_peaks() -> dict:
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -574,11 +579,17 @@ def bench_model(m, torch, device, args, rank, world, dist) -> dict | None:
     prefill_ms = max_over_ranks(e0.elapsed_time(e1))
     decode_ms = max_over_ranks(e1.elapsed_time(e2))
     tokens = torch.stack(out, 1).cpu().numpy().astype(np.int32)   # [B][steps + 1]
-    # one more decode step and a one-layer-deep look at the prefill, split by kind
+    # one more decode step, issued eagerly with CUDA events around every op.
+    # A bounded spin kernel queued first keeps the GPU busy while the host
+    # enqueues the whole step, so each op's events bracket its device time and
+    # not the host's launch latency (ops run back to back, without the
+    # programmatic-dependent-launch overlap of the graph).
     M.profile = mdl.SectionTimer(torch)
+    torch.cuda._sleep(int(0.05 * 1.965e9))
     M.decode_step(tok)
     sync()
     step_split = M.profile.totals_ms()
+    step_ops = M.profile.per_op()
     M.profile = None
     M.close()
     if m.device_status(torch.cuda.current_device()) != 0:
@@ -586,6 +597,16 @@ def bench_model(m, torch, device, args, rank, world, dist) -> dict | None:
     if rank != 0:
         return None
     peaks = measured_peaks()
+    kernels = []
+    for e in step_ops:
+        if e["ms"] <= 0.0 or e["bytes"] <= 0:
+            continue
+        gbs = e["bytes"] / (e["ms"] * 1e-3) / 1e9
+        peak = peaks["hbm_gbs"] if e["link"] == "hbm" else NVLINK_PEER_GBS
+        kernels.append({"op": e["op"], "kernel": e["kernel"], "launches": e["launches"],
+                        "us_per_launch": 1e3 * e["ms"] / e["launches"], "bytes_per_launch": e["bytes"] // e["launches"],
+                        "share_of_step": e["ms"] / sum(x["ms"] for x in step_ops),
+                        "bound": e["link"], "achieved_gbs": gbs, "peak_gbs": peak, "frac": gbs / peak})
     kvh, qh = L.kv_heads // world, L.query_heads // world
     inter = L.intermediate if args.mlp == "replicated" else L.intermediate // world
     params_layer = L.hidden * (qh + 2 * kvh) * L.head_dim + L.hidden * qh * L.head_dim + 3 * L.hidden * inter
@@ -605,8 +626,14 @@ def bench_model(m, torch, device, args, rank, world, dist) -> dict | None:
         "prefill_ms": prefill_ms, "prefill_tokens_per_s": B * S / (prefill_ms * 1e-3),
         "decode_ms_per_step": decode_ms / steps,
         "decode_step_split_ms": step_split,
-        "decode_step_split_note": "one extra step issued eagerly with CUDA events around every op "
-                                  "(includes launch gaps); the timed steps replay a graph",
+        "decode_step_kernels": kernels,
+        "decode_step_split_note": "one extra step of rank 0 issued eagerly behind a bounded spin kernel, CUDA "
+                                  "events around every op (device time of each op run alone, no launch gaps, "
+                                  "no programmatic-dependent-launch overlap); the timed steps replay a graph. "
+                                  "decode_step_kernels: per op its algorithmic bytes (weights, K/V, activations "
+                                  "in and out) / its device time, against hbm_gbs of MEASURED_PEAKS.json, or "
+                                  f"for NVLink the {NVLINK_PEER_GBS:.0f} GB/s per-direction peer copy measured "
+                                  "on this pool",
         "per_rank_roofline": {
             "decode_weight_bytes_per_step": 2 * (params_layer * spec.layers + spec.vocab * L.hidden),
             "decode_weight_gbs": 2 * (params_layer * spec.layers + spec.vocab * L.hidden)

@@ -36,25 +36,40 @@ class ModelSpec:
 
 class SectionTimer:
     """CUDA events around each step of a forward, summed per kind (gemm,
-    attention, collective, elementwise) once the stream has been synchronised."""
+    attention, collective, elementwise) or per named op once the stream has
+    been synchronised.  Each section carries the op's algorithmic bytes (what
+    it must move at least: weights, K/V, activations in and out) and the link
+    they cross ("hbm", or "nvlink" for the peer reads of a reduction)."""
 
     def __init__(self, torch):
         self.torch = torch
         self.marks = []
 
-    def __call__(self, kind):
-        return _Section(self, kind)
+    def __call__(self, kind, op=None, nbytes=0, kernel=None, link="hbm"):
+        return _Section(self, kind, op or kind, int(nbytes), kernel or op or kind, link)
 
     def totals_ms(self) -> dict:
         out = {}
-        for kind, a, b in self.marks:
-            out[kind] = out.get(kind, 0.0) + a.elapsed_time(b)
+        for sec, a, b in self.marks:
+            out[sec.kind] = out.get(sec.kind, 0.0) + a.elapsed_time(b)
         return out
+
+    def per_op(self) -> list:
+        """One entry per named op: sections (launches of the op), device ms,
+        algorithmic bytes, heaviest first."""
+        acc = {}
+        for sec, a, b in self.marks:
+            e = acc.setdefault(sec.op, {"op": sec.op, "kernel": sec.kernel, "kind": sec.kind, "link": sec.link,
+                                        "launches": 0, "ms": 0.0, "bytes": 0})
+            e["launches"] += 1
+            e["ms"] += a.elapsed_time(b)
+            e["bytes"] += sec.nbytes
+        return sorted(acc.values(), key=lambda e: -e["ms"])
 
 
 class _Section:
-    def __init__(self, timer, kind):
-        self.timer, self.kind = timer, kind
+    def __init__(self, timer, kind, op, nbytes, kernel, link):
+        self.timer, self.kind, self.op, self.nbytes, self.kernel, self.link = timer, kind, op, nbytes, kernel, link
 
     def __enter__(self):
         t = self.timer.torch
@@ -64,7 +79,7 @@ class _Section:
 
     def __exit__(self, *exc):
         self.b.record()
-        self.timer.marks.append((self.kind, self.a, self.b))
+        self.timer.marks.append((self, self.a, self.b))
         return False
 
 
@@ -180,6 +195,7 @@ class DeviceModel:
         ws = _att.decode_workspace_bytes(self.geometry, batch, reach)
         self.workspace = torch.zeros(max(ws, 16), dtype=torch.uint8, device=dev)
         self.lengths = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.host_length = 0  # every session's token count, mirrored on the host
         self.profile = None   # a SectionTimer splits the device time by kind of step
         # decode-step reductions over NVLink peer memory (fused with the
         # residual add and RMSNorm); prefill reduces through NCCL
@@ -189,8 +205,14 @@ class DeviceModel:
             self.comm = TpComm(tp_world, tp_rank, batch, L.hidden, group)
 
     # ------------------------------------------------------------ pieces --
-    def _sec(self, kind):
-        return self.profile(kind) if self.profile is not None else _NO_SECTION
+    def _sec(self, kind, op=None, nbytes=0, kernel=None, link="hbm"):
+        if self.profile is None:
+            return _NO_SECTION
+        return self.profile(kind, op, nbytes, kernel, link)
+
+    def _row_bytes(self, rows, width, passes):
+        """bf16 bytes of `passes` reads or writes of a [rows][width] tensor."""
+        return 2 * rows * width * passes
 
     def _all_reduce(self, x):
         if self.world > 1:
@@ -200,18 +222,21 @@ class DeviceModel:
 
     def _norm(self, x, w):
         out = self.torch.empty_like(x)
-        with self._sec("elementwise"):
+        H = self.spec.layer.hidden
+        with self._sec("elementwise", "rmsnorm", self._row_bytes(x.shape[0], H, 2) + 2 * H, "mslim_rmsnorm"):
             _att.rmsnorm(x, w, out, x.shape[0], self.spec.layer.hidden, self.spec.layer.eps)
         return out
 
-    def _gemm(self, x, w, out=None):
+    def _gemm(self, x, w, out=None, op="gemm"):
         """x @ w^T: the decode step's few rows (decode_gemm="own") through
         mslim_cuda_gemv, the tcgen05 weight-streaming projection; prefill rows
         (and decode_gemm="cublas") through cuBLAS."""
         t = self.torch
         rows, (n, k) = x.shape[0], w.shape
-        with self._sec("gemm"):
-            if self.decode_gemm == "own" and rows <= 16 and k % 8 == 0:
+        own = self.decode_gemm == "own" and rows <= 16 and k % 8 == 0
+        nbytes = 2 * (n * k + rows * k + rows * n)
+        with self._sec("gemm", op, nbytes, "mslim_gemv_tc" if own else "cuBLAS GEMM"):
+            if own:
                 y = out if out is not None else t.empty((rows, n), dtype=x.dtype, device=self.device)
                 _att.gemv(x.contiguous(), w, y, rows, n, k)
                 return y
@@ -229,11 +254,13 @@ class DeviceModel:
     def _residual_norm(self, x, delta, w):
         """x = bf16(x + delta) in place; returns RMSNorm(x, w)."""
         out = self.torch.empty_like(x)
-        with self._sec("elementwise"):
+        H = self.spec.layer.hidden
+        with self._sec("elementwise", "residual + RMSNorm", self._row_bytes(x.shape[0], H, 4) + 2 * H,
+                       "mslim_rmsnorm<residual>"):
             _att.residual_rmsnorm(x, delta, w, out, x.shape[0], self.spec.layer.hidden, self.spec.layer.eps)
         return out
 
-    def _reduce_residual_norm(self, inp, w_proj, x, w_norm, reduce: bool, fused: bool):
+    def _reduce_residual_norm(self, inp, w_proj, x, w_norm, reduce: bool, fused: bool, op="gemm"):
         """x += (sum over ranks of) inp @ w_proj^T; returns RMSNorm(x, w_norm).
         fused: the GEMM writes this rank's partial into the communicator slot
         and one kernel reduces over NVLink, adds and normalises (decode);
@@ -241,12 +268,15 @@ class DeviceModel:
         rows = x.shape[0]
         if reduce and fused and self.comm is not None:
             slot = self.comm.next_slot()
-            self._gemm(inp, w_proj, out=self.comm.slot(slot, rows))
+            self._gemm(inp, w_proj, out=self.comm.slot(slot, rows), op=op)
             out = self.torch.empty_like(x)
-            with self._sec("collective"):
+            H = self.spec.layer.hidden
+            # the bytes that cross NVLink into this rank: every peer's partial row
+            with self._sec("collective", "NVLink reduce + residual + RMSNorm",
+                           self._row_bytes(rows, H, self.world - 1), "mslim_tp_allreduce_rmsnorm", "nvlink"):
                 self.comm.allreduce_rmsnorm(slot, x, w_norm, out, rows, self.spec.layer.eps)
             return out
-        y = self._gemm(inp, w_proj)
+        y = self._gemm(inp, w_proj, op=op)
         if reduce:
             self._all_reduce(y)
         return self._residual_norm(x, y, w_norm)
@@ -257,13 +287,14 @@ class DeviceModel:
         final norm after the last layer)."""
         t = self.torch
         W = self.layers[li]
-        n2 = self._reduce_residual_norm(attn.reshape(x.shape[0], -1), W["wo"], x, W["post_norm"], True, fused)
-        gu = self._gemm(n2, W["wgu"])
+        n2 = self._reduce_residual_norm(attn.reshape(x.shape[0], -1), W["wo"], x, W["post_norm"], True, fused,
+                                        op="o projection")
+        gu = self._gemm(n2, W["wgu"], op="gate|up projection")
         act = t.empty((x.shape[0], self.inter), dtype=x.dtype, device=self.device)
-        with self._sec("elementwise"):
+        with self._sec("elementwise", "SwiGLU", self._row_bytes(x.shape[0], self.inter, 3), "mslim_swiglu_rows"):
             _att.swiglu_rows(gu, act, x.shape[0], self.inter)
         nxt = self.layers[li + 1]["in_norm"] if li + 1 < len(self.layers) else self.final_norm
-        return self._reduce_residual_norm(act, W["wd"], x, nxt, self.mlp == "sharded", fused)
+        return self._reduce_residual_norm(act, W["wd"], x, nxt, self.mlp == "sharded", fused, op="down projection")
 
     def _lm_head_argmax(self, n_final):
         """n_final: final-normed bf16 [batch][hidden] -> (int32 ids, bf16 logits
@@ -273,20 +304,21 @@ class DeviceModel:
         CPU path's tie rule (last maximal index) holds across slices."""
         t = self.torch
         B = n_final.shape[0]
-        logits = self._gemm(n_final, self.lm_head)
+        logits = self._gemm(n_final, self.lm_head, op="lm_head")
         ids = t.empty(B, dtype=t.int32, device=self.device)
-        with self._sec("elementwise"):
+        with self._sec("elementwise", "argmax", self._row_bytes(B, self.vocab_hi - self.vocab_lo, 1),
+                       "mslim_argmax"):
             _att.argmax(logits, B, self.vocab_hi - self.vocab_lo, ids, ties_to_last=True)
         if self.world == 1:
             return ids, logits
         import torch.distributed as dist
-        with self._sec("elementwise"):
+        with self._sec("elementwise", "argmax shard key", 0, "torch elementwise"):
             bits = logits.gather(1, ids.long().view(B, 1)).view(t.int16).view(B)
             mine = shard_argmax_key(t, bits, ids, self.vocab_lo)
             every = t.empty((self.world, B), dtype=t.int64, device=self.device)
-        with self._sec("collective"):
+        with self._sec("collective", "argmax all-gather", 8 * B * (self.world - 1), "NCCL all_gather", "nvlink"):
             dist.all_gather_into_tensor(every, mine, group=self.group)
-        with self._sec("elementwise"):
+        with self._sec("elementwise", "argmax shard key", 0, "torch elementwise"):
             best = pick_shard_argmax(t, every)
         return best, logits
 
@@ -325,6 +357,7 @@ class DeviceModel:
                     _att.prefill_causal(self.geometry, q_r[rows], k_r[rows], v[rows], attn[rows], S, 0)
             n = self._after_attention(li, x, attn)
         self.lengths.fill_(S)
+        self.host_length = S
         last = n.view(B, S, L.hidden)[:, S - 1].contiguous()
         return self._lm_head_argmax(last)
 
@@ -335,34 +368,45 @@ class DeviceModel:
         t = self.torch
         B = tokens.shape[0]
         D = self.spec.layer.head_dim
-        with self._sec("elementwise"):
+        H = self.spec.layer.hidden
+        with self._sec("elementwise", "embedding gather", self._row_bytes(B, H, 2), "torch index_select"):
             x = self.embedding.index_select(0, tokens.long()).contiguous()    # [B][hidden]
             pos = self.lengths
             seq = pos + 1
+        # algorithmic bytes of this step's rope + append and attention (every
+        # session holds host_length tokens before the step)
+        rope_bytes = self._row_bytes(B, (2 * self.qh + 4 * self.kvh) * D, 1)
+        ctx = self.host_length + 1
+        attn_bytes = self._row_bytes(B * ctx, self.kvh * D, 2) + self._row_bytes(B, self.qh * D, 2)
+        paged = self.kv_mode != "dense"
+        rope_name = "mslim_rope_append_paged" if paged else "mslim_rope_append_dense"
+        attn_name = ("mslim_decode_persist" if _att.get_decode_schedule() == _att.DECODE_PERSISTENT
+                     else "mslim_decode_split + mslim_decode_merge_row")
         n = self._norm(x, self.layers[0]["in_norm"])
         for li, W in enumerate(self.layers):
-            qkv = self._gemm(n, W["wqkv"])
+            qkv = self._gemm(n, W["wqkv"], op="q|k|v projection")
             q_r = t.empty((B, self.qh * D), dtype=x.dtype, device=self.device)
             attn = t.empty_like(q_r)
             if self.kv_mode == "dense":
-                with self._sec("elementwise"):
+                with self._sec("elementwise", "RoPE + K/V append", rope_bytes, rope_name):
                     _att.rope_append_decode_dense_qkv(self.geometry, qkv, q_r, pos, B, self.rope_cfg,
                                                       self.k_cache[li], self.v_cache[li], self.capacity)
-                with self._sec("attention"):
+                with self._sec("attention", "decode attention", attn_bytes, attn_name):
                     _att.decode_dense(self.geometry, q_r, self.k_cache[li], self.v_cache[li], seq, B,
                                       self.capacity, self.workspace, attn)
             else:
-                with self._sec("elementwise"):
+                with self._sec("elementwise", "RoPE + K/V append", rope_bytes, rope_name):
                     _att.rope_append_decode_paged_qkv(self.geometry, qkv, q_r, pos, B, self.rope_cfg,
                                                       self.k_pool[li], self.v_pool[li], self.n_pages,
                                                       self.page_tokens, self.page_table, self.max_pages)
-                with self._sec("attention"):
+                with self._sec("attention", "decode attention", attn_bytes, attn_name):
                     _att.decode_paged(self.geometry, q_r, self.k_pool[li], self.v_pool[li], self.n_pages,
                                       self.page_tokens, self.page_table, self.max_pages, seq, B,
                                       self.workspace, attn)
             n = self._after_attention(li, x, attn, fused=True)
-        with self._sec("elementwise"):
+        with self._sec("elementwise", "positions", 8 * B, "torch add"):
             self.lengths.add_(1)
+        self.host_length += 1
         return self._lm_head_argmax(n)
 
     # --------------------------------------------------- validation digest --
@@ -404,6 +448,7 @@ class DeviceModel:
         t = self.torch
         self.g_tokens = t.zeros(self.batch, dtype=t.int32, device=self.device)
         saved = self.lengths.clone()
+        saved_host = self.host_length
         self.graph = t.cuda.CUDAGraph()
         side = t.cuda.Stream()
         side.wait_stream(t.cuda.current_stream())
@@ -412,10 +457,12 @@ class DeviceModel:
         t.cuda.current_stream().wait_stream(side)
         # capturing ran nothing; keep the lengths the caller had
         self.lengths.copy_(saved)
+        self.host_length = saved_host
 
     def decode_step_graphed(self, tokens):
         self.g_tokens.copy_(tokens)
         self.graph.replay()
+        self.host_length += 1
         return self.g_out, self.g_logits
 
     def release_graph(self):
