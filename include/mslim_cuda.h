@@ -172,20 +172,28 @@ int mslim_cuda_decode_workspace_bytes(const mslim_geometry_t *geometry, uint32_t
                                       uint32_t max_tokens, uint32_t split_tokens, size_t *bytes);
 
 /* The split size (tokens, a multiple of 64) that split_tokens == 0 selects
- * for n_seq sequences of at most max_tokens tokens.  Outputs depend on the
- * split size only through rounding; a caller that needs the same bits from
- * two calls passes the same explicit value.  Counterpart of the split count
- * that AttentionKernelConfig carries (src/attention_kernel.rs:6-42). */
+ * for n_seq sequences of at most max_tokens tokens: the model of
+ * mslim_cuda_decode_split_tokens_for_lengths with every sequence taken at
+ * max_tokens (256..3072 tokens; remembered per shape).  The number of splits
+ * it gives is not monotone in max_tokens, so a workspace meant for every
+ * history up to some capacity is sized with split_tokens = 256, the shortest
+ * split it takes.  Outputs depend on the split size only through rounding; a
+ * caller that needs the same bits from two calls passes the same explicit
+ * value (or the same max_tokens).  Counterpart of the split count that
+ * AttentionKernelConfig carries (src/attention_kernel.rs:6-42). */
 int mslim_cuda_decode_split_tokens(const mslim_geometry_t *geometry, uint32_t n_seq,
                                    uint32_t max_tokens, uint32_t *split_tokens);
 
 /* A split size for one batch whose token counts the host knows (host int32
  * lengths[n_seq], as the runtime tracks them): the split CTAs of a decode
- * run in waves of the GPU's resident CTAs, so the size is chosen for the
- * fewest waves times the split length rather than from the longest session
- * alone; pass it to the decode calls of that batch (bits are identical for
- * every call with the same split size); 256..3072 tokens.  No reference
- * counterpart: the reference's split-KV plan takes a fixed split count. */
+ * run in waves of the GPU's resident CTAs, each paying a fixed start-up cost
+ * besides its tokens, so every candidate size (3072, 2688, 2048, 1536, 1024,
+ * 768, 512, 256 tokens; none needing more than 16 waves, except 3072) runs
+ * through a model of those CTAs sharing HBM and the fastest is kept (at most
+ * the longest sequence rounded up to 64, at least 256); pass it to the decode
+ * calls of that batch (bits are identical for every call with the same split
+ * size).  No reference counterpart: the reference's split-KV plan takes a
+ * fixed split count. */
 int mslim_cuda_decode_split_tokens_for_lengths(const mslim_geometry_t *geometry, uint32_t n_seq,
                                                const int32_t *lengths, uint32_t *split_tokens);
 

@@ -171,12 +171,38 @@ def _fluid_step_time(lengths, per_seq, slots, st, cap=2.5, fixed=300.0, exit_cos
     return t
 
 
+SPLIT_CANDIDATES = (3072, 2688, 2048, 1536, 1024, 768, 512, 256)
+
+
+def _choose_split(lengths, per_seq, slots, max_waves=16):
+    """The library's choice among the split candidates: the shortest modelled
+    step, the longer split within 0.5 %; a candidate needing more than
+    max_waves waves of CTAs is skipped (except the longest); the result is at
+    most the longest sequence rounded up to 64 tokens, at least 256."""
+    longest = max([0] + [int(x) for x in lengths])
+    best, best_st = 0.0, SPLIT_CANDIDATES[0]
+    for st in SPLIT_CANDIDATES:
+        grid = len(lengths) * per_seq * max(1, -(-longest // st))
+        if st != SPLIT_CANDIDATES[0] and grid > max_waves * slots:
+            continue
+        t = _fluid_step_time(lengths, per_seq, slots, st)
+        if best == 0.0 or t < best * 0.995:
+            best, best_st = t, st
+    return min(best_st, max(256, -(-longest // 64) * 64))
+
+
+def _slots(head_dim):
+    kd = 64 if head_dim <= 64 else 128 if head_dim <= 128 else 256
+    return 148 * (3 if kd == 64 else 2 if kd == 128 else 1)
+
+
 def test_split_tokens_for_host_lengths(m):
     """mslim_cuda_decode_split_tokens_for_lengths runs the model of the split
-    kernel's CTAs on the GPU over the split sizes 3072, 2688, 2048, 1536, 1024
-    and keeps the fastest (the longer split within 0.5 %): it equals this
-    restatement of the model for the C4 draw and its shards of 2, 4 and 8
-    GPUs, and is deterministic."""
+    kernel's CTAs on the GPU over the candidate split sizes and keeps the
+    fastest: it equals this restatement of the model for the C4 draw and its
+    shards of 2, 4 and 8 GPUs, where it picks the sizes measured best on B200
+    (3072 tokens on 1 GPU and on the shards of 4, 2688 on those of 2 and 8),
+    and is deterministic."""
     import numpy as np
     import bench
     from mslim_b200 import workloads
@@ -186,15 +212,43 @@ def test_split_tokens_for_host_lengths(m):
         for rank in sorted({0, world - 1}):
             lengths = L[bench.lpt_shard(L, world, rank)].astype(np.int32)
             st = m.decode_split_tokens_for_lengths(g, lengths)
-            assert st in (3072, 2688, 2048, 1536, 1024)
+            assert st in SPLIT_CANDIDATES
             assert st == m.decode_split_tokens_for_lengths(g, lengths)
-            best, best_st = 0.0, None
-            for cand in (3072, 2688, 2048, 1536, 1024):
-                t = _fluid_step_time(lengths, 8, 296, cand)
-                if best_st is None or t < best * 0.995:
-                    best, best_st = t, cand
-            assert st == best_st, (world, rank, st, best_st)
-    assert m.decode_split_tokens_for_lengths(g, np.zeros(3, np.int32)) % 64 == 0
+            assert st == _choose_split(lengths, 8, 296), (world, rank, st)
+            if rank == 0:
+                assert st == {1: 3072, 2: 2688, 4: 3072, 8: 2688}[world]
+    assert m.decode_split_tokens_for_lengths(g, np.zeros(3, np.int32)) == 256
+    assert m.decode_split_tokens_for_lengths(g, np.array([100, 7], np.int32)) == 256
+
+
+def test_split_tokens_for_device_lengths(m):
+    """split_tokens == 0 (lengths on the device, only the longest known):
+    the same model with every sequence at max_tokens.  C5's decode at TP 1,
+    2 and 8 (8 sessions of ~8.3 K tokens) gets long splits instead of the
+    hundreds of short CTAs a fixed CTAs-per-SM target gave; short histories
+    keep 256-token splits so their few items still spread over the GPU."""
+    import numpy as np
+    cases = [((32, 8, 128), 8, 8260), ((16, 4, 128), 8, 8260), ((4, 1, 128), 8, 8260),
+             ((32, 8, 128), 1, 1025), ((32, 8, 128), 1, 520), ((32, 8, 128), 64, 32768),
+             ((32, 8, 128), 4, 4096), ((32, 8, 64), 4, 4096), ((32, 8, 256), 2, 16384),
+             ((64, 2, 128), 3, 5000), ((32, 8, 128), 1, 40)]
+    for (qh, kvh, d), n_seq, max_tokens in cases:
+        g = m.AttentionGeometry.new(qh, kvh, d)
+        group = qh // kvh
+        chunks = 1 if group <= 16 else group // 16
+        want = _choose_split(np.full(n_seq, max_tokens, np.int32), kvh * chunks, _slots(d))
+        got = m.decode_split_tokens(g, n_seq, max_tokens)
+        assert got == want, ((qh, kvh, d), n_seq, max_tokens, got, want)
+        assert got == m.decode_split_tokens(g, n_seq, max_tokens)     # remembered, same answer
+        assert 256 <= got <= 3072 and got % 64 == 0
+    g = m.AttentionGeometry.new(32, 8, 128)
+    assert m.decode_split_tokens(g, 8, 8260) == 3072          # C5, TP 1
+    assert m.decode_split_tokens(g, 1, 1025) == 256           # C1
+    # a workspace sized at split 256 holds the policy's partials for every
+    # shorter history (the policy's split count is not monotone in the length)
+    cap = 9000
+    big = m.decode_workspace_bytes(g, 1, cap, 256)
+    assert all(m.decode_workspace_bytes(g, 1, t) <= big for t in range(1, cap + 1, 97))
 
 
 def test_kernel_launch_counter_reads_without_a_gpu(m):

@@ -105,13 +105,13 @@ def test_static_scratch_rejects_oversized_requests(m):
 
 
 def test_static_scratch_takes_larger_splits_when_the_policy_split_overflows(m):
-    """64 sessions of 32768 tokens: at the library's own split size the
-    partials need more than the 16 MiB array, so split_tokens == 0 doubles the
-    split until they fit.  The result equals the workspace entry point at that
+    """96 sessions of 32768 tokens: at the library's own split size (3072
+    tokens) the partials need more than the 16 MiB array, so split_tokens == 0
+    doubles the split until they fit.  The result equals the workspace entry point at that
     doubled split, bit for bit, on two calls in a row."""
     torch = torch_mod()
     g = m.AttentionGeometry.new(32, 8, 128)
-    n_seq, L, pt = 64, 32768, 256
+    n_seq, L, pt = 96, 32768, 256
     limit = 16 << 20
     policy = m.decode_split_tokens(g, n_seq, L)
     assert m.decode_workspace_bytes(g, n_seq, L, policy) > limit     # the case overflows

@@ -15,9 +15,11 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
-#include <string>
 #include <queue>
+#include <string>
+#include <tuple>
 #include <vector>
 
 #include "../../include/mslim_cuda.h"
@@ -200,20 +202,102 @@ int decode_shape(const mslim_geometry_t *g, uint32_t nq, DecodeShapeInfo *s) {
     return MSLIM_OK;
 }
 
-// Split policy (tokens per split, a multiple of the 64-token TMA stage):
-// about seven CTAs per SM (3.5 waves of two) if every (session, KV-head
-// chunk) item held max_tokens tokens, at least 256 tokens (four pipeline
-// stages, so a CTA's setup is amortised and the merge combines few partials)
-// and at most 2048.  Sessions shorter than max_tokens make fewer CTAs, so the
-// real count is lower; splits this long were measured faster than shorter
-// ones both for 64 C4 sessions on one GPU and for the 8-session shards of an
-// 8-GPU run (per-CTA setup and the merge cost more than the last wave's
-// imbalance).
-uint32_t policy_split_tokens(uint64_t work_items, uint64_t max_tokens) {
-    const uint64_t target = 148ull * 7;
-    uint64_t st = (work_items * max_tokens + target - 1) / target;
-    st = (st + 63) / 64 * 64;
-    return (uint32_t)std::min<uint64_t>(std::max<uint64_t>(st, 256), 2048);
+// Step time of the split kernel with split size `st`, in token-times of one CTA
+// streaming at its share of HBM under full load.  CTAs start in grid order
+// (split fastest, then KV-head chunk, then session) as the `slots` resident
+// places free up.  While n CTAs run, each streams at min(kCap, slots / n)
+// times its full-load rate: HBM is shared, and a CTA alone is limited by its
+// own pipeline (about 2.5x its full-load share, so the last CTAs of a step
+// speed up only that much).  A CTA costs its tokens plus kFixed (filling its
+// pipeline, combining its warps); a CTA past its session's splits exits at
+// once (kExit).  Every running CTA receives the same service, so the next one
+// to finish is the one with the least service left: a heap of completion
+// levels, O(CTAs log slots).
+double fluid_step_time(const int32_t *lengths, uint32_t n_seq, uint64_t per_seq, uint64_t slots, uint32_t st) {
+    constexpr double kCap = 2.5, kFixed = 300.0, kExit = 8.0;
+    uint64_t max_splits = 1;
+    for (uint32_t i = 0; i < n_seq; ++i)
+        if (lengths[i] > 0) max_splits = std::max<uint64_t>(max_splits, ((uint64_t)lengths[i] + st - 1) / st);
+    std::priority_queue<double, std::vector<double>, std::greater<double>> running;  // completion levels
+    double level = 0.0, t = 0.0;
+    auto finish = [&]() {  // advance to the next completion
+        const double n = (double)running.size();
+        const double rate = std::min(kCap, (double)slots / n);
+        t += (running.top() - level) / rate;
+        level = running.top();
+        running.pop();
+    };
+    for (uint32_t i = 0; i < n_seq; ++i) {
+        const uint64_t L = lengths[i] > 0 ? (uint64_t)lengths[i] : 0;
+        const uint64_t n = L ? (L + st - 1) / st : 0;
+        const uint64_t slen = n ? ((L + n - 1) / n + 63) / 64 * 64 : 0;
+        for (uint64_t h = 0; h < per_seq; ++h)
+            for (uint64_t k = 0; k < max_splits; ++k) {
+                const double work = k < n ? (double)std::min<uint64_t>(slen, L - k * slen) + kFixed : kExit;
+                if (running.size() == slots) finish();
+                running.push(level + work);
+            }
+    }
+    while (!running.empty()) finish();
+    return t;
+}
+
+// Resident split CTAs per GPU: shared memory allows three per SM at head_dim
+// 64, two at 128 and one at 256 (the kernel's stage rings).
+uint64_t decode_slots(uint32_t kernel_dim) { return 148ull * (kernel_dim <= 64 ? 3 : kernel_dim <= 128 ? 2 : 1); }
+
+// Split sizes the policies choose from, longest first: the sizes the model was
+// checked against on the C4 shards of 1, 2, 4 and 8 GPUs (its choice within
+// 2 % of the best measured; sizes in between can land the last wave badly),
+// then shorter ones for small batches, where more CTAs than items pay.
+constexpr uint32_t kSplitCandidates[] = {3072, 2688, 2048, 1536, 1024, 768, 512, 256};
+// A split that needs more than this many waves of CTAs is not modelled: its
+// per-CTA costs outweigh any tail it could balance (and the model's heap would
+// grow with the CTA count).  The longest candidate is always modelled.
+constexpr uint64_t kPolicyMaxWaves = 16;
+
+// The candidate with the shortest modelled step (the longer split when two are
+// within 0.5 %), at most the longest sequence rounded up to the 64-token stage
+// and at least 256 tokens.  `lengths` holds n_seq sequences, each with per_seq
+// (KV-head chunk) items.
+uint32_t choose_split(const int32_t *lengths, uint32_t n_seq, uint64_t per_seq, uint64_t slots) {
+    uint64_t longest = 0;
+    for (uint32_t i = 0; i < n_seq; ++i) longest = std::max<uint64_t>(longest, lengths[i] > 0 ? (uint64_t)lengths[i] : 0);
+    double best = 0.0;
+    uint32_t best_st = kSplitCandidates[0];
+    for (uint32_t st : kSplitCandidates) {
+        const uint64_t grid = (uint64_t)n_seq * per_seq * std::max<uint64_t>(1, (longest + st - 1) / st);
+        if (st != kSplitCandidates[0] && grid > kPolicyMaxWaves * slots) continue;
+        const double t = fluid_step_time(lengths, n_seq, per_seq, slots, st);
+        if (best == 0.0 || t < best * 0.995) {
+            best = t;
+            best_st = st;
+        }
+    }
+    const uint64_t cap = std::max<uint64_t>(256, (longest + 63) / 64 * 64);
+    return (uint32_t)std::min<uint64_t>(best_st, cap);
+}
+
+// Split policy when only the longest sequence is known (lengths on the
+// device): the same model with every one of the work_items (sequence x query
+// block, KV-head chunk) items at max_tokens.  Remembered per shape, so a
+// decode loop pays for the model once.
+uint32_t policy_split_tokens(uint64_t work_items, uint64_t max_tokens, uint64_t slots) {
+    static std::mutex mu;
+    static std::map<std::tuple<uint64_t, uint64_t, uint64_t>, uint32_t> memo;
+    const int32_t len = (int32_t)std::min<uint64_t>(max_tokens, 0x7fffffffu);
+    const auto key = std::make_tuple(work_items, (uint64_t)len, slots);
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        auto it = memo.find(key);
+        if (it != memo.end()) return it->second;
+    }
+    // uniform lengths: one sequence of work_items items walks the same CTAs
+    const uint32_t st = choose_split(&len, 1, work_items, slots);
+    std::lock_guard<std::mutex> lock(mu);
+    if (memo.size() >= 4096) memo.clear();
+    memo.emplace(key, st);
+    return st;
 }
 
 // The kernel runs at the next head_dim in {64, 128, 256}; the caller's
@@ -599,7 +683,7 @@ int mslim_cuda_decode_workspace_bytes(const mslim_geometry_t *geometry, uint32_t
     if (int rc = decode_shape(geometry, 1, &sh)) return rc;
     if (split_tokens == 0)
         split_tokens = policy_split_tokens((uint64_t)n_seq * geometry->kv_heads * sh.head_chunks,
-                                           max_tokens);
+                                           max_tokens, decode_slots(kernel_dim_for(geometry->head_dim)));
     if (split_tokens % 64 != 0)
         return fail(MSLIM_ERR_SHAPE_MISMATCH, "split_tokens must be a multiple of 64");
     const uint64_t splits = (max_tokens + split_tokens - 1) / split_tokens;
@@ -614,53 +698,10 @@ int mslim_cuda_decode_split_tokens(const mslim_geometry_t *geometry, uint32_t n_
     if (n_seq == 0 || max_tokens == 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty batch");
     DecodeShapeInfo sh;
     if (int rc = decode_shape(geometry, 1, &sh)) return rc;
-    *split_tokens = policy_split_tokens((uint64_t)n_seq * geometry->kv_heads * sh.head_chunks, max_tokens);
+    *split_tokens = policy_split_tokens((uint64_t)n_seq * geometry->kv_heads * sh.head_chunks, max_tokens,
+                                        decode_slots(kernel_dim_for(geometry->head_dim)));
     return MSLIM_OK;
 }
-
-namespace {
-
-// Step time of the split kernel with split size `st`, in token-times of one CTA
-// streaming at its share of HBM under full load.  CTAs start in grid order
-// (split fastest, then KV-head chunk, then session) as the `slots` resident
-// places free up.  While n CTAs run, each streams at min(kCap, slots / n)
-// times its full-load rate: HBM is shared, and a CTA alone is limited by its
-// own pipeline (about 2.5x its full-load share, so the last CTAs of a step
-// speed up only that much).  A CTA costs its tokens plus kFixed (filling its
-// pipeline, combining its warps); a CTA past its session's splits exits at
-// once (kExit).  Every running CTA receives the same service, so the next one
-// to finish is the one with the least service left: a heap of completion
-// levels, O(CTAs log slots).
-double fluid_step_time(const int32_t *lengths, uint32_t n_seq, uint64_t per_seq, uint64_t slots, uint32_t st) {
-    constexpr double kCap = 2.5, kFixed = 300.0, kExit = 8.0;
-    uint64_t max_splits = 1;
-    for (uint32_t i = 0; i < n_seq; ++i)
-        if (lengths[i] > 0) max_splits = std::max<uint64_t>(max_splits, ((uint64_t)lengths[i] + st - 1) / st);
-    std::priority_queue<double, std::vector<double>, std::greater<double>> running;  // completion levels
-    double level = 0.0, t = 0.0;
-    auto finish = [&]() {  // advance to the next completion
-        const double n = (double)running.size();
-        const double rate = std::min(kCap, (double)slots / n);
-        t += (running.top() - level) / rate;
-        level = running.top();
-        running.pop();
-    };
-    for (uint32_t i = 0; i < n_seq; ++i) {
-        const uint64_t L = lengths[i] > 0 ? (uint64_t)lengths[i] : 0;
-        const uint64_t n = L ? (L + st - 1) / st : 0;
-        const uint64_t slen = n ? ((L + n - 1) / n + 63) / 64 * 64 : 0;
-        for (uint64_t h = 0; h < per_seq; ++h)
-            for (uint64_t k = 0; k < max_splits; ++k) {
-                const double work = k < n ? (double)std::min<uint64_t>(slen, L - k * slen) + kFixed : kExit;
-                if (running.size() == slots) finish();
-                running.push(level + work);
-            }
-    }
-    while (!running.empty()) finish();
-    return t;
-}
-
-}  // namespace
 
 int mslim_cuda_decode_split_tokens_for_lengths(const mslim_geometry_t *geometry, uint32_t n_seq,
                                                const int32_t *lengths, uint32_t *split_tokens) {
@@ -669,27 +710,10 @@ int mslim_cuda_decode_split_tokens_for_lengths(const mslim_geometry_t *geometry,
     if (n_seq == 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty batch");
     DecodeShapeInfo sh;
     if (int rc = decode_shape(geometry, 1, &sh)) return rc;
-    // resident split CTAs: shared memory allows three per SM at head_dim 64,
-    // two at 128 and one at 256 (the kernel's stage rings)
-    const uint32_t kd = kernel_dim_for(geometry->head_dim);
-    const uint64_t slots = 148ull * (kd <= 64 ? 3 : kd <= 128 ? 2 : 1);
-    const uint64_t per_seq = (uint64_t)geometry->kv_heads * sh.head_chunks;
-    // Every candidate split runs through fluid_step_time (a model of the split
-    // kernel's CTAs on the GPU, above); the fastest wins, the longer split when
-    // two are within 0.5 %.  The candidates are the sizes the model was checked
-    // against on the C4 shards of 1, 2, 4 and 8 GPUs (its choice within 2 % of
-    // the best measured; sizes in between can land the last wave badly).
-    static const uint32_t kCandidates[] = {3072, 2688, 2048, 1536, 1024};
-    double best = 0.0;
-    uint32_t best_st = 2048;
-    for (uint32_t st : kCandidates) {
-        const double t = fluid_step_time(lengths, n_seq, per_seq, slots, st);
-        if (best == 0.0 || t < best * 0.995) {
-            best = t;
-            best_st = st;
-        }
-    }
-    *split_tokens = best_st;
+    // every candidate split through the model of the split kernel's CTAs on
+    // the GPU (fluid_step_time); choose_split keeps the fastest
+    *split_tokens = choose_split(lengths, n_seq, (uint64_t)geometry->kv_heads * sh.head_chunks,
+                                 decode_slots(kernel_dim_for(geometry->head_dim)));
     return MSLIM_OK;
 }
 
@@ -705,7 +729,7 @@ static int decode_common_checks(const mslim_geometry_t *geometry, uint32_t n_seq
     if (int rc = decode_shape(geometry, 1, &sh)) return rc;
     if (*split_tokens == 0)
         *split_tokens = policy_split_tokens((uint64_t)n_seq * geometry->kv_heads * sh.head_chunks,
-                                            max_tokens);
+                                            max_tokens, decode_slots(kernel_dim_for(geometry->head_dim)));
     return MSLIM_OK;
 }
 
@@ -1468,7 +1492,8 @@ int mslim_cuda_plan_run(mslim_plan_t *plan, const void *q, size_t q_bytes, const
             const uint64_t splits = std::min<uint64_t>(plan->config.splits, history);
             st = (uint32_t)(((history + splits - 1) / splits + 63) / 64 * 64);
         } else {
-            st = policy_split_tokens((uint64_t)sh.q_blocks * g->kv_heads * sh.head_chunks, history);
+            st = policy_split_tokens((uint64_t)sh.q_blocks * g->kv_heads * sh.head_chunks, history,
+                                     decode_slots(kernel_dim_for(g->head_dim)));
         }
         // Keep the partials inside the plan's scratch.
         while (partial_bytes(g, 1, queries, (history + st - 1) / st) > plan->scratch_bytes) st *= 2;
@@ -1663,7 +1688,7 @@ int mslim_cuda_backend_decode(mslim_backend_t *b, const mslim_geometry_t *geomet
     const uint32_t KD = DE <= 64 ? 64 : DE <= 128 ? 128 : 256;
     DecodeShapeInfo sh;
     if (int rc = decode_shape(geometry, 1, &sh)) return rc;
-    const uint32_t st = policy_split_tokens((uint64_t)KVH * sh.head_chunks, tokens);
+    const uint32_t st = policy_split_tokens((uint64_t)KVH * sh.head_chunks, tokens, decode_slots(KD));
     const uint64_t splits = (tokens + st - 1) / st;
     mslim_geometry_t kg = {QH, KVH, KD};
     const size_t q_bytes = (size_t)QH * KD * 4;

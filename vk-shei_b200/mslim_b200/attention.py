@@ -542,7 +542,9 @@ class GpuEngine:
         self.max_tokens = max_tokens
         self._workspace = None
         if geometry is not None and max_tokens > 0:
-            self._workspace = torch.zeros(max(decode_workspace_bytes(geometry, 1, max_tokens), 16),
+            # sized for the shortest split the library's policy takes (256
+            # tokens), so the policy's split for any history up to max_tokens fits
+            self._workspace = torch.zeros(max(decode_workspace_bytes(geometry, 1, max_tokens, 256), 16),
                                           dtype=torch.uint8, device=f"cuda:{device}")
 
     def set_attention_kernel(self, config: AttentionKernelConfig, geometry: AttentionGeometry,
