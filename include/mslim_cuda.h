@@ -174,7 +174,8 @@ int mslim_cuda_decode_workspace_bytes(const mslim_geometry_t *geometry, uint32_t
 /* The split size (tokens, a multiple of 64) that split_tokens == 0 selects
  * for n_seq sequences of at most max_tokens tokens: the model of
  * mslim_cuda_decode_split_tokens_for_lengths with every sequence taken at
- * max_tokens (256..3072 tokens; remembered per shape).  The number of splits
+ * max_tokens, its constants fitted to sweeps of equal-length batches (256..3072
+ * tokens; remembered per shape).  The number of splits
  * it gives is not monotone in max_tokens, so a workspace meant for every
  * history up to some capacity is sized with split_tokens = 256, the shortest
  * split it takes.  Outputs depend on the split size only through rounding; a

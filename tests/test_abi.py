@@ -174,18 +174,19 @@ def _fluid_step_time(lengths, per_seq, slots, st, cap=2.5, fixed=300.0, exit_cos
 SPLIT_CANDIDATES = (3072, 2688, 2048, 1536, 1024, 768, 512, 256)
 
 
-def _choose_split(lengths, per_seq, slots, max_waves=16):
+def _choose_split(lengths, per_seq, slots, cap, max_waves=16):
     """The library's choice among the split candidates: the shortest modelled
-    step, the longer split within 0.5 %; a candidate needing more than
-    max_waves waves of CTAs is skipped (except the longest); the result is at
-    most the longest sequence rounded up to 64 tokens, at least 256."""
+    step (per-CTA speed-up cap `cap`), the longer split within 0.5 %; a
+    candidate needing more than max_waves waves of CTAs is skipped (except the
+    longest); the result is at most the longest sequence rounded up to 64
+    tokens, at least 256."""
     longest = max([0] + [int(x) for x in lengths])
     best, best_st = 0.0, SPLIT_CANDIDATES[0]
     for st in SPLIT_CANDIDATES:
         grid = len(lengths) * per_seq * max(1, -(-longest // st))
         if st != SPLIT_CANDIDATES[0] and grid > max_waves * slots:
             continue
-        t = _fluid_step_time(lengths, per_seq, slots, st)
+        t = _fluid_step_time(lengths, per_seq, slots, st, cap=cap)
         if best == 0.0 or t < best * 0.995:
             best, best_st = t, st
     return min(best_st, max(256, -(-longest // 64) * 64))
@@ -214,7 +215,7 @@ def test_split_tokens_for_host_lengths(m):
             st = m.decode_split_tokens_for_lengths(g, lengths)
             assert st in SPLIT_CANDIDATES
             assert st == m.decode_split_tokens_for_lengths(g, lengths)
-            assert st == _choose_split(lengths, 8, 296), (world, rank, st)
+            assert st == _choose_split(lengths, 8, 296, cap=2.5), (world, rank, st)
             if rank == 0:
                 assert st == {1: 3072, 2: 2688, 4: 3072, 8: 2688}[world]
     assert m.decode_split_tokens_for_lengths(g, np.zeros(3, np.int32)) == 256
@@ -223,10 +224,12 @@ def test_split_tokens_for_host_lengths(m):
 
 def test_split_tokens_for_device_lengths(m):
     """split_tokens == 0 (lengths on the device, only the longest known):
-    the same model with every sequence at max_tokens.  C5's decode at TP 1,
-    2 and 8 (8 sessions of ~8.3 K tokens) gets long splits instead of the
-    hundreds of short CTAs a fixed CTAs-per-SM target gave; short histories
-    keep 256-token splits so their few items still spread over the GPU."""
+    the same model with every sequence at max_tokens and a per-CTA speed-up
+    cap of 1 (equal lengths: every CTA of a wave starts and ends together).
+    The picks for C5's decode at TP 1, 2 and 8 (8 sessions of ~8.3 K tokens)
+    are the splits measured fastest for those shapes on B200 (one full wave of
+    CTAs each); short histories keep 256-token splits so their few items
+    still spread over the GPU."""
     import numpy as np
     cases = [((32, 8, 128), 8, 8260), ((16, 4, 128), 8, 8260), ((4, 1, 128), 8, 8260),
              ((32, 8, 128), 1, 1025), ((32, 8, 128), 1, 520), ((32, 8, 128), 64, 32768),
@@ -236,13 +239,15 @@ def test_split_tokens_for_device_lengths(m):
         g = m.AttentionGeometry.new(qh, kvh, d)
         group = qh // kvh
         chunks = 1 if group <= 16 else group // 16
-        want = _choose_split(np.full(n_seq, max_tokens, np.int32), kvh * chunks, _slots(d))
+        want = _choose_split(np.full(n_seq, max_tokens, np.int32), kvh * chunks, _slots(d), cap=1.0)
         got = m.decode_split_tokens(g, n_seq, max_tokens)
         assert got == want, ((qh, kvh, d), n_seq, max_tokens, got, want)
         assert got == m.decode_split_tokens(g, n_seq, max_tokens)     # remembered, same answer
         assert 256 <= got <= 3072 and got % 64 == 0
     g = m.AttentionGeometry.new(32, 8, 128)
-    assert m.decode_split_tokens(g, 8, 8260) == 3072          # C5, TP 1
+    assert m.decode_split_tokens(g, 8, 8260) == 2688          # C5, TP 1 (256 CTAs)
+    assert m.decode_split_tokens(m.AttentionGeometry.new(16, 4, 128), 8, 8260) == 1024   # TP 2 (288 CTAs)
+    assert m.decode_split_tokens(m.AttentionGeometry.new(4, 1, 128), 8, 8260) == 256     # TP 8 (264 CTAs)
     assert m.decode_split_tokens(g, 1, 1025) == 256           # C1
     # a workspace sized at split 256 holds the policy's partials for every
     # shorter history (the policy's split count is not monotone in the length)

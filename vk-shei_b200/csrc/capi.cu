@@ -205,16 +205,18 @@ int decode_shape(const mslim_geometry_t *g, uint32_t nq, DecodeShapeInfo *s) {
 // Step time of the split kernel with split size `st`, in token-times of one CTA
 // streaming at its share of HBM under full load.  CTAs start in grid order
 // (split fastest, then KV-head chunk, then session) as the `slots` resident
-// places free up.  While n CTAs run, each streams at min(kCap, slots / n)
-// times its full-load rate: HBM is shared, and a CTA alone is limited by its
-// own pipeline (about 2.5x its full-load share, so the last CTAs of a step
-// speed up only that much).  A CTA costs its tokens plus kFixed (filling its
-// pipeline, combining its warps); a CTA past its session's splits exits at
-// once (kExit).  Every running CTA receives the same service, so the next one
-// to finish is the one with the least service left: a heap of completion
-// levels, O(CTAs log slots).
-double fluid_step_time(const int32_t *lengths, uint32_t n_seq, uint64_t per_seq, uint64_t slots, uint32_t st) {
-    constexpr double kCap = 2.5, kFixed = 300.0, kExit = 8.0;
+// places free up.  While n CTAs run, each streams at min(cap, slots / n)
+// times its full-load rate: HBM is shared, and a CTA is also limited by its
+// own pipeline.  `cap` is fitted to measured split sweeps of the kernel on
+// B200 (see the two policies below).  A CTA costs its tokens plus kFixed
+// (filling its pipeline, combining its warps); a CTA past its session's splits
+// exits at once (kExit).  Every running CTA receives the same service, so the
+// next one to finish is the one with the least service left: a heap of
+// completion levels, O(CTAs log slots).
+double fluid_step_time(const int32_t *lengths, uint32_t n_seq, uint64_t per_seq, uint64_t slots, uint32_t st,
+                       double cap) {
+    constexpr double kFixed = 300.0, kExit = 8.0;
+    const double kCap = cap;
     uint64_t max_splits = 1;
     for (uint32_t i = 0; i < n_seq; ++i)
         if (lengths[i] > 0) max_splits = std::max<uint64_t>(max_splits, ((uint64_t)lengths[i] + st - 1) / st);
@@ -256,11 +258,23 @@ constexpr uint32_t kSplitCandidates[] = {3072, 2688, 2048, 1536, 1024, 768, 512,
 // grow with the CTA count).  The longest candidate is always modelled.
 constexpr uint64_t kPolicyMaxWaves = 16;
 
+// Per-CTA speed-up cap of the model, fitted per policy to sweeps of every
+// candidate split on one B200 (the policy's pick against the fastest measured):
+// sessions of varied lengths (the C4 draw and its LPT shards of 2, 4 and 8
+// GPUs; CTAs that finish early leave their HBM share to the long ones) fit
+// 2.5, within 2.2 % of the fastest on every shard; equal lengths (the policy
+// without host lengths assumes every session at max_tokens; every CTA of a
+// wave starts and ends together, so a part-filled wave cannot speed up) fit
+// 1.0, within 1.2 % of the fastest on 14 shapes from 1 session of 128 K
+// tokens to 64 of 1 K, head_dim 64 to 256, GQA groups 4 to 32.
+constexpr double kCapVariedLengths = 2.5;
+constexpr double kCapEqualLengths = 1.0;
+
 // The candidate with the shortest modelled step (the longer split when two are
 // within 0.5 %), at most the longest sequence rounded up to the 64-token stage
 // and at least 256 tokens.  `lengths` holds n_seq sequences, each with per_seq
 // (KV-head chunk) items.
-uint32_t choose_split(const int32_t *lengths, uint32_t n_seq, uint64_t per_seq, uint64_t slots) {
+uint32_t choose_split(const int32_t *lengths, uint32_t n_seq, uint64_t per_seq, uint64_t slots, double cap) {
     uint64_t longest = 0;
     for (uint32_t i = 0; i < n_seq; ++i) longest = std::max<uint64_t>(longest, lengths[i] > 0 ? (uint64_t)lengths[i] : 0);
     double best = 0.0;
@@ -268,20 +282,20 @@ uint32_t choose_split(const int32_t *lengths, uint32_t n_seq, uint64_t per_seq, 
     for (uint32_t st : kSplitCandidates) {
         const uint64_t grid = (uint64_t)n_seq * per_seq * std::max<uint64_t>(1, (longest + st - 1) / st);
         if (st != kSplitCandidates[0] && grid > kPolicyMaxWaves * slots) continue;
-        const double t = fluid_step_time(lengths, n_seq, per_seq, slots, st);
+        const double t = fluid_step_time(lengths, n_seq, per_seq, slots, st, cap);
         if (best == 0.0 || t < best * 0.995) {
             best = t;
             best_st = st;
         }
     }
-    const uint64_t cap = std::max<uint64_t>(256, (longest + 63) / 64 * 64);
-    return (uint32_t)std::min<uint64_t>(best_st, cap);
+    const uint64_t limit = std::max<uint64_t>(256, (longest + 63) / 64 * 64);
+    return (uint32_t)std::min<uint64_t>(best_st, limit);
 }
 
 // Split policy when only the longest sequence is known (lengths on the
 // device): the same model with every one of the work_items (sequence x query
-// block, KV-head chunk) items at max_tokens.  Remembered per shape, so a
-// decode loop pays for the model once.
+// block, KV-head chunk) items at max_tokens, and the equal-lengths cap.
+// Remembered per shape, so a decode loop pays for the model once.
 uint32_t policy_split_tokens(uint64_t work_items, uint64_t max_tokens, uint64_t slots) {
     static std::mutex mu;
     static std::map<std::tuple<uint64_t, uint64_t, uint64_t>, uint32_t> memo;
@@ -293,7 +307,7 @@ uint32_t policy_split_tokens(uint64_t work_items, uint64_t max_tokens, uint64_t 
         if (it != memo.end()) return it->second;
     }
     // uniform lengths: one sequence of work_items items walks the same CTAs
-    const uint32_t st = choose_split(&len, 1, work_items, slots);
+    const uint32_t st = choose_split(&len, 1, work_items, slots, kCapEqualLengths);
     std::lock_guard<std::mutex> lock(mu);
     if (memo.size() >= 4096) memo.clear();
     memo.emplace(key, st);
@@ -713,7 +727,7 @@ int mslim_cuda_decode_split_tokens_for_lengths(const mslim_geometry_t *geometry,
     // every candidate split through the model of the split kernel's CTAs on
     // the GPU (fluid_step_time); choose_split keeps the fastest
     *split_tokens = choose_split(lengths, n_seq, (uint64_t)geometry->kv_heads * sh.head_chunks,
-                                 decode_slots(kernel_dim_for(geometry->head_dim)));
+                                 decode_slots(kernel_dim_for(geometry->head_dim)), kCapVariedLengths);
     return MSLIM_OK;
 }
 
