@@ -86,6 +86,9 @@ def parse():
                          "own (mslim_cuda_gemv) or cublas")
     ap.add_argument("--gemv", action="store_true",
                     help="the C5 decode projections: mslim_cuda_gemv against cuBLAS, per shape")
+    ap.add_argument("--split-sweep", action="store_true",
+                    help="time every candidate split size of the decode on equal-length batches and on the "
+                         "C4 shards (one JSON line per case; the data the split policies are fitted to)")
     ap.add_argument("--layer", action="store_true",
                     help="C3: one Llama-3-8B layer, 512-token prefill + 8 decode steps, CPU path beside it")
     return ap.parse_args()
@@ -514,6 +517,108 @@ def bench_layer(m, torch, device, args) -> dict:
     }
 
 
+SPLIT_CANDIDATES = (256, 512, 768, 1024, 1536, 2048, 2688, 3072)
+# equal-length batches: ((query heads, KV heads, head_dim), sessions, tokens, name)
+SPLIT_SWEEP_SHAPES = [
+    ((32, 8, 128), 8, 8257, "C5 tp1"), ((16, 4, 128), 8, 8257, "C5 tp2"), ((4, 1, 128), 8, 8257, "C5 tp8"),
+    ((32, 8, 128), 4, 4096, "b4 4k"), ((32, 8, 128), 16, 2048, "b16 2k"), ((32, 8, 128), 1, 131072, "b1 128k"),
+    ((32, 8, 64), 4, 4096, "d64 b4 4k"), ((32, 8, 256), 2, 16384, "d256 b2 16k"),
+    ((64, 2, 128), 3, 5000, "g32 b3 5k"), ((32, 8, 128), 32, 16384, "b32 16k"),
+    ((32, 8, 128), 8, 32768, "b8 32k"), ((32, 8, 128), 2, 65536, "b2 64k"),
+    ((16, 4, 128), 4, 4096, "tp2 b4 4k"), ((32, 8, 128), 64, 1024, "b64 1k"), ((8, 2, 128), 8, 16384, "tp4 b8 16k"),
+]
+SPLIT_SWEEP_SHARDS = [(1, 0), (2, 0), (2, 1), (4, 0), (4, 3), (8, 0), (8, 3), (8, 7)]
+
+
+def _graph_us(torch, call, reps: int) -> float:
+    """Median of three graph replays of `reps` calls, microseconds per call."""
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.graph(graph, stream=side):
+        for _ in range(reps):
+            call()
+    torch.cuda.current_stream().wait_stream(side)
+    graph.replay()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(3):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        graph.replay()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b) * 1e3 / reps)
+    del graph
+    return sorted(times)[1]
+
+
+def bench_split_sweep(m, torch, device, args) -> None:
+    """Every candidate split size of the split-KV decode, timed on one GPU:
+    equal-length batches (dense caches, several rotating copies so the K/V
+    streamed per graph replay exceeds L2) with the pick of the policy without
+    host lengths, then the C4 shards of 1, 2, 4 and 8 GPUs (ColdStore pages)
+    with the pick of mslim_cuda_decode_split_tokens_for_lengths.  One JSON
+    line per case, microseconds per decode call."""
+    import numpy as np
+    from mslim_b200 import workloads
+    for (qh, kvh, d), n_seq, L, name in SPLIT_SWEEP_SHAPES:
+        g = m.AttentionGeometry.new(qh, kvh, d)
+        cap = L + 3
+        per = n_seq * cap * kvh * d * 4
+        copies = max(1, -(-(512 << 20) // per))
+        ks = [torch.randn((n_seq, cap, kvh, d), device=device, dtype=torch.bfloat16) for _ in range(copies)]
+        vs = [torch.randn((n_seq, cap, kvh, d), device=device, dtype=torch.bfloat16) for _ in range(copies)]
+        q = torch.randn((n_seq, qh, d), device=device, dtype=torch.bfloat16)
+        seq = torch.full((n_seq,), L, dtype=torch.int32, device=device)
+        ws = torch.zeros(m.decode_workspace_bytes(g, n_seq, cap, 256), dtype=torch.uint8, device=device)
+        o = torch.empty((n_seq, qh, d), device=device, dtype=torch.bfloat16)
+        us = {}
+        for st in SPLIT_CANDIDATES:
+            if st > max(256, (cap + 63) // 64 * 64) and st != SPLIT_CANDIDATES[-1]:
+                continue   # one split per session, the same CTAs as the longest candidate
+
+            def calls(st=st):
+                for i in range(copies):
+                    m.decode_dense(g, q, ks[i], vs[i], seq, n_seq, cap, ws, o, st)
+            us[st] = _graph_us(torch, calls, max(4, 40 // copies)) / copies
+        pick = m.decode_split_tokens(g, n_seq, cap)
+        print(json.dumps({"case": name, "geometry": [qh, kvh, d], "sessions": n_seq, "tokens": L,
+                          "max_tokens": cap, "us": {str(k): round(v, 2) for k, v in us.items()},
+                          "policy": "mslim_cuda_decode_split_tokens", "pick": pick,
+                          "fastest": min(us, key=us.get)}), flush=True)
+        del ks, vs
+        torch.cuda.empty_cache()
+    layout = workloads.c4_layout(seed=3)
+    lengths_all = layout.lengths[:64]
+    for world, rank in SPLIT_SWEEP_SHARDS:
+        lengths = lengths_all[lpt_shard(lengths_all, world, rank)].astype(np.int32)
+        c4 = C4Pages(np, torch, device, m, lengths, seed=3 + rank)
+        pick = c4.split_tokens
+        c4.ws = torch.zeros(m.decode_workspace_bytes(c4.g, c4.n_seq, c4.max_pages * PAGE, 256),
+                            dtype=torch.uint8, device=device)
+        us = {}
+
+        def c4_step():
+            c4.stream = torch.cuda.current_stream()   # the capturing stream inside the graph
+            c4.step()
+        for st in SPLIT_CANDIDATES:
+            c4.split_tokens = st
+            us[st] = _graph_us(torch, c4_step, 40 if world >= 4 else 20)
+        print(json.dumps({"case": f"C4 shard {rank}/{world}", "geometry": [QH, KVH, D], "sessions": c4.n_seq,
+                          "tokens": c4.tokens, "us": {str(k): round(v, 2) for k, v in us.items()},
+                          "policy": "mslim_cuda_decode_split_tokens_for_lengths", "pick": pick,
+                          "fastest": min(us, key=us.get)}), flush=True)
+        c4.close()
+        del c4
+        torch.cuda.empty_cache()
+    if m.device_status(torch.cuda.current_device()) != 0:
+        raise SystemExit("device status reported an error during the split sweep")
+
+
 def bench_model(m, torch, device, args, rank, world, dist) -> dict | None:
     """C5: a Llama-3-8B-shaped decoder with random
     weights, batch 8, 8192-token prefill then 256 greedy decode steps,
@@ -679,6 +784,9 @@ def main():
         return
     if args.gemv:
         print(json.dumps(bench_gemv(m, torch, device, args)), flush=True)
+        return
+    if args.split_sweep:
+        bench_split_sweep(m, torch, device, args)
         return
     if args.model:
         line = bench_model(m, torch, device, args, rank, world, dist)
