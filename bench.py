@@ -399,7 +399,8 @@ def bench_gemv(m, torch, device, args) -> dict:
     """The C5 decode step's projections (batch 8 rows; TP 1 and per-rank TP 8
     shapes) through mslim_cuda_gemv (the tcgen05 weight stream) and through
     cuBLAS (torch.matmul), each as 40 calls captured in one CUDA graph, best
-    of five replays between CUDA events.  Weight copies rotate so that every
+    of five replays between CUDA events; the gate|up shapes also with SwiGLU
+    (mslim_cuda_gemv_swiglu, or either projection then mslim_cuda_swiglu_rows).  Weight copies rotate so that every
     call streams its weights from HBM (> 400 MB of weights per replay)."""
     from mslim_b200 import attention as att
     torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = False
@@ -414,13 +415,26 @@ def bench_gemv(m, torch, device, args) -> dict:
         x = torch.randn((rows, k), generator=gen, device=device, dtype=torch.bfloat16)
         y = torch.empty((rows, n), device=device, dtype=torch.bfloat16)
         res = {"shape": name, "n": n, "k": k, "rows": rows, "weight_bytes": wbytes}
-        for kind in ("own", "cublas"):
+        act = torch.empty((rows, n // 2), device=device, dtype=torch.bfloat16)
+        # gate|up shapes: also SwiGLU, fused into the projection (interleaved
+        # weights) or as a second launch after either projection
+        kinds = ("own", "cublas") + (("fused_swiglu", "own_then_swiglu", "cublas_then_swiglu")
+                                     if "gate_up" in name else ())
+        for kind in kinds:
             def call(i, st):
                 w = ws[i % copies]
                 if kind == "own":
                     att.gemv(x, w, y, rows, n, k, stream=st)
-                else:
+                elif kind == "cublas":
                     torch.matmul(x, w.t(), out=y)
+                elif kind == "fused_swiglu":
+                    att.gemv_swiglu(x, w, act, rows, n // 2, k, stream=st)
+                else:
+                    if kind == "own_then_swiglu":
+                        att.gemv(x, w, y, rows, n, k, stream=st)
+                    else:
+                        torch.matmul(x, w.t(), out=y)
+                    att.swiglu_rows(y, act, rows * (n // 2) // 64, 64, stream=st)
             stream = torch.cuda.current_stream()
             for i in range(6):
                 call(i, stream)

@@ -392,6 +392,21 @@ int mslim_cuda_swiglu(const void *gate, const void *up, void *out, uint64_t n, v
 int mslim_cuda_gemv(const void *x, const void *w, void *y, uint32_t m, uint32_t n, uint32_t k, uint32_t ldy,
                     void *stream);
 
+/* A SwiGLU MLP's gate and up projections and the activation in one launch
+ * (llm_prefill_fused_swiglu_reuse8, assets/gpu_llm.cl:1323-1337, which fuses
+ * the gate/up GEMVs with llm_swiglu the same way):
+ * out[r][i] = bf16(bf16(g / (1 + exp(-g))) * u), g and u the bf16-rounded
+ * projections of x[r] on feature i's gate and up weight rows.  w_gu: bf16
+ * [2 * width][k], gate and up rows interleaved in blocks of 64 -- rows
+ * 128b .. 128b+63 are the gate rows of features 64b .. 64b+63, rows
+ * 128b+64 .. 128b+127 their up rows; width a multiple of 64; out bf16 rows of
+ * ldo >= width elements; x, m, k, alignment and streaming as mslim_cuda_gemv.
+ * The same bits as mslim_cuda_gemv over w_gu into y [m][2 * width] followed by
+ * mslim_cuda_swiglu_rows(y, out, m * width / 64, 64) (each 128-wide block of y
+ * read as one [gate 64 | up 64] row), without writing y. */
+int mslim_cuda_gemv_swiglu(const void *x, const void *w_gu, void *out, uint32_t m, uint32_t width, uint32_t k,
+                           uint32_t ldo, void *stream);
+
 /* SwiGLU over a fused gate|up projection (no reference counterpart: the
  * reference keeps gate and up in separate buffers, GpuEngine::swiglu):
  * gate_up bf16 [rows][gate (width) | up (width)], out bf16 [rows][width],

@@ -330,6 +330,63 @@ def test_gemv_matches_fp32_reference(m, n, k):
     assert mm.device_status(0) == 0
 
 
+@pytest.mark.parametrize("m,width,k", [(8, 14336, 4096), (8, 7168, 4096), (8, 1792, 4096), (3, 3584, 4096),
+                                       (1, 64, 128), (16, 192, 72)])
+def test_gemv_swiglu_equals_projection_then_swiglu(m, width, k):
+    """The fused gate|up projection + SwiGLU (gpu_llm.cl
+    llm_prefill_fused_swiglu_reuse8) returns the bits of the two-step path:
+    the projection over the interleaved weights, then SwiGLU over each
+    [gate 64 | up 64] block -- and those equal the projection over the
+    concatenated [gate | up] weights followed by SwiGLU over the halves; a
+    second call gives the same bits."""
+    import torch
+    import mslim_b200 as mm
+    rng = np.random.default_rng(m * 11 + width + k)
+    x = _rand_bf16(rng, m * k).reshape(m, k)
+    wg = _rand_bf16(rng, width * k, 0.02).reshape(width, k)
+    wu = _rand_bf16(rng, width * k, 0.02).reshape(width, k)
+    wgu = mm.interleave_gate_up(dev(wg), dev(wu))
+    xd = dev(x)
+    out = torch.full((m, width), 0x7FC1, dtype=torch.int16, device="cuda:0")
+    mm.gemv_swiglu(xd, wgu, out, m, width, k)
+    y = torch.empty((m, 2 * width), dtype=torch.int16, device="cuda:0")
+    mm.gemv(xd, wgu, y, m, 2 * width, k)
+    two_step = torch.empty((m, width), dtype=torch.int16, device="cuda:0")
+    mm.swiglu_rows(y, two_step, m * width // 64, 64)
+    assert torch.equal(out, two_step)
+    cat = dev(np.concatenate([wg, wu]))
+    y_cat = torch.empty((m, 2 * width), dtype=torch.int16, device="cuda:0")
+    mm.gemv(xd, cat, y_cat, m, 2 * width, k)
+    halves = torch.empty((m, width), dtype=torch.int16, device="cuda:0")
+    mm.swiglu_rows(y_cat, halves, m, width)
+    assert torch.equal(out, halves)
+    again = torch.empty_like(out)
+    mm.gemv_swiglu(xd, wgu, again, m, width, k)
+    assert torch.equal(out, again)
+    assert mm.device_status(0) == 0
+
+
+def test_gemv_swiglu_writes_strided_rows_and_rejects_bad_arguments():
+    import torch
+    import mslim_b200 as mm
+    rng = np.random.default_rng(9)
+    m, width, k, ldo = 4, 128, 256, 200
+    x = dev(_rand_bf16(rng, m * k).reshape(m, k))
+    wgu = dev(_rand_bf16(rng, 2 * width * k, 0.02).reshape(2 * width, k))
+    wide = torch.full((m, ldo), 0x1234, dtype=torch.int16, device="cuda:0")
+    mm.gemv_swiglu(x, wgu, wide, m, width, k, ldo=ldo)
+    dense = torch.empty((m, width), dtype=torch.int16, device="cuda:0")
+    mm.gemv_swiglu(x, wgu, dense, m, width, k)
+    got = u16(wide)
+    assert np.array_equal(got[:, :width], u16(dense)) and (got[:, width:] == 0x1234).all()
+    for bad in (dict(m=17), dict(width=96), dict(k=100), dict(ldo=width - 1)):
+        args = dict(m=m, width=width, k=k, ldo=0)
+        args.update(bad)
+        with pytest.raises(mm.ShapeMismatch):
+            mm.gemv_swiglu(x, wgu, dense, args["m"], args["width"], args["k"], ldo=args["ldo"])
+    assert mm.device_status(0) == 0
+
+
 def test_gemv_writes_strided_rows_and_rejects_bad_arguments():
     """ldy > n writes into a wider row (e.g. one slice of a fused output) and
     leaves the rest untouched; bad shapes are refused before any launch."""

@@ -69,9 +69,14 @@ def test_model_greedy_tokens_match_cpu_path(runs, runs_own_gemv, oracle, gemm):
     layers = []
     for W in M.layers:
         wqkv, wgu = _u16(W["wqkv"]), _u16(W["wgu"])
+        if M.gu_interleaved:   # blocks of 64 gate rows, each followed by its 64 up rows
+            blocks = wgu.reshape(inter // 64, 2, 64, -1)
+            wg, wu = blocks[:, 0].reshape(inter, -1), blocks[:, 1].reshape(inter, -1)
+        else:
+            wg, wu = wgu[:inter], wgu[inter:]
         layers.append({"input_norm": _u16(W["in_norm"]), "wq": wqkv[:qd], "wk": wqkv[qd:qd + kd],
                        "wv": wqkv[qd + kd:], "wo": _u16(W["wo"]), "post_norm": _u16(W["post_norm"]),
-                       "wg": wgu[:inter], "wu": wgu[inter:], "wd": _u16(W["wd"])})
+                       "wg": wg, "wu": wu, "wd": _u16(W["wd"])})
     emb = _u16(M.embedding)
     fnorm = _u16(M.final_norm)
     exact = near = 0

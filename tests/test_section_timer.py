@@ -50,3 +50,21 @@ def test_section_defaults_name_the_kind():
     sec = timer("elementwise")
     assert (sec.kind, sec.op, sec.kernel, sec.nbytes, sec.link) == ("elementwise", "elementwise", "elementwise",
                                                                       0, "hbm")
+
+
+def test_interleave_gate_up_layout():
+    """Blocks of 64 gate rows, each followed by the up rows of the same 64
+    features (the weight layout of mslim_cuda_gemv_swiglu)."""
+    import pytest
+    import torch
+    from mslim_b200 import attention as att
+    width, k = 192, 8
+    gate = torch.arange(width * k, dtype=torch.int32).reshape(width, k)
+    up = -gate - 1
+    w = att.interleave_gate_up(gate, up)
+    assert w.shape == (2 * width, k)
+    for b in range(width // 64):
+        assert torch.equal(w[128 * b:128 * b + 64], gate[64 * b:64 * b + 64])
+        assert torch.equal(w[128 * b + 64:128 * b + 128], up[64 * b:64 * b + 64])
+    with pytest.raises(att.ShapeMismatch):
+        att.interleave_gate_up(gate[:100], up[:100])

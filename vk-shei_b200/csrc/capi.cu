@@ -1123,6 +1123,35 @@ int mslim_cuda_gemv(const void *x, const void *w, void *y, uint32_t m, uint32_t 
     return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "projection launch");
 }
 
+int mslim_cuda_gemv_swiglu(const void *x, const void *w_gu, void *out, uint32_t m, uint32_t width, uint32_t k,
+                           uint32_t ldo, void *stream) {
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    if (!x || !w_gu || !out) return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
+    if (m == 0 || m > 16) return fail(MSLIM_ERR_SHAPE_MISMATCH, "the decode projection takes 1..16 rows");
+    if (width == 0 || width % 64 != 0 || k == 0 || k % 8 != 0)
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "width must be a positive multiple of 64 and k of 8");
+    if (width > 0x3fffffc0u || k > 0x7fffffc0u) return fail(MSLIM_ERR_SHAPE_MISMATCH, "projection too large");
+    if (ldo < width) return fail(MSLIM_ERR_SHAPE_MISMATCH, "ldo must be at least width");
+    if (!aligned(x, 16) || !aligned(w_gu, 16) || !aligned(out, 2))
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "x and w_gu must be 16-byte aligned");
+    if (out == x || out == w_gu) return fail(MSLIM_ERR_SHAPE_MISMATCH, "the output must not alias an input");
+    const uint32_t n = 2 * width;
+    const mslim::GemvPlan plan = mslim::gemv_plan(m, n, k);
+    CUtensorMap xmap, wmap;
+    {
+        const uint64_t xd[2] = {k, m}, xs[1] = {(uint64_t)k * 2};
+        const uint32_t xbox[2] = {64, 16};
+        const uint64_t wd[2] = {k, n}, ws[1] = {(uint64_t)k * 2};
+        const uint32_t wbox[2] = {64, 128};
+        if (int rc = make_tmap(&xmap, x, 2, xd, xs, xbox)) return rc;
+        if (int rc = make_tmap(&wmap, w_gu, 2, wd, ws, wbox)) return rc;
+    }
+    cudaError_t err = mslim::launch_gemv_tc(xmap, wmap, plan, m, n, static_cast<uint16_t *>(out), ldo,
+                                            status_ptr(dev), static_cast<cudaStream_t>(stream), true);
+    return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "gate|up projection launch");
+}
+
 int mslim_cuda_swiglu_rows(const void *gate_up, void *out, uint32_t rows, uint32_t width, void *stream) {
     int dev;
     if (int rc = current_device(&dev)) return rc;

@@ -29,6 +29,15 @@
 // arrive on its barrier, and it adds them in split order and rounds once, so
 // the result does not depend on which CTA finished first, and nothing goes
 // through global memory (no workspace).
+//
+// SwiGLU form (kSwiGLU): the weight rows are the gate and up projections
+// interleaved in blocks of 64 (a tile's rows 0..63 are gate features
+// 64t..64t+63, rows 64..127 the up features of the same block), so the tile
+// that finishes a block's gate sums also holds its up sums: the epilogue rounds
+// both to bf16 (as the plain form writes them), meets them in shared memory and
+// writes bf16(bf16(silu(g)) * u) for 64 features (gpu_llm.cl
+// llm_prefill_fused_swiglu_reuse8, one launch instead of a projection and an
+// elementwise pass).
 #include "gemv.cuh"
 
 namespace mslim {
@@ -153,6 +162,7 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+template <bool kSwiGLU>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     mslim_gemv_tc(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
                   const GemvParams p) {
@@ -232,13 +242,36 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     griddep_wait();  // outputs are written only once the predecessor is done
     const uint32_t n = tile * 128 + threadIdx.x;
     const uint32_t M = p.m;
+    // The tile's finished sums -> outputs (every thread of the CTA calls it).
+    auto write_rows = [&](const float (&v)[16]) {
+        if constexpr (!kSwiGLU) {
+            if (n < p.n) {
+#pragma unroll
+                for (uint32_t r = 0; r < 16; ++r)
+                    if (r < M) p.y[(size_t)r * p.ldy + n] = bf16_bits_rn(v[r]);
+            }
+        } else {
+            // the ring is idle (every stage consumed, every partial added)
+            float *up = reinterpret_cast<float *>(smem);  // [16 rows][64 features]
+            __syncthreads();
+            if (threadIdx.x >= 64) {
+#pragma unroll
+                for (uint32_t r = 0; r < 16; ++r)
+                    if (r < M) up[r * 64 + (threadIdx.x - 64)] = bf16_round(v[r]);
+            }
+            __syncthreads();
+            const uint32_t i = tile * 64 + threadIdx.x;  // output feature
+            if (threadIdx.x < 64 && i < p.n / 2) {
+#pragma unroll
+                for (uint32_t r = 0; r < 16; ++r)
+                    if (r < M)
+                        p.y[(size_t)r * p.ldy + i] = bf16_bits_rn(silu_mul(bf16_round(v[r]), up[r * 64 + threadIdx.x]));
+            }
+        }
+    };
     cluster_wait();  // every CTA of the cluster has its barriers initialised
     if (p.splits == 1) {
-        if (n < p.n) {
-#pragma unroll
-            for (uint32_t r = 0; r < 16; ++r)
-                if (r < M) p.y[(size_t)r * p.ldy + n] = bf16_bits_rn(acc[r]);
-        }
+        write_rows(acc);
     } else {
         // Partners push their fp32 partials into rank 0's ring, which is idle
         // once rank 0's own MMAs completed (every stage was consumed):
@@ -259,11 +292,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                 for (uint32_t r = 0; r < 16; ++r)
                     if (r < M) sum[r] += red[((s - 1) * 16 + r) * 128 + threadIdx.x];
             }
-            if (n < p.n) {
-#pragma unroll
-                for (uint32_t r = 0; r < 16; ++r)
-                    if (r < M) p.y[(size_t)r * p.ldy + n] = bf16_bits_rn(sum[r]);
-            }
+            write_rows(sum);
         } else {
             mbar_wait_cluster(&bars->go, 0, p.status, 25);
             const uint32_t dst = mapa(smem_u32(red + ((rank - 1) * 16) * 128 + threadIdx.x), 0);
@@ -306,7 +335,7 @@ GemvPlan gemv_plan(uint32_t m, uint32_t n, uint32_t k) {
 }
 
 cudaError_t launch_gemv_tc(const CUtensorMap &xmap, const CUtensorMap &wmap, const GemvPlan &plan, uint32_t m,
-                           uint32_t n, uint16_t *y, uint32_t ldy, int *status, cudaStream_t stream) {
+                           uint32_t n, uint16_t *y, uint32_t ldy, int *status, cudaStream_t stream, bool swiglu) {
     GemvParams p{};
     p.m = m;
     p.n = n;
@@ -317,7 +346,8 @@ cudaError_t launch_gemv_tc(const CUtensorMap &xmap, const CUtensorMap &wmap, con
     p.y = y;
     p.status = status;
     const size_t smem = (size_t)kStages * kStageBytes + sizeof(Bars) + 1024;
-    cudaError_t err = cudaFuncSetAttribute(mslim_gemv_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    auto kernel = swiglu ? mslim_gemv_tc<true> : mslim_gemv_tc<false>;
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess) return err;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(plan.n_tiles, plan.splits);
@@ -333,7 +363,7 @@ cudaError_t launch_gemv_tc(const CUtensorMap &xmap, const CUtensorMap &wmap, con
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    return counted(cudaLaunchKernelEx(&cfg, mslim_gemv_tc, xmap, wmap, p));
+    return counted(cudaLaunchKernelEx(&cfg, kernel, xmap, wmap, p));
 }
 
 }  // namespace mslim

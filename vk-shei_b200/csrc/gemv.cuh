@@ -20,8 +20,11 @@ GemvPlan gemv_plan(uint32_t m, uint32_t n, uint32_t k);
 // Y[m][n] (row stride ldy elements) = bf16(sum_k X[m][k] * W[n][k]), fp32
 // accumulation in TMEM, the splits combined in order over distributed shared
 // memory.  xmap: 2-D bf16 map over X (K, m) with a 64 x 16 box; wmap: over W
-// (K, n) with a 64 x 128 box; both 128-byte swizzle.
+// (K, n) with a 64 x 128 box; both 128-byte swizzle.  swiglu: W's rows are
+// gate and up interleaved in blocks of 64 (n = 2 x width, width % 64 == 0) and
+// Y[m][width] = bf16(bf16(silu(bf16(gate))) * bf16(up)).
 cudaError_t launch_gemv_tc(const CUtensorMap &xmap, const CUtensorMap &wmap, const GemvPlan &plan, uint32_t m,
-                           uint32_t n, uint16_t *y, uint32_t ldy, int *status, cudaStream_t stream);
+                           uint32_t n, uint16_t *y, uint32_t ldy, int *status, cudaStream_t stream,
+                           bool swiglu = false);
 
 }  // namespace mslim

@@ -29,11 +29,6 @@ __device__ __forceinline__ uint32_t add_pair(uint32_t a, uint32_t b) {
     return pack_bf16x2(bf16lo_f32(a) + bf16lo_f32(b), bf16hi_f32(a) + bf16hi_f32(b));
 }
 
-__device__ __forceinline__ float silu_mul(float g, float u) {
-    const float activated = bf16_round(g / (1.0f + expf(-g)));
-    return activated * u;
-}
-
 __device__ __forceinline__ uint32_t swiglu_pair(uint32_t g, uint32_t u) {
     return pack_bf16x2(silu_mul(bf16lo_f32(g), bf16lo_f32(u)), silu_mul(bf16hi_f32(g), bf16hi_f32(u)));
 }

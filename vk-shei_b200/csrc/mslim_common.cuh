@@ -243,6 +243,15 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 __device__ __forceinline__ float bf16lo_f32(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi_f32(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
+// SwiGLU of one gate/up pair already rounded to bf16: bf16(g / (1 + exp(-g)))
+// * u in f32; the caller rounds the product to bf16 (native_cpu_adapter.rs:
+// 553-560, gpu_llm.cl llm_swiglu).  One definition for every kernel that
+// applies it, so the fused and the separate forms return the same bits.
+__device__ __forceinline__ float silu_mul(float g, float u) {
+    const float activated = bf16_round(g / (1.0f + expf(-g)));
+    return activated * u;
+}
+
 __device__ __forceinline__ float fast_exp2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

@@ -88,6 +88,7 @@ SIGNATURES = {
     "mslim_cuda_residual_add": (_int, [_vp, _vp, _vp, ctypes.c_uint64, _vp]),
     "mslim_cuda_swiglu": (_int, [_vp, _vp, _vp, ctypes.c_uint64, _vp]),
     "mslim_cuda_gemv": (_int, [_vp, _vp, _vp, _u32, _u32, _u32, _u32, _vp]),
+    "mslim_cuda_gemv_swiglu": (_int, [_vp, _vp, _vp, _u32, _u32, _u32, _u32, _vp]),
     "mslim_cuda_page_token_hashes": (_int, [_vp, _u32, _u32, _u32, _u32, _vp, _u32, _u32, _vp, _vp]),
     "mslim_cuda_kv_canonical_dense": (_int, [_vp, _u32, _u32, _u32, _vp, _vp]),
     "mslim_cuda_decode_selected_workspace_bytes": (_int, [_vp, _u32, _u32, _u32, _vp]),

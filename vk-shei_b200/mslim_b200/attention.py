@@ -409,6 +409,25 @@ def gemv(x, w, y, m: int, n: int, k: int, ldy: int = 0, stream=None) -> None:
     check(_lib.lib().mslim_cuda_gemv(_ptr(x), _ptr(w), _ptr(y), m, n, k, ldy or n, _stream(stream)))
 
 
+def gemv_swiglu(x, w_gu, out, m: int, width: int, k: int, ldo: int = 0, stream=None) -> None:
+    """The gate|up projection and SwiGLU in one launch; w_gu in the layout of
+    interleave_gate_up (gpu_llm.cl llm_prefill_fused_swiglu_reuse8)."""
+    check(_lib.lib().mslim_cuda_gemv_swiglu(_ptr(x), _ptr(w_gu), _ptr(out), m, width, k, ldo or width,
+                                            _stream(stream)))
+
+
+def interleave_gate_up(gate, up):
+    """[width][k] gate and up weight rows (torch) -> the [2 * width][k] layout
+    of mslim_cuda_gemv_swiglu: blocks of 64 gate rows, each followed by the up
+    rows of the same 64 features."""
+    import torch
+    width, k = gate.shape
+    if width % 64 or up.shape != gate.shape:
+        raise ShapeMismatch("gate and up must be equal [width][k] with width a multiple of 64")
+    blocks = torch.stack([gate.reshape(width // 64, 64, k), up.reshape(width // 64, 64, k)], dim=1)
+    return blocks.reshape(2 * width, k).contiguous()
+
+
 def swiglu_rows(gate_up, out, rows: int, width: int, stream=None) -> None:
     """SwiGLU over rows of a fused [gate | up] projection output."""
     check(_lib.lib().mslim_cuda_swiglu_rows(_ptr(gate_up), _ptr(out), rows, width, _stream(stream)))

@@ -157,7 +157,12 @@ class DeviceModel:
             wo = normal(g, (L.hidden, L.q_dim))[:, q0:q1].contiguous()
             wg = normal(g, (L.intermediate, L.hidden))
             wu = normal(g, (L.intermediate, L.hidden))
-            wgu = torch.cat([wg[i0:i0 + inter], wu[i0:i0 + inter]]).contiguous()
+            if inter % 64 == 0:
+                # gate and up rows interleaved in blocks of 64, the layout of
+                # the fused gate|up projection + SwiGLU (mslim_cuda_gemv_swiglu)
+                wgu = _att.interleave_gate_up(wg[i0:i0 + inter], wu[i0:i0 + inter])
+            else:
+                wgu = torch.cat([wg[i0:i0 + inter], wu[i0:i0 + inter]]).contiguous()
             del wg, wu
             wd = normal(g, (L.hidden, L.intermediate))[:, i0:i0 + inter].contiguous()
             ones = torch.full((L.hidden,), 1.0, dtype=bf, device=dev)
@@ -174,6 +179,7 @@ class DeviceModel:
         self.lm_head = self.embedding[self.vocab_lo:self.vocab_hi]
         self.final_norm = torch.full((L.hidden,), 1.0, dtype=bf, device=dev)
         self.inter = inter
+        self.gu_interleaved = inter % 64 == 0
         # K/V of this rank's heads, per layer
         if kv_mode == "dense":
             self.k_cache = [torch.zeros((batch, capacity, self.kvh, D), dtype=bf, device=dev)
@@ -289,10 +295,21 @@ class DeviceModel:
         W = self.layers[li]
         n2 = self._reduce_residual_norm(attn.reshape(x.shape[0], -1), W["wo"], x, W["post_norm"], True, fused,
                                         op="o projection")
-        gu = self._gemm(n2, W["wgu"], op="gate|up projection")
-        act = t.empty((x.shape[0], self.inter), dtype=x.dtype, device=self.device)
-        with self._sec("elementwise", "SwiGLU", self._row_bytes(x.shape[0], self.inter, 3), "mslim_swiglu_rows"):
-            _att.swiglu_rows(gu, act, x.shape[0], self.inter)
+        rows, H = x.shape[0], self.spec.layer.hidden
+        act = t.empty((rows, self.inter), dtype=x.dtype, device=self.device)
+        if self.gu_interleaved and self.decode_gemm == "own" and rows <= 16:
+            # one launch: the projection's epilogue applies SwiGLU
+            nbytes = 2 * (2 * self.inter * H + rows * H + rows * self.inter)
+            with self._sec("gemm", "gate|up projection + SwiGLU", nbytes, "mslim_gemv_tc<swiglu>"):
+                _att.gemv_swiglu(n2, W["wgu"], act, rows, self.inter, H)
+        else:
+            gu = self._gemm(n2, W["wgu"], op="gate|up projection")
+            with self._sec("elementwise", "SwiGLU", self._row_bytes(rows, self.inter, 3), "mslim_swiglu_rows"):
+                if self.gu_interleaved:
+                    # every 128-wide block of a row is one [gate 64 | up 64] pair
+                    _att.swiglu_rows(gu, act, rows * self.inter // 64, 64)
+                else:
+                    _att.swiglu_rows(gu, act, rows, self.inter)
         nxt = self.layers[li + 1]["in_norm"] if li + 1 < len(self.layers) else self.final_norm
         return self._reduce_residual_norm(act, W["wd"], x, nxt, self.mlp == "sharded", fused, op="down projection")
 
