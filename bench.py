@@ -82,7 +82,7 @@ def parse():
     ap.add_argument("--kv-mode", choices=["dense", "coldstore"], default="dense")
     ap.add_argument("--no-graph", action="store_true", help="C5 decode steps issued eagerly (no CUDA graph)")
     ap.add_argument("--decode-gemm", choices=["auto", "own", "cublas"], default="auto",
-                    help="C5 decode projections: auto (mslim_cuda_gemv at TP > 1, cuBLAS at TP 1), "
+                    help="C5 decode projections: auto (= own), "
                          "own (mslim_cuda_gemv) or cublas")
     ap.add_argument("--gemv", action="store_true",
                     help="the C5 decode projections: mslim_cuda_gemv against cuBLAS, per shape")
@@ -650,10 +650,10 @@ def bench_model(m, torch, device, args, rank, world, dist) -> dict | None:
     spec = mdl.ModelSpec(layers=args.model_layers)
     L = spec.layer
     t0 = time.time()
-    # decode projections: the own tcgen05 GEMV where the ranks' shards are
-    # small (measured faster per step at TP 2 and per shape at TP 8), cuBLAS
-    # at TP 1 (measured 2-3 % faster there); profiles/gemv_c5_shapes.md
-    gemm = args.decode_gemm if args.decode_gemm != "auto" else ("own" if world > 1 else "cublas")
+    # decode projections: the own tcgen05 GEMV at every TP degree, its gate|up
+    # projection with SwiGLU fused into the epilogue (measured faster per step
+    # than cuBLAS at TP 1 and 2, and per shape at TP 8; profiles/gemv_c5_shapes.md)
+    gemm = args.decode_gemm if args.decode_gemm != "auto" else "own"
     M = mdl.DeviceModel(spec, B, S + steps + 4, seed=5, tp_rank=rank, tp_world=world, mlp=args.mlp,
                         kv_mode=args.kv_mode, decode_gemm=gemm)
     build_s = time.time() - t0
