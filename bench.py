@@ -135,6 +135,11 @@ class ClockSampler:
         if self._nvml:
             self._thread = threading.Thread(target=self._run, daemon=True)
             self._thread.start()
+            # the timed regions are short (~0.1 s): return only once the thread
+            # is polling, so its samples cover the region (bounded at 1 s)
+            t0 = time.time()
+            while len(self.samples) < 3 and time.time() - t0 < 1.0:
+                time.sleep(0.001)
 
     def stop(self) -> dict:
         self._stop.set()
