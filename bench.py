@@ -84,6 +84,9 @@ def parse():
     ap.add_argument("--decode-gemm", choices=["auto", "own", "cublas"], default="auto",
                     help="C5 decode projections: auto (= own), "
                          "own (mslim_cuda_gemv) or cublas")
+    ap.add_argument("--decode-qkv", choices=["fused", "separate"], default="fused",
+                    help="C5 decode with the own projections: the q|k|v projection with RoPE + K/V append in its "
+                         "epilogue (fused), or the projection then the append kernel (separate)")
     ap.add_argument("--gemv", action="store_true",
                     help="the C5 decode projections: mslim_cuda_gemv against cuBLAS, per shape")
     ap.add_argument("--split-sweep", action="store_true",
@@ -660,7 +663,7 @@ def bench_model(m, torch, device, args, rank, world, dist) -> dict | None:
     # than cuBLAS at TP 1 and 2, and per shape at TP 8; profiles/gemv_c5_shapes.md)
     gemm = args.decode_gemm if args.decode_gemm != "auto" else "own"
     M = mdl.DeviceModel(spec, B, S + steps + 4, seed=5, tp_rank=rank, tp_world=world, mlp=args.mlp,
-                        kv_mode=args.kv_mode, decode_gemm=gemm)
+                        kv_mode=args.kv_mode, decode_gemm=gemm, fuse_qkv=args.decode_qkv == "fused")
     build_s = time.time() - t0
     ids = torch.from_numpy(np.random.default_rng(5).integers(0, spec.vocab, size=(B, S))).to(device)
 
@@ -746,7 +749,8 @@ def bench_model(m, torch, device, args, rank, world, dist) -> dict | None:
                    "parallelism": f"tp{world} by KV-head group, MLP {args.mlp}", "kv": args.kv_mode,
                    "allreduce_per_layer": 1 if args.mlp == "replicated" else 2,
                    "decode_issue": "one CUDA graph per step" if graphed else "eager",
-                   "decode_projections": "mslim_cuda_gemv" if gemm == "own" else "cuBLAS"},
+                   "decode_projections": "mslim_cuda_gemv" if gemm == "own" else "cuBLAS",
+                   "decode_qkv": args.decode_qkv if gemm == "own" else "separate"},
         "prefill_ms": prefill_ms, "prefill_tokens_per_s": B * S / (prefill_ms * 1e-3),
         "decode_ms_per_step": decode_ms / steps,
         "decode_step_split_ms": step_split,

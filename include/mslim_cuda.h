@@ -543,6 +543,30 @@ int mslim_cuda_rope_append_decode_paged_qkv(const mslim_geometry_t *geometry, co
                                             uint32_t n_pages, uint32_t page_tokens,
                                             const int32_t *page_table, uint32_t max_pages, void *stream);
 
+/* The decode step's q|k|v projection with RoPE and the K/V append in its
+ * epilogue (the reference's run_layer projects q, k and v, rotates q and k
+ * and appends k and v, src/gpu_llm/mod.rs:2090-2125; its opt-in
+ * llm_prefill_fused_qkv_reuse8, assets/gpu_llm.cl:1253, fuses the three
+ * projections the same way, without the rotation): x bf16
+ * [n_seq][k] (1 <= n_seq <= 16, k a multiple of 8, 16-byte aligned), w_qkv
+ * bf16 [(query_heads + 2 kv_heads) * 128][k] (q, k, v weight rows, 16-byte
+ * aligned); head_dim must be 128 (else MSLIM_ERR_INVALID_GEOMETRY).  The same
+ * bits as mslim_cuda_gemv into qkv [n_seq][(QH + 2 KVH) * 128] followed by
+ * mslim_cuda_rope_append_decode_{dense,paged}_qkv with the same arguments,
+ * including their handling of a position or page id outside the store (that
+ * row is not written; mslim_cuda_device_status reports it), without writing
+ * or re-reading qkv.  Like mslim_cuda_gemv it starts streaming w_qkv before
+ * the preceding kernel in the stream has finished. */
+int mslim_cuda_gemv_qkv_rope_append_dense(const mslim_geometry_t *geometry, const void *x, const void *w_qkv,
+                                          uint32_t k, const int32_t *positions, uint32_t n_seq,
+                                          const mslim_rope_config_t *rope, void *q_out, void *k_cache,
+                                          void *v_cache, uint32_t max_tokens, void *stream);
+int mslim_cuda_gemv_qkv_rope_append_paged(const mslim_geometry_t *geometry, const void *x, const void *w_qkv,
+                                          uint32_t k, const int32_t *positions, uint32_t n_seq,
+                                          const mslim_rope_config_t *rope, void *q_out, void *k_pool,
+                                          void *v_pool, uint32_t n_pages, uint32_t page_tokens,
+                                          const int32_t *page_table, uint32_t max_pages, void *stream);
+
 /* ------------------------------------------- isolated backend (L3) -- */
 
 typedef struct mslim_backend mslim_backend_t;

@@ -266,6 +266,101 @@ def test_fused_qkv_append_matches_separate_inputs(paged):
     assert m.device_status(0) == 0
 
 
+def _qkv_rope_two_ways(m, g, cfg, x, w, pos, k, paged, T=600, pt=256):
+    """(q_out, K store, V store) of the fused q|k|v projection + RoPE + append
+    and of the plain projection followed by the q|k|v append, each from
+    zeroed stores and a poisoned q_out; the fused one twice."""
+    import torch
+    B = x.shape[0]
+    QH, KVH = g.query_heads, g.kv_heads
+    mp = -(-T // pt)
+    table = dev(np.random.default_rng(1).permutation(B * mp).astype(np.int32).reshape(B, mp))
+    runs = []
+    for form in ("two-step", "fused", "fused"):
+        q_out = torch.full((B, QH * 128), 0x7FC1, dtype=torch.int16, device="cuda:0")
+        shape = (B * mp, KVH, pt, 128) if paged else (B, T, KVH, 128)
+        kc = torch.zeros(shape, dtype=torch.int16, device="cuda:0")
+        vc = torch.zeros_like(kc)
+        if form == "fused":
+            if paged:
+                m.gemv_qkv_rope_append_paged(g, x, w, k, pos, B, cfg, q_out, kc, vc, B * mp, pt, table, mp)
+            else:
+                m.gemv_qkv_rope_append_dense(g, x, w, k, pos, B, cfg, q_out, kc, vc, T)
+        else:
+            qkv = torch.empty((B, (QH + 2 * KVH) * 128), dtype=torch.int16, device="cuda:0")
+            m.gemv(x, w, qkv, B, (QH + 2 * KVH) * 128, k)
+            if paged:
+                m.rope_append_decode_paged_qkv(g, qkv, q_out, pos, B, cfg, kc, vc, B * mp, pt, table, mp)
+            else:
+                m.rope_append_decode_dense_qkv(g, qkv, q_out, pos, B, cfg, kc, vc, T)
+        status = m.device_status(0)
+        runs.append(([u16(q_out), u16(kc), u16(vc)], status))
+    return runs
+
+
+@pytest.mark.parametrize("paged", [False, True])
+@pytest.mark.parametrize("qh,kvh,b,k", [(32, 8, 8, 4096), (16, 4, 8, 4096), (4, 1, 8, 4096), (32, 8, 3, 512),
+                                        (8, 2, 16, 72)])
+def test_gemv_qkv_rope_append_equals_projection_then_append(paged, qh, kvh, b, k):
+    """The decode q|k|v projection with RoPE + K/V append in its epilogue
+    writes the bits of the projection followed by the q|k|v append kernel:
+    q_out, the K and the V store (dense caches or ColdStore pages), on two
+    calls in a row; at C5's TP 1, 2 and 8 head counts and small shapes."""
+    import mslim_b200 as m
+    from mslim_b200 import attention as att
+    rng = np.random.default_rng(qh * 17 + b + k)
+    g = att.AttentionGeometry.new(qh, kvh, 128)
+    cfg = att.RopeKernelConfig(theta=500000.0)
+    x = dev(_rand_bf16(rng, b * k).reshape(b, k))
+    w = dev(_rand_bf16(rng, (qh + 2 * kvh) * 128 * k, 0.02).reshape(-1, k))
+    pos = dev(rng.integers(0, 600, size=b).astype(np.int32))
+    runs = _qkv_rope_two_ways(m, g, cfg, x, w, pos, k, paged)
+    (want, s0), (got, s1), (again, s2) = runs
+    assert s0 == s1 == s2 == 0
+    for a, c, d in zip(want, got, again):
+        assert np.array_equal(a, c) and np.array_equal(c, d)
+
+
+@pytest.mark.parametrize("paged", [False, True])
+def test_gemv_qkv_rope_append_skips_rows_outside_the_store(paged):
+    """A position outside the store (and, paged, a page id outside the pool)
+    writes nothing for that row, in the fused form as in the two-step one,
+    and the status word reports it; the other rows are written."""
+    import mslim_b200 as m
+    from mslim_b200 import attention as att
+    rng = np.random.default_rng(29)
+    qh, kvh, b, k = 8, 2, 4, 256
+    g = att.AttentionGeometry.new(qh, kvh, 128)
+    cfg = att.RopeKernelConfig(theta=10000.0)
+    x = dev(_rand_bf16(rng, b * k).reshape(b, k))
+    w = dev(_rand_bf16(rng, (qh + 2 * kvh) * 128 * k, 0.02).reshape(-1, k))
+    pos = dev(np.array([5, -1, 800, 599], np.int32))      # rows 1 and 2: outside the 600 / 768-token stores
+    runs = _qkv_rope_two_ways(m, g, cfg, x, w, pos, k, paged)
+    (want, s0), (got, s1), _ = runs
+    assert s0 != 0 and s1 != 0
+    for a, c in zip(want, got):
+        assert np.array_equal(a, c)
+    q_out = got[0]
+    assert (q_out[1] == 0x7FC1).all() and (q_out[2] == 0x7FC1).all() and not (q_out[0] == 0x7FC1).all()
+
+
+def test_gemv_qkv_rope_append_rejects_other_head_dims_and_batches():
+    import torch
+    import mslim_b200 as m
+    from mslim_b200 import attention as att
+    cfg = att.RopeKernelConfig(theta=10000.0)
+    x = torch.zeros((17, 64), dtype=torch.int16, device="cuda:0")
+    w = torch.zeros((6 * 128, 64), dtype=torch.int16, device="cuda:0")
+    q_out = torch.zeros((17, 4 * 128), dtype=torch.int16, device="cuda:0")
+    kc = torch.zeros((17, 16, 1, 128), dtype=torch.int16, device="cuda:0")
+    pos = torch.zeros(17, dtype=torch.int32, device="cuda:0")
+    with pytest.raises(m.InvalidGeometry):
+        m.gemv_qkv_rope_append_dense(att.AttentionGeometry.new(4, 1, 64), x, w, 64, pos, 4, cfg, q_out, kc, kc, 16)
+    with pytest.raises(m.ShapeMismatch):
+        m.gemv_qkv_rope_append_dense(att.AttentionGeometry.new(4, 1, 128), x, w, 64, pos, 17, cfg, q_out, kc, kc, 16)
+    assert m.device_status(0) == 0
+
+
 @pytest.mark.parametrize("paged", [False, True])
 @pytest.mark.parametrize("qh,kvh,d", [(32, 8, 128), (4, 1, 128), (8, 2, 80), (2, 2, 256)])
 def test_rope_append_vector_and_scalar_forms_agree(paged, qh, kvh, d):

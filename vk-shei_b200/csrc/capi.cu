@@ -1450,6 +1450,76 @@ int mslim_cuda_rope_append_decode_paged_qkv(const mslim_geometry_t *geometry, co
     return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "RoPE decode append launch");
 }
 
+// The decode q|k|v projection with RoPE + K/V append in its epilogue: the
+// checks of mslim_cuda_gemv and of the q|k|v append entry points.
+static int gemv_qkv_rope_append(const mslim_geometry_t *geometry, const void *x, const void *w_qkv, uint32_t k,
+                                const int32_t *positions, uint32_t n_seq, const mslim_rope_config_t *rope,
+                                void *q_out, mslim::GemvRopeAppend e, void *stream) {
+    if (int rc = check_geometry(geometry)) return rc;
+    if (geometry->head_dim != 128)
+        return fail(MSLIM_ERR_INVALID_GEOMETRY,
+                    "the fused q|k|v projection needs head_dim 128 (got %u); use mslim_cuda_gemv and "
+                    "mslim_cuda_rope_append_decode_*_qkv", geometry->head_dim);
+    int dev;
+    if (int rc = current_device(&dev)) return rc;
+    if (!x || !w_qkv || !q_out || !positions || !e.k_dst || !e.v_dst) return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
+    if (n_seq == 0 || n_seq > 16) return fail(MSLIM_ERR_SHAPE_MISMATCH, "the decode projection takes 1..16 rows");
+    if (k == 0 || k % 8 != 0 || k > 0x7fffffc0u) return fail(MSLIM_ERR_SHAPE_MISMATCH, "k must be a positive multiple of 8");
+    if (!aligned(x, 16) || !aligned(w_qkv, 16) || !aligned(q_out, 2))
+        return fail(MSLIM_ERR_SHAPE_MISMATCH, "x and w_qkv must be 16-byte aligned");
+    const uint64_t n64 = ((uint64_t)geometry->query_heads + 2ull * geometry->kv_heads) * 128;
+    if (n64 > 0x7fffff80u) return fail(MSLIM_ERR_SHAPE_MISMATCH, "projection too large");
+    if (int rc = build_rope_table(rope, 128, &e.table)) return rc;
+    e.positions = positions;
+    e.q_out = static_cast<uint16_t *>(q_out);
+    e.qheads = geometry->query_heads;
+    e.kvheads = geometry->kv_heads;
+    const uint32_t n = (uint32_t)n64;
+    const mslim::GemvPlan plan = mslim::gemv_plan(n_seq, n, k);
+    CUtensorMap xmap, wmap;
+    {
+        const uint64_t xd[2] = {k, n_seq}, xs[1] = {(uint64_t)k * 2};
+        const uint32_t xbox[2] = {64, 16};
+        const uint64_t wd[2] = {k, n}, ws[1] = {(uint64_t)k * 2};
+        const uint32_t wbox[2] = {64, 128};
+        if (int rc = make_tmap(&xmap, x, 2, xd, xs, xbox)) return rc;
+        if (int rc = make_tmap(&wmap, w_qkv, 2, wd, ws, wbox)) return rc;
+    }
+    cudaError_t err = mslim::launch_gemv_qkv_rope_append(xmap, wmap, plan, n_seq, n, e, status_ptr(dev),
+                                                         static_cast<cudaStream_t>(stream));
+    return err == cudaSuccess ? MSLIM_OK : cuda_fail(err, "q|k|v projection launch");
+}
+
+int mslim_cuda_gemv_qkv_rope_append_dense(const mslim_geometry_t *geometry, const void *x, const void *w_qkv,
+                                          uint32_t k, const int32_t *positions, uint32_t n_seq,
+                                          const mslim_rope_config_t *rope, void *q_out, void *k_cache,
+                                          void *v_cache, uint32_t max_tokens, void *stream) {
+    if (max_tokens == 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty cache");
+    mslim::GemvRopeAppend e{};
+    e.k_dst = static_cast<uint16_t *>(k_cache);
+    e.v_dst = static_cast<uint16_t *>(v_cache);
+    e.page_table = nullptr;
+    e.max_tokens = max_tokens;
+    return gemv_qkv_rope_append(geometry, x, w_qkv, k, positions, n_seq, rope, q_out, e, stream);
+}
+
+int mslim_cuda_gemv_qkv_rope_append_paged(const mslim_geometry_t *geometry, const void *x, const void *w_qkv,
+                                          uint32_t k, const int32_t *positions, uint32_t n_seq,
+                                          const mslim_rope_config_t *rope, void *q_out, void *k_pool,
+                                          void *v_pool, uint32_t n_pages, uint32_t page_tokens,
+                                          const int32_t *page_table, uint32_t max_pages, void *stream) {
+    if (!page_table) return fail(MSLIM_ERR_SHAPE_MISMATCH, "null buffer");
+    if (page_tokens == 0 || n_pages == 0 || max_pages == 0) return fail(MSLIM_ERR_SHAPE_MISMATCH, "empty page pool");
+    mslim::GemvRopeAppend e{};
+    e.k_dst = static_cast<uint16_t *>(k_pool);
+    e.v_dst = static_cast<uint16_t *>(v_pool);
+    e.page_table = page_table;
+    e.n_pages = n_pages;
+    e.page_tokens = page_tokens;
+    e.max_pages = max_pages;
+    return gemv_qkv_rope_append(geometry, x, w_qkv, k, positions, n_seq, rope, q_out, e, stream);
+}
+
 // -------------------------------------------------------------- plan --
 
 int mslim_cuda_plan_build(const mslim_kernel_config_t *config, const mslim_geometry_t *geometry,

@@ -38,12 +38,20 @@
 // writes bf16(bf16(silu(g)) * u) for 64 features (gpu_llm.cl
 // llm_prefill_fused_swiglu_reuse8, one launch instead of a projection and an
 // elementwise pass).
+//
+// RoPE + append form (head_dim 128): every tile of the q|k|v projection is one
+// head; the epilogue rounds the tile to bf16 (as the plain form writes it),
+// pairs features i and i + 64 through shared memory, rotates q and k heads
+// with the shared RoPE arithmetic and writes q to q_out and k / v into the
+// decode token's K/V row -- the work of mslim_rope_append_{dense,paged} on
+// the projection's output, without writing or re-reading that output.
 #include "gemv.cuh"
 
 namespace mslim {
 
 namespace {
 
+constexpr int kEpiPlain = 0, kEpiSwiGLU = 1, kEpiRope = 2;
 constexpr int kStages = 4;
 constexpr int kWBytes = 128 * 128;              // [128 rows][64 bf16] swizzled: 16 KB
 constexpr int kXBytes = 16 * 128;               // [16 rows][64 bf16]: 2 KB
@@ -162,10 +170,10 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-template <bool kSwiGLU>
+template <int kEpi>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     mslim_gemv_tc(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
-                  const GemvParams p) {
+                  const GemvParams p, const __grid_constant__ GemvRopeAppend e) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     Bars *bars = reinterpret_cast<Bars *>(smem + kStages * kStageBytes);
@@ -244,13 +252,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     const uint32_t M = p.m;
     // The tile's finished sums -> outputs (every thread of the CTA calls it).
     auto write_rows = [&](const float (&v)[16]) {
-        if constexpr (!kSwiGLU) {
+        if constexpr (kEpi == kEpiPlain) {
             if (n < p.n) {
 #pragma unroll
                 for (uint32_t r = 0; r < 16; ++r)
                     if (r < M) p.y[(size_t)r * p.ldy + n] = bf16_bits_rn(v[r]);
             }
-        } else {
+        } else if constexpr (kEpi == kEpiSwiGLU) {
             // the ring is idle (every stage consumed, every partial added)
             float *up = reinterpret_cast<float *>(smem);  // [16 rows][64 features]
             __syncthreads();
@@ -266,6 +274,50 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                 for (uint32_t r = 0; r < 16; ++r)
                     if (r < M)
                         p.y[(size_t)r * p.ldy + i] = bf16_bits_rn(silu_mul(bf16_round(v[r]), up[r * 64 + threadIdx.x]));
+            }
+        } else {
+            // the ring is idle: the tile's bf16 values, [16 rows][128 features]
+            float *xs = reinterpret_cast<float *>(smem);
+            __syncthreads();
+#pragma unroll
+            for (uint32_t r = 0; r < 16; ++r)
+                if (r < M) xs[r * 128 + threadIdx.x] = bf16_round(v[r]);
+            __syncthreads();
+            const uint32_t head = tile, t = threadIdx.x, i = t & 63;
+            const bool is_q = head < e.qheads, is_k = !is_q && head < e.qheads + e.kvheads;
+            // KV head of a k or v tile (0 for q tiles, whose rows go to q_out)
+            const uint32_t kh = is_q ? 0 : is_k ? head - e.qheads : head - e.qheads - e.kvheads;
+            for (uint32_t r = 0; r < M; ++r) {
+                // the destination checks of mslim_rope_append_{dense,paged}
+                const int32_t pp = e.positions[r];
+                uint16_t *kv_row;  // this head's 128-element K or V row of the token
+                bool bad;
+                if (e.page_table) {
+                    bad = pp < 0 || (uint64_t)pp >= (uint64_t)e.max_pages * e.page_tokens;
+                    const int32_t phys = bad ? 0 : e.page_table[(size_t)r * e.max_pages + (uint32_t)pp / e.page_tokens];
+                    bad = bad || phys < 0 || (uint32_t)phys >= e.n_pages;
+                    kv_row = (is_k ? e.k_dst : e.v_dst) +
+                             (((size_t)(bad ? 0 : phys) * e.kvheads + kh) * e.page_tokens + (uint32_t)pp % e.page_tokens) *
+                                 128;
+                } else {
+                    bad = pp < 0 || (uint32_t)pp >= e.max_tokens;
+                    kv_row = (is_k ? e.k_dst : e.v_dst) + (((size_t)r * e.max_tokens + (bad ? 0 : pp)) * e.kvheads + kh) * 128;
+                }
+                if (bad) {
+                    if (t == 0 && p.status) atomicExch(p.status, MSLIM_DEVICE_BAD_PAGE_CODE);
+                    continue;
+                }
+                float out;
+                if (is_q || is_k) {
+                    float oa, ob;
+                    rope_rotate(xs[r * 128 + i], xs[r * 128 + i + 64], rope_cs(rope_angle(e.table, (int)i, (uint32_t)pp)),
+                                oa, ob);
+                    out = t < 64 ? oa : ob;
+                } else {
+                    out = xs[r * 128 + t];
+                }
+                uint16_t *dst = is_q ? e.q_out + ((size_t)r * e.qheads + head) * 128 : kv_row;
+                dst[t] = bf16_bits_rn(out);
             }
         }
     };
@@ -334,19 +386,13 @@ GemvPlan gemv_plan(uint32_t m, uint32_t n, uint32_t k) {
     return pl;
 }
 
-cudaError_t launch_gemv_tc(const CUtensorMap &xmap, const CUtensorMap &wmap, const GemvPlan &plan, uint32_t m,
-                           uint32_t n, uint16_t *y, uint32_t ldy, int *status, cudaStream_t stream, bool swiglu) {
-    GemvParams p{};
-    p.m = m;
-    p.n = n;
-    p.ldy = ldy;
-    p.k_steps = plan.k_steps;
-    p.k_tiles = plan.k_tiles;
-    p.splits = plan.splits;
-    p.y = y;
-    p.status = status;
+namespace {
+
+cudaError_t launch_gemv_any(const CUtensorMap &xmap, const CUtensorMap &wmap, const GemvPlan &plan,
+                            const GemvParams &p, const GemvRopeAppend &e, int epi, cudaStream_t stream) {
     const size_t smem = (size_t)kStages * kStageBytes + sizeof(Bars) + 1024;
-    auto kernel = swiglu ? mslim_gemv_tc<true> : mslim_gemv_tc<false>;
+    auto kernel = epi == kEpiSwiGLU ? mslim_gemv_tc<kEpiSwiGLU>
+                                    : epi == kEpiRope ? mslim_gemv_tc<kEpiRope> : mslim_gemv_tc<kEpiPlain>;
     cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess) return err;
     cudaLaunchConfig_t cfg = {};
@@ -363,7 +409,39 @@ cudaError_t launch_gemv_tc(const CUtensorMap &xmap, const CUtensorMap &wmap, con
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    return counted(cudaLaunchKernelEx(&cfg, kernel, xmap, wmap, p));
+    return counted(cudaLaunchKernelEx(&cfg, kernel, xmap, wmap, p, e));
 }
+
+}  // namespace
+
+cudaError_t launch_gemv_tc(const CUtensorMap &xmap, const CUtensorMap &wmap, const GemvPlan &plan, uint32_t m,
+                           uint32_t n, uint16_t *y, uint32_t ldy, int *status, cudaStream_t stream, bool swiglu) {
+    GemvParams p{};
+    p.m = m;
+    p.n = n;
+    p.ldy = ldy;
+    p.k_steps = plan.k_steps;
+    p.k_tiles = plan.k_tiles;
+    p.splits = plan.splits;
+    p.y = y;
+    p.status = status;
+    return launch_gemv_any(xmap, wmap, plan, p, GemvRopeAppend{}, swiglu ? kEpiSwiGLU : kEpiPlain, stream);
+}
+
+cudaError_t launch_gemv_qkv_rope_append(const CUtensorMap &xmap, const CUtensorMap &wmap, const GemvPlan &plan,
+                                        uint32_t m, uint32_t n, const GemvRopeAppend &e, int *status,
+                                        cudaStream_t stream) {
+    GemvParams p{};
+    p.m = m;
+    p.n = n;
+    p.ldy = n;
+    p.k_steps = plan.k_steps;
+    p.k_tiles = plan.k_tiles;
+    p.splits = plan.splits;
+    p.y = nullptr;
+    p.status = status;
+    return launch_gemv_any(xmap, wmap, plan, p, e, kEpiRope, stream);
+}
+
 
 }  // namespace mslim

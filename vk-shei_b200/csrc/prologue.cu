@@ -19,23 +19,6 @@ namespace mslim {
 
 namespace {
 
-__device__ __forceinline__ float rope_angle(const RopeTable &t, int i, uint32_t position) {
-    const float pos = (float)position;
-    return t.multiply ? pos * t.freq[i] : __fdiv_rn(pos, t.freq[i]);
-}
-
-// (cos, sin) of one angle, each rounded to bf16.
-__device__ __forceinline__ float2 rope_cs(float angle) {
-    double sd, cd;
-    sincos((double)angle, &sd, &cd);
-    return make_float2(bf16_round((float)cd), bf16_round((float)sd));
-}
-
-__device__ __forceinline__ void rope_rotate(float a, float b, float2 cs, float &out_a, float &out_b) {
-    out_a = bf16_round(bf16_round(a * cs.x) - bf16_round(b * cs.y));
-    out_b = bf16_round(bf16_round(b * cs.x) + bf16_round(a * cs.y));
-}
-
 // The angle depends on (position, i) only, so a CTA that rotates every head
 // of one token evaluates its D/2 (cos, sin) pairs once, into shared memory.
 constexpr int kRopeMaxHalf = 128;

@@ -16,6 +16,26 @@ struct RopeTable {
     int multiply;
 };
 
+// The RoPE arithmetic, shared by every kernel that rotates (the RoPE and
+// RoPE + append kernels, and the q|k|v projection that applies them in its
+// epilogue), so all of them return the same bits.
+__device__ __forceinline__ float rope_angle(const RopeTable &t, int i, uint32_t position) {
+    const float pos = (float)position;
+    return t.multiply ? pos * t.freq[i] : __fdiv_rn(pos, t.freq[i]);
+}
+
+// (cos, sin) of one angle, each rounded to bf16.
+__device__ __forceinline__ float2 rope_cs(float angle) {
+    double sd, cd;
+    sincos((double)angle, &sd, &cd);
+    return make_float2(bf16_round((float)cd), bf16_round((float)sd));
+}
+
+__device__ __forceinline__ void rope_rotate(float a, float b, float2 cs, float &out_a, float &out_b) {
+    out_a = bf16_round(bf16_round(a * cs.x) - bf16_round(b * cs.y));
+    out_b = bf16_round(bf16_round(b * cs.x) + bf16_round(a * cs.y));
+}
+
 cudaError_t launch_rmsnorm(const uint16_t *x, const uint16_t *w, uint16_t *y, uint32_t tokens,
                            uint32_t hidden, float eps, cudaStream_t stream);
 // x = bf16(x + delta) in place, then y = RMSNorm(x): one pass per row.

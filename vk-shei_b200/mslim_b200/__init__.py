@@ -14,7 +14,8 @@ from .attention import (AttentionGeometry, AttentionKernelConfig, AttentionKerne
                         argmax, swiglu_rows, residual_rmsnorm, gemv, gemv_swiglu, interleave_gate_up, page_token_hashes, kv_canonical_dense, kv_canonical_paged,
                         decode_selected, decode_selected_paged, decode_selected_workspace_bytes,
                         rope_append_decode_dense_qkv,
-                        rope_append_decode_paged_qkv)
+                        rope_append_decode_paged_qkv, gemv_qkv_rope_append_dense,
+                        gemv_qkv_rope_append_paged)
 
 LIB_PATH = _lib.LIB_PATH
 

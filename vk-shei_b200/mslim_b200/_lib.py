@@ -101,6 +101,10 @@ SIGNATURES = {
     "mslim_cuda_argmax": (_int, [_vp, _u32, _u32, _int, _vp, _vp]),
     "mslim_cuda_residual_rmsnorm": (_int, [_vp, _vp, _vp, _vp, _u32, _u32, ctypes.c_float, _vp]),
     "mslim_cuda_rope_append_decode_dense_qkv": (_int, [_G, _vp, _vp, _vp, _u32, _R, _vp, _vp, _u32, _vp]),
+    "mslim_cuda_gemv_qkv_rope_append_dense": (_int, [_G, _vp, _vp, _u32, _vp, _u32, _R, _vp, _vp, _vp, _u32,
+                                                     _vp]),
+    "mslim_cuda_gemv_qkv_rope_append_paged": (_int, [_G, _vp, _vp, _u32, _vp, _u32, _R, _vp, _vp, _vp, _u32,
+                                                     _u32, _vp, _u32, _vp]),
     "mslim_cuda_rope_append_decode_paged_qkv": (_int, [_G, _vp, _vp, _vp, _u32, _R, _vp, _vp, _u32, _u32, _vp,
                                                        _u32, _vp]),
     "mslim_cuda_rmsnorm": (_int, [_vp, _vp, _vp, _u32, _u32, ctypes.c_float, _vp]),

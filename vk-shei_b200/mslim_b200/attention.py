@@ -456,6 +456,27 @@ def rope_append_decode_paged_qkv(geometry: AttentionGeometry, qkv, q_out, positi
         _ptr(k_pool), _ptr(v_pool), n_pages, page_tokens, _ptr(page_table), max_pages, _stream(stream)))
 
 
+def gemv_qkv_rope_append_dense(geometry: AttentionGeometry, x, w_qkv, k: int, positions, n_seq: int,
+                               cfg: RopeKernelConfig, q_out, k_cache, v_cache, max_tokens: int,
+                               stream=None) -> None:
+    """The decode q|k|v projection with rope_append_decode_dense_qkv in its
+    epilogue (head_dim 128)."""
+    check(_lib.lib().mslim_cuda_gemv_qkv_rope_append_dense(
+        ctypes.byref(geometry.c()), _ptr(x), _ptr(w_qkv), k, _ptr(positions), n_seq, ctypes.byref(cfg.c()),
+        _ptr(q_out), _ptr(k_cache), _ptr(v_cache), max_tokens, _stream(stream)))
+
+
+def gemv_qkv_rope_append_paged(geometry: AttentionGeometry, x, w_qkv, k: int, positions, n_seq: int,
+                               cfg: RopeKernelConfig, q_out, k_pool, v_pool, n_pages: int, page_tokens: int,
+                               page_table, max_pages: int, stream=None) -> None:
+    """The decode q|k|v projection with rope_append_decode_paged_qkv in its
+    epilogue (head_dim 128)."""
+    check(_lib.lib().mslim_cuda_gemv_qkv_rope_append_paged(
+        ctypes.byref(geometry.c()), _ptr(x), _ptr(w_qkv), k, _ptr(positions), n_seq, ctypes.byref(cfg.c()),
+        _ptr(q_out), _ptr(k_pool), _ptr(v_pool), n_pages, page_tokens, _ptr(page_table), max_pages,
+        _stream(stream)))
+
+
 def argmax(logits, rows: int, vocab: int, token_ids, ties_to_last: bool = True, stream=None) -> None:
     """GpuEngine::argmax (src/gpu_llm/gpu_resources.rs:1065) / the CPU greedy
     step (src/native_cpu_adapter.rs:582-587): int32 token id per row."""

@@ -112,7 +112,7 @@ def pick_shard_argmax(torch, every):
 class DeviceModel:
     def __init__(self, spec: ModelSpec, batch: int, capacity: int, seed: int = 5, tp_rank: int = 0,
                  tp_world: int = 1, mlp: str = "sharded", kv_mode: str = "dense", page_tokens: int = 256,
-                 group=None, device=None, decode_gemm: str = "cublas"):
+                 group=None, device=None, decode_gemm: str = "cublas", fuse_qkv: bool = True):
         import torch
         L = spec.layer
         if L.kv_heads % tp_world or L.intermediate % tp_world:
@@ -129,6 +129,7 @@ class DeviceModel:
         if decode_gemm not in ("own", "cublas"):
             raise ValueError("decode_gemm is 'own' (mslim_cuda_gemv) or 'cublas'")
         self.decode_gemm = decode_gemm
+        self.fuse_qkv = fuse_qkv
         self.batch, self.capacity = batch, capacity
         self.kvh = L.kv_heads // tp_world
         self.qh = L.query_heads // tp_world
@@ -399,23 +400,40 @@ class DeviceModel:
         rope_name = "mslim_rope_append_paged" if paged else "mslim_rope_append_dense"
         attn_name = ("mslim_decode_persist" if _att.get_decode_schedule() == _att.DECODE_PERSISTENT
                      else "mslim_decode_split + mslim_decode_merge_row")
+        # one launch for the q|k|v projection, RoPE and the K/V append where
+        # the own projection serves the step (head_dim 128: a head per tile)
+        fused_qkv = self.fuse_qkv and self.decode_gemm == "own" and D == 128 and B <= 16 and H % 8 == 0
+        qkv_bytes = 2 * ((self.qh + 2 * self.kvh) * D * H + B * H) + rope_bytes // 2
         n = self._norm(x, self.layers[0]["in_norm"])
         for li, W in enumerate(self.layers):
-            qkv = self._gemm(n, W["wqkv"], op="q|k|v projection")
             q_r = t.empty((B, self.qh * D), dtype=x.dtype, device=self.device)
             attn = t.empty_like(q_r)
+            if fused_qkv:
+                with self._sec("gemm", "q|k|v projection + RoPE + K/V append", qkv_bytes,
+                               "mslim_gemv_tc<rope_append>"):
+                    if self.kv_mode == "dense":
+                        _att.gemv_qkv_rope_append_dense(self.geometry, n, W["wqkv"], H, pos, B, self.rope_cfg, q_r,
+                                                        self.k_cache[li], self.v_cache[li], self.capacity)
+                    else:
+                        _att.gemv_qkv_rope_append_paged(self.geometry, n, W["wqkv"], H, pos, B, self.rope_cfg, q_r,
+                                                        self.k_pool[li], self.v_pool[li], self.n_pages,
+                                                        self.page_tokens, self.page_table, self.max_pages)
+            else:
+                qkv = self._gemm(n, W["wqkv"], op="q|k|v projection")
             if self.kv_mode == "dense":
-                with self._sec("elementwise", "RoPE + K/V append", rope_bytes, rope_name):
-                    _att.rope_append_decode_dense_qkv(self.geometry, qkv, q_r, pos, B, self.rope_cfg,
-                                                      self.k_cache[li], self.v_cache[li], self.capacity)
+                if not fused_qkv:
+                    with self._sec("elementwise", "RoPE + K/V append", rope_bytes, rope_name):
+                        _att.rope_append_decode_dense_qkv(self.geometry, qkv, q_r, pos, B, self.rope_cfg,
+                                                          self.k_cache[li], self.v_cache[li], self.capacity)
                 with self._sec("attention", "decode attention", attn_bytes, attn_name):
                     _att.decode_dense(self.geometry, q_r, self.k_cache[li], self.v_cache[li], seq, B,
                                       self.capacity, self.workspace, attn)
             else:
-                with self._sec("elementwise", "RoPE + K/V append", rope_bytes, rope_name):
-                    _att.rope_append_decode_paged_qkv(self.geometry, qkv, q_r, pos, B, self.rope_cfg,
-                                                      self.k_pool[li], self.v_pool[li], self.n_pages,
-                                                      self.page_tokens, self.page_table, self.max_pages)
+                if not fused_qkv:
+                    with self._sec("elementwise", "RoPE + K/V append", rope_bytes, rope_name):
+                        _att.rope_append_decode_paged_qkv(self.geometry, qkv, q_r, pos, B, self.rope_cfg,
+                                                          self.k_pool[li], self.v_pool[li], self.n_pages,
+                                                          self.page_tokens, self.page_table, self.max_pages)
                 with self._sec("attention", "decode attention", attn_bytes, attn_name):
                     _att.decode_paged(self.geometry, q_r, self.k_pool[li], self.v_pool[li], self.n_pages,
                                       self.page_tokens, self.page_table, self.max_pages, seq, B,
