@@ -84,7 +84,7 @@ def parse():
     ap.add_argument("--decode-gemm", choices=["auto", "own", "cublas"], default="auto",
                     help="C5 decode projections: auto (= own), "
                          "own (mslim_cuda_gemv) or cublas")
-    ap.add_argument("--decode-qkv", choices=["fused", "separate"], default="fused",
+    ap.add_argument("--decode-qkv", choices=["fused", "separate"], default="separate",
                     help="C5 decode with the own projections: the q|k|v projection with RoPE + K/V append in its "
                          "epilogue (fused), or the projection then the append kernel (separate)")
     ap.add_argument("--gemv", action="store_true",

@@ -287,36 +287,60 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
             const bool is_q = head < e.qheads, is_k = !is_q && head < e.qheads + e.kvheads;
             // KV head of a k or v tile (0 for q tiles, whose rows go to q_out)
             const uint32_t kh = is_q ? 0 : is_k ? head - e.qheads : head - e.qheads - e.kvheads;
-            for (uint32_t r = 0; r < M; ++r) {
-                // the destination checks of mslim_rope_append_{dense,paged}
-                const int32_t pp = e.positions[r];
-                uint16_t *kv_row;  // this head's 128-element K or V row of the token
+            // Each row's destination once, by thread r, in parallel: its
+            // position and (paged) physical page, or -1 where the checks of
+            // mslim_rope_append_{dense,paged} reject the row (nothing is
+            // written for it and the status word records it).  [16] int pairs
+            // after the tile's values.
+            int32_t *row_pos = reinterpret_cast<int32_t *>(xs + 16 * 128);
+            int32_t *row_phys = row_pos + 16;
+            if (t < M) {
+                const int32_t pp = e.positions[t];
+                int32_t phys = 0;
                 bool bad;
                 if (e.page_table) {
                     bad = pp < 0 || (uint64_t)pp >= (uint64_t)e.max_pages * e.page_tokens;
-                    const int32_t phys = bad ? 0 : e.page_table[(size_t)r * e.max_pages + (uint32_t)pp / e.page_tokens];
+                    if (!bad) phys = e.page_table[(size_t)t * e.max_pages + (uint32_t)pp / e.page_tokens];
                     bad = bad || phys < 0 || (uint32_t)phys >= e.n_pages;
-                    kv_row = (is_k ? e.k_dst : e.v_dst) +
-                             (((size_t)(bad ? 0 : phys) * e.kvheads + kh) * e.page_tokens + (uint32_t)pp % e.page_tokens) *
-                                 128;
                 } else {
                     bad = pp < 0 || (uint32_t)pp >= e.max_tokens;
-                    kv_row = (is_k ? e.k_dst : e.v_dst) + (((size_t)r * e.max_tokens + (bad ? 0 : pp)) * e.kvheads + kh) * 128;
                 }
-                if (bad) {
-                    if (t == 0 && p.status) atomicExch(p.status, MSLIM_DEVICE_BAD_PAGE_CODE);
-                    continue;
+                if (bad && p.status) atomicExch(p.status, MSLIM_DEVICE_BAD_PAGE_CODE);
+                row_pos[t] = bad ? -1 : pp;
+                row_phys[t] = phys;
+            }
+            __syncthreads();
+            // the (cos, sin) of every (row, pair) once, shared by the tile's
+            // threads: [16 rows][64 pairs]
+            float2 *cs = reinterpret_cast<float2 *>(row_pos + 32);
+            if (is_q || is_k) {
+                for (uint32_t j = t; j < M * 64; j += kThreads) {
+                    const int32_t pj = row_pos[j >> 6];
+                    cs[j] = pj >= 0 ? rope_cs(rope_angle(e.table, (int)(j & 63), (uint32_t)pj)) : make_float2(0.f, 0.f);
                 }
+            }
+            __syncthreads();
+            for (uint32_t r = 0; r < M; ++r) {
+                const int32_t pp = row_pos[r];
+                if (pp < 0) continue;
                 float out;
                 if (is_q || is_k) {
                     float oa, ob;
-                    rope_rotate(xs[r * 128 + i], xs[r * 128 + i + 64], rope_cs(rope_angle(e.table, (int)i, (uint32_t)pp)),
-                                oa, ob);
+                    rope_rotate(xs[r * 128 + i], xs[r * 128 + i + 64], cs[r * 64 + i], oa, ob);
                     out = t < 64 ? oa : ob;
                 } else {
                     out = xs[r * 128 + t];
                 }
-                uint16_t *dst = is_q ? e.q_out + ((size_t)r * e.qheads + head) * 128 : kv_row;
+                uint16_t *dst;
+                if (is_q) {
+                    dst = e.q_out + ((size_t)r * e.qheads + head) * 128;
+                } else {
+                    uint16_t *base = is_k ? e.k_dst : e.v_dst;
+                    dst = e.page_table
+                              ? base + (((size_t)row_phys[r] * e.kvheads + kh) * e.page_tokens +
+                                        (uint32_t)pp % e.page_tokens) * 128
+                              : base + (((size_t)r * e.max_tokens + (uint32_t)pp) * e.kvheads + kh) * 128;
+                }
                 dst[t] = bf16_bits_rn(out);
             }
         }
