@@ -660,7 +660,7 @@ def bench_model(m, torch, device, args, rank, world, dist) -> dict | None:
     t0 = time.time()
     # decode projections: the own tcgen05 GEMV at every TP degree, its gate|up
     # projection with SwiGLU fused into the epilogue (measured faster per step
-    # than cuBLAS at TP 1 and 2, and per shape at TP 8; profiles/gemv_c5_shapes.md)
+    # than cuBLAS at TP 1 and 2, and per shape at TP 8; `--gemv` times each shape)
     gemm = args.decode_gemm if args.decode_gemm != "auto" else "own"
     M = mdl.DeviceModel(spec, B, S + steps + 4, seed=5, tp_rank=rank, tp_world=world, mlp=args.mlp,
                         kv_mode=args.kv_mode, decode_gemm=gemm, fuse_qkv=args.decode_qkv == "fused")
