@@ -181,6 +181,8 @@ def _choose_split(lengths, per_seq, slots, cap, max_waves=16):
     longest); the result is at most the longest sequence rounded up to 64
     tokens, at least 256."""
     longest = max([0] + [int(x) for x in lengths])
+    if len(lengths) * per_seq * max(1, -(-longest // SPLIT_CANDIDATES[0])) > max_waves * slots:
+        return min(SPLIT_CANDIDATES[0], max(256, -(-longest // 64) * 64))   # only the longest is modelled
     best, best_st = 0.0, SPLIT_CANDIDATES[0]
     for st in SPLIT_CANDIDATES:
         grid = len(lengths) * per_seq * max(1, -(-longest // st))
@@ -249,6 +251,14 @@ def test_split_tokens_for_device_lengths(m):
     assert m.decode_split_tokens(m.AttentionGeometry.new(16, 4, 128), 8, 8260) == 1024   # TP 2 (288 CTAs)
     assert m.decode_split_tokens(m.AttentionGeometry.new(4, 1, 128), 8, 8260) == 256     # TP 8 (264 CTAs)
     assert m.decode_split_tokens(g, 1, 1025) == 256           # C1
+    # many waves at the longest split: the answer is the longest split, without
+    # simulating millions of CTAs (a decode call pays for the policy)
+    import time
+    t0 = time.perf_counter()
+    assert m.decode_split_tokens(g, 4096, 131072) == 3072
+    lens = np.full(4096, 131072, np.int32)
+    assert m.decode_split_tokens_for_lengths(g, lens) == 3072 == _choose_split(lens, 8, 296, cap=2.5)
+    assert time.perf_counter() - t0 < 0.5
     # a workspace sized at split 256 holds the policy's partials for every
     # shorter history (the policy's split count is not monotone in the length)
     cap = 9000

@@ -277,6 +277,13 @@ constexpr double kCapEqualLengths = 1.0;
 uint32_t choose_split(const int32_t *lengths, uint32_t n_seq, uint64_t per_seq, uint64_t slots, double cap) {
     uint64_t longest = 0;
     for (uint32_t i = 0; i < n_seq; ++i) longest = std::max<uint64_t>(longest, lengths[i] > 0 ? (uint64_t)lengths[i] : 0);
+    const uint64_t limit = std::max<uint64_t>(256, (longest + 63) / 64 * 64);
+    // Past kPolicyMaxWaves waves at the longest candidate every shorter one is
+    // pruned too, so the model's answer is the longest: skip the simulation
+    // (whose cost grows with the CTA count).
+    const uint64_t longest_grid =
+        (uint64_t)n_seq * per_seq * std::max<uint64_t>(1, (longest + kSplitCandidates[0] - 1) / kSplitCandidates[0]);
+    if (longest_grid > kPolicyMaxWaves * slots) return (uint32_t)std::min<uint64_t>(kSplitCandidates[0], limit);
     double best = 0.0;
     uint32_t best_st = kSplitCandidates[0];
     for (uint32_t st : kSplitCandidates) {
@@ -288,7 +295,6 @@ uint32_t choose_split(const int32_t *lengths, uint32_t n_seq, uint64_t per_seq, 
             best_st = st;
         }
     }
-    const uint64_t limit = std::max<uint64_t>(256, (longest + 63) / 64 * 64);
     return (uint32_t)std::min<uint64_t>(best_st, limit);
 }
 
